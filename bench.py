@@ -1,0 +1,319 @@
+"""Benchmark: batch-1 greedy decode of the 1.1B (TinyLlama-shape) Q4_K_M model.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl fiber|reference]
+
+Workload (seeded synthetic model, random init, weights N(0, 0.02) quantized with
+the Q4_K_M recipe): dim 2048, 22 layers, 32 query / 4 KV heads, head_dim 64,
+SwiGLU 5632, vocab 32000. A 128-token seeded prompt is prefilled once; one
+*step* is 512 greedy decode tokens at positions 128..639 (each step restarts at
+position 128 and overwrites the same KV rows). ``value`` is decode tokens/s with
+all inputs resident in HBM, timed with CUDA events on the decode stream (the
+weights, 633 MB per token, exceed the 126 MB L2, so no flush is needed).
+``e2e`` is the same loop through the public C call fiber_forward_token with
+host buffers: every token copies its inputs in and its argmax out.
+With --gpus N (torchrun) every rank decodes its own replica (weak scaling:
+the model fits one GPU and the decode loop has no data-parallel exchange).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path[:0] = [ROOT, os.path.join(ROOT, "fiber-inference_b200")]
+
+METRIC = "decode tok/s (1.1B Q4_K_M, bs=1); dequant-GEMV HBM GB/s vs B200 peak"
+PROMPT_LEN, DECODE_LEN, SEED = 128, 512, 1234
+MODEL_PATH = "/tmp/fiber_bench_tinyllama_q4km.gguf"
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback"
+
+
+class Clocks:
+    """nvidia-smi samples during the timed region."""
+
+    def __init__(self, device: int):
+        self.device, self.samples, self.proc = device, [], None
+
+    def __enter__(self):
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.device}", f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.samples.append([s.strip() for s in line.split(",")])
+
+    def __exit__(self, *a):
+        if self.proc:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for s in self.samples:
+            try:
+                sm.append(float(s[1]))
+                mx = float(s[2])
+                for n, v in zip(names, s[5:9]):
+                    if v.strip().lower() == "active":
+                        reasons.add(n)
+            except (ValueError, IndexError):
+                continue
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def make_model(path: str):
+    import fiber_b200 as fb
+
+    if not os.path.exists(path):
+        tmp = path + f".{os.getpid()}.tmp"
+        fb.write_model(tmp, fb.synth_cfg("tinyllama", seed=SEED))
+        os.replace(tmp, path)
+    return path
+
+
+def prompt_ids(vocab: int) -> np.ndarray:
+    return np.random.default_rng(SEED).integers(1, vocab, PROMPT_LEN).astype(np.int32)
+
+
+def gemv_bandwidth(device: int, n_launch: int = 2000):
+    """Single Q4_K GEMV 5632x2048 (random super-blocks), 40 rotating weight
+    copies (260 MB > L2); CUDA events on torch's stream."""
+    import torch
+
+    import fiber_b200 as fb
+
+    rows, cols, copies = 5632, 2048, 40
+    blocks = fb.random_blocks(fb.GGML_Q4_K, rows, cols, seed=2024)
+    w = torch.from_numpy(np.tile(blocks, copies)).to(f"cuda:{device}")
+    nb = blocks.size
+    x = torch.from_numpy(fb.randn(cols, seed=7)).to(f"cuda:{device}")
+    y = torch.empty(rows, dtype=torch.float32, device=f"cuda:{device}")
+    st = torch.cuda.current_stream(device)
+    base = w.data_ptr()
+    for i in range(50):
+        fb.gemv(fb.GGML_Q4_K, base + (i % copies) * nb, x.data_ptr(), y.data_ptr(), rows, cols, st)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(device)
+    e0.record(st)
+    for i in range(n_launch):
+        fb.gemv(fb.GGML_Q4_K, base + (i % copies) * nb, x.data_ptr(), y.data_ptr(), rows, cols, st)
+    e1.record(st)
+    e1.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / n_launch
+    algo = rows * cols // 256 * 144 + cols * 4 + rows * 4
+    return {"workload": "Q4_K GEMV 5632x2048, x fp32, 40 rotating weight copies", "us_per_launch": us,
+            "algorithmic_bytes": algo, "gbs": algo / us / 1e3}
+
+
+def cpu_reference_decode(path: str, budget_s: float, n_tokens_max: int):
+    """The reference's own C path on the host cores: fiber_model_t built by
+    gguf.c + dequant.h, cpu_forward_token with an OpenMP cblas_sgemv stand-in
+    (oracle/_ref); falls back to the restated oracle when _ref is absent."""
+    from oracle import oracle as orc
+
+    if orc.ref_available():
+        m, kind = orc.RefModel(path), "reference"
+        kv = m.kv(PROMPT_LEN + DECODE_LEN)
+        fwd = kv.forward
+    else:
+        m, kind = orc.Model(path), "port"
+        st = m.state(PROMPT_LEN + DECODE_LEN, kv_fp16=False)
+        fwd = st.forward
+    tok, n, t0 = 1, 0, time.perf_counter()
+    while n < n_tokens_max and (n < 2 or time.perf_counter() - t0 < budget_s):
+        lg = fwd(tok, n)
+        tok = int(np.argmax(lg))
+        n += 1
+    dt = time.perf_counter() - t0
+    return {"value": n / dt, "unit": "tok/s", "cores": os.cpu_count(), "kind": kind,
+            "sample": f"{n} greedy decode tokens at positions 0..{n - 1} of the same model, fp32 weights "
+                      f"(4.4 GB) via OpenMP sgemv on {os.cpu_count()} threads"}
+
+
+def run_reference(args, rank: int, world: int):
+    if rank != 0:
+        return
+    path = make_model(MODEL_PATH)
+    per_step = 4
+    cb = cpu_reference_decode(path, budget_s=1e9, n_tokens_max=per_step * (args.warmup + args.steps))
+    line = {"metric": METRIC, "value": cb["value"], "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": per_step * 1e3 / cb["value"], "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded random init)",
+            "impl": "reference",
+            "config": {"workload": "1.1B Q4_K_M batch-1 greedy decode (reference CPU path)",
+                       "step": f"{per_step} decode tokens"},
+            "cpu_baseline": {"value": cb["value"], "unit": "tok/s", "cores": cb["cores"], "kind": cb["kind"],
+                             "sample": cb["sample"]},
+            "e2e": {"value": cb["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="fiber", choices=["fiber", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=20.0)
+    args = ap.parse_args()
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+
+    import torch
+
+    import fiber_b200 as fb
+
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize(local)
+
+    path = MODEL_PATH if world == 1 else MODEL_PATH.replace(".gguf", f".r{rank}.gguf")
+    make_model(path)
+    hm = fb.HostModel(path)
+    p = hm.params
+    ctx = fb.Context(hm, device=local, max_seq=PROMPT_LEN + DECODE_LEN)
+    kv = ctx.kv(PROMPT_LEN + DECODE_LEN)
+    prompt = prompt_ids(p.vocab_size)
+    t0 = time.perf_counter()
+    first = ctx.prefill(kv, prompt)
+    prefill_tps = PROMPT_LEN / (time.perf_counter() - t0)
+
+    ref_tokens = None
+    for _ in range(args.warmup):
+        toks, _ = ctx.decode_greedy(kv, first, PROMPT_LEN, DECODE_LEN)
+        ref_tokens = toks if ref_tokens is None else ref_tokens
+    barrier()
+    ms_total, deterministic = 0.0, True
+    with Clocks(local) as clk:
+        wall0 = time.perf_counter()
+        for _ in range(args.steps):
+            toks, ms = ctx.decode_greedy(kv, first, PROMPT_LEN, DECODE_LEN)
+            ms_total += ms
+            if ref_tokens is not None and not np.array_equal(toks, ref_tokens):
+                deterministic = False
+        barrier()
+        wall = time.perf_counter() - wall0
+    if dist is not None:
+        t = torch.tensor([ms_total], device=f"cuda:{local}", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_total = float(t.item())
+    tokens_all = world * args.steps * DECODE_LEN
+    value = tokens_all / (ms_total / 1e3)
+
+    # per-kernel profile pass (eager launches with CUDA events on the decode stream)
+    ctx.set_profile(True)
+    ctx.decode_greedy(kv, first, PROMPT_LEN, DECODE_LEN)
+    prof = {k: ctx.profile(i) for i, k in enumerate(["gemv", "attention", "lm_head"])}
+    ctx.set_profile(False)
+
+    # e2e through the public C call with host buffers, one step
+    barrier()
+    e0 = time.perf_counter()
+    tok = first
+    for i in range(DECODE_LEN):
+        tok, _ = ctx.forward(kv, tok, PROMPT_LEN + i, want_logits=False)
+    barrier()
+    e2e_s = time.perf_counter() - e0
+    e2e_val = world * DECODE_LEN / e2e_s
+
+    if dist is not None:
+        dist.barrier()
+    if rank != 0:
+        ctx.close()
+        if dist is not None:
+            dist.destroy_process_group()
+        return
+
+    peak, peak_kind = peaks()
+    gemv_ms, gemv_bytes = prof["gemv"]
+    attn_ms, attn_bytes = prof["attention"]
+    lm_ms, lm_bytes = prof["lm_head"]
+    achieved = gemv_bytes / (gemv_ms / 1e3) / 1e9
+    weights_per_tok = gemv_bytes + lm_bytes
+    mean_kv = attn_bytes
+    step_bytes = weights_per_tok + mean_kv
+    single = gemv_bandwidth(local)
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_reference_decode(path, budget_s=args.cpu_seconds, n_tokens_max=400)
+    launches = ctx.step_launches() * DECODE_LEN * args.steps
+    line = {
+        "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_total / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded random-init weights, seeded prompt ids)",
+        "config": {"workload": "1.1B Q4_K_M (TinyLlama shape) batch-1 greedy decode",
+                   "model": "dim 2048, 22 layers, 32/4 heads, hd 64, ffn 5632, vocab 32000, Q4_K_M",
+                   "prompt": PROMPT_LEN, "decode_tokens_per_step": DECODE_LEN, "global_batch": 1,
+                   "parallelism": f"replicas x{world}", "l2": "inputs larger than L2 (633 MB weights/token)",
+                   "deterministic_tokens": deterministic, "prefill_tok_s": prefill_tps},
+        "roofline": {"bound": "hbm", "kernel": "dequant-fused GEMVs (QKV, Wo, gate/up+SwiGLU, down) of one token",
+                     "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "peak_source": peak_kind, "traffic": None,
+                     "algorithmic_bytes_per_step": gemv_bytes, "ms_per_step": gemv_ms},
+        "decode_roofline": {"bytes_per_token": step_bytes, "achieved_gbs": step_bytes * value / world / 1e9,
+                            "frac": step_bytes * value / world / 1e9 / peak,
+                            "kernel_ms_per_token": {"gemv": gemv_ms, "attention": attn_ms, "lm_head": lm_ms}},
+        "gemv_single": dict(single, frac=single["gbs"] / peak),
+        "e2e": {"value": e2e_val, "unit": "tok/s", "h2d_bytes_per_step": 32 * DECODE_LEN,
+                "d2h_bytes_per_step": 32 * DECODE_LEN, "api": "fiber_forward_token (host token/pos in, argmax out)"},
+        "gpu_launches": launches,
+        "clocks": clk.summary(),
+        "wall_s": wall,
+    }
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    print(json.dumps(line), flush=True)
+    ctx.close()
+    if dist is not None:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,204 @@
+// attention.cuh — GQA decode attention over the paged fp16 KV cache, with the
+// RoPE of q/k and the KV append of the new position fused in.
+//
+// Reference semantics (metal/kernels.metal:374-504, src/fiber_proof.m:30-51,
+// 79-109): half-split RoPE on pairs (i, i + hd/2) with angle pos * theta^(-2i/hd);
+// K/V of the new position stored at `pos`; per query head h (kv head
+// h * n_kv / n_heads) softmax(q.K_t * 1/sqrt(hd)) over t <= pos, then sum p_t V_t.
+//
+// Split-K (flash-decoding): CTA (chunk c, kv head g) handles the page of
+// positions [c*P, c*P + P) for all G = n_heads / n_kv query heads sharing g, so
+// each K/V page is read from HBM once per step. It writes (max, sum, o[hd]) per
+// head to scratch; the last CTA of each kv head (atomic ticket) merges the
+// chunks into the output. Dot products q.K and the RoPE rotations use the
+// reference's operation order with unfused multiplies and adds, so for equal
+// inputs the scores are bit-identical to the CPU path.
+#pragma once
+#include "quant.cuh"
+
+namespace fiber {
+
+struct AttnParams {
+    const float *qkv;         // q [n_heads*hd] | k [n_kv*hd] | v [n_kv*hd], unrotated
+    const float2 *rope;       // [max_seq][hd/2] (cos, sin), computed on the host like the CPU path
+    uint16_t *k_pool;         // fp16 bits, [page][layer][kv_head][P][hd]
+    uint16_t *v_pool;
+    const int32_t *page_table;  // [max_pages] for this sequence slot
+    const int32_t *pos_ptr;   // current position (device)
+    float *part;              // [n_kv][max_chunks][G][hd + 2]
+    unsigned int *count;      // [n_kv], zero between launches
+    float *out;               // [n_heads * hd]
+    int layer, n_layers, n_kv, n_heads, max_chunks, max_seq;
+    float scale;
+    int *err;                 // set to 1 when pos is out of range
+};
+
+constexpr int ATTN_THREADS = 128;
+constexpr int ATTN_P = 64;  // positions per page / chunk
+
+template <int HD, int G>
+__global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const AttnParams a) {
+    constexpr int P = ATTN_P;
+    constexpr int KST = HD + 2;  // padded K row (halves) -> conflict-free column walks
+    __shared__ float qs[G][HD];
+    __shared__ __align__(16) uint16_t ks[P][KST];
+    __shared__ __align__(16) uint16_t vs[P][HD];
+    __shared__ float sc[G][P];
+    __shared__ float mx[G], sm[G];
+    __shared__ unsigned int ticket;
+
+    const int c = blockIdx.x, g = blockIdx.y, tid = threadIdx.x;
+    const int pos = *a.pos_ptr;
+    if (pos < 0 || pos >= a.max_seq) {
+        if (c == 0 && g == 0 && tid == 0) *a.err = 1;
+        return;
+    }
+    const int seq = pos + 1;
+    const int nch = (seq + P - 1) / P;
+    if (c >= nch) return;
+    const int t0 = c * P;
+    const int nt = min(P, seq - t0);
+    const int kvd = a.n_kv * HD;
+    const float2 *rp = a.rope + (size_t)pos * (HD / 2);
+
+    // rotated queries of the G heads of this group
+    for (int i = tid; i < G * (HD / 2); i += ATTN_THREADS) {
+        const int h = i / (HD / 2), j = i % (HD / 2);
+        const float *qh = a.qkv + (size_t)(g * G + h) * HD;
+        const float x1 = qh[j], x2 = qh[j + HD / 2];
+        const float2 cs = rp[j];
+        qs[h][j] = __fsub_rn(__fmul_rn(x1, cs.x), __fmul_rn(x2, cs.y));
+        qs[h][j + HD / 2] = __fadd_rn(__fmul_rn(x1, cs.y), __fmul_rn(x2, cs.x));
+    }
+
+    const int page = a.page_table[c];
+    const size_t base = (((size_t)page * a.n_layers + a.layer) * a.n_kv + g) * (size_t)P * HD;
+    uint16_t *kp = a.k_pool + base, *vp = a.v_pool + base;
+
+    // the chunk holding `pos` appends the new K (rotated) and V, rounded to fp16
+    if (c == nch - 1) {
+        const int tn = pos - t0;
+        const float *kr = a.qkv + (size_t)a.n_heads * HD + (size_t)g * HD;
+        const float *vr = a.qkv + (size_t)a.n_heads * HD + kvd + (size_t)g * HD;
+        for (int j = tid; j < HD / 2; j += ATTN_THREADS) {
+            const float x1 = kr[j], x2 = kr[j + HD / 2];
+            const float2 cs = rp[j];
+            const float y1 = __fsub_rn(__fmul_rn(x1, cs.x), __fmul_rn(x2, cs.y));
+            const float y2 = __fadd_rn(__fmul_rn(x1, cs.y), __fmul_rn(x2, cs.x));
+            kp[(size_t)tn * HD + j] = __half_as_ushort(__float2half_rn(y1));
+            kp[(size_t)tn * HD + j + HD / 2] = __half_as_ushort(__float2half_rn(y2));
+        }
+        for (int j = tid; j < HD; j += ATTN_THREADS) vp[(size_t)tn * HD + j] = __half_as_ushort(__float2half_rn(vr[j]));
+        __syncthreads();  // block-wide visibility of the appended row
+    }
+
+    // stage the chunk: K with padded rows, V dense (16-byte loads)
+    constexpr int V8 = HD / 8;  // uint4 per row
+    for (int i = tid; i < nt * V8; i += ATTN_THREADS) {
+        const int t = i / V8, k8 = i % V8;
+        const uint4 kv4 = __ldcg(reinterpret_cast<const uint4 *>(kp + (size_t)t * HD) + k8);
+        const uint4 vv4 = __ldcg(reinterpret_cast<const uint4 *>(vp + (size_t)t * HD) + k8);
+        uint32_t *kd = reinterpret_cast<uint32_t *>(&ks[t][8 * k8]);
+        kd[0] = kv4.x; kd[1] = kv4.y; kd[2] = kv4.z; kd[3] = kv4.w;
+        *reinterpret_cast<uint4 *>(&vs[t][8 * k8]) = vv4;
+    }
+    __syncthreads();
+
+    // scores: one (head, position) dot product per thread, sequential over d
+    for (int i = tid; i < G * P; i += ATTN_THREADS) {
+        const int h = i / P, t = i % P;
+        if (t < nt) {
+            float dot = 0.f;
+#pragma unroll 8
+            for (int d = 0; d < HD; d++)
+                dot = __fadd_rn(dot, __fmul_rn(qs[h][d], __half2float(__ushort_as_half(ks[t][d]))));
+            sc[h][t] = __fmul_rn(dot, a.scale);
+        }
+    }
+    __syncthreads();
+
+    // chunk-local softmax statistics, one warp per head
+    const int warp = tid >> 5, lane = tid & 31;
+    for (int h = warp; h < G; h += ATTN_THREADS / 32) {
+        float m = -INFINITY;
+        for (int t = lane; t < nt; t += 32) m = fmaxf(m, sc[h][t]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        float s = 0.f;
+        for (int t = lane; t < nt; t += 32) {
+            const float e = expf(sc[h][t] - m);
+            sc[h][t] = e;
+            s += e;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+        if (lane == 0) {
+            mx[h] = m;
+            sm[h] = s;
+        }
+    }
+    __syncthreads();
+
+    // unnormalised P.V for the chunk
+    float *pc = a.part + ((size_t)g * a.max_chunks + c) * G * (HD + 2);
+    for (int i = tid; i < G * HD; i += ATTN_THREADS) {
+        const int h = i / HD, d = i % HD;
+        float o = 0.f;
+        for (int t = 0; t < nt; t++) o = fmaf(sc[h][t], __half2float(__ushort_as_half(vs[t][d])), o);
+        pc[h * (HD + 2) + 2 + d] = o;
+    }
+    if (tid < G) {
+        pc[tid * (HD + 2) + 0] = mx[tid];
+        pc[tid * (HD + 2) + 1] = sm[tid];
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) ticket = atomicAdd(a.count + g, 1u);
+    __syncthreads();
+    if (ticket != (unsigned)(nch - 1)) return;
+
+    // last chunk of this kv head: merge
+    __threadfence();
+    const float *pg = a.part + (size_t)g * a.max_chunks * G * (HD + 2);
+    for (int i = tid; i < G * HD; i += ATTN_THREADS) {
+        const int h = i / HD, d = i % HD;
+        float M = -INFINITY;
+        for (int k = 0; k < nch; k++) M = fmaxf(M, __ldcg(pg + ((size_t)k * G + h) * (HD + 2)));
+        float L = 0.f, O = 0.f;
+        for (int k = 0; k < nch; k++) {
+            const float *e = pg + ((size_t)k * G + h) * (HD + 2);
+            const float w = expf(__ldcg(e) - M);
+            L = fmaf(w, __ldcg(e + 1), L);
+            O = fmaf(w, __ldcg(e + 2 + d), O);
+        }
+        a.out[(size_t)(g * G + h) * HD + d] = O / L;
+    }
+    if (tid == 0) a.count[g] = 0u;
+}
+
+// Embedding row of `*token` (fp16-rounded like the reference's fp16 buf_x,
+// src/gpu_ffn.m:466-482) into the fp32 residual stream.
+template <int T>
+__global__ void embed_kernel(const uint8_t *__restrict__ tab, const int32_t *__restrict__ token, float *x, int dim,
+                             int vocab, int *err) {
+    int tok = *token;
+    if (tok < 0 || tok >= vocab) {
+        if (threadIdx.x == 0 && blockIdx.x == 0) *err = 2;
+        tok = 0;
+    }
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < dim; i += gridDim.x * blockDim.x) {
+        float v;
+        if constexpr (T == T_F16) {
+            v = h2f(reinterpret_cast<const uint16_t *>(tab)[(size_t)tok * dim + i]);
+        } else if constexpr (T == T_F32) {
+            v = round_f16(reinterpret_cast<const float *>(tab)[(size_t)tok * dim + i]);
+        } else {
+            constexpr int BB = T == T_Q4_K ? 144 : (T == T_Q5_K ? 176 : 210);
+            const uint8_t *blk = tab + ((size_t)tok * (dim >> 8) + (i >> 8)) * BB;
+            v = round_f16(decode_elem<T>(blk, i & 255));
+        }
+        x[i] = v;
+    }
+}
+
+}  // namespace fiber

@@ -1,0 +1,836 @@
+// fiber_cuda.cu — host side of libfiber_cuda.so: model upload, paged KV cache,
+// decode-step enqueue, CUDA-graph capture and the extern "C" entry points of
+// include/gpu_ffn.h, include/kv_cache.h and include/fiber_cuda.h.
+//
+// One decode step (src/gpu_ffn.m:488-617 of the reference) is 2 + 5 * n_layers
+// kernels on the context's stream:
+//   embed(token)                                   gpu_embed, on the device
+//   per layer: RMSNorm+[Wq;Wk;Wv]                  rmsnorm + 3 matvecs
+//              RoPE+KV append+GQA attention        rope_qk, kv_store_kv, attention_decode
+//              Wo (+residual)                      matvec + residual_rmsnorm's add
+//              RMSNorm+[W1,W3]+SwiGLU              rmsnorm + 2 matvecs + silu_gate
+//              W2 (+residual)                      matvec + residual_add
+//   RMSNorm+lm_head+argmax                         rmsnorm + matvec_f32 + sampler argmax
+// The step reads token and position from device memory, so it is captured once
+// into a CUDA graph and replayed for every token.
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include <vector>
+
+#include "attention.cuh"
+#include "fiber_cuda.h"
+#include "gemv.cuh"
+
+using namespace fiber;
+
+// ---- errors --------------------------------------------------------------------
+
+static thread_local char g_err[512] = "";
+
+static int set_err(int code, const char *fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_err, sizeof(g_err), fmt, ap);
+    va_end(ap);
+    return code;
+}
+
+#define CK(call)                                                                                  \
+    do {                                                                                          \
+        cudaError_t e_ = (call);                                                                  \
+        if (e_ != cudaSuccess)                                                                    \
+            return set_err(FIBER_ECUDA, "%s:%d %s: %s", __FILE__, __LINE__, #call, cudaGetErrorString(e_)); \
+    } while (0)
+
+extern "C" const char *fiber_last_error(void) { return g_err; }
+
+extern "C" int fiber_device_count(void) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess) return 0;
+    return n;
+}
+
+// ---- small helpers ----------------------------------------------------------------
+
+static int block_bytes(int t) {
+    switch (t) {
+    case T_Q4_K: return 144;
+    case T_Q5_K: return 176;
+    case T_Q6_K: return 210;
+    case T_F16: return 512;
+    default: return 0;
+    }
+}
+
+static const char *tname(int t) {
+    switch (t) {
+    case T_F32: return "F32";
+    case T_F16: return "F16";
+    case T_Q4_K: return "Q4_K";
+    case T_Q5_K: return "Q5_K";
+    case T_Q6_K: return "Q6_K";
+    default: return "unsupported";
+    }
+}
+
+static bool matrix_type_ok(int t) { return t == T_Q4_K || t == T_Q5_K || t == T_Q6_K || t == T_F16; }
+
+constexpr int GEMV_ROWS = 2;
+constexpr int GEMV_TILE = GEMV_ROWS * GEMV_WARPS;
+
+template <int T, int EPI>
+static cudaError_t launch_gemv_t(const GemvParams &p, int grid, cudaStream_t st) {
+    const size_t smem = (size_t)p.cols * sizeof(float);
+    auto k = gemv_kernel<T, EPI, GEMV_ROWS>;
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+    }
+    k<<<grid, GEMV_THREADS, smem, st>>>(p);
+    return cudaGetLastError();
+}
+
+template <int EPI>
+static cudaError_t launch_gemv(int type, const GemvParams &p, int grid, cudaStream_t st) {
+    switch (type) {
+    case T_Q4_K: return launch_gemv_t<T_Q4_K, EPI>(p, grid, st);
+    case T_Q5_K: return launch_gemv_t<T_Q5_K, EPI>(p, grid, st);
+    case T_Q6_K: return launch_gemv_t<T_Q6_K, EPI>(p, grid, st);
+    case T_F16: return launch_gemv_t<T_F16, EPI>(p, grid, st);
+    default: return cudaErrorInvalidValue;
+    }
+}
+
+// All segments of one launch must share a type (the kernel is specialised on
+// it); a QKV projection with mixed types is split into per-type launches.
+static GemvParams one_seg(const uint8_t *w, int type, int rows, int out_off, int cols) {
+    GemvParams p;
+    memset(&p, 0, sizeof(p));
+    p.seg[0] = {w, type, rows, out_off};
+    p.nseg = 1;
+    p.tiles[0] = (rows + GEMV_TILE - 1) / GEMV_TILE;
+    p.cols = cols;
+    return p;
+}
+
+static int grid_of(const GemvParams &p) {
+    int g = 0;
+    for (int s = 0; s < p.nseg; s++) g += p.tiles[s];
+    return g;
+}
+
+// ---- KV cache ------------------------------------------------------------------------
+
+extern "C" void kv_cache_free(kv_cache_t *kv) {
+    if (!kv) return;
+    int prev = -1;
+    cudaGetDevice(&prev);
+    cudaSetDevice(kv->device);
+    cudaFree(kv->k_pool);
+    cudaFree(kv->v_pool);
+    cudaFree(kv->page_table);
+    if (prev >= 0) cudaSetDevice(prev);
+    free(kv);
+}
+
+extern "C" kv_cache_t *kv_cache_init_paged(int device, int n_layers, int n_kv_heads, int head_dim, int max_seq,
+                                           int max_batch, int page_size) {
+    if (n_layers <= 0 || n_kv_heads <= 0 || head_dim <= 0 || head_dim % 8 || max_seq <= 0 || max_batch <= 0 ||
+        page_size != ATTN_P) {
+        set_err(FIBER_EARG, "kv_cache_init: bad shape (layers=%d kv_heads=%d head_dim=%d max_seq=%d batch=%d page=%d; page must be %d)",
+                n_layers, n_kv_heads, head_dim, max_seq, max_batch, page_size, ATTN_P);
+        return nullptr;
+    }
+    if (cudaSetDevice(device) != cudaSuccess) {
+        set_err(FIBER_ECUDA, "kv_cache_init: cannot select device %d", device);
+        return nullptr;
+    }
+    kv_cache_t *kv = (kv_cache_t *)calloc(1, sizeof(kv_cache_t));
+    kv->n_layers = n_layers;
+    kv->n_kv_heads = n_kv_heads;
+    kv->head_dim = head_dim;
+    kv->max_seq = max_seq;
+    kv->device = device;
+    kv->max_batch = max_batch;
+    kv->page_size = page_size;
+    kv->max_pages_per_seq = (max_seq + page_size - 1) / page_size;
+    kv->n_pages = kv->max_pages_per_seq * max_batch;
+    const size_t elems = (size_t)kv->n_pages * n_layers * n_kv_heads * page_size * head_dim;
+    std::vector<int32_t> pt((size_t)kv->n_pages);
+    for (int i = 0; i < kv->n_pages; i++) pt[i] = i;
+    if (cudaMalloc(&kv->k_pool, elems * 2) != cudaSuccess || cudaMalloc(&kv->v_pool, elems * 2) != cudaSuccess ||
+        cudaMalloc(&kv->page_table, pt.size() * 4) != cudaSuccess ||
+        cudaMemset(kv->k_pool, 0, elems * 2) != cudaSuccess || cudaMemset(kv->v_pool, 0, elems * 2) != cudaSuccess ||
+        cudaMemcpy(kv->page_table, pt.data(), pt.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess) {
+        set_err(FIBER_ENOMEM, "kv_cache_init: allocating %.1f MB failed", 4.0 * elems / 1e6);
+        kv_cache_free(kv);
+        return nullptr;
+    }
+    return kv;
+}
+
+extern "C" kv_cache_t *kv_cache_init(int device, int n_layers, int n_kv_heads, int head_dim, int max_seq) {
+    kv_cache_t *kv = kv_cache_init_paged(device, n_layers, n_kv_heads, head_dim, max_seq, 1, ATTN_P);
+    if (kv)
+        printf("KV Cache: %d layers, %d KV-heads, head_dim=%d, max_seq=%d (%.1f MB, paged fp16)\n", n_layers,
+               n_kv_heads, head_dim, max_seq,
+               4.0 * kv->n_pages * n_layers * n_kv_heads * kv->page_size * head_dim / (1024.0 * 1024.0));
+    return kv;
+}
+
+static size_t kv_offset(const kv_cache_t *kv, int page, int layer, int head, int in_page) {
+    return ((((size_t)page * kv->n_layers + layer) * kv->n_kv_heads + head) * kv->page_size + in_page) * kv->head_dim;
+}
+
+static int kv_copy(kv_cache_t *kv, int slot, int layer, int pos, int n_pos, float *k, float *v, bool write) {
+    if (!kv || slot < 0 || slot >= kv->max_batch || layer < 0 || layer >= kv->n_layers || pos < 0 || n_pos < 0 ||
+        pos + n_pos > kv->max_seq)
+        return set_err(FIBER_EARG, "kv_cache copy: out of range (slot %d layer %d pos %d n %d)", slot, layer, pos, n_pos);
+    CK(cudaSetDevice(kv->device));
+    std::vector<int32_t> pt((size_t)kv->max_pages_per_seq);
+    CK(cudaMemcpy(pt.data(), kv->page_table + (size_t)slot * kv->max_pages_per_seq, pt.size() * 4,
+                  cudaMemcpyDeviceToHost));
+    const int hd = kv->head_dim, kvd = kv->n_kv_heads * hd;
+    std::vector<uint16_t> hk((size_t)hd), hv((size_t)hd);
+    for (int t = 0; t < n_pos; t++) {
+        const int p = pos + t, page = pt[p / kv->page_size], ip = p % kv->page_size;
+        for (int h = 0; h < kv->n_kv_heads; h++) {
+            const size_t off = kv_offset(kv, page, layer, h, ip);
+            if (write) {
+                for (int d = 0; d < hd; d++) {
+                    hk[d] = __half_as_ushort(__float2half_rn(k[(size_t)t * kvd + h * hd + d]));
+                    hv[d] = __half_as_ushort(__float2half_rn(v[(size_t)t * kvd + h * hd + d]));
+                }
+                CK(cudaMemcpy(kv->k_pool + off, hk.data(), (size_t)hd * 2, cudaMemcpyHostToDevice));
+                CK(cudaMemcpy(kv->v_pool + off, hv.data(), (size_t)hd * 2, cudaMemcpyHostToDevice));
+            } else {
+                CK(cudaMemcpy(hk.data(), kv->k_pool + off, (size_t)hd * 2, cudaMemcpyDeviceToHost));
+                CK(cudaMemcpy(hv.data(), kv->v_pool + off, (size_t)hd * 2, cudaMemcpyDeviceToHost));
+                for (int d = 0; d < hd; d++) {
+                    k[(size_t)t * kvd + h * hd + d] = __half2float(__ushort_as_half(hk[d]));
+                    v[(size_t)t * kvd + h * hd + d] = __half2float(__ushort_as_half(hv[d]));
+                }
+            }
+        }
+    }
+    return FIBER_OK;
+}
+
+extern "C" int kv_cache_write(kv_cache_t *kv, int slot, int layer, int pos, int n_pos, const float *k, const float *v) {
+    return kv_copy(kv, slot, layer, pos, n_pos, const_cast<float *>(k), const_cast<float *>(v), true);
+}
+
+extern "C" int kv_cache_read(const kv_cache_t *kv, int slot, int layer, int pos, int n_pos, float *k, float *v) {
+    return kv_copy(const_cast<kv_cache_t *>(kv), slot, layer, pos, n_pos, k, v, false);
+}
+
+// ---- context ---------------------------------------------------------------------------
+
+struct LayerDev {
+    const uint8_t *wq, *wk, *wv, *wo, *w1, *w2, *w3;
+    const float *attn_norm, *ffn_norm;
+    int tq, tk, tv, to, t1, t2, t3;
+};
+
+struct StepIO {  // device-side step state, one 32-byte block so it moves in one copy
+    int32_t token, pos, argmax, err, step, pad[3];
+};
+
+struct Graph {
+    cudaGraphExec_t exec = nullptr;
+    const kv_cache_t *kv = nullptr;
+};
+
+struct gpu_context {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    model_params_t p{};
+    int max_seq = 0, max_chunks = 0, kvd = 0, G = 0;
+    uint8_t *d_data = nullptr;
+    size_t data_bytes = 0;
+    std::vector<LayerDev> L;
+    const uint8_t *embd = nullptr, *out = nullptr;
+    const float *out_norm = nullptr;
+    int t_embd = 0, t_out = 0;
+    float *x = nullptr, *qkv = nullptr, *att = nullptr, *h = nullptr, *logits = nullptr;
+    float2 *rope = nullptr;
+    StepIO *io = nullptr;            // device
+    int32_t *rec = nullptr;          // device [max_seq]: tokens of the greedy loop
+    float *att_part = nullptr;       // attention split-K partials (scratch)
+    unsigned int *att_cnt = nullptr; // attention merge tickets (scratch)
+    float2 *am_part = nullptr;       // lm_head argmax partials (scratch)
+    unsigned int *am_cnt = nullptr;  // lm_head merge ticket (scratch)
+    StepIO *h_io = nullptr;          // pinned
+    float *h_logits = nullptr;       // pinned
+    std::vector<float> logits_copy;
+    Graph g_step, g_loop;
+    cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+    int profile = 0;
+    double prof_ms[3] = {0, 0, 0}, prof_bytes[3] = {0, 0, 0};
+    int prof_steps = 0;
+};
+
+static void free_graph(Graph &g) {
+    if (g.exec) cudaGraphExecDestroy(g.exec);
+    g.exec = nullptr;
+    g.kv = nullptr;
+}
+
+extern "C" void fiber_cuda_free(fiber_ctx_t *c) {
+    if (!c) return;
+    cudaSetDevice(c->device);
+    if (c->stream) cudaStreamSynchronize(c->stream);
+    free_graph(c->g_step);
+    free_graph(c->g_loop);
+    void *dev[] = {c->d_data, c->x, c->qkv, c->att, c->h, c->logits, c->rope, c->io, c->rec,
+                   c->att_part, c->att_cnt, c->am_part, c->am_cnt};
+    for (void *p : dev)
+        if (p) cudaFree(p);
+    if (c->h_io) cudaFreeHost(c->h_io);
+    if (c->h_logits) cudaFreeHost(c->h_logits);
+    if (c->ev0) cudaEventDestroy(c->ev0);
+    if (c->ev1) cudaEventDestroy(c->ev1);
+    if (c->stream) cudaStreamDestroy(c->stream);
+    delete c;
+}
+
+static int ctx_init(gpu_context *c, const model_t *m, int device, int max_seq) {
+    const model_params_t &p = m->params;
+    c->device = device;
+    c->p = p;
+    c->max_seq = max_seq;
+    c->kvd = (int)(p.n_kv_heads * p.head_dim);
+    c->G = (int)(p.n_heads / p.n_kv_heads);
+    c->max_chunks = (max_seq + ATTN_P - 1) / ATTN_P;
+    if (p.dim % 256 || p.ffn_dim % 256)
+        return set_err(FIBER_EUNSUPPORTED, "dim (%u) and ffn_dim (%u) must be multiples of 256", p.dim, p.ffn_dim);
+    if (!(p.head_dim == 64 || p.head_dim == 128))
+        return set_err(FIBER_EUNSUPPORTED, "head_dim %u not supported (64 or 128)", p.head_dim);
+    if (!(c->G == 1 || c->G == 2 || c->G == 4 || c->G == 8))
+        return set_err(FIBER_EUNSUPPORTED, "GQA group %d not supported (1, 2, 4, 8)", c->G);
+    if (!m->output_norm || m->output_norm_type != GGML_TYPE_F32)
+        return set_err(FIBER_EUNSUPPORTED, "output_norm.weight must be F32");
+    if (!matrix_type_ok(m->output_type))
+        return set_err(FIBER_EUNSUPPORTED, "classifier type %s not supported", tname(m->output_type));
+    c->t_embd = m->token_embd_type;
+    if (!(matrix_type_ok(c->t_embd) || c->t_embd == T_F32))
+        return set_err(FIBER_EUNSUPPORTED, "token_embd type %s not supported", tname(m->token_embd_type));
+    for (uint32_t l = 0; l < p.n_layers; l++) {
+        const layer_weights_t &w = m->layers[l];
+        const int ts[7] = {w.wq_type, w.wk_type, w.wv_type, w.wo_type, w.w1_type, w.w2_type, w.w3_type};
+        for (int t : ts)
+            if (!matrix_type_ok(t)) return set_err(FIBER_EUNSUPPORTED, "layer %u: weight type %s not supported", l, tname(t));
+        if (w.attn_norm_type != GGML_TYPE_F32 || w.ffn_norm_type != GGML_TYPE_F32)
+            return set_err(FIBER_EUNSUPPORTED, "layer %u: norms must be F32", l);
+        if (w.w1_type != w.w3_type)
+            return set_err(FIBER_EUNSUPPORTED, "layer %u: ffn_gate and ffn_up must share a type", l);
+    }
+
+    CK(cudaSetDevice(device));
+    CK(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
+    CK(cudaEventCreate(&c->ev0));
+    CK(cudaEventCreate(&c->ev1));
+
+    // GGUF data section, unchanged
+    const gguf_file_t *gf = m->gf;
+    c->data_bytes = gf->file_size - gf->data_offset;
+    if (cudaMalloc(&c->d_data, c->data_bytes) != cudaSuccess)
+        return set_err(FIBER_ENOMEM, "cannot allocate %.1f MB for weights", c->data_bytes / 1e6);
+    CK(cudaMemcpy(c->d_data, (const uint8_t *)gf->data + gf->data_offset, c->data_bytes, cudaMemcpyHostToDevice));
+    auto dp = [&](uint64_t off) { return c->d_data + off; };
+    c->L.resize(p.n_layers);
+    for (uint32_t l = 0; l < p.n_layers; l++) {
+        const layer_weights_t &w = m->layers[l];
+        const layer_offsets_t &o = m->layer_off[l];
+        LayerDev &d = c->L[l];
+        d.wq = dp(o.wq); d.wk = dp(o.wk); d.wv = dp(o.wv); d.wo = dp(o.wo);
+        d.w1 = dp(o.w1); d.w2 = dp(o.w2); d.w3 = dp(o.w3);
+        d.attn_norm = (const float *)dp(o.attn_norm);
+        d.ffn_norm = (const float *)dp(o.ffn_norm);
+        d.tq = w.wq_type; d.tk = w.wk_type; d.tv = w.wv_type; d.to = w.wo_type;
+        d.t1 = w.w1_type; d.t2 = w.w2_type; d.t3 = w.w3_type;
+    }
+    c->embd = dp(m->token_embd_off);
+    c->out = dp(m->output_off);
+    c->out_norm = (const float *)dp(m->output_norm_off);
+    c->t_out = m->output_type;
+
+    const int dim = p.dim, ffn = p.ffn_dim, V = p.vocab_size;
+    const int lm_tiles = (V + GEMV_TILE - 1) / GEMV_TILE;
+    CK(cudaMalloc(&c->x, (size_t)dim * 4));
+    CK(cudaMalloc(&c->qkv, (size_t)(dim + 2 * c->kvd) * 4));
+    CK(cudaMalloc(&c->att, (size_t)dim * 4));
+    CK(cudaMalloc(&c->h, (size_t)ffn * 4));
+    CK(cudaMalloc(&c->logits, (size_t)V * 4));
+    CK(cudaMalloc(&c->rope, (size_t)max_seq * (p.head_dim / 2) * sizeof(float2)));
+    CK(cudaMalloc(&c->io, sizeof(StepIO)));
+    CK(cudaMalloc(&c->rec, (size_t)max_seq * 4));
+    CK(cudaMalloc(&c->att_part, (size_t)p.n_kv_heads * c->max_chunks * c->G * (p.head_dim + 2) * 4));
+    CK(cudaMalloc(&c->att_cnt, (size_t)p.n_kv_heads * 4));
+    CK(cudaMalloc(&c->am_part, (size_t)lm_tiles * sizeof(float2)));
+    CK(cudaMalloc(&c->am_cnt, 4));
+    CK(cudaMemset(c->att_cnt, 0, (size_t)p.n_kv_heads * 4));
+    CK(cudaMemset(c->am_cnt, 0, 4));
+    CK(cudaMemset(c->io, 0, sizeof(StepIO)));
+    CK(cudaMemset(c->x, 0, (size_t)dim * 4));
+    CK(cudaMallocHost(&c->h_io, sizeof(StepIO)));
+    CK(cudaMallocHost(&c->h_logits, (size_t)V * 4));
+    memset(c->h_io, 0, sizeof(StepIO));
+    c->logits_copy.resize(V);
+
+    // RoPE table with the CPU path's expressions (src/fiber_proof.m:33-35)
+    const int hd = p.head_dim;
+    std::vector<float2> tab((size_t)max_seq * (hd / 2));
+    for (int pos = 0; pos < max_seq; pos++)
+        for (int i = 0; i < hd / 2; i++) {
+            const float freq = 1.0f / powf(p.rope_freq_base, 2.0f * i / (float)hd);
+            const float angle = pos * freq;
+            tab[(size_t)pos * (hd / 2) + i] = make_float2(cosf(angle), sinf(angle));
+        }
+    CK(cudaMemcpy(c->rope, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice));
+    return FIBER_OK;
+}
+
+extern "C" fiber_ctx_t *fiber_cuda_init(const model_t *m, int device, int max_batch, int max_seq) {
+    if (!m || !m->layers) {
+        set_err(FIBER_EARG, "fiber_cuda_init: no model");
+        return nullptr;
+    }
+    if (max_batch != 1) {
+        set_err(FIBER_EUNSUPPORTED, "fiber_cuda_init: max_batch %d (only 1 is implemented)", max_batch);
+        return nullptr;
+    }
+    if (max_seq <= 0) max_seq = (int)m->params.context_length;
+    gpu_context *c = new gpu_context();
+    if (ctx_init(c, m, device, max_seq) != FIBER_OK) {
+        fprintf(stderr, "fiber_cuda_init: %s\n", g_err);
+        fiber_cuda_free(c);
+        return nullptr;
+    }
+    return c;
+}
+
+// ---- the decode step ------------------------------------------------------------------
+
+enum { K_GEMV = 0, K_ATTN = 1, K_LM = 2 };
+
+struct Prof {  // optional per-kernel timing (eager launches only)
+    gpu_context *c;
+    std::vector<cudaEvent_t> ev;
+    std::vector<int> kind;
+    int n = 0;
+    void begin(int k) {
+        if (!c) return;
+        if ((int)ev.size() < 2 * (n + 1)) {
+            cudaEvent_t a, b;
+            cudaEventCreate(&a);
+            cudaEventCreate(&b);
+            ev.push_back(a);
+            ev.push_back(b);
+            kind.push_back(k);
+        }
+        kind[n] = k;
+        cudaEventRecord(ev[2 * n], c->stream);
+    }
+    void end() {
+        if (!c) return;
+        cudaEventRecord(ev[2 * n + 1], c->stream);
+        n++;
+    }
+    ~Prof() {
+        for (auto e : ev) cudaEventDestroy(e);
+    }
+};
+
+static cudaError_t enqueue_qkv(gpu_context *c, const LayerDev &d, cudaStream_t st) {
+    const int dim = c->p.dim, kvd = c->kvd;
+    GemvParams p;
+    memset(&p, 0, sizeof(p));
+    p.cols = dim;
+    p.x = c->x;
+    p.norm_w = d.attn_norm;
+    p.eps = c->p.rms_norm_eps;
+    p.y = c->qkv;
+    const uint8_t *ws[3] = {d.wq, d.wk, d.wv};
+    const int ts[3] = {d.tq, d.tk, d.tv}, rows[3] = {dim, kvd, kvd}, offs[3] = {0, dim, dim + kvd};
+    // group consecutive segments sharing a type into one launch
+    int s = 0;
+    while (s < 3) {
+        GemvParams q = p;
+        q.nseg = 0;
+        const int t = ts[s];
+        while (s < 3 && ts[s] == t) {
+            q.seg[q.nseg] = {ws[s], t, rows[s], offs[s]};
+            q.tiles[q.nseg] = (rows[s] + GEMV_TILE - 1) / GEMV_TILE;
+            q.nseg++;
+            s++;
+        }
+        cudaError_t e = launch_gemv<EPI_STORE>(t, q, grid_of(q), st);
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
+}
+
+template <int HD, int G>
+static cudaError_t launch_attn_t(const AttnParams &a, cudaStream_t st) {
+    dim3 grid(a.max_chunks, a.n_kv);
+    attn_decode_kernel<HD, G><<<grid, ATTN_THREADS, 0, st>>>(a);
+    return cudaGetLastError();
+}
+
+static cudaError_t launch_attn(gpu_context *c, const AttnParams &a, cudaStream_t st) {
+    const int hd = c->p.head_dim, G = c->G;
+#define ATT_CASE(H, GG) \
+    if (hd == H && G == GG) return launch_attn_t<H, GG>(a, st);
+    ATT_CASE(64, 1) ATT_CASE(64, 2) ATT_CASE(64, 4) ATT_CASE(64, 8)
+    ATT_CASE(128, 1) ATT_CASE(128, 2) ATT_CASE(128, 4) ATT_CASE(128, 8)
+#undef ATT_CASE
+    return cudaErrorInvalidValue;
+}
+
+static cudaError_t launch_embed(gpu_context *c, cudaStream_t st) {
+    const int dim = c->p.dim, V = c->p.vocab_size, grid = (dim + 255) / 256;
+    int *err = &c->io->err;
+    const int32_t *tok = &c->io->token;
+    switch (c->t_embd) {
+    case T_Q4_K: embed_kernel<T_Q4_K><<<grid, 256, 0, st>>>(c->embd, tok, c->x, dim, V, err); break;
+    case T_Q5_K: embed_kernel<T_Q5_K><<<grid, 256, 0, st>>>(c->embd, tok, c->x, dim, V, err); break;
+    case T_Q6_K: embed_kernel<T_Q6_K><<<grid, 256, 0, st>>>(c->embd, tok, c->x, dim, V, err); break;
+    case T_F16: embed_kernel<T_F16><<<grid, 256, 0, st>>>(c->embd, tok, c->x, dim, V, err); break;
+    case T_F32: embed_kernel<T_F32><<<grid, 256, 0, st>>>(c->embd, tok, c->x, dim, V, err); break;
+    default: return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+}
+
+static cudaError_t enqueue_lm_head(gpu_context *c, bool loop, cudaStream_t st) {
+    GemvParams p = one_seg(c->out, c->t_out, (int)c->p.vocab_size, 0, (int)c->p.dim);
+    p.x = c->x;
+    p.norm_w = c->out_norm;
+    p.eps = c->p.rms_norm_eps;
+    p.y = c->logits;
+    p.am_part = c->am_part;
+    p.am_count = c->am_cnt;
+    p.am_out = &c->io->argmax;
+    if (loop) {
+        p.adv_token = &c->io->token;
+        p.adv_pos = &c->io->pos;
+        p.rec_tokens = c->rec;
+        p.rec_step = &c->io->step;
+    }
+    return launch_gemv<EPI_ARGMAX>(c->t_out, p, grid_of(p), st);
+}
+
+// Enqueue one full decode step. `loop` makes the lm_head feed its argmax back as
+// the next token and advance the position (device-resident greedy decoding).
+static cudaError_t enqueue_step(gpu_context *c, const kv_cache_t *kv, bool loop, cudaStream_t st, Prof *pf) {
+    const model_params_t &p = c->p;
+    const int dim = p.dim, ffn = p.ffn_dim;
+    cudaError_t e;
+    if ((e = launch_embed(c, st)) != cudaSuccess) return e;
+    AttnParams a;
+    memset(&a, 0, sizeof(a));
+    a.qkv = c->qkv;
+    a.rope = c->rope;
+    a.k_pool = kv->k_pool;
+    a.v_pool = kv->v_pool;
+    a.page_table = kv->page_table;
+    a.pos_ptr = &c->io->pos;
+    a.part = c->att_part;
+    a.count = c->att_cnt;
+    a.out = c->att;
+    a.n_layers = p.n_layers;
+    a.n_kv = p.n_kv_heads;
+    a.n_heads = p.n_heads;
+    a.max_chunks = c->max_chunks;
+    a.max_seq = c->max_seq < kv->max_seq ? c->max_seq : kv->max_seq;
+    a.scale = 1.0f / sqrtf((float)p.head_dim);
+    a.err = &c->io->err;
+    for (uint32_t l = 0; l < p.n_layers; l++) {
+        const LayerDev &d = c->L[l];
+        if (pf) pf->begin(K_GEMV);
+        if ((e = enqueue_qkv(c, d, st)) != cudaSuccess) return e;
+        if (pf) pf->end();
+        a.layer = l;
+        if (pf) pf->begin(K_ATTN);
+        if ((e = launch_attn(c, a, st)) != cudaSuccess) return e;
+        if (pf) pf->end();
+        GemvParams wo = one_seg(d.wo, d.to, dim, 0, dim);
+        wo.x = c->att;
+        wo.resid = c->x;
+        if (pf) pf->begin(K_GEMV);
+        if ((e = launch_gemv<EPI_RESID>(d.to, wo, grid_of(wo), st)) != cudaSuccess) return e;
+        GemvParams up = one_seg(d.w1, d.t1, ffn, 0, dim);
+        up.w_up = d.w3;
+        up.x = c->x;
+        up.norm_w = d.ffn_norm;
+        up.eps = p.rms_norm_eps;
+        up.y = c->h;
+        if ((e = launch_gemv<EPI_SWIGLU>(d.t1, up, grid_of(up), st)) != cudaSuccess) return e;
+        GemvParams dn = one_seg(d.w2, d.t2, dim, 0, ffn);
+        dn.x = c->h;
+        dn.resid = c->x;
+        if ((e = launch_gemv<EPI_RESID>(d.t2, dn, grid_of(dn), st)) != cudaSuccess) return e;
+        if (pf) pf->end();
+    }
+    if (pf) pf->begin(K_LM);
+    e = enqueue_lm_head(c, loop, st);
+    if (pf) pf->end();
+    return e;
+}
+
+static int get_graph(gpu_context *c, const kv_cache_t *kv, bool loop, cudaGraphExec_t *out) {
+    Graph &g = loop ? c->g_loop : c->g_step;
+    if (g.exec && g.kv == kv) {
+        *out = g.exec;
+        return FIBER_OK;
+    }
+    free_graph(g);
+    cudaGraph_t graph;
+    CK(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
+    cudaError_t e = enqueue_step(c, kv, loop, c->stream, nullptr);
+    cudaError_t e2 = cudaStreamEndCapture(c->stream, &graph);
+    if (e != cudaSuccess) return set_err(FIBER_ECUDA, "capturing the decode step: %s", cudaGetErrorString(e));
+    if (e2 != cudaSuccess) return set_err(FIBER_ECUDA, "end capture: %s", cudaGetErrorString(e2));
+    e = cudaGraphInstantiate(&g.exec, graph, 0);
+    cudaGraphDestroy(graph);
+    if (e != cudaSuccess) return set_err(FIBER_ECUDA, "graph instantiate: %s", cudaGetErrorString(e));
+    g.kv = kv;
+    *out = g.exec;
+    return FIBER_OK;
+}
+
+static int check_kv(gpu_context *c, const kv_cache_t *kv) {
+    if (!kv) return set_err(FIBER_EARG, "no KV cache");
+    if (kv->device != c->device || kv->n_layers != (int)c->p.n_layers || kv->n_kv_heads != (int)c->p.n_kv_heads ||
+        kv->head_dim != (int)c->p.head_dim || kv->page_size != ATTN_P)
+        return set_err(FIBER_EARG, "KV cache does not match the model/device");
+    return FIBER_OK;
+}
+
+static int device_status(gpu_context *c) {
+    if (c->h_io->err == 1) return set_err(FIBER_EARG, "position out of range on the device");
+    if (c->h_io->err == 2) return set_err(FIBER_EARG, "token id out of range on the device");
+    return FIBER_OK;
+}
+
+extern "C" int fiber_forward_token(fiber_ctx_t *c, kv_cache_t *kv, const int32_t *tokens, const int32_t *pos,
+                                   int batch, float *logits_or_null, int32_t *argmax_or_null) {
+    if (!c || !tokens || !pos) return set_err(FIBER_EARG, "fiber_forward_token: null argument");
+    if (batch != 1) return set_err(FIBER_EUNSUPPORTED, "fiber_forward_token: batch %d (only 1 is implemented)", batch);
+    int rc = check_kv(c, kv);
+    if (rc) return rc;
+    const int lim = c->max_seq < kv->max_seq ? c->max_seq : kv->max_seq;
+    if (pos[0] < 0 || pos[0] >= lim) return set_err(FIBER_EARG, "position %d outside [0, %d)", pos[0], lim);
+    if (tokens[0] < 0 || tokens[0] >= (int)c->p.vocab_size) return set_err(FIBER_EARG, "token %d out of range", tokens[0]);
+    CK(cudaSetDevice(c->device));
+    cudaGraphExec_t g;
+    if ((rc = get_graph(c, kv, false, &g)) != FIBER_OK) return rc;
+    c->h_io->token = tokens[0];
+    c->h_io->pos = pos[0];
+    c->h_io->err = 0;
+    CK(cudaMemcpyAsync(c->io, c->h_io, sizeof(StepIO), cudaMemcpyHostToDevice, c->stream));
+    CK(cudaGraphLaunch(g, c->stream));
+    if (logits_or_null)
+        CK(cudaMemcpyAsync(c->h_logits, c->logits, (size_t)c->p.vocab_size * 4, cudaMemcpyDeviceToHost, c->stream));
+    CK(cudaMemcpyAsync(c->h_io, c->io, sizeof(StepIO), cudaMemcpyDeviceToHost, c->stream));
+    CK(cudaStreamSynchronize(c->stream));
+    if ((rc = device_status(c)) != FIBER_OK) return rc;
+    if (logits_or_null) memcpy(logits_or_null, c->h_logits, (size_t)c->p.vocab_size * 4);
+    if (argmax_or_null) argmax_or_null[0] = c->h_io->argmax;
+    return FIBER_OK;
+}
+
+extern "C" int fiber_prefill(fiber_ctx_t *c, kv_cache_t *kv, const int32_t *tokens, int n, int start_pos,
+                             int32_t *argmax_out) {
+    if (!c || !tokens || n <= 0) return set_err(FIBER_EARG, "fiber_prefill: empty prompt");
+    for (int i = 0; i < n; i++) {
+        const int32_t pos = start_pos + i;
+        int rc = fiber_forward_token(c, kv, tokens + i, &pos, 1, nullptr, i == n - 1 ? argmax_out : nullptr);
+        if (rc) return rc;
+    }
+    return FIBER_OK;
+}
+
+static void prof_account(gpu_context *c, Prof &pf, const kv_cache_t *kv, int pos) {
+    (void)kv;
+    for (int i = 0; i < pf.n; i++) {
+        float ms = 0.f;
+        cudaEventElapsedTime(&ms, pf.ev[2 * i], pf.ev[2 * i + 1]);
+        c->prof_ms[pf.kind[i]] += ms;
+    }
+    pf.n = 0;
+    // algorithmic bytes of this step
+    const model_params_t &p = c->p;
+    double w = 0.0;
+    for (uint32_t l = 0; l < p.n_layers; l++) {
+        const LayerDev &d = c->L[l];
+        auto mb = [&](int t, double rows, double cols) { return rows * cols / 256.0 * block_bytes(t); };
+        w += mb(d.tq, p.dim, p.dim) + mb(d.tk, c->kvd, p.dim) + mb(d.tv, c->kvd, p.dim) + mb(d.to, p.dim, p.dim) +
+             mb(d.t1, p.ffn_dim, p.dim) + mb(d.t3, p.ffn_dim, p.dim) + mb(d.t2, p.dim, p.ffn_dim);
+        w += 4.0 * (2 * p.dim) * 2 + 4.0 * (p.dim + 2 * c->kvd) + 4.0 * p.dim * 3 + 4.0 * p.ffn_dim * 2;  // norms + vectors
+    }
+    c->prof_bytes[K_GEMV] += w;
+    c->prof_bytes[K_ATTN] += (double)p.n_layers * 2.0 * c->kvd * 2.0 * (pos + 1);
+    c->prof_bytes[K_LM] += (double)p.vocab_size * p.dim / 256.0 * block_bytes(c->t_out) + 4.0 * p.vocab_size;
+    c->prof_steps++;
+}
+
+extern "C" int fiber_step_launches(fiber_ctx_t *c) {
+    if (!c) return set_err(FIBER_EARG, "no context");
+    int n = 2;  // embed + lm_head
+    for (const LayerDev &d : c->L) n += 4 + 1 + (d.tk != d.tq) + (d.tv != d.tk);
+    return n;
+}
+
+extern "C" int fiber_set_profile(fiber_ctx_t *c, int enable) {
+    if (!c) return set_err(FIBER_EARG, "no context");
+    c->profile = enable;
+    memset(c->prof_ms, 0, sizeof(c->prof_ms));
+    memset(c->prof_bytes, 0, sizeof(c->prof_bytes));
+    c->prof_steps = 0;
+    return FIBER_OK;
+}
+
+extern "C" int fiber_profile_get(fiber_ctx_t *c, int kind, double *ms, double *bytes) {
+    if (!c || kind < 0 || kind > 2) return set_err(FIBER_EARG, "fiber_profile_get: bad kind");
+    const double n = c->prof_steps > 0 ? c->prof_steps : 1;
+    if (ms) *ms = c->prof_ms[kind] / n;
+    if (bytes) *bytes = c->prof_bytes[kind] / n;
+    return FIBER_OK;
+}
+
+extern "C" int fiber_decode_greedy(fiber_ctx_t *c, kv_cache_t *kv, int32_t first_token, int start_pos, int n_steps,
+                                   int32_t *h_tokens_out, float *ms_out) {
+    if (!c || n_steps <= 0) return set_err(FIBER_EARG, "fiber_decode_greedy: bad arguments");
+    int rc = check_kv(c, kv);
+    if (rc) return rc;
+    const int lim = c->max_seq < kv->max_seq ? c->max_seq : kv->max_seq;
+    if (start_pos < 0 || start_pos + n_steps > lim)
+        return set_err(FIBER_EARG, "decode of %d steps from %d exceeds max_seq %d", n_steps, start_pos, lim);
+    if (first_token < 0 || first_token >= (int)c->p.vocab_size) return set_err(FIBER_EARG, "token %d out of range", first_token);
+    CK(cudaSetDevice(c->device));
+    c->h_io->token = first_token;
+    c->h_io->pos = start_pos;
+    c->h_io->step = 0;
+    c->h_io->err = 0;
+    CK(cudaMemcpyAsync(c->io, c->h_io, sizeof(StepIO), cudaMemcpyHostToDevice, c->stream));
+    if (c->profile) {
+        Prof pf;
+        pf.c = c;
+        for (int i = 0; i < n_steps; i++) {
+            cudaError_t e = enqueue_step(c, kv, true, c->stream, &pf);
+            if (e != cudaSuccess) return set_err(FIBER_ECUDA, "profiled step: %s", cudaGetErrorString(e));
+            CK(cudaStreamSynchronize(c->stream));
+            prof_account(c, pf, kv, start_pos + i);
+        }
+        if (ms_out) *ms_out = 0.f;
+    } else {
+        cudaGraphExec_t g;
+        if ((rc = get_graph(c, kv, true, &g)) != FIBER_OK) return rc;
+        CK(cudaEventRecord(c->ev0, c->stream));
+        for (int i = 0; i < n_steps; i++) CK(cudaGraphLaunch(g, c->stream));
+        CK(cudaEventRecord(c->ev1, c->stream));
+        CK(cudaEventSynchronize(c->ev1));
+        if (ms_out) CK(cudaEventElapsedTime(ms_out, c->ev0, c->ev1));
+    }
+    CK(cudaMemcpyAsync(c->h_io, c->io, sizeof(StepIO), cudaMemcpyDeviceToHost, c->stream));
+    if (h_tokens_out) CK(cudaMemcpyAsync(h_tokens_out, c->rec, (size_t)n_steps * 4, cudaMemcpyDeviceToHost, c->stream));
+    CK(cudaStreamSynchronize(c->stream));
+    return device_status(c);
+}
+
+// ---- reference-named API (include/gpu_ffn.h) --------------------------------------------
+
+extern "C" gpu_context_t *gpu_init(const model_t *m) {
+    gpu_context_t *c = fiber_cuda_init(m, 0, 1, m ? (int)m->params.context_length : 0);
+    if (c) {
+        cudaDeviceProp prop;
+        if (cudaGetDeviceProperties(&prop, 0) == cudaSuccess) printf("GPU: %s\n", prop.name);
+        printf("GPU: %.1f MB of GGUF tensor data resident in HBM\n", c->data_bytes / (1024.0 * 1024.0));
+    }
+    return c;
+}
+
+extern "C" void gpu_free(gpu_context_t *c) { fiber_cuda_free(c); }
+
+extern "C" void gpu_embed(gpu_context_t *c, const model_t *m, int token_id) {
+    (void)m;
+    if (c) c->h_io->token = token_id;
+}
+
+extern "C" double gpu_forward_token(gpu_context_t *c, const model_t *m, kv_cache_t *kv, int pos) {
+    (void)m;
+    if (!c) return -1.0;
+    struct timespec t0, t1;
+    clock_gettime(CLOCK_MONOTONIC, &t0);
+    const int32_t tok = c->h_io->token, p = pos;
+    const int rc = fiber_forward_token(c, kv, &tok, &p, 1, c->logits_copy.data(), nullptr);
+    clock_gettime(CLOCK_MONOTONIC, &t1);
+    if (rc != FIBER_OK) {
+        fprintf(stderr, "gpu_forward_token: %s\n", g_err);
+        return -1.0;
+    }
+    return (t1.tv_sec - t0.tv_sec) * 1e3 + (t1.tv_nsec - t0.tv_nsec) / 1e6;
+}
+
+extern "C" const float *gpu_get_logits(gpu_context_t *c) { return c ? c->logits_copy.data() : nullptr; }
+
+extern "C" void gpu_forward_classifier(gpu_context_t *c, const model_t *m) {
+    (void)m;
+    if (!c) return;
+    if (cudaSetDevice(c->device) != cudaSuccess || enqueue_lm_head(c, false, c->stream) != cudaSuccess ||
+        cudaMemcpyAsync(c->logits_copy.data(), c->logits, (size_t)c->p.vocab_size * 4, cudaMemcpyDeviceToHost,
+                        c->stream) != cudaSuccess ||
+        cudaStreamSynchronize(c->stream) != cudaSuccess)
+        fprintf(stderr, "gpu_forward_classifier: CUDA error\n");
+}
+
+extern "C" int gpu_get_device(gpu_context_t *c) { return c ? c->device : -1; }
+
+// ---- kernel-level entry points -----------------------------------------------------------
+
+extern "C" int fiber_gemv(int type, const void *d_w, const float *d_x, float *d_y, int rows, int cols, void *stream) {
+    if (!matrix_type_ok(type)) return set_err(FIBER_EARG, "fiber_gemv: type %d not supported", type);
+    if (!d_w || !d_x || !d_y || rows <= 0 || cols <= 0 || cols % 256)
+        return set_err(FIBER_EARG, "fiber_gemv: bad shape %dx%d (cols must be a positive multiple of 256)", rows, cols);
+    if (((uintptr_t)d_w & 15) || ((uintptr_t)d_x & 15))
+        return set_err(FIBER_EARG, "fiber_gemv: weights and x must be 16-byte aligned");
+    GemvParams p = one_seg((const uint8_t *)d_w, type, rows, 0, cols);
+    p.x = d_x;
+    p.y = d_y;
+    CK(launch_gemv<EPI_STORE>(type, p, grid_of(p), (cudaStream_t)stream));
+    return FIBER_OK;
+}
+
+extern "C" int fiber_gemv_host(int type, const void *d_w, const float *h_x, float *h_y, int rows, int cols,
+                               float *d_x, float *d_y, void *stream) {
+    cudaStream_t st = (cudaStream_t)stream;
+    CK(cudaMemcpyAsync(d_x, h_x, (size_t)cols * 4, cudaMemcpyHostToDevice, st));
+    int rc = fiber_gemv(type, d_w, d_x, d_y, rows, cols, stream);
+    if (rc) return rc;
+    CK(cudaMemcpyAsync(h_y, d_y, (size_t)rows * 4, cudaMemcpyDeviceToHost, st));
+    CK(cudaStreamSynchronize(st));
+    return FIBER_OK;
+}
+
+extern "C" int fiber_dequant(int type, const void *d_w, void *d_out, int rows, int cols, void *stream) {
+    if (!matrix_type_ok(type) || !d_w || !d_out || rows <= 0 || cols <= 0 || cols % 256)
+        return set_err(FIBER_EARG, "fiber_dequant: bad arguments");
+    cudaStream_t st = (cudaStream_t)stream;
+    const int grid = 148 * 8;
+    const uint8_t *w = (const uint8_t *)d_w;
+    switch (type) {
+    case T_Q4_K: dequant_kernel<T_Q4_K><<<grid, 256, 0, st>>>(w, d_out, rows, cols); break;
+    case T_Q5_K: dequant_kernel<T_Q5_K><<<grid, 256, 0, st>>>(w, d_out, rows, cols); break;
+    case T_Q6_K: dequant_kernel<T_Q6_K><<<grid, 256, 0, st>>>(w, d_out, rows, cols); break;
+    case T_F16: dequant_kernel<T_F16><<<grid, 256, 0, st>>>(w, d_out, rows, cols); break;
+    }
+    CK(cudaGetLastError());
+    return FIBER_OK;
+}

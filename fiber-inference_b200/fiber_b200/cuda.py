@@ -1,2 +1,212 @@
-"""Device API bindings (filled in with libfiber_cuda.so)."""
-__all__ = []
+"""ctypes bindings of libfiber_cuda.so (include/fiber_cuda.h, gpu_ffn.h, kv_cache.h).
+
+Device buffers handed to the kernel-level calls are plain device addresses
+(e.g. ``torch.Tensor.data_ptr()``); the model-level calls own their memory.
+Every call raises ``FiberError`` with ``fiber_last_error()`` on a non-zero status.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+from . import CUDA_SO, ModelParams  # noqa: F401
+
+__all__ = ["FiberError", "cuda_lib", "cuda_available", "gemv", "gemv_host", "dequant", "Context", "KVCache",
+           "device_count"]
+
+F32P = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
+I32P = np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS")
+
+EXPORTED = [
+    "fiber_last_error", "fiber_device_count", "fiber_cuda_init", "fiber_cuda_free", "fiber_forward_token",
+    "fiber_prefill", "fiber_decode_greedy", "fiber_step_launches", "fiber_set_profile", "fiber_profile_get", "fiber_gemv",
+    "fiber_dequant", "fiber_gemv_host", "gpu_init", "gpu_free", "gpu_embed", "gpu_forward_token",
+    "gpu_get_logits", "gpu_forward_classifier", "gpu_get_device", "kv_cache_init", "kv_cache_init_paged",
+    "kv_cache_free", "kv_cache_write", "kv_cache_read",
+]
+
+
+class FiberError(RuntimeError):
+    pass
+
+
+class KVCacheT(C.Structure):
+    _fields_ = [("n_layers", C.c_int), ("n_kv_heads", C.c_int), ("head_dim", C.c_int), ("max_seq", C.c_int),
+                ("device", C.c_int), ("max_batch", C.c_int), ("page_size", C.c_int),
+                ("max_pages_per_seq", C.c_int), ("n_pages", C.c_int), ("k_pool", C.c_void_p),
+                ("v_pool", C.c_void_p), ("page_table", C.c_void_p)]
+
+
+_cuda = None
+
+
+def cuda_lib() -> C.CDLL:
+    """Load libfiber_cuda.so (no GPU needed to load it)."""
+    global _cuda
+    if _cuda is None:
+        if not os.path.exists(CUDA_SO):
+            raise FiberError(f"{CUDA_SO} missing: run `make -C fiber-inference_b200 cuda`")
+        L = C.CDLL(CUDA_SO)
+        L.fiber_last_error.restype = C.c_char_p
+        L.fiber_cuda_init.restype = C.c_void_p
+        L.fiber_cuda_init.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int]
+        L.fiber_cuda_free.argtypes = [C.c_void_p]
+        L.fiber_forward_token.argtypes = [C.c_void_p, C.c_void_p, I32P, I32P, C.c_int, C.c_void_p, C.c_void_p]
+        L.fiber_prefill.argtypes = [C.c_void_p, C.c_void_p, I32P, C.c_int, C.c_int, C.c_void_p]
+        L.fiber_decode_greedy.argtypes = [C.c_void_p, C.c_void_p, C.c_int32, C.c_int, C.c_int, C.c_void_p,
+                                          C.c_void_p]
+        L.fiber_step_launches.argtypes = [C.c_void_p]
+        L.fiber_set_profile.argtypes = [C.c_void_p, C.c_int]
+        L.fiber_profile_get.argtypes = [C.c_void_p, C.c_int, C.POINTER(C.c_double), C.POINTER(C.c_double)]
+        L.fiber_gemv.argtypes = [C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p]
+        L.fiber_gemv_host.argtypes = [C.c_int, C.c_void_p, F32P, F32P, C.c_int, C.c_int, C.c_void_p, C.c_void_p,
+                                      C.c_void_p]
+        L.fiber_dequant.argtypes = [C.c_int, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p]
+        L.kv_cache_init.restype = C.POINTER(KVCacheT)
+        L.kv_cache_init.argtypes = [C.c_int] * 5
+        L.kv_cache_init_paged.restype = C.POINTER(KVCacheT)
+        L.kv_cache_init_paged.argtypes = [C.c_int] * 7
+        L.kv_cache_free.argtypes = [C.c_void_p]
+        L.kv_cache_write.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, F32P, F32P]
+        L.kv_cache_read.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, F32P, F32P]
+        L.gpu_init.restype = C.c_void_p
+        L.gpu_init.argtypes = [C.c_void_p]
+        L.gpu_free.argtypes = [C.c_void_p]
+        L.gpu_embed.argtypes = [C.c_void_p, C.c_void_p, C.c_int]
+        L.gpu_forward_token.restype = C.c_double
+        L.gpu_forward_token.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int]
+        L.gpu_get_logits.restype = C.POINTER(C.c_float)
+        L.gpu_get_logits.argtypes = [C.c_void_p]
+        L.gpu_forward_classifier.argtypes = [C.c_void_p, C.c_void_p]
+        L.gpu_get_device.argtypes = [C.c_void_p]
+        _cuda = L
+    return _cuda
+
+
+def _check(rc: int, what: str):
+    if rc != 0:
+        raise FiberError(f"{what}: {cuda_lib().fiber_last_error().decode()} (status {rc})")
+
+
+def device_count() -> int:
+    return int(cuda_lib().fiber_device_count())
+
+
+def cuda_available() -> bool:
+    try:
+        return device_count() > 0
+    except (OSError, FiberError):
+        return False
+
+
+def _stream_ptr(stream) -> int | None:
+    if stream is None:
+        return None
+    return int(getattr(stream, "cuda_stream", stream))
+
+
+def gemv(ggml_type: int, d_w: int, d_x: int, d_y: int, rows: int, cols: int, stream=None):
+    _check(cuda_lib().fiber_gemv(ggml_type, d_w, d_x, d_y, rows, cols, _stream_ptr(stream)), "fiber_gemv")
+
+
+def gemv_host(ggml_type: int, d_w: int, x: np.ndarray, y: np.ndarray, rows: int, cols: int, d_x: int, d_y: int,
+              stream=None):
+    _check(cuda_lib().fiber_gemv_host(ggml_type, d_w, x, y, rows, cols, d_x, d_y, _stream_ptr(stream)),
+           "fiber_gemv_host")
+
+
+def dequant(ggml_type: int, d_w: int, d_out: int, rows: int, cols: int, stream=None):
+    _check(cuda_lib().fiber_dequant(ggml_type, d_w, d_out, rows, cols, _stream_ptr(stream)), "fiber_dequant")
+
+
+class KVCache:
+    def __init__(self, device: int, n_layers: int, n_kv_heads: int, head_dim: int, max_seq: int):
+        self.ptr = cuda_lib().kv_cache_init(device, n_layers, n_kv_heads, head_dim, max_seq)
+        if not self.ptr:
+            raise FiberError(f"kv_cache_init: {cuda_lib().fiber_last_error().decode()}")
+        self.s = self.ptr.contents
+
+    @property
+    def addr(self) -> int:
+        return C.cast(self.ptr, C.c_void_p).value
+
+    def close(self):
+        if self.ptr:
+            cuda_lib().kv_cache_free(self.addr)
+            self.ptr = None
+
+    __del__ = close
+
+    def write(self, layer: int, pos: int, k: np.ndarray, v: np.ndarray, slot: int = 0):
+        k = np.ascontiguousarray(k, np.float32)
+        v = np.ascontiguousarray(v, np.float32)
+        n = k.shape[0] if k.ndim == 2 else 1
+        _check(cuda_lib().kv_cache_write(self.addr, slot, layer, pos, n, k, v), "kv_cache_write")
+
+    def read(self, layer: int, pos: int, n: int, slot: int = 0):
+        kvd = self.s.n_kv_heads * self.s.head_dim
+        k = np.empty((n, kvd), np.float32)
+        v = np.empty((n, kvd), np.float32)
+        _check(cuda_lib().kv_cache_read(self.addr, slot, layer, pos, n, k, v), "kv_cache_read")
+        return k, v
+
+
+class Context:
+    """fiber_cuda_init over a host model (fiber_b200.HostModel)."""
+
+    def __init__(self, host_model, device: int = 0, max_seq: int = 0):
+        self.model = host_model
+        self.p = host_model.params
+        self.h = cuda_lib().fiber_cuda_init(host_model.h, device, 1, max_seq)
+        if not self.h:
+            raise FiberError(f"fiber_cuda_init: {cuda_lib().fiber_last_error().decode()}")
+        self.device = device
+        self.max_seq = max_seq or self.p.context_length
+
+    def close(self):
+        if self.h:
+            cuda_lib().fiber_cuda_free(self.h)
+            self.h = None
+
+    __del__ = close
+
+    def kv(self, max_seq: int | None = None) -> KVCache:
+        return KVCache(self.device, self.p.n_layers, self.p.n_kv_heads, self.p.head_dim, max_seq or self.max_seq)
+
+    def forward(self, kv: KVCache, token: int, pos: int, want_logits: bool = True):
+        lg = np.empty(self.p.vocab_size, np.float32) if want_logits else None
+        am = np.zeros(1, np.int32)
+        _check(cuda_lib().fiber_forward_token(self.h, kv.addr, np.array([token], np.int32),
+                                              np.array([pos], np.int32), 1,
+                                              lg.ctypes.data if lg is not None else None, am.ctypes.data),
+               "fiber_forward_token")
+        return int(am[0]), lg
+
+    def prefill(self, kv: KVCache, tokens, start_pos: int = 0) -> int:
+        t = np.ascontiguousarray(tokens, np.int32)
+        am = np.zeros(1, np.int32)
+        _check(cuda_lib().fiber_prefill(self.h, kv.addr, t, len(t), start_pos, am.ctypes.data), "fiber_prefill")
+        return int(am[0])
+
+    def decode_greedy(self, kv: KVCache, first_token: int, start_pos: int, n_steps: int):
+        out = np.zeros(n_steps, np.int32)
+        ms = C.c_float(0.0)
+        _check(cuda_lib().fiber_decode_greedy(self.h, kv.addr, int(first_token), int(start_pos), int(n_steps),
+                                              out.ctypes.data, C.addressof(ms)), "fiber_decode_greedy")
+        return out, float(ms.value)
+
+    def step_launches(self) -> int:
+        n = cuda_lib().fiber_step_launches(self.h)
+        if n < 0:
+            _check(n, "fiber_step_launches")
+        return int(n)
+
+    def set_profile(self, enable: bool):
+        _check(cuda_lib().fiber_set_profile(self.h, int(enable)), "fiber_set_profile")
+
+    def profile(self, kind: int):
+        ms, b = C.c_double(), C.c_double()
+        _check(cuda_lib().fiber_profile_get(self.h, kind, C.byref(ms), C.byref(b)), "fiber_profile_get")
+        return ms.value, b.value

@@ -1,0 +1,97 @@
+/* fiber_cuda.h — extern "C" API of libfiber_cuda.so beyond the reference's names.
+ *
+ * Conventions: plain pointers and sizes; `stream` is a cudaStream_t passed as
+ * void* (NULL = the default stream); "d_" pointers are device memory, "h_"
+ * pointers host memory. Every function returns FIBER_OK (0) or a negative
+ * FIBER_E* code and never exits; fiber_last_error() describes the last failure
+ * on the calling thread. One host thread per context; all device work of a
+ * context runs on its own stream.
+ *
+ * Numerics (identical on every path): K-quant weights are decoded exactly as
+ * the reference's CPU dequantizer does it (src/dequant.h:9-58: fp32 products,
+ * one rounding to fp16) -- Q5_K as the reference's Metal kernel does
+ * (metal/kernels.metal:141-169, fp32) -- activations and accumulation are fp32,
+ * the KV cache is fp16.
+ */
+#ifndef FIBER_CUDA_H
+#define FIBER_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include "gpu_ffn.h"
+#include "kv_cache.h"
+#include "model.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FIBER_OK 0
+#define FIBER_EARG (-1)         /* bad argument / unsupported shape or type */
+#define FIBER_ECUDA (-2)        /* CUDA runtime error */
+#define FIBER_ENOMEM (-3)       /* device or pinned allocation failed */
+#define FIBER_EUNSUPPORTED (-4) /* model feature the kernels do not cover */
+#define FIBER_ETIMEOUT (-5)     /* a bounded device-side wait gave up */
+
+const char *fiber_last_error(void);
+int fiber_device_count(void);
+
+/* ---- model-level decode (batch-1 greedy loop of src/main.m:553-586) ---------- */
+
+typedef struct gpu_context fiber_ctx_t;
+
+/* Upload the GGUF data section unchanged to `device`, resolve per-layer device
+ * pointers once, allocate activations and scratch for up to max_seq positions.
+ * (gpu_init equivalent, src/gpu_ffn.m:141-204.) max_batch must be 1. */
+fiber_ctx_t *fiber_cuda_init(const model_t *m, int device, int max_batch, int max_seq);
+void fiber_cuda_free(fiber_ctx_t *ctx);
+
+/* One decode step for `batch` sequences (batch must be 1): embeds tokens[i] at
+ * position pos[i] (host arrays), runs all layers and the classifier, then, if
+ * non-NULL, copies the fp32 logits [batch][vocab] and the greedy argmax
+ * (lowest index on ties, src/sampler.c:38-46) to host memory. Blocks until done. */
+int fiber_forward_token(fiber_ctx_t *ctx, kv_cache_t *kv, const int32_t *tokens,
+                        const int32_t *pos, int batch, float *logits_or_null,
+                        int32_t *argmax_or_null);
+
+/* Prompt of n tokens at positions start_pos.. (token by token through the same
+ * decode step); *argmax_out (optional) gets the greedy token after the last one. */
+int fiber_prefill(fiber_ctx_t *ctx, kv_cache_t *kv, const int32_t *tokens, int n, int start_pos,
+                  int32_t *argmax_out);
+
+/* Device-resident greedy loop: n_steps decode steps starting with first_token at
+ * start_pos; each step's argmax feeds the next on the device (one graph replay
+ * per step, no host round trip). h_tokens_out[i] = argmax of step i. If ms_out
+ * is non-NULL it receives the device time of the n_steps replays (CUDA events
+ * on the context stream). */
+int fiber_decode_greedy(fiber_ctx_t *ctx, kv_cache_t *kv, int32_t first_token, int start_pos,
+                        int n_steps, int32_t *h_tokens_out, float *ms_out);
+
+/* Number of kernels one decode step launches (all of them this library's own). */
+int fiber_step_launches(fiber_ctx_t *ctx);
+
+/* Average device time per launch of the dominant decode kernel kind during the
+ * last fiber_decode_greedy call with profiling enabled (see fiber_set_profile). */
+int fiber_set_profile(fiber_ctx_t *ctx, int enable);
+/* kind: 0 = all quantized GEMVs of a step, 1 = attention, 2 = lm_head.
+ * *ms = summed device time of that kind per step; *bytes = its algorithmic bytes per step. */
+int fiber_profile_get(fiber_ctx_t *ctx, int kind, double *ms, double *bytes);
+
+/* ---- kernel-level entry points (device pointers) -------------------------------- */
+
+/* y[r] = sum_k W[r,k] * x[k] for rows x cols weights in GGUF layout
+ * (ggml_type Q4_K / Q5_K / Q6_K / F16; cols % 256 == 0), fp32 x and y. */
+int fiber_gemv(int ggml_type, const void *d_w, const float *d_x, float *d_y, int rows, int cols,
+               void *stream);
+/* Decoded weights: fp16 bits for Q4_K/Q6_K/F16, fp32 for Q5_K, [rows][cols]. */
+int fiber_dequant(int ggml_type, const void *d_w, void *d_out, int rows, int cols, void *stream);
+/* Same GEMV with host buffers: copies x in and y out around the launch on the
+ * given stream and synchronizes (d_w stays resident). */
+int fiber_gemv_host(int ggml_type, const void *d_w, const float *h_x, float *h_y, int rows,
+                    int cols, float *d_x_scratch, float *d_y_scratch, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif
