@@ -49,6 +49,11 @@ static int set_err(int code, const char *fmt, ...) {
 
 extern "C" const char *fiber_last_error(void) { return g_err; }
 
+// lets the other translation units of this library report through fiber_last_error()
+__attribute__((visibility("hidden"))) void fiber_set_error_message(const char *msg) {
+    snprintf(g_err, sizeof(g_err), "%s", msg);
+}
+
 extern "C" int fiber_device_count(void) {
     int n = 0;
     if (cudaGetDeviceCount(&n) != cudaSuccess) return 0;

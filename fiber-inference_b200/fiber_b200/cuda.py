@@ -13,7 +13,7 @@ import numpy as np
 
 from . import CUDA_SO, ModelParams  # noqa: F401
 
-__all__ = ["FiberError", "cuda_lib", "cuda_available", "gemv", "gemv_host", "dequant", "Context", "KVCache",
+__all__ = ["FiberError", "cuda_lib", "cuda_available", "gemv", "gemv_host", "gemv_argmax_noalloc", "dequant", "Context", "KVCache",
            "device_count"]
 
 F32P = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
@@ -24,7 +24,7 @@ EXPORTED = [
     "fiber_prefill", "fiber_decode_greedy", "fiber_step_launches", "fiber_set_profile", "fiber_profile_get", "fiber_gemv",
     "fiber_dequant", "fiber_gemv_host", "gpu_init", "gpu_free", "gpu_embed", "gpu_forward_token",
     "gpu_get_logits", "gpu_forward_classifier", "gpu_get_device", "kv_cache_init", "kv_cache_init_paged",
-    "kv_cache_free", "kv_cache_write", "kv_cache_read",
+    "kv_cache_free", "kv_cache_write", "kv_cache_read", "fiber_gemv_argmax_noalloc",
 ]
 
 
@@ -64,6 +64,8 @@ def cuda_lib() -> C.CDLL:
         L.fiber_gemv_host.argtypes = [C.c_int, C.c_void_p, F32P, F32P, C.c_int, C.c_int, C.c_void_p, C.c_void_p,
                                       C.c_void_p]
         L.fiber_dequant.argtypes = [C.c_int, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p]
+        L.fiber_gemv_argmax_noalloc.argtypes = [C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int,
+                                                C.c_int, C.c_void_p]
         L.kv_cache_init.restype = C.POINTER(KVCacheT)
         L.kv_cache_init.argtypes = [C.c_int] * 5
         L.kv_cache_init_paged.restype = C.POINTER(KVCacheT)
@@ -115,6 +117,13 @@ def gemv_host(ggml_type: int, d_w: int, x: np.ndarray, y: np.ndarray, rows: int,
               stream=None):
     _check(cuda_lib().fiber_gemv_host(ggml_type, d_w, x, y, rows, cols, d_x, d_y, _stream_ptr(stream)),
            "fiber_gemv_host")
+
+
+def gemv_argmax_noalloc(ggml_type: int, d_w: int, d_x: int, d_y: int, d_argmax: int, rows: int, cols: int,
+                        stream=None):
+    """Greedy lm_head step whose scratch is a static device array (no allocation)."""
+    _check(cuda_lib().fiber_gemv_argmax_noalloc(ggml_type, d_w, d_x, d_y, d_argmax, rows, cols, _stream_ptr(stream)),
+           "fiber_gemv_argmax_noalloc")
 
 
 def dequant(ggml_type: int, d_w: int, d_out: int, rows: int, cols: int, stream=None):

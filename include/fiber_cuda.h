@@ -91,6 +91,26 @@ int fiber_dequant(int ggml_type, const void *d_w, void *d_out, int rows, int col
 int fiber_gemv_host(int ggml_type, const void *d_w, const float *h_x, float *h_y, int rows,
                     int cols, float *d_x_scratch, float *d_y_scratch, void *stream);
 
+/* ---- allocation-free greedy lm_head step ----------------------------------------
+ * No counterpart in the reference. Same result as fiber_gemv followed by a greedy
+ * argmax (first index of the maximum, src/sampler.c:38-46): d_y = W.x and
+ * *d_argmax, both device memory, enqueued on `stream`. It exists for callers that
+ * cannot allocate device memory where they run the step: a host application
+ * whose own pool owns all device memory and forbids further cudaMalloc, or a
+ * latency-critical loop that cannot accept cudaMalloc's implicit device
+ * synchronization. The kernel's cross-CTA scratch (one value/index pair per CTA
+ * and a merge ticket, about 128 KB) is a fixed static device array that every GPU
+ * loading this library holds until the process exits; the call makes no
+ * cudaMalloc, cudaFree or other allocating call. The first call on a device looks
+ * up the array's device address with that device current, so make that first
+ * call before any stream capture. Every call shares the array and it keeps the
+ * last call's contents; the ticket is cleared at the start of each call. Calls
+ * that overlap on the GPU (e.g. on two streams of one device) race on it.
+ * rows > FIBER_NOALLOC_MAX_ROWS returns FIBER_EARG. */
+#define FIBER_NOALLOC_MAX_ROWS 262144
+int fiber_gemv_argmax_noalloc(int ggml_type, const void *d_w, const float *d_x, float *d_y,
+                              int32_t *d_argmax, int rows, int cols, void *stream);
+
 #ifdef __cplusplus
 }
 #endif
