@@ -107,9 +107,11 @@ def prompt_ids(vocab: int) -> np.ndarray:
     return np.random.default_rng(SEED).integers(1, vocab, PROMPT_LEN).astype(np.int32)
 
 
-def gemv_bandwidth(device: int, n_launch: int = 2000):
+def gemv_bandwidth(device: int, n_launch: int = 400, reps: int = 5):
     """Single Q4_K GEMV 5632x2048 (random super-blocks), 40 rotating weight
-    copies (260 MB > L2); CUDA events on torch's stream."""
+    copies (260 MB > L2). The launches are captured once in a CUDA graph so the
+    timing (CUDA events on the capturing stream) sees the GPU, not the Python
+    launch loop."""
     import torch
 
     import fiber_b200 as fb
@@ -120,21 +122,28 @@ def gemv_bandwidth(device: int, n_launch: int = 2000):
     nb = blocks.size
     x = torch.from_numpy(fb.randn(cols, seed=7)).to(f"cuda:{device}")
     y = torch.empty(rows, dtype=torch.float32, device=f"cuda:{device}")
-    st = torch.cuda.current_stream(device)
     base = w.data_ptr()
-    for i in range(50):
-        fb.gemv(fb.GGML_Q4_K, base + (i % copies) * nb, x.data_ptr(), y.data_ptr(), rows, cols, st)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize(device)
-    e0.record(st)
-    for i in range(n_launch):
-        fb.gemv(fb.GGML_Q4_K, base + (i % copies) * nb, x.data_ptr(), y.data_ptr(), rows, cols, st)
-    e1.record(st)
-    e1.synchronize()
-    us = e0.elapsed_time(e1) * 1e3 / n_launch
+    st = torch.cuda.Stream(device)
+    with torch.cuda.stream(st):
+        for i in range(copies):
+            fb.gemv(fb.GGML_Q4_K, base + i * nb, x.data_ptr(), y.data_ptr(), rows, cols, st)
+        st.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=st):
+            for i in range(n_launch):
+                fb.gemv(fb.GGML_Q4_K, base + (i % copies) * nb, x.data_ptr(), y.data_ptr(), rows, cols, st)
+        g.replay()
+        st.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for _ in range(reps):
+            g.replay()
+        e1.record(st)
+        e1.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / (n_launch * reps)
     algo = rows * cols // 256 * 144 + cols * 4 + rows * 4
-    return {"workload": "Q4_K GEMV 5632x2048, x fp32, 40 rotating weight copies", "us_per_launch": us,
-            "algorithmic_bytes": algo, "gbs": algo / us / 1e3}
+    return {"workload": "Q4_K GEMV 5632x2048, x fp32, 40 rotating weight copies, graph of back-to-back launches",
+            "us_per_launch": us, "algorithmic_bytes": algo, "gbs": algo / us / 1e3}
 
 
 def cpu_reference_decode(path: str, budget_s: float, n_tokens_max: int):
@@ -188,6 +197,9 @@ def main():
     ap.add_argument("--impl", default="fiber", choices=["fiber", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=20.0)
+    ap.add_argument("--prompt-len", type=int, default=PROMPT_LEN, help="shorter runs for profiling only")
+    ap.add_argument("--decode-len", type=int, default=DECODE_LEN, help="shorter runs for profiling only")
+    ap.add_argument("--skip-extras", action="store_true", help="no single-GEMV, e2e or CPU legs (profiling)")
     args = ap.parse_args()
 
     rank = int(os.environ.get("RANK", "0"))
@@ -214,54 +226,57 @@ def main():
             dist.barrier()
         torch.cuda.synchronize(local)
 
+    P, D = args.prompt_len, args.decode_len
     path = MODEL_PATH if world == 1 else MODEL_PATH.replace(".gguf", f".r{rank}.gguf")
     make_model(path)
     hm = fb.HostModel(path)
     p = hm.params
-    ctx = fb.Context(hm, device=local, max_seq=PROMPT_LEN + DECODE_LEN)
-    kv = ctx.kv(PROMPT_LEN + DECODE_LEN)
-    prompt = prompt_ids(p.vocab_size)
+    ctx = fb.Context(hm, device=local, max_seq=P + D)
+    kv = ctx.kv(P + D)
+    prompt = prompt_ids(p.vocab_size)[:P]
     t0 = time.perf_counter()
     first = ctx.prefill(kv, prompt)
-    prefill_tps = PROMPT_LEN / (time.perf_counter() - t0)
+    prefill_tps = P / (time.perf_counter() - t0)
 
     ref_tokens = None
     for _ in range(args.warmup):
-        toks, _ = ctx.decode_greedy(kv, first, PROMPT_LEN, DECODE_LEN)
+        toks, _ = ctx.decode_greedy(kv, first, P, D)
         ref_tokens = toks if ref_tokens is None else ref_tokens
     barrier()
     ms_total, deterministic = 0.0, True
     with Clocks(local) as clk:
         wall0 = time.perf_counter()
         for _ in range(args.steps):
-            toks, ms = ctx.decode_greedy(kv, first, PROMPT_LEN, DECODE_LEN)
+            toks, ms = ctx.decode_greedy(kv, first, P, D)
             ms_total += ms
             if ref_tokens is not None and not np.array_equal(toks, ref_tokens):
                 deterministic = False
+            ref_tokens = toks if ref_tokens is None else ref_tokens
         barrier()
         wall = time.perf_counter() - wall0
     if dist is not None:
         t = torch.tensor([ms_total], device=f"cuda:{local}", dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms_total = float(t.item())
-    tokens_all = world * args.steps * DECODE_LEN
-    value = tokens_all / (ms_total / 1e3)
+    value = world * args.steps * D / (ms_total / 1e3)
 
-    # per-kernel profile pass (eager launches with CUDA events on the decode stream)
-    ctx.set_profile(True)
-    ctx.decode_greedy(kv, first, PROMPT_LEN, DECODE_LEN)
-    prof = {k: ctx.profile(i) for i, k in enumerate(["gemv", "attention", "lm_head"])}
-    ctx.set_profile(False)
+    # per-kernel device time: a graph of each kind's per-layer launches, CUDA events on the decode stream
+    mid = P + D // 2
+    kern = {}
+    for kind, name in enumerate(fb.Context.KINDS):
+        us, b = ctx.time_kernel(kv, kind, mid, reps=20)
+        kern[name] = {"us_per_launch": us, "bytes_per_launch": b, "gbs": b / us / 1e3}
 
-    # e2e through the public C call with host buffers, one step
-    barrier()
-    e0 = time.perf_counter()
-    tok = first
-    for i in range(DECODE_LEN):
-        tok, _ = ctx.forward(kv, tok, PROMPT_LEN + i, want_logits=False)
-    barrier()
-    e2e_s = time.perf_counter() - e0
-    e2e_val = world * DECODE_LEN / e2e_s
+    e2e_val = None
+    if not args.skip_extras:
+        # e2e through the public C call with host buffers, one step
+        barrier()
+        e0 = time.perf_counter()
+        tok = first
+        for i in range(D):
+            tok, _ = ctx.forward(kv, tok, P + i, want_logits=False)
+        barrier()
+        e2e_val = world * D / (time.perf_counter() - e0)
 
     if dist is not None:
         dist.barrier()
@@ -272,43 +287,41 @@ def main():
         return
 
     peak, peak_kind = peaks()
-    gemv_ms, gemv_bytes = prof["gemv"]
-    attn_ms, attn_bytes = prof["attention"]
-    lm_ms, lm_bytes = prof["lm_head"]
-    achieved = gemv_bytes / (gemv_ms / 1e3) / 1e9
-    weights_per_tok = gemv_bytes + lm_bytes
-    mean_kv = attn_bytes
-    step_bytes = weights_per_tok + mean_kv
-    single = gemv_bandwidth(local)
-    cpu = None
-    if world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_reference_decode(path, budget_s=args.cpu_seconds, n_tokens_max=400)
-    launches = ctx.step_launches() * DECODE_LEN * args.steps
+    L = p.n_layers
+    gemv_kinds = ["qkv", "wo", "gate_up", "down"]
+    dominant = max(gemv_kinds + ["attention", "lm_head"],
+                   key=lambda k: kern[k]["us_per_launch"] * (1 if k == "lm_head" else L))
+    dk = kern[dominant]
+    step_bytes = sum(kern[k]["bytes_per_launch"] * L for k in gemv_kinds + ["attention"]) + \
+        kern["lm_head"]["bytes_per_launch"] + kern["embed"]["bytes_per_launch"]
+    launches = ctx.step_launches() * D * args.steps
     line = {
         "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_total / args.steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded random-init weights, seeded prompt ids)",
         "config": {"workload": "1.1B Q4_K_M (TinyLlama shape) batch-1 greedy decode",
                    "model": "dim 2048, 22 layers, 32/4 heads, hd 64, ffn 5632, vocab 32000, Q4_K_M",
-                   "prompt": PROMPT_LEN, "decode_tokens_per_step": DECODE_LEN, "global_batch": 1,
+                   "prompt": P, "decode_tokens_per_step": D, "global_batch": 1,
                    "parallelism": f"replicas x{world}", "l2": "inputs larger than L2 (633 MB weights/token)",
                    "deterministic_tokens": deterministic, "prefill_tok_s": prefill_tps},
-        "roofline": {"bound": "hbm", "kernel": "dequant-fused GEMVs (QKV, Wo, gate/up+SwiGLU, down) of one token",
-                     "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "peak_source": peak_kind, "traffic": None,
-                     "algorithmic_bytes_per_step": gemv_bytes, "ms_per_step": gemv_ms},
+        "roofline": {"bound": "hbm", "kernel": dominant, "achieved": dk["gbs"], "peak": peak, "unit": "GB/s",
+                     "frac": dk["gbs"] / peak, "peak_source": peak_kind, "traffic": None,
+                     "algorithmic_bytes_per_launch": dk["bytes_per_launch"], "us_per_launch": dk["us_per_launch"],
+                     "timing": "CUDA graph of the kernel's per-layer launches, CUDA events on the decode stream"},
         "decode_roofline": {"bytes_per_token": step_bytes, "achieved_gbs": step_bytes * value / world / 1e9,
-                            "frac": step_bytes * value / world / 1e9 / peak,
-                            "kernel_ms_per_token": {"gemv": gemv_ms, "attention": attn_ms, "lm_head": lm_ms}},
-        "gemv_single": dict(single, frac=single["gbs"] / peak),
-        "e2e": {"value": e2e_val, "unit": "tok/s", "h2d_bytes_per_step": 32 * DECODE_LEN,
-                "d2h_bytes_per_step": 32 * DECODE_LEN, "api": "fiber_forward_token (host token/pos in, argmax out)"},
+                            "frac": step_bytes * value / world / 1e9 / peak, "kernels": kern,
+                            "kv_position_for_kernel_timing": mid},
+        "e2e": {"value": e2e_val, "unit": "tok/s", "h2d_bytes_per_step": 32 * D, "d2h_bytes_per_step": 32 * D,
+                "api": "fiber_forward_token (host token/pos in, argmax out)"},
         "gpu_launches": launches,
         "clocks": clk.summary(),
         "wall_s": wall,
     }
-    if cpu is not None:
-        line["cpu_baseline"] = cpu
+    if not args.skip_extras:
+        single = gemv_bandwidth(local)
+        line["gemv_single"] = dict(single, frac=single["gbs"] / peak)
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_reference_decode(path, budget_s=args.cpu_seconds, n_tokens_max=400)
     print(json.dumps(line), flush=True)
     ctx.close()
     if dist is not None:

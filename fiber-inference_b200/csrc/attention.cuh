@@ -33,21 +33,27 @@ struct AttnParams {
     int *err;                 // set to 1 when pos is out of range
 };
 
-constexpr int ATTN_THREADS = 128;
-constexpr int ATTN_P = 64;  // positions per page / chunk
+constexpr int ATTN_THREADS = 256;  // 8 warps
+constexpr int ATTN_P = 64;         // positions per page / chunk
+constexpr int ATTN_MAX_CHUNKS = 512;
 
+// CTA (chunk c, kv head g): warps own query heads (G <= 8: one head per warp,
+// lanes over positions for q.K and over head dims for P.V, softmax by
+// shuffles); the chunk-local (max, sum, o[hd]) go to scratch and the last CTA of
+// the kv head merges all chunks, loading every partial it needs at once.
 template <int HD, int G>
 __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const AttnParams a) {
     constexpr int P = ATTN_P;
-    constexpr int KST = HD + 2;  // padded K row (halves) -> conflict-free column walks
+    constexpr int KST = HD + 2;  // padded K row (halves): lanes walking d stay on distinct banks
+    constexpr int DPL = HD / 32; // head dims per lane in P.V
     __shared__ float qs[G][HD];
     __shared__ __align__(16) uint16_t ks[P][KST];
     __shared__ __align__(16) uint16_t vs[P][HD];
-    __shared__ float sc[G][P];
-    __shared__ float mx[G], sm[G];
     __shared__ unsigned int ticket;
 
-    const int c = blockIdx.x, g = blockIdx.y, tid = threadIdx.x;
+    const int c = blockIdx.x, g = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    pdl_trigger();
+    pdl_wait();
     const int pos = *a.pos_ptr;
     if (pos < 0 || pos >= a.max_seq) {
         if (c == 0 && g == 0 && tid == 0) *a.err = 1;
@@ -61,12 +67,12 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const AttnPar
     const int kvd = a.n_kv * HD;
     const float2 *rp = a.rope + (size_t)pos * (HD / 2);
 
-    // rotated queries of the G heads of this group
+    // rotated queries of the G heads of this group (half-split pairs)
     for (int i = tid; i < G * (HD / 2); i += ATTN_THREADS) {
         const int h = i / (HD / 2), j = i % (HD / 2);
         const float *qh = a.qkv + (size_t)(g * G + h) * HD;
-        const float x1 = qh[j], x2 = qh[j + HD / 2];
-        const float2 cs = rp[j];
+        const float x1 = __ldcg(qh + j), x2 = __ldcg(qh + j + HD / 2);
+        const float2 cs = __ldg(rp + j);
         qs[h][j] = __fsub_rn(__fmul_rn(x1, cs.x), __fmul_rn(x2, cs.y));
         qs[h][j + HD / 2] = __fadd_rn(__fmul_rn(x1, cs.y), __fmul_rn(x2, cs.x));
     }
@@ -81,19 +87,19 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const AttnPar
         const float *kr = a.qkv + (size_t)a.n_heads * HD + (size_t)g * HD;
         const float *vr = a.qkv + (size_t)a.n_heads * HD + kvd + (size_t)g * HD;
         for (int j = tid; j < HD / 2; j += ATTN_THREADS) {
-            const float x1 = kr[j], x2 = kr[j + HD / 2];
-            const float2 cs = rp[j];
+            const float x1 = __ldcg(kr + j), x2 = __ldcg(kr + j + HD / 2);
+            const float2 cs = __ldg(rp + j);
             const float y1 = __fsub_rn(__fmul_rn(x1, cs.x), __fmul_rn(x2, cs.y));
             const float y2 = __fadd_rn(__fmul_rn(x1, cs.y), __fmul_rn(x2, cs.x));
             kp[(size_t)tn * HD + j] = __half_as_ushort(__float2half_rn(y1));
             kp[(size_t)tn * HD + j + HD / 2] = __half_as_ushort(__float2half_rn(y2));
         }
-        for (int j = tid; j < HD; j += ATTN_THREADS) vp[(size_t)tn * HD + j] = __half_as_ushort(__float2half_rn(vr[j]));
+        for (int j = tid; j < HD; j += ATTN_THREADS) vp[(size_t)tn * HD + j] = __half_as_ushort(__float2half_rn(__ldcg(vr + j)));
         __syncthreads();  // block-wide visibility of the appended row
     }
 
     // stage the chunk: K with padded rows, V dense (16-byte loads)
-    constexpr int V8 = HD / 8;  // uint4 per row
+    constexpr int V8 = HD / 8;
     for (int i = tid; i < nt * V8; i += ATTN_THREADS) {
         const int t = i / V8, k8 = i % V8;
         const uint4 kv4 = __ldcg(reinterpret_cast<const uint4 *>(kp + (size_t)t * HD) + k8);
@@ -104,52 +110,55 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const AttnPar
     }
     __syncthreads();
 
-    // scores: one (head, position) dot product per thread, sequential over d
-    for (int i = tid; i < G * P; i += ATTN_THREADS) {
-        const int h = i / P, t = i % P;
-        if (t < nt) {
-            float dot = 0.f;
-#pragma unroll 8
-            for (int d = 0; d < HD; d++)
-                dot = __fadd_rn(dot, __fmul_rn(qs[h][d], __half2float(__ushort_as_half(ks[t][d]))));
-            sc[h][t] = __fmul_rn(dot, a.scale);
-        }
-    }
-    __syncthreads();
-
-    // chunk-local softmax statistics, one warp per head
-    const int warp = tid >> 5, lane = tid & 31;
+    float *pg = a.part + (size_t)g * a.max_chunks * G * (HD + 2);
     for (int h = warp; h < G; h += ATTN_THREADS / 32) {
-        float m = -INFINITY;
-        for (int t = lane; t < nt; t += 32) m = fmaxf(m, sc[h][t]);
+        // scores for positions lane and lane+32; four interleaved partial sums
+        float s[2];
+#pragma unroll
+        for (int k = 0; k < 2; k++) {
+            const int t = lane + 32 * k;
+            float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;
+            if (t < nt) {
+#pragma unroll
+                for (int d = 0; d < HD; d += 4) {
+                    d0 = fmaf(qs[h][d + 0], __half2float(__ushort_as_half(ks[t][d + 0])), d0);
+                    d1 = fmaf(qs[h][d + 1], __half2float(__ushort_as_half(ks[t][d + 1])), d1);
+                    d2 = fmaf(qs[h][d + 2], __half2float(__ushort_as_half(ks[t][d + 2])), d2);
+                    d3 = fmaf(qs[h][d + 3], __half2float(__ushort_as_half(ks[t][d + 3])), d3);
+                }
+            }
+            s[k] = t < nt ? __fmul_rn((d0 + d1) + (d2 + d3), a.scale) : -INFINITY;
+        }
+        float m = fmaxf(s[0], s[1]);
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        float s = 0.f;
-        for (int t = lane; t < nt; t += 32) {
-            const float e = expf(sc[h][t] - m);
-            sc[h][t] = e;
-            s += e;
-        }
+        const float e0 = lane < nt ? expf(s[0] - m) : 0.f;
+        const float e1 = lane + 32 < nt ? expf(s[1] - m) : 0.f;
+        float l = e0 + e1;
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-        if (lane == 0) {
-            mx[h] = m;
-            sm[h] = s;
+        for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+        // P.V: lane owns dims lane + 32*j; position weights come by shuffle
+        float o[DPL], o2[DPL];
+#pragma unroll
+        for (int j = 0; j < DPL; j++) o[j] = o2[j] = 0.f;
+        const int n0 = min(nt, 32);
+        for (int t = 0; t < n0; t++) {
+            const float w = __shfl_sync(0xffffffffu, e0, t);
+#pragma unroll
+            for (int j = 0; j < DPL; j++) o[j] = fmaf(w, __half2float(__ushort_as_half(vs[t][lane + 32 * j])), o[j]);
         }
-    }
-    __syncthreads();
-
-    // unnormalised P.V for the chunk
-    float *pc = a.part + ((size_t)g * a.max_chunks + c) * G * (HD + 2);
-    for (int i = tid; i < G * HD; i += ATTN_THREADS) {
-        const int h = i / HD, d = i % HD;
-        float o = 0.f;
-        for (int t = 0; t < nt; t++) o = fmaf(sc[h][t], __half2float(__ushort_as_half(vs[t][d])), o);
-        pc[h * (HD + 2) + 2 + d] = o;
-    }
-    if (tid < G) {
-        pc[tid * (HD + 2) + 0] = mx[tid];
-        pc[tid * (HD + 2) + 1] = sm[tid];
+        for (int t = 32; t < nt; t++) {
+            const float w = __shfl_sync(0xffffffffu, e1, t - 32);
+#pragma unroll
+            for (int j = 0; j < DPL; j++) o2[j] = fmaf(w, __half2float(__ushort_as_half(vs[t][lane + 32 * j])), o2[j]);
+        }
+        float *pc = pg + ((size_t)c * G + h) * (HD + 2);
+#pragma unroll
+        for (int j = 0; j < DPL; j++) pc[2 + lane + 32 * j] = o[j] + o2[j];
+        if (lane == 0) {
+            pc[0] = m;
+            pc[1] = l;
+        }
     }
     __threadfence();
     __syncthreads();
@@ -157,21 +166,39 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const AttnPar
     __syncthreads();
     if (ticket != (unsigned)(nch - 1)) return;
 
-    // last chunk of this kv head: merge
+    // last CTA of this kv head: merge the nch chunks of every head (warp per head)
     __threadfence();
-    const float *pg = a.part + (size_t)g * a.max_chunks * G * (HD + 2);
-    for (int i = tid; i < G * HD; i += ATTN_THREADS) {
-        const int h = i / HD, d = i % HD;
+    for (int h = warp; h < G; h += ATTN_THREADS / 32) {
         float M = -INFINITY;
-        for (int k = 0; k < nch; k++) M = fmaxf(M, __ldcg(pg + ((size_t)k * G + h) * (HD + 2)));
-        float L = 0.f, O = 0.f;
-        for (int k = 0; k < nch; k++) {
-            const float *e = pg + ((size_t)k * G + h) * (HD + 2);
-            const float w = expf(__ldcg(e) - M);
-            L = fmaf(w, __ldcg(e + 1), L);
-            O = fmaf(w, __ldcg(e + 2 + d), O);
+        for (int k = lane; k < nch; k += 32) M = fmaxf(M, __ldcg(pg + ((size_t)k * G + h) * (HD + 2)));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+        float Lsum = 0.f;
+        float O[DPL];
+#pragma unroll
+        for (int j = 0; j < DPL; j++) O[j] = 0.f;
+        for (int k0 = 0; k0 < nch; k0 += 32) {
+            // lane k0+lane fetches its chunk's weight; partial outputs loaded per chunk
+            const int kk = k0 + lane;
+            float w = 0.f;
+            if (kk < nch) {
+                const float *e = pg + ((size_t)kk * G + h) * (HD + 2);
+                w = expf(__ldcg(e) - M);
+                Lsum = fmaf(w, __ldcg(e + 1), Lsum);
+            }
+            const int kn = min(32, nch - k0);
+#pragma unroll 4
+            for (int k = 0; k < kn; k++) {
+                const float wk = __shfl_sync(0xffffffffu, w, k);
+                const float *e = pg + ((size_t)(k0 + k) * G + h) * (HD + 2) + 2;
+#pragma unroll
+                for (int j = 0; j < DPL; j++) O[j] = fmaf(wk, __ldcg(e + lane + 32 * j), O[j]);
+            }
         }
-        a.out[(size_t)(g * G + h) * HD + d] = O / L;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) Lsum += __shfl_xor_sync(0xffffffffu, Lsum, o);
+#pragma unroll
+        for (int j = 0; j < DPL; j++) a.out[(size_t)(g * G + h) * HD + lane + 32 * j] = O[j] / Lsum;
     }
     if (tid == 0) a.count[g] = 0u;
 }
@@ -181,6 +208,8 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const AttnPar
 template <int T>
 __global__ void embed_kernel(const uint8_t *__restrict__ tab, const int32_t *__restrict__ token, float *x, int dim,
                              int vocab, int *err) {
+    pdl_trigger();
+    pdl_wait();
     int tok = *token;
     if (tok < 0 || tok >= vocab) {
         if (threadIdx.x == 0 && blockIdx.x == 0) *err = 2;

@@ -25,6 +25,8 @@
 #include "attention.cuh"
 #include "fiber_cuda.h"
 #include "gemv.cuh"
+#include "gemv_tc.cuh"
+#include "launch.cuh"
 
 using namespace fiber;
 
@@ -96,12 +98,97 @@ static cudaError_t launch_gemv_t(const GemvParams &p, int grid, cudaStream_t st)
         cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
     }
-    k<<<grid, GEMV_THREADS, smem, st>>>(p);
-    return cudaGetLastError();
+    return launch_pdl(k, dim3(grid), dim3(GEMV_THREADS), smem, st, p);
+}
+
+static int sm_count() {
+    static int cache[64];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+    if (!cache[dev]) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+        cache[dev] = n;
+    }
+    return cache[dev];
+}
+
+// v2 launch (gemv_tc.cuh): tiles of 16 rows; one tile per CTA while the grid fits
+// about four CTAs per SM, else a persistent grid of 2 CTAs per SM with a ring of
+// up to 4 tiles each.
+template <int T, int EPI, int NMAT>
+static cudaError_t launch_tc_t(TcParams p, cudaStream_t st) {
+    const int sms = sm_count();
+    const int nb = p.cols / 256;
+    p.row_bytes = nb * TcType<T>::BB;
+    p.per_row_copy = (p.row_bytes % 16) == 0;
+    p.stride = p.per_row_copy ? p.row_bytes + (16 - p.row_bytes % 128 + 128) % 128 : p.row_bytes;
+    p.n_tiles = 0;
+    for (int s = 0; s < p.nseg; s++) {
+        p.seg[s].tiles = (p.seg[s].rows + TC_M - 1) / TC_M;
+        p.n_tiles += p.seg[s].tiles;
+    }
+    const size_t tile_bytes = (size_t)NMAT * TC_M * p.stride;
+    size_t fixed = (size_t)nb * 1024;
+    int grid;
+    if (p.n_tiles <= 4 * sms) {
+        grid = p.n_tiles;
+        p.stages = 1;
+    } else {
+        grid = 2 * sms;
+        const long long fit = ((long long)112 * 1024 - (long long)fixed) / (long long)tile_bytes;
+        p.stages = (int)(fit < 1 ? 1 : (fit > 4 ? 4 : fit));
+    }
+    size_t smem = p.stages * tile_bytes + fixed;
+    p.stage_x = smem + (size_t)p.cols * 4 <= 227 * 1024;  // fp32 copy of x while staging, if it fits
+    if (p.stage_x) smem += (size_t)p.cols * 4;
+    if (smem > 227 * 1024) return cudaErrorNotSupported;  // caller falls back to the v1 kernel
+    auto k = gemv_tc_kernel<T, EPI, NMAT>;
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+    }
+    return launch_pdl(k, dim3(grid), dim3(TC_THREADS), smem, st, p);
+}
+
+static TcParams to_tc(const GemvParams &g) {
+    TcParams p;
+    memset(&p, 0, sizeof(p));
+    p.nseg = g.nseg;
+    for (int s = 0; s < g.nseg; s++) {
+        p.seg[s].w = g.seg[s].w;
+        p.seg[s].w2 = g.w_up;
+        p.seg[s].rows = g.seg[s].rows;
+        p.seg[s].out_off = g.seg[s].out_off;
+    }
+    p.cols = g.cols;
+    p.x = g.x;
+    p.norm_w = g.norm_w;
+    p.eps = g.eps;
+    p.y = g.y;
+    p.resid = g.resid;
+    p.am_part = g.am_part;
+    p.am_count = g.am_count;
+    p.am_out = g.am_out;
+    p.adv_token = g.adv_token;
+    p.adv_pos = g.adv_pos;
+    p.rec_tokens = g.rec_tokens;
+    p.rec_step = g.rec_step;
+    return p;
 }
 
 template <int EPI>
 static cudaError_t launch_gemv(int type, const GemvParams &p, int grid, cudaStream_t st) {
+    constexpr int NM = EPI == EPI_SWIGLU ? 2 : 1;
+    cudaError_t e = cudaErrorNotSupported;
+    switch (type) {
+    case T_Q4_K: e = launch_tc_t<T_Q4_K, EPI, NM>(to_tc(p), st); break;
+    case T_Q6_K: e = launch_tc_t<T_Q6_K, EPI, NM>(to_tc(p), st); break;
+    case T_F16: e = launch_tc_t<T_F16, EPI, NM>(to_tc(p), st); break;
+    default: break;
+    }
+    if (e != cudaErrorNotSupported) return e;
+    // Q5_K, or a tile that does not fit in shared memory: the v1 kernel
     switch (type) {
     case T_Q4_K: return launch_gemv_t<T_Q4_K, EPI>(p, grid, st);
     case T_Q5_K: return launch_gemv_t<T_Q5_K, EPI>(p, grid, st);
@@ -275,9 +362,6 @@ struct gpu_context {
     std::vector<float> logits_copy;
     Graph g_step, g_loop;
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
-    int profile = 0;
-    double prof_ms[3] = {0, 0, 0}, prof_bytes[3] = {0, 0, 0};
-    int prof_steps = 0;
 };
 
 static void free_graph(Graph &g) {
@@ -312,6 +396,8 @@ static int ctx_init(gpu_context *c, const model_t *m, int device, int max_seq) {
     c->kvd = (int)(p.n_kv_heads * p.head_dim);
     c->G = (int)(p.n_heads / p.n_kv_heads);
     c->max_chunks = (max_seq + ATTN_P - 1) / ATTN_P;
+    if (c->max_chunks > ATTN_MAX_CHUNKS)
+        return set_err(FIBER_EUNSUPPORTED, "max_seq %d exceeds %d positions", max_seq, ATTN_MAX_CHUNKS * ATTN_P);
     if (p.dim % 256 || p.ffn_dim % 256)
         return set_err(FIBER_EUNSUPPORTED, "dim (%u) and ffn_dim (%u) must be multiples of 256", p.dim, p.ffn_dim);
     if (!(p.head_dim == 64 || p.head_dim == 128))
@@ -422,36 +508,6 @@ extern "C" fiber_ctx_t *fiber_cuda_init(const model_t *m, int device, int max_ba
 
 // ---- the decode step ------------------------------------------------------------------
 
-enum { K_GEMV = 0, K_ATTN = 1, K_LM = 2 };
-
-struct Prof {  // optional per-kernel timing (eager launches only)
-    gpu_context *c;
-    std::vector<cudaEvent_t> ev;
-    std::vector<int> kind;
-    int n = 0;
-    void begin(int k) {
-        if (!c) return;
-        if ((int)ev.size() < 2 * (n + 1)) {
-            cudaEvent_t a, b;
-            cudaEventCreate(&a);
-            cudaEventCreate(&b);
-            ev.push_back(a);
-            ev.push_back(b);
-            kind.push_back(k);
-        }
-        kind[n] = k;
-        cudaEventRecord(ev[2 * n], c->stream);
-    }
-    void end() {
-        if (!c) return;
-        cudaEventRecord(ev[2 * n + 1], c->stream);
-        n++;
-    }
-    ~Prof() {
-        for (auto e : ev) cudaEventDestroy(e);
-    }
-};
-
 static cudaError_t enqueue_qkv(gpu_context *c, const LayerDev &d, cudaStream_t st) {
     const int dim = c->p.dim, kvd = c->kvd;
     GemvParams p;
@@ -483,9 +539,7 @@ static cudaError_t enqueue_qkv(gpu_context *c, const LayerDev &d, cudaStream_t s
 
 template <int HD, int G>
 static cudaError_t launch_attn_t(const AttnParams &a, cudaStream_t st) {
-    dim3 grid(a.max_chunks, a.n_kv);
-    attn_decode_kernel<HD, G><<<grid, ATTN_THREADS, 0, st>>>(a);
-    return cudaGetLastError();
+    return launch_pdl(attn_decode_kernel<HD, G>, dim3(a.max_chunks, a.n_kv), dim3(ATTN_THREADS), 0, st, a);
 }
 
 static cudaError_t launch_attn(gpu_context *c, const AttnParams &a, cudaStream_t st) {
@@ -502,15 +556,15 @@ static cudaError_t launch_embed(gpu_context *c, cudaStream_t st) {
     const int dim = c->p.dim, V = c->p.vocab_size, grid = (dim + 255) / 256;
     int *err = &c->io->err;
     const int32_t *tok = &c->io->token;
+    const dim3 g(grid), b(256);
     switch (c->t_embd) {
-    case T_Q4_K: embed_kernel<T_Q4_K><<<grid, 256, 0, st>>>(c->embd, tok, c->x, dim, V, err); break;
-    case T_Q5_K: embed_kernel<T_Q5_K><<<grid, 256, 0, st>>>(c->embd, tok, c->x, dim, V, err); break;
-    case T_Q6_K: embed_kernel<T_Q6_K><<<grid, 256, 0, st>>>(c->embd, tok, c->x, dim, V, err); break;
-    case T_F16: embed_kernel<T_F16><<<grid, 256, 0, st>>>(c->embd, tok, c->x, dim, V, err); break;
-    case T_F32: embed_kernel<T_F32><<<grid, 256, 0, st>>>(c->embd, tok, c->x, dim, V, err); break;
+    case T_Q4_K: return launch_pdl(embed_kernel<T_Q4_K>, g, b, 0, st, c->embd, tok, c->x, dim, V, err);
+    case T_Q5_K: return launch_pdl(embed_kernel<T_Q5_K>, g, b, 0, st, c->embd, tok, c->x, dim, V, err);
+    case T_Q6_K: return launch_pdl(embed_kernel<T_Q6_K>, g, b, 0, st, c->embd, tok, c->x, dim, V, err);
+    case T_F16: return launch_pdl(embed_kernel<T_F16>, g, b, 0, st, c->embd, tok, c->x, dim, V, err);
+    case T_F32: return launch_pdl(embed_kernel<T_F32>, g, b, 0, st, c->embd, tok, c->x, dim, V, err);
     default: return cudaErrorInvalidValue;
     }
-    return cudaGetLastError();
 }
 
 static cudaError_t enqueue_lm_head(gpu_context *c, bool loop, cudaStream_t st) {
@@ -531,13 +585,8 @@ static cudaError_t enqueue_lm_head(gpu_context *c, bool loop, cudaStream_t st) {
     return launch_gemv<EPI_ARGMAX>(c->t_out, p, grid_of(p), st);
 }
 
-// Enqueue one full decode step. `loop` makes the lm_head feed its argmax back as
-// the next token and advance the position (device-resident greedy decoding).
-static cudaError_t enqueue_step(gpu_context *c, const kv_cache_t *kv, bool loop, cudaStream_t st, Prof *pf) {
+static AttnParams attn_params(gpu_context *c, const kv_cache_t *kv) {
     const model_params_t &p = c->p;
-    const int dim = p.dim, ffn = p.ffn_dim;
-    cudaError_t e;
-    if ((e = launch_embed(c, st)) != cudaSuccess) return e;
     AttnParams a;
     memset(&a, 0, sizeof(a));
     a.qkv = c->qkv;
@@ -556,36 +605,56 @@ static cudaError_t enqueue_step(gpu_context *c, const kv_cache_t *kv, bool loop,
     a.max_seq = c->max_seq < kv->max_seq ? c->max_seq : kv->max_seq;
     a.scale = 1.0f / sqrtf((float)p.head_dim);
     a.err = &c->io->err;
-    for (uint32_t l = 0; l < p.n_layers; l++) {
-        const LayerDev &d = c->L[l];
-        if (pf) pf->begin(K_GEMV);
-        if ((e = enqueue_qkv(c, d, st)) != cudaSuccess) return e;
-        if (pf) pf->end();
+    return a;
+}
+
+// One kernel kind of layer l as the decode step issues it (kind: 0 QKV,
+// 1 attention, 2 Wo, 3 gate/up+SwiGLU, 4 down, 5 lm_head, 6 embedding).
+static cudaError_t enqueue_kind(gpu_context *c, const kv_cache_t *kv, int kind, int l, bool loop, cudaStream_t st) {
+    const model_params_t &p = c->p;
+    const int dim = p.dim, ffn = p.ffn_dim;
+    const LayerDev &d = c->L[l];
+    switch (kind) {
+    case 0: return enqueue_qkv(c, d, st);
+    case 1: {
+        AttnParams a = attn_params(c, kv);
         a.layer = l;
-        if (pf) pf->begin(K_ATTN);
-        if ((e = launch_attn(c, a, st)) != cudaSuccess) return e;
-        if (pf) pf->end();
+        return launch_attn(c, a, st);
+    }
+    case 2: {
         GemvParams wo = one_seg(d.wo, d.to, dim, 0, dim);
         wo.x = c->att;
         wo.resid = c->x;
-        if (pf) pf->begin(K_GEMV);
-        if ((e = launch_gemv<EPI_RESID>(d.to, wo, grid_of(wo), st)) != cudaSuccess) return e;
+        return launch_gemv<EPI_RESID>(d.to, wo, grid_of(wo), st);
+    }
+    case 3: {
         GemvParams up = one_seg(d.w1, d.t1, ffn, 0, dim);
         up.w_up = d.w3;
         up.x = c->x;
         up.norm_w = d.ffn_norm;
         up.eps = p.rms_norm_eps;
         up.y = c->h;
-        if ((e = launch_gemv<EPI_SWIGLU>(d.t1, up, grid_of(up), st)) != cudaSuccess) return e;
+        return launch_gemv<EPI_SWIGLU>(d.t1, up, grid_of(up), st);
+    }
+    case 4: {
         GemvParams dn = one_seg(d.w2, d.t2, dim, 0, ffn);
         dn.x = c->h;
         dn.resid = c->x;
-        if ((e = launch_gemv<EPI_RESID>(d.t2, dn, grid_of(dn), st)) != cudaSuccess) return e;
-        if (pf) pf->end();
+        return launch_gemv<EPI_RESID>(d.t2, dn, grid_of(dn), st);
     }
-    if (pf) pf->begin(K_LM);
-    e = enqueue_lm_head(c, loop, st);
-    if (pf) pf->end();
+    case 5: return enqueue_lm_head(c, loop, st);
+    case 6: return launch_embed(c, st);
+    default: return cudaErrorInvalidValue;
+    }
+}
+
+// Enqueue one full decode step. `loop` makes the lm_head feed its argmax back as
+// the next token and advance the position (device-resident greedy decoding).
+static cudaError_t enqueue_step(gpu_context *c, const kv_cache_t *kv, bool loop, cudaStream_t st) {
+    cudaError_t e = enqueue_kind(c, kv, 6, 0, loop, st);
+    for (uint32_t l = 0; l < c->p.n_layers && e == cudaSuccess; l++)
+        for (int kind = 0; kind <= 4 && e == cudaSuccess; kind++) e = enqueue_kind(c, kv, kind, (int)l, loop, st);
+    if (e == cudaSuccess) e = enqueue_lm_head(c, loop, st);
     return e;
 }
 
@@ -598,7 +667,7 @@ static int get_graph(gpu_context *c, const kv_cache_t *kv, bool loop, cudaGraphE
     free_graph(g);
     cudaGraph_t graph;
     CK(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
-    cudaError_t e = enqueue_step(c, kv, loop, c->stream, nullptr);
+    cudaError_t e = enqueue_step(c, kv, loop, c->stream);
     cudaError_t e2 = cudaStreamEndCapture(c->stream, &graph);
     if (e != cudaSuccess) return set_err(FIBER_ECUDA, "capturing the decode step: %s", cudaGetErrorString(e));
     if (e2 != cudaSuccess) return set_err(FIBER_ECUDA, "end capture: %s", cudaGetErrorString(e2));
@@ -662,30 +731,6 @@ extern "C" int fiber_prefill(fiber_ctx_t *c, kv_cache_t *kv, const int32_t *toke
     return FIBER_OK;
 }
 
-static void prof_account(gpu_context *c, Prof &pf, const kv_cache_t *kv, int pos) {
-    (void)kv;
-    for (int i = 0; i < pf.n; i++) {
-        float ms = 0.f;
-        cudaEventElapsedTime(&ms, pf.ev[2 * i], pf.ev[2 * i + 1]);
-        c->prof_ms[pf.kind[i]] += ms;
-    }
-    pf.n = 0;
-    // algorithmic bytes of this step
-    const model_params_t &p = c->p;
-    double w = 0.0;
-    for (uint32_t l = 0; l < p.n_layers; l++) {
-        const LayerDev &d = c->L[l];
-        auto mb = [&](int t, double rows, double cols) { return rows * cols / 256.0 * block_bytes(t); };
-        w += mb(d.tq, p.dim, p.dim) + mb(d.tk, c->kvd, p.dim) + mb(d.tv, c->kvd, p.dim) + mb(d.to, p.dim, p.dim) +
-             mb(d.t1, p.ffn_dim, p.dim) + mb(d.t3, p.ffn_dim, p.dim) + mb(d.t2, p.dim, p.ffn_dim);
-        w += 4.0 * (2 * p.dim) * 2 + 4.0 * (p.dim + 2 * c->kvd) + 4.0 * p.dim * 3 + 4.0 * p.ffn_dim * 2;  // norms + vectors
-    }
-    c->prof_bytes[K_GEMV] += w;
-    c->prof_bytes[K_ATTN] += (double)p.n_layers * 2.0 * c->kvd * 2.0 * (pos + 1);
-    c->prof_bytes[K_LM] += (double)p.vocab_size * p.dim / 256.0 * block_bytes(c->t_out) + 4.0 * p.vocab_size;
-    c->prof_steps++;
-}
-
 extern "C" int fiber_step_launches(fiber_ctx_t *c) {
     if (!c) return set_err(FIBER_EARG, "no context");
     int n = 2;  // embed + lm_head
@@ -693,22 +738,64 @@ extern "C" int fiber_step_launches(fiber_ctx_t *c) {
     return n;
 }
 
-extern "C" int fiber_set_profile(fiber_ctx_t *c, int enable) {
-    if (!c) return set_err(FIBER_EARG, "no context");
-    c->profile = enable;
-    memset(c->prof_ms, 0, sizeof(c->prof_ms));
-    memset(c->prof_bytes, 0, sizeof(c->prof_bytes));
-    c->prof_steps = 0;
+static double kind_bytes(gpu_context *c, int kind, int l, int pos) {
+    const model_params_t &p = c->p;
+    const LayerDev &d = c->L[l];
+    auto mb = [&](int t, double rows, double cols) { return rows * cols / 256.0 * block_bytes(t); };
+    switch (kind) {
+    case 0: return mb(d.tq, p.dim, p.dim) + mb(d.tk, c->kvd, p.dim) + mb(d.tv, c->kvd, p.dim) + 4.0 * p.dim * 2 +
+                   4.0 * (p.dim + 2 * c->kvd);
+    case 1: return 2.0 * c->kvd * 2.0 * (pos + 1) + 4.0 * (p.dim + 2 * c->kvd) + 4.0 * p.dim;
+    case 2: return mb(d.to, p.dim, p.dim) + 4.0 * p.dim * 3;
+    case 3: return mb(d.t1, p.ffn_dim, p.dim) + mb(d.t3, p.ffn_dim, p.dim) + 4.0 * p.dim * 2 + 4.0 * p.ffn_dim;
+    case 4: return mb(d.t2, p.dim, p.ffn_dim) + 4.0 * p.ffn_dim + 4.0 * p.dim * 2;
+    case 5: return mb(c->t_out, p.vocab_size, p.dim) + 4.0 * p.dim * 2 + 4.0 * p.vocab_size;
+    case 6: return (double)p.dim / 256.0 * block_bytes(c->t_embd) + 4.0 * p.dim;
+    default: return 0.0;
+    }
+}
+
+extern "C" int fiber_time_kernel(fiber_ctx_t *c, kv_cache_t *kv, int kind, int pos, int reps, double *us_per_launch,
+                                 double *bytes_per_launch) {
+    if (!c || kind < 0 || kind > 6 || reps <= 0) return set_err(FIBER_EARG, "fiber_time_kernel: bad arguments");
+    int rc = check_kv(c, kv);
+    if (rc) return rc;
+    const int lim = c->max_seq < kv->max_seq ? c->max_seq : kv->max_seq;
+    if (pos < 0 || pos >= lim) return set_err(FIBER_EARG, "fiber_time_kernel: position %d outside [0, %d)", pos, lim);
+    CK(cudaSetDevice(c->device));
+    c->h_io->pos = pos;
+    c->h_io->err = 0;
+    CK(cudaMemcpyAsync(c->io, c->h_io, sizeof(StepIO), cudaMemcpyHostToDevice, c->stream));
+    const int L = (int)c->p.n_layers;
+    cudaGraph_t graph;
+    CK(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
+    cudaError_t e = cudaSuccess;
+    double bytes = 0.0;
+    for (int l = 0; l < L && e == cudaSuccess; l++) {
+        e = enqueue_kind(c, kv, kind, l, false, c->stream);
+        bytes += kind_bytes(c, kind, l, pos);
+    }
+    cudaError_t e2 = cudaStreamEndCapture(c->stream, &graph);
+    if (e != cudaSuccess || e2 != cudaSuccess)
+        return set_err(FIBER_ECUDA, "fiber_time_kernel capture: %s", cudaGetErrorString(e != cudaSuccess ? e : e2));
+    cudaGraphExec_t exec;
+    e = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    if (e != cudaSuccess) return set_err(FIBER_ECUDA, "fiber_time_kernel instantiate: %s", cudaGetErrorString(e));
+    e = cudaGraphLaunch(exec, c->stream);  // warm-up replay
+    if (e == cudaSuccess) e = cudaEventRecord(c->ev0, c->stream);
+    for (int r = 0; r < reps && e == cudaSuccess; r++) e = cudaGraphLaunch(exec, c->stream);
+    if (e == cudaSuccess) e = cudaEventRecord(c->ev1, c->stream);
+    if (e == cudaSuccess) e = cudaEventSynchronize(c->ev1);
+    float ms = 0.f;
+    if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, c->ev0, c->ev1);
+    cudaGraphExecDestroy(exec);
+    if (e != cudaSuccess) return set_err(FIBER_ECUDA, "fiber_time_kernel: %s", cudaGetErrorString(e));
+    if (us_per_launch) *us_per_launch = 1e3 * ms / ((double)reps * L);
+    if (bytes_per_launch) *bytes_per_launch = bytes / L;
     return FIBER_OK;
 }
 
-extern "C" int fiber_profile_get(fiber_ctx_t *c, int kind, double *ms, double *bytes) {
-    if (!c || kind < 0 || kind > 2) return set_err(FIBER_EARG, "fiber_profile_get: bad kind");
-    const double n = c->prof_steps > 0 ? c->prof_steps : 1;
-    if (ms) *ms = c->prof_ms[kind] / n;
-    if (bytes) *bytes = c->prof_bytes[kind] / n;
-    return FIBER_OK;
-}
 
 extern "C" int fiber_decode_greedy(fiber_ctx_t *c, kv_cache_t *kv, int32_t first_token, int start_pos, int n_steps,
                                    int32_t *h_tokens_out, float *ms_out) {
@@ -725,17 +812,7 @@ extern "C" int fiber_decode_greedy(fiber_ctx_t *c, kv_cache_t *kv, int32_t first
     c->h_io->step = 0;
     c->h_io->err = 0;
     CK(cudaMemcpyAsync(c->io, c->h_io, sizeof(StepIO), cudaMemcpyHostToDevice, c->stream));
-    if (c->profile) {
-        Prof pf;
-        pf.c = c;
-        for (int i = 0; i < n_steps; i++) {
-            cudaError_t e = enqueue_step(c, kv, true, c->stream, &pf);
-            if (e != cudaSuccess) return set_err(FIBER_ECUDA, "profiled step: %s", cudaGetErrorString(e));
-            CK(cudaStreamSynchronize(c->stream));
-            prof_account(c, pf, kv, start_pos + i);
-        }
-        if (ms_out) *ms_out = 0.f;
-    } else {
+    {
         cudaGraphExec_t g;
         if ((rc = get_graph(c, kv, true, &g)) != FIBER_OK) return rc;
         CK(cudaEventRecord(c->ev0, c->stream));

@@ -237,6 +237,8 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(const GemvParams p) 
     __shared__ float2 am_warp[GEMV_WARPS];
     __shared__ unsigned int am_ticket;
 
+    pdl_trigger();
+    pdl_wait();
     // locate segment and tile
     int tile = blockIdx.x, s = 0;
     while (s + 1 < p.nseg && tile >= p.tiles[s]) tile -= p.tiles[s++];

@@ -15,6 +15,14 @@ namespace fiber {
 
 enum : int { T_F32 = 0, T_F16 = 1, T_Q4_K = 12, T_Q5_K = 13, T_Q6_K = 14 };
 
+// Programmatic dependent launch (every kernel of the decode step uses both):
+// pdl_trigger lets the next kernel in the stream start its prologue; pdl_wait
+// blocks until the previous kernel has completed and its writes are visible.
+// Every kernel waits before it reads or writes any activation, so completion of
+// a kernel implies completion of all earlier ones.
+FDEV void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+FDEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 FDEV float h2f(uint32_t bits16) { return __half2float(__ushort_as_half((unsigned short)(bits16 & 0xFFFFu))); }
 FDEV float round_f16(float v) { return __half2float(__float2half_rn(v)); }
 

@@ -21,7 +21,7 @@ I32P = np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS")
 
 EXPORTED = [
     "fiber_last_error", "fiber_device_count", "fiber_cuda_init", "fiber_cuda_free", "fiber_forward_token",
-    "fiber_prefill", "fiber_decode_greedy", "fiber_step_launches", "fiber_set_profile", "fiber_profile_get", "fiber_gemv",
+    "fiber_prefill", "fiber_decode_greedy", "fiber_step_launches", "fiber_time_kernel", "fiber_gemv",
     "fiber_dequant", "fiber_gemv_host", "gpu_init", "gpu_free", "gpu_embed", "gpu_forward_token",
     "gpu_get_logits", "gpu_forward_classifier", "gpu_get_device", "kv_cache_init", "kv_cache_init_paged",
     "kv_cache_free", "kv_cache_write", "kv_cache_read", "fiber_gemv_argmax_noalloc",
@@ -58,8 +58,8 @@ def cuda_lib() -> C.CDLL:
         L.fiber_decode_greedy.argtypes = [C.c_void_p, C.c_void_p, C.c_int32, C.c_int, C.c_int, C.c_void_p,
                                           C.c_void_p]
         L.fiber_step_launches.argtypes = [C.c_void_p]
-        L.fiber_set_profile.argtypes = [C.c_void_p, C.c_int]
-        L.fiber_profile_get.argtypes = [C.c_void_p, C.c_int, C.POINTER(C.c_double), C.POINTER(C.c_double)]
+        L.fiber_time_kernel.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.POINTER(C.c_double),
+                                        C.POINTER(C.c_double)]
         L.fiber_gemv.argtypes = [C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p]
         L.fiber_gemv_host.argtypes = [C.c_int, C.c_void_p, F32P, F32P, C.c_int, C.c_int, C.c_void_p, C.c_void_p,
                                       C.c_void_p]
@@ -212,10 +212,11 @@ class Context:
             _check(n, "fiber_step_launches")
         return int(n)
 
-    def set_profile(self, enable: bool):
-        _check(cuda_lib().fiber_set_profile(self.h, int(enable)), "fiber_set_profile")
+    KINDS = ["qkv", "attention", "wo", "gate_up", "down", "lm_head", "embed"]
 
-    def profile(self, kind: int):
-        ms, b = C.c_double(), C.c_double()
-        _check(cuda_lib().fiber_profile_get(self.h, kind, C.byref(ms), C.byref(b)), "fiber_profile_get")
-        return ms.value, b.value
+    def time_kernel(self, kv: KVCache, kind: int, pos: int, reps: int = 20):
+        """(microseconds per launch, algorithmic bytes per launch) of one kernel kind."""
+        us, b = C.c_double(), C.c_double()
+        _check(cuda_lib().fiber_time_kernel(self.h, kv.addr, kind, pos, reps, C.byref(us), C.byref(b)),
+               "fiber_time_kernel")
+        return us.value, b.value

@@ -71,12 +71,16 @@ int fiber_decode_greedy(fiber_ctx_t *ctx, kv_cache_t *kv, int32_t first_token, i
 /* Number of kernels one decode step launches (all of them this library's own). */
 int fiber_step_launches(fiber_ctx_t *ctx);
 
-/* Average device time per launch of the dominant decode kernel kind during the
- * last fiber_decode_greedy call with profiling enabled (see fiber_set_profile). */
-int fiber_set_profile(fiber_ctx_t *ctx, int enable);
-/* kind: 0 = all quantized GEMVs of a step, 1 = attention, 2 = lm_head.
- * *ms = summed device time of that kind per step; *bytes = its algorithmic bytes per step. */
-int fiber_profile_get(fiber_ctx_t *ctx, int kind, double *ms, double *bytes);
+/* Device time of one kernel kind of the decode step, measured the way it runs in
+ * the step: a CUDA graph of its n_layers per-layer launches (lm_head and embed:
+ * n_layers repeats) is replayed `reps` times between CUDA events on the context
+ * stream, with the position set to `pos` (attention reads pos+1 KV rows and
+ * rewrites row pos). kind: 0 QKV, 1 attention, 2 Wo, 3 gate/up+SwiGLU, 4 down,
+ * 5 lm_head+argmax, 6 embedding. Outputs: average microseconds per launch and
+ * algorithmic bytes per launch (weights + KV + vectors). Overwrites the hidden
+ * state: call it between decode calls. */
+int fiber_time_kernel(fiber_ctx_t *ctx, kv_cache_t *kv, int kind, int pos, int reps,
+                      double *us_per_launch, double *bytes_per_launch);
 
 /* ---- kernel-level entry points (device pointers) -------------------------------- */
 
