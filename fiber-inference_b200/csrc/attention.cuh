@@ -37,31 +37,32 @@ constexpr int ATTN_THREADS = 256;  // 8 warps
 constexpr int ATTN_P = 64;         // positions per page / chunk
 constexpr int ATTN_MAX_CHUNKS = 512;
 
-// CTA (chunk c, kv head g): warps own query heads (G <= 8: one head per warp,
-// lanes over positions for q.K and over head dims for P.V, softmax by
-// shuffles); the chunk-local (max, sum, o[hd]) go to scratch and the last CTA of
-// the kv head merges all chunks, loading every partial it needs at once.
-template <int HD, int G>
-__global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const AttnParams a) {
-    constexpr int P = ATTN_P;
-    constexpr int KST = HD + 2;  // padded K row (halves): lanes walking d stay on distinct banks
-    constexpr int DPL = HD / 32; // head dims per lane in P.V
-    __shared__ float qs[G][HD];
-    __shared__ __align__(16) uint16_t ks[P][KST];
-    __shared__ __align__(16) uint16_t vs[P][HD];
-    __shared__ unsigned int ticket;
+struct SyncThreads {
+    FDEV void operator()() const { __syncthreads(); }
+};
 
-    const int c = blockIdx.x, g = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    pdl_trigger();
-    pdl_wait();
-    const int pos = *a.pos_ptr;
-    if (pos < 0 || pos >= a.max_seq) {
-        if (c == 0 && g == 0 && tid == 0) *a.err = 1;
-        return;
-    }
+// Shared memory one attention unit needs (qs, padded K rows, V rows).
+template <int HD, int G>
+constexpr int attn_smem_bytes() {
+    return G * HD * 4 + ATTN_P * (HD + 2) * 2 + ATTN_P * HD * 2;
+}
+
+// One (chunk c, kv head g) unit, run by ATTN_THREADS threads synchronised by
+// `bar`: warps own query heads (G <= 8: one head per warp, lanes over positions
+// for q.K and over head dims for P.V, softmax by shuffles); the chunk-local
+// (max, sum, o[hd]) go to scratch and the last unit of the kv head merges all
+// chunks, loading every partial it needs at once.
+template <int HD, int G, class Bar>
+FDEV void attn_unit(const AttnParams &a, int c, int g, int pos, uint8_t *sm, unsigned int *ticket, Bar bar) {
+    constexpr int P = ATTN_P;
+    constexpr int KST = HD + 2;   // padded K row (halves): lanes walking d stay on distinct banks
+    constexpr int DPL = HD / 32;  // head dims per lane in P.V
+    float(*qs)[HD] = reinterpret_cast<float(*)[HD]>(sm);
+    uint16_t(*ks)[KST] = reinterpret_cast<uint16_t(*)[KST]>(sm + G * HD * 4);
+    uint16_t(*vs)[HD] = reinterpret_cast<uint16_t(*)[HD]>(sm + G * HD * 4 + P * KST * 2);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int seq = pos + 1;
     const int nch = (seq + P - 1) / P;
-    if (c >= nch) return;
     const int t0 = c * P;
     const int nt = min(P, seq - t0);
     const int kvd = a.n_kv * HD;
@@ -95,7 +96,7 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const AttnPar
             kp[(size_t)tn * HD + j + HD / 2] = __half_as_ushort(__float2half_rn(y2));
         }
         for (int j = tid; j < HD; j += ATTN_THREADS) vp[(size_t)tn * HD + j] = __half_as_ushort(__float2half_rn(__ldcg(vr + j)));
-        __syncthreads();  // block-wide visibility of the appended row
+        bar();  // unit-wide visibility of the appended row
     }
 
     // stage the chunk: K with padded rows, V dense (16-byte loads)
@@ -108,7 +109,7 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const AttnPar
         kd[0] = kv4.x; kd[1] = kv4.y; kd[2] = kv4.z; kd[3] = kv4.w;
         *reinterpret_cast<uint4 *>(&vs[t][8 * k8]) = vv4;
     }
-    __syncthreads();
+    bar();
 
     float *pg = a.part + (size_t)g * a.max_chunks * G * (HD + 2);
     for (int h = warp; h < G; h += ATTN_THREADS / 32) {
@@ -161,46 +162,63 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const AttnPar
         }
     }
     __threadfence();
-    __syncthreads();
-    if (tid == 0) ticket = atomicAdd(a.count + g, 1u);
-    __syncthreads();
-    if (ticket != (unsigned)(nch - 1)) return;
-
-    // last CTA of this kv head: merge the nch chunks of every head (warp per head)
-    __threadfence();
-    for (int h = warp; h < G; h += ATTN_THREADS / 32) {
-        float M = -INFINITY;
-        for (int k = lane; k < nch; k += 32) M = fmaxf(M, __ldcg(pg + ((size_t)k * G + h) * (HD + 2)));
+    bar();
+    if (tid == 0) *ticket = atomicAdd(a.count + g, 1u);
+    bar();
+    const bool last = *ticket == (unsigned)(nch - 1);
+    if (last) {
+        // last unit of this kv head: merge the nch chunks of every head (warp per head)
+        __threadfence();
+        for (int h = warp; h < G; h += ATTN_THREADS / 32) {
+            float M = -INFINITY;
+            for (int k = lane; k < nch; k += 32) M = fmaxf(M, __ldcg(pg + ((size_t)k * G + h) * (HD + 2)));
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-        float Lsum = 0.f;
-        float O[DPL];
+            for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+            float Lsum = 0.f;
+            float O[DPL];
 #pragma unroll
-        for (int j = 0; j < DPL; j++) O[j] = 0.f;
-        for (int k0 = 0; k0 < nch; k0 += 32) {
-            // lane k0+lane fetches its chunk's weight; partial outputs loaded per chunk
-            const int kk = k0 + lane;
-            float w = 0.f;
-            if (kk < nch) {
-                const float *e = pg + ((size_t)kk * G + h) * (HD + 2);
-                w = expf(__ldcg(e) - M);
-                Lsum = fmaf(w, __ldcg(e + 1), Lsum);
-            }
-            const int kn = min(32, nch - k0);
+            for (int j = 0; j < DPL; j++) O[j] = 0.f;
+            for (int k0 = 0; k0 < nch; k0 += 32) {
+                const int kk = k0 + lane;
+                float w = 0.f;
+                if (kk < nch) {
+                    const float *e = pg + ((size_t)kk * G + h) * (HD + 2);
+                    w = expf(__ldcg(e) - M);
+                    Lsum = fmaf(w, __ldcg(e + 1), Lsum);
+                }
+                const int kn = min(32, nch - k0);
 #pragma unroll 4
-            for (int k = 0; k < kn; k++) {
-                const float wk = __shfl_sync(0xffffffffu, w, k);
-                const float *e = pg + ((size_t)(k0 + k) * G + h) * (HD + 2) + 2;
+                for (int k = 0; k < kn; k++) {
+                    const float wk = __shfl_sync(0xffffffffu, w, k);
+                    const float *e = pg + ((size_t)(k0 + k) * G + h) * (HD + 2) + 2;
 #pragma unroll
-                for (int j = 0; j < DPL; j++) O[j] = fmaf(wk, __ldcg(e + lane + 32 * j), O[j]);
+                    for (int j = 0; j < DPL; j++) O[j] = fmaf(wk, __ldcg(e + lane + 32 * j), O[j]);
+                }
             }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) Lsum += __shfl_xor_sync(0xffffffffu, Lsum, o);
+#pragma unroll
+            for (int j = 0; j < DPL; j++) a.out[(size_t)(g * G + h) * HD + lane + 32 * j] = O[j] / Lsum;
         }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) Lsum += __shfl_xor_sync(0xffffffffu, Lsum, o);
-#pragma unroll
-        for (int j = 0; j < DPL; j++) a.out[(size_t)(g * G + h) * HD + lane + 32 * j] = O[j] / Lsum;
+        if (tid == 0) a.count[g] = 0u;
     }
-    if (tid == 0) a.count[g] = 0u;
+    bar();  // shared memory and the ticket are reused by the next unit
+}
+
+template <int HD, int G>
+__global__ void __launch_bounds__(ATTN_THREADS) attn_decode_kernel(const AttnParams a) {
+    __shared__ __align__(16) uint8_t sm[attn_smem_bytes<HD, G>()];
+    __shared__ unsigned int ticket;
+    pdl_trigger();
+    pdl_wait();
+    const int pos = *a.pos_ptr;
+    if (pos < 0 || pos >= a.max_seq) {
+        if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) *a.err = 1;
+        return;
+    }
+    const int nch = (pos + ATTN_P) / ATTN_P;
+    if ((int)blockIdx.x >= nch) return;
+    attn_unit<HD, G>(a, blockIdx.x, blockIdx.y, pos, sm, &ticket, SyncThreads());
 }
 
 // Embedding row of `*token` (fp16-rounded like the reference's fp16 buf_x,

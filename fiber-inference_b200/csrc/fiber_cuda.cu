@@ -20,6 +20,7 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <algorithm>
 #include <vector>
 
 #include "attention.cuh"
@@ -27,6 +28,7 @@
 #include "gemv.cuh"
 #include "gemv_tc.cuh"
 #include "launch.cuh"
+#include "persistent.cuh"
 
 using namespace fiber;
 
@@ -362,6 +364,15 @@ struct gpu_context {
     std::vector<float> logits_copy;
     Graph g_step, g_loop;
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+    // persistent one-kernel step (persistent.cuh)
+    int mode = 0;                  // 0: persistent kernel when supported, 1: one kernel per phase
+    bool pk_ok = false;            // the model fits the persistent kernel
+    PPhase *d_phases = nullptr;
+    std::vector<PPhase> phases;
+    unsigned int *d_bar = nullptr;
+    int pk_ring = 0, pk_xfr = 0, pk_xs = 0, pk_grid = 0;
+    size_t pk_smem = 0;
+    void *pk_kernel = nullptr;
 };
 
 static void free_graph(Graph &g) {
@@ -377,7 +388,7 @@ extern "C" void fiber_cuda_free(fiber_ctx_t *c) {
     free_graph(c->g_step);
     free_graph(c->g_loop);
     void *dev[] = {c->d_data, c->x, c->qkv, c->att, c->h, c->logits, c->rope, c->io, c->rec,
-                   c->att_part, c->att_cnt, c->am_part, c->am_cnt};
+                   c->att_part, c->att_cnt, c->am_part, c->am_cnt, c->d_phases, c->d_bar};
     for (void *p : dev)
         if (p) cudaFree(p);
     if (c->h_io) cudaFreeHost(c->h_io);
@@ -386,6 +397,153 @@ extern "C" void fiber_cuda_free(fiber_ctx_t *c) {
     if (c->ev1) cudaEventDestroy(c->ev1);
     if (c->stream) cudaStreamDestroy(c->stream);
     delete c;
+}
+
+static bool tc_type_ok(int t) { return t == T_Q4_K || t == T_Q6_K || t == T_F16; }
+
+static PSeg make_pseg(const uint8_t *w, const uint8_t *w2, int type, int rows, int out_off, int cols) {
+    PSeg sg;
+    memset(&sg, 0, sizeof(sg));
+    sg.w = w;
+    sg.w2 = w2;
+    sg.type = type;
+    sg.rows = rows;
+    sg.out_off = out_off;
+    sg.tiles = (rows + TC_M - 1) / TC_M;
+    sg.row_bytes = cols / 256 * block_bytes(type);
+    sg.per_row = sg.row_bytes % 16 == 0;
+    sg.stride = sg.per_row ? sg.row_bytes + (16 - sg.row_bytes % 128 + 128) % 128 : sg.row_bytes;
+    return sg;
+}
+
+template <int HD, int G>
+static void *pk_kernel_ptr() {
+    return reinterpret_cast<void *>(decode_persistent_kernel<HD, G>);
+}
+
+// Phase table and launch geometry of the persistent step kernel; leaves
+// pk_ok false (per-phase kernels only) when the model does not fit it.
+static int pk_build(gpu_context *c) {
+    const model_params_t &p = c->p;
+    const int dim = p.dim, ffn = p.ffn_dim, kvd = c->kvd, hd = p.head_dim;
+    c->pk_ok = false;
+    bool types_ok = tc_type_ok(c->t_out);
+    for (const LayerDev &d : c->L) {
+        const int ts[7] = {d.tq, d.tk, d.tv, d.to, d.t1, d.t2, d.t3};
+        for (int t : ts) types_ok = types_ok && tc_type_ok(t);
+        int distinct = 1 + (d.tk != d.tq) + (d.tv != d.tq && d.tv != d.tk);
+        types_ok = types_ok && distinct <= 2;
+    }
+#define PK_CASE(H, GG) \
+    if (hd == H && c->G == GG) c->pk_kernel = pk_kernel_ptr<H, GG>();
+    PK_CASE(64, 1) PK_CASE(64, 2) PK_CASE(64, 4) PK_CASE(64, 8)
+    PK_CASE(128, 1) PK_CASE(128, 2) PK_CASE(128, 4) PK_CASE(128, 8)
+#undef PK_CASE
+    if (!types_ok || !c->pk_kernel) return FIBER_OK;
+
+    std::vector<PPhase> &ph = c->phases;
+    ph.clear();
+    auto base = [&](int kind, int cols, int layer) {
+        PPhase f;
+        memset(&f, 0, sizeof(f));
+        f.kind = kind;
+        f.cols = cols;
+        f.layer = layer;
+        f.nmat = 1;
+        f.eps = p.rms_norm_eps;
+        return f;
+    };
+    for (uint32_t l = 0; l < p.n_layers; l++) {
+        const LayerDev &d = c->L[l];
+        PPhase q = base(PH_QKV, dim, l);
+        q.nseg = 3;
+        q.seg[0] = make_pseg(d.wq, nullptr, d.tq, dim, 0, dim);
+        q.seg[1] = make_pseg(d.wk, nullptr, d.tk, kvd, dim, dim);
+        q.seg[2] = make_pseg(d.wv, nullptr, d.tv, kvd, dim + kvd, dim);
+        q.x = c->x;
+        q.norm_w = d.attn_norm;
+        q.y = c->qkv;
+        q.embed_in = l == 0;
+        ph.push_back(q);
+        ph.push_back(base(PH_ATTN, dim, l));
+        PPhase o = base(PH_RESID, dim, l);
+        o.nseg = 1;
+        o.seg[0] = make_pseg(d.wo, nullptr, d.to, dim, 0, dim);
+        o.x = c->att;
+        o.resid = c->x;
+        ph.push_back(o);
+        PPhase u = base(PH_SWIGLU, dim, l);
+        u.nseg = 1;
+        u.nmat = 2;
+        u.seg[0] = make_pseg(d.w1, d.w3, d.t1, ffn, 0, dim);
+        u.x = c->x;
+        u.norm_w = d.ffn_norm;
+        u.y = c->h;
+        ph.push_back(u);
+        PPhase dn = base(PH_RESID, ffn, l);
+        dn.nseg = 1;
+        dn.seg[0] = make_pseg(d.w2, nullptr, d.t2, dim, 0, ffn);
+        dn.x = c->h;
+        dn.resid = c->x;
+        ph.push_back(dn);
+    }
+    PPhase lm = base(PH_LM, dim, 0);
+    lm.nseg = 1;
+    lm.seg[0] = make_pseg(c->out, nullptr, c->t_out, p.vocab_size, 0, dim);
+    lm.x = c->x;
+    lm.norm_w = c->out_norm;
+    lm.y = c->logits;
+    ph.push_back(lm);
+    size_t max_tile = 0;
+    int xfr = 0;
+    for (PPhase &f : ph) {
+        f.n_tiles = 0;
+        for (int k = 0; k < f.nseg; k++) {
+            f.n_tiles += f.seg[k].tiles;
+            max_tile = std::max(max_tile, (size_t)f.nmat * TC_M * f.seg[k].stride);
+        }
+        int types = 1;
+        for (int k = 1; k < f.nseg; k++)
+            if (f.seg[k].type != f.seg[0].type) types = 2;
+        if (f.kind != PH_ATTN) xfr = std::max(xfr, types * (f.cols / 256) * 1024);
+    }
+    const int attn_need = [&] {
+        switch (hd * 16 + c->G) {
+        case 64 * 16 + 1: return attn_smem_bytes<64, 1>();
+        case 64 * 16 + 2: return attn_smem_bytes<64, 2>();
+        case 64 * 16 + 4: return attn_smem_bytes<64, 4>();
+        case 64 * 16 + 8: return attn_smem_bytes<64, 8>();
+        case 128 * 16 + 1: return attn_smem_bytes<128, 1>();
+        case 128 * 16 + 2: return attn_smem_bytes<128, 2>();
+        case 128 * 16 + 4: return attn_smem_bytes<128, 4>();
+        default: return attn_smem_bytes<128, 8>();
+        }
+    }();
+    int xs = std::max(dim, ffn);
+    if (xfr + xs * 4 < attn_need) xs = (attn_need - xfr + 3) / 4;
+    cudaFuncAttributes fa;
+    CK(cudaFuncGetAttributes(&fa, c->pk_kernel));
+    int optin = 0;
+    CK(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, c->device));
+    const long long avail = (long long)optin - (long long)fa.sharedSizeBytes - xfr - (long long)xs * 4 - 1024;
+    if (avail < (long long)max_tile) return FIBER_OK;  // tiles do not fit: per-phase kernels
+    c->pk_ring = (int)(avail & ~127ll);
+    c->pk_xfr = xfr;
+    c->pk_xs = xs;
+    c->pk_smem = (size_t)c->pk_ring + xfr + (size_t)xs * 4;
+    CK(cudaFuncSetAttribute(c->pk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)c->pk_smem));
+    int per_sm = 0, sms = 0;
+    CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, c->pk_kernel, PK_THREADS, c->pk_smem));
+    CK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, c->device));
+    if (per_sm < 1) return FIBER_OK;
+    c->pk_grid = sms;
+    CK(cudaMalloc(&c->d_phases, ph.size() * sizeof(PPhase)));
+    CK(cudaMemcpy(c->d_phases, ph.data(), ph.size() * sizeof(PPhase), cudaMemcpyHostToDevice));
+    CK(cudaMalloc(&c->d_bar, ph.size() * sizeof(unsigned int)));
+    CK(cudaMemset(c->d_bar, 0, ph.size() * sizeof(unsigned int)));
+    if (c->pk_grid > (int)((p.vocab_size + TC_M - 1) / TC_M)) c->pk_grid = (p.vocab_size + TC_M - 1) / TC_M;
+    c->pk_ok = true;
+    return FIBER_OK;
 }
 
 static int ctx_init(gpu_context *c, const model_t *m, int device, int max_seq) {
@@ -484,7 +642,7 @@ static int ctx_init(gpu_context *c, const model_t *m, int device, int max_seq) {
             tab[(size_t)pos * (hd / 2) + i] = make_float2(cosf(angle), sinf(angle));
         }
     CK(cudaMemcpy(c->rope, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice));
-    return FIBER_OK;
+    return pk_build(c);
 }
 
 extern "C" fiber_ctx_t *fiber_cuda_init(const model_t *m, int device, int max_batch, int max_seq) {
@@ -650,7 +808,48 @@ static cudaError_t enqueue_kind(gpu_context *c, const kv_cache_t *kv, int kind, 
 
 // Enqueue one full decode step. `loop` makes the lm_head feed its argmax back as
 // the next token and advance the position (device-resident greedy decoding).
+static cudaError_t enqueue_persistent(gpu_context *c, const kv_cache_t *kv, bool loop, cudaStream_t st) {
+    PParams P;
+    memset(&P, 0, sizeof(P));
+    P.phases = c->d_phases;
+    P.n_phases = (int)c->phases.size();
+    P.bar = c->d_bar;
+    P.embd = c->embd;
+    P.embd_type = c->t_embd;
+    P.dim = c->p.dim;
+    P.vocab = c->p.vocab_size;
+    P.x = c->x;
+    P.attn = attn_params(c, kv);
+    P.am_part = c->am_part;
+    P.am_count = c->am_cnt;
+    P.io_token = &c->io->token;
+    P.io_pos = &c->io->pos;
+    P.io_argmax = &c->io->argmax;
+    P.io_err = &c->io->err;
+    P.io_step = &c->io->step;
+    P.rec_tokens = c->rec;
+    P.loop = loop ? 1 : 0;
+    P.ring_bytes = c->pk_ring;
+    P.xf_bytes = c->pk_xfr;
+    P.xs_floats = c->pk_xs;
+    cudaError_t e = cudaMemsetAsync(c->d_bar, 0, c->phases.size() * sizeof(unsigned int), st);
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(c->pk_grid);
+    cfg.blockDim = dim3(PK_THREADS);
+    cfg.dynamicSmemBytes = c->pk_smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;  // all CTAs co-resident: the grid barriers rely on it
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    void *args[] = {&P};
+    return cudaLaunchKernelExC(&cfg, c->pk_kernel, args);
+}
+
 static cudaError_t enqueue_step(gpu_context *c, const kv_cache_t *kv, bool loop, cudaStream_t st) {
+    if (c->mode == 0 && c->pk_ok) return enqueue_persistent(c, kv, loop, st);
     cudaError_t e = enqueue_kind(c, kv, 6, 0, loop, st);
     for (uint32_t l = 0; l < c->p.n_layers && e == cudaSuccess; l++)
         for (int kind = 0; kind <= 4 && e == cudaSuccess; kind++) e = enqueue_kind(c, kv, kind, (int)l, loop, st);
@@ -679,6 +878,21 @@ static int get_graph(gpu_context *c, const kv_cache_t *kv, bool loop, cudaGraphE
     return FIBER_OK;
 }
 
+// One decode step on the context stream: the persistent kernel is launched
+// directly (one memset + one kernel), the per-phase path replays its graph.
+static int run_step(gpu_context *c, const kv_cache_t *kv, bool loop) {
+    if (c->mode == 0 && c->pk_ok) {
+        cudaError_t e = enqueue_persistent(c, kv, loop, c->stream);
+        if (e != cudaSuccess) return set_err(FIBER_ECUDA, "persistent step launch: %s", cudaGetErrorString(e));
+        return FIBER_OK;
+    }
+    cudaGraphExec_t g;
+    int rc = get_graph(c, kv, loop, &g);
+    if (rc != FIBER_OK) return rc;
+    CK(cudaGraphLaunch(g, c->stream));
+    return FIBER_OK;
+}
+
 static int check_kv(gpu_context *c, const kv_cache_t *kv) {
     if (!kv) return set_err(FIBER_EARG, "no KV cache");
     if (kv->device != c->device || kv->n_layers != (int)c->p.n_layers || kv->n_kv_heads != (int)c->p.n_kv_heads ||
@@ -690,6 +904,13 @@ static int check_kv(gpu_context *c, const kv_cache_t *kv) {
 static int device_status(gpu_context *c) {
     if (c->h_io->err == 1) return set_err(FIBER_EARG, "position out of range on the device");
     if (c->h_io->err == 2) return set_err(FIBER_EARG, "token id out of range on the device");
+    if (c->h_io->err == 4) {
+        // a bounded wait gave up mid-step: merge tickets may be left non-zero
+        cudaMemset(c->att_cnt, 0, (size_t)c->p.n_kv_heads * sizeof(unsigned int));
+        cudaMemset(c->am_cnt, 0, sizeof(unsigned int));
+        cudaDeviceSynchronize();
+        return set_err(FIBER_ETIMEOUT, "a device-side wait timed out during the decode step");
+    }
     return FIBER_OK;
 }
 
@@ -703,13 +924,11 @@ extern "C" int fiber_forward_token(fiber_ctx_t *c, kv_cache_t *kv, const int32_t
     if (pos[0] < 0 || pos[0] >= lim) return set_err(FIBER_EARG, "position %d outside [0, %d)", pos[0], lim);
     if (tokens[0] < 0 || tokens[0] >= (int)c->p.vocab_size) return set_err(FIBER_EARG, "token %d out of range", tokens[0]);
     CK(cudaSetDevice(c->device));
-    cudaGraphExec_t g;
-    if ((rc = get_graph(c, kv, false, &g)) != FIBER_OK) return rc;
     c->h_io->token = tokens[0];
     c->h_io->pos = pos[0];
     c->h_io->err = 0;
     CK(cudaMemcpyAsync(c->io, c->h_io, sizeof(StepIO), cudaMemcpyHostToDevice, c->stream));
-    CK(cudaGraphLaunch(g, c->stream));
+    if ((rc = run_step(c, kv, false)) != FIBER_OK) return rc;
     if (logits_or_null)
         CK(cudaMemcpyAsync(c->h_logits, c->logits, (size_t)c->p.vocab_size * 4, cudaMemcpyDeviceToHost, c->stream));
     CK(cudaMemcpyAsync(c->h_io, c->io, sizeof(StepIO), cudaMemcpyDeviceToHost, c->stream));
@@ -731,8 +950,25 @@ extern "C" int fiber_prefill(fiber_ctx_t *c, kv_cache_t *kv, const int32_t *toke
     return FIBER_OK;
 }
 
+extern "C" int fiber_set_decode_mode(fiber_ctx_t *c, int mode) {
+    if (!c || mode < 0 || mode > 1) return set_err(FIBER_EARG, "fiber_set_decode_mode: mode must be 0 or 1");
+    if (mode == 0 && !c->pk_ok) return set_err(FIBER_EUNSUPPORTED, "the persistent step kernel does not fit this model");
+    if (c->mode != mode) {
+        free_graph(c->g_step);
+        free_graph(c->g_loop);
+        c->mode = mode;
+    }
+    return FIBER_OK;
+}
+
+extern "C" int fiber_get_decode_mode(fiber_ctx_t *c) {
+    if (!c) return set_err(FIBER_EARG, "no context");
+    return (c->mode == 0 && c->pk_ok) ? 0 : 1;
+}
+
 extern "C" int fiber_step_launches(fiber_ctx_t *c) {
     if (!c) return set_err(FIBER_EARG, "no context");
+    if (c->mode == 0 && c->pk_ok) return 1;
     int n = 2;  // embed + lm_head
     for (const LayerDev &d : c->L) n += 4 + 1 + (d.tk != d.tq) + (d.tv != d.tk);
     return n;
@@ -813,10 +1049,13 @@ extern "C" int fiber_decode_greedy(fiber_ctx_t *c, kv_cache_t *kv, int32_t first
     c->h_io->err = 0;
     CK(cudaMemcpyAsync(c->io, c->h_io, sizeof(StepIO), cudaMemcpyHostToDevice, c->stream));
     {
-        cudaGraphExec_t g;
-        if ((rc = get_graph(c, kv, true, &g)) != FIBER_OK) return rc;
+        if (!(c->mode == 0 && c->pk_ok)) {  // build the graph before the timed region
+            cudaGraphExec_t g;
+            if ((rc = get_graph(c, kv, true, &g)) != FIBER_OK) return rc;
+        }
         CK(cudaEventRecord(c->ev0, c->stream));
-        for (int i = 0; i < n_steps; i++) CK(cudaGraphLaunch(g, c->stream));
+        for (int i = 0; i < n_steps; i++)
+            if ((rc = run_step(c, kv, true)) != FIBER_OK) return rc;
         CK(cudaEventRecord(c->ev1, c->stream));
         CK(cudaEventSynchronize(c->ev1));
         if (ms_out) CK(cudaEventElapsedTime(ms_out, c->ev0, c->ev1));

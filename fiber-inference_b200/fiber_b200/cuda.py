@@ -21,7 +21,8 @@ I32P = np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS")
 
 EXPORTED = [
     "fiber_last_error", "fiber_device_count", "fiber_cuda_init", "fiber_cuda_free", "fiber_forward_token",
-    "fiber_prefill", "fiber_decode_greedy", "fiber_step_launches", "fiber_time_kernel", "fiber_gemv",
+    "fiber_prefill", "fiber_decode_greedy", "fiber_step_launches", "fiber_set_decode_mode",
+    "fiber_get_decode_mode", "fiber_time_kernel", "fiber_gemv",
     "fiber_dequant", "fiber_gemv_host", "gpu_init", "gpu_free", "gpu_embed", "gpu_forward_token",
     "gpu_get_logits", "gpu_forward_classifier", "gpu_get_device", "kv_cache_init", "kv_cache_init_paged",
     "kv_cache_free", "kv_cache_write", "kv_cache_read", "fiber_gemv_argmax_noalloc",
@@ -58,6 +59,8 @@ def cuda_lib() -> C.CDLL:
         L.fiber_decode_greedy.argtypes = [C.c_void_p, C.c_void_p, C.c_int32, C.c_int, C.c_int, C.c_void_p,
                                           C.c_void_p]
         L.fiber_step_launches.argtypes = [C.c_void_p]
+        L.fiber_set_decode_mode.argtypes = [C.c_void_p, C.c_int]
+        L.fiber_get_decode_mode.argtypes = [C.c_void_p]
         L.fiber_time_kernel.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.POINTER(C.c_double),
                                         C.POINTER(C.c_double)]
         L.fiber_gemv.argtypes = [C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p]
@@ -205,6 +208,14 @@ class Context:
         _check(cuda_lib().fiber_decode_greedy(self.h, kv.addr, int(first_token), int(start_pos), int(n_steps),
                                               out.ctypes.data, C.addressof(ms)), "fiber_decode_greedy")
         return out, float(ms.value)
+
+    def set_mode(self, mode: int):
+        """0: persistent one-kernel step (default when supported); 1: one kernel per phase."""
+        _check(cuda_lib().fiber_set_decode_mode(self.h, int(mode)), "fiber_set_decode_mode")
+
+    @property
+    def mode(self) -> int:
+        return int(cuda_lib().fiber_get_decode_mode(self.h))
 
     def step_launches(self) -> int:
         n = cuda_lib().fiber_step_launches(self.h)

@@ -68,6 +68,15 @@ int fiber_prefill(fiber_ctx_t *ctx, kv_cache_t *kv, const int32_t *tokens, int n
 int fiber_decode_greedy(fiber_ctx_t *ctx, kv_cache_t *kv, int32_t first_token, int start_pos,
                         int n_steps, int32_t *h_tokens_out, float *ms_out);
 
+/* How a decode step runs. mode 0 (default when the model fits): one cooperative
+ * persistent kernel per step -- every SM streams its weight tiles of all phases
+ * through a shared-memory ring and the phases are separated by grid barriers.
+ * mode 1: one kernel per phase (2 + 5 * n_layers launches, PDL-chained).
+ * Both give the same tokens; mode 1 also serves models the persistent kernel
+ * does not cover (Q5_K weights). Returns FIBER_EUNSUPPORTED for mode 0 then. */
+int fiber_set_decode_mode(fiber_ctx_t *ctx, int mode);
+int fiber_get_decode_mode(fiber_ctx_t *ctx);
+
 /* Number of kernels one decode step launches (all of them this library's own). */
 int fiber_step_launches(fiber_ctx_t *ctx);
 

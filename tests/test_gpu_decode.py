@@ -21,16 +21,25 @@ def _rel_rms(a, b):
     return float(np.sqrt(np.mean((a.astype(np.float64) - b) ** 2)) / np.sqrt(np.mean(b.astype(np.float64) ** 2)))
 
 
+def _ctx(hm, max_seq, mode):
+    ctx = fb.Context(hm, max_seq=max_seq)
+    if mode == 0 and ctx.mode != 0:
+        pytest.skip("the persistent step kernel does not cover this model")
+    ctx.set_mode(mode)
+    return ctx
+
+
 def _prompt(vocab, n, seed):
     rng = np.random.default_rng(seed)
     return rng.integers(1, vocab, n).astype(np.int32)
 
 
+@pytest.mark.parametrize("mode", [0, 1])
 @pytest.mark.parametrize("name", ["q4km", "q5km", "f16", "q6k", "gqa8", "hd128"])
-def test_teacher_forced_logits(tiny_model, name):
+def test_teacher_forced_logits(tiny_model, name, mode):
     path = tiny_model(name)
     hm = fb.HostModel(path)
-    ctx = fb.Context(hm, max_seq=256)
+    ctx = _ctx(hm, 256, mode)
     kv = ctx.kv(256)
     om = orc.Model(path)
     st = om.state(256, kv_fp16=True)
@@ -43,11 +52,12 @@ def test_teacher_forced_logits(tiny_model, name):
         assert am == int(np.argmax(lg))
 
 
+@pytest.mark.parametrize("mode", [0, 1])
 @pytest.mark.parametrize("name", ["q4km", "q5km", "f16", "gqa8"])
-def test_greedy_tokens_match_oracle(tiny_model, name):
+def test_greedy_tokens_match_oracle(tiny_model, name, mode):
     path = tiny_model(name)
     hm = fb.HostModel(path)
-    ctx = fb.Context(hm, max_seq=512)
+    ctx = _ctx(hm, 512, mode)
     kv = ctx.kv(512)
     prompt = _prompt(hm.params.vocab_size, 16, 2)
     n_gen = 150
@@ -60,10 +70,11 @@ def test_greedy_tokens_match_oracle(tiny_model, name):
     assert dev.tolist() == want[1:].tolist()
 
 
-def test_device_loop_equals_host_loop(tiny_model):
+@pytest.mark.parametrize("mode", [0, 1])
+def test_device_loop_equals_host_loop(tiny_model, mode):
     path = tiny_model("gqa8")
     hm = fb.HostModel(path)
-    ctx = fb.Context(hm, max_seq=512)
+    ctx = _ctx(hm, 512, mode)
     prompt = _prompt(hm.params.vocab_size, 10, 3)
     kv1 = ctx.kv(512)
     first = ctx.prefill(kv1, prompt)
@@ -102,13 +113,14 @@ def test_kv_cache_contents_match_oracle(tiny_model):
             assert np.abs(v[pos] - ov).max() <= 2e-3 * (np.abs(ov).max() + 1e-3)
 
 
-def test_prefilled_long_context(tiny_model):
+@pytest.mark.parametrize("mode", [0, 1])
+def test_prefilled_long_context(tiny_model, mode):
     """Long context over many KV pages: cache pre-filled with seeded N(0,1)
     keys/values (as in the long-context workload), then greedy decode."""
     path = tiny_model("gqa8")
     hm = fb.HostModel(path)
     p = hm.params
-    ctx = fb.Context(hm, max_seq=1024)
+    ctx = _ctx(hm, 1024, mode)
     kv = ctx.kv(1024)
     om = orc.Model(path)
     st = om.state(1024, kv_fp16=True)
@@ -170,3 +182,23 @@ def test_errors_are_reported_not_faulted(tiny_model):
         ctx.decode_greedy(kv, 1, 60, 10)
     am, _ = ctx.forward(kv, 1, 0)  # context still usable
     assert 0 <= am < hm.params.vocab_size
+
+
+@pytest.mark.parametrize("name", ["q4km", "f16", "gqa8", "hd128", "q6k"])
+def test_persistent_and_per_phase_kernels_agree(tiny_model, name):
+    """Both ways of running a step compute the same arithmetic per row; the
+    token sequences must match and the logits agree to fp32 reordering noise."""
+    path = tiny_model(name)
+    hm = fb.HostModel(path)
+    a = _ctx(hm, 256, 0)
+    b = _ctx(hm, 256, 1)
+    ka, kb = a.kv(256), b.kv(256)
+    toks = _prompt(hm.params.vocab_size, 70, 9)
+    for pos, t in enumerate(toks):
+        ia, la = a.forward(ka, int(t), pos)
+        ib, lb = b.forward(kb, int(t), pos)
+        assert np.abs(la - lb).max() <= 1e-4 * (np.abs(lb).max() + 1), pos
+        assert ia == ib, pos
+    ga, _ = a.decode_greedy(ka, 3, len(toks), 60)
+    gb, _ = b.decode_greedy(kb, 3, len(toks), 60)
+    assert ga.tolist() == gb.tolist()
