@@ -370,7 +370,9 @@ struct gpu_context {
     PPhase *d_phases = nullptr;
     std::vector<PPhase> phases;
     unsigned int *d_bar = nullptr;
-    int pk_ring = 0, pk_xfr = 0, pk_xs = 0, pk_grid = 0;
+    uint16_t *pk_gf[4] = {};       // phase-input fragments: QKV/lm_head, Wo, gate/up, down
+    float *pk_ss[2] = {};          // per-CTA sums of squares: before gate/up, before QKV/lm_head
+    int pk_ring = 0, pk_xfr = 0, pk_xs = 0, pk_nw = 0, pk_grid = 0;
     size_t pk_smem = 0;
     void *pk_kernel = nullptr;
 };
@@ -388,7 +390,8 @@ extern "C" void fiber_cuda_free(fiber_ctx_t *c) {
     free_graph(c->g_step);
     free_graph(c->g_loop);
     void *dev[] = {c->d_data, c->x, c->qkv, c->att, c->h, c->logits, c->rope, c->io, c->rec,
-                   c->att_part, c->att_cnt, c->am_part, c->am_cnt, c->d_phases, c->d_bar};
+                   c->att_part, c->att_cnt, c->am_part, c->am_cnt, c->d_phases, c->d_bar,
+                   c->pk_gf[0], c->pk_gf[1], c->pk_gf[2], c->pk_gf[3], c->pk_ss[0], c->pk_ss[1]};
     for (void *p : dev)
         if (p) cudaFree(p);
     if (c->h_io) cudaFreeHost(c->h_io);
@@ -494,8 +497,50 @@ static int pk_build(gpu_context *c) {
     lm.norm_w = c->out_norm;
     lm.y = c->logits;
     ph.push_back(lm);
-    size_t max_tile = 0;
-    int xfr = 0;
+    int sms = 0;
+    CK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, c->device));
+    const int grid = std::min(sms, (int)((p.vocab_size + TC_M - 1) / TC_M));
+    if (grid > 256) return FIBER_OK;  // per-CTA partial sums are staged in 256 slots
+
+    // phase-input hand-off: each phase's epilogue writes the next phase's input
+    // as fragments (one layout per weight type of the next phase) and, before a
+    // normed phase, per-CTA sums of squares
+    const size_t gf_bytes[4] = {2 * (size_t)dim * 4, 2 * (size_t)dim * 4, 2 * (size_t)dim * 4, 2 * (size_t)ffn * 4};
+    for (int k = 0; k < 4; k++) CK(cudaMalloc(&c->pk_gf[k], gf_bytes[k]));
+    for (int k = 0; k < 2; k++) {
+        CK(cudaMalloc(&c->pk_ss[k], 256 * sizeof(float)));
+        CK(cudaMemset(c->pk_ss[k], 0, 256 * sizeof(float)));
+    }
+    auto layouts = [](const PPhase &f, int &a, int &b) {
+        a = f.seg[0].type;
+        b = -1;
+        for (int k = 1; k < f.nseg; k++)
+            if (f.seg[k].type != a && b < 0) b = f.seg[k].type;
+    };
+    for (size_t i = 0; i + 1 < ph.size(); i++) {
+        PPhase &f = ph[i], &nx = ph[i + 1];
+        if (f.kind == PH_QKV) continue;  // q/k/v go to the attention phase
+        layouts(nx, f.out_types[0], f.out_types[1]);
+        f.n_out = nx.cols;
+        if (f.kind == PH_ATTN) {
+            f.gf_out = c->pk_gf[1];
+        } else if (f.kind == PH_SWIGLU) {
+            f.gf_out = c->pk_gf[3];
+        } else {  // Wo (next: gate/up) or down (next: QKV or lm_head), both residual
+            const bool wo = nx.kind == PH_SWIGLU;
+            f.gf_out = c->pk_gf[wo ? 2 : 0];
+            f.nw_out = nx.norm_w;
+            f.ss_out = nx.norm_w ? c->pk_ss[wo ? 0 : 1] : nullptr;
+        }
+        if (!nx.embed_in) {
+            nx.gf_in = reinterpret_cast<const uint2 *>(f.gf_out);
+            nx.ss_in = f.ss_out;
+        }
+    }
+    size_t max_tile = (size_t)4 * ATTN_P * hd;  // attention: one K page and one V page (fp16)
+    // the Wo staging merges attention partials through the fragment region:
+    // [n_heads][units per KV head] weights and [n_heads] sums
+    int xfr = (int)(((size_t)p.n_heads * (3 * std::max(1, grid / (int)p.n_kv_heads) + 1) * 4 + 1023) & ~(size_t)1023);
     for (PPhase &f : ph) {
         f.n_tiles = 0;
         for (int k = 0; k < f.nseg; k++) {
@@ -525,23 +570,28 @@ static int pk_build(gpu_context *c) {
     CK(cudaFuncGetAttributes(&fa, c->pk_kernel));
     int optin = 0;
     CK(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, c->device));
-    const long long avail = (long long)optin - (long long)fa.sharedSizeBytes - xfr - (long long)xs * 4 - 1024;
+    const int nw = dim;  // RMSNorm weights (every normed phase reads dim columns)
+    const long long avail = (long long)optin - (long long)fa.sharedSizeBytes - xfr - (long long)(xs + nw) * 4 - 1024;
     if (avail < (long long)max_tile) return FIBER_OK;  // tiles do not fit: per-phase kernels
     c->pk_ring = (int)(avail & ~127ll);
+    // tuning knob: cap the weight ring (KB); the default is all shared memory left
+    if (const char *e = getenv("FIBER_PK_RING_KB")) {
+        const long long cap = atoll(e) * 1024;
+        if (cap >= (long long)max_tile && cap < c->pk_ring) c->pk_ring = (int)(cap & ~127ll);
+    }
     c->pk_xfr = xfr;
     c->pk_xs = xs;
-    c->pk_smem = (size_t)c->pk_ring + xfr + (size_t)xs * 4;
+    c->pk_nw = nw;
+    c->pk_smem = (size_t)c->pk_ring + xfr + (size_t)(xs + nw) * 4;
     CK(cudaFuncSetAttribute(c->pk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)c->pk_smem));
-    int per_sm = 0, sms = 0;
+    int per_sm = 0;
     CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, c->pk_kernel, PK_THREADS, c->pk_smem));
-    CK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, c->device));
     if (per_sm < 1) return FIBER_OK;
-    c->pk_grid = sms;
+    c->pk_grid = grid;
     CK(cudaMalloc(&c->d_phases, ph.size() * sizeof(PPhase)));
     CK(cudaMemcpy(c->d_phases, ph.data(), ph.size() * sizeof(PPhase), cudaMemcpyHostToDevice));
     CK(cudaMalloc(&c->d_bar, ph.size() * sizeof(unsigned int)));
     CK(cudaMemset(c->d_bar, 0, ph.size() * sizeof(unsigned int)));
-    if (c->pk_grid > (int)((p.vocab_size + TC_M - 1) / TC_M)) c->pk_grid = (p.vocab_size + TC_M - 1) / TC_M;
     c->pk_ok = true;
     return FIBER_OK;
 }
@@ -619,7 +669,8 @@ static int ctx_init(gpu_context *c, const model_t *m, int device, int max_seq) {
     CK(cudaMalloc(&c->rope, (size_t)max_seq * (p.head_dim / 2) * sizeof(float2)));
     CK(cudaMalloc(&c->io, sizeof(StepIO)));
     CK(cudaMalloc(&c->rec, (size_t)max_seq * 4));
-    CK(cudaMalloc(&c->att_part, (size_t)p.n_kv_heads * c->max_chunks * c->G * (p.head_dim + 2) * 4));
+    // records of hd + 2 floats (per-phase kernels) or PK_REC(hd) floats (persistent kernel)
+    CK(cudaMalloc(&c->att_part, (size_t)p.n_kv_heads * c->max_chunks * c->G * (p.head_dim + 4) * 4));
     CK(cudaMalloc(&c->att_cnt, (size_t)p.n_kv_heads * 4));
     CK(cudaMalloc(&c->am_part, (size_t)lm_tiles * sizeof(float2)));
     CK(cudaMalloc(&c->am_cnt, 4));
@@ -808,7 +859,8 @@ static cudaError_t enqueue_kind(gpu_context *c, const kv_cache_t *kv, int kind, 
 
 // Enqueue one full decode step. `loop` makes the lm_head feed its argmax back as
 // the next token and advance the position (device-resident greedy decoding).
-static cudaError_t enqueue_persistent(gpu_context *c, const kv_cache_t *kv, bool loop, cudaStream_t st) {
+static cudaError_t enqueue_persistent(gpu_context *c, const kv_cache_t *kv, bool loop, cudaStream_t st,
+                                      unsigned long long *trace = nullptr) {
     PParams P;
     memset(&P, 0, sizeof(P));
     P.phases = c->d_phases;
@@ -832,6 +884,8 @@ static cudaError_t enqueue_persistent(gpu_context *c, const kv_cache_t *kv, bool
     P.ring_bytes = c->pk_ring;
     P.xf_bytes = c->pk_xfr;
     P.xs_floats = c->pk_xs;
+    P.nw_floats = c->pk_nw;
+    P.trace = trace;
     cudaError_t e = cudaMemsetAsync(c->d_bar, 0, c->phases.size() * sizeof(unsigned int), st);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
@@ -972,6 +1026,36 @@ extern "C" int fiber_step_launches(fiber_ctx_t *c) {
     int n = 2;  // embed + lm_head
     for (const LayerDev &d : c->L) n += 4 + 1 + (d.tk != d.tq) + (d.tv != d.tk);
     return n;
+}
+
+extern "C" int fiber_trace_step(fiber_ctx_t *c, kv_cache_t *kv, int token, int pos, uint64_t *out, size_t cap,
+                                int *n_phases, int *n_ctas) {
+    if (!c || !out || !n_phases || !n_ctas) return set_err(FIBER_EARG, "fiber_trace_step: null argument");
+    if (!c->pk_ok) return set_err(FIBER_EUNSUPPORTED, "the persistent step kernel does not cover this model");
+    int rc = check_kv(c, kv);
+    if (rc) return rc;
+    const int lim = c->max_seq < kv->max_seq ? c->max_seq : kv->max_seq;
+    if (pos < 0 || pos >= lim) return set_err(FIBER_EARG, "position %d outside [0, %d)", pos, lim);
+    if (token < 0 || token >= (int)c->p.vocab_size) return set_err(FIBER_EARG, "token %d out of range", token);
+    const size_t n = c->phases.size() * (size_t)c->pk_grid * PK_TRACE_FIELDS;
+    *n_phases = (int)c->phases.size();
+    *n_ctas = c->pk_grid;
+    if (cap < n) return set_err(FIBER_EARG, "trace buffer holds %zu values, %zu needed", cap, n);
+    CK(cudaSetDevice(c->device));
+    unsigned long long *d_tr = nullptr;
+    CK(cudaMalloc(&d_tr, n * 8));
+    cudaError_t e = cudaMemsetAsync(d_tr, 0, n * 8, c->stream);
+    c->h_io->token = token;
+    c->h_io->pos = pos;
+    c->h_io->err = 0;
+    if (e == cudaSuccess) e = cudaMemcpyAsync(c->io, c->h_io, sizeof(StepIO), cudaMemcpyHostToDevice, c->stream);
+    if (e == cudaSuccess) e = enqueue_persistent(c, kv, false, c->stream, d_tr);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(out, d_tr, n * 8, cudaMemcpyDeviceToHost, c->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(c->h_io, c->io, sizeof(StepIO), cudaMemcpyDeviceToHost, c->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+    cudaFree(d_tr);
+    if (e != cudaSuccess) return set_err(FIBER_ECUDA, "trace step: %s", cudaGetErrorString(e));
+    return device_status(c);
 }
 
 static double kind_bytes(gpu_context *c, int kind, int l, int pos) {

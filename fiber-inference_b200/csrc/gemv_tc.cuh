@@ -109,14 +109,24 @@ FDEV void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_
 template <int T>
 struct TcType;
 
+#define HDCE __host__ __device__ constexpr inline
+
+// elem(t, s, i): element (0..255) of a super-block that lane t's k-slot i of
+// k-step s holds; pos(kk, t, s, i) is its inverse (checked exhaustively below).
 template <>
 struct TcType<T_Q4_K> {
     static constexpr int BB = 144;
     // word u = s/2 of the lane's 32 quant bytes [32t, 32t+32); v = s%2
-    static FDEV int elem(int t, int s, int i) {
+    static HDCE int elem(int t, int s, int i) {
         const int u = s >> 1, v = s & 1;
         const int base = 64 * t + 4 * u + v;
         return base + (i & 1) * 2 + (i >> 1) * 32;
+    }
+    static HDCE void pos(int kk, int &t, int &s, int &i) {
+        t = kk >> 6;
+        const int r = kk & 63, r2 = r & 31;
+        s = 2 * (r2 >> 2) + (r2 & 1);
+        i = 2 * (r >> 5) + ((r2 >> 1) & 1);
     }
 };
 
@@ -124,19 +134,44 @@ template <>
 struct TcType<T_Q6_K> {
     static constexpr int BB = 210;
     // lane t: half h = t/2, positions l in [16*(t%2), +16); step s = 4u + k
-    static FDEV int elem(int t, int s, int i) {
+    static HDCE int elem(int t, int s, int i) {
         const int h = t >> 1, lh = t & 1, u = s >> 2, k = s & 3;
         const int l0 = 16 * lh + 4 * u;
         const int di = (i == 0) ? 0 : (i == 1) ? 2 : (i == 2) ? 1 : 3;
         return 128 * h + l0 + di + 32 * k;
+    }
+    static HDCE void pos(int kk, int &t, int &s, int &i) {
+        const int h = kk >> 7, r = kk & 127, k = r >> 5, l = r & 31;
+        const int di = l & 3;
+        t = 2 * h + (l >> 4);
+        s = 4 * ((l >> 2) & 3) + k;
+        i = (di == 1) ? 2 : (di == 2) ? 1 : di;
     }
 };
 
 template <>
 struct TcType<T_F16> {
     static constexpr int BB = 512;
-    static FDEV int elem(int t, int s, int i) { return 16 * s + 2 * t + (i & 1) + (i >> 1) * 8; }
+    static HDCE int elem(int t, int s, int i) { return 16 * s + 2 * t + (i & 1) + (i >> 1) * 8; }
+    static HDCE void pos(int kk, int &t, int &s, int &i) {
+        s = kk >> 4;
+        const int r = kk & 15, r2 = r & 7;
+        t = r2 >> 1;
+        i = 2 * (r >> 3) + (r2 & 1);
+    }
 };
+
+template <int T>
+HDCE bool tc_pos_roundtrip() {
+    for (int kk = 0; kk < 256; kk++) {
+        int t = 0, s = 0, i = 0;
+        TcType<T>::pos(kk, t, s, i);
+        if (t < 0 || t > 3 || s < 0 || s > 15 || i < 0 || i > 3 || TcType<T>::elem(t, s, i) != kk) return false;
+    }
+    return true;
+}
+static_assert(tc_pos_roundtrip<T_Q4_K>() && tc_pos_roundtrip<T_Q6_K>() && tc_pos_roundtrip<T_F16>(),
+              "fragment slot maps must be inverse bijections on a super-block");
 
 // ---- per-type tile dot: accumulate one super-block of rows g, g+8 --------------------
 

@@ -5,20 +5,25 @@
 // latency and an x-staging/epilogue chain (~5-10 us) for ~0.5-2 us of data.
 // Here every SM runs one CTA for the whole step:
 //   * warp 8 (producer, one lane) walks the CTA's weight tiles of ALL phases in
-//     consumption order and streams them with cp.async.bulk into a shared-memory
-//     byte ring (FIFO, an mbarrier full/empty pair per tile in flight), so weight
-//     loading runs ahead across phase boundaries and barrier waits;
-//   * warps 0..7 (consumers) wait for the phase's input (grid barrier), stage x
-//     as fp16 hi/lo fragments (through the RMSNorm where the reference has one),
-//     decode + multiply each tile on the tensor cores (TcDot) and run the
-//     phase's epilogue; consumers synchronise among themselves with named
-//     barrier 1, never with the producer;
+//     consumption order, and the K/V pages of its attention units, and streams
+//     them with cp.async.bulk into a shared-memory byte ring (FIFO, an mbarrier
+//     full/empty pair per tile in flight), so loading runs ahead across phase
+//     boundaries and barrier waits;
+//   * warps 0..7 (consumers) wait for the phase's input (grid barrier), copy it
+//     in as fp16 hi/lo MMA fragments, decode + multiply each tile on the tensor
+//     cores (TcDot) and run the phase's epilogue, which writes the next phase's
+//     input fragments (times the next RMSNorm weights) and per-CTA sums of
+//     squares, so the RMSNorm scale is applied to the next phase's dot products;
+//     consumers synchronise among themselves with named barrier 1, never with
+//     the producer;
 //   * between phases a grid barrier: one arrive counter per phase in global
 //     memory (zeroed before each launch), polled with bounded spins.
 // Phases per token: per layer QKV (layer 0 stages the embedding row itself),
-// attention (RoPE, KV append, split-K chunks merged by the last CTA of each KV
-// head), Wo (+residual), gate/up (+RMSNorm, SwiGLU), down (+residual); then
-// lm_head (+RMSNorm, greedy argmax).
+// attention (RoPE, KV append, per-unit partial softmax over prefetched pages),
+// attention merged by the last unit of each KV head into Wo's input, Wo (+residual), gate/up
+// (+RMSNorm, SwiGLU), down (+residual); then lm_head (+RMSNorm, greedy argmax).
+// Each phase body is a separate non-inlined function so that its registers are
+// allocated on its own; the per-CTA state lives in shared memory.
 // Every wait is bounded: on timeout the kernel records an error code (4) in the
 // step state, stops issuing work and returns once its own copies have landed.
 #pragma once
@@ -31,7 +36,16 @@ constexpr int PK_CONSUMERS = 256;               // 8 warps
 constexpr int PK_WARPS = PK_CONSUMERS / 32;
 constexpr int PK_THREADS = PK_CONSUMERS + 32;   // + producer warp
 constexpr int PK_NDESC = 16;                    // tiles in flight per CTA
+constexpr int PK_RPRE = 8;                      // residual rows prefetched for this many tiles
 constexpr long long PK_SPIN_LIMIT = 1ll << 22;  // grid-barrier polls (with ~100 ns sleeps)
+// Optional per-phase, per-CTA timeline (PParams::trace non-null), fields:
+//  0 globaltimer (ns) when the phase's grid barrier released the CTA
+//  1 SM cycles spent at that barrier     2 cycles staging the input vector
+//  3 cycles in the tile loop (or attention units)   4 of those waiting for tiles to land
+//  5 cycles from the end of the tile loop to the arrive
+//  6 producer: globaltimer (ns) after issuing the phase's last tile   7 producer: cycles waiting for ring space
+//  8 of field 2: cycles until the input statistics are reduced   9 of field 2: cycles staging the fragments
+constexpr int PK_TRACE_FIELDS = 10;
 
 enum : int { PH_QKV = 0, PH_ATTN = 1, PH_RESID = 2, PH_SWIGLU = 3, PH_LM = 4 };
 
@@ -46,7 +60,7 @@ struct PSeg {
     int per_row;    // 1: one bulk copy per row; 0: one per tile (plus a plain-copied tail)
 };
 
-struct PPhase {
+struct __align__(16) PPhase {
     int kind;
     int nseg;
     int nmat;       // 2 for SwiGLU (gate + up), else 1
@@ -59,8 +73,26 @@ struct PPhase {
     const float *norm_w;
     float *y;
     float *resid;
+    // input of the phase as MMA fragments (written by the previous phase): one
+    // layout per weight type of the phase, 4 * cols bytes each; null for the
+    // embedding input, which the phase stages itself
+    const uint2 *gf_in;
+    const float *ss_in;     // per-CTA sums of squares of the input (RMSNorm), or null
+    // outputs that feed the next phase: its input fragments (value * nw_out) and
+    // per-CTA sums of squares (ss_out), when this phase's outputs are its input
+    uint16_t *gf_out;
+    const float *nw_out;    // RMSNorm weights of the next phase, or null
+    float *ss_out;          // [gridDim.x] partial sums of squares, or null
+    int out_types[2];       // weight types of the next phase's layouts (-1: none)
+    int n_out;              // elements of the next phase's input
+    int pad_;
     PSeg seg[3];
 };
+static_assert(sizeof(PPhase) % 16 == 0 && sizeof(PPhase) / 16 <= 32, "phase descriptors are copied in 16-byte chunks");
+
+// Largest activation magnitude the fp16 hi/lo fragments represent; beyond it
+// the step reports error 5 instead of computing with an overflowed input.
+constexpr float PK_FRAG_MAX = 65504.0f;
 
 struct PParams {
     const PPhase *phases;  // device array
@@ -79,12 +111,39 @@ struct PParams {
     int ring_bytes;
     int xf_bytes;          // fragment region (one or two staged types)
     int xs_floats;         // fp32 staging copy of x
+    int nw_floats;         // RMSNorm weights of the phase (prefetched)
+    unsigned long long *trace;  // [n_phases][gridDim.x][PK_TRACE_FIELDS] or null
 };
 
+// ---- per-CTA state (shared memory) -------------------------------------------------
+// dynamic: [ring ring_bytes][fragments xf_bytes][xs xs_floats][norm weights nw_floats]
+extern __shared__ __align__(128) uint8_t pk_dyn[];
+__shared__ __align__(8) uint64_t pk_full[PK_NDESC];
+__shared__ __align__(8) uint64_t pk_empty[PK_NDESC];
+__shared__ __align__(16) PPhase pk_F[2];         // descriptors of the current and the next phase
+__shared__ __align__(16) float pk_rpre[PK_RPRE * TC_M];   // residual rows of this CTA's first tiles
+__shared__ __align__(16) float pk_nwpre[PK_RPRE * TC_M];  // next phase's norm weights for those rows
+__shared__ __align__(16) float pk_ssin[256];              // per-CTA sums of squares of the input
+__shared__ float pk_red[PK_WARPS * 2 * TC_M];
+__shared__ float2 pk_cand[PK_WARPS];
+__shared__ float pk_stat[2 * PK_WARPS];
+__shared__ unsigned int pk_ticket;
+__shared__ volatile int pk_abort;                // set by any thread that gives up (producer included)
+__shared__ int pk_stop;                          // consumers' uniform copy, written by thread 0 before a barrier
+__shared__ int pk_tile_off[PK_NDESC];            // ring offset of each tile in flight (producer -> consumers)
+
+FDEV uint8_t *pk_ring() { return pk_dyn; }
+FDEV uint2 *pk_xf(const PParams &P) { return reinterpret_cast<uint2 *>(pk_dyn + P.ring_bytes); }
+FDEV float *pk_xs(const PParams &P) { return reinterpret_cast<float *>(pk_dyn + P.ring_bytes + P.xf_bytes); }
+FDEV float *pk_nws(const PParams &P) { return pk_xs(P) + P.xs_floats; }
+
+FDEV unsigned long long gtimer() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+
 FDEV void cbar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
-struct ConsumerBar {
-    FDEV void operator()() const { cbar(); }
-};
 FDEV void mbar_arrive(uint64_t *bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
@@ -103,18 +162,97 @@ FDEV uint32_t ld_acquire_u32(const unsigned int *p) {
     return v;
 }
 
-// Staging for the persistent kernel (256 consumer threads, named barrier).
+FDEV void cp_async16(void *sdst, const void *gsrc) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(sdst)), "l"(gsrc) : "memory");
+}
+FDEV void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// Copy phase descriptor `src` into shared memory with 16-byte async copies
+// (lanes of one warp); complete after cp_async_wait_all + a barrier.
+FDEV void pk_fetch_phase(PPhase *dst, const PPhase *src, int lane) {
+    constexpr int CH = (int)(sizeof(PPhase) / 16);
+    if (lane < CH) cp_async16(reinterpret_cast<uint4 *>(dst) + lane, reinterpret_cast<const uint4 *>(src) + lane);
+}
+
+// mbarrier wait that suspends the thread (up to hint_ns) instead of spinning, so
+// a waiting thread takes no issue slots from the warps that share its scheduler.
+FDEV bool mbar_try_wait_hint(uint64_t *bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+
+constexpr unsigned long long PK_WAIT_NS = 2000000000ull;  // a ring wait gives up after 2 s
+
+// Bounded mbarrier wait (time-limited) that also gives up when another thread
+// has aborted.
+FDEV bool pk_mbar_wait(uint64_t *bar, uint32_t parity) {
+    const unsigned long long t0 = gtimer();
+    for (;;) {
+        if (mbar_try_wait_hint(bar, parity, 20000)) return true;
+        if (pk_abort || gtimer() - t0 > PK_WAIT_NS) return false;
+    }
+}
+
+// Per-thread trace marks (thread 0 of the consumers; tr is null otherwise).
+struct PkTrace {
+    unsigned long long *tr;
+    long long ck;
+    FDEV void mark(int field) {
+        if (tr) {
+            const long long n = clock64();
+            tr[field] = (unsigned long long)(n - ck);
+            ck = n;
+        }
+    }
+    FDEV void put(int field, unsigned long long v) {
+        if (tr) tr[field] = v;
+    }
+};
+
+// ---- consumer side of the ring -------------------------------------------------------
+// Every consumer thread calls acquire/release in the same order; thread 0 alone
+// waits on the mbarrier (bounded) and publishes the stop decision before the
+// barrier, so all threads agree. acquire returns null when the step stops.
+FDEV const uint8_t *ring_acquire(const PParams &P, int seq, long long &wfull) {
+    const int d = seq % PK_NDESC;
+    if (threadIdx.x == 0) {
+        const long long w0 = clock64();
+        if (!pk_mbar_wait(&pk_full[d], (uint32_t)((seq / PK_NDESC) & 1))) {
+            pk_abort = 1;
+            *P.io_err = 4;
+        }
+        wfull += clock64() - w0;
+        pk_stop = pk_abort;
+    }
+    cbar();
+    return pk_stop ? nullptr : pk_ring() + pk_tile_off[d];
+}
+FDEV void ring_release(int seq) {
+    cbar();
+    if (threadIdx.x == 0) mbar_arrive(&pk_empty[seq % PK_NDESC]);
+}
+
+// ---- GEMV pieces ---------------------------------------------------------------------
+
+// Fragments of the staged input for weight type T: fp16 hi/lo pairs of
+// scale * x[k] (times rrms * norm[k] where the phase has an RMSNorm), in the
+// k-slot order TcDot<T> consumes (TcType<T>::elem). Reads x and the norm
+// weights from shared memory.
 template <int T>
-FDEV float pk_stage(const PPhase &F, const float *xsrc, bool xsrc_smem, float rrms, float scale, uint2 *xf) {
-    const int nb = F.cols >> 8;
+FDEV void pk_stage(int nb, const float *xs, const float *nws, float rrms, float scale, uint2 *xf) {
     for (int f = threadIdx.x; f < nb * 64; f += PK_CONSUMERS) {
         const int b = f >> 6, s = (f >> 2) & 15, t = f & 3;
         __half hi[4], lo[4];
 #pragma unroll
         for (int i = 0; i < 4; i++) {
             const int k = b * 256 + TcType<T>::elem(t, s, i);
-            float v = xsrc_smem ? xsrc[k] : __ldcg(xsrc + k);
-            if (F.norm_w) v = __fmul_rn(__fmul_rn(v, rrms), __ldg(F.norm_w + k));
+            float v = xs[k];
+            if (nws) v = __fmul_rn(__fmul_rn(v, rrms), nws[k]);
             v *= scale;
             hi[i] = __float2half_rn(v);
             lo[i] = __float2half_rn(v - __half2float(hi[i]));
@@ -124,83 +262,597 @@ FDEV float pk_stage(const PPhase &F, const float *xsrc, bool xsrc_smem, float rr
         xf[2 * f + 1] = make_uint2((uint32_t)__half_as_ushort(lo[0]) | ((uint32_t)__half_as_ushort(lo[1]) << 16),
                                    (uint32_t)__half_as_ushort(lo[2]) | ((uint32_t)__half_as_ushort(lo[3]) << 16));
     }
-    return 0.f;
 }
 
-// Bounded mbarrier wait that also gives up when another thread has aborted.
-FDEV bool pk_mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag) {
-    for (long long i = 0; i < TC_WAIT_LIMIT; i++) {
-        if (mbar_try_wait(bar, parity)) return true;
-        if ((i & 255) == 255 && *abort_flag) return false;
-    }
-    return false;
+// Input element k (of a phase whose weights are of type T) as fp16 hi/lo pair
+// into fragment layout gf: group f = (k/256)*64 + s*4 + t holds 8 halves, the
+// four hi slots then the four lo slots (the order pk_stage writes and TcDot reads).
+template <int T>
+FDEV void pk_frag_put(uint16_t *gf, int k, float v) {
+    int t = 0, s = 0, i = 0;
+    TcType<T>::pos(k & 255, t, s, i);
+    const int f = (k >> 8) * 64 + s * 4 + t;
+    const __half hi = __float2half_rn(v);
+    const __half lo = __float2half_rn(v - __half2float(hi));
+    gf[8 * f + i] = __half_as_ushort(hi);
+    gf[8 * f + 4 + i] = __half_as_ushort(lo);
 }
 
-template <int HD, int G>
-__global__ void __launch_bounds__(PK_THREADS, 1) decode_persistent_kernel(const PParams P) {
-    extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ __align__(8) uint64_t full[PK_NDESC], empty[PK_NDESC];
-    __shared__ float red[PK_WARPS * 2 * TC_M];
-    __shared__ float2 cand[PK_WARPS];
-    __shared__ float stat[2 * PK_WARPS];
-    __shared__ unsigned int ticket;
-    __shared__ volatile int abort_flag;  // set by any thread that gives up (producer included)
-    __shared__ int stop;                 // consumers' uniform copy: written by thread 0 before a barrier
-    __shared__ int tile_off[PK_NDESC];  // ring offset of each tile in flight (producer -> consumers)
-
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    uint8_t *ring = smem;
-    uint2 *xf0 = reinterpret_cast<uint2 *>(smem + P.ring_bytes);
-    float *xs = reinterpret_cast<float *>(smem + P.ring_bytes + P.xf_bytes);
-
-    if (tid == 0) {
-        for (int d = 0; d < PK_NDESC; d++) {
-            mbar_init(&full[d], 1);
-            mbar_init(&empty[d], 1);
+// Write v as element k of the next phase's input, in each of its layouts.
+// Returns false (nothing written) when v is outside the fragment range.
+FDEV bool pk_frag_out(const PPhase &F, int k, float v) {
+    if (!(fabsf(v) < PK_FRAG_MAX)) return false;
+#pragma unroll
+    for (int j = 0; j < 2; j++) {
+        const int ty = F.out_types[j];
+        if (ty < 0) break;
+        uint16_t *gf = F.gf_out + (size_t)j * 2 * F.n_out;
+        switch (ty) {
+        case T_Q4_K: pk_frag_put<T_Q4_K>(gf, k, v); break;
+        case T_Q6_K: pk_frag_put<T_Q6_K>(gf, k, v); break;
+        default: pk_frag_put<T_F16>(gf, k, v); break;
         }
-        mbar_fence_init();
-        abort_flag = 0;
-        stop = 0;
     }
-    __syncthreads();  // the only full-CTA barrier
+    return true;
+}
 
-    // ------------------------------------------------------------------ producer
-    if (warp == PK_WARPS) {
-        if (lane != 0) return;
-        int head = 0, used = 0, need[PK_NDESC];
-        long long seq = 0, oldest = 0;
-        for (int ph = 0; ph < P.n_phases && !abort_flag; ph++) {
-            const PPhase &F = P.phases[ph];
-            if (F.kind == PH_ATTN) continue;
-            for (int tile = blockIdx.x; tile < F.n_tiles && !abort_flag; tile += gridDim.x) {
+// One tile (16 rows of each of NMAT matrices) against the staged fragments:
+// warp w takes super-blocks w, w + 8, ...; its per-row partial sums go to pk_red.
+template <int T, int NMAT>
+FDEV void pk_dot(const uint8_t *buf, int stride, const uint2 *xf, int nb) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    float acc[NMAT][4];
+#pragma unroll
+    for (int m = 0; m < NMAT; m++)
+#pragma unroll
+        for (int i = 0; i < 4; i++) acc[m][i] = 0.f;
+    for (int b = warp; b < nb; b += PK_WARPS) {
+        const uint2 *xfb = xf + (size_t)b * 128;
+#pragma unroll
+        for (int m = 0; m < NMAT; m++) {
+            const uint8_t *mb = buf + (size_t)m * TC_M * stride + (size_t)b * TcType<T>::BB;
+            TcDot<T>::run(mb + (size_t)g * stride, mb + (size_t)(g + 8) * stride, xfb, g, t, acc[m]);
+        }
+    }
+    if (t == 0) {
+#pragma unroll
+        for (int m = 0; m < NMAT; m++) {
+            pk_red[(warp * 2 + m) * TC_M + g] = acc[m][0] + acc[m][1];
+            pk_red[(warp * 2 + m) * TC_M + g + 8] = acc[m][2] + acc[m][3];
+        }
+    }
+}
+
+// ---- attention -----------------------------------------------------------------------
+
+// Partial record of one (unit, query head): max, sum, 2 pad, o[hd] (16-byte aligned o).
+#define PK_REC(hd) ((hd) + 4)
+
+// Attention work split of one layer: nch pages of ATTN_P positions; U units per
+// KV head (at most one per CTA and KV head), unit u covering pages
+// [u*nch/U, (u+1)*nch/U). Producer and consumers derive it from the same pos.
+FDEV void pk_attn_geom(int pos, int n_kv, int grid, int &nch, int &U) {
+    nch = pos / ATTN_P + 1;
+    U = min(nch, max(1, grid / n_kv));
+}
+
+// One attention unit of the persistent step (KV head g, unit u, pages [p0, p1)):
+// RoPE of q, the new position's K/V (rotated, fp16) appended to the cache by the
+// unit that holds the last page, the unit's pages taken from the ring (the
+// producer prefetched them), then per page the same score / softmax / P.V
+// arithmetic as attn_unit, pages combined online, and one (max, sum, o[hd])
+// partial per query head written for the merge in the next phase.
+// Returns false when the step was stopped.
+template <int HD, int G>
+FDEV bool pk_attn_unit(const PParams &P, const PPhase &F, int g, int u, int U, int p0, int p1, int pos, int &seq,
+                       long long &wfull) {
+    const int layer = F.layer;
+    constexpr int PG = ATTN_P;
+    constexpr int KST = HD + 2;
+    constexpr int DPL = HD / 32;
+    const AttnParams &a = P.attn;
+    uint8_t *sm = reinterpret_cast<uint8_t *>(pk_xf(P));
+    float(*qs)[HD] = reinterpret_cast<float(*)[HD]>(sm);
+    uint16_t(*ks)[KST] = reinterpret_cast<uint16_t(*)[KST]>(sm + G * HD * 4);
+    uint16_t *nk = reinterpret_cast<uint16_t *>(sm + G * HD * 4 + PG * KST * 2);  // new K row (16-byte aligned)
+    uint16_t *nv = nk + HD;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int seqlen = pos + 1, nch = pos / PG + 1, tn = pos - (nch - 1) * PG;
+    const int kvd = a.n_kv * HD;
+    const float2 *rp = a.rope + (size_t)pos * (HD / 2);
+
+    for (int i = tid; i < G * (HD / 2); i += PK_CONSUMERS) {
+        const int h = i / (HD / 2), j = i % (HD / 2);
+        const float *qh = a.qkv + (size_t)(g * G + h) * HD;
+        const float x1 = __ldcg(qh + j), x2 = __ldcg(qh + j + HD / 2);
+        const float2 cs = __ldg(rp + j);
+        qs[h][j] = __fsub_rn(__fmul_rn(x1, cs.x), __fmul_rn(x2, cs.y));
+        qs[h][j + HD / 2] = __fadd_rn(__fmul_rn(x1, cs.y), __fmul_rn(x2, cs.x));
+    }
+    if (p1 == nch) {
+        const int page = a.page_table[nch - 1];
+        const size_t base = (((size_t)page * a.n_layers + layer) * a.n_kv + g) * (size_t)PG * HD;
+        uint16_t *kp = a.k_pool + base, *vp = a.v_pool + base;
+        const float *kr = a.qkv + (size_t)a.n_heads * HD + (size_t)g * HD;
+        const float *vr = kr + kvd;
+        for (int j = tid; j < HD / 2; j += PK_CONSUMERS) {
+            const float x1 = __ldcg(kr + j), x2 = __ldcg(kr + j + HD / 2);
+            const float2 cs = __ldg(rp + j);
+            const uint16_t y1 = __half_as_ushort(__float2half_rn(__fsub_rn(__fmul_rn(x1, cs.x), __fmul_rn(x2, cs.y))));
+            const uint16_t y2 = __half_as_ushort(__float2half_rn(__fadd_rn(__fmul_rn(x1, cs.y), __fmul_rn(x2, cs.x))));
+            nk[j] = y1;
+            nk[j + HD / 2] = y2;
+            kp[(size_t)tn * HD + j] = y1;
+            kp[(size_t)tn * HD + j + HD / 2] = y2;
+        }
+        for (int j = tid; j < HD; j += PK_CONSUMERS) {
+            const uint16_t h16 = __half_as_ushort(__float2half_rn(__ldcg(vr + j)));
+            nv[j] = h16;
+            vp[(size_t)tn * HD + j] = h16;
+        }
+    }
+
+    float m_run = -INFINITY, l_run = 0.f, o_run[DPL];
+#pragma unroll
+    for (int j = 0; j < DPL; j++) o_run[j] = 0.f;
+    for (int pg = p0; pg < p1; pg++) {
+        const uint8_t *tile = ring_acquire(P, seq, wfull);  // also publishes qs / nk / nv
+        if (!tile) return false;
+        const uint16_t *kpg = reinterpret_cast<const uint16_t *>(tile);
+        uint16_t *vpg = const_cast<uint16_t *>(kpg + PG * HD);
+        const int t0 = pg * PG, nt = min(PG, seqlen - t0);
+        const bool last = pg == nch - 1;
+        constexpr int V8 = HD / 8;
+        for (int i = tid; i < nt * V8; i += PK_CONSUMERS) {
+            const int t = i / V8, k8 = i % V8;
+            const uint4 kv4 = (last && t == tn) ? reinterpret_cast<const uint4 *>(nk)[k8]
+                                                : reinterpret_cast<const uint4 *>(kpg + (size_t)t * HD)[k8];
+            uint32_t *kd = reinterpret_cast<uint32_t *>(&ks[t][8 * k8]);
+            kd[0] = kv4.x; kd[1] = kv4.y; kd[2] = kv4.z; kd[3] = kv4.w;
+        }
+        if (last)
+            for (int j = tid; j < HD / 2; j += PK_CONSUMERS)
+                reinterpret_cast<uint32_t *>(vpg + (size_t)tn * HD)[j] = reinterpret_cast<const uint32_t *>(nv)[j];
+        cbar();
+        if (warp < G) {
+            const int h = warp;
+            float sc2[2];
+#pragma unroll
+            for (int k = 0; k < 2; k++) {
+                const int t = lane + 32 * k;
+                float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;
+                if (t < nt) {
+#pragma unroll
+                    for (int d = 0; d < HD; d += 4) {
+                        d0 = fmaf(qs[h][d + 0], __half2float(__ushort_as_half(ks[t][d + 0])), d0);
+                        d1 = fmaf(qs[h][d + 1], __half2float(__ushort_as_half(ks[t][d + 1])), d1);
+                        d2 = fmaf(qs[h][d + 2], __half2float(__ushort_as_half(ks[t][d + 2])), d2);
+                        d3 = fmaf(qs[h][d + 3], __half2float(__ushort_as_half(ks[t][d + 3])), d3);
+                    }
+                }
+                sc2[k] = t < nt ? __fmul_rn((d0 + d1) + (d2 + d3), a.scale) : -INFINITY;
+            }
+            float m = fmaxf(sc2[0], sc2[1]);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+            const float e0 = lane < nt ? expf(sc2[0] - m) : 0.f;
+            const float e1 = lane + 32 < nt ? expf(sc2[1] - m) : 0.f;
+            float l = e0 + e1;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+            float o1[DPL], o2[DPL];
+#pragma unroll
+            for (int j = 0; j < DPL; j++) o1[j] = o2[j] = 0.f;
+            const int n0 = min(nt, 32);
+            for (int t = 0; t < n0; t++) {
+                const float w = __shfl_sync(0xffffffffu, e0, t);
+#pragma unroll
+                for (int j = 0; j < DPL; j++)
+                    o1[j] = fmaf(w, __half2float(__ushort_as_half(vpg[(size_t)t * HD + lane + 32 * j])), o1[j]);
+            }
+            for (int t = 32; t < nt; t++) {
+                const float w = __shfl_sync(0xffffffffu, e1, t - 32);
+#pragma unroll
+                for (int j = 0; j < DPL; j++)
+                    o2[j] = fmaf(w, __half2float(__ushort_as_half(vpg[(size_t)t * HD + lane + 32 * j])), o2[j]);
+            }
+            if (pg == p0) {
+                m_run = m;
+                l_run = l;
+#pragma unroll
+                for (int j = 0; j < DPL; j++) o_run[j] = o1[j] + o2[j];
+            } else {
+                const float M = fmaxf(m_run, m);
+                const float al = expf(m_run - M), be = expf(m - M);
+                l_run = fmaf(al, l_run, be * l);
+#pragma unroll
+                for (int j = 0; j < DPL; j++) o_run[j] = fmaf(al, o_run[j], be * (o1[j] + o2[j]));
+                m_run = M;
+            }
+        }
+        ring_release(seq);
+        seq++;
+    }
+    if (warp < G) {
+        float *pc = a.part + ((size_t)(g * a.max_chunks + u) * G + warp) * PK_REC(HD);
+#pragma unroll
+        for (int j = 0; j < DPL; j++) pc[4 + lane + 32 * j] = o_run[j];
+        if (lane == 0) {
+            pc[0] = m_run;
+            pc[1] = l_run;
+        }
+    }
+
+    // the last unit of this KV head merges the U partials (max, exp weights,
+    // weighted sums) and writes the heads' outputs as Wo's input fragments
+    __threadfence();
+    cbar();
+    if (tid == 0) pk_ticket = atomicAdd(a.count + g, 1u);
+    cbar();
+    if (pk_ticket != (unsigned)(U - 1)) return true;
+    __threadfence();
+    float2 *ml = reinterpret_cast<float2 *>(sm);          // [G][U] (max, sum)
+    float *wts = reinterpret_cast<float *>(ml + G * U);   // [G][U] exp weights
+    float *lsum = wts + G * U;                            // [G]
+    const size_t ustride = (size_t)G * PK_REC(HD);
+    const float *pg0 = a.part + (size_t)g * a.max_chunks * G * PK_REC(HD);
+    for (int i = tid; i < G * U; i += PK_CONSUMERS) {
+        const int h = i / U, uu = i % U;
+        ml[i] = __ldcg(reinterpret_cast<const float2 *>(pg0 + uu * ustride + (size_t)h * PK_REC(HD)));
+    }
+    cbar();
+    if (warp < (8 * G + 31) / 32) {  // 8 lanes per head, whole warps (full-mask shuffles)
+        const int h = tid >> 3, j = tid & 7;
+        const bool valid = h < G;
+        float M = -INFINITY;
+        if (valid)
+            for (int uu = j; uu < U; uu += 8) M = fmaxf(M, ml[h * U + uu].x);
+        M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, 1, 8));
+        M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, 2, 8));
+        M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, 4, 8));
+        float L = 0.f;
+        if (valid)
+            for (int uu = j; uu < U; uu += 8) {
+                const float w = expf(ml[h * U + uu].x - M);
+                wts[h * U + uu] = w;
+                L = fmaf(w, ml[h * U + uu].y, L);
+            }
+        L += __shfl_xor_sync(0xffffffffu, L, 1, 8);
+        L += __shfl_xor_sync(0xffffffffu, L, 2, 8);
+        L += __shfl_xor_sync(0xffffffffu, L, 4, 8);
+        if (valid && j == 0) lsum[h] = L;
+    }
+    cbar();
+    bool ok = true;
+    for (int q = tid; q < G * HD / 4; q += PK_CONSUMERS) {
+        const int h = (4 * q) / HD, dd = (4 * q) % HD;
+        const float4 *pb = reinterpret_cast<const float4 *>(pg0 + (size_t)h * PK_REC(HD) + 4 + dd);
+        float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int u0 = 0; u0 < U; u0 += 4) {
+            float4 o[4];
+#pragma unroll
+            for (int j = 0; j < 4; j++)
+                if (u0 + j < U) o[j] = __ldcg(pb + (u0 + j) * (ustride >> 2));
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                if (u0 + j < U) {
+                    const float w = wts[h * U + u0 + j];
+                    O.x = fmaf(w, o[j].x, O.x);
+                    O.y = fmaf(w, o[j].y, O.y);
+                    O.z = fmaf(w, o[j].z, O.z);
+                    O.w = fmaf(w, o[j].w, O.w);
+                }
+            }
+        }
+        const float L = lsum[h];
+        const int k0 = (g * G + h) * HD + dd;
+        ok &= pk_frag_out(F, k0 + 0, O.x / L);
+        ok &= pk_frag_out(F, k0 + 1, O.y / L);
+        ok &= pk_frag_out(F, k0 + 2, O.z / L);
+        ok &= pk_frag_out(F, k0 + 3, O.w / L);
+    }
+    if (!ok) *P.io_err = 5;
+    if (tid == 0) a.count[g] = 0u;
+    cbar();  // shared memory reused by the next unit
+    return true;
+}
+
+// Attention phase of layer `layer`: this CTA's units. Returns false when stopped.
+template <int HD, int G>
+__device__ __noinline__ bool pk_attn_phase(const PParams &P, const PPhase &F, int pos, int nch, int U, int &seq,
+                                           long long &wfull) {
+    if (pos < 0 || pos >= P.attn.max_seq) {
+        if (threadIdx.x == 0 && blockIdx.x == 0) *P.io_err = 1;
+        return true;
+    }
+    for (int ui = blockIdx.x; ui < P.attn.n_kv * U; ui += gridDim.x) {
+        const int g = ui / U, u = ui % U;
+        if (!pk_attn_unit<HD, G>(P, F, g, u, U, u * nch / U, (u + 1) * nch / U, pos, seq, wfull)) return false;
+    }
+    return true;
+}
+
+// ---- GEMV phase ----------------------------------------------------------------------
+
+// One GEMV phase of this CTA: stage the input fragments (written by the previous
+// phase, or the embedding row staged here), then decode + multiply its tiles
+// from the ring and apply the epilogue, which also writes the next phase's
+// input fragments. Returns false when the step stopped.
+template <int HD, int G>
+__device__ __noinline__ bool pk_gemv_phase(const PParams &P, const PPhase &F, int token0, int &seq, long long &wfull,
+                                           float &best_v, int &best_i, PkTrace &T) {
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int n = F.cols, nb = n >> 8;
+    // layouts: one per weight type of the phase (at most two: QKV may mix Q4_K and Q6_K)
+    const int type_a = F.seg[0].type;
+    int type_b = -1;
+    for (int k = 1; k < F.nseg; k++)
+        if (F.seg[k].type != type_a && type_b < 0) type_b = F.seg[k].type;
+    uint2 *xf0 = pk_xf(P), *xf1 = xf0 + (size_t)nb * 128;  // second layout follows the first
+    float rrms = 1.0f;
+    if (F.embed_in) {
+        // embedding row of the current token: every CTA decodes it, sums its
+        // squares and stages x * norm itself
+        const float *nw = F.norm_w ? pk_nws(P) : nullptr;
+        float *xs = pk_xs(P);
+        int tok = token0;
+        if (tok < 0 || tok >= P.vocab) {
+            if (tid == 0 && blockIdx.x == 0) *P.io_err = 2;
+            tok = 0;
+        }
+        float ss = 0.f;
+        for (int i = tid; i < n; i += PK_CONSUMERS) {
+            float v;
+            switch (P.embd_type) {
+            case T_F16: v = h2f(reinterpret_cast<const uint16_t *>(P.embd)[(size_t)tok * n + i]); break;
+            case T_F32: v = round_f16(reinterpret_cast<const float *>(P.embd)[(size_t)tok * n + i]); break;
+            case T_Q4_K: v = round_f16(decode_elem<T_Q4_K>(P.embd + ((size_t)tok * (n >> 8) + (i >> 8)) * 144, i & 255)); break;
+            case T_Q5_K: v = round_f16(decode_elem<T_Q5_K>(P.embd + ((size_t)tok * (n >> 8) + (i >> 8)) * 176, i & 255)); break;
+            default: v = round_f16(decode_elem<T_Q6_K>(P.embd + ((size_t)tok * (n >> 8) + (i >> 8)) * 210, i & 255)); break;
+            }
+            xs[i] = v;
+            if (blockIdx.x == 0) P.x[i] = v;  // the residual stream starts as the embedding
+            ss = fmaf(v, v, ss);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        if (lane == 0) pk_stat[warp] = ss;
+        cbar();
+        ss = 0.f;
+#pragma unroll
+        for (int w = 0; w < PK_WARPS; w++) ss += pk_stat[w];
+        if (nw) rrms = 1.0f / sqrtf(ss / (float)n + F.eps);
+        for (int pass = 0; pass < (type_b >= 0 ? 2 : 1); pass++) {
+            uint2 *dst = pass ? xf1 : xf0;
+            switch (pass ? type_b : type_a) {
+            case T_Q4_K: pk_stage<T_Q4_K>(nb, xs, nw, 1.0f, 1.0f, dst); break;
+            case T_Q6_K: pk_stage<T_Q6_K>(nb, xs, nw, 1.0f, 1.0f, dst); break;
+            default: pk_stage<T_F16>(nb, xs, nw, 1.0f, 1.0f, dst); break;
+            }
+        }
+        cbar();
+    } else {
+        // fragments and per-CTA sums of squares written by the previous phase
+        const int chunks = (type_b >= 0 ? 2 : 1) * (n >> 2);  // 16-byte chunks, 4n bytes per layout
+        for (int c = tid; c < chunks; c += PK_CONSUMERS) cp_async16(xf0 + 2 * c, F.gf_in + 2 * c);
+        if (F.ss_in)
+            for (int c = tid; c < ((int)gridDim.x + 3) / 4; c += PK_CONSUMERS) cp_async16(pk_ssin + 4 * c, F.ss_in + 4 * c);
+        cp_async_wait_all();
+        cbar();
+        if (F.ss_in && tid < TC_M) {
+            float ss = 0.f;
+            for (int i = 0; i < (int)gridDim.x; i++) ss += pk_ssin[i];
+            rrms = 1.0f / sqrtf(ss / (float)n + F.eps);
+        }
+    }
+    T.mark(2);
+
+    // ---- tiles of this CTA
+    const int my_tiles = (F.n_tiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
+    float ssacc = 0.f;
+    bool ok = true;
+    for (int k = 0; k < my_tiles; k++) {
+        const int tile = (int)blockIdx.x + k * (int)gridDim.x;
+        int sidx, lt;
+        locate_p(F, tile, sidx, lt);
+        const PSeg &S = F.seg[sidx];
+        const uint8_t *buf = ring_acquire(P, seq, wfull);
+        if (!buf) return false;
+        const uint2 *xf = (S.type == type_a) ? xf0 : xf1;
+        if (F.nmat == 2) {
+            switch (S.type) {
+            case T_Q4_K: pk_dot<T_Q4_K, 2>(buf, S.stride, xf, nb); break;
+            case T_Q6_K: pk_dot<T_Q6_K, 2>(buf, S.stride, xf, nb); break;
+            default: pk_dot<T_F16, 2>(buf, S.stride, xf, nb); break;
+            }
+        } else {
+            switch (S.type) {
+            case T_Q4_K: pk_dot<T_Q4_K, 1>(buf, S.stride, xf, nb); break;
+            case T_Q6_K: pk_dot<T_Q6_K, 1>(buf, S.stride, xf, nb); break;
+            default: pk_dot<T_F16, 1>(buf, S.stride, xf, nb); break;
+            }
+        }
+        ring_release(seq);  // tile consumed, partials visible
+        if (tid < TC_M) {
+            const int r = lt * TC_M + tid;
+            float v0 = 0.f, v1 = 0.f;
+#pragma unroll
+            for (int w = 0; w < PK_WARPS; w++) v0 += pk_red[(w * 2) * TC_M + tid];
+            v0 *= rrms;
+            if (F.nmat == 2) {
+#pragma unroll
+                for (int w = 0; w < PK_WARPS; w++) v1 += pk_red[(w * 2 + 1) * TC_M + tid];
+                v1 *= rrms;
+            }
+            if (r < S.rows) {
+                if (F.kind == PH_QKV) {
+                    F.y[S.out_off + r] = v0;
+                } else if (F.kind == PH_RESID) {
+                    const bool pre = k < PK_RPRE && (r & ~3) + 4 <= S.rows;  // fetched before the barrier
+                    const float xv = __fadd_rn(pre ? pk_rpre[k * TC_M + tid] : __ldcg(F.resid + r), v0);
+                    F.resid[r] = xv;
+                    if (F.ss_out) ssacc = fmaf(xv, xv, ssacc);
+                    if (F.gf_out) {
+                        const float nwv = F.nw_out ? (pre ? pk_nwpre[k * TC_M + tid] : __ldg(F.nw_out + r)) : 1.0f;
+                        ok &= pk_frag_out(F, r, F.nw_out ? __fmul_rn(xv, nwv) : xv);
+                    }
+                } else if (F.kind == PH_SWIGLU) {
+                    const float h = __fmul_rn(__fdiv_rn(v0, __fadd_rn(1.0f, expf(-v0))), v1);
+                    F.y[r] = h;
+                    if (F.gf_out) ok &= pk_frag_out(F, r, h);
+                } else {  // PH_LM
+                    F.y[r] = v0;
+                    if (better(v0, r, best_v, best_i)) {
+                        best_v = v0;
+                        best_i = r;
+                    }
+                }
+            }
+        }
+        cbar();  // pk_red reused by the next tile
+        seq++;
+    }
+    if (F.ss_out && warp == 0) {
+        // this CTA's sum of squares of its output rows (threads 0..15 hold them)
+        float v = tid < TC_M ? ssacc : 0.f;
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if (lane == 0) F.ss_out[blockIdx.x] = v;
+    }
+    if (!ok) *P.io_err = 5;
+    return true;
+}
+
+// Greedy argmax after the lm_head phase: CTA candidate, then the last CTA reduces
+// all candidates, publishes the token and (loop mode) advances the step state.
+FDEV void pk_argmax_finish(const PParams &P, float best_v, int best_i) {
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (warp == 0) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, best_v, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, best_i, o);
+            if (better(ov, oi, best_v, best_i)) {
+                best_v = ov;
+                best_i = oi;
+            }
+        }
+        if (lane == 0) {
+            P.am_part[blockIdx.x] = make_float2(best_v, __int_as_float(best_i));
+            __threadfence();
+            pk_ticket = atomicAdd(P.am_count, 1u);
+        }
+    }
+    cbar();
+    if (pk_ticket != gridDim.x - 1) return;
+    __threadfence();
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int i = tid; i < (int)gridDim.x; i += PK_CONSUMERS) {
+        const float2 e2 = __ldcg(P.am_part + i);
+        const int ei = __float_as_int(e2.y);
+        if (better(e2.x, ei, bv, bi)) {
+            bv = e2.x;
+            bi = ei;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (better(ov, oi, bv, bi)) {
+            bv = ov;
+            bi = oi;
+        }
+    }
+    if (lane == 0) pk_cand[warp] = make_float2(bv, __int_as_float(bi));
+    cbar();
+    if (tid == 0) {
+        for (int w = 1; w < PK_WARPS; w++) {
+            const int wi = __float_as_int(pk_cand[w].y);
+            if (better(pk_cand[w].x, wi, bv, bi)) {
+                bv = pk_cand[w].x;
+                bi = wi;
+            }
+        }
+        if (bi == 0x7fffffff) bi = 0;
+        *P.io_argmax = bi;
+        if (P.loop) {
+            *P.io_token = bi;
+            *P.io_pos = *P.io_pos + 1;
+            const int st = *P.io_step;
+            P.rec_tokens[st] = bi;
+            *P.io_step = st + 1;
+        }
+        *P.am_count = 0u;
+    }
+}
+
+// ---- producer ------------------------------------------------------------------------
+
+// Single-thread producer: ring space for the next tile is a slot and `size`
+// contiguous bytes (the ring's end is skipped when the tile would straddle it).
+template <int HD>
+__device__ __noinline__ void pk_producer(const PParams &P, int pos, int nch, int U) {
+    uint8_t *ring = pk_ring();
+    int head = 0, used = 0, need[PK_NDESC];
+    long long seq = 0, oldest = 0, pwait = 0;
+    auto reserve = [&](int size, int &d) -> uint8_t * {
+        int skip;
+        for (;;) {
+            if (seq == oldest) head = 0;  // ring empty: restart at the front
+            skip = head + size > P.ring_bytes ? P.ring_bytes - head : 0;
+            if (seq - oldest < PK_NDESC && used + skip + size <= P.ring_bytes) break;
+            const int od = (int)(oldest % PK_NDESC);
+            const long long w0 = clock64();
+            const bool got = pk_mbar_wait(&pk_empty[od], (uint32_t)((oldest / PK_NDESC) & 1));
+            pwait += clock64() - w0;
+            if (!got) {
+                pk_abort = 1;
+                *P.io_err = 4;
+                return nullptr;
+            }
+            used -= need[od];
+            oldest++;
+        }
+        if (skip) head = 0;
+        uint8_t *dst = ring + head;
+        head += size;
+        d = (int)(seq % PK_NDESC);
+        need[d] = skip + size;
+        used += skip + size;
+        pk_tile_off[d] = (int)(dst - ring);
+        return dst;
+    };
+    const bool pos_ok = pos >= 0 && pos < P.attn.max_seq;
+    for (int ph = 0; ph < P.n_phases && !pk_abort; ph++) {
+        const PPhase &F = P.phases[ph];
+        pwait = 0;
+        if (F.kind == PH_ATTN) {
+            // the K and V pages of this CTA's units (same order the consumers take them)
+            constexpr uint32_t PAGE = ATTN_P * HD * 2;
+            for (int ui = blockIdx.x; pos_ok && ui < P.attn.n_kv * U && !pk_abort; ui += gridDim.x) {
+                const int g = ui / U, u = ui % U;
+                for (int pg = u * nch / U; pg < (u + 1) * nch / U; pg++) {
+                    int d;
+                    uint8_t *dst = reserve(2 * PAGE, d);
+                    if (!dst) break;
+                    const size_t base =
+                        (((size_t)P.attn.page_table[pg] * P.attn.n_layers + F.layer) * P.attn.n_kv + g) * (size_t)ATTN_P * HD;
+                    mbar_expect_tx(&pk_full[d], 2 * PAGE);
+                    bulk_g2s(dst, P.attn.k_pool + base, PAGE, &pk_full[d]);
+                    bulk_g2s(dst + PAGE, P.attn.v_pool + base, PAGE, &pk_full[d]);
+                    seq++;
+                }
+            }
+        } else {
+            for (int tile = blockIdx.x; tile < F.n_tiles && !pk_abort; tile += gridDim.x) {
                 int s, lt;
                 locate_p(F, tile, s, lt);
                 const PSeg &S = F.seg[s];
-                const int size = tile_bytes_of(S, F.nmat);
-                // wait for ring space: a slot, and `size` contiguous bytes (skipping
-                // the ring's end when the tile would straddle it)
-                int skip;
-                for (;;) {
-                    if (seq == oldest) head = 0;  // ring empty: restart at the front
-                    skip = head + size > P.ring_bytes ? P.ring_bytes - head : 0;
-                    if (seq - oldest < PK_NDESC && used + skip + size <= P.ring_bytes) break;
-                    const int od = (int)(oldest % PK_NDESC);
-                    if (!pk_mbar_wait(&empty[od], (uint32_t)((oldest / PK_NDESC) & 1), &abort_flag)) {
-                        abort_flag = 1;
-                        *P.io_err = 4;
-                        break;
-                    }
-                    used -= need[od];
-                    oldest++;
-                }
-                if (abort_flag) break;
-                if (skip) head = 0;
-                uint8_t *dst = ring + head;
-                head += size;
-                const int d = (int)(seq % PK_NDESC);
-                need[d] = skip + size;
-                used += skip + size;
-                tile_off[d] = (int)(dst - ring);
+                int d;
+                uint8_t *dst = reserve(tile_bytes_of(S, F.nmat), d);
+                if (!dst) break;
                 // issue: plain-copied tail first, then the arrive (release), then the bulk copies
                 const int r0 = lt * TC_M, nrows = min(TC_M, S.rows - r0);
                 const uint32_t mat_bytes = (uint32_t)nrows * S.row_bytes;
@@ -210,41 +862,94 @@ __global__ void __launch_bounds__(PK_THREADS, 1) decode_persistent_kernel(const 
                     uint8_t *mdst = dst + (size_t)m * TC_M * S.stride;
                     for (uint32_t k = main_bytes; k < mat_bytes; k++) mdst[k] = src[k];
                 }
-                mbar_expect_tx(&full[d], main_bytes * F.nmat);
+                mbar_expect_tx(&pk_full[d], main_bytes * F.nmat);
                 for (int m = 0; m < F.nmat; m++) {
                     const uint8_t *src = (m == 0 ? S.w : S.w2) + (size_t)r0 * S.row_bytes;
                     uint8_t *mdst = dst + (size_t)m * TC_M * S.stride;
                     if (S.per_row) {
                         for (int r = 0; r < nrows; r++)
-                            bulk_g2s(mdst + (size_t)r * S.stride, src + (size_t)r * S.row_bytes, S.row_bytes, &full[d]);
+                            bulk_g2s(mdst + (size_t)r * S.stride, src + (size_t)r * S.row_bytes, S.row_bytes, &pk_full[d]);
                     } else if (main_bytes) {
-                        bulk_g2s(mdst, src, main_bytes, &full[d]);
+                        bulk_g2s(mdst, src, main_bytes, &pk_full[d]);
                     }
                 }
                 seq++;
             }
         }
-        // copies still in flight land before the CTA can exit: the consumers wait
-        // on every tile; after an abort, wait (bounded) here for the issued ones.
-        if (abort_flag)
-            for (long long k = oldest; k < seq; k++)
-                mbar_wait(&full[k % PK_NDESC], (uint32_t)((k / PK_NDESC) & 1));
+        if (P.trace) {
+            unsigned long long *tr = P.trace + ((size_t)ph * gridDim.x + blockIdx.x) * PK_TRACE_FIELDS;
+            tr[6] = gtimer();
+            tr[7] = (unsigned long long)pwait;
+        }
+    }
+    // copies still in flight land before the CTA can exit: the consumers wait
+    // on every tile; after an abort, wait (bounded) here for the issued ones.
+    if (pk_abort)
+        for (long long k = oldest; k < seq; k++) mbar_wait(&pk_full[k % PK_NDESC], (uint32_t)((k / PK_NDESC) & 1));
+}
+
+// ---- the kernel ----------------------------------------------------------------------
+
+template <int HD, int G>
+__global__ void __launch_bounds__(PK_THREADS, 1) decode_persistent_kernel(const __grid_constant__ PParams P) {
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (tid == 0) {
+        for (int d = 0; d < PK_NDESC; d++) {
+            mbar_init(&pk_full[d], 1);
+            mbar_init(&pk_empty[d], 1);
+        }
+        mbar_fence_init();
+        pk_abort = 0;
+        pk_stop = 0;
+    }
+    if (warp == 0) pk_fetch_phase(&pk_F[0], P.phases, lane);
+    cp_async_wait_all();
+    __syncthreads();  // the only full-CTA barrier
+
+    // attention geometry of this step (pos is final for the whole launch)
+    const int pos = *P.attn.pos_ptr;
+    int nch = 0, U = 0;
+    if (pos >= 0 && pos < P.attn.max_seq) pk_attn_geom(pos, P.attn.n_kv, gridDim.x, nch, U);
+
+    if (warp == PK_WARPS) {
+        if (lane == 0) pk_producer<HD>(P, pos, nch, U);
         return;
     }
 
     // ------------------------------------------------------------------ consumers
-    const int g = lane >> 2, t = lane & 3;
-    long long seq = 0;
+    const int token0 = *P.io_token;
+    int seq = 0;
     float best_v = -INFINITY;
     int best_i = 0x7fffffff;
-    const int token0 = *P.io_token;
+    PkTrace T{nullptr, clock64()};
+    long long wfull = 0;
+    float *nws = pk_nws(P);
 
     for (int ph = 0; ph < P.n_phases; ph++) {
-        const PPhase &F = P.phases[ph];
+        const PPhase &F = pk_F[ph & 1];  // fetched during the previous phase
+        T.tr = (P.trace && tid == 0) ? P.trace + ((size_t)ph * gridDim.x + blockIdx.x) * PK_TRACE_FIELDS : nullptr;
+        const bool gemv = F.kind != PH_ATTN && (int)blockIdx.x < F.n_tiles;
+        // inputs that do not depend on the previous phase, fetched before its barrier:
+        // the embedding phase's RMSNorm weights; the residual rows (final since two
+        // barriers ago) and the next phase's norm weights for this CTA's first tiles
+        if (gemv && F.embed_in && F.norm_w)
+            for (int i = tid; i < (F.cols >> 2); i += PK_CONSUMERS) cp_async16(nws + 4 * i, F.norm_w + 4 * i);
+        if (gemv && F.kind == PH_RESID) {
+            const int my_tiles = (F.n_tiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
+            const int cnt = min(my_tiles, PK_RPRE);
+            for (int i = tid; i < cnt * 4; i += PK_CONSUMERS) {
+                const int r0 = ((int)blockIdx.x + (i >> 2) * (int)gridDim.x) * TC_M + 4 * (i & 3);
+                if (r0 + 4 <= F.seg[0].rows) {
+                    cp_async16(pk_rpre + 4 * i, F.resid + r0);
+                    if (F.nw_out) cp_async16(pk_nwpre + 4 * i, F.nw_out + r0);
+                }
+            }
+        }
+        if (!gemv && F.kind != PH_ATTN && F.ss_out && tid == 0) F.ss_out[blockIdx.x] = 0.f;  // no rows here
         // wait until every CTA finished the previous phase (thread 0 polls; the
         // stop decision is published before the barrier so all consumers agree)
-        if (ph > 0) {
-            if (tid == 0) {
+        if (tid == 0) {
+            if (ph > 0) {
                 bool ok = false;
                 const unsigned int *cnt = P.bar + (ph - 1);
                 for (long long i = 0; i < PK_SPIN_LIMIT; i++) {
@@ -252,254 +957,52 @@ __global__ void __launch_bounds__(PK_THREADS, 1) decode_persistent_kernel(const 
                         ok = true;
                         break;
                     }
-                    if ((i & 63) == 63 && abort_flag) break;
-                    __nanosleep(64);
+                    if ((i & 63) == 63 && pk_abort) break;
+                    __nanosleep(32);
                 }
                 if (ok) {
                     __threadfence();  // order this CTA's reads of the phase inputs after the barrier
                 } else {
-                    abort_flag = 1;
+                    pk_abort = 1;
                     *P.io_err = 4;
                 }
-                stop = abort_flag;
             }
-            cbar();
-            if (stop) break;
+            pk_stop = pk_abort;
         }
+        cp_async_wait_all();
+        cbar();
+        if (pk_stop) break;
+        // the next phase's descriptor, into the other buffer (read only after the
+        // arrive barrier below)
+        if (warp == 0 && ph + 1 < P.n_phases) pk_fetch_phase(&pk_F[(ph + 1) & 1], P.phases + ph + 1, lane);
+        T.put(0, gtimer());
+        T.mark(1);
+        wfull = 0;
 
-        if (F.kind == PH_ATTN) {
-            const int pos = *P.attn.pos_ptr;
-            if (pos < 0 || pos >= P.attn.max_seq) {
-                if (tid == 0 && blockIdx.x == 0) *P.io_err = 1;
-            } else {
-                AttnParams a = P.attn;
-                a.layer = F.layer;
-                const int nch = (pos + ATTN_P) / ATTN_P, units = nch * a.n_kv;
-                for (int u = blockIdx.x; u < units; u += gridDim.x)
-                    attn_unit<HD, G>(a, u / a.n_kv, u % a.n_kv, pos, reinterpret_cast<uint8_t *>(xf0), &ticket,
-                                     ConsumerBar());
-            }
-        } else if ((int)blockIdx.x < F.n_tiles) {
-            // ---- stage the input vector
-            const int n = F.cols, nb = n >> 8;
-            const float *xin = F.x;
-            bool in_smem = false;
-            if (F.embed_in) {
-                // embedding row of the current token, computed by every CTA into xs
-                int tok = token0;
-                if (tok < 0 || tok >= P.vocab) {
-                    if (tid == 0 && blockIdx.x == 0) *P.io_err = 2;
-                    tok = 0;
-                }
-                for (int i = tid; i < n; i += PK_CONSUMERS) {
-                    float v;
-                    switch (P.embd_type) {
-                    case T_F16: v = h2f(reinterpret_cast<const uint16_t *>(P.embd)[(size_t)tok * n + i]); break;
-                    case T_F32: v = round_f16(reinterpret_cast<const float *>(P.embd)[(size_t)tok * n + i]); break;
-                    case T_Q4_K: v = round_f16(decode_elem<T_Q4_K>(P.embd + ((size_t)tok * (n >> 8) + (i >> 8)) * 144, i & 255)); break;
-                    case T_Q5_K: v = round_f16(decode_elem<T_Q5_K>(P.embd + ((size_t)tok * (n >> 8) + (i >> 8)) * 176, i & 255)); break;
-                    default: v = round_f16(decode_elem<T_Q6_K>(P.embd + ((size_t)tok * (n >> 8) + (i >> 8)) * 210, i & 255)); break;
-                    }
-                    xs[i] = v;
-                    if (blockIdx.x == 0) P.x[i] = v;  // the residual stream starts as the embedding
-                }
-                cbar();
-                xin = xs;
-                in_smem = true;
-            } else if (P.xs_floats >= n) {
-                for (int i = tid * 4; i < n; i += PK_CONSUMERS * 4)
-                    *reinterpret_cast<float4 *>(xs + i) = __ldcg(reinterpret_cast<const float4 *>(F.x + i));
-                cbar();
-                xin = xs;
-                in_smem = true;
-            }
-            // sum of squares and max |x| (scale choice), one reduction
-            float ss = 0.f, mx = 0.f;
-            for (int i = tid; i < n; i += PK_CONSUMERS) {
-                const float v = in_smem ? xin[i] : __ldcg(xin + i);
-                ss = fmaf(v, v, ss);
-                mx = fmaxf(mx, fabsf(F.norm_w ? v * __ldg(F.norm_w + i) : v));
-            }
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-                ss += __shfl_xor_sync(0xffffffffu, ss, o);
-                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-            }
-            if (lane == 0) {
-                stat[2 * warp] = ss;
-                stat[2 * warp + 1] = mx;
-            }
-            cbar();
-            ss = 0.f;
-            mx = 0.f;
-            for (int w = 0; w < PK_WARPS; w++) {
-                ss += stat[2 * w];
-                mx = fmaxf(mx, stat[2 * w + 1]);
-            }
-            const float rrms = F.norm_w ? 1.0f / sqrtf(ss / (float)n + F.eps) : 1.0f;
-            mx *= rrms;
-            int e = 0;
-            if (mx > 0.f) frexpf(mx, &e);
-            const int sh = (mx > 0.f && isfinite(mx)) ? (14 - e) : 0;
-            const float scale = ldexpf(1.0f, sh), unscale = ldexpf(1.0f, -sh);
-            // fragments for each weight type of the phase (at most two: QKV may mix Q4_K and Q6_K)
-            const int type_a = F.seg[0].type;
-            int type_b = -1;
-            for (int k = 1; k < F.nseg; k++)
-                if (F.seg[k].type != type_a) type_b = F.seg[k].type;
-            auto stage = [&](int ty, uint2 *dst) {
-                switch (ty) {
-                case T_Q4_K: pk_stage<T_Q4_K>(F, xin, in_smem, rrms, scale, dst); break;
-                case T_Q6_K: pk_stage<T_Q6_K>(F, xin, in_smem, rrms, scale, dst); break;
-                default: pk_stage<T_F16>(F, xin, in_smem, rrms, scale, dst); break;
-                }
-            };
-            uint2 *xf1 = xf0 + (size_t)nb * 128;  // second type's fragments follow the first's
-            stage(type_a, xf0);
-            if (type_b >= 0) stage(type_b, xf1);
-            cbar();
-
-            // ---- tiles of this CTA
-            for (int tile = blockIdx.x; tile < F.n_tiles; tile += gridDim.x) {
-                int sidx, lt;
-                locate_p(F, tile, sidx, lt);
-                const PSeg &S = F.seg[sidx];
-                const int d = (int)(seq % PK_NDESC);
-                if (tid == 0) {
-                    if (!pk_mbar_wait(&full[d], (uint32_t)((seq / PK_NDESC) & 1), &abort_flag)) {
-                        abort_flag = 1;
-                        *P.io_err = 4;
-                    }
-                    stop = abort_flag;
-                }
-                cbar();  // tile landed (thread 0 observed the mbarrier) and `stop` is published
-                if (stop) break;
-                const uint8_t *buf = ring + tile_off[d];
-                const uint2 *xf = (S.type == type_a) ? xf0 : xf1;
-                const int bb = S.type == T_Q4_K ? 144 : (S.type == T_Q6_K ? 210 : 512);
-                float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-                for (int b = warp; b < nb; b += PK_WARPS) {
-                    const uint2 *xfb = xf + (size_t)b * 128;
-                    for (int m = 0; m < F.nmat; m++) {
-                        const uint8_t *mb = buf + (size_t)m * TC_M * S.stride + (size_t)b * bb;
-                        const uint8_t *rg = mb + (size_t)g * S.stride, *rg8 = mb + (size_t)(g + 8) * S.stride;
-                        switch (S.type) {
-                        case T_Q4_K: TcDot<T_Q4_K>::run(rg, rg8, xfb, g, t, acc[m]); break;
-                        case T_Q6_K: TcDot<T_Q6_K>::run(rg, rg8, xfb, g, t, acc[m]); break;
-                        default: TcDot<T_F16>::run(rg, rg8, xfb, g, t, acc[m]); break;
-                        }
-                    }
-                }
-                if (t == 0) {
-                    for (int m = 0; m < F.nmat; m++) {
-                        red[(warp * 2 + m) * TC_M + g] = acc[m][0] + acc[m][1];
-                        red[(warp * 2 + m) * TC_M + g + 8] = acc[m][2] + acc[m][3];
-                    }
-                }
-                cbar();  // tile consumed, partials visible
-                if (tid == 0) mbar_arrive(&empty[d]);
-                if (tid < TC_M) {
-                    const int r = lt * TC_M + tid;
-                    float v[2] = {0.f, 0.f};
-                    for (int m = 0; m < F.nmat; m++) {
-                        float sum = 0.f;
-#pragma unroll
-                        for (int w = 0; w < PK_WARPS; w++) sum += red[(w * 2 + m) * TC_M + tid];
-                        v[m] = sum * unscale;
-                    }
-                    if (r < S.rows) {
-                        if (F.kind == PH_QKV) {
-                            F.y[S.out_off + r] = v[0];
-                        } else if (F.kind == PH_RESID) {
-                            F.resid[r] = __fadd_rn(__ldcg(F.resid + r), v[0]);
-                        } else if (F.kind == PH_SWIGLU) {
-                            F.y[r] = __fmul_rn(__fdiv_rn(v[0], __fadd_rn(1.0f, expf(-v[0]))), v[1]);
-                        } else {  // PH_LM
-                            F.y[r] = v[0];
-                            if (better(v[0], r, best_v, best_i)) {
-                                best_v = v[0];
-                                best_i = r;
-                            }
-                        }
-                    }
-                }
-                cbar();  // red reused by the next tile
-                seq++;
-            }
-            if (stop) break;
-        }
+        bool ok = true;
+        if (F.kind == PH_ATTN)
+            ok = pk_attn_phase<HD, G>(P, F, pos, nch, U, seq, wfull);
+        else if (gemv)
+            ok = pk_gemv_phase<HD, G>(P, F, token0, seq, wfull, best_v, best_i, T);
+        if (!ok) break;
+        T.mark(3);
+        T.put(4, (unsigned long long)wfull);
 
         if (F.kind == PH_LM) {
-            // greedy argmax: CTA candidate, then the last CTA reduces all of them
-            if (warp == 0) {
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) {
-                    const float ov = __shfl_xor_sync(0xffffffffu, best_v, o);
-                    const int oi = __shfl_xor_sync(0xffffffffu, best_i, o);
-                    if (better(ov, oi, best_v, best_i)) {
-                        best_v = ov;
-                        best_i = oi;
-                    }
-                }
-                if (lane == 0) {
-                    P.am_part[blockIdx.x] = make_float2(best_v, __int_as_float(best_i));
-                    __threadfence();
-                    ticket = atomicAdd(P.am_count, 1u);
-                }
-            }
-            cbar();
-            if (ticket == gridDim.x - 1) {
-                __threadfence();
-                float bv = -INFINITY;
-                int bi = 0x7fffffff;
-                for (int i = tid; i < (int)gridDim.x; i += PK_CONSUMERS) {
-                    const float2 e2 = __ldcg(P.am_part + i);
-                    const int ei = __float_as_int(e2.y);
-                    if (better(e2.x, ei, bv, bi)) {
-                        bv = e2.x;
-                        bi = ei;
-                    }
-                }
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) {
-                    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-                    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-                    if (better(ov, oi, bv, bi)) {
-                        bv = ov;
-                        bi = oi;
-                    }
-                }
-                if (lane == 0) cand[warp] = make_float2(bv, __int_as_float(bi));
-                cbar();
-                if (tid == 0) {
-                    for (int w = 1; w < PK_WARPS; w++) {
-                        const int wi = __float_as_int(cand[w].y);
-                        if (better(cand[w].x, wi, bv, bi)) {
-                            bv = cand[w].x;
-                            bi = wi;
-                        }
-                    }
-                    if (bi == 0x7fffffff) bi = 0;
-                    *P.io_argmax = bi;
-                    if (P.loop) {
-                        *P.io_token = bi;
-                        *P.io_pos = *P.io_pos + 1;
-                        const int st = *P.io_step;
-                        P.rec_tokens[st] = bi;
-                        *P.io_step = st + 1;
-                    }
-                    *P.am_count = 0u;
-                }
-            }
+            pk_argmax_finish(P, best_v, best_i);
         } else {
-            // arrive: this CTA's outputs of the phase are written
+            // arrive: this CTA's outputs of the phase are written; the next
+            // descriptor has landed
+            cp_async_wait_all();
             cbar();
             if (tid == 0) {
                 __threadfence();
                 atomicAdd(P.bar + ph, 1u);
             }
         }
+        T.mark(5);
     }
+    cp_async_wait_all();
 }
 
 }  // namespace fiber

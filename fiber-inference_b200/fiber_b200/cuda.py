@@ -22,7 +22,7 @@ I32P = np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS")
 EXPORTED = [
     "fiber_last_error", "fiber_device_count", "fiber_cuda_init", "fiber_cuda_free", "fiber_forward_token",
     "fiber_prefill", "fiber_decode_greedy", "fiber_step_launches", "fiber_set_decode_mode",
-    "fiber_get_decode_mode", "fiber_time_kernel", "fiber_gemv",
+    "fiber_get_decode_mode", "fiber_trace_step", "fiber_time_kernel", "fiber_gemv",
     "fiber_dequant", "fiber_gemv_host", "gpu_init", "gpu_free", "gpu_embed", "gpu_forward_token",
     "gpu_get_logits", "gpu_forward_classifier", "gpu_get_device", "kv_cache_init", "kv_cache_init_paged",
     "kv_cache_free", "kv_cache_write", "kv_cache_read", "fiber_gemv_argmax_noalloc",
@@ -61,6 +61,8 @@ def cuda_lib() -> C.CDLL:
         L.fiber_step_launches.argtypes = [C.c_void_p]
         L.fiber_set_decode_mode.argtypes = [C.c_void_p, C.c_int]
         L.fiber_get_decode_mode.argtypes = [C.c_void_p]
+        L.fiber_trace_step.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_size_t,
+                                       C.POINTER(C.c_int), C.POINTER(C.c_int)]
         L.fiber_time_kernel.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.POINTER(C.c_double),
                                         C.POINTER(C.c_double)]
         L.fiber_gemv.argtypes = [C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p]
@@ -222,6 +224,19 @@ class Context:
         if n < 0:
             _check(n, "fiber_step_launches")
         return int(n)
+
+    TRACE_FIELDS = ["t_release_ns", "cyc_barrier", "cyc_stage", "cyc_tiles", "cyc_wait_tiles", "cyc_arrive",
+                    "t_producer_done_ns", "cyc_producer_wait", "cyc_stage_stats", "cyc_stage_frags"]
+
+    def trace_step(self, kv: KVCache, token: int, pos: int, max_phases: int = 4096, max_ctas: int = 1024):
+        """Per-phase, per-CTA timeline of one persistent step: uint64 array
+        [n_phases, n_ctas, len(TRACE_FIELDS)] with the fields of TRACE_FIELDS."""
+        nf = len(self.TRACE_FIELDS)
+        buf = np.zeros(max_phases * max_ctas * nf, np.uint64)
+        nph, nct = C.c_int(), C.c_int()
+        _check(cuda_lib().fiber_trace_step(self.h, kv.addr, int(token), int(pos), buf.ctypes.data, buf.size,
+                                           C.byref(nph), C.byref(nct)), "fiber_trace_step")
+        return buf[: nph.value * nct.value * nf].reshape(nph.value, nct.value, nf)
 
     KINDS = ["qkv", "attention", "wo", "gate_up", "down", "lm_head", "embed"]
 

@@ -80,6 +80,19 @@ int fiber_get_decode_mode(fiber_ctx_t *ctx);
 /* Number of kernels one decode step launches (all of them this library's own). */
 int fiber_step_launches(fiber_ctx_t *ctx);
 
+/* Timeline of one persistent decode step (mode 0): runs the step for `token` at
+ * `pos` and fills out[n_phases][n_ctas][10] (uint64) with, per phase and CTA:
+ * 0 globaltimer ns when the phase's grid barrier released the CTA, 1 SM cycles
+ * at that barrier, 2 cycles staging the input vector, 3 cycles in the tile loop
+ * (attention: the units), 4 of those waiting for weight tiles to land, 5 cycles
+ * to the arrive, 6 globaltimer ns when the producer issued the phase's last
+ * tile, 7 producer cycles spent waiting for ring space in the phase, 8 of
+ * field 2 the cycles until the input statistics are reduced, 9 of field 2 the
+ * cycles staging the fragments.
+ * `cap` is the number of uint64 values `out` holds. */
+int fiber_trace_step(fiber_ctx_t *ctx, kv_cache_t *kv, int token, int pos, uint64_t *out, size_t cap,
+                     int *n_phases, int *n_ctas);
+
 /* Device time of one kernel kind of the decode step, measured the way it runs in
  * the step: a CUDA graph of its n_layers per-layer launches (lm_head and embed:
  * n_layers repeats) is replayed `reps` times between CUDA events on the context
