@@ -40,7 +40,7 @@ constexpr int PK_RPRE = 8;                      // residual rows prefetched for 
 constexpr long long PK_SPIN_LIMIT = 1ll << 22;  // grid-barrier polls (with ~100 ns sleeps)
 // Optional per-phase, per-CTA timeline (PParams::trace non-null), fields:
 //  0 globaltimer (ns) when the phase's grid barrier released the CTA
-//  1 SM cycles spent at that barrier     2 cycles staging the input vector
+//  1 SM cycles from the phase start to that release     2 cycles staging the input vector
 //  3 cycles in the tile loop (or attention units)   4 of those waiting for tiles to land
 //  5 cycles from the end of the tile loop to the arrive
 //  6 producer: globaltimer (ns) after issuing the phase's last tile   7 producer: cycles waiting for ring space
@@ -130,6 +130,7 @@ __shared__ float pk_stat[2 * PK_WARPS];
 __shared__ unsigned int pk_ticket;
 __shared__ volatile int pk_abort;                // set by any thread that gives up (producer included)
 __shared__ int pk_stop;                          // consumers' uniform copy, written by thread 0 before a barrier
+__shared__ int pk_gstop;                         // the same for the grid-barrier wait
 __shared__ int pk_tile_off[PK_NDESC];            // ring offset of each tile in flight (producer -> consumers)
 
 FDEV uint8_t *pk_ring() { return pk_dyn; }
@@ -143,7 +144,7 @@ FDEV unsigned long long gtimer() {
     return t;
 }
 
-FDEV void cbar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+FDEV void cbar() { asm volatile("bar.sync 1, %0;" ::"n"(PK_CONSUMERS) : "memory"); }
 FDEV void mbar_arrive(uint64_t *bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
@@ -237,6 +238,34 @@ FDEV void ring_release(int seq) {
     if (threadIdx.x == 0) mbar_arrive(&pk_empty[seq % PK_NDESC]);
 }
 
+// Wait until every CTA has finished phase ph - 1 (all consumer threads; thread 0
+// polls the arrive counter with bounded spins and publishes the stop decision
+// before the barrier). Also completes this thread's async copies.
+FDEV bool pk_grid_wait(const PParams &P, int ph) {
+    if (threadIdx.x == 0) {
+        if (ph > 0) {
+            bool ok = false;
+            const unsigned int *cnt = P.bar + (ph - 1);
+            for (long long i = 0; i < PK_SPIN_LIMIT; i++) {
+                if (ld_acquire_u32(cnt) >= gridDim.x) {
+                    ok = true;
+                    break;
+                }
+                if ((i & 63) == 63 && pk_abort) break;
+                __nanosleep(32);
+            }
+            if (!ok) {
+                pk_abort = 1;
+                *P.io_err = 4;
+            }
+        }
+        pk_gstop = pk_abort;
+    }
+    cp_async_wait_all();
+    cbar();
+    return !pk_gstop;
+}
+
 // ---- GEMV pieces ---------------------------------------------------------------------
 
 // Fragments of the staged input for weight type T: fp16 hi/lo pairs of
@@ -325,264 +354,260 @@ FDEV void pk_dot(const uint8_t *buf, int stride, const uint2 *xf, int nb) {
 
 // ---- attention -----------------------------------------------------------------------
 
-// Partial record of one (unit, query head): max, sum, 2 pad, o[hd] (16-byte aligned o).
-#define PK_REC(hd) ((hd) + 4)
-
-// Attention work split of one layer: nch pages of ATTN_P positions; U units per
-// KV head (at most one per CTA and KV head), unit u covering pages
-// [u*nch/U, (u+1)*nch/U). Producer and consumers derive it from the same pos.
-FDEV void pk_attn_geom(int pos, int n_kv, int grid, int &nch, int &U) {
-    nch = pos / ATTN_P + 1;
-    U = min(nch, max(1, grid / n_kv));
-}
-
-// One attention unit of the persistent step (KV head g, unit u, pages [p0, p1)):
-// RoPE of q, the new position's K/V (rotated, fp16) appended to the cache by the
-// unit that holds the last page, the unit's pages taken from the ring (the
-// producer prefetched them), then per page the same score / softmax / P.V
-// arithmetic as attn_unit, pages combined online, and one (max, sum, o[hd])
-// partial per query head written for the merge in the next phase.
-// Returns false when the step was stopped.
+// One query head h of the attention phase, on one CTA: RoPE of q and of the new
+// position's k; the CTA holding query head g*G (g = h's KV head) appends the new
+// K/V row (fp16) to the cache; the KV head's pages come through the ring (the
+// producer prefetched them, in page order) and warp w takes pages w, w+8, ...,
+// combining its pages online (max, sum, o); the eight warp results are merged in
+// shared memory in warp order and the head's output is written as Wo's input
+// fragments (elements h*hd .. h*hd + hd - 1). Scores use fp32 FMAs over fp16 K
+// (lanes over positions, each lane starting at a rotated word so the reads of
+// the dense page are free of bank conflicts). Returns false when the step stopped.
 template <int HD, int G>
-FDEV bool pk_attn_unit(const PParams &P, const PPhase &F, int g, int u, int U, int p0, int p1, int pos, int &seq,
-                       long long &wfull) {
-    const int layer = F.layer;
+FDEV bool pk_attn_head(const PParams &P, const PPhase &F, int h, int pos, int nch, int &seq, long long &wfull) {
     constexpr int PG = ATTN_P;
-    constexpr int KST = HD + 2;
-    constexpr int DPL = HD / 32;
+    constexpr int W = HD / 2;    // 32-bit words of a K/V row
+    constexpr int DPL = HD / 32;  // head dims per lane in P.V
     const AttnParams &a = P.attn;
     uint8_t *sm = reinterpret_cast<uint8_t *>(pk_xf(P));
-    float(*qs)[HD] = reinterpret_cast<float(*)[HD]>(sm);
-    uint16_t(*ks)[KST] = reinterpret_cast<uint16_t(*)[KST]>(sm + G * HD * 4);
-    uint16_t *nk = reinterpret_cast<uint16_t *>(sm + G * HD * 4 + PG * KST * 2);  // new K row (16-byte aligned)
-    uint16_t *nv = nk + HD;
+    float *qs = reinterpret_cast<float *>(sm);                       // [HD] rotated q
+    uint16_t *nk = reinterpret_cast<uint16_t *>(sm + HD * 4);        // [HD] new K row (fp16)
+    uint16_t *nv = nk + HD;                                          // [HD] new V row (fp16)
+    float *wm = reinterpret_cast<float *>(sm + HD * 4 + HD * 4);     // [PK_WARPS][HD + 2] warp results
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int seqlen = pos + 1, nch = pos / PG + 1, tn = pos - (nch - 1) * PG;
-    const int kvd = a.n_kv * HD;
+    const int g = h / G, seqlen = pos + 1, tn = pos - (nch - 1) * PG;
     const float2 *rp = a.rope + (size_t)pos * (HD / 2);
-
-    for (int i = tid; i < G * (HD / 2); i += PK_CONSUMERS) {
-        const int h = i / (HD / 2), j = i % (HD / 2);
-        const float *qh = a.qkv + (size_t)(g * G + h) * HD;
-        const float x1 = __ldcg(qh + j), x2 = __ldcg(qh + j + HD / 2);
+    const float *qh = a.qkv + (size_t)h * HD;
+    const float *kr = a.qkv + (size_t)a.n_heads * HD + (size_t)g * HD;
+    const float *vr = kr + (size_t)a.n_kv * HD;
+    const bool writer = h % G == 0;  // appends the new K/V row of KV head g
+    const size_t base = (((size_t)a.page_table[nch - 1] * a.n_layers + F.layer) * a.n_kv + g) * (size_t)PG * HD;
+    for (int j = tid; j < HD / 2; j += PK_CONSUMERS) {
         const float2 cs = __ldg(rp + j);
-        qs[h][j] = __fsub_rn(__fmul_rn(x1, cs.x), __fmul_rn(x2, cs.y));
-        qs[h][j + HD / 2] = __fadd_rn(__fmul_rn(x1, cs.y), __fmul_rn(x2, cs.x));
-    }
-    if (p1 == nch) {
-        const int page = a.page_table[nch - 1];
-        const size_t base = (((size_t)page * a.n_layers + layer) * a.n_kv + g) * (size_t)PG * HD;
-        uint16_t *kp = a.k_pool + base, *vp = a.v_pool + base;
-        const float *kr = a.qkv + (size_t)a.n_heads * HD + (size_t)g * HD;
-        const float *vr = kr + kvd;
-        for (int j = tid; j < HD / 2; j += PK_CONSUMERS) {
-            const float x1 = __ldcg(kr + j), x2 = __ldcg(kr + j + HD / 2);
-            const float2 cs = __ldg(rp + j);
-            const uint16_t y1 = __half_as_ushort(__float2half_rn(__fsub_rn(__fmul_rn(x1, cs.x), __fmul_rn(x2, cs.y))));
-            const uint16_t y2 = __half_as_ushort(__float2half_rn(__fadd_rn(__fmul_rn(x1, cs.y), __fmul_rn(x2, cs.x))));
-            nk[j] = y1;
-            nk[j + HD / 2] = y2;
-            kp[(size_t)tn * HD + j] = y1;
-            kp[(size_t)tn * HD + j + HD / 2] = y2;
-        }
-        for (int j = tid; j < HD; j += PK_CONSUMERS) {
-            const uint16_t h16 = __half_as_ushort(__float2half_rn(__ldcg(vr + j)));
-            nv[j] = h16;
-            vp[(size_t)tn * HD + j] = h16;
+        const float x1 = __ldcg(qh + j), x2 = __ldcg(qh + j + HD / 2);
+        qs[j] = __fsub_rn(__fmul_rn(x1, cs.x), __fmul_rn(x2, cs.y));
+        qs[j + HD / 2] = __fadd_rn(__fmul_rn(x1, cs.y), __fmul_rn(x2, cs.x));
+        const float k1 = __ldcg(kr + j), k2 = __ldcg(kr + j + HD / 2);
+        const uint16_t y1 = __half_as_ushort(__float2half_rn(__fsub_rn(__fmul_rn(k1, cs.x), __fmul_rn(k2, cs.y))));
+        const uint16_t y2 = __half_as_ushort(__float2half_rn(__fadd_rn(__fmul_rn(k1, cs.y), __fmul_rn(k2, cs.x))));
+        nk[j] = y1;
+        nk[j + HD / 2] = y2;
+        if (writer) {
+            a.k_pool[base + (size_t)tn * HD + j] = y1;
+            a.k_pool[base + (size_t)tn * HD + j + HD / 2] = y2;
         }
     }
+    for (int j = tid; j < HD; j += PK_CONSUMERS) {
+        const uint16_t h16 = __half_as_ushort(__float2half_rn(__ldcg(vr + j)));
+        nv[j] = h16;
+        if (writer) a.v_pool[base + (size_t)tn * HD + j] = h16;
+    }
+    cbar();  // qs, nk, nv ready
 
     float m_run = -INFINITY, l_run = 0.f, o_run[DPL];
 #pragma unroll
     for (int j = 0; j < DPL; j++) o_run[j] = 0.f;
-    for (int pg = p0; pg < p1; pg++) {
-        const uint8_t *tile = ring_acquire(P, seq, wfull);  // also publishes qs / nk / nv
-        if (!tile) return false;
-        const uint16_t *kpg = reinterpret_cast<const uint16_t *>(tile);
-        uint16_t *vpg = const_cast<uint16_t *>(kpg + PG * HD);
+    bool stopped = false;
+    for (int pg = warp; pg < nch; pg += PK_WARPS) {
+        const long long sq = seq + pg;
+        const int d = (int)(sq % PK_NDESC);
+        int got = 1;
+        if (lane == 0) {
+            const long long w0 = clock64();
+            got = pk_mbar_wait(&pk_full[d], (uint32_t)((sq / PK_NDESC) & 1));
+            if (!got) {
+                pk_abort = 1;
+                *P.io_err = 4;
+            }
+            if (tid == 0) wfull += clock64() - w0;
+        }
+        if (!__shfl_sync(0xffffffffu, got, 0)) {
+            stopped = true;
+            break;
+        }
+        const uint8_t *tile = pk_ring() + pk_tile_off[d];
+        const uint32_t *kw = reinterpret_cast<const uint32_t *>(tile);
+        uint16_t *vpg = reinterpret_cast<uint16_t *>(const_cast<uint8_t *>(tile)) + PG * HD;
         const int t0 = pg * PG, nt = min(PG, seqlen - t0);
         const bool last = pg == nch - 1;
-        constexpr int V8 = HD / 8;
-        for (int i = tid; i < nt * V8; i += PK_CONSUMERS) {
-            const int t = i / V8, k8 = i % V8;
-            const uint4 kv4 = (last && t == tn) ? reinterpret_cast<const uint4 *>(nk)[k8]
-                                                : reinterpret_cast<const uint4 *>(kpg + (size_t)t * HD)[k8];
-            uint32_t *kd = reinterpret_cast<uint32_t *>(&ks[t][8 * k8]);
-            kd[0] = kv4.x; kd[1] = kv4.y; kd[2] = kv4.z; kd[3] = kv4.w;
-        }
-        if (last)
-            for (int j = tid; j < HD / 2; j += PK_CONSUMERS)
+        if (last) {  // the page holding pos: the new V row replaces the copy's (stale) row
+            for (int j = lane; j < W; j += 32)
                 reinterpret_cast<uint32_t *>(vpg + (size_t)tn * HD)[j] = reinterpret_cast<const uint32_t *>(nv)[j];
-        cbar();
-        if (warp < G) {
-            const int h = warp;
-            float sc2[2];
+            __syncwarp();
+        }
+        // scores of positions lane and lane + 32
+        float sc2[2];
 #pragma unroll
-            for (int k = 0; k < 2; k++) {
-                const int t = lane + 32 * k;
-                float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;
-                if (t < nt) {
-#pragma unroll
-                    for (int d = 0; d < HD; d += 4) {
-                        d0 = fmaf(qs[h][d + 0], __half2float(__ushort_as_half(ks[t][d + 0])), d0);
-                        d1 = fmaf(qs[h][d + 1], __half2float(__ushort_as_half(ks[t][d + 1])), d1);
-                        d2 = fmaf(qs[h][d + 2], __half2float(__ushort_as_half(ks[t][d + 2])), d2);
-                        d3 = fmaf(qs[h][d + 3], __half2float(__ushort_as_half(ks[t][d + 3])), d3);
-                    }
+        for (int k = 0; k < 2; k++) {
+            const int t = lane + 32 * k;
+            const uint32_t *row = (last && t == tn) ? reinterpret_cast<const uint32_t *>(nk) : kw + (size_t)t * W;
+            float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;
+            if (t < nt) {
+#pragma unroll 8
+                for (int w2 = 0; w2 < W; w2 += 2) {
+                    const int wa = (w2 + lane) % W, wb = (w2 + 1 + lane) % W;
+                    const float2 ka = __half22float2(*reinterpret_cast<const __half2 *>(row + wa));
+                    const float2 kb = __half22float2(*reinterpret_cast<const __half2 *>(row + wb));
+                    const float2 qa = *reinterpret_cast<const float2 *>(qs + 2 * wa);
+                    const float2 qb = *reinterpret_cast<const float2 *>(qs + 2 * wb);
+                    d0 = fmaf(qa.x, ka.x, d0);
+                    d1 = fmaf(qa.y, ka.y, d1);
+                    d2 = fmaf(qb.x, kb.x, d2);
+                    d3 = fmaf(qb.y, kb.y, d3);
                 }
-                sc2[k] = t < nt ? __fmul_rn((d0 + d1) + (d2 + d3), a.scale) : -INFINITY;
             }
-            float m = fmaxf(sc2[0], sc2[1]);
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-            const float e0 = lane < nt ? expf(sc2[0] - m) : 0.f;
-            const float e1 = lane + 32 < nt ? expf(sc2[1] - m) : 0.f;
-            float l = e0 + e1;
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
-            float o1[DPL], o2[DPL];
-#pragma unroll
-            for (int j = 0; j < DPL; j++) o1[j] = o2[j] = 0.f;
-            const int n0 = min(nt, 32);
-            for (int t = 0; t < n0; t++) {
-                const float w = __shfl_sync(0xffffffffu, e0, t);
-#pragma unroll
-                for (int j = 0; j < DPL; j++)
-                    o1[j] = fmaf(w, __half2float(__ushort_as_half(vpg[(size_t)t * HD + lane + 32 * j])), o1[j]);
-            }
-            for (int t = 32; t < nt; t++) {
-                const float w = __shfl_sync(0xffffffffu, e1, t - 32);
-#pragma unroll
-                for (int j = 0; j < DPL; j++)
-                    o2[j] = fmaf(w, __half2float(__ushort_as_half(vpg[(size_t)t * HD + lane + 32 * j])), o2[j]);
-            }
-            if (pg == p0) {
-                m_run = m;
-                l_run = l;
-#pragma unroll
-                for (int j = 0; j < DPL; j++) o_run[j] = o1[j] + o2[j];
-            } else {
-                const float M = fmaxf(m_run, m);
-                const float al = expf(m_run - M), be = expf(m - M);
-                l_run = fmaf(al, l_run, be * l);
-#pragma unroll
-                for (int j = 0; j < DPL; j++) o_run[j] = fmaf(al, o_run[j], be * (o1[j] + o2[j]));
-                m_run = M;
-            }
+            sc2[k] = t < nt ? __fmul_rn((d0 + d1) + (d2 + d3), a.scale) : -INFINITY;
         }
-        ring_release(seq);
-        seq++;
-    }
-    if (warp < G) {
-        float *pc = a.part + ((size_t)(g * a.max_chunks + u) * G + warp) * PK_REC(HD);
+        float m = fmaxf(sc2[0], sc2[1]);
 #pragma unroll
-        for (int j = 0; j < DPL; j++) pc[4 + lane + 32 * j] = o_run[j];
-        if (lane == 0) {
-            pc[0] = m_run;
-            pc[1] = l_run;
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        const float e0 = lane < nt ? expf(sc2[0] - m) : 0.f;
+        const float e1 = lane + 32 < nt ? expf(sc2[1] - m) : 0.f;
+        float l = e0 + e1;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+        float o1[DPL], o2[DPL];
+#pragma unroll
+        for (int j = 0; j < DPL; j++) o1[j] = o2[j] = 0.f;
+        const int n0 = min(nt, 32);
+        for (int t = 0; t < n0; t++) {
+            const float w = __shfl_sync(0xffffffffu, e0, t);
+#pragma unroll
+            for (int j = 0; j < DPL; j++)
+                o1[j] = fmaf(w, __half2float(__ushort_as_half(vpg[(size_t)t * HD + lane + 32 * j])), o1[j]);
+        }
+        for (int t = 32; t < nt; t++) {
+            const float w = __shfl_sync(0xffffffffu, e1, t - 32);
+#pragma unroll
+            for (int j = 0; j < DPL; j++)
+                o2[j] = fmaf(w, __half2float(__ushort_as_half(vpg[(size_t)t * HD + lane + 32 * j])), o2[j]);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&pk_empty[d]);  // page consumed
+        if (pg == warp) {
+            m_run = m;
+            l_run = l;
+#pragma unroll
+            for (int j = 0; j < DPL; j++) o_run[j] = o1[j] + o2[j];
+        } else {
+            const float M = fmaxf(m_run, m);
+            const float al = expf(m_run - M), be = expf(m - M);
+            l_run = fmaf(al, l_run, be * l);
+#pragma unroll
+            for (int j = 0; j < DPL; j++) o_run[j] = fmaf(al, o_run[j], be * (o1[j] + o2[j]));
+            m_run = M;
         }
     }
-
-    // the last unit of this KV head merges the U partials (max, exp weights,
-    // weighted sums) and writes the heads' outputs as Wo's input fragments
-    __threadfence();
-    cbar();
-    if (tid == 0) pk_ticket = atomicAdd(a.count + g, 1u);
-    cbar();
-    if (pk_ticket != (unsigned)(U - 1)) return true;
-    __threadfence();
-    float2 *ml = reinterpret_cast<float2 *>(sm);          // [G][U] (max, sum)
-    float *wts = reinterpret_cast<float *>(ml + G * U);   // [G][U] exp weights
-    float *lsum = wts + G * U;                            // [G]
-    const size_t ustride = (size_t)G * PK_REC(HD);
-    const float *pg0 = a.part + (size_t)g * a.max_chunks * G * PK_REC(HD);
-    for (int i = tid; i < G * U; i += PK_CONSUMERS) {
-        const int h = i / U, uu = i % U;
-        ml[i] = __ldcg(reinterpret_cast<const float2 *>(pg0 + uu * ustride + (size_t)h * PK_REC(HD)));
+    // warp results -> shared memory, merged in warp order
+    float *wr = wm + warp * (HD + 2);
+#pragma unroll
+    for (int j = 0; j < DPL; j++) wr[2 + lane + 32 * j] = o_run[j];
+    if (lane == 0) {
+        wr[0] = stopped ? -INFINITY : m_run;
+        wr[1] = l_run;
     }
     cbar();
-    if (warp < (8 * G + 31) / 32) {  // 8 lanes per head, whole warps (full-mask shuffles)
-        const int h = tid >> 3, j = tid & 7;
-        const bool valid = h < G;
-        float M = -INFINITY;
-        if (valid)
-            for (int uu = j; uu < U; uu += 8) M = fmaxf(M, ml[h * U + uu].x);
-        M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, 1, 8));
-        M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, 2, 8));
-        M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, 4, 8));
-        float L = 0.f;
-        if (valid)
-            for (int uu = j; uu < U; uu += 8) {
-                const float w = expf(ml[h * U + uu].x - M);
-                wts[h * U + uu] = w;
-                L = fmaf(w, ml[h * U + uu].y, L);
-            }
-        L += __shfl_xor_sync(0xffffffffu, L, 1, 8);
-        L += __shfl_xor_sync(0xffffffffu, L, 2, 8);
-        L += __shfl_xor_sync(0xffffffffu, L, 4, 8);
-        if (valid && j == 0) lsum[h] = L;
-    }
-    cbar();
+    if (tid == 0) pk_stop = pk_abort;
+    seq += nch;
     bool ok = true;
-    for (int q = tid; q < G * HD / 4; q += PK_CONSUMERS) {
-        const int h = (4 * q) / HD, dd = (4 * q) % HD;
-        const float4 *pb = reinterpret_cast<const float4 *>(pg0 + (size_t)h * PK_REC(HD) + 4 + dd);
-        float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int u0 = 0; u0 < U; u0 += 4) {
-            float4 o[4];
+    for (int dd = tid; dd < HD; dd += PK_CONSUMERS) {
+        float M = -INFINITY;
 #pragma unroll
-            for (int j = 0; j < 4; j++)
-                if (u0 + j < U) o[j] = __ldcg(pb + (u0 + j) * (ustride >> 2));
+        for (int w = 0; w < PK_WARPS; w++) M = fmaxf(M, wm[w * (HD + 2)]);
+        float L = 0.f, O = 0.f;
 #pragma unroll
-            for (int j = 0; j < 4; j++) {
-                if (u0 + j < U) {
-                    const float w = wts[h * U + u0 + j];
-                    O.x = fmaf(w, o[j].x, O.x);
-                    O.y = fmaf(w, o[j].y, O.y);
-                    O.z = fmaf(w, o[j].z, O.z);
-                    O.w = fmaf(w, o[j].w, O.w);
-                }
-            }
+        for (int w = 0; w < PK_WARPS; w++) {
+            const float mw = wm[w * (HD + 2)];
+            if (mw == -INFINITY) continue;  // a warp without pages
+            const float e = expf(mw - M);
+            L = fmaf(e, wm[w * (HD + 2) + 1], L);
+            O = fmaf(e, wm[w * (HD + 2) + 2 + dd], O);
         }
-        const float L = lsum[h];
-        const int k0 = (g * G + h) * HD + dd;
-        ok &= pk_frag_out(F, k0 + 0, O.x / L);
-        ok &= pk_frag_out(F, k0 + 1, O.y / L);
-        ok &= pk_frag_out(F, k0 + 2, O.z / L);
-        ok &= pk_frag_out(F, k0 + 3, O.w / L);
+        ok &= pk_frag_out(F, h * HD + dd, O / L);
     }
     if (!ok) *P.io_err = 5;
-    if (tid == 0) a.count[g] = 0u;
-    cbar();  // shared memory reused by the next unit
-    return true;
+    cbar();  // pk_stop published; shared memory reused by the next head
+    return !pk_stop;
 }
 
-// Attention phase of layer `layer`: this CTA's units. Returns false when stopped.
+// Attention phase: this CTA's query heads. Returns false when stopped.
 template <int HD, int G>
-__device__ __noinline__ bool pk_attn_phase(const PParams &P, const PPhase &F, int pos, int nch, int U, int &seq,
+__device__ __noinline__ bool pk_attn_phase(const PParams &P, const PPhase &F, int pos, int nch, int &seq,
                                            long long &wfull) {
     if (pos < 0 || pos >= P.attn.max_seq) {
         if (threadIdx.x == 0 && blockIdx.x == 0) *P.io_err = 1;
         return true;
     }
-    for (int ui = blockIdx.x; ui < P.attn.n_kv * U; ui += gridDim.x) {
-        const int g = ui / U, u = ui % U;
-        if (!pk_attn_unit<HD, G>(P, F, g, u, U, u * nch / U, (u + 1) * nch / U, pos, seq, wfull)) return false;
-    }
+    for (int h = blockIdx.x; h < P.attn.n_heads; h += gridDim.x)
+        if (!pk_attn_head<HD, G>(P, F, h, pos, nch, seq, wfull)) return false;
     return true;
 }
 
 // ---- GEMV phase ----------------------------------------------------------------------
+
+// Layer 0: every CTA decodes the embedding row of the current token, sums its
+// squares and stages x * norm as fragments itself; returns the RMSNorm scale.
+__device__ __noinline__ float pk_stage_embed(const PParams &P, const PPhase &F, int token0, int type_a, int type_b) {
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int n = F.cols, nb = n >> 8;
+    uint2 *xf0 = pk_xf(P), *xf1 = xf0 + (size_t)nb * 128;
+    float rrms = 1.0f;
+    // embedding row of the current token: every CTA decodes it, sums its
+    // squares and stages x * norm itself
+    const float *nw = F.norm_w ? pk_nws(P) : nullptr;
+    float *xs = pk_xs(P);
+    int tok = token0;
+    if (tok < 0 || tok >= P.vocab) {
+        if (tid == 0 && blockIdx.x == 0) *P.io_err = 2;
+        tok = 0;
+    }
+    float ss = 0.f;
+    for (int i = tid; i < n; i += PK_CONSUMERS) {
+        float v;
+        switch (P.embd_type) {
+        case T_F16: v = h2f(reinterpret_cast<const uint16_t *>(P.embd)[(size_t)tok * n + i]); break;
+        case T_F32: v = round_f16(reinterpret_cast<const float *>(P.embd)[(size_t)tok * n + i]); break;
+        case T_Q4_K: v = round_f16(decode_elem<T_Q4_K>(P.embd + ((size_t)tok * (n >> 8) + (i >> 8)) * 144, i & 255)); break;
+        case T_Q5_K: v = round_f16(decode_elem<T_Q5_K>(P.embd + ((size_t)tok * (n >> 8) + (i >> 8)) * 176, i & 255)); break;
+        default: v = round_f16(decode_elem<T_Q6_K>(P.embd + ((size_t)tok * (n >> 8) + (i >> 8)) * 210, i & 255)); break;
+        }
+        xs[i] = v;
+        if (blockIdx.x == 0) P.x[i] = v;  // the residual stream starts as the embedding
+        ss = fmaf(v, v, ss);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (lane == 0) pk_stat[warp] = ss;
+    cbar();
+    ss = 0.f;
+#pragma unroll
+    for (int w = 0; w < PK_WARPS; w++) ss += pk_stat[w];
+    if (nw) rrms = 1.0f / sqrtf(ss / (float)n + F.eps);
+    for (int pass = 0; pass < (type_b >= 0 ? 2 : 1); pass++) {
+        uint2 *dst = pass ? xf1 : xf0;
+        switch (pass ? type_b : type_a) {
+        case T_Q4_K: pk_stage<T_Q4_K>(nb, xs, nw, 1.0f, 1.0f, dst); break;
+        case T_Q6_K: pk_stage<T_Q6_K>(nb, xs, nw, 1.0f, 1.0f, dst); break;
+        default: pk_stage<T_F16>(nb, xs, nw, 1.0f, 1.0f, dst); break;
+        }
+    }
+    cbar();
+    return rrms;
+}
 
 // One GEMV phase of this CTA: stage the input fragments (written by the previous
 // phase, or the embedding row staged here), then decode + multiply its tiles
 // from the ring and apply the epilogue, which also writes the next phase's
 // input fragments. Returns false when the step stopped.
 template <int HD, int G>
-__device__ __noinline__ bool pk_gemv_phase(const PParams &P, const PPhase &F, int token0, int &seq, long long &wfull,
-                                           float &best_v, int &best_i, PkTrace &T) {
+__device__ __noinline__ bool pk_gemv_phase(const PParams &P, const PPhase &F, int ph, int token0, int &seq,
+                                           long long &wfull, float &best_v, int &best_i, PkTrace &T) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int n = F.cols, nb = n >> 8;
+    if (!pk_grid_wait(P, ph)) return false;
+    T.put(0, gtimer());
+    T.mark(1);
+
     // layouts: one per weight type of the phase (at most two: QKV may mix Q4_K and Q6_K)
     const int type_a = F.seg[0].type;
     int type_b = -1;
@@ -591,46 +616,7 @@ __device__ __noinline__ bool pk_gemv_phase(const PParams &P, const PPhase &F, in
     uint2 *xf0 = pk_xf(P), *xf1 = xf0 + (size_t)nb * 128;  // second layout follows the first
     float rrms = 1.0f;
     if (F.embed_in) {
-        // embedding row of the current token: every CTA decodes it, sums its
-        // squares and stages x * norm itself
-        const float *nw = F.norm_w ? pk_nws(P) : nullptr;
-        float *xs = pk_xs(P);
-        int tok = token0;
-        if (tok < 0 || tok >= P.vocab) {
-            if (tid == 0 && blockIdx.x == 0) *P.io_err = 2;
-            tok = 0;
-        }
-        float ss = 0.f;
-        for (int i = tid; i < n; i += PK_CONSUMERS) {
-            float v;
-            switch (P.embd_type) {
-            case T_F16: v = h2f(reinterpret_cast<const uint16_t *>(P.embd)[(size_t)tok * n + i]); break;
-            case T_F32: v = round_f16(reinterpret_cast<const float *>(P.embd)[(size_t)tok * n + i]); break;
-            case T_Q4_K: v = round_f16(decode_elem<T_Q4_K>(P.embd + ((size_t)tok * (n >> 8) + (i >> 8)) * 144, i & 255)); break;
-            case T_Q5_K: v = round_f16(decode_elem<T_Q5_K>(P.embd + ((size_t)tok * (n >> 8) + (i >> 8)) * 176, i & 255)); break;
-            default: v = round_f16(decode_elem<T_Q6_K>(P.embd + ((size_t)tok * (n >> 8) + (i >> 8)) * 210, i & 255)); break;
-            }
-            xs[i] = v;
-            if (blockIdx.x == 0) P.x[i] = v;  // the residual stream starts as the embedding
-            ss = fmaf(v, v, ss);
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-        if (lane == 0) pk_stat[warp] = ss;
-        cbar();
-        ss = 0.f;
-#pragma unroll
-        for (int w = 0; w < PK_WARPS; w++) ss += pk_stat[w];
-        if (nw) rrms = 1.0f / sqrtf(ss / (float)n + F.eps);
-        for (int pass = 0; pass < (type_b >= 0 ? 2 : 1); pass++) {
-            uint2 *dst = pass ? xf1 : xf0;
-            switch (pass ? type_b : type_a) {
-            case T_Q4_K: pk_stage<T_Q4_K>(nb, xs, nw, 1.0f, 1.0f, dst); break;
-            case T_Q6_K: pk_stage<T_Q6_K>(nb, xs, nw, 1.0f, 1.0f, dst); break;
-            default: pk_stage<T_F16>(nb, xs, nw, 1.0f, 1.0f, dst); break;
-            }
-        }
-        cbar();
+        rrms = pk_stage_embed(P, F, token0, type_a, type_b);
     } else {
         // fragments and per-CTA sums of squares written by the previous phase
         const int chunks = (type_b >= 0 ? 2 : 1) * (n >> 2);  // 16-byte chunks, 4n bytes per layout
@@ -639,9 +625,12 @@ __device__ __noinline__ bool pk_gemv_phase(const PParams &P, const PPhase &F, in
             for (int c = tid; c < ((int)gridDim.x + 3) / 4; c += PK_CONSUMERS) cp_async16(pk_ssin + 4 * c, F.ss_in + 4 * c);
         cp_async_wait_all();
         cbar();
-        if (F.ss_in && tid < TC_M) {
+        if (F.ss_in && warp == 0) {
+            // sum of the per-CTA partials: fixed per-lane strides, then a fixed tree
             float ss = 0.f;
-            for (int i = 0; i < (int)gridDim.x; i++) ss += pk_ssin[i];
+            for (int i = lane; i < (int)gridDim.x; i += 32) ss += pk_ssin[i];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
             rrms = 1.0f / sqrtf(ss / (float)n + F.eps);
         }
     }
@@ -793,7 +782,7 @@ FDEV void pk_argmax_finish(const PParams &P, float best_v, int best_i) {
 // Single-thread producer: ring space for the next tile is a slot and `size`
 // contiguous bytes (the ring's end is skipped when the tile would straddle it).
 template <int HD>
-__device__ __noinline__ void pk_producer(const PParams &P, int pos, int nch, int U) {
+__device__ __noinline__ void pk_producer(const PParams &P, int pos, int nch) {
     uint8_t *ring = pk_ring();
     int head = 0, used = 0, need[PK_NDESC];
     long long seq = 0, oldest = 0, pwait = 0;
@@ -829,11 +818,12 @@ __device__ __noinline__ void pk_producer(const PParams &P, int pos, int nch, int
         const PPhase &F = P.phases[ph];
         pwait = 0;
         if (F.kind == PH_ATTN) {
-            // the K and V pages of this CTA's units (same order the consumers take them)
+            // the K and V pages of the KV head of each of this CTA's query heads, in page order
             constexpr uint32_t PAGE = ATTN_P * HD * 2;
-            for (int ui = blockIdx.x; pos_ok && ui < P.attn.n_kv * U && !pk_abort; ui += gridDim.x) {
-                const int g = ui / U, u = ui % U;
-                for (int pg = u * nch / U; pg < (u + 1) * nch / U; pg++) {
+            const int G = P.attn.n_heads / P.attn.n_kv;
+            for (int h = blockIdx.x; pos_ok && h < P.attn.n_heads && !pk_abort; h += gridDim.x) {
+                const int g = h / G;
+                for (int pg = 0; pg < nch; pg++) {
                     int d;
                     uint8_t *dst = reserve(2 * PAGE, d);
                     if (!dst) break;
@@ -906,13 +896,12 @@ __global__ void __launch_bounds__(PK_THREADS, 1) decode_persistent_kernel(const 
     cp_async_wait_all();
     __syncthreads();  // the only full-CTA barrier
 
-    // attention geometry of this step (pos is final for the whole launch)
+    // attention pages of this step (pos is final for the whole launch)
     const int pos = *P.attn.pos_ptr;
-    int nch = 0, U = 0;
-    if (pos >= 0 && pos < P.attn.max_seq) pk_attn_geom(pos, P.attn.n_kv, gridDim.x, nch, U);
+    const int nch = (pos >= 0 && pos < P.attn.max_seq) ? pos / ATTN_P + 1 : 0;
 
     if (warp == PK_WARPS) {
-        if (lane == 0) pk_producer<HD>(P, pos, nch, U);
+        if (lane == 0) pk_producer<HD>(P, pos, nch);
         return;
     }
 
@@ -927,6 +916,10 @@ __global__ void __launch_bounds__(PK_THREADS, 1) decode_persistent_kernel(const 
 
     for (int ph = 0; ph < P.n_phases; ph++) {
         const PPhase &F = pk_F[ph & 1];  // fetched during the previous phase
+        wfull = 0;
+        // the next phase's descriptor, into the other buffer (last read in phase
+        // ph - 1; complete at this phase's arrive barrier)
+        if (warp == 0 && ph + 1 < P.n_phases) pk_fetch_phase(&pk_F[(ph + 1) & 1], P.phases + ph + 1, lane);
         T.tr = (P.trace && tid == 0) ? P.trace + ((size_t)ph * gridDim.x + blockIdx.x) * PK_TRACE_FIELDS : nullptr;
         const bool gemv = F.kind != PH_ATTN && (int)blockIdx.x < F.n_tiles;
         // inputs that do not depend on the previous phase, fetched before its barrier:
@@ -946,44 +939,15 @@ __global__ void __launch_bounds__(PK_THREADS, 1) decode_persistent_kernel(const 
             }
         }
         if (!gemv && F.kind != PH_ATTN && F.ss_out && tid == 0) F.ss_out[blockIdx.x] = 0.f;  // no rows here
-        // wait until every CTA finished the previous phase (thread 0 polls; the
-        // stop decision is published before the barrier so all consumers agree)
-        if (tid == 0) {
-            if (ph > 0) {
-                bool ok = false;
-                const unsigned int *cnt = P.bar + (ph - 1);
-                for (long long i = 0; i < PK_SPIN_LIMIT; i++) {
-                    if (ld_acquire_u32(cnt) >= gridDim.x) {
-                        ok = true;
-                        break;
-                    }
-                    if ((i & 63) == 63 && pk_abort) break;
-                    __nanosleep(32);
-                }
-                if (ok) {
-                    __threadfence();  // order this CTA's reads of the phase inputs after the barrier
-                } else {
-                    pk_abort = 1;
-                    *P.io_err = 4;
-                }
-            }
-            pk_stop = pk_abort;
-        }
-        cp_async_wait_all();
-        cbar();
-        if (pk_stop) break;
-        // the next phase's descriptor, into the other buffer (read only after the
-        // arrive barrier below)
-        if (warp == 0 && ph + 1 < P.n_phases) pk_fetch_phase(&pk_F[(ph + 1) & 1], P.phases + ph + 1, lane);
-        T.put(0, gtimer());
-        T.mark(1);
-        wfull = 0;
-
         bool ok = true;
-        if (F.kind == PH_ATTN)
-            ok = pk_attn_phase<HD, G>(P, F, pos, nch, U, seq, wfull);
-        else if (gemv)
-            ok = pk_gemv_phase<HD, G>(P, F, token0, seq, wfull, best_v, best_i, T);
+        if (gemv) {
+            ok = pk_gemv_phase<HD, G>(P, F, ph, token0, seq, wfull, best_v, best_i, T);  // waits for phase ph - 1 itself
+        } else {
+            if (!pk_grid_wait(P, ph)) break;
+            T.put(0, gtimer());
+            T.mark(1);
+            if (F.kind == PH_ATTN) ok = pk_attn_phase<HD, G>(P, F, pos, nch, seq, wfull);
+        }
         if (!ok) break;
         T.mark(3);
         T.put(4, (unsigned long long)wfull);
