@@ -93,6 +93,22 @@ class Clocks:
                 "samples": len(sm)}
 
 
+# DRAM traffic of one decode_persistent_kernel launch from an ncu capture (prefill step at
+# position 5): dram__bytes_read.sum + dram__bytes_write.sum, and that launch's algorithmic bytes.
+PK_CAPTURE = {"dram_bytes": 635_117_056 + 4_474_368, "algorithmic_bytes": 633_500_000, "position": 5}
+
+
+def traffic_of(mode: int, roof: dict) -> dict:
+    """Per-launch DRAM traffic of the dominant kernel, scaled from the ncu capture by the
+    algorithmic bytes of the timed launches (traffic tracks the bytes streamed)."""
+    if mode != 0:
+        return {"traffic": None}
+    ratio = PK_CAPTURE["dram_bytes"] / PK_CAPTURE["algorithmic_bytes"]
+    return {"traffic": roof["algorithmic_bytes_per_launch"] * ratio,
+            "traffic_source": f"ncu capture at position {PK_CAPTURE['position']}: traffic/algorithmic = {ratio:.3f}, "
+                              "scaled to the timed launches' algorithmic bytes"}
+
+
 def make_model(path: str):
     import fiber_b200 as fb
 
@@ -321,7 +337,7 @@ def main():
                    "deterministic_tokens": deterministic, "prefill_tok_s": prefill_tps,
                    "step_mode": "persistent kernel per token" if mode == 0 else "one kernel per phase"},
         "roofline": dict(roof, bound="hbm", peak=peak, unit="GB/s", frac=roof["achieved"] / peak,
-                         peak_source=peak_kind, traffic=None),
+                         peak_source=peak_kind, **traffic_of(mode, roof)),
         "decode_roofline": {"bytes_per_token": step_bytes, "achieved_gbs": step_bytes * value / world / 1e9,
                             "frac": step_bytes * value / world / 1e9 / peak, "per_phase_kernels": kern,
                             "kv_position_for_kernel_timing": mid},

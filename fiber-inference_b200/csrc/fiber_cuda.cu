@@ -958,6 +958,9 @@ static int check_kv(gpu_context *c, const kv_cache_t *kv) {
 static int device_status(gpu_context *c) {
     if (c->h_io->err == 1) return set_err(FIBER_EARG, "position out of range on the device");
     if (c->h_io->err == 2) return set_err(FIBER_EARG, "token id out of range on the device");
+    if (c->h_io->err == 5)
+        return set_err(FIBER_EUNSUPPORTED,
+                       "an activation exceeded the fp16 fragment range of the persistent kernel; use decode mode 1");
     if (c->h_io->err == 4) {
         // a bounded wait gave up mid-step: merge tickets may be left non-zero
         cudaMemset(c->att_cnt, 0, (size_t)c->p.n_kv_heads * sizeof(unsigned int));
