@@ -15,6 +15,7 @@
 // into a CUDA graph and replayed for every token.
 #include <cuda_runtime.h>
 #include <math.h>
+#include <nccl.h>
 #include <stdarg.h>
 #include <stdio.h>
 #include <stdlib.h>
@@ -375,6 +376,13 @@ struct gpu_context {
     int pk_ring = 0, pk_xfr = 0, pk_xs = 0, pk_nw = 0, pk_grid = 0;
     size_t pk_smem = 0;
     void *pk_kernel = nullptr;
+    // tensor parallelism: this rank's share of query heads, KV heads and FFN blocks
+    // (the whole model when tp_world == 1)
+    int tp_rank = 0, tp_world = 1;
+    int nh_l = 0, nkv_l = 0, ffn_l = 0, h0 = 0, g0 = 0, f0b = 0;
+    float *x2 = nullptr;            // second residual buffer: Wo's all-reduced output
+    uint8_t *d_shard = nullptr;     // Wo / W_down shards along their input dimension
+    ncclComm_t comm = nullptr;
 };
 
 static void free_graph(Graph &g) {
@@ -389,7 +397,8 @@ extern "C" void fiber_cuda_free(fiber_ctx_t *c) {
     if (c->stream) cudaStreamSynchronize(c->stream);
     free_graph(c->g_step);
     free_graph(c->g_loop);
-    void *dev[] = {c->d_data, c->x, c->qkv, c->att, c->h, c->logits, c->rope, c->io, c->rec,
+    if (c->comm) ncclCommDestroy(c->comm);
+    void *dev[] = {c->x2, c->d_shard, c->d_data, c->x, c->qkv, c->att, c->h, c->logits, c->rope, c->io, c->rec,
                    c->att_part, c->att_cnt, c->am_part, c->am_cnt, c->d_phases, c->d_bar,
                    c->pk_gf[0], c->pk_gf[1], c->pk_gf[2], c->pk_gf[3], c->pk_ss[0], c->pk_ss[1]};
     for (void *p : dev)
@@ -596,7 +605,10 @@ static int pk_build(gpu_context *c) {
     return FIBER_OK;
 }
 
-static int ctx_init(gpu_context *c, const model_t *m, int device, int max_seq) {
+static int tp_setup(gpu_context *c, const model_t *m, int rank, int world, const uint8_t *nccl_id);
+
+static int ctx_init(gpu_context *c, const model_t *m, int device, int max_seq, int rank, int world,
+                    const uint8_t *nccl_id) {
     const model_params_t &p = m->params;
     c->device = device;
     c->p = p;
@@ -693,7 +705,127 @@ static int ctx_init(gpu_context *c, const model_t *m, int device, int max_seq) {
             tab[(size_t)pos * (hd / 2) + i] = make_float2(cosf(angle), sinf(angle));
         }
     CK(cudaMemcpy(c->rope, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice));
+    int rc = tp_setup(c, m, rank, world, nccl_id);
+    if (rc) return rc;
+    if (world > 1) {
+        c->mode = 1;  // sharded steps run the per-phase kernels with NCCL all-reduces
+        return FIBER_OK;
+    }
     return pk_build(c);
+}
+
+// ---- tensor parallelism ------------------------------------------------------------
+
+extern "C" int fiber_tp_plan(const model_params_t *p, int rank, int world, fiber_tp_plan_t *out) {
+    if (!p || !out) return set_err(FIBER_EARG, "fiber_tp_plan: null argument");
+    if (world < 1 || rank < 0 || rank >= world) return set_err(FIBER_EARG, "rank %d of world %d", rank, world);
+    const int nh = (int)p->n_heads, nkv = (int)p->n_kv_heads, hd = (int)p->head_dim, nblk = (int)p->ffn_dim / 256;
+    if (nh % world || nkv % world)
+        return set_err(FIBER_EUNSUPPORTED, "%d query / %d KV heads do not split over %d ranks", nh, nkv, world);
+    if ((nh / world) * hd % 256)
+        return set_err(FIBER_EUNSUPPORTED, "Wo shards of %d columns are not whole super-blocks", (nh / world) * hd);
+    if (p->ffn_dim % 256 || nblk < world)
+        return set_err(FIBER_EUNSUPPORTED, "ffn_dim %u does not split into %d shards of super-blocks", p->ffn_dim, world);
+    out->rank = rank;
+    out->world = world;
+    out->heads = nh / world;
+    out->head0 = rank * out->heads;
+    out->kv_heads = nkv / world;
+    out->kv_head0 = rank * out->kv_heads;
+    out->ffn_block0 = rank * nblk / world;
+    out->ffn_blocks = (rank + 1) * nblk / world - out->ffn_block0;
+    return FIBER_OK;
+}
+
+extern "C" int fiber_tp_unique_id(uint8_t out[FIBER_TP_ID_BYTES]) {
+    static_assert(sizeof(ncclUniqueId) == FIBER_TP_ID_BYTES, "ncclUniqueId size");
+    if (!out) return set_err(FIBER_EARG, "fiber_tp_unique_id: null argument");
+    ncclUniqueId id;
+    const ncclResult_t r = ncclGetUniqueId(&id);
+    if (r != ncclSuccess) return set_err(FIBER_ECUDA, "ncclGetUniqueId: %s", ncclGetErrorString(r));
+    memcpy(out, &id, sizeof(id));
+    return FIBER_OK;
+}
+
+// Shard the model for rank `rank`: row ranges of Wq/Wk/Wv and W_gate/W_up are
+// addressed in place in the uploaded GGUF data; Wo and W_down are cut along their
+// input dimension (whole super-blocks of every row) into d_shard; an NCCL
+// communicator joins the ranks.
+static int tp_setup(gpu_context *c, const model_t *m, int rank, int world, const uint8_t *nccl_id) {
+    const model_params_t &p = c->p;
+    fiber_tp_plan_t plan;
+    int rc = fiber_tp_plan(&p, rank, world, &plan);
+    if (rc) return rc;
+    const int dim = p.dim, hd = p.head_dim;
+    c->tp_rank = rank;
+    c->tp_world = world;
+    c->nh_l = plan.heads;
+    c->nkv_l = plan.kv_heads;
+    c->h0 = plan.head0;
+    c->g0 = plan.kv_head0;
+    c->f0b = plan.ffn_block0;
+    c->ffn_l = plan.ffn_blocks * 256;
+    if (world == 1) return FIBER_OK;
+    auto rb = [](int cols, int type) { return (size_t)(cols / 256) * block_bytes(type); };
+    const uint8_t *host = (const uint8_t *)m->gf->data + m->gf->data_offset;
+    size_t shard_bytes = 0;
+    for (uint32_t l = 0; l < p.n_layers; l++)
+        shard_bytes += (size_t)dim * (rb(c->nh_l * hd, c->L[l].to) + rb(c->ffn_l, c->L[l].t2));
+    CK(cudaMalloc(&c->d_shard, shard_bytes));
+    uint8_t *dst = c->d_shard;
+    for (uint32_t l = 0; l < p.n_layers; l++) {
+        LayerDev &d = c->L[l];
+        const layer_offsets_t &o = m->layer_off[l];
+        d.wq += (size_t)c->h0 * hd * rb(dim, d.tq);
+        d.wk += (size_t)c->g0 * hd * rb(dim, d.tk);
+        d.wv += (size_t)c->g0 * hd * rb(dim, d.tv);
+        d.w1 += (size_t)c->f0b * 256 * rb(dim, d.t1);
+        d.w3 += (size_t)c->f0b * 256 * rb(dim, d.t3);
+        const size_t wo_row = rb(dim, d.to), wo_cut = rb(c->nh_l * hd, d.to), wo_off = rb(c->h0 * hd, d.to);
+        CK(cudaMemcpy2D(dst, wo_cut, host + o.wo + wo_off, wo_row, wo_cut, dim, cudaMemcpyHostToDevice));
+        d.wo = dst;
+        dst += (size_t)dim * wo_cut;
+        const size_t w2_row = rb(p.ffn_dim, d.t2), w2_cut = rb(c->ffn_l, d.t2), w2_off = rb(c->f0b * 256, d.t2);
+        CK(cudaMemcpy2D(dst, w2_cut, host + o.w2 + w2_off, w2_row, w2_cut, dim, cudaMemcpyHostToDevice));
+        d.w2 = dst;
+        dst += (size_t)dim * w2_cut;
+    }
+    CK(cudaMalloc(&c->x2, (size_t)dim * 4));
+    CK(cudaMemset(c->x2, 0, (size_t)dim * 4));
+    ncclUniqueId id;
+    memcpy(&id, nccl_id, sizeof(id));
+    const ncclResult_t r = ncclCommInitRank(&c->comm, world, id, rank);
+    if (r != ncclSuccess) return set_err(FIBER_ECUDA, "ncclCommInitRank: %s", ncclGetErrorString(r));
+    return FIBER_OK;
+}
+
+extern "C" fiber_ctx_t *fiber_cuda_init_tp(const model_t *m, int device, int rank, int world,
+                                           const uint8_t nccl_id[FIBER_TP_ID_BYTES], int max_seq) {
+    if (!m || !m->layers || (world > 1 && !nccl_id)) {
+        set_err(FIBER_EARG, "fiber_cuda_init_tp: no model or no communicator id");
+        return nullptr;
+    }
+    if (max_seq <= 0) max_seq = (int)m->params.context_length;
+    gpu_context *c = new gpu_context();
+    if (ctx_init(c, m, device, max_seq, rank, world, nccl_id) != FIBER_OK) {
+        fprintf(stderr, "fiber_cuda_init_tp: %s\n", g_err);
+        fiber_cuda_free(c);
+        return nullptr;
+    }
+    return c;
+}
+
+extern "C" int fiber_tp_info(fiber_ctx_t *c, fiber_tp_plan_t *out) {
+    if (!c || !out) return set_err(FIBER_EARG, "fiber_tp_info: null argument");
+    out->rank = c->tp_rank;
+    out->world = c->tp_world;
+    out->heads = c->nh_l;
+    out->head0 = c->h0;
+    out->kv_heads = c->nkv_l;
+    out->kv_head0 = c->g0;
+    out->ffn_block0 = c->f0b;
+    out->ffn_blocks = c->ffn_l / 256;
+    return FIBER_OK;
 }
 
 extern "C" fiber_ctx_t *fiber_cuda_init(const model_t *m, int device, int max_batch, int max_seq) {
@@ -707,7 +839,7 @@ extern "C" fiber_ctx_t *fiber_cuda_init(const model_t *m, int device, int max_ba
     }
     if (max_seq <= 0) max_seq = (int)m->params.context_length;
     gpu_context *c = new gpu_context();
-    if (ctx_init(c, m, device, max_seq) != FIBER_OK) {
+    if (ctx_init(c, m, device, max_seq, 0, 1, nullptr) != FIBER_OK) {
         fprintf(stderr, "fiber_cuda_init: %s\n", g_err);
         fiber_cuda_free(c);
         return nullptr;
@@ -718,7 +850,7 @@ extern "C" fiber_ctx_t *fiber_cuda_init(const model_t *m, int device, int max_ba
 // ---- the decode step ------------------------------------------------------------------
 
 static cudaError_t enqueue_qkv(gpu_context *c, const LayerDev &d, cudaStream_t st) {
-    const int dim = c->p.dim, kvd = c->kvd;
+    const int dim = c->p.dim, qd = c->nh_l * (int)c->p.head_dim, kvd = c->nkv_l * (int)c->p.head_dim;
     GemvParams p;
     memset(&p, 0, sizeof(p));
     p.cols = dim;
@@ -727,7 +859,7 @@ static cudaError_t enqueue_qkv(gpu_context *c, const LayerDev &d, cudaStream_t s
     p.eps = c->p.rms_norm_eps;
     p.y = c->qkv;
     const uint8_t *ws[3] = {d.wq, d.wk, d.wv};
-    const int ts[3] = {d.tq, d.tk, d.tv}, rows[3] = {dim, kvd, kvd}, offs[3] = {0, dim, dim + kvd};
+    const int ts[3] = {d.tq, d.tk, d.tv}, rows[3] = {qd, kvd, kvd}, offs[3] = {0, qd, qd + kvd};
     // group consecutive segments sharing a type into one launch
     int s = 0;
     while (s < 3) {
@@ -808,8 +940,8 @@ static AttnParams attn_params(gpu_context *c, const kv_cache_t *kv) {
     a.count = c->att_cnt;
     a.out = c->att;
     a.n_layers = p.n_layers;
-    a.n_kv = p.n_kv_heads;
-    a.n_heads = p.n_heads;
+    a.n_kv = c->nkv_l;
+    a.n_heads = c->nh_l;
     a.max_chunks = c->max_chunks;
     a.max_seq = c->max_seq < kv->max_seq ? c->max_seq : kv->max_seq;
     a.scale = 1.0f / sqrtf((float)p.head_dim);
@@ -831,24 +963,28 @@ static cudaError_t enqueue_kind(gpu_context *c, const kv_cache_t *kv, int kind, 
         return launch_attn(c, a, st);
     }
     case 2: {
-        GemvParams wo = one_seg(d.wo, d.to, dim, 0, dim);
+        // TP: each rank's partial product over its heads goes to x2 (rank 0 adds the
+        // residual) and is all-reduced by the caller; otherwise in place on x
+        GemvParams wo = one_seg(d.wo, d.to, dim, 0, c->nh_l * (int)p.head_dim);
         wo.x = c->att;
-        wo.resid = c->x;
+        wo.resid = c->tp_world > 1 && c->tp_rank > 0 ? nullptr : c->x;
+        wo.y = c->tp_world > 1 ? c->x2 : nullptr;
         return launch_gemv<EPI_RESID>(d.to, wo, grid_of(wo), st);
     }
     case 3: {
-        GemvParams up = one_seg(d.w1, d.t1, ffn, 0, dim);
+        GemvParams up = one_seg(d.w1, d.t1, c->ffn_l, 0, dim);
         up.w_up = d.w3;
-        up.x = c->x;
+        up.x = c->tp_world > 1 ? c->x2 : c->x;
         up.norm_w = d.ffn_norm;
         up.eps = p.rms_norm_eps;
         up.y = c->h;
         return launch_gemv<EPI_SWIGLU>(d.t1, up, grid_of(up), st);
     }
     case 4: {
-        GemvParams dn = one_seg(d.w2, d.t2, dim, 0, ffn);
+        GemvParams dn = one_seg(d.w2, d.t2, dim, 0, c->ffn_l);
         dn.x = c->h;
-        dn.resid = c->x;
+        dn.resid = c->tp_world > 1 ? (c->tp_rank > 0 ? nullptr : c->x2) : c->x;
+        dn.y = c->tp_world > 1 ? c->x : nullptr;
         return launch_gemv<EPI_RESID>(d.t2, dn, grid_of(dn), st);
     }
     case 5: return enqueue_lm_head(c, loop, st);
@@ -906,7 +1042,15 @@ static cudaError_t enqueue_step(gpu_context *c, const kv_cache_t *kv, bool loop,
     if (c->mode == 0 && c->pk_ok) return enqueue_persistent(c, kv, loop, st);
     cudaError_t e = enqueue_kind(c, kv, 6, 0, loop, st);
     for (uint32_t l = 0; l < c->p.n_layers && e == cudaSuccess; l++)
-        for (int kind = 0; kind <= 4 && e == cudaSuccess; kind++) e = enqueue_kind(c, kv, kind, (int)l, loop, st);
+        for (int kind = 0; kind <= 4 && e == cudaSuccess; kind++) {
+            e = enqueue_kind(c, kv, kind, (int)l, loop, st);
+            if (e == cudaSuccess && c->tp_world > 1 && (kind == 2 || kind == 4)) {
+                // sum of the ranks' partial products (+ residual from rank 0)
+                float *buf = kind == 2 ? c->x2 : c->x;
+                if (ncclAllReduce(buf, buf, c->p.dim, ncclFloat, ncclSum, c->comm, st) != ncclSuccess)
+                    e = cudaErrorUnknown;
+            }
+        }
     if (e == cudaSuccess) e = enqueue_lm_head(c, loop, st);
     return e;
 }
@@ -949,7 +1093,7 @@ static int run_step(gpu_context *c, const kv_cache_t *kv, bool loop) {
 
 static int check_kv(gpu_context *c, const kv_cache_t *kv) {
     if (!kv) return set_err(FIBER_EARG, "no KV cache");
-    if (kv->device != c->device || kv->n_layers != (int)c->p.n_layers || kv->n_kv_heads != (int)c->p.n_kv_heads ||
+    if (kv->device != c->device || kv->n_layers != (int)c->p.n_layers || kv->n_kv_heads != c->nkv_l ||
         kv->head_dim != (int)c->p.head_dim || kv->page_size != ATTN_P)
         return set_err(FIBER_EARG, "KV cache does not match the model/device");
     return FIBER_OK;

@@ -212,7 +212,7 @@ struct GemvParams {
     const float *norm_w;
     float eps;
     float *y;                 // STORE: y[out_off + r]; SWIGLU: y[r]; ARGMAX: logits
-    float *resid;             // RESID: resid[r] += acc
+    float *resid;             // RESID: resid[r] += acc (y null), or y[r] = resid[r] + acc (resid may be null)
     const uint8_t *w_up;      // SWIGLU: up matrix (same type as seg[0])
     // ARGMAX scratch and outputs
     float2 *am_part;          // [gridDim.x] (value, index bits)
@@ -265,7 +265,11 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(const GemvParams p) 
                 p.y[r] = __fmul_rn(sg_, up);
             }
         } else if constexpr (EPI == EPI_RESID) {
-            if (lane == 0) p.resid[r] = __fadd_rn(p.resid[r], acc);
+            if (lane == 0) {
+                // in place (y null): resid[r] += acc; out of place: y[r] = (resid ? resid[r] : 0) + acc
+                float *dst = p.y ? p.y : p.resid;
+                dst[r] = p.resid ? __fadd_rn(p.resid[r], acc) : acc;
+            }
         } else if constexpr (EPI == EPI_ARGMAX) {
             if (lane == 0) p.y[r] = acc;
             if (better(acc, r, best_v, best_i)) {

@@ -527,7 +527,7 @@ __global__ void __launch_bounds__(TC_THREADS) gemv_tc_kernel(const TcParams p) {
     pdl_wait();
     float resid_in = 0.f;
     if constexpr (EPI == EPI_RESID) {
-        if (my_tiles == 1 && tid < TC_M) {
+        if (p.resid && my_tiles == 1 && tid < TC_M) {
             int sg0, lt0;
             locate(p, (int)blockIdx.x, sg0, lt0);
             const int r = lt0 * TC_M + tid;
@@ -590,7 +590,9 @@ __global__ void __launch_bounds__(TC_THREADS) gemv_tc_kernel(const TcParams p) {
                 if constexpr (EPI == EPI_STORE) {
                     p.y[p.seg[sg].out_off + r] = v[0];
                 } else if constexpr (EPI == EPI_RESID) {
-                    p.resid[r] = __fadd_rn(my_tiles == 1 ? resid_in : __ldcg(p.resid + r), v[0]);
+                    // in place (y null): resid[r] += v; out of place: y[r] = (resid ? resid[r] : 0) + v
+                    float *dst = p.y ? p.y : p.resid;
+                    dst[r] = p.resid ? __fadd_rn(my_tiles == 1 ? resid_in : __ldcg(p.resid + r), v[0]) : v[0];
                 } else if constexpr (EPI == EPI_SWIGLU) {
                     const float gt = v[0];
                     p.y[r] = __fmul_rn(__fdiv_rn(gt, __fadd_rn(1.0f, expf(-gt))), v[NMAT - 1]);

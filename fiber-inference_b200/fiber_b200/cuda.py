@@ -14,7 +14,7 @@ import numpy as np
 from . import CUDA_SO, ModelParams  # noqa: F401
 
 __all__ = ["FiberError", "cuda_lib", "cuda_available", "gemv", "gemv_host", "gemv_argmax_noalloc", "dequant", "Context", "KVCache",
-           "device_count"]
+           "device_count", "TPPlan", "TP_ID_BYTES", "tp_plan", "tp_unique_id"]
 
 F32P = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
 I32P = np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS")
@@ -22,7 +22,8 @@ I32P = np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS")
 EXPORTED = [
     "fiber_last_error", "fiber_device_count", "fiber_cuda_init", "fiber_cuda_free", "fiber_forward_token",
     "fiber_prefill", "fiber_decode_greedy", "fiber_step_launches", "fiber_set_decode_mode",
-    "fiber_get_decode_mode", "fiber_trace_step", "fiber_time_kernel", "fiber_gemv",
+    "fiber_get_decode_mode", "fiber_trace_step", "fiber_time_kernel", "fiber_gemv", "fiber_tp_plan",
+    "fiber_tp_unique_id", "fiber_cuda_init_tp", "fiber_tp_info",
     "fiber_dequant", "fiber_gemv_host", "gpu_init", "gpu_free", "gpu_embed", "gpu_forward_token",
     "gpu_get_logits", "gpu_forward_classifier", "gpu_get_device", "kv_cache_init", "kv_cache_init_paged",
     "kv_cache_free", "kv_cache_write", "kv_cache_read", "fiber_gemv_argmax_noalloc",
@@ -31,6 +32,14 @@ EXPORTED = [
 
 class FiberError(RuntimeError):
     pass
+
+
+class TPPlan(C.Structure):
+    _fields_ = [("rank", C.c_int), ("world", C.c_int), ("heads", C.c_int), ("head0", C.c_int),
+                ("kv_heads", C.c_int), ("kv_head0", C.c_int), ("ffn_block0", C.c_int), ("ffn_blocks", C.c_int)]
+
+
+TP_ID_BYTES = 128
 
 
 class KVCacheT(C.Structure):
@@ -61,6 +70,11 @@ def cuda_lib() -> C.CDLL:
         L.fiber_step_launches.argtypes = [C.c_void_p]
         L.fiber_set_decode_mode.argtypes = [C.c_void_p, C.c_int]
         L.fiber_get_decode_mode.argtypes = [C.c_void_p]
+        L.fiber_tp_plan.argtypes = [C.c_void_p, C.c_int, C.c_int, C.POINTER(TPPlan)]
+        L.fiber_tp_unique_id.argtypes = [C.c_void_p]
+        L.fiber_cuda_init_tp.restype = C.c_void_p
+        L.fiber_cuda_init_tp.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_int]
+        L.fiber_tp_info.argtypes = [C.c_void_p, C.POINTER(TPPlan)]
         L.fiber_trace_step.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_size_t,
                                        C.POINTER(C.c_int), C.POINTER(C.c_int)]
         L.fiber_time_kernel.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.POINTER(C.c_double),
@@ -167,17 +181,38 @@ class KVCache:
         return k, v
 
 
-class Context:
-    """fiber_cuda_init over a host model (fiber_b200.HostModel)."""
+def tp_plan(params, rank: int, world: int) -> TPPlan:
+    """fiber_tp_plan: this rank's heads / KV heads / FFN blocks (host only, no GPU)."""
+    out = TPPlan()
+    _check(cuda_lib().fiber_tp_plan(C.byref(params), rank, world, C.byref(out)), "fiber_tp_plan")
+    return out
 
-    def __init__(self, host_model, device: int = 0, max_seq: int = 0):
+
+def tp_unique_id() -> bytes:
+    buf = (C.c_uint8 * TP_ID_BYTES)()
+    _check(cuda_lib().fiber_tp_unique_id(buf), "fiber_tp_unique_id")
+    return bytes(buf)
+
+
+class Context:
+    """fiber_cuda_init over a host model (fiber_b200.HostModel); with tp=(rank, world,
+    id bytes) a tensor-parallel context (fiber_cuda_init_tp)."""
+
+    def __init__(self, host_model, device: int = 0, max_seq: int = 0, tp=None):
         self.model = host_model
         self.p = host_model.params
-        self.h = cuda_lib().fiber_cuda_init(host_model.h, device, 1, max_seq)
+        if tp is None:
+            self.h = cuda_lib().fiber_cuda_init(host_model.h, device, 1, max_seq)
+        else:
+            rank, world, nid = tp
+            idbuf = (C.c_uint8 * TP_ID_BYTES).from_buffer_copy(nid)
+            self.h = cuda_lib().fiber_cuda_init_tp(host_model.h, device, rank, world, idbuf, max_seq)
         if not self.h:
             raise FiberError(f"fiber_cuda_init: {cuda_lib().fiber_last_error().decode()}")
         self.device = device
         self.max_seq = max_seq or self.p.context_length
+        self.plan = TPPlan()
+        _check(cuda_lib().fiber_tp_info(self.h, C.byref(self.plan)), "fiber_tp_info")
 
     def close(self):
         if self.h:
@@ -187,7 +222,7 @@ class Context:
     __del__ = close
 
     def kv(self, max_seq: int | None = None) -> KVCache:
-        return KVCache(self.device, self.p.n_layers, self.p.n_kv_heads, self.p.head_dim, max_seq or self.max_seq)
+        return KVCache(self.device, self.p.n_layers, self.plan.kv_heads, self.p.head_dim, max_seq or self.max_seq)
 
     def forward(self, kv: KVCache, token: int, pos: int, want_logits: bool = True):
         lg = np.empty(self.p.vocab_size, np.float32) if want_logits else None

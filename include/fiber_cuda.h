@@ -80,6 +80,41 @@ int fiber_get_decode_mode(fiber_ctx_t *ctx);
 /* Number of kernels one decode step launches (all of them this library's own). */
 int fiber_step_launches(fiber_ctx_t *ctx);
 
+/* ---- tensor parallelism (one process per GPU) ------------------------------------ */
+
+#define FIBER_TP_ID_BYTES 128
+
+/* This rank's share of the model: query heads [head0, head0 + heads), KV heads
+ * [kv_head0, kv_head0 + kv_heads), FFN blocks of 256 [ffn_block0, + ffn_blocks). */
+typedef struct {
+    int rank, world;
+    int heads, head0;
+    int kv_heads, kv_head0;
+    int ffn_block0, ffn_blocks;
+} fiber_tp_plan_t;
+
+/* Pure host computation of the split (no GPU): heads and KV heads evenly, FFN
+ * super-blocks as evenly as whole blocks allow; FIBER_EUNSUPPORTED when the model
+ * does not split over `world` (Wo shards must be whole super-blocks). */
+int fiber_tp_plan(const model_params_t *p, int rank, int world, fiber_tp_plan_t *out);
+
+/* Communicator id for fiber_cuda_init_tp, made on rank 0 and passed to every rank
+ * by the caller (FIBER_TP_ID_BYTES bytes). */
+int fiber_tp_unique_id(uint8_t out[FIBER_TP_ID_BYTES]);
+
+/* Tensor-parallel context for rank `rank` of `world` on CUDA device `device`
+ * (replaces the reference's single-device gpu_init for the sharded 7B/13B
+ * decode): Wq/Wk/Wv and W_gate/W_up split by rows (heads, FFN blocks), Wo and
+ * W_down split along their input dimension at super-block granularity; the
+ * embedding, norms and lm_head are replicated. Every decode step all-reduces
+ * (NCCL, sum) the dim-vector after Wo and after W_down inside the step graph, so
+ * every rank holds the same residual stream and the same greedy token. Must be
+ * called by all ranks together. The KV cache holds this rank's KV heads
+ * (fiber_tp_info). Steps run the per-phase kernels (decode mode 1). */
+fiber_ctx_t *fiber_cuda_init_tp(const model_t *m, int device, int rank, int world,
+                                const uint8_t nccl_id[FIBER_TP_ID_BYTES], int max_seq);
+int fiber_tp_info(fiber_ctx_t *ctx, fiber_tp_plan_t *out);
+
 /* Timeline of one persistent decode step (mode 0): runs the step for `token` at
  * `pos` and fills out[n_phases][n_ctas][10] (uint64) with, per phase and CTA:
  * 0 globaltimer ns when the phase's grid barrier released the CTA, 1 SM cycles

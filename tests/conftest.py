@@ -51,6 +51,10 @@ TINY_MODELS = {
                  seed=15, context_length=1024),
     "hd128": dict(dim=512, n_layers=2, n_heads=4, n_kv_heads=4, ffn_dim=768, vocab=900, recipe="Q4_K_M", seed=16,
                   context_length=512),
+    # splits over 2 ranks: 4 query / 2 KV heads and 2 of 4 FFN super-blocks each; Q4_K_M puts
+    # Q6_K on attn_v / ffn_down of layer 0, so both shard paths (144- and 210-byte blocks) run
+    "tp": dict(dim=512, n_layers=3, n_heads=8, n_kv_heads=4, ffn_dim=1024, vocab=1100, recipe="Q4_K_M", seed=17,
+               context_length=512),
 }
 
 

@@ -1,0 +1,78 @@
+"""Tensor-parallel decode on two GPUs (one process per GPU, NCCL all-reduce after
+Wo and W_down): both ranks produce the oracle's greedy tokens, and teacher-forced
+logits stay within the decode tolerances. Skipped with fewer than two GPUs."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+import fiber_b200 as fb
+from oracle import oracle as orc
+
+pytestmark = pytest.mark.gpu
+
+MAX_ABS, REL_RMS = 2e-2, 1e-3
+
+
+def _worker(rank, world, nid, path, prompt, n_gen, q):
+    try:
+        hm = fb.HostModel(path)
+        ctx = fb.Context(hm, device=rank, max_seq=256, tp=(rank, world, nid))
+        kv = ctx.kv(256)
+        logits = []
+        for pos, t in enumerate(prompt[:6]):  # teacher-forced, every rank in lockstep
+            _, lg = ctx.forward(kv, int(t), pos)
+            logits.append(lg)
+        kv2 = ctx.kv(256)
+        first = ctx.prefill(kv2, np.asarray(prompt, np.int32))
+        toks, _ = ctx.decode_greedy(kv2, first, len(prompt), n_gen)
+        plan = ctx.plan
+        q.put((rank, first, toks.tolist(), np.stack(logits), (plan.heads, plan.kv_heads, plan.ffn_blocks), None))
+        ctx.close()
+    except Exception as e:  # report instead of hanging the parent
+        q.put((rank, None, None, None, None, repr(e)))
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_tp2_matches_oracle(tiny_model):
+    path = tiny_model("tp")
+    hm = fb.HostModel(path)
+    p = hm.params
+    rng = np.random.default_rng(5)
+    prompt = rng.integers(1, p.vocab_size, 12).astype(np.int32)
+    n_gen = 60
+    nid = fb.tp_unique_id()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_worker, args=(r, 2, nid, path, prompt, n_gen, q)) for r in range(2)]
+    for pr in procs:
+        pr.start()
+    res = {}
+    try:
+        for _ in range(2):
+            r = q.get(timeout=300)
+            res[r[0]] = r
+    finally:
+        for pr in procs:
+            pr.join(timeout=60)
+            if pr.is_alive():
+                pr.kill()
+    for r in (0, 1):
+        assert res[r][5] is None, res[r][5]
+    assert res[0][4] == (4, 2, 2) and res[1][4] == (4, 2, 2)
+
+    om = orc.Model(path)
+    st = om.state(256, kv_fp16=True)
+    want_lg = np.stack([st.forward(int(t), pos) for pos, t in enumerate(prompt[:6])])
+    for r in (0, 1):
+        lg = res[r][3]
+        assert np.abs(lg - want_lg).max() < MAX_ABS
+        err = np.sqrt(np.mean((lg.astype(np.float64) - want_lg) ** 2) / np.mean(want_lg.astype(np.float64) ** 2))
+        assert err < REL_RMS
+    st2 = om.state(256, kv_fp16=True)
+    want = st2.generate(prompt, n_gen)
+    for r in (0, 1):
+        assert res[r][1] == want[0]
+        assert res[r][2] == want[1:].tolist()
