@@ -205,6 +205,79 @@ def run_reference(args, rank: int, world: int):
     print(json.dumps(line), flush=True)
 
 
+MODEL_7B = "/tmp/fiber_bench_llama7b_q4km.gguf"
+# Q4_K_M 7B: 32 layers x (Q4_K 113,836,032 B or Q6_K-recipe 129,785,856 B) + Q6_K output 107,520,000 B
+WEIGHTS_7B = 16 * 113_836_032 + 16 * 129_785_856 + 107_520_000 + 32 * 2 * 16_384 + 16_384 + 2_304
+
+
+def run_7b_tp(args, fb, torch, dist, rank, world, local):
+    """Config 5: 7B Q4_K_M (dim 4096, 32 layers, 32 heads, hd 128, ffn 11008) batch-1 greedy
+    decode, tensor-parallel over the N ranks (one process per GPU; NCCL all-reduce after Wo
+    and W_down inside each step's graph). Total work is fixed: scaling is strong."""
+    # config 5: 512-token prompt, 256 decode steps (shorter only when asked for)
+    P = 512 if args.prompt_len == PROMPT_LEN else args.prompt_len
+    D = 256 if args.decode_len == DECODE_LEN else args.decode_len
+    if rank == 0 and not os.path.exists(MODEL_7B):
+        fb.write_model(MODEL_7B + ".tmp", fb.synth_cfg("llama7b"))
+        os.replace(MODEL_7B + ".tmp", MODEL_7B)
+    box = [fb.tp_unique_id() if rank == 0 else None]
+    if dist is not None:
+        dist.barrier()
+        dist.broadcast_object_list(box, src=0)
+    hm = fb.HostModel(MODEL_7B)
+    ctx = fb.Context(hm, device=local, max_seq=P + D, tp=(rank, world, box[0]))
+    kv = ctx.kv(P + D)
+    prompt = prompt_ids(hm.params.vocab_size)[:P]
+    t0 = time.perf_counter()
+    first = ctx.prefill(kv, prompt)
+    prefill_tps = P / (time.perf_counter() - t0)
+    for _ in range(args.warmup):
+        ctx.decode_greedy(kv, first, P, D)
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize(local)
+    ms_total, toks0 = 0.0, None
+    with Clocks(local) as clk:
+        for _ in range(args.steps):
+            toks, ms = ctx.decode_greedy(kv, first, P, D)
+            ms_total += ms
+            toks0 = toks if toks0 is None else toks0
+    if dist is not None:
+        t = torch.tensor([ms_total], device=f"cuda:{local}", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_total = float(t.item())
+        h = torch.tensor([int(np.sum(toks0.astype(np.int64) * np.arange(1, D + 1)))], device=f"cuda:{local}")
+        hs = [torch.zeros_like(h) for _ in range(world)]
+        dist.all_gather(hs, h)
+        same = all(int(x.item()) == int(h.item()) for x in hs)
+    else:
+        same = True
+    value = args.steps * D / (ms_total / 1e3)
+    peak, peak_kind = peaks()
+    kv_bytes = 524_288 * (P + D / 2)  # mean KV read per token over the decode positions
+    bytes_tok = WEIGHTS_7B + kv_bytes
+    if rank == 0:
+        line = {"metric": "decode tok/s (7B Q4_K_M, bs=1, tensor-parallel)", "value": value, "unit": "tok/s",
+                "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_total / args.steps,
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+                "data": "synthetic (seeded random-init weights, seeded prompt ids)",
+                "config": {"workload": "7B Q4_K_M (Llama-2-7B shape) batch-1 greedy decode, tensor-parallel",
+                           "model": "dim 4096, 32 layers, 32/32 heads, hd 128, ffn 11008, vocab 32000, Q4_K_M",
+                           "prompt": P, "decode_tokens_per_step": D, "global_batch": 1,
+                           "parallelism": f"tp{world}", "step_mode": "one kernel per phase + NCCL all-reduce",
+                           "tokens_identical_on_all_ranks": same, "prefill_tok_s": prefill_tps},
+                "roofline": {"bound": "hbm", "achieved": bytes_tok * value / world / 1e9, "peak": peak, "unit": "GB/s",
+                             "frac": bytes_tok * value / world / 1e9 / peak, "peak_source": peak_kind,
+                             "traffic": None, "algorithmic_bytes_per_token": bytes_tok,
+                             "note": "per GPU: weights and KV of the whole model divided over the ranks"},
+                "gpu_launches": ctx.step_launches() * D * args.steps, "clocks": clk.summary()}
+        print(json.dumps(line), flush=True)
+    ctx.close()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -218,6 +291,9 @@ def main():
     ap.add_argument("--skip-extras", action="store_true", help="no single-GEMV, e2e or CPU legs (profiling)")
     ap.add_argument("--step-mode", type=int, default=None, choices=[0, 1],
                     help="0: one persistent kernel per token (default when the model fits it); 1: one kernel per phase")
+    ap.add_argument("--workload", default="1.1b", choices=["1.1b", "7b-tp"],
+                    help="1.1b: the headline 1.1B Q4_K_M decode (replicas for N>1); "
+                         "7b-tp: 7B Q4_K_M decode tensor-parallel over the N GPUs")
     args = ap.parse_args()
 
     rank = int(os.environ.get("RANK", "0"))
@@ -238,6 +314,8 @@ def main():
         import torch.distributed as dist
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+    if args.workload == "7b-tp":
+        return run_7b_tp(args, fb, torch, dist, rank, world, local)
 
     def barrier():
         if dist is not None:
