@@ -278,6 +278,76 @@ def run_7b_tp(args, fb, torch, dist, rank, world, local):
         dist.destroy_process_group()
 
 
+def run_config(args, fb, torch, dist, rank, world, local):
+    """Configs 2 and 4 (batch 1, one replica per rank): the fp16 stories-shaped model with a
+    32-token prompt and 256 greedy steps; the 1.1B Q5_K_M model decoding 256 steps after its
+    KV cache was pre-filled with seeded N(0,1) fp16 keys/values for 2048 positions."""
+    if args.workload == "stories":
+        path, preset, P, D = "/tmp/fiber_bench_stories_f16.gguf", "stories", 32, 256
+    else:
+        path, preset, P, D = "/tmp/fiber_bench_tinyllama_q5km.gguf", "tinyllama-q5", 2048, 256
+    if args.decode_len != DECODE_LEN:
+        D = args.decode_len
+    if not os.path.exists(path):
+        tmp = path + f".{os.getpid()}.tmp"
+        fb.write_model(tmp, fb.synth_cfg(preset, seed=SEED))
+        os.replace(tmp, path)
+    hm = fb.HostModel(path)
+    p = hm.params
+    ctx = fb.Context(hm, device=local, max_seq=P + D)
+    kv = ctx.kv(P + D)
+    kvd = p.n_kv_heads * p.head_dim
+    if args.workload == "stories":
+        first = ctx.prefill(kv, prompt_ids(p.vocab_size)[:P])
+    else:
+        for layer in range(p.n_layers):
+            kv.write(layer, 0, fb.randn(P * kvd, seed=100 + layer).reshape(P, kvd),
+                     fb.randn(P * kvd, seed=200 + layer).reshape(P, kvd))
+        first = 5
+    for _ in range(args.warmup):
+        ctx.decode_greedy(kv, first, P, D)
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize(local)
+    ms_total = 0.0
+    with Clocks(local) as clk:
+        for _ in range(args.steps):
+            _, ms = ctx.decode_greedy(kv, first, P, D)
+            ms_total += ms
+    if dist is not None:
+        t = torch.tensor([ms_total], device=f"cuda:{local}", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_total = float(t.item())
+    value = world * args.steps * D / (ms_total / 1e3)
+    mid = P + D // 2
+    step_bytes = 0.0
+    for kind in range(7):
+        _, b = ctx.time_kernel(kv, kind, mid, reps=2)
+        step_bytes += b * (1 if kind >= 5 else p.n_layers)
+    peak, peak_kind = peaks()
+    if rank == 0:
+        name = {"stories": "stories fp16 (dim 768, 12 layers, 12 heads, ffn 2048, vocab 32000, tied)",
+                "q5km-long": "1.1B Q5_K_M (TinyLlama shape), KV pre-filled to 2048 positions"}[args.workload]
+        line = {"metric": f"decode tok/s ({args.workload}, bs=1)", "value": value, "unit": "tok/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_total / args.steps,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "f32" if args.workload != "stories" else "f16 weights, f32 activations",
+                "data": "synthetic (seeded random-init weights; seeded prompt ids or seeded N(0,1) KV)",
+                "config": {"workload": name, "context": P, "decode_tokens_per_step": D, "global_batch": 1,
+                           "parallelism": f"replicas x{world}",
+                           "step_mode": "persistent kernel per token" if ctx.mode == 0 else "one kernel per phase"},
+                "roofline": {"bound": "hbm", "achieved": step_bytes * value / world / 1e9, "peak": peak,
+                             "unit": "GB/s", "frac": step_bytes * value / world / 1e9 / peak,
+                             "peak_source": peak_kind, "traffic": None,
+                             "algorithmic_bytes_per_token": step_bytes, "kv_position": mid},
+                "gpu_launches": ctx.step_launches() * D * args.steps, "clocks": clk.summary()}
+        print(json.dumps(line), flush=True)
+    ctx.close()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -291,9 +361,11 @@ def main():
     ap.add_argument("--skip-extras", action="store_true", help="no single-GEMV, e2e or CPU legs (profiling)")
     ap.add_argument("--step-mode", type=int, default=None, choices=[0, 1],
                     help="0: one persistent kernel per token (default when the model fits it); 1: one kernel per phase")
-    ap.add_argument("--workload", default="1.1b", choices=["1.1b", "7b-tp"],
+    ap.add_argument("--workload", default="1.1b", choices=["1.1b", "7b-tp", "stories", "q5km-long"],
                     help="1.1b: the headline 1.1B Q4_K_M decode (replicas for N>1); "
-                         "7b-tp: 7B Q4_K_M decode tensor-parallel over the N GPUs")
+                         "7b-tp: 7B Q4_K_M decode tensor-parallel over the N GPUs; "
+                         "stories: fp16 stories-shaped model (dim 768, 12 layers), 32-token prompt, 256 steps; "
+                         "q5km-long: 1.1B Q5_K_M with the KV cache pre-filled to 2048 positions, 256 steps")
     args = ap.parse_args()
 
     rank = int(os.environ.get("RANK", "0"))
@@ -316,6 +388,8 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
     if args.workload == "7b-tp":
         return run_7b_tp(args, fb, torch, dist, rank, world, local)
+    if args.workload in ("stories", "q5km-long"):
+        return run_config(args, fb, torch, dist, rank, world, local)
 
     def barrier():
         if dist is not None:

@@ -44,7 +44,7 @@ constexpr long long PK_SPIN_LIMIT = 1ll << 22;  // grid-barrier polls (with ~100
 //  3 cycles in the tile loop (or attention units)   4 of those waiting for tiles to land
 //  5 cycles from the end of the tile loop to the arrive
 //  6 producer: globaltimer (ns) after issuing the phase's last tile   7 producer: cycles waiting for ring space
-//  8 of field 2: cycles until the input statistics are reduced   9 of field 2: cycles staging the fragments
+//  8, 9 attention: cycles until q/k/v are staged, cycles of the page loop (first head of the CTA)
 constexpr int PK_TRACE_FIELDS = 10;
 
 enum : int { PH_QKV = 0, PH_ATTN = 1, PH_RESID = 2, PH_SWIGLU = 3, PH_LM = 4 };
@@ -364,7 +364,9 @@ FDEV void pk_dot(const uint8_t *buf, int stride, const uint2 *xf, int nb) {
 // (lanes over positions, each lane starting at a rotated word so the reads of
 // the dense page are free of bank conflicts). Returns false when the step stopped.
 template <int HD, int G>
-FDEV bool pk_attn_head(const PParams &P, const PPhase &F, int h, int pos, int nch, int &seq, long long &wfull) {
+FDEV bool pk_attn_head(const PParams &P, const PPhase &F, int h, int pos, int nch, int &seq, long long &wfull,
+                       unsigned long long *tr) {
+    const long long c0 = clock64();
     constexpr int PG = ATTN_P;
     constexpr int W = HD / 2;    // 32-bit words of a K/V row
     constexpr int DPL = HD / 32;  // head dims per lane in P.V
@@ -403,6 +405,7 @@ FDEV bool pk_attn_head(const PParams &P, const PPhase &F, int h, int pos, int nc
         if (writer) a.v_pool[base + (size_t)tn * HD + j] = h16;
     }
     cbar();  // qs, nk, nv ready
+    const long long c1 = clock64();
 
     float m_run = -INFINITY, l_run = 0.f, o_run[DPL];
 #pragma unroll
@@ -498,7 +501,7 @@ FDEV bool pk_attn_head(const PParams &P, const PPhase &F, int h, int pos, int nc
             m_run = M;
         }
     }
-    // warp results -> shared memory, merged in warp order
+    // warp results -> shared memory, merged in warp order (trace: 8 = q/k/v ready, 9 = page loop)
     float *wr = wm + warp * (HD + 2);
 #pragma unroll
     for (int j = 0; j < DPL; j++) wr[2 + lane + 32 * j] = o_run[j];
@@ -508,6 +511,10 @@ FDEV bool pk_attn_head(const PParams &P, const PPhase &F, int h, int pos, int nc
     }
     cbar();
     if (tid == 0) pk_stop = pk_abort;
+    if (tr) {
+        tr[8] = (unsigned long long)(c1 - c0);
+        tr[9] = (unsigned long long)(clock64() - c1);
+    }
     seq += nch;
     bool ok = true;
     for (int dd = tid; dd < HD; dd += PK_CONSUMERS) {
@@ -533,13 +540,13 @@ FDEV bool pk_attn_head(const PParams &P, const PPhase &F, int h, int pos, int nc
 // Attention phase: this CTA's query heads. Returns false when stopped.
 template <int HD, int G>
 __device__ __noinline__ bool pk_attn_phase(const PParams &P, const PPhase &F, int pos, int nch, int &seq,
-                                           long long &wfull) {
+                                           long long &wfull, unsigned long long *tr) {
     if (pos < 0 || pos >= P.attn.max_seq) {
         if (threadIdx.x == 0 && blockIdx.x == 0) *P.io_err = 1;
         return true;
     }
     for (int h = blockIdx.x; h < P.attn.n_heads; h += gridDim.x)
-        if (!pk_attn_head<HD, G>(P, F, h, pos, nch, seq, wfull)) return false;
+        if (!pk_attn_head<HD, G>(P, F, h, pos, nch, seq, wfull, h == (int)blockIdx.x ? tr : nullptr)) return false;
     return true;
 }
 
@@ -946,7 +953,7 @@ __global__ void __launch_bounds__(PK_THREADS, 1) decode_persistent_kernel(const 
             if (!pk_grid_wait(P, ph)) break;
             T.put(0, gtimer());
             T.mark(1);
-            if (F.kind == PH_ATTN) ok = pk_attn_phase<HD, G>(P, F, pos, nch, seq, wfull);
+            if (F.kind == PH_ATTN) ok = pk_attn_phase<HD, G>(P, F, pos, nch, seq, wfull, T.tr);
         }
         if (!ok) break;
         T.mark(3);

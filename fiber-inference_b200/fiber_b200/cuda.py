@@ -261,7 +261,7 @@ class Context:
         return int(n)
 
     TRACE_FIELDS = ["t_release_ns", "cyc_barrier", "cyc_stage", "cyc_tiles", "cyc_wait_tiles", "cyc_arrive",
-                    "t_producer_done_ns", "cyc_producer_wait", "cyc_stage_stats", "cyc_stage_frags"]
+                    "t_producer_done_ns", "cyc_producer_wait", "cyc_attn_qkv", "cyc_attn_pages"]
 
     def trace_step(self, kv: KVCache, token: int, pos: int, max_phases: int = 4096, max_ctas: int = 1024):
         """Per-phase, per-CTA timeline of one persistent step: uint64 array

@@ -121,9 +121,8 @@ int fiber_tp_info(fiber_ctx_t *ctx, fiber_tp_plan_t *out);
  * at that barrier, 2 cycles staging the input vector, 3 cycles in the tile loop
  * (attention: the units), 4 of those waiting for weight tiles to land, 5 cycles
  * to the arrive, 6 globaltimer ns when the producer issued the phase's last
- * tile, 7 producer cycles spent waiting for ring space in the phase, 8 of
- * field 2 the cycles until the input statistics are reduced, 9 of field 2 the
- * cycles staging the fragments.
+ * tile, 7 producer cycles spent waiting for ring space in the phase; attention
+ * phases: 8 cycles until q/k/v are staged, 9 cycles of the page loop.
  * `cap` is the number of uint64 values `out` holds. */
 int fiber_trace_step(fiber_ctx_t *ctx, kv_cache_t *kv, int token, int pos, uint64_t *out, size_t cap,
                      int *n_phases, int *n_ctas);
