@@ -30,6 +30,7 @@
 #include "gemv_tc.cuh"
 #include "launch.cuh"
 #include "persistent.cuh"
+#include "gemm_tc5.cuh"
 
 using namespace fiber;
 
@@ -1384,5 +1385,64 @@ extern "C" int fiber_dequant(int type, const void *d_w, void *d_out, int rows, i
     case T_F16: dequant_kernel<T_F16><<<grid, 256, 0, st>>>(w, d_out, rows, cols); break;
     }
     CK(cudaGetLastError());
+    return FIBER_OK;
+}
+
+// ---- tensor-core dequant-GEMM (prefill) -------------------------------------------------
+
+template <int T>
+static cudaError_t launch_g5_t(const G5Params &p, cudaStream_t st) {
+    const int smem = g5_smem_bytes(T);
+    cudaError_t e = cudaFuncSetAttribute(gemm_tc5_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    const dim3 grid((p.rows + G5_M - 1) / G5_M, (p.ntok + G5_T - 1) / G5_T);
+    gemm_tc5_kernel<T><<<grid, G5_THREADS, smem, st>>>(p);
+    return cudaGetLastError();
+}
+
+static cudaError_t launch_g5(const G5Params &p, cudaStream_t st) {
+    switch (p.type) {
+    case T_Q4_K: return launch_g5_t<T_Q4_K>(p, st);
+    case T_Q6_K: return launch_g5_t<T_Q6_K>(p, st);
+    case T_F16: return launch_g5_t<T_F16>(p, st);
+    default: return cudaErrorInvalidValue;
+    }
+}
+
+static __device__ int g_g5_err;
+
+extern "C" int fiber_gemm(int ggml_type, const void *d_w, int rows, int cols, const float *d_x, int ntok, int ldx,
+                          const float *d_rrms, const float *d_nw, float *d_y, int ldy, int out_off, int accumulate,
+                          void *stream) {
+    if (!d_w || !d_x || !d_y || rows <= 0 || ntok <= 0 || cols <= 0 || cols % 256 || ldx < cols ||
+        ldy < out_off + rows)
+        return set_err(FIBER_EARG, "fiber_gemm: bad arguments");
+    if (!(ggml_type == T_Q4_K || ggml_type == T_Q6_K || ggml_type == T_F16))
+        return set_err(FIBER_EUNSUPPORTED, "fiber_gemm: type %s not supported (Q4_K, Q6_K, F16)", tname(ggml_type));
+    cudaStream_t st = (cudaStream_t)stream;
+    int *err = nullptr;
+    CK(cudaGetSymbolAddress((void **)&err, g_g5_err));
+    CK(cudaMemsetAsync(err, 0, sizeof(int), st));
+    G5Params p;
+    memset(&p, 0, sizeof(p));
+    p.w = (const uint8_t *)d_w;
+    p.type = ggml_type;
+    p.rows = rows;
+    p.cols = cols;
+    p.ntok = ntok;
+    p.x = d_x;
+    p.ldx = ldx;
+    p.rrms = d_rrms;
+    p.nw = d_nw;
+    p.y = d_y;
+    p.ldy = ldy;
+    p.out_off = out_off;
+    p.epi = accumulate ? G5_RESID : G5_STORE;
+    p.err = err;
+    CK(launch_g5(p, st));
+    int h_err = 0;
+    CK(cudaMemcpyAsync(&h_err, err, sizeof(int), cudaMemcpyDeviceToHost, st));
+    CK(cudaStreamSynchronize(st));
+    if (h_err) return set_err(FIBER_ETIMEOUT, "fiber_gemm: a tensor-core wait timed out");
     return FIBER_OK;
 }

@@ -14,7 +14,7 @@ import numpy as np
 from . import CUDA_SO, ModelParams  # noqa: F401
 
 __all__ = ["FiberError", "cuda_lib", "cuda_available", "gemv", "gemv_host", "gemv_argmax_noalloc", "dequant", "Context", "KVCache",
-           "device_count", "TPPlan", "TP_ID_BYTES", "tp_plan", "tp_unique_id"]
+           "device_count", "TPPlan", "TP_ID_BYTES", "tp_plan", "tp_unique_id", "gemm"]
 
 F32P = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
 I32P = np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS")
@@ -23,7 +23,7 @@ EXPORTED = [
     "fiber_last_error", "fiber_device_count", "fiber_cuda_init", "fiber_cuda_free", "fiber_forward_token",
     "fiber_prefill", "fiber_decode_greedy", "fiber_step_launches", "fiber_set_decode_mode",
     "fiber_get_decode_mode", "fiber_trace_step", "fiber_time_kernel", "fiber_gemv", "fiber_tp_plan",
-    "fiber_tp_unique_id", "fiber_cuda_init_tp", "fiber_tp_info",
+    "fiber_tp_unique_id", "fiber_cuda_init_tp", "fiber_tp_info", "fiber_gemm",
     "fiber_dequant", "fiber_gemv_host", "gpu_init", "gpu_free", "gpu_embed", "gpu_forward_token",
     "gpu_get_logits", "gpu_forward_classifier", "gpu_get_device", "kv_cache_init", "kv_cache_init_paged",
     "kv_cache_free", "kv_cache_write", "kv_cache_read", "fiber_gemv_argmax_noalloc",
@@ -75,6 +75,8 @@ def cuda_lib() -> C.CDLL:
         L.fiber_cuda_init_tp.restype = C.c_void_p
         L.fiber_cuda_init_tp.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_int]
         L.fiber_tp_info.argtypes = [C.c_void_p, C.POINTER(TPPlan)]
+        L.fiber_gemm.argtypes = [C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_void_p,
+                                 C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p]
         L.fiber_trace_step.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_size_t,
                                        C.POINTER(C.c_int), C.POINTER(C.c_int)]
         L.fiber_time_kernel.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.POINTER(C.c_double),
@@ -143,6 +145,14 @@ def gemv_argmax_noalloc(ggml_type: int, d_w: int, d_x: int, d_y: int, d_argmax: 
     """Greedy lm_head step whose scratch is a static device array (no allocation)."""
     _check(cuda_lib().fiber_gemv_argmax_noalloc(ggml_type, d_w, d_x, d_y, d_argmax, rows, cols, _stream_ptr(stream)),
            "fiber_gemv_argmax_noalloc")
+
+
+def gemm(ggml_type: int, d_w: int, rows: int, cols: int, d_x: int, ntok: int, d_y: int, ldy: int,
+         out_off: int = 0, d_rrms: int | None = None, d_nw: int | None = None, accumulate: bool = False,
+         ldx: int | None = None, stream=None):
+    """fiber_gemm: y[t][out_off + r] (+)= sum_k W[r,k] * xn[t][k] on the tensor cores."""
+    _check(cuda_lib().fiber_gemm(ggml_type, d_w, rows, cols, d_x, ntok, ldx or cols, d_rrms, d_nw, d_y, ldy, out_off,
+                                 1 if accumulate else 0, _stream_ptr(stream)), "fiber_gemm")
 
 
 def dequant(ggml_type: int, d_w: int, d_out: int, rows: int, cols: int, stream=None):

@@ -144,6 +144,15 @@ int fiber_time_kernel(fiber_ctx_t *ctx, kv_cache_t *kv, int kind, int pos, int r
  * (ggml_type Q4_K / Q5_K / Q6_K / F16; cols % 256 == 0), fp32 x and y. */
 int fiber_gemv(int ggml_type, const void *d_w, const float *d_x, float *d_y, int rows, int cols,
                void *stream);
+/* Tensor-core dequant-GEMM (the prefill building block; tcgen05, fp32 accumulation):
+ * y[t][out_off + r] = (accumulate ? y[t][out_off + r] : 0) + sum_k W[r,k] * xn[t][k]
+ * for t < ntok, with xn = x * rrms[t] * nw[k] when d_rrms/d_nw are given (RMSNorm
+ * folded in) and xn = x otherwise. W: Q4_K / Q6_K / F16 super-blocks, cols % 256 == 0;
+ * x: [ntok][ldx] fp32; y: [ntok][ldy] fp32. The weights are decoded exactly as the
+ * GEMV does; x is split into fp16 hi + lo parts. Synchronizes the stream. */
+int fiber_gemm(int ggml_type, const void *d_w, int rows, int cols, const float *d_x, int ntok, int ldx,
+               const float *d_rrms, const float *d_nw, float *d_y, int ldy, int out_off, int accumulate,
+               void *stream);
 /* Decoded weights: fp16 bits for Q4_K/Q6_K/F16, fp32 for Q5_K, [rows][cols]. */
 int fiber_dequant(int ggml_type, const void *d_w, void *d_out, int rows, int cols, void *stream);
 /* Same GEMV with host buffers: copies x in and y out around the launch on the
