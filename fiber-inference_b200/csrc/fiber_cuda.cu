@@ -31,6 +31,7 @@
 #include "launch.cuh"
 #include "persistent.cuh"
 #include "gemm_tc5.cuh"
+#include "prefill.cuh"
 
 using namespace fiber;
 
@@ -384,6 +385,11 @@ struct gpu_context {
     float *x2 = nullptr;            // second residual buffer: Wo's all-reduced output
     uint8_t *d_shard = nullptr;     // Wo / W_down shards along their input dimension
     ncclComm_t comm = nullptr;
+    // batched prefill (tensor-core GEMMs): buffers for a chunk of pf_cap tokens
+    int prefill_mode = 0;           // 0: batched when the model allows it, 1: token by token
+    int pf_cap = 0;
+    float *pf_x = nullptr, *pf_qkv = nullptr, *pf_att = nullptr, *pf_hg = nullptr, *pf_hu = nullptr, *pf_rr = nullptr;
+    int32_t *pf_tok = nullptr;
 };
 
 static void free_graph(Graph &g) {
@@ -399,7 +405,7 @@ extern "C" void fiber_cuda_free(fiber_ctx_t *c) {
     free_graph(c->g_step);
     free_graph(c->g_loop);
     if (c->comm) ncclCommDestroy(c->comm);
-    void *dev[] = {c->x2, c->d_shard, c->d_data, c->x, c->qkv, c->att, c->h, c->logits, c->rope, c->io, c->rec,
+    void *dev[] = {c->pf_x, c->pf_qkv, c->pf_att, c->pf_hg, c->pf_hu, c->pf_rr, c->pf_tok, c->x2, c->d_shard, c->d_data, c->x, c->qkv, c->att, c->h, c->logits, c->rope, c->io, c->rec,
                    c->att_part, c->att_cnt, c->am_part, c->am_cnt, c->d_phases, c->d_bar,
                    c->pk_gf[0], c->pk_gf[1], c->pk_gf[2], c->pk_gf[3], c->pk_ss[0], c->pk_ss[1]};
     for (void *p : dev)
@@ -1141,9 +1147,201 @@ extern "C" int fiber_forward_token(fiber_ctx_t *c, kv_cache_t *kv, const int32_t
     return FIBER_OK;
 }
 
+// ---- batched prefill ------------------------------------------------------------------
+
+constexpr int PF_CHUNK = 128;  // tokens per pass of the layer stack
+
+static cudaError_t launch_g5(const G5Params &p, cudaStream_t st);
+
+static bool g5_type_ok(int t) { return t == T_Q4_K || t == T_Q6_K || t == T_F16; }
+
+static bool prefill_batched_ok(const gpu_context *c) {
+    if (c->tp_world != 1 || c->prefill_mode != 0) return false;
+    if (!g5_type_ok(c->t_out) || c->G > 8) return false;
+    for (const LayerDev &d : c->L) {
+        const int ts[7] = {d.tq, d.tk, d.tv, d.to, d.t1, d.t2, d.t3};
+        for (int t : ts)
+            if (!g5_type_ok(t)) return false;
+    }
+    return true;
+}
+
+template <int HD, int G>
+static cudaError_t launch_attn_prefill_t(const AttnPrefillParams &a, int n, cudaStream_t st) {
+    attn_prefill_kernel<HD, G><<<dim3(n, a.n_kv), ATTN_THREADS, 0, st>>>(a);
+    return cudaGetLastError();
+}
+
+static cudaError_t launch_attn_prefill(const gpu_context *c, const AttnPrefillParams &a, int n, cudaStream_t st) {
+    const int hd = c->p.head_dim, G = c->G;
+#define APF_CASE(H, GG) \
+    if (hd == H && G == GG) return launch_attn_prefill_t<H, GG>(a, n, st);
+    APF_CASE(64, 1) APF_CASE(64, 2) APF_CASE(64, 4) APF_CASE(64, 8)
+    APF_CASE(128, 1) APF_CASE(128, 2) APF_CASE(128, 4) APF_CASE(128, 8)
+#undef APF_CASE
+    return cudaErrorInvalidValue;
+}
+
+static cudaError_t launch_embed_rows(const gpu_context *c, const int32_t *tok, float *X, int n, cudaStream_t st) {
+    const int dim = c->p.dim, V = c->p.vocab_size;
+    const dim3 g((dim + 255) / 256, n), b(256);
+    int *err = &c->io->err;
+    switch (c->t_embd) {
+    case T_Q4_K: embed_rows_kernel<T_Q4_K><<<g, b, 0, st>>>(c->embd, tok, X, dim, V, err); break;
+    case T_Q5_K: embed_rows_kernel<T_Q5_K><<<g, b, 0, st>>>(c->embd, tok, X, dim, V, err); break;
+    case T_Q6_K: embed_rows_kernel<T_Q6_K><<<g, b, 0, st>>>(c->embd, tok, X, dim, V, err); break;
+    case T_F16: embed_rows_kernel<T_F16><<<g, b, 0, st>>>(c->embd, tok, X, dim, V, err); break;
+    case T_F32: embed_rows_kernel<T_F32><<<g, b, 0, st>>>(c->embd, tok, X, dim, V, err); break;
+    default: return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+}
+
+// One tensor-core GEMM of the prefill: y[t][off + r] (+)= W[r,:] . xn[t,:]
+static cudaError_t pf_gemm(gpu_context *c, const uint8_t *w, int type, int rows, int cols, const float *x, int ldx,
+                           const float *rr, const float *nw, float *y, int ldy, int off, bool acc, int n,
+                           cudaStream_t st) {
+    G5Params g;
+    memset(&g, 0, sizeof(g));
+    g.w = w;
+    g.type = type;
+    g.rows = rows;
+    g.cols = cols;
+    g.ntok = n;
+    g.x = x;
+    g.ldx = ldx;
+    g.rrms = rr;
+    g.nw = nw;
+    g.y = y;
+    g.ldy = ldy;
+    g.out_off = off;
+    g.epi = acc ? G5_RESID : G5_STORE;
+    g.err = &c->io->err;
+    return launch_g5(g, st);
+}
+
+// Layers of the model over `n` prompt tokens at positions start .. start + n - 1:
+// embedding rows, then per layer RMSNorm scale + QKV GEMMs, RoPE + KV append,
+// causal attention, Wo GEMM (+residual), RMSNorm scale + gate/up GEMMs, SwiGLU,
+// down GEMM (+residual). Leaves the last token's hidden state in c->x.
+static cudaError_t enqueue_prefill_chunk(gpu_context *c, const kv_cache_t *kv, int n, int start, cudaStream_t st) {
+    const model_params_t &p = c->p;
+    const int dim = p.dim, ffn = p.ffn_dim, hd = p.head_dim, kvd = c->kvd, ldq = dim + 2 * kvd;
+    cudaError_t e = launch_embed_rows(c, c->pf_tok, c->pf_x, n, st);
+    for (uint32_t l = 0; l < p.n_layers && e == cudaSuccess; l++) {
+        const LayerDev &d = c->L[l];
+        rms_rows_kernel<<<n, 256, 0, st>>>(c->pf_x, dim, p.rms_norm_eps, c->pf_rr);
+        if ((e = cudaGetLastError()) != cudaSuccess) break;
+        if ((e = pf_gemm(c, d.wq, d.tq, dim, dim, c->pf_x, dim, c->pf_rr, d.attn_norm, c->pf_qkv, ldq, 0, false, n, st)))
+            break;
+        if ((e = pf_gemm(c, d.wk, d.tk, kvd, dim, c->pf_x, dim, c->pf_rr, d.attn_norm, c->pf_qkv, ldq, dim, false, n,
+                         st)))
+            break;
+        if ((e = pf_gemm(c, d.wv, d.tv, kvd, dim, c->pf_x, dim, c->pf_rr, d.attn_norm, c->pf_qkv, ldq, dim + kvd,
+                         false, n, st)))
+            break;
+        RopeKvParams rk;
+        rk.qkv = c->pf_qkv;
+        rk.ldq = ldq;
+        rk.start = start;
+        rk.rope = c->rope;
+        rk.n_heads = p.n_heads;
+        rk.n_kv = p.n_kv_heads;
+        rk.hd = hd;
+        rk.k_pool = kv->k_pool;
+        rk.v_pool = kv->v_pool;
+        rk.page_table = kv->page_table;
+        rk.layer = l;
+        rk.n_layers = p.n_layers;
+        rope_kv_kernel<<<n, 256, 0, st>>>(rk);
+        if ((e = cudaGetLastError()) != cudaSuccess) break;
+        AttnPrefillParams ap;
+        ap.qkv = c->pf_qkv;
+        ap.ldq = ldq;
+        ap.out = c->pf_att;
+        ap.ldo = dim;
+        ap.start = start;
+        ap.k_pool = kv->k_pool;
+        ap.v_pool = kv->v_pool;
+        ap.page_table = kv->page_table;
+        ap.layer = l;
+        ap.n_layers = p.n_layers;
+        ap.n_kv = p.n_kv_heads;
+        ap.n_heads = p.n_heads;
+        ap.scale = 1.0f / sqrtf((float)hd);
+        if ((e = launch_attn_prefill(c, ap, n, st))) break;
+        if ((e = pf_gemm(c, d.wo, d.to, dim, dim, c->pf_att, dim, nullptr, nullptr, c->pf_x, dim, 0, true, n, st)))
+            break;
+        rms_rows_kernel<<<n, 256, 0, st>>>(c->pf_x, dim, p.rms_norm_eps, c->pf_rr);
+        if ((e = cudaGetLastError()) != cudaSuccess) break;
+        if ((e = pf_gemm(c, d.w1, d.t1, ffn, dim, c->pf_x, dim, c->pf_rr, d.ffn_norm, c->pf_hg, ffn, 0, false, n, st)))
+            break;
+        if ((e = pf_gemm(c, d.w3, d.t3, ffn, dim, c->pf_x, dim, c->pf_rr, d.ffn_norm, c->pf_hu, ffn, 0, false, n, st)))
+            break;
+        swiglu_rows_kernel<<<(n * ffn + 255) / 256, 256, 0, st>>>(c->pf_hg, c->pf_hu, (size_t)n * ffn);
+        if ((e = cudaGetLastError()) != cudaSuccess) break;
+        e = pf_gemm(c, d.w2, d.t2, dim, ffn, c->pf_hg, ffn, nullptr, nullptr, c->pf_x, dim, 0, true, n, st);
+    }
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(c->x, c->pf_x + (size_t)(n - 1) * dim, (size_t)dim * 4, cudaMemcpyDeviceToDevice, st);
+    return e;
+}
+
+static int prefill_batched(gpu_context *c, kv_cache_t *kv, const int32_t *tokens, int n, int start_pos,
+                           int32_t *argmax_out) {
+    const model_params_t &p = c->p;
+    if (!c->pf_cap) {
+        const size_t T = PF_CHUNK;
+        CK(cudaMalloc(&c->pf_x, T * p.dim * 4));
+        CK(cudaMalloc(&c->pf_qkv, T * (p.dim + 2 * c->kvd) * 4));
+        CK(cudaMalloc(&c->pf_att, T * p.dim * 4));
+        CK(cudaMalloc(&c->pf_hg, T * p.ffn_dim * 4));
+        CK(cudaMalloc(&c->pf_hu, T * p.ffn_dim * 4));
+        CK(cudaMalloc(&c->pf_rr, T * 4));
+        CK(cudaMalloc(&c->pf_tok, T * 4));
+        c->pf_cap = PF_CHUNK;
+    }
+    c->h_io->err = 0;
+    CK(cudaMemcpyAsync(c->io, c->h_io, sizeof(StepIO), cudaMemcpyHostToDevice, c->stream));
+    for (int i = 0; i < n; i += c->pf_cap) {
+        const int m = std::min(c->pf_cap, n - i);
+        CK(cudaMemcpyAsync(c->pf_tok, tokens + i, (size_t)m * 4, cudaMemcpyHostToDevice, c->stream));
+        cudaError_t e = enqueue_prefill_chunk(c, kv, m, start_pos + i, c->stream);
+        if (e != cudaSuccess) return set_err(FIBER_ECUDA, "batched prefill: %s", cudaGetErrorString(e));
+        CK(cudaStreamSynchronize(c->stream));  // pf_tok is reused by the next chunk
+    }
+    cudaError_t e = enqueue_lm_head(c, false, c->stream);
+    if (e != cudaSuccess) return set_err(FIBER_ECUDA, "prefill lm_head: %s", cudaGetErrorString(e));
+    CK(cudaMemcpyAsync(c->h_io, c->io, sizeof(StepIO), cudaMemcpyDeviceToHost, c->stream));
+    CK(cudaStreamSynchronize(c->stream));
+    if (c->h_io->err == 6) return set_err(FIBER_ETIMEOUT, "batched prefill: a tensor-core wait timed out");
+    int rc = device_status(c);
+    if (rc) return rc;
+    if (argmax_out) *argmax_out = c->h_io->argmax;
+    return FIBER_OK;
+}
+
+extern "C" int fiber_set_prefill_mode(fiber_ctx_t *c, int mode) {
+    if (!c || mode < 0 || mode > 1) return set_err(FIBER_EARG, "fiber_set_prefill_mode: mode must be 0 or 1");
+    c->prefill_mode = mode;
+    return FIBER_OK;
+}
+
 extern "C" int fiber_prefill(fiber_ctx_t *c, kv_cache_t *kv, const int32_t *tokens, int n, int start_pos,
                              int32_t *argmax_out) {
     if (!c || !tokens || n <= 0) return set_err(FIBER_EARG, "fiber_prefill: empty prompt");
+    if (n > 1 && prefill_batched_ok(c)) {
+        int rc = check_kv(c, kv);
+        if (rc) return rc;
+        const int lim = c->max_seq < kv->max_seq ? c->max_seq : kv->max_seq;
+        if (start_pos < 0 || start_pos + n > lim)
+            return set_err(FIBER_EARG, "prefill positions %d..%d outside [0, %d)", start_pos, start_pos + n - 1, lim);
+        for (int i = 0; i < n; i++)
+            if (tokens[i] < 0 || tokens[i] >= (int)c->p.vocab_size)
+                return set_err(FIBER_EARG, "token %d out of range", tokens[i]);
+        CK(cudaSetDevice(c->device));
+        return prefill_batched(c, kv, tokens, n, start_pos, argmax_out);
+    }
     for (int i = 0; i < n; i++) {
         const int32_t pos = start_pos + i;
         int rc = fiber_forward_token(c, kv, tokens + i, &pos, 1, nullptr, i == n - 1 ? argmax_out : nullptr);

@@ -1,0 +1,203 @@
+// prefill.cuh — the non-GEMM kernels of the batched prefill (a prompt chunk of n
+// tokens at positions start .. start + n - 1 in one pass per layer). The
+// projections run on the tensor cores (gemm_tc5.cuh); these kernels do the
+// per-token parts with the decode path's arithmetic:
+//   embed_rows_kernel   embedding rows of the n tokens (fp16-rounded, as gpu_embed)
+//   rms_rows_kernel     per-token 1/sqrt(mean(x^2) + eps) (the GEMM applies it)
+//   rope_kv_kernel      half-split RoPE of q (in place) and k; K/V appended (fp16)
+//   attn_prefill_kernel causal GQA attention of each token over the cache
+//   swiglu_rows_kernel  h = silu(gate) * up
+#pragma once
+#include "attention.cuh"
+
+namespace fiber {
+
+template <int T>
+__global__ void embed_rows_kernel(const uint8_t *__restrict__ tab, const int32_t *__restrict__ tokens, float *X,
+                                  int dim, int vocab, int *err) {
+    const int t = blockIdx.y;
+    int tok = tokens[t];
+    if (tok < 0 || tok >= vocab) {
+        if (threadIdx.x == 0 && blockIdx.x == 0) *err = 2;
+        tok = 0;
+    }
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < dim; i += gridDim.x * blockDim.x) {
+        float v;
+        if constexpr (T == T_F16) {
+            v = h2f(reinterpret_cast<const uint16_t *>(tab)[(size_t)tok * dim + i]);
+        } else if constexpr (T == T_F32) {
+            v = round_f16(reinterpret_cast<const float *>(tab)[(size_t)tok * dim + i]);
+        } else {
+            constexpr int BB = T == T_Q4_K ? 144 : (T == T_Q5_K ? 176 : 210);
+            v = round_f16(decode_elem<T>(tab + ((size_t)tok * (dim >> 8) + (i >> 8)) * BB, i & 255));
+        }
+        X[(size_t)t * dim + i] = v;
+    }
+}
+
+__global__ void rms_rows_kernel(const float *__restrict__ X, int dim, float eps, float *rr) {
+    __shared__ float part[32];
+    const float *x = X + (size_t)blockIdx.x * dim;
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < dim; i += blockDim.x) ss = fmaf(x[i], x[i], ss);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float s = 0.f;
+        for (int w = 0; w < (int)(blockDim.x >> 5); w++) s += part[w];
+        rr[blockIdx.x] = 1.0f / sqrtf(s / (float)dim + eps);
+    }
+}
+
+struct RopeKvParams {
+    float *qkv;            // [n][ldq]: q | k | v of each token (q rotated in place)
+    int ldq;
+    int start;             // position of token 0
+    const float2 *rope;    // [max_seq][hd/2]
+    int n_heads, n_kv, hd;
+    uint16_t *k_pool, *v_pool;
+    const int32_t *page_table;
+    int layer, n_layers;
+};
+
+// One CTA per token: rotate q and k (the decode path's expressions), store K and V.
+__global__ void rope_kv_kernel(const RopeKvParams a) {
+    const int t = blockIdx.x, pos = a.start + t, hd = a.hd, half = hd / 2;
+    float *q = a.qkv + (size_t)t * a.ldq;
+    const float *k = q + (size_t)a.n_heads * hd, *v = k + (size_t)a.n_kv * hd;
+    const float2 *rp = a.rope + (size_t)pos * half;
+    for (int i = threadIdx.x; i < a.n_heads * half; i += blockDim.x) {
+        const int h = i / half, j = i % half;
+        const float2 cs = rp[j];
+        const float x1 = q[h * hd + j], x2 = q[h * hd + j + half];
+        q[h * hd + j] = __fsub_rn(__fmul_rn(x1, cs.x), __fmul_rn(x2, cs.y));
+        q[h * hd + j + half] = __fadd_rn(__fmul_rn(x1, cs.y), __fmul_rn(x2, cs.x));
+    }
+    const int page = a.page_table[pos / ATTN_P], tn = pos % ATTN_P;
+    for (int i = threadIdx.x; i < a.n_kv * half; i += blockDim.x) {
+        const int g = i / half, j = i % half;
+        const float2 cs = rp[j];
+        const float x1 = k[g * hd + j], x2 = k[g * hd + j + half];
+        uint16_t *kp = a.k_pool + ((((size_t)page * a.n_layers + a.layer) * a.n_kv + g) * ATTN_P + tn) * hd;
+        kp[j] = __half_as_ushort(__float2half_rn(__fsub_rn(__fmul_rn(x1, cs.x), __fmul_rn(x2, cs.y))));
+        kp[j + half] = __half_as_ushort(__float2half_rn(__fadd_rn(__fmul_rn(x1, cs.y), __fmul_rn(x2, cs.x))));
+    }
+    for (int i = threadIdx.x; i < a.n_kv * hd; i += blockDim.x) {
+        const int g = i / hd, d = i % hd;
+        uint16_t *vp = a.v_pool + ((((size_t)page * a.n_layers + a.layer) * a.n_kv + g) * ATTN_P + tn) * hd;
+        vp[d] = __half_as_ushort(__float2half_rn(v[g * hd + d]));
+    }
+}
+
+struct AttnPrefillParams {
+    const float *qkv;      // [n][ldq], q rotated
+    int ldq;
+    float *out;            // [n][ldo]
+    int ldo;
+    int start;
+    const uint16_t *k_pool, *v_pool;
+    const int32_t *page_table;
+    int layer, n_layers, n_kv, n_heads;
+    float scale;
+};
+
+// CTA (token t, KV head g): the G query heads of g attend to positions 0 .. start + t,
+// page by page (64 positions) with the decode path's score / softmax / P.V arithmetic,
+// pages combined online.
+template <int HD, int G>
+__global__ void __launch_bounds__(ATTN_THREADS) attn_prefill_kernel(const AttnPrefillParams a) {
+    constexpr int P = ATTN_P, KST = HD + 2, DPL = HD / 32;
+    __shared__ __align__(16) float qs[G][HD];
+    __shared__ __align__(16) uint16_t ks[P][KST];
+    __shared__ __align__(16) uint16_t vs[P][HD];
+    const int t = blockIdx.x, g = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int seqlen = a.start + t + 1, nch = (seqlen + P - 1) / P;
+    for (int i = tid; i < G * HD; i += ATTN_THREADS)
+        qs[i / HD][i % HD] = a.qkv[(size_t)t * a.ldq + (size_t)(g * G + i / HD) * HD + i % HD];
+    float m_run = -INFINITY, l_run = 0.f, o_run[DPL];
+#pragma unroll
+    for (int j = 0; j < DPL; j++) o_run[j] = 0.f;
+    for (int c = 0; c < nch; c++) {
+        __syncthreads();  // previous page consumed (and qs staged)
+        const int t0 = c * P, nt = min(P, seqlen - t0);
+        const size_t base = (((size_t)a.page_table[c] * a.n_layers + a.layer) * a.n_kv + g) * (size_t)P * HD;
+        constexpr int V8 = HD / 8;
+        for (int i = tid; i < nt * V8; i += ATTN_THREADS) {
+            const int r = i / V8, k8 = i % V8;
+            const uint4 kv4 = *reinterpret_cast<const uint4 *>(a.k_pool + base + (size_t)r * HD + 8 * k8);
+            const uint4 vv4 = *reinterpret_cast<const uint4 *>(a.v_pool + base + (size_t)r * HD + 8 * k8);
+            uint32_t *kd = reinterpret_cast<uint32_t *>(&ks[r][8 * k8]);
+            kd[0] = kv4.x; kd[1] = kv4.y; kd[2] = kv4.z; kd[3] = kv4.w;
+            *reinterpret_cast<uint4 *>(&vs[r][8 * k8]) = vv4;
+        }
+        __syncthreads();
+        for (int h = warp; h < G; h += ATTN_THREADS / 32) {
+            float sc2[2];
+#pragma unroll
+            for (int k = 0; k < 2; k++) {
+                const int r = lane + 32 * k;
+                float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;
+                if (r < nt) {
+#pragma unroll
+                    for (int d = 0; d < HD; d += 4) {
+                        d0 = fmaf(qs[h][d + 0], __half2float(__ushort_as_half(ks[r][d + 0])), d0);
+                        d1 = fmaf(qs[h][d + 1], __half2float(__ushort_as_half(ks[r][d + 1])), d1);
+                        d2 = fmaf(qs[h][d + 2], __half2float(__ushort_as_half(ks[r][d + 2])), d2);
+                        d3 = fmaf(qs[h][d + 3], __half2float(__ushort_as_half(ks[r][d + 3])), d3);
+                    }
+                }
+                sc2[k] = r < nt ? __fmul_rn((d0 + d1) + (d2 + d3), a.scale) : -INFINITY;
+            }
+            float m = fmaxf(sc2[0], sc2[1]);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+            const float e0 = lane < nt ? expf(sc2[0] - m) : 0.f;
+            const float e1 = lane + 32 < nt ? expf(sc2[1] - m) : 0.f;
+            float l = e0 + e1;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+            float o1[DPL], o2[DPL];
+#pragma unroll
+            for (int j = 0; j < DPL; j++) o1[j] = o2[j] = 0.f;
+            for (int r = 0; r < min(nt, 32); r++) {
+                const float w = __shfl_sync(0xffffffffu, e0, r);
+#pragma unroll
+                for (int j = 0; j < DPL; j++) o1[j] = fmaf(w, __half2float(__ushort_as_half(vs[r][lane + 32 * j])), o1[j]);
+            }
+            for (int r = 32; r < nt; r++) {
+                const float w = __shfl_sync(0xffffffffu, e1, r - 32);
+#pragma unroll
+                for (int j = 0; j < DPL; j++) o2[j] = fmaf(w, __half2float(__ushort_as_half(vs[r][lane + 32 * j])), o2[j]);
+            }
+            // G <= 8 heads: warp h keeps head h's running state across pages
+            if (c == 0) {
+                m_run = m;
+                l_run = l;
+#pragma unroll
+                for (int j = 0; j < DPL; j++) o_run[j] = o1[j] + o2[j];
+            } else {
+                const float M = fmaxf(m_run, m);
+                const float al = expf(m_run - M), be = expf(m - M);
+                l_run = fmaf(al, l_run, be * l);
+#pragma unroll
+                for (int j = 0; j < DPL; j++) o_run[j] = fmaf(al, o_run[j], be * (o1[j] + o2[j]));
+                m_run = M;
+            }
+        }
+    }
+    if (warp < G)
+#pragma unroll
+        for (int j = 0; j < DPL; j++)
+            a.out[(size_t)t * a.ldo + (size_t)(g * G + warp) * HD + lane + 32 * j] = o_run[j] / l_run;
+}
+
+__global__ void swiglu_rows_kernel(float *hg, const float *__restrict__ hu, size_t n) {
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const float g = hg[i];
+        hg[i] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), hu[i]);
+    }
+}
+
+}  // namespace fiber

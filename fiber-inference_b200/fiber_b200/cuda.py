@@ -23,7 +23,7 @@ EXPORTED = [
     "fiber_last_error", "fiber_device_count", "fiber_cuda_init", "fiber_cuda_free", "fiber_forward_token",
     "fiber_prefill", "fiber_decode_greedy", "fiber_step_launches", "fiber_set_decode_mode",
     "fiber_get_decode_mode", "fiber_trace_step", "fiber_time_kernel", "fiber_gemv", "fiber_tp_plan",
-    "fiber_tp_unique_id", "fiber_cuda_init_tp", "fiber_tp_info", "fiber_gemm",
+    "fiber_tp_unique_id", "fiber_cuda_init_tp", "fiber_tp_info", "fiber_gemm", "fiber_set_prefill_mode",
     "fiber_dequant", "fiber_gemv_host", "gpu_init", "gpu_free", "gpu_embed", "gpu_forward_token",
     "gpu_get_logits", "gpu_forward_classifier", "gpu_get_device", "kv_cache_init", "kv_cache_init_paged",
     "kv_cache_free", "kv_cache_write", "kv_cache_read", "fiber_gemv_argmax_noalloc",
@@ -75,6 +75,7 @@ def cuda_lib() -> C.CDLL:
         L.fiber_cuda_init_tp.restype = C.c_void_p
         L.fiber_cuda_init_tp.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_int]
         L.fiber_tp_info.argtypes = [C.c_void_p, C.POINTER(TPPlan)]
+        L.fiber_set_prefill_mode.argtypes = [C.c_void_p, C.c_int]
         L.fiber_gemm.argtypes = [C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_void_p,
                                  C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p]
         L.fiber_trace_step.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_size_t,
@@ -259,6 +260,10 @@ class Context:
     def set_mode(self, mode: int):
         """0: persistent one-kernel step (default when supported); 1: one kernel per phase."""
         _check(cuda_lib().fiber_set_decode_mode(self.h, int(mode)), "fiber_set_decode_mode")
+
+    def set_prefill_mode(self, mode: int):
+        """0: batched tensor-core prefill when supported (default); 1: one decode step per token."""
+        _check(cuda_lib().fiber_set_prefill_mode(self.h, int(mode)), "fiber_set_prefill_mode")
 
     @property
     def mode(self) -> int:

@@ -75,6 +75,13 @@ int fiber_decode_greedy(fiber_ctx_t *ctx, kv_cache_t *kv, int32_t first_token, i
  * Both give the same tokens; mode 1 also serves models the persistent kernel
  * does not cover (Q5_K weights). Returns FIBER_EUNSUPPORTED for mode 0 then. */
 int fiber_set_decode_mode(fiber_ctx_t *ctx, int mode);
+
+/* Prefill path of fiber_prefill: 0 (default) = batched, the prompt in chunks of 128
+ * tokens through tensor-core dequant-GEMMs (tcgen05) with causal attention over the
+ * cache, when every matrix is Q4_K / Q6_K / F16 and the context is not sharded;
+ * 1 = one decode step per token. Both fill the same KV cache and return the first
+ * generated token. */
+int fiber_set_prefill_mode(fiber_ctx_t *ctx, int mode);
 int fiber_get_decode_mode(fiber_ctx_t *ctx);
 
 /* Number of kernels one decode step launches (all of them this library's own). */
