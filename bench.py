@@ -348,6 +348,64 @@ def run_config(args, fb, torch, dist, rank, world, local):
         dist.destroy_process_group()
 
 
+def run_prefill(args, fb, torch, dist, rank, world, local):
+    """Batched prefill of a 512-token prompt (1.1B Q4_K_M): tokens/s through fiber_prefill and the
+    tensor-core GEMM throughput it implies (2 x params FLOPs per token; the kernels run twice the
+    columns for the hi/lo split of x, reported separately)."""
+    P = 512 if args.prompt_len == PROMPT_LEN else args.prompt_len
+    path = MODEL_PATH if world == 1 else MODEL_PATH.replace(".gguf", f".r{rank}.gguf")
+    make_model(path)
+    hm = fb.HostModel(path)
+    p = hm.params
+    ctx = fb.Context(hm, device=local, max_seq=P + 8)
+    kv = ctx.kv(P + 8)
+    prompt = np.resize(prompt_ids(p.vocab_size), P).astype(np.int32)
+    for _ in range(args.warmup):
+        ctx.prefill(kv, prompt)
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize(local)
+    times = []
+    with Clocks(local) as clk:
+        for _ in range(args.steps):
+            t0 = time.perf_counter()
+            ctx.prefill(kv, prompt)  # synchronizes the context stream before returning
+            times.append(time.perf_counter() - t0)
+    sec = sum(times)
+    if dist is not None:
+        t = torch.tensor([sec], device=f"cuda:{local}", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        sec = float(t.item())
+    value = world * args.steps * P / sec
+    n_params = p.n_layers * (2 * p.dim * p.dim + 2 * p.dim * p.n_kv_heads * p.head_dim + 3 * p.dim * p.ffn_dim)
+    flops_tok = 2.0 * n_params
+    peak_tf, peak_src = 1590.0, "fallback bf16"
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peak_tf, peak_src = float(json.load(f)["bf16_tflops"]), "measured bf16 burst"
+    except (OSError, KeyError, ValueError):
+        pass
+    if rank == 0:
+        ach = flops_tok * value / world / 1e12
+        line = {"metric": "prefill tok/s (1.1B Q4_K_M, 512-token prompt)", "value": value, "unit": "tok/s",
+                "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec / args.steps * 1e3,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16 x f16 -> f32",
+                "data": "synthetic (seeded random-init weights, seeded prompt ids)",
+                "config": {"workload": "1.1B Q4_K_M batched prefill (tcgen05 dequant-GEMMs)", "prompt": P,
+                           "chunk": fb.PREFILL_CHUNK, "parallelism": f"replicas x{world}",
+                           "timing": "host clock around fiber_prefill (it synchronizes its stream)"},
+                "roofline": {"bound": "tensor", "achieved": ach, "peak": peak_tf, "unit": "TFLOP/s",
+                             "frac": ach / peak_tf, "peak_source": peak_src,
+                             "algorithmic_flops_per_token": flops_tok,
+                             "issued_tensor_tflops": 2 * ach, "note": "issued = x split into fp16 hi and lo columns"},
+                "clocks": clk.summary()}
+        print(json.dumps(line), flush=True)
+    ctx.close()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -361,11 +419,12 @@ def main():
     ap.add_argument("--skip-extras", action="store_true", help="no single-GEMV, e2e or CPU legs (profiling)")
     ap.add_argument("--step-mode", type=int, default=None, choices=[0, 1],
                     help="0: one persistent kernel per token (default when the model fits it); 1: one kernel per phase")
-    ap.add_argument("--workload", default="1.1b", choices=["1.1b", "7b-tp", "stories", "q5km-long"],
+    ap.add_argument("--workload", default="1.1b", choices=["1.1b", "7b-tp", "stories", "q5km-long", "prefill"],
                     help="1.1b: the headline 1.1B Q4_K_M decode (replicas for N>1); "
                          "7b-tp: 7B Q4_K_M decode tensor-parallel over the N GPUs; "
                          "stories: fp16 stories-shaped model (dim 768, 12 layers), 32-token prompt, 256 steps; "
-                         "q5km-long: 1.1B Q5_K_M with the KV cache pre-filled to 2048 positions, 256 steps")
+                         "q5km-long: 1.1B Q5_K_M with the KV cache pre-filled to 2048 positions, 256 steps; "
+                         "prefill: 1.1B Q4_K_M batched prefill of a 512-token prompt")
     args = ap.parse_args()
 
     rank = int(os.environ.get("RANK", "0"))
@@ -390,6 +449,8 @@ def main():
         return run_7b_tp(args, fb, torch, dist, rank, world, local)
     if args.workload in ("stories", "q5km-long"):
         return run_config(args, fb, torch, dist, rank, world, local)
+    if args.workload == "prefill":
+        return run_prefill(args, fb, torch, dist, rank, world, local)
 
     def barrier():
         if dist is not None:

@@ -13,6 +13,8 @@
 //   RMSNorm+lm_head+argmax                         rmsnorm + matvec_f32 + sampler argmax
 // The step reads token and position from device memory, so it is captured once
 // into a CUDA graph and replayed for every token.
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 #include <math.h>
 #include <nccl.h>
@@ -388,7 +390,9 @@ struct gpu_context {
     // batched prefill (tensor-core GEMMs): buffers for a chunk of pf_cap tokens
     int prefill_mode = 0;           // 0: batched when the model allows it, 1: token by token
     int pf_cap = 0;
-    float *pf_x = nullptr, *pf_qkv = nullptr, *pf_att = nullptr, *pf_hg = nullptr, *pf_hu = nullptr, *pf_rr = nullptr;
+    float *pf_x = nullptr, *pf_qkv = nullptr, *pf_att = nullptr, *pf_hg = nullptr, *pf_hu = nullptr;
+    uint8_t *pf_bp = nullptr;          // GEMM input packed as the MMA's B operand (hi / lo fp16)
+    std::vector<CUtensorMap> pf_maps;  // per layer: tensor maps of wq wk wv wo w1 w2 w3
     int32_t *pf_tok = nullptr;
 };
 
@@ -405,7 +409,7 @@ extern "C" void fiber_cuda_free(fiber_ctx_t *c) {
     free_graph(c->g_step);
     free_graph(c->g_loop);
     if (c->comm) ncclCommDestroy(c->comm);
-    void *dev[] = {c->pf_x, c->pf_qkv, c->pf_att, c->pf_hg, c->pf_hu, c->pf_rr, c->pf_tok, c->x2, c->d_shard, c->d_data, c->x, c->qkv, c->att, c->h, c->logits, c->rope, c->io, c->rec,
+    void *dev[] = {c->pf_x, c->pf_qkv, c->pf_att, c->pf_hg, c->pf_hu, c->pf_bp, c->pf_tok, c->x2, c->d_shard, c->d_data, c->x, c->qkv, c->att, c->h, c->logits, c->rope, c->io, c->rec,
                    c->att_part, c->att_cnt, c->am_part, c->am_cnt, c->d_phases, c->d_bar,
                    c->pk_gf[0], c->pk_gf[1], c->pk_gf[2], c->pk_gf[3], c->pk_ss[0], c->pk_ss[1]};
     for (void *p : dev)
@@ -657,7 +661,8 @@ static int ctx_init(gpu_context *c, const model_t *m, int device, int max_seq, i
     // GGUF data section, unchanged
     const gguf_file_t *gf = m->gf;
     c->data_bytes = gf->file_size - gf->data_offset;
-    if (cudaMalloc(&c->d_data, c->data_bytes) != cudaSuccess)
+    // + 256 bytes: the prefill GEMM reads Q6_K blocks through 16-byte-aligned spans
+    if (cudaMalloc(&c->d_data, c->data_bytes + 256) != cudaSuccess)
         return set_err(FIBER_ENOMEM, "cannot allocate %.1f MB for weights", c->data_bytes / 1e6);
     CK(cudaMemcpy(c->d_data, (const uint8_t *)gf->data + gf->data_offset, c->data_bytes, cudaMemcpyHostToDevice));
     auto dp = [&](uint64_t off) { return c->d_data + off; };
@@ -1149,7 +1154,7 @@ extern "C" int fiber_forward_token(fiber_ctx_t *c, kv_cache_t *kv, const int32_t
 
 // ---- batched prefill ------------------------------------------------------------------
 
-constexpr int PF_CHUNK = 128;  // tokens per pass of the layer stack
+constexpr int PF_CHUNK = FIBER_PREFILL_CHUNK;  // tokens per pass of the layer stack
 
 static cudaError_t launch_g5(const G5Params &p, cudaStream_t st);
 
@@ -1162,6 +1167,10 @@ static bool prefill_batched_ok(const gpu_context *c) {
         const int ts[7] = {d.tq, d.tk, d.tv, d.to, d.t1, d.t2, d.t3};
         for (int t : ts)
             if (!g5_type_ok(t)) return false;
+        // the GEMM streams weight rows with 16-byte-aligned bulk / tensor copies
+        const uint8_t *ws[7] = {d.wq, d.wk, d.wv, d.wo, d.w1, d.w2, d.w3};
+        for (const uint8_t *w : ws)
+            if ((uintptr_t)w & 15) return false;
     }
     return true;
 }
@@ -1197,21 +1206,65 @@ static cudaError_t launch_embed_rows(const gpu_context *c, const int32_t *tok, f
     return cudaGetLastError();
 }
 
-// One tensor-core GEMM of the prefill: y[t][off + r] (+)= W[r,:] . xn[t,:]
-static cudaError_t pf_gemm(gpu_context *c, const uint8_t *w, int type, int rows, int cols, const float *x, int ldx,
-                           const float *rr, const float *nw, float *y, int ldy, int off, bool acc, int n,
-                           cudaStream_t st) {
+// 2D tensor map over a Q4_K (bytes) or F16 (fp16 elements) weight matrix with a box of
+// 128 rows x one K unit (a super-block / 128 values); other types need none.
+static bool g5_make_map(CUtensorMap *map, const uint8_t *w, int type, int rows, int cols) {
+    memset(map, 0, sizeof(*map));
+    if (type != T_Q4_K && type != T_F16) return true;
+    static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+    if (!encode) {
+        void *fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault, &q) !=
+                cudaSuccess ||
+            q != cudaDriverEntryPointSuccess || !fn)
+            return false;
+        encode = (PFN_cuTensorMapEncodeTiled_v12000)fn;
+    }
+    const bool q4 = type == T_Q4_K;
+    const cuuint64_t row_bytes = q4 ? (cuuint64_t)cols / 256 * 144 : (cuuint64_t)cols * 2;
+    const cuuint64_t dims[2] = {q4 ? row_bytes : (cuuint64_t)cols, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {row_bytes};
+    const cuuint32_t box[2] = {q4 ? 144u : 128u, (cuuint32_t)G5_M};
+    const cuuint32_t estr[2] = {1, 1};
+    return encode(map, q4 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, (void *)w, dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+static cudaError_t launch_g5_pack(const G5PackParams &a, cudaStream_t st) {
+    g5_pack_kernel<<<((a.ntok + G5_T - 1) / G5_T) * (G5_T / 4), 128, 0, st>>>(a);
+    return cudaGetLastError();
+}
+
+// Pack n rows of x (RMS-normalised with weights nw when given) into c->pf_bp.
+static cudaError_t pf_pack(gpu_context *c, const float *x, int cols, const float *nw, int n, cudaStream_t st) {
+    G5PackParams a;
+    memset(&a, 0, sizeof(a));
+    a.x = x;
+    a.ldx = cols;
+    a.ntok = n;
+    a.cols = cols;
+    a.nw = nw;
+    a.own_rms = nw != nullptr;
+    a.eps = c->p.rms_norm_eps;
+    a.bp = c->pf_bp;
+    a.err = &c->io->err;
+    return launch_g5_pack(a, st);
+}
+
+// One tensor-core GEMM of the prefill on the packed input: y[t][off + r] (+)= W[r,:] . xn[t,:]
+static cudaError_t pf_gemm(gpu_context *c, const CUtensorMap &map, const uint8_t *w, int type, int rows, int cols,
+                           float *y, int ldy, int off, bool acc, int n, cudaStream_t st) {
     G5Params g;
     memset(&g, 0, sizeof(g));
+    g.wmap = map;
     g.w = w;
     g.type = type;
     g.rows = rows;
     g.cols = cols;
     g.ntok = n;
-    g.x = x;
-    g.ldx = ldx;
-    g.rrms = rr;
-    g.nw = nw;
+    g.bp = c->pf_bp;
     g.y = y;
     g.ldy = ldy;
     g.out_off = off;
@@ -1221,25 +1274,20 @@ static cudaError_t pf_gemm(gpu_context *c, const uint8_t *w, int type, int rows,
 }
 
 // Layers of the model over `n` prompt tokens at positions start .. start + n - 1:
-// embedding rows, then per layer RMSNorm scale + QKV GEMMs, RoPE + KV append,
-// causal attention, Wo GEMM (+residual), RMSNorm scale + gate/up GEMMs, SwiGLU,
-// down GEMM (+residual). Leaves the last token's hidden state in c->x.
+// embedding rows, then per layer RMSNorm + packing of the input, QKV GEMMs, RoPE +
+// KV append, causal attention, Wo GEMM (+residual), RMSNorm + packing, gate/up GEMMs,
+// SwiGLU, down GEMM (+residual). Leaves the last token's hidden state in c->x.
 static cudaError_t enqueue_prefill_chunk(gpu_context *c, const kv_cache_t *kv, int n, int start, cudaStream_t st) {
     const model_params_t &p = c->p;
     const int dim = p.dim, ffn = p.ffn_dim, hd = p.head_dim, kvd = c->kvd, ldq = dim + 2 * kvd;
     cudaError_t e = launch_embed_rows(c, c->pf_tok, c->pf_x, n, st);
     for (uint32_t l = 0; l < p.n_layers && e == cudaSuccess; l++) {
         const LayerDev &d = c->L[l];
-        rms_rows_kernel<<<n, 256, 0, st>>>(c->pf_x, dim, p.rms_norm_eps, c->pf_rr);
-        if ((e = cudaGetLastError()) != cudaSuccess) break;
-        if ((e = pf_gemm(c, d.wq, d.tq, dim, dim, c->pf_x, dim, c->pf_rr, d.attn_norm, c->pf_qkv, ldq, 0, false, n, st)))
-            break;
-        if ((e = pf_gemm(c, d.wk, d.tk, kvd, dim, c->pf_x, dim, c->pf_rr, d.attn_norm, c->pf_qkv, ldq, dim, false, n,
-                         st)))
-            break;
-        if ((e = pf_gemm(c, d.wv, d.tv, kvd, dim, c->pf_x, dim, c->pf_rr, d.attn_norm, c->pf_qkv, ldq, dim + kvd,
-                         false, n, st)))
-            break;
+        const CUtensorMap *mp = &c->pf_maps[7 * l];
+        if ((e = pf_pack(c, c->pf_x, dim, d.attn_norm, n, st))) break;
+        if ((e = pf_gemm(c, mp[0], d.wq, d.tq, dim, dim, c->pf_qkv, ldq, 0, false, n, st))) break;
+        if ((e = pf_gemm(c, mp[1], d.wk, d.tk, kvd, dim, c->pf_qkv, ldq, dim, false, n, st))) break;
+        if ((e = pf_gemm(c, mp[2], d.wv, d.tv, kvd, dim, c->pf_qkv, ldq, dim + kvd, false, n, st))) break;
         RopeKvParams rk;
         rk.qkv = c->pf_qkv;
         rk.ldq = ldq;
@@ -1270,17 +1318,15 @@ static cudaError_t enqueue_prefill_chunk(gpu_context *c, const kv_cache_t *kv, i
         ap.n_heads = p.n_heads;
         ap.scale = 1.0f / sqrtf((float)hd);
         if ((e = launch_attn_prefill(c, ap, n, st))) break;
-        if ((e = pf_gemm(c, d.wo, d.to, dim, dim, c->pf_att, dim, nullptr, nullptr, c->pf_x, dim, 0, true, n, st)))
-            break;
-        rms_rows_kernel<<<n, 256, 0, st>>>(c->pf_x, dim, p.rms_norm_eps, c->pf_rr);
-        if ((e = cudaGetLastError()) != cudaSuccess) break;
-        if ((e = pf_gemm(c, d.w1, d.t1, ffn, dim, c->pf_x, dim, c->pf_rr, d.ffn_norm, c->pf_hg, ffn, 0, false, n, st)))
-            break;
-        if ((e = pf_gemm(c, d.w3, d.t3, ffn, dim, c->pf_x, dim, c->pf_rr, d.ffn_norm, c->pf_hu, ffn, 0, false, n, st)))
-            break;
+        if ((e = pf_pack(c, c->pf_att, dim, nullptr, n, st))) break;
+        if ((e = pf_gemm(c, mp[3], d.wo, d.to, dim, dim, c->pf_x, dim, 0, true, n, st))) break;
+        if ((e = pf_pack(c, c->pf_x, dim, d.ffn_norm, n, st))) break;
+        if ((e = pf_gemm(c, mp[4], d.w1, d.t1, ffn, dim, c->pf_hg, ffn, 0, false, n, st))) break;
+        if ((e = pf_gemm(c, mp[6], d.w3, d.t3, ffn, dim, c->pf_hu, ffn, 0, false, n, st))) break;
         swiglu_rows_kernel<<<(n * ffn + 255) / 256, 256, 0, st>>>(c->pf_hg, c->pf_hu, (size_t)n * ffn);
         if ((e = cudaGetLastError()) != cudaSuccess) break;
-        e = pf_gemm(c, d.w2, d.t2, dim, ffn, c->pf_hg, ffn, nullptr, nullptr, c->pf_x, dim, 0, true, n, st);
+        if ((e = pf_pack(c, c->pf_hg, ffn, nullptr, n, st))) break;
+        e = pf_gemm(c, mp[5], d.w2, d.t2, dim, ffn, c->pf_x, dim, 0, true, n, st);
     }
     if (e == cudaSuccess)
         e = cudaMemcpyAsync(c->x, c->pf_x + (size_t)(n - 1) * dim, (size_t)dim * 4, cudaMemcpyDeviceToDevice, st);
@@ -1297,7 +1343,19 @@ static int prefill_batched(gpu_context *c, kv_cache_t *kv, const int32_t *tokens
         CK(cudaMalloc(&c->pf_att, T * p.dim * 4));
         CK(cudaMalloc(&c->pf_hg, T * p.ffn_dim * 4));
         CK(cudaMalloc(&c->pf_hu, T * p.ffn_dim * 4));
-        CK(cudaMalloc(&c->pf_rr, T * 4));
+        const size_t kmax = p.dim > p.ffn_dim ? p.dim : p.ffn_dim;
+        CK(cudaMalloc(&c->pf_bp, (T + G5_T - 1) / G5_T * G5_T * kmax * 4));
+        c->pf_maps.assign(7 * p.n_layers, CUtensorMap{});
+        for (uint32_t l = 0; l < p.n_layers; l++) {
+            const LayerDev &d = c->L[l];
+            CUtensorMap *mp = &c->pf_maps[7 * l];
+            const int dim = p.dim, ffn = p.ffn_dim, kvd = c->kvd;
+            if (!g5_make_map(&mp[0], d.wq, d.tq, dim, dim) || !g5_make_map(&mp[1], d.wk, d.tk, kvd, dim) ||
+                !g5_make_map(&mp[2], d.wv, d.tv, kvd, dim) || !g5_make_map(&mp[3], d.wo, d.to, dim, dim) ||
+                !g5_make_map(&mp[4], d.w1, d.t1, ffn, dim) || !g5_make_map(&mp[5], d.w2, d.t2, dim, ffn) ||
+                !g5_make_map(&mp[6], d.w3, d.t3, ffn, dim))
+                return set_err(FIBER_ECUDA, "batched prefill: cannot build the weight tensor maps");
+        }
         CK(cudaMalloc(&c->pf_tok, T * 4));
         c->pf_cap = PF_CHUNK;
     }
@@ -1613,34 +1671,49 @@ extern "C" int fiber_gemm(int ggml_type, const void *d_w, int rows, int cols, co
                           const float *d_rrms, const float *d_nw, float *d_y, int ldy, int out_off, int accumulate,
                           void *stream) {
     if (!d_w || !d_x || !d_y || rows <= 0 || ntok <= 0 || cols <= 0 || cols % 256 || ldx < cols ||
-        ldy < out_off + rows)
+        ldy < out_off + rows || ldx % 4 || ((uintptr_t)d_w & 15) || ((uintptr_t)d_x & 15) || ((uintptr_t)d_nw & 15))
         return set_err(FIBER_EARG, "fiber_gemm: bad arguments");
     if (!(ggml_type == T_Q4_K || ggml_type == T_Q6_K || ggml_type == T_F16))
         return set_err(FIBER_EUNSUPPORTED, "fiber_gemm: type %s not supported (Q4_K, Q6_K, F16)", tname(ggml_type));
     cudaStream_t st = (cudaStream_t)stream;
+    G5Params p;
+    memset(&p, 0, sizeof(p));
+    if (!g5_make_map(&p.wmap, (const uint8_t *)d_w, ggml_type, rows, cols))
+        return set_err(FIBER_ECUDA, "fiber_gemm: cannot build the weight tensor map");
     int *err = nullptr;
     CK(cudaGetSymbolAddress((void **)&err, g_g5_err));
     CK(cudaMemsetAsync(err, 0, sizeof(int), st));
-    G5Params p;
-    memset(&p, 0, sizeof(p));
+    uint8_t *bp = nullptr;
+    CK(cudaMalloc(&bp, (size_t)(ntok + G5_T - 1) / G5_T * G5_T * cols * 4));
+    G5PackParams a;
+    memset(&a, 0, sizeof(a));
+    a.x = d_x;
+    a.ldx = ldx;
+    a.ntok = ntok;
+    a.cols = cols;
+    a.rrms = d_rrms;
+    a.nw = d_nw;
+    a.bp = bp;
+    a.err = err;
     p.w = (const uint8_t *)d_w;
     p.type = ggml_type;
     p.rows = rows;
     p.cols = cols;
     p.ntok = ntok;
-    p.x = d_x;
-    p.ldx = ldx;
-    p.rrms = d_rrms;
-    p.nw = d_nw;
+    p.bp = bp;
     p.y = d_y;
     p.ldy = ldy;
     p.out_off = out_off;
     p.epi = accumulate ? G5_RESID : G5_STORE;
     p.err = err;
-    CK(launch_g5(p, st));
+    cudaError_t e = launch_g5_pack(a, st);
+    if (e == cudaSuccess) e = launch_g5(p, st);
     int h_err = 0;
-    CK(cudaMemcpyAsync(&h_err, err, sizeof(int), cudaMemcpyDeviceToHost, st));
-    CK(cudaStreamSynchronize(st));
+    if (e == cudaSuccess) e = cudaMemcpyAsync(&h_err, err, sizeof(int), cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    cudaFree(bp);
+    if (e != cudaSuccess) return set_err(FIBER_ECUDA, "fiber_gemm: %s", cudaGetErrorString(e));
+    if (h_err == 5) return set_err(FIBER_EARG, "fiber_gemm: an input value does not fit fp16");
     if (h_err) return set_err(FIBER_ETIMEOUT, "fiber_gemm: a tensor-core wait timed out");
     return FIBER_OK;
 }

@@ -4,59 +4,88 @@
 // Q6_K or F16 super-blocks, rows x cols) and ntok input rows x (fp32, optionally
 // RMS-normalised per token: xn = x * rrms[t] * nw[k]).
 //
-// One CTA computes a 128-row x 64-token tile with tcgen05.mma (kind::f16, M=128,
-// N=128, fp32 accumulators in tensor memory):
-//   * A = the weights, decoded exactly to fp16 (the reference dequantizer's
-//     arithmetic, quant.cuh) into shared memory in the canonical no-swizzle K-major
-//     layout (8x16-byte core matrices: rows 16 B apart, K halves 128 B apart, row
-//     groups 2048 B apart), 128 K columns per chunk, double buffered;
-//   * B = the inputs split into fp16 hi and lo parts (x = hi + lo to ~22 bits) as
-//     two B rows per token (n = 2t: hi, n = 2t+1: lo), same layout;
-//   * one thread issues the 8 MMAs of a chunk (K = 16 each) and commits them to the
-//     chunk buffer's mbarrier; the other threads decode / stage the next chunk;
-//   * epilogue: warps 0..3 read their 32 accumulator lanes (rows) with tcgen05.ld,
-//     add each token's hi and lo columns and store (or add to) Y.
-// Every wait is bounded (%globaltimer); on timeout the CTA records an error,
-// waits (bounded) for its committed MMAs, frees its tensor memory and returns.
+// Two kernels:
+//   * g5_pack_kernel turns the inputs once into the MMA's B operand: per 64-token
+//     tile and 128-wide K chunk a 32 KB block in the canonical no-swizzle K-major
+//     layout (8x16-byte core matrices: rows 16 B apart, K groups of 8 128 B apart,
+//     row groups 2048 B apart), two B rows per token (n = 2t: fp16 hi part, n = 2t+1:
+//     fp16 lo part, x = hi + lo to ~22 bits), RMSNorm folded in;
+//   * gemm_tc5_kernel: one CTA per 128-row x 64-token tile, tcgen05.mma (kind::f16,
+//     M = 128, N = 128, fp32 accumulators in tensor memory), warp-specialised:
+//       warp 0      producer: the raw weight rows of each K unit (a super-block
+//                   column of 128 rows: one 2D tensor copy for Q4_K / F16, one bulk
+//                   copy per row for Q6_K, whose rows are not 16-byte aligned) into a
+//                   ring of raw stages, and each chunk's packed B block (one bulk
+//                   copy) into a ring of B stages;
+//       warp 1      one lane issues the 8 MMAs (K = 16) of each chunk and commits them
+//                   to the barriers that free the B stage and the A buffer;
+//       warps 2-9   decode the chunk's weights exactly to fp16 (the reference
+//                   dequantizer's arithmetic, with the packed instructions of the
+//                   GEMV: quants -> half2 by LOP3 / byte permute, HFMA2, mixed-precision
+//                   FMA, cvt.rn.f16x2) into one of two A buffers, then run the epilogue
+//                   (tcgen05.ld, hi + lo columns added, Y stored or accumulated).
+// Inside every group of 4 K positions the decoded pairs come out as (k0, k2), (k1, k3);
+// A and B both use that order (slots 0..3 hold k0, k2, k1, k3), so the products are
+// unchanged.
+// Every wait is bounded (%globaltimer); on timeout the CTA records an error, waits
+// (bounded) for its copies and committed MMAs, frees its tensor memory and returns.
 #pragma once
-#include "quant.cuh"
+#include <cuda.h>
+
+#include "gemv_tc.cuh"
 
 namespace fiber {
+
+// Instrumentation hook (event id, chunk); compiles to nothing unless a timing harness
+// defines it before including this file.
+#ifndef G5_MARK
+#define G5_MARK(ev, c)
+#endif
 
 constexpr int G5_M = 128;        // weight rows per CTA (MMA M)
 constexpr int G5_T = 64;         // tokens per CTA (MMA N = 2 * G5_T)
 constexpr int G5_N = 2 * G5_T;
 constexpr int G5_KC = 128;       // K per chunk (8 MMAs)
-constexpr int G5_THREADS = 256;
+constexpr int G5_DW = 8;         // decoder warps
+constexpr int G5_THREADS = 64 + 32 * G5_DW;
 constexpr int G5_A_BYTES = G5_M * G5_KC * 2;  // 32 KB
-constexpr int G5_B_BYTES = G5_N * G5_KC * 2;  // 32 KB
+constexpr int G5_B_BYTES = G5_N * G5_KC * 2;  // 32 KB: one packed B block
 constexpr unsigned long long G5_WAIT_NS = 2000000000ull;
 
 enum : int { G5_STORE = 0, G5_RESID = 1 };
 
 struct G5Params {
+    CUtensorMap wmap;      // Q4_K / F16: 2D map of the weights (box 128 rows x one K unit)
     const uint8_t *w;      // weights, rows x cols in GGUF super-blocks
     int type;              // T_Q4_K / T_Q6_K / T_F16
     int rows, cols, ntok;
-    const float *x;        // [ntok][ldx]
-    int ldx;
-    const float *rrms;     // [ntok] or null
-    const float *nw;       // [cols] or null
+    const uint8_t *bp;     // packed B: [ceil(ntok / 64)][cols / 128] blocks of 32 KB
     float *y;              // [ntok][ldy]
     int ldy, out_off;
     int epi;               // G5_STORE: y = acc; G5_RESID: y += acc
     int *err;              // set to 6 when a wait gave up
 };
 
+struct G5PackParams {
+    const float *x;        // [ntok][ldx]
+    int ldx, ntok, cols;
+    const float *rrms;     // [ntok] or null: 1 / rms per token
+    const float *nw;       // [cols] or null: no normalisation
+    int own_rms;           // 1: compute rrms here (eps) instead of reading it
+    float eps;
+    uint8_t *bp;
+    int *err;              // set to 5 when a value does not fit fp16
+};
+
 FDEV uint64_t g5_desc(uint32_t saddr) {
-    // SWIZZLE_NONE K-major: start >> 4, LBO = 128 B (next K half), SBO = 2048 B
+    // SWIZZLE_NONE K-major: start >> 4, LBO = 128 B (next K group), SBO = 2048 B
     // (next 8-row group), version 1 (bits 46-47)
     return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)(128 >> 4) << 16) | ((uint64_t)(2048 >> 4) << 32) |
            (1ull << 46);
 }
 
 // kind::f16 instruction descriptor: D f32, A and B f16, both K-major, N, M
-constexpr uint32_t g5_idesc() {
+HDCE uint32_t g5_idesc() {
     return (1u << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(G5_N >> 3) << 17) | ((uint32_t)(G5_M >> 4) << 24);
 }
 
@@ -69,107 +98,224 @@ FDEV unsigned long long g5_now() {
 FDEV bool g5_try_wait(uint64_t *bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
         : "=r"(ok)
-        : "r"(g5_saddr(bar)), "r"(parity), "r"(20000u)
+        : "r"(g5_saddr(bar)), "r"(parity)
         : "memory");
     return ok != 0;
 }
-FDEV bool g5_wait(uint64_t *bar, uint32_t parity) {
+// Wait for the phase of parity `parity` to complete; gives up when another thread of
+// the CTA has failed, or after G5_WAIT_NS (then marks the CTA failed).
+FDEV bool g5_wait(uint64_t *bar, uint32_t parity, volatile int *fail) {
+    const unsigned long long t0 = g5_now();
+    while (!g5_try_wait(bar, parity)) {
+        if (*fail) return false;
+        if (g5_now() - t0 > G5_WAIT_NS) {
+            *fail = 1;
+            return false;
+        }
+    }
+    return true;
+}
+// Same, ignoring the failure flag (drains in-flight work after a failure).
+FDEV bool g5_drain(uint64_t *bar, uint32_t parity) {
     const unsigned long long t0 = g5_now();
     while (!g5_try_wait(bar, parity))
         if (g5_now() - t0 > G5_WAIT_NS) return false;
     return true;
 }
+FDEV void g5_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(g5_saddr(bar)) : "memory");
+}
+FDEV void g5_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(g5_saddr(bar)), "r"(bytes) : "memory");
+}
+FDEV void g5_bulk(void *sdst, const void *gsrc, uint32_t bytes, uint64_t *bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     g5_saddr(sdst)),
+                 "l"(gsrc), "r"(bytes), "r"(g5_saddr(bar))
+                 : "memory");
+}
+FDEV void g5_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(g5_saddr(bar))
+                 : "memory");
+}
 
-// canonical offset of (row r, k) inside a 128-K chunk tile: core matrix (r/8, k/8)
+// canonical offset of (row r, K slot k) inside a 128-K chunk tile: core matrix (r/8, k/8)
 FDEV int g5_off(int r, int k) { return ((r >> 3) * (G5_KC / 8) + (k >> 3)) * 128 + (r & 7) * 16 + (k & 7) * 2; }
 
-FDEV uint32_t g5_pack(float lo, float hi) {
-    const __half2 h = __floats2half2_rn(lo, hi);
-    return *reinterpret_cast<const uint32_t *>(&h);
+// Bytes of one row's weights per K unit in a raw stage. Q4_K: the 144-byte super-block
+// (two chunks). Q6_K: the super-block (two chunks) is 210 bytes at an even offset, so
+// the 224-byte span from the 16-byte boundary at or below it, which ends at most 14
+// bytes past the block. F16: the chunk's 128 values (256 bytes; one chunk per unit).
+template <int T>
+HDCE int g5_slot() { return T == T_Q4_K ? 144 : (T == T_Q6_K ? 224 : 256); }
+template <int T>
+HDCE int g5_cpu() { return T == T_F16 ? 1 : 2; }  // chunks per K unit
+template <int T>
+HDCE int g5_bstages() { return 3; }
+template <int T>
+HDCE int g5_rstages() { return T == T_Q4_K ? 3 : 2; }
+template <int T>
+HDCE int g5_smem() { return 2 * G5_A_BYTES + g5_bstages<T>() * G5_B_BYTES + g5_rstages<T>() * G5_M * g5_slot<T>(); }
+
+// Decode the 64 weights of row r that chunk c gives this thread (K slots 64*sub ..
+// 64*sub + 63 of the chunk) from the staged bytes `blk` into A (slot order k0 k2 k1 k3).
+template <int T>
+FDEV void g5_decode(const uint8_t *blk, int c, int sub, int r, uint8_t *A);
+
+// Q4_K: chunk c covers half c & 1 of the super-block, i.e. quarter 2 (c & 1) + sub;
+// quarter t holds sub-block 2t (low nibbles: chunk K 64 sub + l) and 2t + 1 (high
+// nibbles: 64 sub + 32 + l), l = 0..31, from the 32 quant bytes at 16 + 32 t.
+template <>
+FDEV void g5_decode<T_Q4_K>(const uint8_t *blk, int c, int sub, int r, uint8_t *A) {
+    using D = TcDot<T_Q4_K>;
+    D::Row row;
+    D::load_row(blk, 2 * (c & 1) + sub, row);
+#pragma unroll
+    for (int v = 0; v < 4; v++) {  // words 2v, 2v+1: l = 8v .. 8v+7
+        uint32_t l0, h0, l1, h1, l2, h2, l3, h3;
+        D::frags(row, 2 * v, l0, h0, l1, h1);      // (l0: k 0,2) (l1: k 1,3) low; h: high
+        D::frags(row, 2 * v + 1, l2, h2, l3, h3);  // k 4,6 / 5,7
+        *reinterpret_cast<uint4 *>(A + g5_off(r, 64 * sub + 8 * v)) = make_uint4(l0, l1, l2, l3);
+        *reinterpret_cast<uint4 *>(A + g5_off(r, 64 * sub + 32 + 8 * v)) = make_uint4(h0, h1, h2, h3);
+    }
 }
 
-// Decode half `half` (elements 128*half .. +127) of the super-block `blk` of weight row
-// r into A; this thread handles elements [64*sub, 64*sub + 64) of that half.
-template <int T>
-FDEV void g5_decode(const uint8_t *blk, int half, int sub, int r, uint8_t *A);
-
+// Q6_K: chunk c covers half h = c & 1 (128 elements: planes k = 0..3, l = 0..31,
+// element 32 k + l); this thread takes l in [16 sub, 16 sub + 16) of every plane.
 template <>
-FDEV void g5_decode<T_Q4_K>(const uint8_t *blk, int half, int sub, int r, uint8_t *A) {
-    const uint16_t *h = reinterpret_cast<const uint16_t *>(blk);
-    const float d = h2f(h[0]), dmin = h2f(h[1]);
-    uint32_t s[3];
-    for (int i = 0; i < 3; i++)
-        s[i] = (uint32_t)blk[4 + 4 * i] | ((uint32_t)blk[5 + 4 * i] << 8) | ((uint32_t)blk[6 + 4 * i] << 16) |
-               ((uint32_t)blk[7 + 4 * i] << 24);
-    const int g = 2 * half + sub;  // 64-element group: sub-blocks 2g (low nibbles), 2g+1 (high)
-    int sc0, m0, sc1, m1;
-    scale_min_k4(2 * g, s[0], s[1], s[2], sc0, m0);
-    scale_min_k4(2 * g + 1, s[0], s[1], s[2], sc1, m1);
-    const float dsc0 = __fmul_rn(d, (float)sc0), dmm0 = __fmul_rn(dmin, (float)m0);
-    const float dsc1 = __fmul_rn(d, (float)sc1), dmm1 = __fmul_rn(dmin, (float)m1);
-    const uint8_t *q = blk + 16 + 32 * g;
-    for (int l0 = 0; l0 < 32; l0 += 8) {
-        uint32_t lo[4], hi[4];
+FDEV void g5_decode<T_Q6_K>(const uint8_t *blk, int c, int sub, int r, uint8_t *A) {
+    using D = TcDot<T_Q6_K>;
+    D::Row row;
+    D::load_row(blk, 2 * (c & 1) + sub, row);
 #pragma unroll
-        for (int j = 0; j < 4; j++) {
-            const int a = q[l0 + 2 * j], b = q[l0 + 2 * j + 1];
-            lo[j] = g5_pack(q4k_weight(dsc0, dmm0, a & 15), q4k_weight(dsc0, dmm0, b & 15));
-            hi[j] = g5_pack(q4k_weight(dsc1, dmm1, a >> 4), q4k_weight(dsc1, dmm1, b >> 4));
+    for (int k = 0; k < 4; k++) {
+#pragma unroll
+        for (int v = 0; v < 2; v++) {  // words 2v, 2v+1: l = 16 sub + 8v .. +7
+            uint32_t a0, b0, a1, b1;
+            D::frags(row, 2 * v, k, a0, b0);
+            D::frags(row, 2 * v + 1, k, a1, b1);
+            *reinterpret_cast<uint4 *>(A + g5_off(r, 32 * k + 16 * sub + 8 * v)) = make_uint4(a0, b0, a1, b1);
         }
-        const int k = 64 * sub + l0;
-        *reinterpret_cast<uint4 *>(A + g5_off(r, k)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-        *reinterpret_cast<uint4 *>(A + g5_off(r, k + 32)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
     }
 }
 
+// F16: the chunk's 128 values of the row; pairs regrouped to (k0, k2), (k1, k3)
 template <>
-FDEV void g5_decode<T_Q6_K>(const uint8_t *blk, int half, int sub, int r, uint8_t *A) {
-    // the Q6_K super-block is two independent 128-element halves: chunk half = block half
-    for (int k0 = 64 * sub; k0 < 64 * sub + 64; k0 += 8) {
-        uint32_t v[4];
+FDEV void g5_decode<T_F16>(const uint8_t *blk, int c, int sub, int r, uint8_t *A) {
+    (void)c;
+    const uint4 *e = reinterpret_cast<const uint4 *>(blk) + 8 * sub;
 #pragma unroll
-        for (int j = 0; j < 4; j++)
-            v[j] = g5_pack(decode_elem<T_Q6_K>(blk, 128 * half + k0 + 2 * j),
-                           decode_elem<T_Q6_K>(blk, 128 * half + k0 + 2 * j + 1));
-        *reinterpret_cast<uint4 *>(A + g5_off(r, k0)) = make_uint4(v[0], v[1], v[2], v[3]);
+    for (int g = 0; g < 8; g++) {
+        const uint4 w = e[g];
+        *reinterpret_cast<uint4 *>(A + g5_off(r, 64 * sub + 8 * g)) =
+            make_uint4(__byte_perm(w.x, w.y, 0x5410), __byte_perm(w.x, w.y, 0x7632), __byte_perm(w.z, w.w, 0x5410),
+                       __byte_perm(w.z, w.w, 0x7632));
     }
 }
 
-template <>
-FDEV void g5_decode<T_F16>(const uint8_t *blk, int half, int sub, int r, uint8_t *A) {
-    const uint16_t *e = reinterpret_cast<const uint16_t *>(blk) + 128 * half + 64 * sub;
-    for (int k0 = 0; k0 < 64; k0 += 8) {
-        uint32_t v[4];
-#pragma unroll
-        for (int j = 0; j < 4; j++) v[j] = (uint32_t)e[k0 + 2 * j] | ((uint32_t)e[k0 + 2 * j + 1] << 16);
-        *reinterpret_cast<uint4 *>(A + g5_off(r, 64 * sub + k0)) = make_uint4(v[0], v[1], v[2], v[3]);
-    }
+// ---- input packing ----------------------------------------------------------------------
+
+// Byte offset of (B row n of token tile `tile`, K group g = k / 8) in the packed input.
+FDEV size_t g5_bp_off(int tile, int nchunk, int n, int g) {
+    return ((size_t)(tile * nchunk + (g >> 4)) << 15) + (size_t)((((n >> 3) * 16) + (g & 15)) << 7) + ((n & 7) << 4);
 }
+
+// One CTA (128 threads) per 4 tokens = one 8-row group of a token tile: optional
+// per-token 1/rms, then for every K group of 8 the hi or lo fp16 parts in slot order
+// k0 k2 k1 k3 k4 k6 k5 k7. Tokens past ntok get zero rows.
+__global__ void __launch_bounds__(128) g5_pack_kernel(const G5PackParams a) {
+    __shared__ float rr[4];
+    const int tile = blockIdx.x >> 4, grp = blockIdx.x & 15, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int t0 = tile * G5_T + 4 * grp, nchunk = a.cols / G5_KC;
+    {
+        const int t = t0 + warp;
+        float r = 1.0f;
+        if (t < a.ntok && a.nw) {
+            if (a.own_rms) {
+                const float *x = a.x + (size_t)t * a.ldx;
+                float ss = 0.f;
+                for (int i = lane; i < a.cols; i += 32) ss = fmaf(x[i], x[i], ss);
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+                r = 1.0f / sqrtf(ss / (float)a.cols + a.eps);
+            } else if (a.rrms) {
+                r = a.rrms[t];
+            }
+        }
+        if (lane == 0) rr[warp] = r;
+    }
+    __syncthreads();
+    bool bad = false;
+    for (int i = tid; i < a.cols; i += 128) {
+        const int g = i >> 3, nr = i & 7, tt = nr >> 1, t = t0 + tt;
+        uint4 out = make_uint4(0u, 0u, 0u, 0u);
+        if (t < a.ntok) {
+            const float4 *xp = reinterpret_cast<const float4 *>(a.x + (size_t)t * a.ldx + 8 * g);
+            const float4 x0 = xp[0], x1 = xp[1];
+            float v[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+            if (a.nw) {
+                const float4 n0 = reinterpret_cast<const float4 *>(a.nw + 8 * g)[0];
+                const float4 n1 = reinterpret_cast<const float4 *>(a.nw + 8 * g)[1];
+                const float nv[8] = {n0.x, n0.y, n0.z, n0.w, n1.x, n1.y, n1.z, n1.w};
+#pragma unroll
+                for (int j = 0; j < 8; j++) v[j] = __fmul_rn(__fmul_rn(v[j], rr[tt]), nv[j]);
+            }
+            uint16_t h[8];
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                bad |= !(fabsf(v[j]) < 65504.0f);
+                const __half hi = __float2half_rn(v[j]);
+                h[j] = (nr & 1) ? __half_as_ushort(__float2half_rn(v[j] - __half2float(hi))) : __half_as_ushort(hi);
+            }
+            out = make_uint4((uint32_t)h[0] | ((uint32_t)h[2] << 16), (uint32_t)h[1] | ((uint32_t)h[3] << 16),
+                             (uint32_t)h[4] | ((uint32_t)h[6] << 16), (uint32_t)h[5] | ((uint32_t)h[7] << 16));
+        }
+        *reinterpret_cast<uint4 *>(a.bp + g5_bp_off(tile, nchunk, 8 * grp + nr, g)) = out;
+    }
+    if (bad) *a.err = 5;
+}
+
+// ---- the GEMM ------------------------------------------------------------------------------
 
 template <int T>
-__global__ void __launch_bounds__(G5_THREADS, 1) gemm_tc5_kernel(const G5Params p) {
-    extern __shared__ __align__(1024) uint8_t g5_smem[];
-    __shared__ __align__(8) uint64_t done[2];
-    __shared__ uint32_t tmem_slot;
-    __shared__ int fail;
+__global__ void __launch_bounds__(G5_THREADS, 1) gemm_tc5_kernel(const __grid_constant__ G5Params p) {
     constexpr int BB = T == T_Q4_K ? 144 : (T == T_Q6_K ? 210 : 512);
-    uint8_t *A[2] = {g5_smem, g5_smem + G5_A_BYTES};
-    uint8_t *B[2] = {g5_smem + 2 * G5_A_BYTES, g5_smem + 2 * G5_A_BYTES + G5_B_BYTES};
-    uint8_t *raw = g5_smem + 2 * G5_A_BYTES + 2 * G5_B_BYTES;  // [128 rows][one super-block]
+    constexpr int S = g5_slot<T>(), CPU = g5_cpu<T>(), NB = g5_bstages<T>(), NR = g5_rstages<T>();
+    extern __shared__ __align__(1024) uint8_t g5_smem[];
+    __shared__ __align__(8) uint64_t bfull[NB], bempty[NB], rfull[NR], rempty[NR], afull[2], afree[2], accb;
+    __shared__ uint32_t tmem_slot;
+    __shared__ volatile int fail;
+    __shared__ int n_issued;
+    uint8_t *const Abuf = g5_smem;                                     // [2][G5_A_BYTES]
+    uint8_t *const Bbuf = g5_smem + 2 * G5_A_BYTES;                    // [NB][G5_B_BYTES]
+    uint8_t *const Rbuf = g5_smem + 2 * G5_A_BYTES + NB * G5_B_BYTES;  // [NR][128 rows x S]
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int row0 = blockIdx.x * G5_M, tok0 = blockIdx.y * G5_T;
-    const int nb = p.cols / 256, nchunk = p.cols / G5_KC;
-    const size_t row_bytes = (size_t)nb * BB;
+    const int row0 = blockIdx.x * G5_M, tile = blockIdx.y;
+    const int nchunk = p.cols / G5_KC;
+    const int vrows = min(G5_M, p.rows - row0);
+    const size_t row_bytes = (size_t)(p.cols / 256) * BB;
 
     if (tid == 0) {
-        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(g5_saddr(&done[0])) : "memory");
-        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(g5_saddr(&done[1])) : "memory");
+        for (int s = 0; s < NB; s++) {
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(g5_saddr(&bfull[s])) : "memory");
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(g5_saddr(&bempty[s])) : "memory");
+        }
+        for (int s = 0; s < NR; s++) {
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(g5_saddr(&rfull[s])) : "memory");
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(g5_saddr(&rempty[s])), "r"(G5_DW) : "memory");
+        }
+        for (int a = 0; a < 2; a++) {
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(g5_saddr(&afull[a])), "r"(G5_DW) : "memory");
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(g5_saddr(&afree[a])) : "memory");
+        }
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(g5_saddr(&accb)) : "memory");
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         fail = 0;
+        n_issued = 0;
     }
-    if (warp == 0) {  // 128 fp32 accumulator columns x 128 lanes
+    if (warp == 1) {  // 128 fp32 accumulator columns x 128 lanes
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(g5_saddr(&tmem_slot)),
                      "r"(G5_N)
                      : "memory");
@@ -179,123 +325,168 @@ __global__ void __launch_bounds__(G5_THREADS, 1) gemm_tc5_kernel(const G5Params 
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = tmem_slot;
+    G5_MARK(11, 0);
 
-    int issued = 0;  // chunks whose MMAs were committed
-    for (int c = 0; c < nchunk; c++) {
-        const int buf = c & 1;
-        if (c >= 2) {  // the MMAs of chunk c - 2 have read this buffer
-            if (tid == 0 && !g5_wait(&done[buf], (uint32_t)(((c - 2) >> 1) & 1))) fail = 1;
-            __syncthreads();
-            if (fail) break;
-        }
-        if ((c & 1) == 0 || G5_KC == 256) {  // raw super-block column c*128/256 of the 128 rows
-            const int b = c * G5_KC / 256;
-            __syncthreads();  // previous raw block fully decoded
-            for (int i = tid; i < G5_M * BB / 2; i += G5_THREADS) {
-                const int r = i / (BB / 2), o = i % (BB / 2);
-                uint16_t v = 0;
-                if (row0 + r < p.rows)
-                    v = reinterpret_cast<const uint16_t *>(p.w + (size_t)(row0 + r) * row_bytes + (size_t)b * BB)[o];
-                reinterpret_cast<uint16_t *>(raw + r * BB)[o] = v;
-            }
-            __syncthreads();
-        }
-        // A: decode this chunk's half of the super-block for the 128 rows
-        {
-            const int r = tid >> 1, sub = tid & 1, half = c & 1;
-            g5_decode<T>(raw + r * BB, half, sub, r, A[buf]);
-        }
-        // B: the inputs of the chunk as hi / lo rows
-        for (int i = tid; i < G5_T * (G5_KC / 8); i += G5_THREADS) {
-            const int t = i / (G5_KC / 8), k8 = (i % (G5_KC / 8)) * 8, k = c * G5_KC + k8;
-            uint32_t vh[4] = {0, 0, 0, 0}, vl[4] = {0, 0, 0, 0};
-            if (tok0 + t < p.ntok) {
-                const float *xr = p.x + (size_t)(tok0 + t) * p.ldx + k;
-                const float rr = p.rrms ? p.rrms[tok0 + t] : 1.0f;
-#pragma unroll
-                for (int j = 0; j < 4; j++) {
-                    float a = xr[2 * j], b = xr[2 * j + 1];
-                    if (p.nw) {
-                        a = __fmul_rn(__fmul_rn(a, rr), p.nw[k + 2 * j]);
-                        b = __fmul_rn(__fmul_rn(b, rr), p.nw[k + 2 * j + 1]);
+    if (warp == 0) {
+        // ---- producer: raw stage u % NR <- K unit u of the 128 rows; B stage c % NB <- the
+        // packed inputs of chunk c. Issue order: unit u before its chunks.
+        int c = 0, u = 0;
+        bool ok = true;
+        for (; c < nchunk && ok; c++) {
+            if (c % CPU == 0) {
+                const int rs = u % NR;
+                if (u >= NR) ok = g5_wait(&rempty[rs], (uint32_t)((u / NR - 1) & 1), &fail);
+                ok = __all_sync(0xffffffffu, ok);
+                if (!ok) break;
+                G5_MARK(0, c);
+                uint8_t *dst = Rbuf + rs * (G5_M * S);
+                if (T == T_Q6_K) {
+                    if (lane == 0) g5_expect_tx(&rfull[rs], (uint32_t)(vrows * S));
+                    __syncwarp();
+                    for (int r = lane; r < vrows; r += 32) {
+                        const uintptr_t src = reinterpret_cast<uintptr_t>(p.w + (size_t)(row0 + r) * row_bytes) +
+                                              (size_t)u * BB;
+                        g5_bulk(dst + r * S, reinterpret_cast<const void *>(src & ~(uintptr_t)15), (uint32_t)S,
+                                &rfull[rs]);
                     }
-                    const __half ah = __float2half_rn(a), bh = __float2half_rn(b);
-                    const __half al = __float2half_rn(a - __half2float(ah)), bl = __float2half_rn(b - __half2float(bh));
-                    vh[j] = (uint32_t)__half_as_ushort(ah) | ((uint32_t)__half_as_ushort(bh) << 16);
-                    vl[j] = (uint32_t)__half_as_ushort(al) | ((uint32_t)__half_as_ushort(bl) << 16);
+                } else if (lane == 0) {
+                    // box = 128 rows x one unit (rows past the matrix read as zeros)
+                    g5_expect_tx(&rfull[rs], (uint32_t)(G5_M * S));
+                    const int x = T == T_Q4_K ? u * 144 : u * 128;  // bytes (Q4_K) / fp16 elements (F16)
+                    asm volatile(
+                        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, "
+                        "{%2, %3}], [%4];" ::"r"(g5_saddr(dst)),
+                        "l"(reinterpret_cast<uint64_t>(&p.wmap)), "r"(x), "r"(row0), "r"(g5_saddr(&rfull[rs]))
+                        : "memory");
                 }
+                u++;
             }
-            *reinterpret_cast<uint4 *>(B[buf] + g5_off(2 * t, k8)) = make_uint4(vh[0], vh[1], vh[2], vh[3]);
-            *reinterpret_cast<uint4 *>(B[buf] + g5_off(2 * t + 1, k8)) = make_uint4(vl[0], vl[1], vl[2], vl[3]);
+            const int s = c % NB;
+            if (c >= NB) ok = g5_wait(&bempty[s], (uint32_t)((c / NB - 1) & 1), &fail);
+            ok = __all_sync(0xffffffffu, ok);
+            if (!ok) break;
+            if (lane == 0) {
+                g5_expect_tx(&bfull[s], (uint32_t)G5_B_BYTES);
+                g5_bulk(Bbuf + s * G5_B_BYTES, p.bp + ((size_t)(tile * nchunk + c) << 15), (uint32_t)G5_B_BYTES,
+                        &bfull[s]);
+            }
+            G5_MARK(1, c);
         }
-        // generic-proxy shared-memory writes -> visible to the tensor core
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        __syncthreads();
-        if (tid == 0) {
+        // every copy issued has landed before the CTA exits
+        if (lane == 0) {
+            for (int s = 0; s < NB && s < c; s++)
+                g5_drain(&bfull[s], (uint32_t)(((s + ((c - 1 - s) / NB) * NB) / NB) & 1));
+            for (int s = 0; s < NR && s < u; s++)
+                g5_drain(&rfull[s], (uint32_t)(((s + ((u - 1 - s) / NR) * NR) / NR) & 1));
+        }
+    } else if (warp == 1) {
+        // ---- MMA issuer
+        if (lane == 0) {
+            int c = 0;
+            for (; c < nchunk; c++) {
+                const int s = c % NB, a = c & 1;
+                if (!g5_wait(&bfull[s], (uint32_t)((c / NB) & 1), &fail)) break;
+                G5_MARK(6, c);
+                if (!g5_wait(&afull[a], (uint32_t)((c >> 1) & 1), &fail)) break;
+                G5_MARK(7, c);
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const uint32_t a0 = g5_saddr(Abuf + a * G5_A_BYTES), b0 = g5_saddr(Bbuf + s * G5_B_BYTES);
+#pragma unroll
+                for (int k = 0; k < G5_KC / 16; k++) {
+                    const uint64_t da = g5_desc(a0 + k * 256), db = g5_desc(b0 + k * 256);
+                    const uint32_t acc = (c > 0 || k > 0) ? 1u : 0u;
+                    asm volatile(
+                        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+                        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem),
+                        "l"(da), "l"(db), "r"(g5_idesc()), "r"(acc)
+                        : "memory");
+                }
+                g5_commit(&bempty[s]);
+                g5_commit(&afree[a]);
+                G5_MARK(8, c);
+            }
+            if (c > 0) g5_commit(&accb);  // completes when every issued MMA has
+            n_issued = c;
+        }
+    } else {
+        // ---- decoders: thread (row r, half sub of the chunk's 128 K)
+        const int i = tid - 64, r = i >> 1, sub = i & 1;
+        const int shift = T == T_Q6_K && r < vrows
+                              ? (int)((reinterpret_cast<uintptr_t>(p.w + (size_t)(row0 + r) * row_bytes)) & 15)
+                              : 0;
+        bool ok = true;
+        for (int c = 0; c < nchunk && ok; c++) {
+            const int u = c / CPU, rs = u % NR, a = c & 1;
+            ok = g5_wait(&rfull[rs], (uint32_t)((u / NR) & 1), &fail);
+            G5_MARK(2, c);
+            if (ok && c >= 2) ok = g5_wait(&afree[a], (uint32_t)(((c >> 1) - 1) & 1), &fail);
+            G5_MARK(3, c);
+            ok = __all_sync(0xffffffffu, ok);  // warp-uniform exit (the warp arrives as one)
+            if (!ok) break;
+            // Q6_K: the span starts at the 16-byte boundary at or below the block
+            const uint8_t *blk = Rbuf + rs * (G5_M * S) + r * S;
+            if (T == T_Q6_K) blk += (shift + u * BB) & 15;
+            g5_decode<T>(blk, c, sub, r, Abuf + a * G5_A_BYTES);
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor core
+            __syncwarp();
+            if (lane == 0) {
+                g5_arrive(&afull[a]);
+                if (c % CPU == CPU - 1) g5_arrive(&rempty[rs]);
+            }
+            G5_MARK(4, c);
+        }
+        // ---- epilogue: warp w reads TMEM lanes 32 (w % 4) .. +31 (= weight rows), column
+        // half (w - 2) / 4 (32 tokens x hi / lo)
+        const bool epi = ok && nchunk > 0 && g5_wait(&accb, 0u, &fail);
+        if (__all_sync(0xffffffffu, epi)) {  // tcgen05.ld needs the whole warp
+            G5_MARK(9, 0);
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            const uint32_t a0 = g5_saddr(A[buf]), b0 = g5_saddr(B[buf]);
-#pragma unroll
-            for (int s = 0; s < G5_KC / 16; s++) {
-                const uint64_t da = g5_desc(a0 + s * 256), db = g5_desc(b0 + s * 256);
-                const uint32_t acc = (c > 0 || s > 0) ? 1u : 0u;
+            const int q = warp & 3, rr = 32 * q + lane, ch = (warp - 2) >> 2;
+            for (int c0 = 64 * ch; c0 < 64 * ch + 64; c0 += 16) {
+                uint32_t v[16];
+                const uint32_t addr = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c0;
                 asm volatile(
-                    "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-                    " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem),
-                    "l"(da), "l"(db), "r"(g5_idesc()), "r"(acc)
+                    "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, "
+                    "[%16];"
+                    : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+                      "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]),
+                      "=r"(v[15])
+                    : "r"(addr)
                     : "memory");
-            }
-            asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                             g5_saddr(&done[buf]))
-                         : "memory");
-        }
-        issued = c + 1;
-    }
-    // all committed MMAs complete (a commit covers every earlier MMA of the thread)
-    if (issued > 0 && tid == 0) {
-        const int c = issued - 1;
-        if (!g5_wait(&done[c & 1], (uint32_t)((c >> 1) & 1))) fail = 1;
-    }
-    __syncthreads();
-    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    if (fail) {
-        if (tid == 0) *p.err = 6;
-    } else if (warp < 4) {
-        // lanes 32*warp .. +31 = weight rows; 16 columns (8 tokens) per load
-        const int r = warp * 32 + lane;
-        for (int c0 = 0; c0 < G5_N; c0 += 16) {
-            uint32_t v[16];
-            const uint32_t addr = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0;
-            asm volatile(
-                "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-                : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
-                  "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]),
-                  "=r"(v[15])
-                : "r"(addr)
-                : "memory");
-            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-            if (row0 + r < p.rows) {
+                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                if (rr < vrows) {
 #pragma unroll
-                for (int j = 0; j < 8; j++) {
-                    const int t = tok0 + c0 / 2 + j;
-                    if (t < p.ntok) {
-                        const float y = __fadd_rn(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1]));
-                        float *dst = p.y + (size_t)t * p.ldy + p.out_off + row0 + r;
-                        *dst = p.epi == G5_RESID ? __fadd_rn(*dst, y) : y;
+                    for (int j = 0; j < 8; j++) {
+                        const int t = tile * G5_T + c0 / 2 + j;
+                        if (t < p.ntok) {
+                            const float y = __fadd_rn(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1]));
+                            float *dst = p.y + (size_t)t * p.ldy + p.out_off + row0 + rr;
+                            *dst = p.epi == G5_RESID ? __fadd_rn(*dst, y) : y;
+                        }
                     }
                 }
             }
         }
     }
+    G5_MARK(10, 0);
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
-    if (warp == 0) {
+    if (fail) {
+        // let the committed MMAs finish before the tensor memory is released
+        if (tid == 0) {
+            if (n_issued > 0) g5_drain(&accb, 0u);
+            *p.err = 6;
+        }
+        __syncthreads();
+    }
+    if (warp == 1) {
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(G5_N) : "memory");
     }
 }
 
-constexpr int g5_smem_bytes(int type) {
-    return 2 * G5_A_BYTES + 2 * G5_B_BYTES + G5_M * (type == T_Q4_K ? 144 : (type == T_Q6_K ? 210 : 512));
+HDCE int g5_smem_bytes(int type) {
+    return type == T_Q4_K ? g5_smem<T_Q4_K>() : type == T_Q6_K ? g5_smem<T_Q6_K>() : g5_smem<T_F16>();
 }
 
 }  // namespace fiber

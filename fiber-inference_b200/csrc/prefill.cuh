@@ -1,9 +1,9 @@
 // prefill.cuh — the non-GEMM kernels of the batched prefill (a prompt chunk of n
 // tokens at positions start .. start + n - 1 in one pass per layer). The
 // projections run on the tensor cores (gemm_tc5.cuh); these kernels do the
-// per-token parts with the decode path's arithmetic:
+// per-token parts with the decode path's arithmetic (the RMSNorms are folded into the
+// GEMM's input packing):
 //   embed_rows_kernel   embedding rows of the n tokens (fp16-rounded, as gpu_embed)
-//   rms_rows_kernel     per-token 1/sqrt(mean(x^2) + eps) (the GEMM applies it)
 //   rope_kv_kernel      half-split RoPE of q (in place) and k; K/V appended (fp16)
 //   attn_prefill_kernel causal GQA attention of each token over the cache
 //   swiglu_rows_kernel  h = silu(gate) * up
@@ -32,22 +32,6 @@ __global__ void embed_rows_kernel(const uint8_t *__restrict__ tab, const int32_t
             v = round_f16(decode_elem<T>(tab + ((size_t)tok * (dim >> 8) + (i >> 8)) * BB, i & 255));
         }
         X[(size_t)t * dim + i] = v;
-    }
-}
-
-__global__ void rms_rows_kernel(const float *__restrict__ X, int dim, float eps, float *rr) {
-    __shared__ float part[32];
-    const float *x = X + (size_t)blockIdx.x * dim;
-    float ss = 0.f;
-    for (int i = threadIdx.x; i < dim; i += blockDim.x) ss = fmaf(x[i], x[i], ss);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ss;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        float s = 0.f;
-        for (int w = 0; w < (int)(blockDim.x >> 5); w++) s += part[w];
-        rr[blockIdx.x] = 1.0f / sqrtf(s / (float)dim + eps);
     }
 }
 

@@ -14,7 +14,9 @@ import numpy as np
 from . import CUDA_SO, ModelParams  # noqa: F401
 
 __all__ = ["FiberError", "cuda_lib", "cuda_available", "gemv", "gemv_host", "gemv_argmax_noalloc", "dequant", "Context", "KVCache",
-           "device_count", "TPPlan", "TP_ID_BYTES", "tp_plan", "tp_unique_id", "gemm"]
+           "device_count", "TPPlan", "TP_ID_BYTES", "tp_plan", "tp_unique_id", "gemm", "PREFILL_CHUNK"]
+
+PREFILL_CHUNK = 512  # FIBER_PREFILL_CHUNK: tokens per pass of the batched prefill
 
 F32P = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
 I32P = np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS")

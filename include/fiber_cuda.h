@@ -76,8 +76,11 @@ int fiber_decode_greedy(fiber_ctx_t *ctx, kv_cache_t *kv, int32_t first_token, i
  * does not cover (Q5_K weights). Returns FIBER_EUNSUPPORTED for mode 0 then. */
 int fiber_set_decode_mode(fiber_ctx_t *ctx, int mode);
 
-/* Prefill path of fiber_prefill: 0 (default) = batched, the prompt in chunks of 128
- * tokens through tensor-core dequant-GEMMs (tcgen05) with causal attention over the
+/* Tokens per pass of the batched prefill through the layer stack. */
+#define FIBER_PREFILL_CHUNK 512
+
+/* Prefill path of fiber_prefill: 0 (default) = batched, the prompt in chunks of
+ * FIBER_PREFILL_CHUNK tokens through tensor-core dequant-GEMMs (tcgen05) with causal attention over the
  * cache, when every matrix is Q4_K / Q6_K / F16 and the context is not sharded;
  * 1 = one decode step per token. Both fill the same KV cache and return the first
  * generated token. */
@@ -153,10 +156,14 @@ int fiber_gemv(int ggml_type, const void *d_w, const float *d_x, float *d_y, int
                void *stream);
 /* Tensor-core dequant-GEMM (the prefill building block; tcgen05, fp32 accumulation):
  * y[t][out_off + r] = (accumulate ? y[t][out_off + r] : 0) + sum_k W[r,k] * xn[t][k]
- * for t < ntok, with xn = x * rrms[t] * nw[k] when d_rrms/d_nw are given (RMSNorm
- * folded in) and xn = x otherwise. W: Q4_K / Q6_K / F16 super-blocks, cols % 256 == 0;
- * x: [ntok][ldx] fp32; y: [ntok][ldy] fp32. The weights are decoded exactly as the
- * GEMV does; x is split into fp16 hi + lo parts. Synchronizes the stream. */
+ * for t < ntok, with xn = x * rrms[t] * nw[k] when d_nw is given (RMSNorm folded
+ * in; rrms taken as 1 when d_rrms is null) and xn = x otherwise. W: Q4_K / Q6_K / F16
+ * super-blocks, cols % 256 == 0; x: [ntok][ldx] fp32; y: [ntok][ldy] fp32. The
+ * weights are decoded exactly as the GEMV does; xn is split into fp16 hi + lo parts
+ * and must stay below 65504 in magnitude (else FIBER_EARG). d_w, d_x and d_nw must
+ * be 16-byte aligned and ldx a multiple of 4; Q6_K rows are read through
+ * 16-byte-aligned spans, so 14 bytes after the last block must be readable.
+ * Allocates a packed copy of x for the call and synchronizes the stream. */
 int fiber_gemm(int ggml_type, const void *d_w, int rows, int cols, const float *d_x, int ntok, int ldx,
                const float *d_rrms, const float *d_nw, float *d_y, int ldy, int out_off, int accumulate,
                void *stream);

@@ -29,7 +29,9 @@ def _weights(t, rows, cols, seed):
         return _dev(w.view(np.uint8).reshape(-1)), w.astype(np.float64)
     blocks = fb.random_blocks(t, rows, cols, seed=seed)
     w = orc.dequant_f16(t, blocks, rows, cols).astype(np.float64)
-    return _dev(blocks), w
+    # Q6_K rows are read through 16-byte-aligned spans: keep 14+ readable bytes after
+    padded = np.concatenate([np.asarray(blocks, dtype=np.uint8).reshape(-1), np.zeros(256, np.uint8)])
+    return _dev(padded), w
 
 
 @pytest.mark.parametrize("t", [fb.GGML_Q4_K, fb.GGML_Q6_K, fb.GGML_F16])
