@@ -394,6 +394,14 @@ struct gpu_context {
     uint8_t *pf_bp = nullptr;          // GEMM input packed as the MMA's B operand (hi / lo fp16)
     std::vector<CUtensorMap> pf_maps;  // per layer: tensor maps of wq wk wv wo w1 w2 w3
     int32_t *pf_tok = nullptr;
+    // batched decode: max_batch sequences per step, sequence t in KV slot t
+    int max_batch = 1;
+    CUtensorMap out_map;               // tensor map of the classifier (lm_head GEMM)
+    int32_t *bt_pos = nullptr, *bt_arg = nullptr, *bt_rec = nullptr;  // [max_batch], [max_batch], [max_seq][max_batch]
+    int *bt_step = nullptr;
+    float *bt_logits = nullptr;        // [max_batch][vocab]
+    Graph g_batch;                     // captured greedy batch step (g_batch_n sequences)
+    int g_batch_n = 0;
 };
 
 static void free_graph(Graph &g) {
@@ -408,8 +416,9 @@ extern "C" void fiber_cuda_free(fiber_ctx_t *c) {
     if (c->stream) cudaStreamSynchronize(c->stream);
     free_graph(c->g_step);
     free_graph(c->g_loop);
+    free_graph(c->g_batch);
     if (c->comm) ncclCommDestroy(c->comm);
-    void *dev[] = {c->pf_x, c->pf_qkv, c->pf_att, c->pf_hg, c->pf_hu, c->pf_bp, c->pf_tok, c->x2, c->d_shard, c->d_data, c->x, c->qkv, c->att, c->h, c->logits, c->rope, c->io, c->rec,
+    void *dev[] = {c->bt_pos, c->bt_arg, c->bt_rec, c->bt_step, c->bt_logits, c->pf_x, c->pf_qkv, c->pf_att, c->pf_hg, c->pf_hu, c->pf_bp, c->pf_tok, c->x2, c->d_shard, c->d_data, c->x, c->qkv, c->att, c->h, c->logits, c->rope, c->io, c->rec,
                    c->att_part, c->att_cnt, c->am_part, c->am_cnt, c->d_phases, c->d_bar,
                    c->pk_gf[0], c->pk_gf[1], c->pk_gf[2], c->pk_gf[3], c->pk_ss[0], c->pk_ss[1]};
     for (void *p : dev)
@@ -840,13 +849,15 @@ extern "C" int fiber_tp_info(fiber_ctx_t *c, fiber_tp_plan_t *out) {
     return FIBER_OK;
 }
 
+static bool batched_ok(const gpu_context *c);
+
 extern "C" fiber_ctx_t *fiber_cuda_init(const model_t *m, int device, int max_batch, int max_seq) {
     if (!m || !m->layers) {
         set_err(FIBER_EARG, "fiber_cuda_init: no model");
         return nullptr;
     }
-    if (max_batch != 1) {
-        set_err(FIBER_EUNSUPPORTED, "fiber_cuda_init: max_batch %d (only 1 is implemented)", max_batch);
+    if (max_batch < 1 || max_batch > FIBER_MAX_BATCH) {
+        set_err(FIBER_EARG, "fiber_cuda_init: max_batch %d outside [1, %d]", max_batch, FIBER_MAX_BATCH);
         return nullptr;
     }
     if (max_seq <= 0) max_seq = (int)m->params.context_length;
@@ -856,6 +867,13 @@ extern "C" fiber_ctx_t *fiber_cuda_init(const model_t *m, int device, int max_ba
         fiber_cuda_free(c);
         return nullptr;
     }
+    if (max_batch > 1 && !batched_ok(c)) {
+        set_err(FIBER_EUNSUPPORTED,
+                "fiber_cuda_init: batched decode needs Q4_K/Q5_K/Q6_K/F16 matrices, 16-byte aligned, GQA group <= 8");
+        fiber_cuda_free(c);
+        return nullptr;
+    }
+    c->max_batch = max_batch;
     return c;
 }
 
@@ -1127,10 +1145,13 @@ static int device_status(gpu_context *c) {
     return FIBER_OK;
 }
 
+static int forward_batch(gpu_context *c, kv_cache_t *kv, const int32_t *tokens, const int32_t *pos, int batch,
+                         float *logits_or_null, int32_t *argmax_or_null);
+
 extern "C" int fiber_forward_token(fiber_ctx_t *c, kv_cache_t *kv, const int32_t *tokens, const int32_t *pos,
                                    int batch, float *logits_or_null, int32_t *argmax_or_null) {
     if (!c || !tokens || !pos) return set_err(FIBER_EARG, "fiber_forward_token: null argument");
-    if (batch != 1) return set_err(FIBER_EUNSUPPORTED, "fiber_forward_token: batch %d (only 1 is implemented)", batch);
+    if (batch != 1) return forward_batch(c, kv, tokens, pos, batch, logits_or_null, argmax_or_null);
     int rc = check_kv(c, kv);
     if (rc) return rc;
     const int lim = c->max_seq < kv->max_seq ? c->max_seq : kv->max_seq;
@@ -1158,11 +1179,13 @@ constexpr int PF_CHUNK = FIBER_PREFILL_CHUNK;  // tokens per pass of the layer s
 
 static cudaError_t launch_g5(const G5Params &p, cudaStream_t st);
 
-static bool g5_type_ok(int t) { return t == T_Q4_K || t == T_Q6_K || t == T_F16; }
+static bool g5_type_ok(int t) { return t == T_Q4_K || t == T_Q5_K || t == T_Q6_K || t == T_F16; }
 
-static bool prefill_batched_ok(const gpu_context *c) {
-    if (c->tp_world != 1 || c->prefill_mode != 0) return false;
-    if (!g5_type_ok(c->t_out) || c->G > 8) return false;
+// The batched layer pass (tensor-core GEMMs) covers this model: prefill chunks and
+// batched decode steps.
+static bool batched_ok(const gpu_context *c) {
+    if (c->tp_world != 1) return false;
+    if (!g5_type_ok(c->t_out) || c->G > 8 || ((uintptr_t)c->out & 15)) return false;
     for (const LayerDev &d : c->L) {
         const int ts[7] = {d.tq, d.tk, d.tv, d.to, d.t1, d.t2, d.t3};
         for (int t : ts)
@@ -1174,6 +1197,8 @@ static bool prefill_batched_ok(const gpu_context *c) {
     }
     return true;
 }
+
+static bool prefill_batched_ok(const gpu_context *c) { return c->prefill_mode == 0 && batched_ok(c); }
 
 template <int HD, int G>
 static cudaError_t launch_attn_prefill_t(const AttnPrefillParams &a, int n, cudaStream_t st) {
@@ -1206,11 +1231,11 @@ static cudaError_t launch_embed_rows(const gpu_context *c, const int32_t *tok, f
     return cudaGetLastError();
 }
 
-// 2D tensor map over a Q4_K (bytes) or F16 (fp16 elements) weight matrix with a box of
-// 128 rows x one K unit (a super-block / 128 values); other types need none.
+// 2D tensor map over a Q4_K / Q5_K (bytes) or F16 (fp16 elements) weight matrix with a
+// box of 128 rows x one K unit (a super-block / 128 values); Q6_K needs none.
 static bool g5_make_map(CUtensorMap *map, const uint8_t *w, int type, int rows, int cols) {
     memset(map, 0, sizeof(*map));
-    if (type != T_Q4_K && type != T_F16) return true;
+    if (type != T_Q4_K && type != T_Q5_K && type != T_F16) return true;
     static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
     if (!encode) {
         void *fn = nullptr;
@@ -1221,11 +1246,12 @@ static bool g5_make_map(CUtensorMap *map, const uint8_t *w, int type, int rows, 
             return false;
         encode = (PFN_cuTensorMapEncodeTiled_v12000)fn;
     }
-    const bool q4 = type == T_Q4_K;
-    const cuuint64_t row_bytes = q4 ? (cuuint64_t)cols / 256 * 144 : (cuuint64_t)cols * 2;
+    const bool q4 = type != T_F16;  // byte elements, one super-block per box row
+    const cuuint32_t bb = type == T_Q4_K ? 144u : 176u;
+    const cuuint64_t row_bytes = q4 ? (cuuint64_t)cols / 256 * bb : (cuuint64_t)cols * 2;
     const cuuint64_t dims[2] = {q4 ? row_bytes : (cuuint64_t)cols, (cuuint64_t)rows};
     const cuuint64_t strides[1] = {row_bytes};
-    const cuuint32_t box[2] = {q4 ? 144u : 128u, (cuuint32_t)G5_M};
+    const cuuint32_t box[2] = {q4 ? bb : 128u, (cuuint32_t)G5_M};
     const cuuint32_t estr[2] = {1, 1};
     return encode(map, q4 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, (void *)w, dims, strides,
                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
@@ -1273,14 +1299,14 @@ static cudaError_t pf_gemm(gpu_context *c, const CUtensorMap &map, const uint8_t
     return launch_g5(g, st);
 }
 
-// Layers of the model over `n` prompt tokens at positions start .. start + n - 1:
-// embedding rows, then per layer RMSNorm + packing of the input, QKV GEMMs, RoPE +
-// KV append, causal attention, Wo GEMM (+residual), RMSNorm + packing, gate/up GEMMs,
-// SwiGLU, down GEMM (+residual). Leaves the last token's hidden state in c->x.
-static cudaError_t enqueue_prefill_chunk(gpu_context *c, const kv_cache_t *kv, int n, int start, cudaStream_t st) {
+// The layers over `n` tokens whose hidden states are in c->pf_x, each at its place
+// (position, KV slot): per layer RMSNorm + packing of the input, QKV GEMMs, RoPE + KV
+// append, causal attention, Wo GEMM (+residual), RMSNorm + packing, gate/up GEMMs,
+// SwiGLU, down GEMM (+residual).
+static cudaError_t enqueue_layers(gpu_context *c, const kv_cache_t *kv, int n, const TokenPlace &at, cudaStream_t st) {
     const model_params_t &p = c->p;
     const int dim = p.dim, ffn = p.ffn_dim, hd = p.head_dim, kvd = c->kvd, ldq = dim + 2 * kvd;
-    cudaError_t e = launch_embed_rows(c, c->pf_tok, c->pf_x, n, st);
+    cudaError_t e = cudaSuccess;
     for (uint32_t l = 0; l < p.n_layers && e == cudaSuccess; l++) {
         const LayerDev &d = c->L[l];
         const CUtensorMap *mp = &c->pf_maps[7 * l];
@@ -1291,7 +1317,7 @@ static cudaError_t enqueue_prefill_chunk(gpu_context *c, const kv_cache_t *kv, i
         RopeKvParams rk;
         rk.qkv = c->pf_qkv;
         rk.ldq = ldq;
-        rk.start = start;
+        rk.at = at;
         rk.rope = c->rope;
         rk.n_heads = p.n_heads;
         rk.n_kv = p.n_kv_heads;
@@ -1308,7 +1334,7 @@ static cudaError_t enqueue_prefill_chunk(gpu_context *c, const kv_cache_t *kv, i
         ap.ldq = ldq;
         ap.out = c->pf_att;
         ap.ldo = dim;
-        ap.start = start;
+        ap.at = at;
         ap.k_pool = kv->k_pool;
         ap.v_pool = kv->v_pool;
         ap.page_table = kv->page_table;
@@ -1328,43 +1354,105 @@ static cudaError_t enqueue_prefill_chunk(gpu_context *c, const kv_cache_t *kv, i
         if ((e = pf_pack(c, c->pf_hg, ffn, nullptr, n, st))) break;
         e = pf_gemm(c, mp[5], d.w2, d.t2, dim, ffn, c->pf_x, dim, 0, true, n, st);
     }
-    if (e == cudaSuccess)
-        e = cudaMemcpyAsync(c->x, c->pf_x + (size_t)(n - 1) * dim, (size_t)dim * 4, cudaMemcpyDeviceToDevice, st);
     return e;
 }
 
-static int prefill_batched(gpu_context *c, kv_cache_t *kv, const int32_t *tokens, int n, int start_pos,
-                           int32_t *argmax_out) {
-    const model_params_t &p = c->p;
-    if (!c->pf_cap) {
-        const size_t T = PF_CHUNK;
-        CK(cudaMalloc(&c->pf_x, T * p.dim * 4));
-        CK(cudaMalloc(&c->pf_qkv, T * (p.dim + 2 * c->kvd) * 4));
-        CK(cudaMalloc(&c->pf_att, T * p.dim * 4));
-        CK(cudaMalloc(&c->pf_hg, T * p.ffn_dim * 4));
-        CK(cudaMalloc(&c->pf_hu, T * p.ffn_dim * 4));
-        const size_t kmax = p.dim > p.ffn_dim ? p.dim : p.ffn_dim;
-        CK(cudaMalloc(&c->pf_bp, (T + G5_T - 1) / G5_T * G5_T * kmax * 4));
-        c->pf_maps.assign(7 * p.n_layers, CUtensorMap{});
-        for (uint32_t l = 0; l < p.n_layers; l++) {
-            const LayerDev &d = c->L[l];
-            CUtensorMap *mp = &c->pf_maps[7 * l];
-            const int dim = p.dim, ffn = p.ffn_dim, kvd = c->kvd;
-            if (!g5_make_map(&mp[0], d.wq, d.tq, dim, dim) || !g5_make_map(&mp[1], d.wk, d.tk, kvd, dim) ||
-                !g5_make_map(&mp[2], d.wv, d.tv, kvd, dim) || !g5_make_map(&mp[3], d.wo, d.to, dim, dim) ||
-                !g5_make_map(&mp[4], d.w1, d.t1, ffn, dim) || !g5_make_map(&mp[5], d.w2, d.t2, dim, ffn) ||
-                !g5_make_map(&mp[6], d.w3, d.t3, ffn, dim))
-                return set_err(FIBER_ECUDA, "batched prefill: cannot build the weight tensor maps");
-        }
-        CK(cudaMalloc(&c->pf_tok, T * 4));
-        c->pf_cap = PF_CHUNK;
+static TokenPlace place_of(gpu_context *c, const kv_cache_t *kv) {
+    TokenPlace at;
+    memset(&at, 0, sizeof(at));
+    at.max_pages = kv->max_pages_per_seq;
+    at.max_pos = c->max_seq < kv->max_seq ? c->max_seq : kv->max_seq;
+    at.err = &c->io->err;
+    return at;
+}
+
+// A prompt chunk of `n` tokens (c->pf_tok) of KV slot `slot` at positions start ..:
+// embedding rows and the layers; leaves the last token's hidden state in c->x.
+static cudaError_t enqueue_prefill_chunk(gpu_context *c, const kv_cache_t *kv, int n, int start, int slot,
+                                         cudaStream_t st) {
+    TokenPlace at = place_of(c, kv);
+    at.start = start;
+    at.slot = slot;
+    cudaError_t e = launch_embed_rows(c, c->pf_tok, c->pf_x, n, st);
+    if (e == cudaSuccess) e = enqueue_layers(c, kv, n, at, st);
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(c->x, c->pf_x + (size_t)(n - 1) * c->p.dim, (size_t)c->p.dim * 4,
+                            cudaMemcpyDeviceToDevice, st);
+    return e;
+}
+
+// One greedy decode step of `n` sequences: token c->pf_tok[t] at position c->bt_pos[t]
+// of KV slot t. Embedding rows, the layers, final RMSNorm + the classifier as one GEMM
+// over the n rows (c->bt_logits), argmax per row (c->bt_arg). `loop` feeds the argmax
+// back as the next tokens, advances the positions and records the tokens.
+static cudaError_t enqueue_batch_step(gpu_context *c, const kv_cache_t *kv, int n, bool loop, cudaStream_t st) {
+    const int dim = c->p.dim, V = c->p.vocab_size;
+    TokenPlace at = place_of(c, kv);
+    at.pos = c->bt_pos;
+    at.slot_step = 1;
+    cudaError_t e = launch_embed_rows(c, c->pf_tok, c->pf_x, n, st);
+    if (e == cudaSuccess) e = enqueue_layers(c, kv, n, at, st);
+    if (e == cudaSuccess) e = pf_pack(c, c->pf_x, dim, c->out_norm, n, st);
+    if (e == cudaSuccess) e = pf_gemm(c, c->out_map, c->out, c->t_out, V, dim, c->bt_logits, V, 0, false, n, st);
+    if (e == cudaSuccess) {
+        argmax_rows_kernel<<<n, 256, 0, st>>>(c->bt_logits, V, V, c->bt_arg);
+        e = cudaGetLastError();
     }
+    if (e == cudaSuccess && loop) {
+        batch_advance_kernel<<<1, 64, 0, st>>>(c->bt_arg, c->pf_tok, c->bt_pos, c->bt_rec, c->bt_step, n);
+        e = cudaGetLastError();
+    }
+    return e;
+}
+
+// Buffers and tensor maps of the batched layer pass, made on first use.
+static int pf_alloc(gpu_context *c) {
+    if (c->pf_cap) return FIBER_OK;
+    const model_params_t &p = c->p;
+    const size_t T = PF_CHUNK;
+    CK(cudaMalloc(&c->pf_x, T * p.dim * 4));
+    CK(cudaMalloc(&c->pf_qkv, T * (p.dim + 2 * c->kvd) * 4));
+    CK(cudaMalloc(&c->pf_att, T * p.dim * 4));
+    CK(cudaMalloc(&c->pf_hg, T * p.ffn_dim * 4));
+    CK(cudaMalloc(&c->pf_hu, T * p.ffn_dim * 4));
+    const size_t kmax = p.dim > p.ffn_dim ? p.dim : p.ffn_dim;
+    CK(cudaMalloc(&c->pf_bp, (T + G5_T - 1) / G5_T * G5_T * kmax * 4));
+    CK(cudaMalloc(&c->pf_tok, T * 4));
+    const size_t B = c->max_batch;
+    CK(cudaMalloc(&c->bt_pos, B * 4));
+    CK(cudaMalloc(&c->bt_arg, B * 4));
+    CK(cudaMalloc(&c->bt_rec, B * c->max_seq * 4));
+    CK(cudaMalloc(&c->bt_step, sizeof(int)));
+    CK(cudaMalloc(&c->bt_logits, B * p.vocab_size * 4));
+    c->pf_maps.assign(7 * p.n_layers, CUtensorMap{});
+    const int dim = p.dim, ffn = p.ffn_dim, kvd = c->kvd;
+    for (uint32_t l = 0; l < p.n_layers; l++) {
+        const LayerDev &d = c->L[l];
+        CUtensorMap *mp = &c->pf_maps[7 * l];
+        if (!g5_make_map(&mp[0], d.wq, d.tq, dim, dim) || !g5_make_map(&mp[1], d.wk, d.tk, kvd, dim) ||
+            !g5_make_map(&mp[2], d.wv, d.tv, kvd, dim) || !g5_make_map(&mp[3], d.wo, d.to, dim, dim) ||
+            !g5_make_map(&mp[4], d.w1, d.t1, ffn, dim) || !g5_make_map(&mp[5], d.w2, d.t2, dim, ffn) ||
+            !g5_make_map(&mp[6], d.w3, d.t3, ffn, dim))
+            return set_err(FIBER_ECUDA, "batched layer pass: cannot build the weight tensor maps");
+    }
+    if (!g5_make_map(&c->out_map, c->out, c->t_out, (int)p.vocab_size, dim))
+        return set_err(FIBER_ECUDA, "batched layer pass: cannot build the classifier tensor map");
+    c->pf_cap = PF_CHUNK;
+    return FIBER_OK;
+}
+
+
+
+static int prefill_batched(gpu_context *c, kv_cache_t *kv, int slot, const int32_t *tokens, int n, int start_pos,
+                           int32_t *argmax_out) {
+    int rc = pf_alloc(c);
+    if (rc) return rc;
     c->h_io->err = 0;
     CK(cudaMemcpyAsync(c->io, c->h_io, sizeof(StepIO), cudaMemcpyHostToDevice, c->stream));
     for (int i = 0; i < n; i += c->pf_cap) {
         const int m = std::min(c->pf_cap, n - i);
         CK(cudaMemcpyAsync(c->pf_tok, tokens + i, (size_t)m * 4, cudaMemcpyHostToDevice, c->stream));
-        cudaError_t e = enqueue_prefill_chunk(c, kv, m, start_pos + i, c->stream);
+        cudaError_t e = enqueue_prefill_chunk(c, kv, m, start_pos + i, slot, c->stream);
         if (e != cudaSuccess) return set_err(FIBER_ECUDA, "batched prefill: %s", cudaGetErrorString(e));
         CK(cudaStreamSynchronize(c->stream));  // pf_tok is reused by the next chunk
     }
@@ -1373,8 +1461,7 @@ static int prefill_batched(gpu_context *c, kv_cache_t *kv, const int32_t *tokens
     CK(cudaMemcpyAsync(c->h_io, c->io, sizeof(StepIO), cudaMemcpyDeviceToHost, c->stream));
     CK(cudaStreamSynchronize(c->stream));
     if (c->h_io->err == 6) return set_err(FIBER_ETIMEOUT, "batched prefill: a tensor-core wait timed out");
-    int rc = device_status(c);
-    if (rc) return rc;
+    if ((rc = device_status(c))) return rc;
     if (argmax_out) *argmax_out = c->h_io->argmax;
     return FIBER_OK;
 }
@@ -1385,20 +1472,26 @@ extern "C" int fiber_set_prefill_mode(fiber_ctx_t *c, int mode) {
     return FIBER_OK;
 }
 
+static int prefill_checks(gpu_context *c, kv_cache_t *kv, const int32_t *tokens, int n, int start_pos) {
+    int rc = check_kv(c, kv);
+    if (rc) return rc;
+    const int lim = c->max_seq < kv->max_seq ? c->max_seq : kv->max_seq;
+    if (start_pos < 0 || start_pos + n > lim)
+        return set_err(FIBER_EARG, "prefill positions %d..%d outside [0, %d)", start_pos, start_pos + n - 1, lim);
+    for (int i = 0; i < n; i++)
+        if (tokens[i] < 0 || tokens[i] >= (int)c->p.vocab_size)
+            return set_err(FIBER_EARG, "token %d out of range", tokens[i]);
+    return FIBER_OK;
+}
+
 extern "C" int fiber_prefill(fiber_ctx_t *c, kv_cache_t *kv, const int32_t *tokens, int n, int start_pos,
                              int32_t *argmax_out) {
     if (!c || !tokens || n <= 0) return set_err(FIBER_EARG, "fiber_prefill: empty prompt");
     if (n > 1 && prefill_batched_ok(c)) {
-        int rc = check_kv(c, kv);
+        int rc = prefill_checks(c, kv, tokens, n, start_pos);
         if (rc) return rc;
-        const int lim = c->max_seq < kv->max_seq ? c->max_seq : kv->max_seq;
-        if (start_pos < 0 || start_pos + n > lim)
-            return set_err(FIBER_EARG, "prefill positions %d..%d outside [0, %d)", start_pos, start_pos + n - 1, lim);
-        for (int i = 0; i < n; i++)
-            if (tokens[i] < 0 || tokens[i] >= (int)c->p.vocab_size)
-                return set_err(FIBER_EARG, "token %d out of range", tokens[i]);
         CK(cudaSetDevice(c->device));
-        return prefill_batched(c, kv, tokens, n, start_pos, argmax_out);
+        return prefill_batched(c, kv, 0, tokens, n, start_pos, argmax_out);
     }
     for (int i = 0; i < n; i++) {
         const int32_t pos = start_pos + i;
@@ -1406,6 +1499,107 @@ extern "C" int fiber_prefill(fiber_ctx_t *c, kv_cache_t *kv, const int32_t *toke
         if (rc) return rc;
     }
     return FIBER_OK;
+}
+
+extern "C" int fiber_prefill_slot(fiber_ctx_t *c, kv_cache_t *kv, int slot, const int32_t *tokens, int n,
+                                  int start_pos, int32_t *argmax_out) {
+    if (!c || !tokens || n <= 0) return set_err(FIBER_EARG, "fiber_prefill_slot: empty prompt");
+    if (!kv || slot < 0 || slot >= kv->max_batch) return set_err(FIBER_EARG, "fiber_prefill_slot: no slot %d", slot);
+    if (!batched_ok(c)) return set_err(FIBER_EUNSUPPORTED, "fiber_prefill_slot: the batched layer pass does not cover this model");
+    int rc = prefill_checks(c, kv, tokens, n, start_pos);
+    if (rc) return rc;
+    CK(cudaSetDevice(c->device));
+    return prefill_batched(c, kv, slot, tokens, n, start_pos, argmax_out);
+}
+
+// ---- batched decode -------------------------------------------------------------------
+
+static int batch_checks(gpu_context *c, kv_cache_t *kv, const int32_t *tokens, const int32_t *pos, int batch,
+                        int n_steps) {
+    if (!tokens || !pos) return set_err(FIBER_EARG, "batched decode: null argument");
+    if (batch < 1 || batch > c->max_batch)
+        return set_err(FIBER_EARG, "batch %d outside [1, max_batch %d]", batch, c->max_batch);
+    int rc = check_kv(c, kv);
+    if (rc) return rc;
+    if (batch > kv->max_batch) return set_err(FIBER_EARG, "batch %d exceeds the KV cache's %d slots", batch, kv->max_batch);
+    const int lim = c->max_seq < kv->max_seq ? c->max_seq : kv->max_seq;
+    for (int t = 0; t < batch; t++) {
+        if (pos[t] < 0 || pos[t] + n_steps > lim)
+            return set_err(FIBER_EARG, "sequence %d: positions %d..%d outside [0, %d)", t, pos[t], pos[t] + n_steps - 1,
+                           lim);
+        if (tokens[t] < 0 || tokens[t] >= (int)c->p.vocab_size)
+            return set_err(FIBER_EARG, "sequence %d: token %d out of range", t, tokens[t]);
+    }
+    return FIBER_OK;
+}
+
+static int batch_status(gpu_context *c) {
+    if (c->h_io->err == 6) return set_err(FIBER_ETIMEOUT, "batched decode: a tensor-core wait timed out");
+    if (c->h_io->err == 3) return set_err(FIBER_EARG, "batched decode: a position left the cache on the device");
+    return device_status(c);
+}
+
+static int forward_batch(gpu_context *c, kv_cache_t *kv, const int32_t *tokens, const int32_t *pos, int batch,
+                         float *logits_or_null, int32_t *argmax_or_null) {
+    int rc = batch_checks(c, kv, tokens, pos, batch, 1);
+    if (rc) return rc;
+    CK(cudaSetDevice(c->device));
+    if ((rc = pf_alloc(c))) return rc;
+    c->h_io->err = 0;
+    CK(cudaMemcpyAsync(c->io, c->h_io, sizeof(StepIO), cudaMemcpyHostToDevice, c->stream));
+    CK(cudaMemcpyAsync(c->pf_tok, tokens, (size_t)batch * 4, cudaMemcpyHostToDevice, c->stream));
+    CK(cudaMemcpyAsync(c->bt_pos, pos, (size_t)batch * 4, cudaMemcpyHostToDevice, c->stream));
+    cudaError_t e = enqueue_batch_step(c, kv, batch, false, c->stream);
+    if (e != cudaSuccess) return set_err(FIBER_ECUDA, "batched decode step: %s", cudaGetErrorString(e));
+    if (logits_or_null)
+        CK(cudaMemcpyAsync(logits_or_null, c->bt_logits, (size_t)batch * c->p.vocab_size * 4, cudaMemcpyDeviceToHost,
+                           c->stream));
+    if (argmax_or_null)
+        CK(cudaMemcpyAsync(argmax_or_null, c->bt_arg, (size_t)batch * 4, cudaMemcpyDeviceToHost, c->stream));
+    CK(cudaMemcpyAsync(c->h_io, c->io, sizeof(StepIO), cudaMemcpyDeviceToHost, c->stream));
+    CK(cudaStreamSynchronize(c->stream));
+    return batch_status(c);
+}
+
+extern "C" int fiber_decode_greedy_batch(fiber_ctx_t *c, kv_cache_t *kv, const int32_t *first_tokens,
+                                         const int32_t *start_pos, int batch, int n_steps, int32_t *h_tokens_out,
+                                         float *ms_out) {
+    if (!c || n_steps <= 0) return set_err(FIBER_EARG, "fiber_decode_greedy_batch: bad arguments");
+    if (!batched_ok(c)) return set_err(FIBER_EUNSUPPORTED, "batched decode does not cover this model");
+    int rc = batch_checks(c, kv, first_tokens, start_pos, batch, n_steps);
+    if (rc) return rc;
+    CK(cudaSetDevice(c->device));
+    if ((rc = pf_alloc(c))) return rc;
+    c->h_io->err = 0;
+    CK(cudaMemcpyAsync(c->io, c->h_io, sizeof(StepIO), cudaMemcpyHostToDevice, c->stream));
+    CK(cudaMemcpyAsync(c->pf_tok, first_tokens, (size_t)batch * 4, cudaMemcpyHostToDevice, c->stream));
+    CK(cudaMemcpyAsync(c->bt_pos, start_pos, (size_t)batch * 4, cudaMemcpyHostToDevice, c->stream));
+    CK(cudaMemsetAsync(c->bt_step, 0, sizeof(int), c->stream));
+    Graph &g = c->g_batch;
+    if (!(g.exec && g.kv == kv && c->g_batch_n == batch)) {  // capture before the timed region
+        free_graph(g);
+        cudaGraph_t graph;
+        CK(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
+        cudaError_t e = enqueue_batch_step(c, kv, batch, true, c->stream);
+        cudaError_t e2 = cudaStreamEndCapture(c->stream, &graph);
+        if (e != cudaSuccess) return set_err(FIBER_ECUDA, "capturing the batch step: %s", cudaGetErrorString(e));
+        if (e2 != cudaSuccess) return set_err(FIBER_ECUDA, "end capture: %s", cudaGetErrorString(e2));
+        e = cudaGraphInstantiate(&g.exec, graph, 0);
+        cudaGraphDestroy(graph);
+        if (e != cudaSuccess) return set_err(FIBER_ECUDA, "graph instantiate: %s", cudaGetErrorString(e));
+        g.kv = kv;
+        c->g_batch_n = batch;
+    }
+    CK(cudaEventRecord(c->ev0, c->stream));
+    for (int i = 0; i < n_steps; i++) CK(cudaGraphLaunch(g.exec, c->stream));
+    CK(cudaEventRecord(c->ev1, c->stream));
+    CK(cudaEventSynchronize(c->ev1));
+    if (ms_out) CK(cudaEventElapsedTime(ms_out, c->ev0, c->ev1));
+    if (h_tokens_out)
+        CK(cudaMemcpyAsync(h_tokens_out, c->bt_rec, (size_t)n_steps * batch * 4, cudaMemcpyDeviceToHost, c->stream));
+    CK(cudaMemcpyAsync(c->h_io, c->io, sizeof(StepIO), cudaMemcpyDeviceToHost, c->stream));
+    CK(cudaStreamSynchronize(c->stream));
+    return batch_status(c);
 }
 
 extern "C" int fiber_set_decode_mode(fiber_ctx_t *c, int mode) {
@@ -1659,6 +1853,7 @@ static cudaError_t launch_g5_t(const G5Params &p, cudaStream_t st) {
 static cudaError_t launch_g5(const G5Params &p, cudaStream_t st) {
     switch (p.type) {
     case T_Q4_K: return launch_g5_t<T_Q4_K>(p, st);
+    case T_Q5_K: return launch_g5_t<T_Q5_K>(p, st);
     case T_Q6_K: return launch_g5_t<T_Q6_K>(p, st);
     case T_F16: return launch_g5_t<T_F16>(p, st);
     default: return cudaErrorInvalidValue;
@@ -1673,8 +1868,9 @@ extern "C" int fiber_gemm(int ggml_type, const void *d_w, int rows, int cols, co
     if (!d_w || !d_x || !d_y || rows <= 0 || ntok <= 0 || cols <= 0 || cols % 256 || ldx < cols ||
         ldy < out_off + rows || ldx % 4 || ((uintptr_t)d_w & 15) || ((uintptr_t)d_x & 15) || ((uintptr_t)d_nw & 15))
         return set_err(FIBER_EARG, "fiber_gemm: bad arguments");
-    if (!(ggml_type == T_Q4_K || ggml_type == T_Q6_K || ggml_type == T_F16))
-        return set_err(FIBER_EUNSUPPORTED, "fiber_gemm: type %s not supported (Q4_K, Q6_K, F16)", tname(ggml_type));
+    if (!g5_type_ok(ggml_type))
+        return set_err(FIBER_EUNSUPPORTED, "fiber_gemm: type %s not supported (Q4_K, Q5_K, Q6_K, F16)",
+                       tname(ggml_type));
     cudaStream_t st = (cudaStream_t)stream;
     G5Params p;
     memset(&p, 0, sizeof(p));

@@ -1,7 +1,7 @@
 // gemm_tc5.cuh — dequant-GEMM for batched prefill on the 5th-generation tensor cores.
 //
 // Y[t][out_off + r] (op)= sum_k W[r][k] * xn[t][k] for a GGUF weight matrix W (Q4_K,
-// Q6_K or F16 super-blocks, rows x cols) and ntok input rows x (fp32, optionally
+// Q5_K, Q6_K or F16 super-blocks, rows x cols) and ntok input rows x (fp32, optionally
 // RMS-normalised per token: xn = x * rrms[t] * nw[k]).
 //
 // Two kernels:
@@ -13,7 +13,7 @@
 //   * gemm_tc5_kernel: one CTA per 128-row x 64-token tile, tcgen05.mma (kind::f16,
 //     M = 128, N = 128, fp32 accumulators in tensor memory), warp-specialised:
 //       warp 0      producer: the raw weight rows of each K unit (a super-block
-//                   column of 128 rows: one 2D tensor copy for Q4_K / F16, one bulk
+//                   column of 128 rows: one 2D tensor copy for Q4_K / Q5_K / F16, one bulk
 //                   copy per row for Q6_K, whose rows are not 16-byte aligned) into a
 //                   ring of raw stages, and each chunk's packed B block (one bulk
 //                   copy) into a ring of B stages;
@@ -24,6 +24,9 @@
 //                   GEMV: quants -> half2 by LOP3 / byte permute, HFMA2, mixed-precision
 //                   FMA, cvt.rn.f16x2) into one of two A buffers, then run the epilogue
 //                   (tcgen05.ld, hi + lo columns added, Y stored or accumulated).
+// Q5_K weights are fp32 values (the Metal kernel's arithmetic, no fp16 rounding): they
+// are split into fp16 hi and lo parts, two A tiles per chunk whose MMAs accumulate into
+// the same tensor-memory tile (w = hi + lo to ~22 bits, like x).
 // Inside every group of 4 K positions the decoded pairs come out as (k0, k2), (k1, k3);
 // A and B both use that order (slots 0..3 hold k0, k2, k1, k3), so the products are
 // unchanged.
@@ -55,9 +58,9 @@ constexpr unsigned long long G5_WAIT_NS = 2000000000ull;
 enum : int { G5_STORE = 0, G5_RESID = 1 };
 
 struct G5Params {
-    CUtensorMap wmap;      // Q4_K / F16: 2D map of the weights (box 128 rows x one K unit)
+    CUtensorMap wmap;      // Q4_K / Q5_K / F16: 2D map of the weights (box 128 rows x one K unit)
     const uint8_t *w;      // weights, rows x cols in GGUF super-blocks
-    int type;              // T_Q4_K / T_Q6_K / T_F16
+    int type;              // T_Q4_K / T_Q5_K / T_Q6_K / T_F16
     int rows, cols, ntok;
     const uint8_t *bp;     // packed B: [ceil(ntok / 64)][cols / 128] blocks of 32 KB
     float *y;              // [ntok][ldy]
@@ -144,31 +147,38 @@ FDEV void g5_commit(uint64_t *bar) {
 // canonical offset of (row r, K slot k) inside a 128-K chunk tile: core matrix (r/8, k/8)
 FDEV int g5_off(int r, int k) { return ((r >> 3) * (G5_KC / 8) + (k >> 3)) * 128 + (r & 7) * 16 + (k & 7) * 2; }
 
-// Bytes of one row's weights per K unit in a raw stage. Q4_K: the 144-byte super-block
-// (two chunks). Q6_K: the super-block (two chunks) is 210 bytes at an even offset, so
-// the 224-byte span from the 16-byte boundary at or below it, which ends at most 14
-// bytes past the block. F16: the chunk's 128 values (256 bytes; one chunk per unit).
+// Bytes of one row's weights per K unit in a raw stage. Q4_K / Q5_K: the 144 / 176-byte
+// super-block (two chunks). Q6_K: the super-block (two chunks) is 210 bytes at an even
+// offset, so the 224-byte span from the 16-byte boundary at or below it, which ends at
+// most 14 bytes past the block. F16: the chunk's 128 values (256 bytes; one chunk per unit).
 template <int T>
-HDCE int g5_slot() { return T == T_Q4_K ? 144 : (T == T_Q6_K ? 224 : 256); }
+HDCE int g5_bb() { return T == T_Q4_K ? 144 : (T == T_Q5_K ? 176 : (T == T_Q6_K ? 210 : 512)); }
+template <int T>
+HDCE int g5_slot() { return T == T_Q4_K ? 144 : (T == T_Q5_K ? 176 : (T == T_Q6_K ? 224 : 256)); }
 template <int T>
 HDCE int g5_cpu() { return T == T_F16 ? 1 : 2; }  // chunks per K unit
 template <int T>
-HDCE int g5_bstages() { return 3; }
+HDCE int g5_aparts() { return T == T_Q5_K ? 2 : 1; }  // A tiles per chunk (Q5_K: hi, lo)
 template <int T>
-HDCE int g5_rstages() { return T == T_Q4_K ? 3 : 2; }
+HDCE int g5_bstages() { return T == T_Q5_K ? 2 : 3; }
 template <int T>
-HDCE int g5_smem() { return 2 * G5_A_BYTES + g5_bstages<T>() * G5_B_BYTES + g5_rstages<T>() * G5_M * g5_slot<T>(); }
+HDCE int g5_rstages() { return T == T_Q4_K ? 3 : (T == T_Q5_K ? 1 : 2); }
+template <int T>
+HDCE int g5_smem() {
+    return 2 * g5_aparts<T>() * G5_A_BYTES + g5_bstages<T>() * G5_B_BYTES + g5_rstages<T>() * G5_M * g5_slot<T>();
+}
 
 // Decode the 64 weights of row r that chunk c gives this thread (K slots 64*sub ..
-// 64*sub + 63 of the chunk) from the staged bytes `blk` into A (slot order k0 k2 k1 k3).
+// 64*sub + 63 of the chunk) from the staged bytes `blk` into A (slot order k0 k2 k1 k3;
+// Q5_K: fp16 hi parts into A, lo parts into A2).
 template <int T>
-FDEV void g5_decode(const uint8_t *blk, int c, int sub, int r, uint8_t *A);
+FDEV void g5_decode(const uint8_t *blk, int c, int sub, int r, uint8_t *A, uint8_t *A2);
 
 // Q4_K: chunk c covers half c & 1 of the super-block, i.e. quarter 2 (c & 1) + sub;
 // quarter t holds sub-block 2t (low nibbles: chunk K 64 sub + l) and 2t + 1 (high
 // nibbles: 64 sub + 32 + l), l = 0..31, from the 32 quant bytes at 16 + 32 t.
 template <>
-FDEV void g5_decode<T_Q4_K>(const uint8_t *blk, int c, int sub, int r, uint8_t *A) {
+FDEV void g5_decode<T_Q4_K>(const uint8_t *blk, int c, int sub, int r, uint8_t *A, uint8_t *) {
     using D = TcDot<T_Q4_K>;
     D::Row row;
     D::load_row(blk, 2 * (c & 1) + sub, row);
@@ -185,7 +195,7 @@ FDEV void g5_decode<T_Q4_K>(const uint8_t *blk, int c, int sub, int r, uint8_t *
 // Q6_K: chunk c covers half h = c & 1 (128 elements: planes k = 0..3, l = 0..31,
 // element 32 k + l); this thread takes l in [16 sub, 16 sub + 16) of every plane.
 template <>
-FDEV void g5_decode<T_Q6_K>(const uint8_t *blk, int c, int sub, int r, uint8_t *A) {
+FDEV void g5_decode<T_Q6_K>(const uint8_t *blk, int c, int sub, int r, uint8_t *A, uint8_t *) {
     using D = TcDot<T_Q6_K>;
     D::Row row;
     D::load_row(blk, 2 * (c & 1) + sub, row);
@@ -201,9 +211,50 @@ FDEV void g5_decode<T_Q6_K>(const uint8_t *blk, int c, int sub, int r, uint8_t *
     }
 }
 
+// Q5_K (layout as Q4_K plus qh[32] at 16, qs at 48): element 64 t + 32 s + l has quant
+// nib + 16 * ((qh[l] >> (2 t + s)) & 1), nib the low (s = 0) or high (s = 1) nibble of
+// qs[32 t + l]; value fp32((d*sc) * q - dmin*m). Same quarters as Q4_K.
+template <>
+FDEV void g5_decode<T_Q5_K>(const uint8_t *blk, int c, int sub, int r, uint8_t *A, uint8_t *A2) {
+    const uint4 hdr = *reinterpret_cast<const uint4 *>(blk);
+    const float d = h2f(hdr.x & 0xFFFFu), dmin = h2f(hdr.x >> 16);
+    const int t = 2 * (c & 1) + sub;
+    int sc0, m0, sc1, m1;
+    scale_min_k4(2 * t, hdr.y, hdr.z, hdr.w, sc0, m0);
+    scale_min_k4(2 * t + 1, hdr.y, hdr.z, hdr.w, sc1, m1);
+    const float dsc0 = __fmul_rn(d, (float)sc0), dmm0 = __fmul_rn(dmin, (float)m0);
+    const float dsc1 = __fmul_rn(d, (float)sc1), dmm1 = __fmul_rn(dmin, (float)m1);
+#pragma unroll
+    for (int v = 0; v < 4; v++) {  // l = 8v .. 8v+7
+        const uint2 qs = *reinterpret_cast<const uint2 *>(blk + 48 + 32 * t + 8 * v);
+        const uint2 qh = *reinterpret_cast<const uint2 *>(blk + 16 + 8 * v);
+        uint16_t lh[8], ll[8], hh[8], hl[8];  // low / high sub-block, hi / lo fp16 parts
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            const uint32_t q = ((j < 4 ? qs.x : qs.y) >> (8 * (j & 3))) & 0xFFu;
+            const uint32_t h = ((j < 4 ? qh.x : qh.y) >> (8 * (j & 3))) & 0xFFu;
+            const float w0 = q5k_weight(dsc0, dmm0, (int)((q & 15u) | (((h >> (2 * t)) & 1u) << 4)));
+            const float w1 = q5k_weight(dsc1, dmm1, (int)((q >> 4) | (((h >> (2 * t + 1)) & 1u) << 4)));
+            const __half a0 = __float2half_rn(w0), a1 = __float2half_rn(w1);
+            lh[j] = __half_as_ushort(a0);
+            ll[j] = __half_as_ushort(__float2half_rn(w0 - __half2float(a0)));
+            hh[j] = __half_as_ushort(a1);
+            hl[j] = __half_as_ushort(__float2half_rn(w1 - __half2float(a1)));
+        }
+        auto pk = [](const uint16_t *e) {  // slot order k0 k2 k1 k3 k4 k6 k5 k7
+            return make_uint4((uint32_t)e[0] | ((uint32_t)e[2] << 16), (uint32_t)e[1] | ((uint32_t)e[3] << 16),
+                              (uint32_t)e[4] | ((uint32_t)e[6] << 16), (uint32_t)e[5] | ((uint32_t)e[7] << 16));
+        };
+        *reinterpret_cast<uint4 *>(A + g5_off(r, 64 * sub + 8 * v)) = pk(lh);
+        *reinterpret_cast<uint4 *>(A2 + g5_off(r, 64 * sub + 8 * v)) = pk(ll);
+        *reinterpret_cast<uint4 *>(A + g5_off(r, 64 * sub + 32 + 8 * v)) = pk(hh);
+        *reinterpret_cast<uint4 *>(A2 + g5_off(r, 64 * sub + 32 + 8 * v)) = pk(hl);
+    }
+}
+
 // F16: the chunk's 128 values of the row; pairs regrouped to (k0, k2), (k1, k3)
 template <>
-FDEV void g5_decode<T_F16>(const uint8_t *blk, int c, int sub, int r, uint8_t *A) {
+FDEV void g5_decode<T_F16>(const uint8_t *blk, int c, int sub, int r, uint8_t *A, uint8_t *) {
     (void)c;
     const uint4 *e = reinterpret_cast<const uint4 *>(blk) + 8 * sub;
 #pragma unroll
@@ -281,16 +332,16 @@ __global__ void __launch_bounds__(128) g5_pack_kernel(const G5PackParams a) {
 
 template <int T>
 __global__ void __launch_bounds__(G5_THREADS, 1) gemm_tc5_kernel(const __grid_constant__ G5Params p) {
-    constexpr int BB = T == T_Q4_K ? 144 : (T == T_Q6_K ? 210 : 512);
-    constexpr int S = g5_slot<T>(), CPU = g5_cpu<T>(), NB = g5_bstages<T>(), NR = g5_rstages<T>();
+    constexpr int BB = g5_bb<T>(), S = g5_slot<T>(), CPU = g5_cpu<T>(), NB = g5_bstages<T>(), NR = g5_rstages<T>();
+    constexpr int AP = g5_aparts<T>(), AS = AP * G5_A_BYTES;  // A tiles per chunk, bytes per A stage
     extern __shared__ __align__(1024) uint8_t g5_smem[];
     __shared__ __align__(8) uint64_t bfull[NB], bempty[NB], rfull[NR], rempty[NR], afull[2], afree[2], accb;
     __shared__ uint32_t tmem_slot;
     __shared__ volatile int fail;
     __shared__ int n_issued;
-    uint8_t *const Abuf = g5_smem;                                     // [2][G5_A_BYTES]
-    uint8_t *const Bbuf = g5_smem + 2 * G5_A_BYTES;                    // [NB][G5_B_BYTES]
-    uint8_t *const Rbuf = g5_smem + 2 * G5_A_BYTES + NB * G5_B_BYTES;  // [NR][128 rows x S]
+    uint8_t *const Abuf = g5_smem;                             // [2][AP][G5_A_BYTES]
+    uint8_t *const Bbuf = g5_smem + 2 * AS;                    // [NB][G5_B_BYTES]
+    uint8_t *const Rbuf = g5_smem + 2 * AS + NB * G5_B_BYTES;  // [NR][128 rows x S]
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int row0 = blockIdx.x * G5_M, tile = blockIdx.y;
     const int nchunk = p.cols / G5_KC;
@@ -352,7 +403,7 @@ __global__ void __launch_bounds__(G5_THREADS, 1) gemm_tc5_kernel(const __grid_co
                 } else if (lane == 0) {
                     // box = 128 rows x one unit (rows past the matrix read as zeros)
                     g5_expect_tx(&rfull[rs], (uint32_t)(G5_M * S));
-                    const int x = T == T_Q4_K ? u * 144 : u * 128;  // bytes (Q4_K) / fp16 elements (F16)
+                    const int x = T == T_F16 ? u * 128 : u * BB;  // fp16 elements (F16) / bytes
                     asm volatile(
                         "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, "
                         "{%2, %3}], [%4];" ::"r"(g5_saddr(dst)),
@@ -390,16 +441,20 @@ __global__ void __launch_bounds__(G5_THREADS, 1) gemm_tc5_kernel(const __grid_co
                 if (!g5_wait(&afull[a], (uint32_t)((c >> 1) & 1), &fail)) break;
                 G5_MARK(7, c);
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                const uint32_t a0 = g5_saddr(Abuf + a * G5_A_BYTES), b0 = g5_saddr(Bbuf + s * G5_B_BYTES);
+                const uint32_t b0 = g5_saddr(Bbuf + s * G5_B_BYTES);
 #pragma unroll
-                for (int k = 0; k < G5_KC / 16; k++) {
-                    const uint64_t da = g5_desc(a0 + k * 256), db = g5_desc(b0 + k * 256);
-                    const uint32_t acc = (c > 0 || k > 0) ? 1u : 0u;
-                    asm volatile(
-                        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-                        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem),
-                        "l"(da), "l"(db), "r"(g5_idesc()), "r"(acc)
-                        : "memory");
+                for (int part = 0; part < AP; part++) {
+                    const uint32_t a0 = g5_saddr(Abuf + a * AS + part * G5_A_BYTES);
+#pragma unroll
+                    for (int k = 0; k < G5_KC / 16; k++) {
+                        const uint64_t da = g5_desc(a0 + k * 256), db = g5_desc(b0 + k * 256);
+                        const uint32_t acc = (c > 0 || part > 0 || k > 0) ? 1u : 0u;
+                        asm volatile(
+                            "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+                            " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem),
+                            "l"(da), "l"(db), "r"(g5_idesc()), "r"(acc)
+                            : "memory");
+                    }
                 }
                 g5_commit(&bempty[s]);
                 g5_commit(&afree[a]);
@@ -426,7 +481,7 @@ __global__ void __launch_bounds__(G5_THREADS, 1) gemm_tc5_kernel(const __grid_co
             // Q6_K: the span starts at the 16-byte boundary at or below the block
             const uint8_t *blk = Rbuf + rs * (G5_M * S) + r * S;
             if (T == T_Q6_K) blk += (shift + u * BB) & 15;
-            g5_decode<T>(blk, c, sub, r, Abuf + a * G5_A_BYTES);
+            g5_decode<T>(blk, c, sub, r, Abuf + a * AS, Abuf + a * AS + (AP - 1) * G5_A_BYTES);
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor core
             __syncwarp();
             if (lane == 0) {
@@ -486,7 +541,10 @@ __global__ void __launch_bounds__(G5_THREADS, 1) gemm_tc5_kernel(const __grid_co
 }
 
 HDCE int g5_smem_bytes(int type) {
-    return type == T_Q4_K ? g5_smem<T_Q4_K>() : type == T_Q6_K ? g5_smem<T_Q6_K>() : g5_smem<T_F16>();
+    return type == T_Q4_K   ? g5_smem<T_Q4_K>()
+           : type == T_Q5_K ? g5_smem<T_Q5_K>()
+           : type == T_Q6_K ? g5_smem<T_Q6_K>()
+                            : g5_smem<T_F16>();
 }
 
 }  // namespace fiber

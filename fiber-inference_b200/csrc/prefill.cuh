@@ -1,12 +1,15 @@
-// prefill.cuh — the non-GEMM kernels of the batched prefill (a prompt chunk of n
-// tokens at positions start .. start + n - 1 in one pass per layer). The
-// projections run on the tensor cores (gemm_tc5.cuh); these kernels do the
+// prefill.cuh — the non-GEMM kernels of a batched layer pass: n tokens in one pass per
+// layer, either a prompt chunk of one sequence (positions start .. start + n - 1, one
+// KV slot) or one decode step of n sequences (token t at position pos[t] in KV slot
+// t). The projections run on the tensor cores (gemm_tc5.cuh); these kernels do the
 // per-token parts with the decode path's arithmetic (the RMSNorms are folded into the
 // GEMM's input packing):
 //   embed_rows_kernel   embedding rows of the n tokens (fp16-rounded, as gpu_embed)
 //   rope_kv_kernel      half-split RoPE of q (in place) and k; K/V appended (fp16)
 //   attn_prefill_kernel causal GQA attention of each token over the cache
 //   swiglu_rows_kernel  h = silu(gate) * up
+//   argmax_rows_kernel  greedy token of each logits row (lowest index on ties)
+//   batch_advance_kernel  device-resident greedy loop: argmax -> next token, pos + 1
 #pragma once
 #include "attention.cuh"
 
@@ -35,10 +38,25 @@ __global__ void embed_rows_kernel(const uint8_t *__restrict__ tab, const int32_t
     }
 }
 
+// Where token t of a pass sits: position pos[t] (or start + t) of KV slot
+// slot + slot_step * t; page tables are [slot][max_pages].
+struct TokenPlace {
+    int start;             // position of token 0 when pos is null
+    const int32_t *pos;    // [n] per-token positions, or null
+    int slot, slot_step, max_pages;
+    int max_pos;           // positions must stay below this (cache and RoPE table)
+    int *err;              // set to 3 for a position outside [0, max_pos)
+};
+
+FDEV int place_pos(const TokenPlace &p, int t) { return p.pos ? p.pos[t] : p.start + t; }
+FDEV const int32_t *place_pages(const TokenPlace &p, const int32_t *page_table, int t) {
+    return page_table + (size_t)(p.slot + p.slot_step * t) * p.max_pages;
+}
+
 struct RopeKvParams {
     float *qkv;            // [n][ldq]: q | k | v of each token (q rotated in place)
     int ldq;
-    int start;             // position of token 0
+    TokenPlace at;
     const float2 *rope;    // [max_seq][hd/2]
     int n_heads, n_kv, hd;
     uint16_t *k_pool, *v_pool;
@@ -48,10 +66,15 @@ struct RopeKvParams {
 
 // One CTA per token: rotate q and k (the decode path's expressions), store K and V.
 __global__ void rope_kv_kernel(const RopeKvParams a) {
-    const int t = blockIdx.x, pos = a.start + t, hd = a.hd, half = hd / 2;
+    const int t = blockIdx.x, pos = place_pos(a.at, t), hd = a.hd, half = hd / 2;
+    if (pos < 0 || pos >= a.at.max_pos) {
+        if (threadIdx.x == 0) *a.at.err = 3;
+        return;
+    }
     float *q = a.qkv + (size_t)t * a.ldq;
     const float *k = q + (size_t)a.n_heads * hd, *v = k + (size_t)a.n_kv * hd;
     const float2 *rp = a.rope + (size_t)pos * half;
+    const int32_t *pages = place_pages(a.at, a.page_table, t);
     for (int i = threadIdx.x; i < a.n_heads * half; i += blockDim.x) {
         const int h = i / half, j = i % half;
         const float2 cs = rp[j];
@@ -59,7 +82,7 @@ __global__ void rope_kv_kernel(const RopeKvParams a) {
         q[h * hd + j] = __fsub_rn(__fmul_rn(x1, cs.x), __fmul_rn(x2, cs.y));
         q[h * hd + j + half] = __fadd_rn(__fmul_rn(x1, cs.y), __fmul_rn(x2, cs.x));
     }
-    const int page = a.page_table[pos / ATTN_P], tn = pos % ATTN_P;
+    const int page = pages[pos / ATTN_P], tn = pos % ATTN_P;
     for (int i = threadIdx.x; i < a.n_kv * half; i += blockDim.x) {
         const int g = i / half, j = i % half;
         const float2 cs = rp[j];
@@ -80,16 +103,16 @@ struct AttnPrefillParams {
     int ldq;
     float *out;            // [n][ldo]
     int ldo;
-    int start;
+    TokenPlace at;
     const uint16_t *k_pool, *v_pool;
     const int32_t *page_table;
     int layer, n_layers, n_kv, n_heads;
     float scale;
 };
 
-// CTA (token t, KV head g): the G query heads of g attend to positions 0 .. start + t,
-// page by page (64 positions) with the decode path's score / softmax / P.V arithmetic,
-// pages combined online.
+// CTA (token t, KV head g): the G query heads of g attend to positions 0 .. pos(t) of
+// the token's slot, page by page (64 positions) with the decode path's score / softmax
+// / P.V arithmetic, pages combined online.
 template <int HD, int G>
 __global__ void __launch_bounds__(ATTN_THREADS) attn_prefill_kernel(const AttnPrefillParams a) {
     constexpr int P = ATTN_P, KST = HD + 2, DPL = HD / 32;
@@ -97,7 +120,10 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_prefill_kernel(const AttnPr
     __shared__ __align__(16) uint16_t ks[P][KST];
     __shared__ __align__(16) uint16_t vs[P][HD];
     const int t = blockIdx.x, g = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int seqlen = a.start + t + 1, nch = (seqlen + P - 1) / P;
+    const int pos = place_pos(a.at, t);
+    if (pos < 0 || pos >= a.at.max_pos) return;  // rope_kv_kernel reported it
+    const int seqlen = pos + 1, nch = (seqlen + P - 1) / P;
+    const int32_t *pages = place_pages(a.at, a.page_table, t);
     for (int i = tid; i < G * HD; i += ATTN_THREADS)
         qs[i / HD][i % HD] = a.qkv[(size_t)t * a.ldq + (size_t)(g * G + i / HD) * HD + i % HD];
     float m_run = -INFINITY, l_run = 0.f, o_run[DPL];
@@ -106,7 +132,7 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_prefill_kernel(const AttnPr
     for (int c = 0; c < nch; c++) {
         __syncthreads();  // previous page consumed (and qs staged)
         const int t0 = c * P, nt = min(P, seqlen - t0);
-        const size_t base = (((size_t)a.page_table[c] * a.n_layers + a.layer) * a.n_kv + g) * (size_t)P * HD;
+        const size_t base = (((size_t)pages[c] * a.n_layers + a.layer) * a.n_kv + g) * (size_t)P * HD;
         constexpr int V8 = HD / 8;
         for (int i = tid; i < nt * V8; i += ATTN_THREADS) {
             const int r = i / V8, k8 = i % V8;
@@ -182,6 +208,61 @@ __global__ void swiglu_rows_kernel(float *hg, const float *__restrict__ hu, size
         const float g = hg[i];
         hg[i] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), hu[i]);
     }
+}
+
+// One CTA (256 threads) per row: index of the maximum, the lowest index winning ties
+// (the strict > scan of the reference sampler, src/sampler.c:38-46). NaN never wins.
+__global__ void __launch_bounds__(256) argmax_rows_kernel(const float *__restrict__ logits, int V, int ld,
+                                                          int32_t *arg) {
+    __shared__ float bv[8];
+    __shared__ int bi[8];
+    const float *row = logits + (size_t)blockIdx.x * ld;
+    float best = -INFINITY;
+    int idx = V;  // larger than every index: "none yet"
+    for (int i = threadIdx.x; i < V; i += 256) {
+        const float v = row[i];
+        if (v > best) {  // a thread visits indices in increasing order: ties keep the first
+            best = v;
+            idx = i;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+        if (ov > best || (ov == best && oi < idx)) {
+            best = ov;
+            idx = oi;
+        }
+    }
+    if ((threadIdx.x & 31) == 0) {
+        bv[threadIdx.x >> 5] = best;
+        bi[threadIdx.x >> 5] = idx;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < 8; w++)
+            if (bv[w] > best || (bv[w] == best && bi[w] < idx)) {
+                best = bv[w];
+                idx = bi[w];
+            }
+        arg[blockIdx.x] = idx < V ? idx : 0;  // all NaN / -inf: token 0
+    }
+}
+
+// Device-resident greedy loop over n sequences: token[t] <- arg[t], pos[t] + 1, and the
+// token recorded at rec[step * n + t]; one CTA, then the step counter advances.
+__global__ void batch_advance_kernel(const int32_t *arg, int32_t *tokens, int32_t *pos, int32_t *rec, int *step,
+                                     int n) {
+    const int s = *step;
+    for (int t = threadIdx.x; t < n; t += blockDim.x) {
+        const int32_t a = arg[t];
+        tokens[t] = a;
+        pos[t] += 1;
+        rec[(size_t)s * n + t] = a;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) *step = s + 1;
 }
 
 }  // namespace fiber

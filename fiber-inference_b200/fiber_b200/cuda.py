@@ -28,7 +28,8 @@ EXPORTED = [
     "fiber_tp_unique_id", "fiber_cuda_init_tp", "fiber_tp_info", "fiber_gemm", "fiber_set_prefill_mode",
     "fiber_dequant", "fiber_gemv_host", "gpu_init", "gpu_free", "gpu_embed", "gpu_forward_token",
     "gpu_get_logits", "gpu_forward_classifier", "gpu_get_device", "kv_cache_init", "kv_cache_init_paged",
-    "kv_cache_free", "kv_cache_write", "kv_cache_read", "fiber_gemv_argmax_noalloc",
+    "kv_cache_free", "kv_cache_write", "kv_cache_read", "fiber_gemv_argmax_noalloc", "fiber_prefill_slot",
+    "fiber_decode_greedy_batch",
 ]
 
 
@@ -67,6 +68,9 @@ def cuda_lib() -> C.CDLL:
         L.fiber_cuda_free.argtypes = [C.c_void_p]
         L.fiber_forward_token.argtypes = [C.c_void_p, C.c_void_p, I32P, I32P, C.c_int, C.c_void_p, C.c_void_p]
         L.fiber_prefill.argtypes = [C.c_void_p, C.c_void_p, I32P, C.c_int, C.c_int, C.c_void_p]
+        L.fiber_prefill_slot.argtypes = [C.c_void_p, C.c_void_p, C.c_int, I32P, C.c_int, C.c_int, C.c_void_p]
+        L.fiber_decode_greedy_batch.argtypes = [C.c_void_p, C.c_void_p, I32P, I32P, C.c_int, C.c_int, C.c_void_p,
+                                                C.c_void_p]
         L.fiber_decode_greedy.argtypes = [C.c_void_p, C.c_void_p, C.c_int32, C.c_int, C.c_int, C.c_void_p,
                                           C.c_void_p]
         L.fiber_step_launches.argtypes = [C.c_void_p]
@@ -163,8 +167,11 @@ def dequant(ggml_type: int, d_w: int, d_out: int, rows: int, cols: int, stream=N
 
 
 class KVCache:
-    def __init__(self, device: int, n_layers: int, n_kv_heads: int, head_dim: int, max_seq: int):
-        self.ptr = cuda_lib().kv_cache_init(device, n_layers, n_kv_heads, head_dim, max_seq)
+    def __init__(self, device: int, n_layers: int, n_kv_heads: int, head_dim: int, max_seq: int, max_batch: int = 1):
+        if max_batch == 1:
+            self.ptr = cuda_lib().kv_cache_init(device, n_layers, n_kv_heads, head_dim, max_seq)
+        else:
+            self.ptr = cuda_lib().kv_cache_init_paged(device, n_layers, n_kv_heads, head_dim, max_seq, max_batch, 64)
         if not self.ptr:
             raise FiberError(f"kv_cache_init: {cuda_lib().fiber_last_error().decode()}")
         self.s = self.ptr.contents
@@ -211,11 +218,12 @@ class Context:
     """fiber_cuda_init over a host model (fiber_b200.HostModel); with tp=(rank, world,
     id bytes) a tensor-parallel context (fiber_cuda_init_tp)."""
 
-    def __init__(self, host_model, device: int = 0, max_seq: int = 0, tp=None):
+    def __init__(self, host_model, device: int = 0, max_seq: int = 0, tp=None, max_batch: int = 1):
         self.model = host_model
         self.p = host_model.params
+        self.max_batch = max_batch
         if tp is None:
-            self.h = cuda_lib().fiber_cuda_init(host_model.h, device, 1, max_seq)
+            self.h = cuda_lib().fiber_cuda_init(host_model.h, device, max_batch, max_seq)
         else:
             rank, world, nid = tp
             idbuf = (C.c_uint8 * TP_ID_BYTES).from_buffer_copy(nid)
@@ -234,8 +242,9 @@ class Context:
 
     __del__ = close
 
-    def kv(self, max_seq: int | None = None) -> KVCache:
-        return KVCache(self.device, self.p.n_layers, self.plan.kv_heads, self.p.head_dim, max_seq or self.max_seq)
+    def kv(self, max_seq: int | None = None, max_batch: int = 1) -> KVCache:
+        return KVCache(self.device, self.p.n_layers, self.plan.kv_heads, self.p.head_dim, max_seq or self.max_seq,
+                       max_batch)
 
     def forward(self, kv: KVCache, token: int, pos: int, want_logits: bool = True):
         lg = np.empty(self.p.vocab_size, np.float32) if want_logits else None
@@ -246,11 +255,38 @@ class Context:
                "fiber_forward_token")
         return int(am[0]), lg
 
-    def prefill(self, kv: KVCache, tokens, start_pos: int = 0) -> int:
+    def prefill(self, kv: KVCache, tokens, start_pos: int = 0, slot: int | None = None) -> int:
+        """fiber_prefill (slot None: KV slot 0) or fiber_prefill_slot; returns the next greedy token."""
         t = np.ascontiguousarray(tokens, np.int32)
         am = np.zeros(1, np.int32)
-        _check(cuda_lib().fiber_prefill(self.h, kv.addr, t, len(t), start_pos, am.ctypes.data), "fiber_prefill")
+        if slot is None:
+            _check(cuda_lib().fiber_prefill(self.h, kv.addr, t, len(t), start_pos, am.ctypes.data), "fiber_prefill")
+        else:
+            _check(cuda_lib().fiber_prefill_slot(self.h, kv.addr, int(slot), t, len(t), start_pos, am.ctypes.data),
+                   "fiber_prefill_slot")
         return int(am[0])
+
+    def forward_batch(self, kv: KVCache, tokens, pos, want_logits: bool = True):
+        """One decode step of len(tokens) sequences (sequence i on KV slot i):
+        (argmax [batch], logits [batch][vocab] or None)."""
+        t = np.ascontiguousarray(tokens, np.int32)
+        p = np.ascontiguousarray(pos, np.int32)
+        lg = np.empty((len(t), self.p.vocab_size), np.float32) if want_logits else None
+        am = np.zeros(len(t), np.int32)
+        _check(cuda_lib().fiber_forward_token(self.h, kv.addr, t, p, len(t),
+                                              lg.ctypes.data if lg is not None else None, am.ctypes.data),
+               "fiber_forward_token")
+        return am, lg
+
+    def decode_greedy_batch(self, kv: KVCache, first_tokens, start_pos, n_steps: int):
+        """fiber_decode_greedy_batch: (tokens [n_steps][batch], device ms)."""
+        t = np.ascontiguousarray(first_tokens, np.int32)
+        p = np.ascontiguousarray(start_pos, np.int32)
+        out = np.zeros((n_steps, len(t)), np.int32)
+        ms = C.c_float(0.0)
+        _check(cuda_lib().fiber_decode_greedy_batch(self.h, kv.addr, t, p, len(t), int(n_steps), out.ctypes.data,
+                                                    C.addressof(ms)), "fiber_decode_greedy_batch")
+        return out, float(ms.value)
 
     def decode_greedy(self, kv: KVCache, first_token: int, start_pos: int, n_steps: int):
         out = np.zeros(n_steps, np.int32)

@@ -37,28 +37,41 @@ extern "C" {
 const char *fiber_last_error(void);
 int fiber_device_count(void);
 
-/* ---- model-level decode (batch-1 greedy loop of src/main.m:553-586) ---------- */
+/* ---- model-level decode (greedy loop of src/main.m:553-586) --------------------- */
+
+/* Sequences one batched decode step can carry. */
+#define FIBER_MAX_BATCH 64
 
 typedef struct gpu_context fiber_ctx_t;
 
 /* Upload the GGUF data section unchanged to `device`, resolve per-layer device
  * pointers once, allocate activations and scratch for up to max_seq positions.
- * (gpu_init equivalent, src/gpu_ffn.m:141-204.) max_batch must be 1. */
+ * (gpu_init equivalent, src/gpu_ffn.m:141-204.) max_batch (1 .. FIBER_MAX_BATCH)
+ * bounds the sequences of one batched step; above 1 the model must suit the
+ * tensor-core layer pass (Q4_K/Q5_K/Q6_K/F16 matrices, GQA group <= 8), else NULL
+ * with FIBER_EUNSUPPORTED. */
 fiber_ctx_t *fiber_cuda_init(const model_t *m, int device, int max_batch, int max_seq);
 void fiber_cuda_free(fiber_ctx_t *ctx);
 
-/* One decode step for `batch` sequences (batch must be 1): embeds tokens[i] at
+/* One decode step for `batch` sequences (1 .. max_batch): embeds tokens[i] at
  * position pos[i] (host arrays), runs all layers and the classifier, then, if
  * non-NULL, copies the fp32 logits [batch][vocab] and the greedy argmax
- * (lowest index on ties, src/sampler.c:38-46) to host memory. Blocks until done. */
+ * (lowest index on ties, src/sampler.c:38-46) to host memory. Blocks until done.
+ * batch 1 runs the GEMV step on KV slot 0; batch > 1 runs sequence i on KV slot i
+ * through the tensor-core layer pass (the reference decodes one sequence only). */
 int fiber_forward_token(fiber_ctx_t *ctx, kv_cache_t *kv, const int32_t *tokens,
                         const int32_t *pos, int batch, float *logits_or_null,
                         int32_t *argmax_or_null);
 
-/* Prompt of n tokens at positions start_pos.. (token by token through the same
- * decode step); *argmax_out (optional) gets the greedy token after the last one. */
+/* Prompt of n tokens at positions start_pos.. of KV slot 0 (src/main.m:561-563
+ * steps it token by token; here batched, see fiber_set_prefill_mode);
+ * *argmax_out (optional) gets the greedy token after the last one. */
 int fiber_prefill(fiber_ctx_t *ctx, kv_cache_t *kv, const int32_t *tokens, int n, int start_pos,
                   int32_t *argmax_out);
+/* The same for KV slot `slot` (batched layer pass only), to start a batch of
+ * sequences. No counterpart in the reference (one sequence only). */
+int fiber_prefill_slot(fiber_ctx_t *ctx, kv_cache_t *kv, int slot, const int32_t *tokens, int n,
+                       int start_pos, int32_t *argmax_out);
 
 /* Device-resident greedy loop: n_steps decode steps starting with first_token at
  * start_pos; each step's argmax feeds the next on the device (one graph replay
@@ -67,6 +80,14 @@ int fiber_prefill(fiber_ctx_t *ctx, kv_cache_t *kv, const int32_t *tokens, int n
  * on the context stream). */
 int fiber_decode_greedy(fiber_ctx_t *ctx, kv_cache_t *kv, int32_t first_token, int start_pos,
                         int n_steps, int32_t *h_tokens_out, float *ms_out);
+/* The device-resident greedy loop for `batch` sequences (1 .. max_batch): sequence
+ * i starts with first_tokens[i] at start_pos[i] in KV slot i; one captured graph
+ * of the batched step per step. h_tokens_out[step * batch + i] = sequence i's
+ * argmax at that step. ms_out as for fiber_decode_greedy. No counterpart in the
+ * reference (one sequence only). */
+int fiber_decode_greedy_batch(fiber_ctx_t *ctx, kv_cache_t *kv, const int32_t *first_tokens,
+                              const int32_t *start_pos, int batch, int n_steps, int32_t *h_tokens_out,
+                              float *ms_out);
 
 /* How a decode step runs. mode 0 (default when the model fits): one cooperative
  * persistent kernel per step -- every SM streams its weight tiles of all phases
@@ -157,9 +178,10 @@ int fiber_gemv(int ggml_type, const void *d_w, const float *d_x, float *d_y, int
 /* Tensor-core dequant-GEMM (the prefill building block; tcgen05, fp32 accumulation):
  * y[t][out_off + r] = (accumulate ? y[t][out_off + r] : 0) + sum_k W[r,k] * xn[t][k]
  * for t < ntok, with xn = x * rrms[t] * nw[k] when d_nw is given (RMSNorm folded
- * in; rrms taken as 1 when d_rrms is null) and xn = x otherwise. W: Q4_K / Q6_K / F16
- * super-blocks, cols % 256 == 0; x: [ntok][ldx] fp32; y: [ntok][ldy] fp32. The
- * weights are decoded exactly as the GEMV does; xn is split into fp16 hi + lo parts
+ * in; rrms taken as 1 when d_rrms is null) and xn = x otherwise. W: Q4_K / Q5_K /
+ * Q6_K / F16 super-blocks, cols % 256 == 0; x: [ntok][ldx] fp32; y: [ntok][ldy] fp32.
+ * The weights are decoded exactly as the GEMV does (Q5_K's fp32 values as fp16 hi +
+ * lo parts); xn is split into fp16 hi + lo parts
  * and must stay below 65504 in magnitude (else FIBER_EARG). d_w, d_x and d_nw must
  * be 16-byte aligned and ldx a multiple of 4; Q6_K rows are read through
  * 16-byte-aligned spans, so 14 bytes after the last block must be readable.

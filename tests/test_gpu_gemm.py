@@ -28,13 +28,16 @@ def _weights(t, rows, cols, seed):
         w = (np.random.default_rng(seed).standard_normal((rows, cols)) * 0.05).astype(np.float16)
         return _dev(w.view(np.uint8).reshape(-1)), w.astype(np.float64)
     blocks = fb.random_blocks(t, rows, cols, seed=seed)
-    w = orc.dequant_f16(t, blocks, rows, cols).astype(np.float64)
+    if t == fb.GGML_Q5_K:  # fp32 weights (the Metal kernel's arithmetic)
+        w = orc.dequant_f32(t, blocks, rows, cols).astype(np.float64)
+    else:
+        w = orc.dequant_f16(t, blocks, rows, cols).astype(np.float64)
     # Q6_K rows are read through 16-byte-aligned spans: keep 14+ readable bytes after
     padded = np.concatenate([np.asarray(blocks, dtype=np.uint8).reshape(-1), np.zeros(256, np.uint8)])
     return _dev(padded), w
 
 
-@pytest.mark.parametrize("t", [fb.GGML_Q4_K, fb.GGML_Q6_K, fb.GGML_F16])
+@pytest.mark.parametrize("t", [fb.GGML_Q4_K, fb.GGML_Q5_K, fb.GGML_Q6_K, fb.GGML_F16])
 @pytest.mark.parametrize("rows,cols,ntok", [(300, 512, 70), (128, 256, 1), (256, 2048, 64), (130, 768, 129)])
 def test_gemm_matches_decoded_product(t, rows, cols, ntok):
     import torch
@@ -80,4 +83,4 @@ def test_gemm_rejects_bad_shapes():
     with pytest.raises(fb.FiberError):
         fb.gemm(fb.GGML_Q4_K, 1, 128, 200, 1, 4, 1, 128)  # cols not a multiple of 256
     with pytest.raises(fb.FiberError):
-        fb.gemm(fb.GGML_Q5_K, 1, 128, 256, 1, 4, 1, 128)  # type not covered
+        fb.gemm(fb.GGML_F32, 16, 128, 256, 16, 4, 16, 128)  # type not covered

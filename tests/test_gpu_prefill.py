@@ -19,7 +19,7 @@ def _prompt(vocab, n, seed):
     return np.random.default_rng(seed).integers(1, vocab, n).astype(np.int32)
 
 
-@pytest.mark.parametrize("name", ["q4km", "f16", "q6k", "gqa8", "hd128"])
+@pytest.mark.parametrize("name", ["q4km", "q5km", "f16", "q6k", "gqa8", "hd128"])
 def test_batched_prefill_matches_oracle(tiny_model, name):
     path = tiny_model(name)
     hm = fb.HostModel(path)
