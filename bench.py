@@ -406,6 +406,101 @@ def run_prefill(args, fb, torch, dist, rank, world, local):
         dist.destroy_process_group()
 
 
+def run_batch(args, fb, torch, dist, rank, world, local):
+    """Batched greedy decode (config 4 at batch 8 / 32, config 5 at batch 64): B sequences per
+    step on KV slots 0..B-1 through the tensor-core layer pass, one captured graph per step.
+    Config 4: the 1.1B Q5_K_M model, every slot's KV pre-filled with seeded N(0,1) fp16 keys /
+    values for 2048 positions, 256 steps. Config 5: the 7B Q4_K_M model, every slot prefilled
+    with its own 512-token prompt, 256 steps. One replica per rank (weak scaling)."""
+    B = args.batch
+    if args.workload == "7b-tp":
+        path, P, D = MODEL_7B, 512, 256
+        if rank == 0 and not os.path.exists(path):
+            fb.write_model(path + ".tmp", fb.synth_cfg("llama7b"))
+            os.replace(path + ".tmp", path)
+        if dist is not None:
+            dist.barrier()
+    else:
+        path, P, D = "/tmp/fiber_bench_tinyllama_q5km.gguf", 2048, 256
+        if not os.path.exists(path):
+            tmp = path + f".{os.getpid()}.tmp"
+            fb.write_model(tmp, fb.synth_cfg("tinyllama-q5", seed=SEED))
+            os.replace(tmp, path)
+    if args.decode_len != DECODE_LEN:
+        D = args.decode_len
+    hm = fb.HostModel(path)
+    p = hm.params
+    ctx = fb.Context(hm, device=local, max_seq=P + D, max_batch=B)
+    kv = ctx.kv(P + D, max_batch=B)
+    kvd = p.n_kv_heads * p.head_dim
+    t_fill = time.perf_counter()
+    if args.workload == "7b-tp":
+        base = prompt_ids(p.vocab_size)[:P]
+        firsts = [ctx.prefill(kv, np.roll(base, s), slot=s) for s in range(B)]
+    else:
+        for layer in range(p.n_layers):
+            k = fb.randn(P * kvd, seed=100 + layer).reshape(P, kvd)
+            v = fb.randn(P * kvd, seed=200 + layer).reshape(P, kvd)
+            for s in range(B):
+                kv.write(layer, 0, k, v, slot=s)
+        firsts = [(5 + 7 * s) % p.vocab_size for s in range(B)]
+    t_fill = time.perf_counter() - t_fill
+    starts = [P] * B
+    for _ in range(args.warmup):
+        ctx.decode_greedy_batch(kv, firsts, starts, D)
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize(local)
+    ms_total, wall = 0.0, 0.0
+    with Clocks(local) as clk:
+        for _ in range(args.steps):
+            t0 = time.perf_counter()
+            toks, ms = ctx.decode_greedy_batch(kv, firsts, starts, D)  # host in -> device loop -> host out
+            wall += time.perf_counter() - t0
+            ms_total += ms
+    if dist is not None:
+        t = torch.tensor([ms_total, wall * 1e3], device=f"cuda:{local}", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_total, wall = float(t[0].item()), float(t[1].item()) / 1e3
+    value = world * args.steps * D * B / (ms_total / 1e3)
+    e2e = world * args.steps * D * B / wall
+    mid = P + D // 2
+    if args.workload == "7b-tp":
+        weights, kv_seq = WEIGHTS_7B, 524_288 * mid
+    else:
+        weights, kv_seq = 0.0, 0.0
+        for kind in range(7):
+            _, b = ctx.time_kernel(kv, kind, mid, reps=2)
+            if kind == 1:
+                kv_seq = b * p.n_layers  # attention reads: this sequence's K/V (+ q / out)
+            else:
+                weights += b * (1 if kind >= 5 else p.n_layers)
+    step_bytes = weights + B * kv_seq
+    peak, peak_kind = peaks()
+    if rank == 0:
+        ach = step_bytes * (value / B) / world / 1e9
+        name = {"7b-tp": "7B Q4_K_M (Llama-2-7B shape), each slot prefilled with a 512-token prompt",
+                "q5km-long": "1.1B Q5_K_M (TinyLlama shape), every slot's KV pre-filled to 2048 positions"}[args.workload]
+        line = {"metric": f"decode tok/s ({args.workload}, bs={B})", "value": value, "unit": "tok/s",
+                "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_total / args.steps,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16 x f16 -> f32",
+                "data": "synthetic (seeded random-init weights; seeded prompt ids or seeded N(0,1) KV)",
+                "config": {"workload": name, "context": P, "decode_tokens_per_step": D, "global_batch": B * world,
+                           "parallelism": f"replicas x{world}",
+                           "step_mode": "batched layer pass (tcgen05 GEMMs), one captured graph per step",
+                           "fill_seconds": t_fill},
+                "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 8 * B / D, "d2h_bytes_per_step": 4 * B},
+                "roofline": {"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak,
+                             "peak_source": peak_kind, "traffic": None, "algorithmic_bytes_per_step": step_bytes,
+                             "weight_bytes": weights, "kv_bytes_per_sequence": kv_seq, "kv_position": mid},
+                "gpu_launches": (5 + 14 * p.n_layers) * D * args.steps, "clocks": clk.summary()}
+        print(json.dumps(line), flush=True)
+    ctx.close()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -419,6 +514,8 @@ def main():
     ap.add_argument("--skip-extras", action="store_true", help="no single-GEMV, e2e or CPU legs (profiling)")
     ap.add_argument("--step-mode", type=int, default=None, choices=[0, 1],
                     help="0: one persistent kernel per token (default when the model fits it); 1: one kernel per phase")
+    ap.add_argument("--batch", type=int, default=1,
+                    help="sequences per step for q5km-long / 7b-tp (>1: batched decode, one replica per rank)")
     ap.add_argument("--workload", default="1.1b", choices=["1.1b", "7b-tp", "stories", "q5km-long", "prefill"],
                     help="1.1b: the headline 1.1B Q4_K_M decode (replicas for N>1); "
                          "7b-tp: 7B Q4_K_M decode tensor-parallel over the N GPUs; "
@@ -445,6 +542,8 @@ def main():
         import torch.distributed as dist
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+    if args.batch > 1 and args.workload in ("7b-tp", "q5km-long"):
+        return run_batch(args, fb, torch, dist, rank, world, local)
     if args.workload == "7b-tp":
         return run_7b_tp(args, fb, torch, dist, rank, world, local)
     if args.workload in ("stories", "q5km-long"):

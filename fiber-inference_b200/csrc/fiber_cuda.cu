@@ -402,6 +402,10 @@ struct gpu_context {
     float *bt_logits = nullptr;        // [max_batch][vocab]
     Graph g_batch;                     // captured greedy batch step (g_batch_n sequences)
     int g_batch_n = 0;
+    float *att_ws = nullptr;           // page-split attention states (batched layer pass)
+    unsigned int *att_tickets = nullptr;
+    float *g5_ws = nullptr;            // split-K partial tiles of the GEMMs
+    unsigned int *g5_tickets = nullptr;  // split-K tickets (zero between launches)
 };
 
 static void free_graph(Graph &g) {
@@ -418,7 +422,7 @@ extern "C" void fiber_cuda_free(fiber_ctx_t *c) {
     free_graph(c->g_loop);
     free_graph(c->g_batch);
     if (c->comm) ncclCommDestroy(c->comm);
-    void *dev[] = {c->bt_pos, c->bt_arg, c->bt_rec, c->bt_step, c->bt_logits, c->pf_x, c->pf_qkv, c->pf_att, c->pf_hg, c->pf_hu, c->pf_bp, c->pf_tok, c->x2, c->d_shard, c->d_data, c->x, c->qkv, c->att, c->h, c->logits, c->rope, c->io, c->rec,
+    void *dev[] = {c->att_ws, c->att_tickets, c->g5_ws, c->g5_tickets, c->bt_pos, c->bt_arg, c->bt_rec, c->bt_step, c->bt_logits, c->pf_x, c->pf_qkv, c->pf_att, c->pf_hg, c->pf_hu, c->pf_bp, c->pf_tok, c->x2, c->d_shard, c->d_data, c->x, c->qkv, c->att, c->h, c->logits, c->rope, c->io, c->rec,
                    c->att_part, c->att_cnt, c->am_part, c->am_cnt, c->d_phases, c->d_bar,
                    c->pk_gf[0], c->pk_gf[1], c->pk_gf[2], c->pk_gf[3], c->pk_ss[0], c->pk_ss[1]};
     for (void *p : dev)
@@ -1200,16 +1204,30 @@ static bool batched_ok(const gpu_context *c) {
 
 static bool prefill_batched_ok(const gpu_context *c) { return c->prefill_mode == 0 && batched_ok(c); }
 
+constexpr int ATT_PART_ENTRIES = 2048;  // (token, KV head, split) states of one page-split launch
+
 template <int HD, int G>
-static cudaError_t launch_attn_prefill_t(const AttnPrefillParams &a, int n, cudaStream_t st) {
-    attn_prefill_kernel<HD, G><<<dim3(n, a.n_kv), ATTN_THREADS, 0, st>>>(a);
+static cudaError_t launch_attn_prefill_t(const AttnPrefillParams &a, int n, int ps, cudaStream_t st) {
+    attn_prefill_kernel<HD, G><<<dim3(n, a.n_kv, ps), ATTN_THREADS, 0, st>>>(a);
     return cudaGetLastError();
+}
+
+// Page split: only when the (token, KV head) CTAs alone leave most SMs idle and the
+// contexts can be long.
+static int attn_psplit(int n, int n_kv, int max_pos) {
+    const int base = n * n_kv, pages = (max_pos + ATTN_P - 1) / ATTN_P;
+    if (base * 3 >= sm_count() * 2) return 1;
+    int ps = (2 * sm_count() + base - 1) / base;
+    ps = std::min(ps, std::min(16, pages / 2));
+    ps = std::min(ps, ATT_PART_ENTRIES / base);
+    return ps < 1 ? 1 : ps;
 }
 
 static cudaError_t launch_attn_prefill(const gpu_context *c, const AttnPrefillParams &a, int n, cudaStream_t st) {
     const int hd = c->p.head_dim, G = c->G;
+    const int ps = (a.part && a.tickets) ? attn_psplit(n, a.n_kv, a.at.max_pos) : 1;
 #define APF_CASE(H, GG) \
-    if (hd == H && G == GG) return launch_attn_prefill_t<H, GG>(a, n, st);
+    if (hd == H && G == GG) return launch_attn_prefill_t<H, GG>(a, n, ps, st);
     APF_CASE(64, 1) APF_CASE(64, 2) APF_CASE(64, 4) APF_CASE(64, 8)
     APF_CASE(128, 1) APF_CASE(128, 2) APF_CASE(128, 4) APF_CASE(128, 8)
 #undef APF_CASE
@@ -1259,7 +1277,8 @@ static bool g5_make_map(CUtensorMap *map, const uint8_t *w, int type, int rows, 
 }
 
 static cudaError_t launch_g5_pack(const G5PackParams &a, cudaStream_t st) {
-    g5_pack_kernel<<<((a.ntok + G5_T - 1) / G5_T) * (G5_T / 4), 128, 0, st>>>(a);
+    const dim3 grid(((a.ntok + G5_T - 1) / G5_T) * (G5_T / 4), a.cols / G5_PACK_COLS);
+    g5_pack_kernel<<<grid, 128, 0, st>>>(a);
     return cudaGetLastError();
 }
 
@@ -1296,6 +1315,9 @@ static cudaError_t pf_gemm(gpu_context *c, const CUtensorMap &map, const uint8_t
     g.out_off = off;
     g.epi = acc ? G5_RESID : G5_STORE;
     g.err = &c->io->err;
+    g.ksplit = g5_choose_ksplit(type, rows, cols, n, sm_count());
+    g.ws = c->g5_ws;
+    g.tickets = c->g5_tickets;
     return launch_g5(g, st);
 }
 
@@ -1343,6 +1365,8 @@ static cudaError_t enqueue_layers(gpu_context *c, const kv_cache_t *kv, int n, c
         ap.n_kv = p.n_kv_heads;
         ap.n_heads = p.n_heads;
         ap.scale = 1.0f / sqrtf((float)hd);
+        ap.part = c->att_ws;
+        ap.tickets = c->att_tickets;
         if ((e = launch_attn_prefill(c, ap, n, st))) break;
         if ((e = pf_pack(c, c->pf_att, dim, nullptr, n, st))) break;
         if ((e = pf_gemm(c, mp[3], d.wo, d.to, dim, dim, c->pf_x, dim, 0, true, n, st))) break;
@@ -1424,6 +1448,12 @@ static int pf_alloc(gpu_context *c) {
     CK(cudaMalloc(&c->bt_rec, B * c->max_seq * 4));
     CK(cudaMalloc(&c->bt_step, sizeof(int)));
     CK(cudaMalloc(&c->bt_logits, B * p.vocab_size * 4));
+    CK(cudaMalloc(&c->g5_ws, (size_t)G5_WS_TILES * G5_T * G5_M * 4));
+    CK(cudaMalloc(&c->g5_tickets, G5_TICKETS * sizeof(unsigned int)));
+    CK(cudaMemset(c->g5_tickets, 0, G5_TICKETS * sizeof(unsigned int)));
+    CK(cudaMalloc(&c->att_ws, (size_t)ATT_PART_ENTRIES * c->G * (p.head_dim + 2) * 4));
+    CK(cudaMalloc(&c->att_tickets, ATT_PART_ENTRIES * sizeof(unsigned int)));
+    CK(cudaMemset(c->att_tickets, 0, ATT_PART_ENTRIES * sizeof(unsigned int)));
     c->pf_maps.assign(7 * p.n_layers, CUtensorMap{});
     const int dim = p.dim, ffn = p.ffn_dim, kvd = c->kvd;
     for (uint32_t l = 0; l < p.n_layers; l++) {
@@ -1443,6 +1473,8 @@ static int pf_alloc(gpu_context *c) {
 
 
 
+static void reset_g5_tickets(gpu_context *c);
+
 static int prefill_batched(gpu_context *c, kv_cache_t *kv, int slot, const int32_t *tokens, int n, int start_pos,
                            int32_t *argmax_out) {
     int rc = pf_alloc(c);
@@ -1460,7 +1492,10 @@ static int prefill_batched(gpu_context *c, kv_cache_t *kv, int slot, const int32
     if (e != cudaSuccess) return set_err(FIBER_ECUDA, "prefill lm_head: %s", cudaGetErrorString(e));
     CK(cudaMemcpyAsync(c->h_io, c->io, sizeof(StepIO), cudaMemcpyDeviceToHost, c->stream));
     CK(cudaStreamSynchronize(c->stream));
-    if (c->h_io->err == 6) return set_err(FIBER_ETIMEOUT, "batched prefill: a tensor-core wait timed out");
+    if (c->h_io->err == 6) {
+        reset_g5_tickets(c);
+        return set_err(FIBER_ETIMEOUT, "batched prefill: a tensor-core wait timed out");
+    }
     if ((rc = device_status(c))) return rc;
     if (argmax_out) *argmax_out = c->h_io->argmax;
     return FIBER_OK;
@@ -1533,8 +1568,18 @@ static int batch_checks(gpu_context *c, kv_cache_t *kv, const int32_t *tokens, c
     return FIBER_OK;
 }
 
+// After a timed-out GEMM, split-K tickets may be left non-zero.
+static void reset_g5_tickets(gpu_context *c) {
+    if (c->g5_tickets) cudaMemset(c->g5_tickets, 0, G5_TICKETS * sizeof(unsigned int));
+    if (c->att_tickets) cudaMemset(c->att_tickets, 0, ATT_PART_ENTRIES * sizeof(unsigned int));
+    cudaDeviceSynchronize();
+}
+
 static int batch_status(gpu_context *c) {
-    if (c->h_io->err == 6) return set_err(FIBER_ETIMEOUT, "batched decode: a tensor-core wait timed out");
+    if (c->h_io->err == 6) {
+        reset_g5_tickets(c);
+        return set_err(FIBER_ETIMEOUT, "batched decode: a tensor-core wait timed out");
+    }
     if (c->h_io->err == 3) return set_err(FIBER_EARG, "batched decode: a position left the cache on the device");
     return device_status(c);
 }
@@ -1845,7 +1890,7 @@ static cudaError_t launch_g5_t(const G5Params &p, cudaStream_t st) {
     const int smem = g5_smem_bytes(T);
     cudaError_t e = cudaFuncSetAttribute(gemm_tc5_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
-    const dim3 grid((p.rows + G5_M - 1) / G5_M, (p.ntok + G5_T - 1) / G5_T);
+    const dim3 grid((p.rows + G5_M - 1) / G5_M, (p.ntok + G5_T - 1) / G5_T, p.ksplit > 1 ? p.ksplit : 1);
     gemm_tc5_kernel<T><<<grid, G5_THREADS, smem, st>>>(p);
     return cudaGetLastError();
 }
@@ -1902,12 +1947,22 @@ extern "C" int fiber_gemm(int ggml_type, const void *d_w, int rows, int cols, co
     p.out_off = out_off;
     p.epi = accumulate ? G5_RESID : G5_STORE;
     p.err = err;
-    cudaError_t e = launch_g5_pack(a, st);
+    p.ksplit = g5_choose_ksplit(ggml_type, rows, cols, ntok, sm_count());
+    cudaError_t e = cudaSuccess;
+    if (p.ksplit > 1) {
+        const int tiles = ((rows + G5_M - 1) / G5_M) * ((ntok + G5_T - 1) / G5_T);
+        e = cudaMalloc(&p.ws, (size_t)p.ksplit * tiles * G5_T * G5_M * 4);
+        if (e == cudaSuccess) e = cudaMalloc(&p.tickets, (size_t)tiles * sizeof(unsigned int));
+        if (e == cudaSuccess) e = cudaMemsetAsync(p.tickets, 0, (size_t)tiles * sizeof(unsigned int), st);
+    }
+    if (e == cudaSuccess) e = launch_g5_pack(a, st);
     if (e == cudaSuccess) e = launch_g5(p, st);
     int h_err = 0;
     if (e == cudaSuccess) e = cudaMemcpyAsync(&h_err, err, sizeof(int), cudaMemcpyDeviceToHost, st);
     if (e == cudaSuccess) e = cudaStreamSynchronize(st);
     cudaFree(bp);
+    if (p.ws) cudaFree(p.ws);
+    if (p.tickets) cudaFree(p.tickets);
     if (e != cudaSuccess) return set_err(FIBER_ECUDA, "fiber_gemm: %s", cudaGetErrorString(e));
     if (h_err == 5) return set_err(FIBER_EARG, "fiber_gemm: an input value does not fit fp16");
     if (h_err) return set_err(FIBER_ETIMEOUT, "fiber_gemm: a tensor-core wait timed out");

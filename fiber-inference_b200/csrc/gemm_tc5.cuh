@@ -67,7 +67,28 @@ struct G5Params {
     int ldy, out_off;
     int epi;               // G5_STORE: y = acc; G5_RESID: y += acc
     int *err;              // set to 6 when a wait gave up
+    // split-K (gridDim.z = ksplit > 1): CTA z covers K units [z U / ksplit, (z+1) U / ksplit)
+    // of the U = cols / 256 super-block columns (F16: cols / 128 chunks), writes its fp32
+    // tile to ws, and the last CTA of a tile (ticket) adds the ksplit tiles in order z = 0..
+    int ksplit;            // host side: gridDim.z
+    float *ws;             // [ksplit][token tiles][row tiles][64 tokens][128 rows]
+    unsigned int *tickets; // [token tiles][row tiles], zero between launches
 };
+
+constexpr int G5_WS_TILES = 512;      // partial tiles a split-K launch may write
+constexpr int G5_TICKETS = 4096;      // tiles a split-K launch may have
+
+// Splits of K for a launch of rows x ntok over cols: only when the tiles alone leave
+// most SMs idle; whole K units per split, at most one split per unit.
+HDCE int g5_choose_ksplit(int type, int rows, int cols, int ntok, int n_sm) {
+    const int base = ((rows + G5_M - 1) / G5_M) * ((ntok + G5_T - 1) / G5_T);
+    const int units = type == T_F16 ? cols / G5_KC : cols / 256;
+    if (base * 3 >= n_sm * 2 || base > G5_TICKETS) return 1;
+    int ks = (n_sm + base - 1) / base;
+    if (ks > units) ks = units;
+    if (ks * base > G5_WS_TILES) ks = G5_WS_TILES / base;
+    return ks < 1 ? 1 : ks;
+}
 
 struct G5PackParams {
     const float *x;        // [ntok][ldx]
@@ -273,21 +294,30 @@ FDEV size_t g5_bp_off(int tile, int nchunk, int n, int g) {
     return ((size_t)(tile * nchunk + (g >> 4)) << 15) + (size_t)((((n >> 3) * 16) + (g & 15)) << 7) + ((n & 7) << 4);
 }
 
-// One CTA (128 threads) per 4 tokens = one 8-row group of a token tile: optional
-// per-token 1/rms, then for every K group of 8 the hi or lo fp16 parts in slot order
-// k0 k2 k1 k3 k4 k6 k5 k7. Tokens past ntok get zero rows.
+// One CTA (128 threads) per 4 tokens (one 8-row group of a token tile) and 256 columns:
+// optional per-token 1/rms (over the whole row), then for each K group of 8 the hi or
+// lo fp16 parts in slot order k0 k2 k1 k3 k4 k6 k5 k7. Tokens past ntok get zero rows.
+constexpr int G5_PACK_COLS = 256;
+
 __global__ void __launch_bounds__(128) g5_pack_kernel(const G5PackParams a) {
     __shared__ float rr[4];
     const int tile = blockIdx.x >> 4, grp = blockIdx.x & 15, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int t0 = tile * G5_T + 4 * grp, nchunk = a.cols / G5_KC;
+    const int t0 = tile * G5_T + 4 * grp, nchunk = a.cols / G5_KC, col0 = blockIdx.y * G5_PACK_COLS;
     {
         const int t = t0 + warp;
         float r = 1.0f;
         if (t < a.ntok && a.nw) {
             if (a.own_rms) {
-                const float *x = a.x + (size_t)t * a.ldx;
-                float ss = 0.f;
-                for (int i = lane; i < a.cols; i += 32) ss = fmaf(x[i], x[i], ss);
+                const float4 *x = reinterpret_cast<const float4 *>(a.x + (size_t)t * a.ldx);
+                float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+                for (int i = lane; i < a.cols / 4; i += 32) {
+                    const float4 v = x[i];
+                    s0 = fmaf(v.x, v.x, s0);
+                    s1 = fmaf(v.y, v.y, s1);
+                    s2 = fmaf(v.z, v.z, s2);
+                    s3 = fmaf(v.w, v.w, s3);
+                }
+                float ss = (s0 + s1) + (s2 + s3);
 #pragma unroll
                 for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
                 r = 1.0f / sqrtf(ss / (float)a.cols + a.eps);
@@ -299,8 +329,9 @@ __global__ void __launch_bounds__(128) g5_pack_kernel(const G5PackParams a) {
     }
     __syncthreads();
     bool bad = false;
-    for (int i = tid; i < a.cols; i += 128) {
-        const int g = i >> 3, nr = i & 7, tt = nr >> 1, t = t0 + tt;
+#pragma unroll
+    for (int it = 0; it < G5_PACK_COLS / 128; it++) {  // items (K group g, B row nr): 2 per thread
+        const int i = tid + 128 * it, g = (col0 >> 3) + (i >> 3), nr = i & 7, tt = nr >> 1, t = t0 + tt;
         uint4 out = make_uint4(0u, 0u, 0u, 0u);
         if (t < a.ntok) {
             const float4 *xp = reinterpret_cast<const float4 *>(a.x + (size_t)t * a.ldx + 8 * g);
@@ -342,9 +373,13 @@ __global__ void __launch_bounds__(G5_THREADS, 1) gemm_tc5_kernel(const __grid_co
     uint8_t *const Abuf = g5_smem;                             // [2][AP][G5_A_BYTES]
     uint8_t *const Bbuf = g5_smem + 2 * AS;                    // [NB][G5_B_BYTES]
     uint8_t *const Rbuf = g5_smem + 2 * AS + NB * G5_B_BYTES;  // [NR][128 rows x S]
+    __shared__ int last_cta;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int row0 = blockIdx.x * G5_M, tile = blockIdx.y;
-    const int nchunk = p.cols / G5_KC;
+    const int row0 = blockIdx.x * G5_M, tile = blockIdx.y, ks = gridDim.z, kz = blockIdx.z;
+    const int nchunk = p.cols / G5_KC, nunit = nchunk / CPU;
+    // this CTA's chunks: [cb, ce) = whole K units of its split
+    const int cb = (int)((long long)kz * nunit / ks) * CPU, ce = (int)((long long)(kz + 1) * nunit / ks) * CPU;
+    const int nloc = ce - cb;
     const int vrows = min(G5_M, p.rows - row0);
     const size_t row_bytes = (size_t)(p.cols / 256) * BB;
 
@@ -381,15 +416,16 @@ __global__ void __launch_bounds__(G5_THREADS, 1) gemm_tc5_kernel(const __grid_co
     if (warp == 0) {
         // ---- producer: raw stage u % NR <- K unit u of the 128 rows; B stage c % NB <- the
         // packed inputs of chunk c. Issue order: unit u before its chunks.
-        int c = 0, u = 0;
+        int i = 0, ui = 0;  // local chunk / unit counters (ring slots and parities)
         bool ok = true;
-        for (; c < nchunk && ok; c++) {
-            if (c % CPU == 0) {
-                const int rs = u % NR;
-                if (u >= NR) ok = g5_wait(&rempty[rs], (uint32_t)((u / NR - 1) & 1), &fail);
+        for (; i < nloc && ok; i++) {
+            const int c = cb + i;
+            if (i % CPU == 0) {
+                const int rs = ui % NR, u = c / CPU;
+                if (ui >= NR) ok = g5_wait(&rempty[rs], (uint32_t)((ui / NR - 1) & 1), &fail);
                 ok = __all_sync(0xffffffffu, ok);
                 if (!ok) break;
-                G5_MARK(0, c);
+                G5_MARK(0, i);
                 uint8_t *dst = Rbuf + rs * (G5_M * S);
                 if (T == T_Q6_K) {
                     if (lane == 0) g5_expect_tx(&rfull[rs], (uint32_t)(vrows * S));
@@ -410,10 +446,10 @@ __global__ void __launch_bounds__(G5_THREADS, 1) gemm_tc5_kernel(const __grid_co
                         "l"(reinterpret_cast<uint64_t>(&p.wmap)), "r"(x), "r"(row0), "r"(g5_saddr(&rfull[rs]))
                         : "memory");
                 }
-                u++;
+                ui++;
             }
-            const int s = c % NB;
-            if (c >= NB) ok = g5_wait(&bempty[s], (uint32_t)((c / NB - 1) & 1), &fail);
+            const int s = i % NB;
+            if (i >= NB) ok = g5_wait(&bempty[s], (uint32_t)((i / NB - 1) & 1), &fail);
             ok = __all_sync(0xffffffffu, ok);
             if (!ok) break;
             if (lane == 0) {
@@ -421,25 +457,25 @@ __global__ void __launch_bounds__(G5_THREADS, 1) gemm_tc5_kernel(const __grid_co
                 g5_bulk(Bbuf + s * G5_B_BYTES, p.bp + ((size_t)(tile * nchunk + c) << 15), (uint32_t)G5_B_BYTES,
                         &bfull[s]);
             }
-            G5_MARK(1, c);
+            G5_MARK(1, i);
         }
         // every copy issued has landed before the CTA exits
         if (lane == 0) {
-            for (int s = 0; s < NB && s < c; s++)
-                g5_drain(&bfull[s], (uint32_t)(((s + ((c - 1 - s) / NB) * NB) / NB) & 1));
-            for (int s = 0; s < NR && s < u; s++)
-                g5_drain(&rfull[s], (uint32_t)(((s + ((u - 1 - s) / NR) * NR) / NR) & 1));
+            for (int s = 0; s < NB && s < i; s++)
+                g5_drain(&bfull[s], (uint32_t)(((s + ((i - 1 - s) / NB) * NB) / NB) & 1));
+            for (int s = 0; s < NR && s < ui; s++)
+                g5_drain(&rfull[s], (uint32_t)(((s + ((ui - 1 - s) / NR) * NR) / NR) & 1));
         }
     } else if (warp == 1) {
         // ---- MMA issuer
         if (lane == 0) {
-            int c = 0;
-            for (; c < nchunk; c++) {
-                const int s = c % NB, a = c & 1;
-                if (!g5_wait(&bfull[s], (uint32_t)((c / NB) & 1), &fail)) break;
-                G5_MARK(6, c);
-                if (!g5_wait(&afull[a], (uint32_t)((c >> 1) & 1), &fail)) break;
-                G5_MARK(7, c);
+            int i = 0;
+            for (; i < nloc; i++) {
+                const int s = i % NB, a = i & 1;
+                if (!g5_wait(&bfull[s], (uint32_t)((i / NB) & 1), &fail)) break;
+                G5_MARK(6, i);
+                if (!g5_wait(&afull[a], (uint32_t)((i >> 1) & 1), &fail)) break;
+                G5_MARK(7, i);
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                 const uint32_t b0 = g5_saddr(Bbuf + s * G5_B_BYTES);
 #pragma unroll
@@ -448,7 +484,7 @@ __global__ void __launch_bounds__(G5_THREADS, 1) gemm_tc5_kernel(const __grid_co
 #pragma unroll
                     for (int k = 0; k < G5_KC / 16; k++) {
                         const uint64_t da = g5_desc(a0 + k * 256), db = g5_desc(b0 + k * 256);
-                        const uint32_t acc = (c > 0 || part > 0 || k > 0) ? 1u : 0u;
+                        const uint32_t acc = (i > 0 || part > 0 || k > 0) ? 1u : 0u;
                         asm volatile(
                             "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
                             " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem),
@@ -458,10 +494,10 @@ __global__ void __launch_bounds__(G5_THREADS, 1) gemm_tc5_kernel(const __grid_co
                 }
                 g5_commit(&bempty[s]);
                 g5_commit(&afree[a]);
-                G5_MARK(8, c);
+                G5_MARK(8, i);
             }
-            if (c > 0) g5_commit(&accb);  // completes when every issued MMA has
-            n_issued = c;
+            if (i > 0) g5_commit(&accb);  // completes when every issued MMA has
+            n_issued = i;
         }
     } else {
         // ---- decoders: thread (row r, half sub of the chunk's 128 K)
@@ -470,12 +506,12 @@ __global__ void __launch_bounds__(G5_THREADS, 1) gemm_tc5_kernel(const __grid_co
                               ? (int)((reinterpret_cast<uintptr_t>(p.w + (size_t)(row0 + r) * row_bytes)) & 15)
                               : 0;
         bool ok = true;
-        for (int c = 0; c < nchunk && ok; c++) {
-            const int u = c / CPU, rs = u % NR, a = c & 1;
-            ok = g5_wait(&rfull[rs], (uint32_t)((u / NR) & 1), &fail);
-            G5_MARK(2, c);
-            if (ok && c >= 2) ok = g5_wait(&afree[a], (uint32_t)(((c >> 1) - 1) & 1), &fail);
-            G5_MARK(3, c);
+        for (int i = 0; i < nloc && ok; i++) {
+            const int c = cb + i, u = c / CPU, ui = i / CPU, rs = ui % NR, a = i & 1;
+            ok = g5_wait(&rfull[rs], (uint32_t)((ui / NR) & 1), &fail);
+            G5_MARK(2, i);
+            if (ok && i >= 2) ok = g5_wait(&afree[a], (uint32_t)(((i >> 1) - 1) & 1), &fail);
+            G5_MARK(3, i);
             ok = __all_sync(0xffffffffu, ok);  // warp-uniform exit (the warp arrives as one)
             if (!ok) break;
             // Q6_K: the span starts at the 16-byte boundary at or below the block
@@ -486,13 +522,13 @@ __global__ void __launch_bounds__(G5_THREADS, 1) gemm_tc5_kernel(const __grid_co
             __syncwarp();
             if (lane == 0) {
                 g5_arrive(&afull[a]);
-                if (c % CPU == CPU - 1) g5_arrive(&rempty[rs]);
+                if (i % CPU == CPU - 1) g5_arrive(&rempty[rs]);
             }
-            G5_MARK(4, c);
+            G5_MARK(4, i);
         }
         // ---- epilogue: warp w reads TMEM lanes 32 (w % 4) .. +31 (= weight rows), column
         // half (w - 2) / 4 (32 tokens x hi / lo)
-        const bool epi = ok && nchunk > 0 && g5_wait(&accb, 0u, &fail);
+        const bool epi = ok && nloc > 0 && g5_wait(&accb, 0u, &fail);
         if (__all_sync(0xffffffffu, epi)) {  // tcgen05.ld needs the whole warp
             G5_MARK(9, 0);
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
@@ -509,7 +545,12 @@ __global__ void __launch_bounds__(G5_THREADS, 1) gemm_tc5_kernel(const __grid_co
                     : "r"(addr)
                     : "memory");
                 asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-                if (rr < vrows) {
+                if (ks > 1) {  // this split's partial tile, [token][row]
+                    float *w = p.ws + ((size_t)(kz * gridDim.y + tile) * gridDim.x + blockIdx.x) * (G5_T * G5_M);
+#pragma unroll
+                    for (int j = 0; j < 8; j++)
+                        w[(c0 / 2 + j) * G5_M + rr] = __fadd_rn(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1]));
+                } else if (rr < vrows) {
 #pragma unroll
                     for (int j = 0; j < 8; j++) {
                         const int t = tile * G5_T + c0 / 2 + j;
@@ -526,6 +567,29 @@ __global__ void __launch_bounds__(G5_THREADS, 1) gemm_tc5_kernel(const __grid_co
     G5_MARK(10, 0);
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
+    if (ks > 1 && !fail) {
+        // the last of the ks CTAs of this tile adds the partial tiles in split order
+        unsigned int *ticket = p.tickets + (size_t)tile * gridDim.x + blockIdx.x;
+        if (tid == 0) {
+            __threadfence();
+            last_cta = atomicAdd(ticket, 1u) == (unsigned int)(ks - 1);
+            if (last_cta) __threadfence();
+        }
+        __syncthreads();
+        if (last_cta) {
+            const size_t tstride = (size_t)gridDim.y * gridDim.x * (G5_T * G5_M);
+            const float *w0 = p.ws + ((size_t)tile * gridDim.x + blockIdx.x) * (G5_T * G5_M);
+            for (int e = tid; e < G5_T * G5_M; e += G5_THREADS) {
+                const int t = tile * G5_T + e / G5_M, r = e % G5_M;
+                if (t >= p.ntok || r >= vrows) continue;
+                float y = __ldcg(w0 + e);
+                for (int z = 1; z < ks; z++) y = __fadd_rn(y, __ldcg(w0 + z * tstride + e));
+                float *dst = p.y + (size_t)t * p.ldy + p.out_off + row0 + r;
+                *dst = p.epi == G5_RESID ? __fadd_rn(*dst, y) : y;
+            }
+            if (tid == 0) *ticket = 0u;  // ready for the next launch
+        }
+    }
     if (fail) {
         // let the committed MMAs finish before the tensor memory is released
         if (tid == 0) {

@@ -108,11 +108,17 @@ struct AttnPrefillParams {
     const int32_t *page_table;
     int layer, n_layers, n_kv, n_heads;
     float scale;
+    // page split (gridDim.z = psplit > 1): CTA z takes pages [z P', (z+1) P') of the
+    // token's context, P' = ceil(pages / psplit); it writes its softmax state (max, sum,
+    // unnormalised output per head) to part, and the last CTA of (token, KV head)
+    // (ticket) merges the psplit states in split order
+    float *part;            // [n][n_kv][psplit][G][HD + 2]
+    unsigned int *tickets;  // [n][n_kv], zero between launches
 };
 
-// CTA (token t, KV head g): the G query heads of g attend to positions 0 .. pos(t) of
-// the token's slot, page by page (64 positions) with the decode path's score / softmax
-// / P.V arithmetic, pages combined online.
+// CTA (token t, KV head g[, page split z]): the G query heads of g attend to positions
+// 0 .. pos(t) of the token's slot, page by page (64 positions) with the decode path's
+// score / softmax / P.V arithmetic, pages combined online.
 template <int HD, int G>
 __global__ void __launch_bounds__(ATTN_THREADS) attn_prefill_kernel(const AttnPrefillParams a) {
     constexpr int P = ATTN_P, KST = HD + 2, DPL = HD / 32;
@@ -124,13 +130,16 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_prefill_kernel(const AttnPr
     if (pos < 0 || pos >= a.at.max_pos) return;  // rope_kv_kernel reported it
     const int seqlen = pos + 1, nch = (seqlen + P - 1) / P;
     const int32_t *pages = place_pages(a.at, a.page_table, t);
+    const int ps = gridDim.z, z = blockIdx.z, per = (nch + ps - 1) / ps;
+    const int cbeg = min(nch, z * per), cend = min(nch, cbeg + per);
     for (int i = tid; i < G * HD; i += ATTN_THREADS)
         qs[i / HD][i % HD] = a.qkv[(size_t)t * a.ldq + (size_t)(g * G + i / HD) * HD + i % HD];
     float m_run = -INFINITY, l_run = 0.f, o_run[DPL];
 #pragma unroll
     for (int j = 0; j < DPL; j++) o_run[j] = 0.f;
-    for (int c = 0; c < nch; c++) {
-        __syncthreads();  // previous page consumed (and qs staged)
+    __syncthreads();  // qs staged
+    for (int c = cbeg; c < cend; c++) {
+        __syncthreads();  // previous page consumed
         const int t0 = c * P, nt = min(P, seqlen - t0);
         const size_t base = (((size_t)pages[c] * a.n_layers + a.layer) * a.n_kv + g) * (size_t)P * HD;
         constexpr int V8 = HD / 8;
@@ -182,7 +191,7 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_prefill_kernel(const AttnPr
                 for (int j = 0; j < DPL; j++) o2[j] = fmaf(w, __half2float(__ushort_as_half(vs[r][lane + 32 * j])), o2[j]);
             }
             // G <= 8 heads: warp h keeps head h's running state across pages
-            if (c == 0) {
+            if (c == cbeg) {
                 m_run = m;
                 l_run = l;
 #pragma unroll
@@ -197,10 +206,53 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_prefill_kernel(const AttnPr
             }
         }
     }
-    if (warp < G)
+    if (ps == 1) {
+        if (warp < G)
 #pragma unroll
-        for (int j = 0; j < DPL; j++)
-            a.out[(size_t)t * a.ldo + (size_t)(g * G + warp) * HD + lane + 32 * j] = o_run[j] / l_run;
+            for (int j = 0; j < DPL; j++)
+                a.out[(size_t)t * a.ldo + (size_t)(g * G + warp) * HD + lane + 32 * j] = o_run[j] / l_run;
+        return;
+    }
+    constexpr int ST = HD + 2;  // one head's state: max, sum, output
+    float *mine = a.part + (((size_t)t * a.n_kv + g) * ps + z) * (G * ST);
+    if (warp < G) {
+#pragma unroll
+        for (int j = 0; j < DPL; j++) mine[warp * ST + 2 + lane + 32 * j] = o_run[j];
+        if (lane == 0) {
+            mine[warp * ST] = m_run;
+            mine[warp * ST + 1] = l_run;
+        }
+    }
+    __syncthreads();
+    __shared__ int last;
+    unsigned int *ticket = a.tickets + (size_t)t * a.n_kv + g;
+    if (tid == 0) {
+        __threadfence();
+        last = atomicAdd(ticket, 1u) == (unsigned int)(ps - 1);
+        if (last) __threadfence();
+    }
+    __syncthreads();
+    if (!last) return;
+    if (warp < G) {
+        const float *all = a.part + ((size_t)t * a.n_kv + g) * ps * (G * ST) + warp * ST;
+        float M = -INFINITY;
+        for (int q = 0; q < ps; q++) M = fmaxf(M, __ldcg(all + (size_t)q * G * ST));
+        float L = 0.f, o[DPL];
+#pragma unroll
+        for (int j = 0; j < DPL; j++) o[j] = 0.f;
+        for (int q = 0; q < ps; q++) {
+            const float *st = all + (size_t)q * G * ST;
+            const float mq = __ldcg(st);
+            if (mq == -INFINITY) continue;  // a split without pages
+            const float w = expf(mq - M);
+            L = fmaf(w, __ldcg(st + 1), L);
+#pragma unroll
+            for (int j = 0; j < DPL; j++) o[j] = fmaf(w, __ldcg(st + 2 + lane + 32 * j), o[j]);
+        }
+#pragma unroll
+        for (int j = 0; j < DPL; j++) a.out[(size_t)t * a.ldo + (size_t)(g * G + warp) * HD + lane + 32 * j] = o[j] / L;
+    }
+    if (tid == 0) *ticket = 0u;
 }
 
 __global__ void swiglu_rows_kernel(float *hg, const float *__restrict__ hu, size_t n) {
