@@ -393,6 +393,8 @@ struct gpu_context {
     float *pf_x = nullptr, *pf_qkv = nullptr, *pf_att = nullptr, *pf_hg = nullptr, *pf_hu = nullptr;
     uint8_t *pf_bp = nullptr;          // GEMM input packed as the MMA's B operand (hi / lo fp16)
     std::vector<CUtensorMap> pf_maps;  // per layer: tensor maps of wq wk wv wo w1 w2 w3
+    std::vector<const uint8_t *> pf_w; // per layer: the GEMMs' weights (wq .. w3; padded Q6_K copies)
+    const uint8_t *pf_out = nullptr;   // the classifier as the GEMM reads it
     int32_t *pf_tok = nullptr;
     // batched decode: max_batch sequences per step, sequence t in KV slot t
     int max_batch = 1;
@@ -404,8 +406,7 @@ struct gpu_context {
     int g_batch_n = 0;
     float *att_ws = nullptr;           // page-split attention states (batched layer pass)
     unsigned int *att_tickets = nullptr;
-    float *g5_ws = nullptr;            // split-K partial tiles of the GEMMs
-    unsigned int *g5_tickets = nullptr;  // split-K tickets (zero between launches)
+    std::vector<void *> pf_pad;        // Q6_K matrices re-laid with 16-byte-aligned rows
 };
 
 static void free_graph(Graph &g) {
@@ -422,7 +423,8 @@ extern "C" void fiber_cuda_free(fiber_ctx_t *c) {
     free_graph(c->g_loop);
     free_graph(c->g_batch);
     if (c->comm) ncclCommDestroy(c->comm);
-    void *dev[] = {c->att_ws, c->att_tickets, c->g5_ws, c->g5_tickets, c->bt_pos, c->bt_arg, c->bt_rec, c->bt_step, c->bt_logits, c->pf_x, c->pf_qkv, c->pf_att, c->pf_hg, c->pf_hu, c->pf_bp, c->pf_tok, c->x2, c->d_shard, c->d_data, c->x, c->qkv, c->att, c->h, c->logits, c->rope, c->io, c->rec,
+    for (void *q : c->pf_pad) cudaFree(q);
+    void *dev[] = {c->att_ws, c->att_tickets, c->bt_pos, c->bt_arg, c->bt_rec, c->bt_step, c->bt_logits, c->pf_x, c->pf_qkv, c->pf_att, c->pf_hg, c->pf_hu, c->pf_bp, c->pf_tok, c->x2, c->d_shard, c->d_data, c->x, c->qkv, c->att, c->h, c->logits, c->rope, c->io, c->rec,
                    c->att_part, c->att_cnt, c->am_part, c->am_cnt, c->d_phases, c->d_bar,
                    c->pk_gf[0], c->pk_gf[1], c->pk_gf[2], c->pk_gf[3], c->pk_ss[0], c->pk_ss[1]};
     for (void *p : dev)
@@ -1249,11 +1251,18 @@ static cudaError_t launch_embed_rows(const gpu_context *c, const int32_t *tok, f
     return cudaGetLastError();
 }
 
-// 2D tensor map over a Q4_K / Q5_K (bytes) or F16 (fp16 elements) weight matrix with a
-// box of 128 rows x one K unit (a super-block / 128 values); Q6_K needs none.
+// Row length in bytes of a weight matrix as the GEMM reads it: Q6_K rows are padded to
+// a multiple of 16 bytes (tensor copies need 16-byte-aligned row strides).
+static size_t g5_row_bytes(int type, int cols) {
+    const size_t rb = (size_t)cols / 256 * block_bytes(type);
+    return type == T_Q6_K ? (rb + 15) / 16 * 16 : rb;
+}
+
+// 2D tensor map over a weight matrix (rows of g5_row_bytes, 16-byte aligned) with a box
+// of 128 rows x one K unit: a super-block (Q4_K 144, Q5_K 176 bytes; Q6_K the 224-byte
+// span around its 210-byte block) or 128 fp16 values.
 static bool g5_make_map(CUtensorMap *map, const uint8_t *w, int type, int rows, int cols) {
     memset(map, 0, sizeof(*map));
-    if (type != T_Q4_K && type != T_Q5_K && type != T_F16) return true;
     static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
     if (!encode) {
         void *fn = nullptr;
@@ -1265,8 +1274,8 @@ static bool g5_make_map(CUtensorMap *map, const uint8_t *w, int type, int rows, 
         encode = (PFN_cuTensorMapEncodeTiled_v12000)fn;
     }
     const bool q4 = type != T_F16;  // byte elements, one super-block per box row
-    const cuuint32_t bb = type == T_Q4_K ? 144u : 176u;
-    const cuuint64_t row_bytes = q4 ? (cuuint64_t)cols / 256 * bb : (cuuint64_t)cols * 2;
+    const cuuint32_t bb = type == T_Q4_K ? 144u : (type == T_Q5_K ? 176u : 224u);
+    const cuuint64_t row_bytes = g5_row_bytes(type, cols);
     const cuuint64_t dims[2] = {q4 ? row_bytes : (cuuint64_t)cols, (cuuint64_t)rows};
     const cuuint64_t strides[1] = {row_bytes};
     const cuuint32_t box[2] = {q4 ? bb : 128u, (cuuint32_t)G5_M};
@@ -1274,6 +1283,28 @@ static bool g5_make_map(CUtensorMap *map, const uint8_t *w, int type, int rows, 
     return encode(map, q4 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, (void *)w, dims, strides,
                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// The weights as the GEMM reads them: w itself, or for Q6_K rows that are not a multiple
+// of 16 bytes long a copy with padded rows (kept in c->pf_pad, or handed to the caller
+// to free when c is null).
+static cudaError_t g5_weights(gpu_context *c, const uint8_t *w, int type, int rows, int cols, const uint8_t **out,
+                              void **owned = nullptr) {
+    const size_t rb = (size_t)cols / 256 * block_bytes(type), prb = g5_row_bytes(type, cols);
+    *out = w;
+    if (prb == rb) return cudaSuccess;
+    void *d = nullptr;
+    cudaError_t e = cudaMalloc(&d, prb * rows);
+    if (e != cudaSuccess) return e;
+    e = cudaMemcpy2D(d, prb, w, rb, rb, rows, cudaMemcpyDeviceToDevice);
+    if (e != cudaSuccess) {
+        cudaFree(d);
+        return e;
+    }
+    if (c) c->pf_pad.push_back(d);
+    if (owned) *owned = d;
+    *out = (const uint8_t *)d;
+    return cudaSuccess;
 }
 
 static cudaError_t launch_g5_pack(const G5PackParams &a, cudaStream_t st) {
@@ -1315,9 +1346,6 @@ static cudaError_t pf_gemm(gpu_context *c, const CUtensorMap &map, const uint8_t
     g.out_off = off;
     g.epi = acc ? G5_RESID : G5_STORE;
     g.err = &c->io->err;
-    g.ksplit = g5_choose_ksplit(type, rows, cols, n, sm_count());
-    g.ws = c->g5_ws;
-    g.tickets = c->g5_tickets;
     return launch_g5(g, st);
 }
 
@@ -1332,10 +1360,11 @@ static cudaError_t enqueue_layers(gpu_context *c, const kv_cache_t *kv, int n, c
     for (uint32_t l = 0; l < p.n_layers && e == cudaSuccess; l++) {
         const LayerDev &d = c->L[l];
         const CUtensorMap *mp = &c->pf_maps[7 * l];
+        const uint8_t *const *pw = &c->pf_w[7 * l];
         if ((e = pf_pack(c, c->pf_x, dim, d.attn_norm, n, st))) break;
-        if ((e = pf_gemm(c, mp[0], d.wq, d.tq, dim, dim, c->pf_qkv, ldq, 0, false, n, st))) break;
-        if ((e = pf_gemm(c, mp[1], d.wk, d.tk, kvd, dim, c->pf_qkv, ldq, dim, false, n, st))) break;
-        if ((e = pf_gemm(c, mp[2], d.wv, d.tv, kvd, dim, c->pf_qkv, ldq, dim + kvd, false, n, st))) break;
+        if ((e = pf_gemm(c, mp[0], pw[0], d.tq, dim, dim, c->pf_qkv, ldq, 0, false, n, st))) break;
+        if ((e = pf_gemm(c, mp[1], pw[1], d.tk, kvd, dim, c->pf_qkv, ldq, dim, false, n, st))) break;
+        if ((e = pf_gemm(c, mp[2], pw[2], d.tv, kvd, dim, c->pf_qkv, ldq, dim + kvd, false, n, st))) break;
         RopeKvParams rk;
         rk.qkv = c->pf_qkv;
         rk.ldq = ldq;
@@ -1369,14 +1398,14 @@ static cudaError_t enqueue_layers(gpu_context *c, const kv_cache_t *kv, int n, c
         ap.tickets = c->att_tickets;
         if ((e = launch_attn_prefill(c, ap, n, st))) break;
         if ((e = pf_pack(c, c->pf_att, dim, nullptr, n, st))) break;
-        if ((e = pf_gemm(c, mp[3], d.wo, d.to, dim, dim, c->pf_x, dim, 0, true, n, st))) break;
+        if ((e = pf_gemm(c, mp[3], pw[3], d.to, dim, dim, c->pf_x, dim, 0, true, n, st))) break;
         if ((e = pf_pack(c, c->pf_x, dim, d.ffn_norm, n, st))) break;
-        if ((e = pf_gemm(c, mp[4], d.w1, d.t1, ffn, dim, c->pf_hg, ffn, 0, false, n, st))) break;
-        if ((e = pf_gemm(c, mp[6], d.w3, d.t3, ffn, dim, c->pf_hu, ffn, 0, false, n, st))) break;
+        if ((e = pf_gemm(c, mp[4], pw[4], d.t1, ffn, dim, c->pf_hg, ffn, 0, false, n, st))) break;
+        if ((e = pf_gemm(c, mp[6], pw[6], d.t3, ffn, dim, c->pf_hu, ffn, 0, false, n, st))) break;
         swiglu_rows_kernel<<<(n * ffn + 255) / 256, 256, 0, st>>>(c->pf_hg, c->pf_hu, (size_t)n * ffn);
         if ((e = cudaGetLastError()) != cudaSuccess) break;
         if ((e = pf_pack(c, c->pf_hg, ffn, nullptr, n, st))) break;
-        e = pf_gemm(c, mp[5], d.w2, d.t2, dim, ffn, c->pf_x, dim, 0, true, n, st);
+        e = pf_gemm(c, mp[5], pw[5], d.t2, dim, ffn, c->pf_x, dim, 0, true, n, st);
     }
     return e;
 }
@@ -1417,7 +1446,7 @@ static cudaError_t enqueue_batch_step(gpu_context *c, const kv_cache_t *kv, int 
     cudaError_t e = launch_embed_rows(c, c->pf_tok, c->pf_x, n, st);
     if (e == cudaSuccess) e = enqueue_layers(c, kv, n, at, st);
     if (e == cudaSuccess) e = pf_pack(c, c->pf_x, dim, c->out_norm, n, st);
-    if (e == cudaSuccess) e = pf_gemm(c, c->out_map, c->out, c->t_out, V, dim, c->bt_logits, V, 0, false, n, st);
+    if (e == cudaSuccess) e = pf_gemm(c, c->out_map, c->pf_out, c->t_out, V, dim, c->bt_logits, V, 0, false, n, st);
     if (e == cudaSuccess) {
         argmax_rows_kernel<<<n, 256, 0, st>>>(c->bt_logits, V, V, c->bt_arg);
         e = cudaGetLastError();
@@ -1448,24 +1477,26 @@ static int pf_alloc(gpu_context *c) {
     CK(cudaMalloc(&c->bt_rec, B * c->max_seq * 4));
     CK(cudaMalloc(&c->bt_step, sizeof(int)));
     CK(cudaMalloc(&c->bt_logits, B * p.vocab_size * 4));
-    CK(cudaMalloc(&c->g5_ws, (size_t)G5_WS_TILES * G5_T * G5_M * 4));
-    CK(cudaMalloc(&c->g5_tickets, G5_TICKETS * sizeof(unsigned int)));
-    CK(cudaMemset(c->g5_tickets, 0, G5_TICKETS * sizeof(unsigned int)));
     CK(cudaMalloc(&c->att_ws, (size_t)ATT_PART_ENTRIES * c->G * (p.head_dim + 2) * 4));
     CK(cudaMalloc(&c->att_tickets, ATT_PART_ENTRIES * sizeof(unsigned int)));
     CK(cudaMemset(c->att_tickets, 0, ATT_PART_ENTRIES * sizeof(unsigned int)));
     c->pf_maps.assign(7 * p.n_layers, CUtensorMap{});
+    c->pf_w.assign(7 * p.n_layers, nullptr);
     const int dim = p.dim, ffn = p.ffn_dim, kvd = c->kvd;
     for (uint32_t l = 0; l < p.n_layers; l++) {
         const LayerDev &d = c->L[l];
-        CUtensorMap *mp = &c->pf_maps[7 * l];
-        if (!g5_make_map(&mp[0], d.wq, d.tq, dim, dim) || !g5_make_map(&mp[1], d.wk, d.tk, kvd, dim) ||
-            !g5_make_map(&mp[2], d.wv, d.tv, kvd, dim) || !g5_make_map(&mp[3], d.wo, d.to, dim, dim) ||
-            !g5_make_map(&mp[4], d.w1, d.t1, ffn, dim) || !g5_make_map(&mp[5], d.w2, d.t2, dim, ffn) ||
-            !g5_make_map(&mp[6], d.w3, d.t3, ffn, dim))
-            return set_err(FIBER_ECUDA, "batched layer pass: cannot build the weight tensor maps");
+        const uint8_t *ws[7] = {d.wq, d.wk, d.wv, d.wo, d.w1, d.w2, d.w3};
+        const int ts[7] = {d.tq, d.tk, d.tv, d.to, d.t1, d.t2, d.t3};
+        const int rows[7] = {dim, kvd, kvd, dim, ffn, dim, ffn}, cols[7] = {dim, dim, dim, dim, dim, ffn, dim};
+        for (int k = 0; k < 7; k++) {
+            const uint8_t **pw = &c->pf_w[7 * l + k];
+            CK(g5_weights(c, ws[k], ts[k], rows[k], cols[k], pw));
+            if (!g5_make_map(&c->pf_maps[7 * l + k], *pw, ts[k], rows[k], cols[k]))
+                return set_err(FIBER_ECUDA, "batched layer pass: cannot build the weight tensor maps");
+        }
     }
-    if (!g5_make_map(&c->out_map, c->out, c->t_out, (int)p.vocab_size, dim))
+    CK(g5_weights(c, c->out, c->t_out, (int)p.vocab_size, dim, &c->pf_out));
+    if (!g5_make_map(&c->out_map, c->pf_out, c->t_out, (int)p.vocab_size, dim))
         return set_err(FIBER_ECUDA, "batched layer pass: cannot build the classifier tensor map");
     c->pf_cap = PF_CHUNK;
     return FIBER_OK;
@@ -1570,7 +1601,6 @@ static int batch_checks(gpu_context *c, kv_cache_t *kv, const int32_t *tokens, c
 
 // After a timed-out GEMM, split-K tickets may be left non-zero.
 static void reset_g5_tickets(gpu_context *c) {
-    if (c->g5_tickets) cudaMemset(c->g5_tickets, 0, G5_TICKETS * sizeof(unsigned int));
     if (c->att_tickets) cudaMemset(c->att_tickets, 0, ATT_PART_ENTRIES * sizeof(unsigned int));
     cudaDeviceSynchronize();
 }
@@ -1885,14 +1915,57 @@ extern "C" int fiber_dequant(int type, const void *d_w, void *d_out, int rows, i
 
 // ---- tensor-core dequant-GEMM (prefill) -------------------------------------------------
 
+// Clusters of `ks` GEMM CTAs that fit on the device at once (per device, type and ks).
+template <int T>
+static int g5_cluster_capacity(int ks) {
+    static int cache[64][G5_MAX_KSPLIT + 1];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+    int &v = cache[dev][ks];
+    if (v == 0) {
+        cudaLaunchConfig_t cfg;
+        memset(&cfg, 0, sizeof(cfg));
+        cfg.gridDim = dim3(1, 1, ks);
+        cfg.blockDim = dim3(G5_THREADS);
+        cfg.dynamicSmemBytes = g5_smem_bytes(T);
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 1;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = ks;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, gemm_tc5_kernel<T>, &cfg) != cudaSuccess || n <= 0) n = -1;
+        v = n;
+    }
+    return v;
+}
+
 template <int T>
 static cudaError_t launch_g5_t(const G5Params &p, cudaStream_t st) {
     const int smem = g5_smem_bytes(T);
     cudaError_t e = cudaFuncSetAttribute(gemm_tc5_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
-    const dim3 grid((p.rows + G5_M - 1) / G5_M, (p.ntok + G5_T - 1) / G5_T, p.ksplit > 1 ? p.ksplit : 1);
-    gemm_tc5_kernel<T><<<grid, G5_THREADS, smem, st>>>(p);
-    return cudaGetLastError();
+    // K splits: as many as help (g5_choose_ksplit) while every cluster is resident at once
+    const int base = ((p.rows + G5_M - 1) / G5_M) * ((p.ntok + G5_T - 1) / G5_T);
+    int ks = g5_choose_ksplit(T, p.rows, p.cols, p.ntok, sm_count());
+    while (ks > 1 && g5_cluster_capacity<T>(ks) < base) ks--;
+    cudaGetLastError();  // clear a failed occupancy query
+    cudaLaunchConfig_t cfg;
+    memset(&cfg, 0, sizeof(cfg));
+    cfg.gridDim = dim3((p.rows + G5_M - 1) / G5_M, (p.ntok + G5_T - 1) / G5_T, ks);
+    cfg.blockDim = dim3(G5_THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;  // the K splits of a tile: one cluster
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = ks;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, gemm_tc5_kernel<T>, p);
 }
 
 static cudaError_t launch_g5(const G5Params &p, cudaStream_t st) {
@@ -1919,8 +1992,13 @@ extern "C" int fiber_gemm(int ggml_type, const void *d_w, int rows, int cols, co
     cudaStream_t st = (cudaStream_t)stream;
     G5Params p;
     memset(&p, 0, sizeof(p));
-    if (!g5_make_map(&p.wmap, (const uint8_t *)d_w, ggml_type, rows, cols))
+    const uint8_t *w = (const uint8_t *)d_w;
+    void *pad = nullptr;  // Q6_K rows re-laid at a 16-byte stride for this call
+    CK(g5_weights(nullptr, w, ggml_type, rows, cols, &w, &pad));
+    if (!g5_make_map(&p.wmap, w, ggml_type, rows, cols)) {
+        if (pad) cudaFree(pad);
         return set_err(FIBER_ECUDA, "fiber_gemm: cannot build the weight tensor map");
+    }
     int *err = nullptr;
     CK(cudaGetSymbolAddress((void **)&err, g_g5_err));
     CK(cudaMemsetAsync(err, 0, sizeof(int), st));
@@ -1936,7 +2014,7 @@ extern "C" int fiber_gemm(int ggml_type, const void *d_w, int rows, int cols, co
     a.nw = d_nw;
     a.bp = bp;
     a.err = err;
-    p.w = (const uint8_t *)d_w;
+    p.w = w;
     p.type = ggml_type;
     p.rows = rows;
     p.cols = cols;
@@ -1947,22 +2025,13 @@ extern "C" int fiber_gemm(int ggml_type, const void *d_w, int rows, int cols, co
     p.out_off = out_off;
     p.epi = accumulate ? G5_RESID : G5_STORE;
     p.err = err;
-    p.ksplit = g5_choose_ksplit(ggml_type, rows, cols, ntok, sm_count());
-    cudaError_t e = cudaSuccess;
-    if (p.ksplit > 1) {
-        const int tiles = ((rows + G5_M - 1) / G5_M) * ((ntok + G5_T - 1) / G5_T);
-        e = cudaMalloc(&p.ws, (size_t)p.ksplit * tiles * G5_T * G5_M * 4);
-        if (e == cudaSuccess) e = cudaMalloc(&p.tickets, (size_t)tiles * sizeof(unsigned int));
-        if (e == cudaSuccess) e = cudaMemsetAsync(p.tickets, 0, (size_t)tiles * sizeof(unsigned int), st);
-    }
-    if (e == cudaSuccess) e = launch_g5_pack(a, st);
+    cudaError_t e = launch_g5_pack(a, st);
     if (e == cudaSuccess) e = launch_g5(p, st);
     int h_err = 0;
     if (e == cudaSuccess) e = cudaMemcpyAsync(&h_err, err, sizeof(int), cudaMemcpyDeviceToHost, st);
     if (e == cudaSuccess) e = cudaStreamSynchronize(st);
     cudaFree(bp);
-    if (p.ws) cudaFree(p.ws);
-    if (p.tickets) cudaFree(p.tickets);
+    if (pad) cudaFree(pad);
     if (e != cudaSuccess) return set_err(FIBER_ECUDA, "fiber_gemm: %s", cudaGetErrorString(e));
     if (h_err == 5) return set_err(FIBER_EARG, "fiber_gemm: an input value does not fit fp16");
     if (h_err) return set_err(FIBER_ETIMEOUT, "fiber_gemm: a tensor-core wait timed out");

@@ -13,10 +13,10 @@
 //   * gemm_tc5_kernel: one CTA per 128-row x 64-token tile, tcgen05.mma (kind::f16,
 //     M = 128, N = 128, fp32 accumulators in tensor memory), warp-specialised:
 //       warp 0      producer: the raw weight rows of each K unit (a super-block
-//                   column of 128 rows: one 2D tensor copy for Q4_K / Q5_K / F16, one bulk
-//                   copy per row for Q6_K, whose rows are not 16-byte aligned) into a
-//                   ring of raw stages, and each chunk's packed B block (one bulk
-//                   copy) into a ring of B stages;
+//                   column of 128 rows, one 2D tensor copy; Q6_K matrices whose rows
+//                   are not a multiple of 16 bytes long are given a copy with padded
+//                   rows) into a ring of raw stages, and each chunk's packed B block
+//                   (one bulk copy) into a ring of B stages;
 //       warp 1      one lane issues the 8 MMAs (K = 16) of each chunk and commits them
 //                   to the barriers that free the B stage and the A buffer;
 //       warps 2-9   decode the chunk's weights exactly to fp16 (the reference
@@ -58,8 +58,8 @@ constexpr unsigned long long G5_WAIT_NS = 2000000000ull;
 enum : int { G5_STORE = 0, G5_RESID = 1 };
 
 struct G5Params {
-    CUtensorMap wmap;      // Q4_K / Q5_K / F16: 2D map of the weights (box 128 rows x one K unit)
-    const uint8_t *w;      // weights, rows x cols in GGUF super-blocks
+    CUtensorMap wmap;      // 2D map of the weights: box 128 rows x one K unit (bytes / fp16)
+    const uint8_t *w;      // weights, rows x cols in GGUF super-blocks; rows 16-byte aligned
     int type;              // T_Q4_K / T_Q5_K / T_Q6_K / T_F16
     int rows, cols, ntok;
     const uint8_t *bp;     // packed B: [ceil(ntok / 64)][cols / 128] blocks of 32 KB
@@ -67,39 +67,26 @@ struct G5Params {
     int ldy, out_off;
     int epi;               // G5_STORE: y = acc; G5_RESID: y += acc
     int *err;              // set to 6 when a wait gave up
-    // split-K (gridDim.z = ksplit > 1): CTA z covers K units [z U / ksplit, (z+1) U / ksplit)
-    // of the U = cols / 256 super-block columns (F16: cols / 128 chunks), writes its fp32
-    // tile to ws, and the last CTA of a tile (ticket) adds the ksplit tiles in order z = 0..
-    int ksplit;            // host side: gridDim.z
-    float *ws;             // [ksplit][token tiles][row tiles][64 tokens][128 rows]
-    unsigned int *tickets; // [token tiles][row tiles], zero between launches
 };
+// Split-K: gridDim.z = ks CTAs per tile, launched as one thread-block cluster (1, 1, ks).
+// CTA z covers K units [z U / ks, (z+1) U / ks) of the U = cols / 256 super-block
+// columns (F16: cols / 128 chunks) and leaves its fp32 tile in shared memory; CTA z
+// then adds slice z of the tile over the cluster's CTAs in order 0 .. ks-1
+// (distributed shared memory) and stores it.
 
-constexpr int G5_WS_TILES = 512;      // partial tiles a split-K launch may write
-constexpr int G5_TICKETS = 4096;      // tiles a split-K launch may have
+constexpr int G5_MAX_KSPLIT = 8;  // portable cluster size
 
 // Splits of K for a launch of rows x ntok over cols: only when the tiles alone leave
 // most SMs idle; whole K units per split, at most one split per unit.
 HDCE int g5_choose_ksplit(int type, int rows, int cols, int ntok, int n_sm) {
     const int base = ((rows + G5_M - 1) / G5_M) * ((ntok + G5_T - 1) / G5_T);
     const int units = type == T_F16 ? cols / G5_KC : cols / 256;
-    if (base * 3 >= n_sm * 2 || base > G5_TICKETS) return 1;
+    if (base * 3 >= n_sm * 2) return 1;
     int ks = (n_sm + base - 1) / base;
     if (ks > units) ks = units;
-    if (ks * base > G5_WS_TILES) ks = G5_WS_TILES / base;
+    if (ks > G5_MAX_KSPLIT) ks = G5_MAX_KSPLIT;
     return ks < 1 ? 1 : ks;
 }
-
-struct G5PackParams {
-    const float *x;        // [ntok][ldx]
-    int ldx, ntok, cols;
-    const float *rrms;     // [ntok] or null: 1 / rms per token
-    const float *nw;       // [cols] or null: no normalisation
-    int own_rms;           // 1: compute rrms here (eps) instead of reading it
-    float eps;
-    uint8_t *bp;
-    int *err;              // set to 5 when a value does not fit fp16
-};
 
 FDEV uint64_t g5_desc(uint32_t saddr) {
     // SWIZZLE_NONE K-major: start >> 4, LBO = 128 B (next K group), SBO = 2048 B
@@ -165,13 +152,41 @@ FDEV void g5_commit(uint64_t *bar) {
                  : "memory");
 }
 
+FDEV uint32_t g5_cluster_addr(const void *p, int rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(g5_saddr(p)), "r"(rank));
+    return r;
+}
+FDEV float4 g5_ld_cluster4(uint32_t addr) {
+    float4 v;
+    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(addr)
+                 : "memory");
+    return v;
+}
+FDEV void g5_cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+struct G5PackParams {
+    const float *x;        // [ntok][ldx]
+    int ldx, ntok, cols;
+    const float *rrms;     // [ntok] or null: 1 / rms per token
+    const float *nw;       // [cols] or null: no normalisation
+    int own_rms;           // 1: compute rrms here (eps) instead of reading it
+    float eps;
+    uint8_t *bp;
+    int *err;              // set to 5 when a value does not fit fp16
+};
+
 // canonical offset of (row r, K slot k) inside a 128-K chunk tile: core matrix (r/8, k/8)
 FDEV int g5_off(int r, int k) { return ((r >> 3) * (G5_KC / 8) + (k >> 3)) * 128 + (r & 7) * 16 + (k & 7) * 2; }
 
 // Bytes of one row's weights per K unit in a raw stage. Q4_K / Q5_K: the 144 / 176-byte
 // super-block (two chunks). Q6_K: the super-block (two chunks) is 210 bytes at an even
-// offset, so the 224-byte span from the 16-byte boundary at or below it, which ends at
-// most 14 bytes past the block. F16: the chunk's 128 values (256 bytes; one chunk per unit).
+// offset, so the 224-byte span from the 16-byte boundary at or below it (a tensor copy
+// must start on a 16-byte boundary). F16: the chunk's 128 values (256 bytes).
 template <int T>
 HDCE int g5_bb() { return T == T_Q4_K ? 144 : (T == T_Q5_K ? 176 : (T == T_Q6_K ? 210 : 512)); }
 template <int T>
@@ -233,43 +248,59 @@ FDEV void g5_decode<T_Q6_K>(const uint8_t *blk, int c, int sub, int r, uint8_t *
 }
 
 // Q5_K (layout as Q4_K plus qh[32] at 16, qs at 48): element 64 t + 32 s + l has quant
-// nib + 16 * ((qh[l] >> (2 t + s)) & 1), nib the low (s = 0) or high (s = 1) nibble of
-// qs[32 t + l]; value fp32((d*sc) * q - dmin*m). Same quarters as Q4_K.
+// q = nib + 16 * ((qh[l] >> (2 t + s)) & 1), nib the low (s = 0) or high (s = 1) nibble
+// of qs[32 t + l]; value fp32((d*sc) * q - dmin*m) (both products exact in fp32, one
+// rounding). Packed: half2 (1024 + q) by LOP3; n = q * sc / 2 exactly in fp16 by HFMA2
+// ((1024 + q) * sc/2 - 512 sc, all terms exact); then (2d) * n - dmin*m with one
+// mixed-precision FMA (one rounding) = the fp32 value; hi = fp16(v), lo = fp16(v - hi).
 template <>
 FDEV void g5_decode<T_Q5_K>(const uint8_t *blk, int c, int sub, int r, uint8_t *A, uint8_t *A2) {
     const uint4 hdr = *reinterpret_cast<const uint4 *>(blk);
-    const float d = h2f(hdr.x & 0xFFFFu), dmin = h2f(hdr.x >> 16);
     const int t = 2 * (c & 1) + sub;
     int sc0, m0, sc1, m1;
-    scale_min_k4(2 * t, hdr.y, hdr.z, hdr.w, sc0, m0);
-    scale_min_k4(2 * t + 1, hdr.y, hdr.z, hdr.w, sc1, m1);
-    const float dsc0 = __fmul_rn(d, (float)sc0), dmm0 = __fmul_rn(dmin, (float)m0);
-    const float dsc1 = __fmul_rn(d, (float)sc1), dmm1 = __fmul_rn(dmin, (float)m1);
+    TcDot<T_Q4_K>::scales(hdr, t, sc0, m0, sc1, m1);
+    const float dmin = h2f(hdr.x >> 16);
+    const uint16_t d2 = __half_as_ushort(__float2half_rn(2.0f * h2f(hdr.x & 0xFFFFu)));  // exact
+    const uint32_t A0 = h2_splat(0.5f * (float)sc0), B0 = h2_splat(-512.0f * (float)sc0);
+    const uint32_t A1 = h2_splat(0.5f * (float)sc1), B1 = h2_splat(-512.0f * (float)sc1);
+    const float c0 = -__fmul_rn(dmin, (float)m0), c1 = -__fmul_rn(dmin, (float)m1);
+    const uint4 q0 = *reinterpret_cast<const uint4 *>(blk + 48 + 32 * t);
+    const uint4 q1 = *reinterpret_cast<const uint4 *>(blk + 64 + 32 * t);
+    const uint4 h0 = *reinterpret_cast<const uint4 *>(blk + 16);
+    const uint4 h1 = *reinterpret_cast<const uint4 *>(blk + 32);
+    const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+    const uint32_t hw[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+    // one pair -> (hi word, lo word) of fp16 parts
+    auto pair = [&](uint32_t h, uint32_t Am, uint32_t Bm, float cm, uint32_t &hi, uint32_t &lo) {
+        float a, b;
+        mixed_fma2(hfma2_u(h, Am, Bm), d2, cm, a, b);
+        hi = pack_f16x2(a, b);
+        const __half2 hh = *reinterpret_cast<const __half2 *>(&hi);
+        const float2 hf = __half22float2(hh);
+        lo = pack_f16x2(__fsub_rn(a, hf.x), __fsub_rn(b, hf.y));
+    };
 #pragma unroll
-    for (int v = 0; v < 4; v++) {  // l = 8v .. 8v+7
-        const uint2 qs = *reinterpret_cast<const uint2 *>(blk + 48 + 32 * t + 8 * v);
-        const uint2 qh = *reinterpret_cast<const uint2 *>(blk + 16 + 8 * v);
-        uint16_t lh[8], ll[8], hh[8], hl[8];  // low / high sub-block, hi / lo fp16 parts
+    for (int v = 0; v < 4; v++) {  // words 2v, 2v+1: l = 8v .. 8v+7
+        uint32_t lh[4], ll[4], hh4[4], hl4[4];
 #pragma unroll
-        for (int j = 0; j < 8; j++) {
-            const uint32_t q = ((j < 4 ? qs.x : qs.y) >> (8 * (j & 3))) & 0xFFu;
-            const uint32_t h = ((j < 4 ? qh.x : qh.y) >> (8 * (j & 3))) & 0xFFu;
-            const float w0 = q5k_weight(dsc0, dmm0, (int)((q & 15u) | (((h >> (2 * t)) & 1u) << 4)));
-            const float w1 = q5k_weight(dsc1, dmm1, (int)((q >> 4) | (((h >> (2 * t + 1)) & 1u) << 4)));
-            const __half a0 = __float2half_rn(w0), a1 = __float2half_rn(w1);
-            lh[j] = __half_as_ushort(a0);
-            ll[j] = __half_as_ushort(__float2half_rn(w0 - __half2float(a0)));
-            hh[j] = __half_as_ushort(a1);
-            hl[j] = __half_as_ushort(__float2half_rn(w1 - __half2float(a1)));
+        for (int k = 0; k < 2; k++) {
+            const uint32_t w = qw[2 * v + k], hb = hw[2 * v + k];
+            // bytes 0, 2 and 1, 3 of the word as (1024 + q) half2 pairs; qh bit 2t (low
+            // nibbles) / 2t + 1 (high nibbles) moved to bit 4 of each half
+            const uint32_t e02l = lop3_or_and(w, 0x000F000Fu, 0x64006400u) | (((hb >> (2 * t)) & 0x00010001u) << 4);
+            const uint32_t e13l = lop3_or_and(w >> 8, 0x000F000Fu, 0x64006400u) | (((hb >> (8 + 2 * t)) & 0x00010001u) << 4);
+            const uint32_t e02h = lop3_or_and(w >> 4, 0x000F000Fu, 0x64006400u) | (((hb >> (2 * t + 1)) & 0x00010001u) << 4);
+            const uint32_t e13h = lop3_or_and(w >> 12, 0x000F000Fu, 0x64006400u) | (((hb >> (9 + 2 * t)) & 0x00010001u) << 4);
+            pair(e02l, A0, B0, c0, lh[2 * k], ll[2 * k]);
+            pair(e13l, A0, B0, c0, lh[2 * k + 1], ll[2 * k + 1]);
+            pair(e02h, A1, B1, c1, hh4[2 * k], hl4[2 * k]);
+            pair(e13h, A1, B1, c1, hh4[2 * k + 1], hl4[2 * k + 1]);
         }
-        auto pk = [](const uint16_t *e) {  // slot order k0 k2 k1 k3 k4 k6 k5 k7
-            return make_uint4((uint32_t)e[0] | ((uint32_t)e[2] << 16), (uint32_t)e[1] | ((uint32_t)e[3] << 16),
-                              (uint32_t)e[4] | ((uint32_t)e[6] << 16), (uint32_t)e[5] | ((uint32_t)e[7] << 16));
-        };
-        *reinterpret_cast<uint4 *>(A + g5_off(r, 64 * sub + 8 * v)) = pk(lh);
-        *reinterpret_cast<uint4 *>(A2 + g5_off(r, 64 * sub + 8 * v)) = pk(ll);
-        *reinterpret_cast<uint4 *>(A + g5_off(r, 64 * sub + 32 + 8 * v)) = pk(hh);
-        *reinterpret_cast<uint4 *>(A2 + g5_off(r, 64 * sub + 32 + 8 * v)) = pk(hl);
+        // slot order k0 k2 | k1 k3 | k4 k6 | k5 k7 = (e02, e13) of word 2v, then of 2v+1
+        *reinterpret_cast<uint4 *>(A + g5_off(r, 64 * sub + 8 * v)) = make_uint4(lh[0], lh[1], lh[2], lh[3]);
+        *reinterpret_cast<uint4 *>(A2 + g5_off(r, 64 * sub + 8 * v)) = make_uint4(ll[0], ll[1], ll[2], ll[3]);
+        *reinterpret_cast<uint4 *>(A + g5_off(r, 64 * sub + 32 + 8 * v)) = make_uint4(hh4[0], hh4[1], hh4[2], hh4[3]);
+        *reinterpret_cast<uint4 *>(A2 + g5_off(r, 64 * sub + 32 + 8 * v)) = make_uint4(hl4[0], hl4[1], hl4[2], hl4[3]);
     }
 }
 
@@ -373,7 +404,6 @@ __global__ void __launch_bounds__(G5_THREADS, 1) gemm_tc5_kernel(const __grid_co
     uint8_t *const Abuf = g5_smem;                             // [2][AP][G5_A_BYTES]
     uint8_t *const Bbuf = g5_smem + 2 * AS;                    // [NB][G5_B_BYTES]
     uint8_t *const Rbuf = g5_smem + 2 * AS + NB * G5_B_BYTES;  // [NR][128 rows x S]
-    __shared__ int last_cta;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int row0 = blockIdx.x * G5_M, tile = blockIdx.y, ks = gridDim.z, kz = blockIdx.z;
     const int nchunk = p.cols / G5_KC, nunit = nchunk / CPU;
@@ -381,7 +411,6 @@ __global__ void __launch_bounds__(G5_THREADS, 1) gemm_tc5_kernel(const __grid_co
     const int cb = (int)((long long)kz * nunit / ks) * CPU, ce = (int)((long long)(kz + 1) * nunit / ks) * CPU;
     const int nloc = ce - cb;
     const int vrows = min(G5_M, p.rows - row0);
-    const size_t row_bytes = (size_t)(p.cols / 256) * BB;
 
     if (tid == 0) {
         for (int s = 0; s < NB; s++) {
@@ -412,6 +441,7 @@ __global__ void __launch_bounds__(G5_THREADS, 1) gemm_tc5_kernel(const __grid_co
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = tmem_slot;
     G5_MARK(11, 0);
+    G5_MARK(16, 0);
 
     if (warp == 0) {
         // ---- producer: raw stage u % NR <- K unit u of the 128 rows; B stage c % NB <- the
@@ -427,19 +457,12 @@ __global__ void __launch_bounds__(G5_THREADS, 1) gemm_tc5_kernel(const __grid_co
                 if (!ok) break;
                 G5_MARK(0, i);
                 uint8_t *dst = Rbuf + rs * (G5_M * S);
-                if (T == T_Q6_K) {
-                    if (lane == 0) g5_expect_tx(&rfull[rs], (uint32_t)(vrows * S));
-                    __syncwarp();
-                    for (int r = lane; r < vrows; r += 32) {
-                        const uintptr_t src = reinterpret_cast<uintptr_t>(p.w + (size_t)(row0 + r) * row_bytes) +
-                                              (size_t)u * BB;
-                        g5_bulk(dst + r * S, reinterpret_cast<const void *>(src & ~(uintptr_t)15), (uint32_t)S,
-                                &rfull[rs]);
-                    }
-                } else if (lane == 0) {
-                    // box = 128 rows x one unit (rows past the matrix read as zeros)
+                if (lane == 0) {
+                    // box = 128 rows x one unit (rows past the matrix and bytes past a row
+                    // read as zeros); Q6_K: the 224 bytes from the 16-byte boundary at or
+                    // below the 210-byte block
                     g5_expect_tx(&rfull[rs], (uint32_t)(G5_M * S));
-                    const int x = T == T_F16 ? u * 128 : u * BB;  // fp16 elements (F16) / bytes
+                    const int x = T == T_F16 ? u * 128 : (T == T_Q6_K ? (u * BB) & ~15 : u * BB);
                     asm volatile(
                         "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, "
                         "{%2, %3}], [%4];" ::"r"(g5_saddr(dst)),
@@ -502,9 +525,6 @@ __global__ void __launch_bounds__(G5_THREADS, 1) gemm_tc5_kernel(const __grid_co
     } else {
         // ---- decoders: thread (row r, half sub of the chunk's 128 K)
         const int i = tid - 64, r = i >> 1, sub = i & 1;
-        const int shift = T == T_Q6_K && r < vrows
-                              ? (int)((reinterpret_cast<uintptr_t>(p.w + (size_t)(row0 + r) * row_bytes)) & 15)
-                              : 0;
         bool ok = true;
         for (int i = 0; i < nloc && ok; i++) {
             const int c = cb + i, u = c / CPU, ui = i / CPU, rs = ui % NR, a = i & 1;
@@ -516,7 +536,7 @@ __global__ void __launch_bounds__(G5_THREADS, 1) gemm_tc5_kernel(const __grid_co
             if (!ok) break;
             // Q6_K: the span starts at the 16-byte boundary at or below the block
             const uint8_t *blk = Rbuf + rs * (G5_M * S) + r * S;
-            if (T == T_Q6_K) blk += (shift + u * BB) & 15;
+            if (T == T_Q6_K) blk += (u * BB) & 15;
             g5_decode<T>(blk, c, sub, r, Abuf + a * AS, Abuf + a * AS + (AP - 1) * G5_A_BYTES);
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor core
             __syncwarp();
@@ -545,8 +565,8 @@ __global__ void __launch_bounds__(G5_THREADS, 1) gemm_tc5_kernel(const __grid_co
                     : "r"(addr)
                     : "memory");
                 asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-                if (ks > 1) {  // this split's partial tile, [token][row]
-                    float *w = p.ws + ((size_t)(kz * gridDim.y + tile) * gridDim.x + blockIdx.x) * (G5_T * G5_M);
+                if (ks > 1) {  // this split's partial tile, [token][row], over the B stages
+                    float *w = reinterpret_cast<float *>(Bbuf);
 #pragma unroll
                     for (int j = 0; j < 8; j++)
                         w[(c0 / 2 + j) * G5_M + rr] = __fadd_rn(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1]));
@@ -567,28 +587,38 @@ __global__ void __launch_bounds__(G5_THREADS, 1) gemm_tc5_kernel(const __grid_co
     G5_MARK(10, 0);
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
-    if (ks > 1 && !fail) {
-        // the last of the ks CTAs of this tile adds the partial tiles in split order
-        unsigned int *ticket = p.tickets + (size_t)tile * gridDim.x + blockIdx.x;
-        if (tid == 0) {
-            __threadfence();
-            last_cta = atomicAdd(ticket, 1u) == (unsigned int)(ks - 1);
-            if (last_cta) __threadfence();
-        }
-        __syncthreads();
-        if (last_cta) {
-            const size_t tstride = (size_t)gridDim.y * gridDim.x * (G5_T * G5_M);
-            const float *w0 = p.ws + ((size_t)tile * gridDim.x + blockIdx.x) * (G5_T * G5_M);
-            for (int e = tid; e < G5_T * G5_M; e += G5_THREADS) {
-                const int t = tile * G5_T + e / G5_M, r = e % G5_M;
-                if (t >= p.ntok || r >= vrows) continue;
-                float y = __ldcg(w0 + e);
-                for (int z = 1; z < ks; z++) y = __fadd_rn(y, __ldcg(w0 + z * tstride + e));
-                float *dst = p.y + (size_t)t * p.ldy + p.out_off + row0 + r;
-                *dst = p.epi == G5_RESID ? __fadd_rn(*dst, y) : y;
+    if (ks > 1) {
+        // every CTA of the cluster holds its partial tile; CTA kz adds slice kz of the
+        // tile over the cluster in split order (every CTA reaches both cluster barriers)
+        g5_cluster_sync();
+        G5_MARK(12, 0);
+        if (!fail) {
+            constexpr int Q = G5_T * G5_M / 4;  // float4s per tile
+            const int q0 = kz * Q / ks, q1 = (kz + 1) * Q / ks;
+            for (int q = q0 + tid; q < q1; q += G5_THREADS) {
+                const uint32_t off = (uint32_t)q * 16u;
+                float4 acc = g5_ld_cluster4(g5_cluster_addr(Bbuf, 0) + off);
+                for (int z = 1; z < ks; z++) {
+                    const float4 v = g5_ld_cluster4(g5_cluster_addr(Bbuf, z) + off);
+                    acc.x = __fadd_rn(acc.x, v.x);
+                    acc.y = __fadd_rn(acc.y, v.y);
+                    acc.z = __fadd_rn(acc.z, v.z);
+                    acc.w = __fadd_rn(acc.w, v.w);
+                }
+                const int t = tile * G5_T + (4 * q) / G5_M, r0 = (4 * q) % G5_M;
+                if (t >= p.ntok) continue;
+                const float vals[4] = {acc.x, acc.y, acc.z, acc.w};
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    if (r0 + j >= vrows) break;
+                    float *dst = p.y + (size_t)t * p.ldy + p.out_off + row0 + r0 + j;
+                    *dst = p.epi == G5_RESID ? __fadd_rn(*dst, vals[j]) : vals[j];
+                }
             }
-            if (tid == 0) *ticket = 0u;  // ready for the next launch
         }
+        G5_MARK(13, 0);
+        g5_cluster_sync();  // peers read this CTA's tile until here
+        G5_MARK(14, 0);
     }
     if (fail) {
         // let the committed MMAs finish before the tensor memory is released
@@ -602,6 +632,7 @@ __global__ void __launch_bounds__(G5_THREADS, 1) gemm_tc5_kernel(const __grid_co
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(G5_N) : "memory");
     }
+    G5_MARK(15, 0);
 }
 
 HDCE int g5_smem_bytes(int type) {
