@@ -102,7 +102,7 @@ int fiber_set_decode_mode(fiber_ctx_t *ctx, int mode);
 
 /* Prefill path of fiber_prefill: 0 (default) = batched, the prompt in chunks of
  * FIBER_PREFILL_CHUNK tokens through tensor-core dequant-GEMMs (tcgen05) with causal attention over the
- * cache, when every matrix is Q4_K / Q6_K / F16 and the context is not sharded;
+ * cache, when every matrix is Q4_K / Q5_K / Q6_K / F16 and the context is not sharded;
  * 1 = one decode step per token. Both fill the same KV cache and return the first
  * generated token. */
 int fiber_set_prefill_mode(fiber_ctx_t *ctx, int mode);
