@@ -102,11 +102,36 @@ def host() -> C.CDLL:
         H.tokenizer_bos.argtypes = [C.c_void_p]
         H.sampler_init.argtypes = [C.POINTER(Sampler), C.c_int, C.c_float, C.c_int, C.c_float]
         H.sampler_sample.argtypes = [C.POINTER(Sampler), F32P]
+        H.fiber_karpathy_config.argtypes = [C.c_char_p, C.POINTER(KarpathyConfig)]
+        H.fiber_karpathy_to_gguf.argtypes = [C.c_char_p, C.c_char_p]
+        H.model_open_karpathy.restype = C.c_void_p
+        H.model_open_karpathy.argtypes = [C.c_char_p, C.c_char_p]
         _host = H
     return _host
 
 
 # ---- synthetic models and blocks ------------------------------------------------
+
+class KarpathyConfig(C.Structure):
+    """fiber_karpathy_config_t (include/fiber_ckpt.h)."""
+    _fields_ = [(n, C.c_int32) for n in ("dim", "hidden_dim", "n_layers", "n_heads", "n_kv_heads", "vocab_size",
+                                         "seq_len", "shared_classifier")]
+
+
+def karpathy_config(bin_path: str) -> KarpathyConfig:
+    """Header of a karpathy / llama2.c checkpoint (fiber_karpathy_config)."""
+    out = KarpathyConfig()
+    if host().fiber_karpathy_config(bin_path.encode(), C.byref(out)) != 0:
+        raise ValueError(f"not a karpathy checkpoint: {bin_path}")
+    return out
+
+
+def karpathy_to_gguf(bin_path: str, gguf_path: str) -> str:
+    """Rewrite a karpathy / llama2.c checkpoint as a Llama GGUF (fiber_karpathy_to_gguf)."""
+    if host().fiber_karpathy_to_gguf(bin_path.encode(), gguf_path.encode()) != 0:
+        raise ValueError(f"cannot convert {bin_path}")
+    return gguf_path
+
 
 def synth_cfg(preset: str | None = None, **over) -> SynthCfg:
     cfg = SynthCfg()

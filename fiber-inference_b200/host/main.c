@@ -20,6 +20,7 @@
 #include "fiber_cuda.h"
 #include "fiber_synth.h"
 #include "model.h"
+#include "fiber_ckpt.h"
 #include "sampler.h"
 #include "tokenizer.h"
 
@@ -34,7 +35,8 @@ static double now_ms(void) {
 static void usage(const char *prog) {
     fprintf(stderr, "Usage: %s --model <path.gguf> [options]\n", prog);
     fprintf(stderr, "\nOptions:\n");
-    fprintf(stderr, "  --model <path>      Path to GGUF model file (required)\n");
+    fprintf(stderr, "  --model <path>      Path to GGUF model file (required); a karpathy/llama2.c .bin\n");
+    fprintf(stderr, "                      checkpoint is rewritten as a GGUF in $TMPDIR (or /tmp) first\n");
     fprintf(stderr, "  --prompt <text>     Input prompt (default: \"Hello\")\n");
     fprintf(stderr, "  --tokens <n>        Max tokens to generate (default: 128)\n");
     fprintf(stderr, "  --ctx-len <n>       Max context length (default: model max)\n");
@@ -112,7 +114,18 @@ int main(int argc, char **argv) {
     printf("Fiber-Inference B200 (CUDA decode path)\n\n");
     printf("Loading: %s\n", model_path);
     double t0 = now_ms();
-    model_t *m = model_open(model_path);
+    model_t *m = NULL;
+    const size_t plen = strlen(model_path);
+    if (plen > 4 && strcmp(model_path + plen - 4, ".bin") == 0) {
+        const char *dir = getenv("TMPDIR");
+        const char *base = strrchr(model_path, '/');
+        char gguf_path[4096];
+        snprintf(gguf_path, sizeof(gguf_path), "%s/%s.gguf", dir && *dir ? dir : "/tmp", base ? base + 1 : model_path);
+        printf("karpathy checkpoint: writing %s\n", gguf_path);
+        m = model_open_karpathy(model_path, gguf_path);
+    } else {
+        m = model_open(model_path);
+    }
     if (!m) {
         fprintf(stderr, "Failed to open model\n");
         return 1;

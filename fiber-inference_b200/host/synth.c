@@ -399,11 +399,13 @@ typedef struct {
     int type;
     uint64_t offset;
     size_t bytes;
-    int role;      /* recipe role, or -1 for a norm */
+    int role;      /* recipe role, or a FIBER_ROLE_*_NORM value */
     uint32_t layer;
 } tdesc_t;
 
-int fiber_synth_write_gguf(const char *path, const fiber_synth_cfg_t *cfg) {
+/* Writes the Llama GGUF of cfg's shape; fill (or, when NULL, the seeded generator)
+ * gives every tensor's fp32 values before they are quantized to the recipe's type. */
+static int write_gguf(const char *path, const fiber_synth_cfg_t *cfg, fiber_tensor_fill_fn fill, void *user) {
     const uint32_t L = cfg->n_layers, D = cfg->dim, F = cfg->ffn_dim;
     const uint32_t KV = cfg->n_kv_heads * (cfg->dim / cfg->n_heads);
     if (!L || !D || !F || !cfg->n_heads || !cfg->n_kv_heads || D % cfg->n_heads ||
@@ -430,7 +432,7 @@ int fiber_synth_write_gguf(const char *path, const fiber_synth_cfg_t *cfg) {
         k++;                                                                           \
     } while (0)
     T("token_embd.weight", D, cfg->vocab, fiber_synth_recipe_type(cfg->recipe, 7, 0, L), 7, 0);
-    T("output_norm.weight", D, 1, GGML_TYPE_F32, -1, 0);
+    T("output_norm.weight", D, 1, GGML_TYPE_F32, FIBER_ROLE_OUTPUT_NORM, 0);
     if (!cfg->tied)
         T("output.weight", D, cfg->vocab, fiber_synth_recipe_type(cfg->recipe, 8, 0, L), 8, 0);
     for (uint32_t l = 0; l < L; l++) {
@@ -439,13 +441,13 @@ int fiber_synth_write_gguf(const char *path, const fiber_synth_cfg_t *cfg) {
                                      "ffn_gate", "ffn_down", "ffn_up"};
         const uint64_t in[7] = {D, D, D, D, D, F, D}, out[7] = {D, KV, KV, D, F, D, F};
         snprintf(nm, sizeof(nm), "blk.%u.attn_norm.weight", l);
-        T(nm, D, 1, GGML_TYPE_F32, -1, l);
+        T(nm, D, 1, GGML_TYPE_F32, FIBER_ROLE_ATTN_NORM, l);
         for (int r = 0; r < 7; r++) {
             snprintf(nm, sizeof(nm), "blk.%u.%s.weight", l, suf[r]);
             T(nm, in[r], out[r], fiber_synth_recipe_type(cfg->recipe, r, l, L), r, l);
             if (r == 3) {
                 snprintf(nm, sizeof(nm), "blk.%u.ffn_norm.weight", l);
-                T(nm, D, 1, GGML_TYPE_F32, -1, l);
+                T(nm, D, 1, GGML_TYPE_F32, FIBER_ROLE_FFN_NORM, l);
             }
         }
     }
@@ -539,7 +541,9 @@ int fiber_synth_write_gguf(const char *path, const fiber_synth_cfg_t *cfg) {
     if (!vals || !blob) ok = 0;
     for (size_t i = 0; i < nt && ok; i++) {
         size_t rows = (size_t)td[i].dims[1], cols = (size_t)td[i].dims[0];
-        if (td[i].role < 0) {
+        if (fill) {
+            if (fill(user, td[i].role, td[i].layer, rows, cols, vals) != 0) ok = 0;
+        } else if (td[i].role < 0) {
             for (size_t e = 0; e < cols; e++) vals[e] = cfg->norm_value;
         } else {
 #pragma omp parallel for schedule(static)
@@ -559,4 +563,11 @@ int fiber_synth_write_gguf(const char *path, const fiber_synth_cfg_t *cfg) {
     if (fclose(f) != 0) ok = 0;
     if (!ok) fprintf(stderr, "synth: failed writing %s\n", path);
     return ok ? 0 : -1;
+}
+
+int fiber_synth_write_gguf(const char *path, const fiber_synth_cfg_t *cfg) { return write_gguf(path, cfg, NULL, NULL); }
+
+int fiber_write_gguf_from(const char *path, const fiber_synth_cfg_t *cfg, fiber_tensor_fill_fn fill, void *user) {
+    if (!fill) return -1;
+    return write_gguf(path, cfg, fill, user);
 }

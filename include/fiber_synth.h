@@ -49,6 +49,18 @@ int fiber_synth_preset(const char *name, fiber_synth_cfg_t *cfg);
 /* Write a complete model; returns 0 on success, -1 on error (message on stderr). */
 int fiber_synth_write_gguf(const char *path, const fiber_synth_cfg_t *cfg);
 
+/* Roles of the norm tensors in a fill callback (matrices use the recipe roles below). */
+enum { FIBER_ROLE_OUTPUT_NORM = -1, FIBER_ROLE_ATTN_NORM = -2, FIBER_ROLE_FFN_NORM = -3 };
+
+/* fp32 values of one tensor, rows x cols row-major ([out][in] for matrices; rows = 1 for
+ * norms); role as fiber_synth_recipe_type's (0 wq .. 6 w3, 7 token_embd, 8 output) or a
+ * FIBER_ROLE_*_NORM. Returns 0, or non-zero to abort the write. */
+typedef int (*fiber_tensor_fill_fn)(void *user, int role, uint32_t layer, size_t rows, size_t cols, float *vals);
+
+/* The same file layout and metadata as fiber_synth_write_gguf, with every tensor's values
+ * from fill (quantized to cfg->recipe's types; cfg->seed only names the vocabulary). */
+int fiber_write_gguf_from(const char *path, const fiber_synth_cfg_t *cfg, fiber_tensor_fill_fn fill, void *user);
+
 /* Type the recipe gives tensor `role` of layer `layer` (role: 0 wq,1 wk,2 wv,
  * 3 wo,4 w1 gate,5 w2 down,6 w3 up,7 token_embd,8 output; layer ignored for 7/8). */
 int fiber_synth_recipe_type(int recipe, int role, uint32_t layer, uint32_t n_layers);
