@@ -34,6 +34,7 @@
 #include "persistent.cuh"
 #include "gemm_tc5.cuh"
 #include "prefill.cuh"
+#include "sample.cuh"
 
 using namespace fiber;
 
@@ -407,6 +408,8 @@ struct gpu_context {
     float *att_ws = nullptr;           // page-split attention states (batched layer pass)
     unsigned int *att_tickets = nullptr;
     std::vector<void *> pf_pad;        // Q6_K matrices re-laid with 16-byte-aligned rows
+    unsigned long long *smp_rng = nullptr;  // device sampler state (sampling decode loop)
+    int32_t *smp_out = nullptr;
 };
 
 static void free_graph(Graph &g) {
@@ -424,7 +427,7 @@ extern "C" void fiber_cuda_free(fiber_ctx_t *c) {
     free_graph(c->g_batch);
     if (c->comm) ncclCommDestroy(c->comm);
     for (void *q : c->pf_pad) cudaFree(q);
-    void *dev[] = {c->att_ws, c->att_tickets, c->bt_pos, c->bt_arg, c->bt_rec, c->bt_step, c->bt_logits, c->pf_x, c->pf_qkv, c->pf_att, c->pf_hg, c->pf_hu, c->pf_bp, c->pf_tok, c->x2, c->d_shard, c->d_data, c->x, c->qkv, c->att, c->h, c->logits, c->rope, c->io, c->rec,
+    void *dev[] = {c->smp_rng, c->smp_out, c->att_ws, c->att_tickets, c->bt_pos, c->bt_arg, c->bt_rec, c->bt_step, c->bt_logits, c->pf_x, c->pf_qkv, c->pf_att, c->pf_hg, c->pf_hu, c->pf_bp, c->pf_tok, c->x2, c->d_shard, c->d_data, c->x, c->qkv, c->att, c->h, c->logits, c->rope, c->io, c->rec,
                    c->att_part, c->att_cnt, c->am_part, c->am_cnt, c->d_phases, c->d_bar,
                    c->pk_gf[0], c->pk_gf[1], c->pk_gf[2], c->pk_gf[3], c->pk_ss[0], c->pk_ss[1]};
     for (void *p : dev)
@@ -2037,3 +2040,113 @@ extern "C" int fiber_gemm(int ggml_type, const void *d_w, int rows, int cols, co
     if (h_err) return set_err(FIBER_ETIMEOUT, "fiber_gemm: a tensor-core wait timed out");
     return FIBER_OK;
 }
+
+// ---- sampling on the device (src/sampler.c:48-112) ---------------------------------------
+
+// Fills p.k / p.inv_temp and the shared-memory size; 0 or a FIBER_E* status.
+static int sample_setup(SampleParams &p, int vocab, float temperature, int top_k, float top_p, size_t *smem) {
+    int k = top_k > 0 ? top_k : vocab;
+    if (k > vocab) k = vocab;
+    if (k < vocab && k > SMP_MAX_K)
+        return set_err(FIBER_EUNSUPPORTED, "device sampler: top_k %d above %d (use the host sampler)", k, SMP_MAX_K);
+    if (k == vocab && vocab > SMP_MAX_UNSORTED)
+        return set_err(FIBER_EUNSUPPORTED, "device sampler: unsorted top_k over a vocabulary above %d", SMP_MAX_UNSORTED);
+    p.k = k;
+    p.inv_temp = 1.0f / temperature;
+    p.top_p = top_p;
+    p.vocab = vocab;
+    *smem = k < vocab ? (size_t)SMP_MAX_K * 12 : (size_t)vocab * 4;
+    return FIBER_OK;
+}
+
+static cudaError_t launch_sample(const SampleParams &p, size_t smem, cudaStream_t st) {
+    cudaError_t e = cudaFuncSetAttribute(sample_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    sample_rows_kernel<<<p.rows, SMP_THREADS, smem, st>>>(p);
+    return cudaGetLastError();
+}
+
+static bool greedy_temperature(float t) { return t <= 0.0f || t < 1e-6f; }
+
+extern "C" int fiber_sample(const float *d_logits, int rows, int vocab, int ld, float temperature, int top_k,
+                            float top_p, unsigned long long *d_rng, int32_t *d_out, void *stream) {
+    if (!d_logits || !d_out || rows <= 0 || vocab <= 0 || ld < vocab)
+        return set_err(FIBER_EARG, "fiber_sample: bad arguments");
+    cudaStream_t st = (cudaStream_t)stream;
+    if (greedy_temperature(temperature)) {  // the reference's argmax (first maximum)
+        argmax_rows_kernel<<<rows, 256, 0, st>>>(d_logits, vocab, ld, d_out);
+        CK(cudaGetLastError());
+        return FIBER_OK;
+    }
+    if (!d_rng) return set_err(FIBER_EARG, "fiber_sample: no random state");
+    SampleParams p;
+    memset(&p, 0, sizeof(p));
+    size_t smem = 0;
+    int rc = sample_setup(p, vocab, temperature, top_k, top_p, &smem);
+    if (rc) return rc;
+    p.logits = d_logits;
+    p.ld = ld;
+    p.rows = rows;
+    p.rng = d_rng;
+    p.out = d_out;
+    CK(launch_sample(p, smem, st));
+    return FIBER_OK;
+}
+
+extern "C" int fiber_decode_sample(fiber_ctx_t *c, kv_cache_t *kv, int32_t first_token, int start_pos, int n_steps,
+                                   float temperature, int top_k, float top_p, unsigned long long *rng_state,
+                                   int32_t *h_tokens_out, float *ms_out) {
+    if (!c || !rng_state) return set_err(FIBER_EARG, "fiber_decode_sample: bad arguments");
+    if (greedy_temperature(temperature))
+        return fiber_decode_greedy(c, kv, first_token, start_pos, n_steps, h_tokens_out, ms_out);
+    if (n_steps <= 0) return set_err(FIBER_EARG, "fiber_decode_sample: bad arguments");
+    int rc = check_kv(c, kv);
+    if (rc) return rc;
+    const int lim = c->max_seq < kv->max_seq ? c->max_seq : kv->max_seq;
+    if (start_pos < 0 || start_pos + n_steps > lim)
+        return set_err(FIBER_EARG, "decode of %d steps from %d exceeds max_seq %d", n_steps, start_pos, lim);
+    if (first_token < 0 || first_token >= (int)c->p.vocab_size)
+        return set_err(FIBER_EARG, "token %d out of range", first_token);
+    SampleParams sp;
+    memset(&sp, 0, sizeof(sp));
+    size_t smem = 0;
+    if ((rc = sample_setup(sp, (int)c->p.vocab_size, temperature, top_k, top_p, &smem))) return rc;
+    CK(cudaSetDevice(c->device));
+    if (!c->smp_rng) {
+        CK(cudaMalloc(&c->smp_rng, sizeof(unsigned long long)));
+        CK(cudaMalloc(&c->smp_out, sizeof(int32_t)));
+    }
+    sp.logits = c->logits;
+    sp.ld = (int)c->p.vocab_size;
+    sp.rows = 1;
+    sp.rng = c->smp_rng;
+    sp.out = c->smp_out;
+    sp.adv_token = &c->io->token;
+    sp.adv_pos = &c->io->pos;
+    sp.rec = c->rec;
+    sp.rec_step = &c->io->step;
+    c->h_io->token = first_token;
+    c->h_io->pos = start_pos;
+    c->h_io->step = 0;
+    c->h_io->err = 0;
+    CK(cudaMemcpyAsync(c->io, c->h_io, sizeof(StepIO), cudaMemcpyHostToDevice, c->stream));
+    CK(cudaMemcpyAsync(c->smp_rng, rng_state, sizeof(unsigned long long), cudaMemcpyHostToDevice, c->stream));
+    if (!(c->mode == 0 && c->pk_ok)) {  // build the step graph before the timed region
+        cudaGraphExec_t g;
+        if ((rc = get_graph(c, kv, false, &g)) != FIBER_OK) return rc;
+    }
+    CK(cudaEventRecord(c->ev0, c->stream));
+    for (int i = 0; i < n_steps; i++) {
+        if ((rc = run_step(c, kv, false)) != FIBER_OK) return rc;  // logits of io->token at io->pos
+        CK(launch_sample(sp, smem, c->stream));                    // next token, position + 1
+    }
+    CK(cudaEventRecord(c->ev1, c->stream));
+    CK(cudaEventSynchronize(c->ev1));
+    if (ms_out) CK(cudaEventElapsedTime(ms_out, c->ev0, c->ev1));
+    CK(cudaMemcpyAsync(c->h_io, c->io, sizeof(StepIO), cudaMemcpyDeviceToHost, c->stream));
+    if (h_tokens_out) CK(cudaMemcpyAsync(h_tokens_out, c->rec, (size_t)n_steps * 4, cudaMemcpyDeviceToHost, c->stream));
+    CK(cudaMemcpyAsync(rng_state, c->smp_rng, sizeof(unsigned long long), cudaMemcpyDeviceToHost, c->stream));
+    CK(cudaStreamSynchronize(c->stream));
+    return device_status(c);
+}
+

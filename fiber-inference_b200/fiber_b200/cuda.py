@@ -14,7 +14,8 @@ import numpy as np
 from . import CUDA_SO, ModelParams  # noqa: F401
 
 __all__ = ["FiberError", "cuda_lib", "cuda_available", "gemv", "gemv_host", "gemv_argmax_noalloc", "dequant", "Context", "KVCache",
-           "device_count", "TPPlan", "TP_ID_BYTES", "tp_plan", "tp_unique_id", "gemm", "PREFILL_CHUNK"]
+           "device_count", "TPPlan", "TP_ID_BYTES", "tp_plan", "tp_unique_id", "gemm", "PREFILL_CHUNK",
+           "sample_device"]
 
 PREFILL_CHUNK = 512  # FIBER_PREFILL_CHUNK: tokens per pass of the batched prefill
 
@@ -29,7 +30,7 @@ EXPORTED = [
     "fiber_dequant", "fiber_gemv_host", "gpu_init", "gpu_free", "gpu_embed", "gpu_forward_token",
     "gpu_get_logits", "gpu_forward_classifier", "gpu_get_device", "kv_cache_init", "kv_cache_init_paged",
     "kv_cache_free", "kv_cache_write", "kv_cache_read", "fiber_gemv_argmax_noalloc", "fiber_prefill_slot",
-    "fiber_decode_greedy_batch",
+    "fiber_decode_greedy_batch", "fiber_sample", "fiber_decode_sample",
 ]
 
 
@@ -71,6 +72,10 @@ def cuda_lib() -> C.CDLL:
         L.fiber_prefill_slot.argtypes = [C.c_void_p, C.c_void_p, C.c_int, I32P, C.c_int, C.c_int, C.c_void_p]
         L.fiber_decode_greedy_batch.argtypes = [C.c_void_p, C.c_void_p, I32P, I32P, C.c_int, C.c_int, C.c_void_p,
                                                 C.c_void_p]
+        L.fiber_sample.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_float, C.c_int, C.c_float, C.c_void_p,
+                                   C.c_void_p, C.c_void_p]
+        L.fiber_decode_sample.argtypes = [C.c_void_p, C.c_void_p, C.c_int32, C.c_int, C.c_int, C.c_float, C.c_int,
+                                          C.c_float, C.POINTER(C.c_ulonglong), C.c_void_p, C.c_void_p]
         L.fiber_decode_greedy.argtypes = [C.c_void_p, C.c_void_p, C.c_int32, C.c_int, C.c_int, C.c_void_p,
                                           C.c_void_p]
         L.fiber_step_launches.argtypes = [C.c_void_p]
@@ -160,6 +165,13 @@ def gemm(ggml_type: int, d_w: int, rows: int, cols: int, d_x: int, ntok: int, d_
     """fiber_gemm: y[t][out_off + r] (+)= sum_k W[r,k] * xn[t][k] on the tensor cores."""
     _check(cuda_lib().fiber_gemm(ggml_type, d_w, rows, cols, d_x, ntok, ldx or cols, d_rrms, d_nw, d_y, ldy, out_off,
                                  1 if accumulate else 0, _stream_ptr(stream)), "fiber_gemm")
+
+
+def sample_device(d_logits: int, rows: int, vocab: int, ld: int, temperature: float, top_k: int, top_p: float,
+                  d_rng: int, d_out: int, stream=None):
+    """fiber_sample: one token per logits row on the device (the reference sampler's procedure)."""
+    _check(cuda_lib().fiber_sample(d_logits, rows, vocab, ld, temperature, top_k, top_p, d_rng, d_out,
+                                   _stream_ptr(stream)), "fiber_sample")
 
 
 def dequant(ggml_type: int, d_w: int, d_out: int, rows: int, cols: int, stream=None):
@@ -294,6 +306,17 @@ class Context:
         _check(cuda_lib().fiber_decode_greedy(self.h, kv.addr, int(first_token), int(start_pos), int(n_steps),
                                               out.ctypes.data, C.addressof(ms)), "fiber_decode_greedy")
         return out, float(ms.value)
+
+    def decode_sample(self, kv: KVCache, first_token: int, start_pos: int, n_steps: int, temperature: float,
+                      top_k: int, top_p: float, rng_state: int = 42):
+        """fiber_decode_sample: (tokens, device ms, advanced random state)."""
+        out = np.zeros(n_steps, np.int32)
+        ms = C.c_float(0.0)
+        st = C.c_ulonglong(rng_state)
+        _check(cuda_lib().fiber_decode_sample(self.h, kv.addr, int(first_token), int(start_pos), int(n_steps),
+                                              float(temperature), int(top_k), float(top_p), C.byref(st),
+                                              out.ctypes.data, C.addressof(ms)), "fiber_decode_sample")
+        return out, float(ms.value), int(st.value)
 
     def set_mode(self, mode: int):
         """0: persistent one-kernel step (default when supported); 1: one kernel per phase."""

@@ -89,6 +89,28 @@ int fiber_decode_greedy_batch(fiber_ctx_t *ctx, kv_cache_t *kv, const int32_t *f
                               const int32_t *start_pos, int batch, int n_steps, int32_t *h_tokens_out,
                               float *ms_out);
 
+/* Sampling on the device with the reference sampler's procedure (src/sampler.c:48-112):
+ * temperature <= 0 (or < 1e-6) is the greedy argmax; otherwise logits * (1/T), the
+ * top_k (top_k <= 0: all) largest sorted descending (equal values in index order; with
+ * k = vocab the candidates stay in index order, as the reference leaves them unsorted),
+ * softmax, nucleus cut at top_p, one xorshift64* draw. Sums are taken in the reference's
+ * order; exp is CUDA's expf, so a draw within an ulp of a boundary can differ from the
+ * host sampler. Limits: top_k <= 1024 when below the vocabulary; vocab <= 49152 when
+ * top_k covers it (else FIBER_EUNSUPPORTED; the host sampler has no limit).
+ *
+ * Kernel level: one token per row of d_logits ([rows][ld] fp32) into d_out; d_rng holds
+ * one xorshift64* state per row (the reference starts at 42), advanced by the draw.
+ * Enqueued on `stream`, no synchronization. No counterpart in the reference (host only). */
+int fiber_sample(const float *d_logits, int rows, int vocab, int ld, float temperature, int top_k,
+                 float top_p, unsigned long long *d_rng, int32_t *d_out, void *stream);
+
+/* Device-resident sampling decode loop: as fiber_decode_greedy, with each step's token
+ * drawn by the device sampler above; *rng_state (the reference sampler's state, 42 at
+ * sampler_init) is used and advanced. temperature <= 0 is fiber_decode_greedy. */
+int fiber_decode_sample(fiber_ctx_t *ctx, kv_cache_t *kv, int32_t first_token, int start_pos,
+                        int n_steps, float temperature, int top_k, float top_p,
+                        unsigned long long *rng_state, int32_t *h_tokens_out, float *ms_out);
+
 /* How a decode step runs. mode 0 (default when the model fits): one cooperative
  * persistent kernel per step -- every SM streams its weight tiles of all phases
  * through a shared-memory ring and the phases are separated by grid barriers.

@@ -19,6 +19,7 @@ def declared_functions():
         text = open(h).read()
         text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
         text = re.sub(r"//[^\n]*", "", text)
+        text = re.sub(r"typedef[^;]*;", "", text)  # types (function-pointer typedefs included)
         for m in DECL.finditer(text):
             name = m.group(1)
             if name in {"if", "sizeof", "defined"}:
