@@ -264,7 +264,9 @@ def run_7b_tp(args, fb, torch, dist, rank, world, local):
                 "config": {"workload": "7B Q4_K_M (Llama-2-7B shape) batch-1 greedy decode, tensor-parallel",
                            "model": "dim 4096, 32 layers, 32/32 heads, hd 128, ffn 11008, vocab 32000, Q4_K_M",
                            "prompt": P, "decode_tokens_per_step": D, "global_batch": 1,
-                           "parallelism": f"tp{world}", "step_mode": "one kernel per phase + NCCL all-reduce",
+                           "parallelism": f"tp{world}",
+                           "step_mode": "one kernel per phase + " + {0: "no", 1: "NCCL", 2: "one-shot peer-memory"}[
+                               ctx.tp_collective] + " all-reduce",
                            "tokens_identical_on_all_ranks": same, "prefill_tok_s": prefill_tps},
                 "roofline": {"bound": "hbm", "achieved": bytes_tok * value / world / 1e9, "peak": peak, "unit": "GB/s",
                              "frac": bytes_tok * value / world / 1e9 / peak, "peak_source": peak_kind,

@@ -35,6 +35,7 @@
 #include "gemm_tc5.cuh"
 #include "prefill.cuh"
 #include "sample.cuh"
+#include "allreduce.cuh"
 
 using namespace fiber;
 
@@ -388,6 +389,12 @@ struct gpu_context {
     float *x2 = nullptr;            // second residual buffer: Wo's all-reduced output
     uint8_t *d_shard = nullptr;     // Wo / W_down shards along their input dimension
     ncclComm_t comm = nullptr;
+    // one-shot peer all-reduce (allreduce.cuh): own slot/flag area, peers' areas (CUDA IPC)
+    bool ar_ok = false;
+    void *ar_local = nullptr;
+    void *ar_peer[AR_MAX_WORLD] = {};
+    unsigned int *ar_epoch = nullptr;
+    ArParams ar{};
     // batched prefill (tensor-core GEMMs): buffers for a chunk of pf_cap tokens
     int prefill_mode = 0;           // 0: batched when the model allows it, 1: token by token
     int pf_cap = 0;
@@ -425,6 +432,10 @@ extern "C" void fiber_cuda_free(fiber_ctx_t *c) {
     free_graph(c->g_step);
     free_graph(c->g_loop);
     free_graph(c->g_batch);
+    for (void *q : c->ar_peer)
+        if (q) cudaIpcCloseMemHandle(q);
+    if (c->ar_local) cudaFree(c->ar_local);
+    if (c->ar_epoch) cudaFree(c->ar_epoch);
     if (c->comm) ncclCommDestroy(c->comm);
     for (void *q : c->pf_pad) cudaFree(q);
     void *dev[] = {c->smp_rng, c->smp_out, c->att_ws, c->att_tickets, c->bt_pos, c->bt_arg, c->bt_rec, c->bt_step, c->bt_logits, c->pf_x, c->pf_qkv, c->pf_att, c->pf_hg, c->pf_hu, c->pf_bp, c->pf_tok, c->x2, c->d_shard, c->d_data, c->x, c->qkv, c->att, c->h, c->logits, c->rope, c->io, c->rec,
@@ -781,6 +792,52 @@ extern "C" int fiber_tp_unique_id(uint8_t out[FIBER_TP_ID_BYTES]) {
 // addressed in place in the uploaded GGUF data; Wo and W_down are cut along their
 // input dimension (whole super-blocks of every row) into d_shard; an NCCL
 // communicator joins the ranks.
+// The one-shot all-reduce's buffers: every rank allocates its slot / flag area, the
+// areas' IPC handles are all-gathered over NCCL (which also orders every rank's zeroing
+// before any peer's first push), and each rank maps its peers' areas.
+static int ar_setup(gpu_context *c, int n_max) {
+    const int W = c->tp_world, R = c->tp_rank;
+    const size_t slot_bytes = (size_t)2 * W * n_max * 4, flag_off = (slot_bytes + 255) / 256 * 256;
+    const size_t total = flag_off + (size_t)2 * W * sizeof(unsigned int);
+    CK(cudaMalloc(&c->ar_local, total));
+    CK(cudaMemset(c->ar_local, 0, total));
+    CK(cudaMalloc(&c->ar_epoch, sizeof(unsigned int)));
+    CK(cudaMemset(c->ar_epoch, 0, sizeof(unsigned int)));
+    cudaIpcMemHandle_t mine;
+    CK(cudaIpcGetMemHandle(&mine, c->ar_local));
+    uint8_t *d_h = nullptr;
+    CK(cudaMalloc(&d_h, (size_t)(W + 1) * sizeof(mine)));
+    std::vector<cudaIpcMemHandle_t> all(W);
+    cudaError_t e = cudaMemcpy(d_h + (size_t)W * sizeof(mine), &mine, sizeof(mine), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess &&
+        ncclAllGather(d_h + (size_t)W * sizeof(mine), d_h, sizeof(mine), ncclUint8, c->comm, c->stream) != ncclSuccess)
+        e = cudaErrorUnknown;
+    if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+    if (e == cudaSuccess) e = cudaMemcpy(all.data(), d_h, (size_t)W * sizeof(mine), cudaMemcpyDeviceToHost);
+    cudaFree(d_h);
+    if (e != cudaSuccess) return set_err(FIBER_ECUDA, "all-reduce setup (handle exchange): %s", cudaGetErrorString(e));
+    ArParams &a = c->ar;
+    memset(&a, 0, sizeof(a));
+    a.n_max = n_max;
+    a.rank = R;
+    a.world = W;
+    a.epoch = c->ar_epoch;
+    a.err = &c->io->err;
+    for (int p = 0; p < W; p++) {
+        uint8_t *base = (uint8_t *)c->ar_local;
+        if (p != R) {
+            void *q = nullptr;
+            CK(cudaIpcOpenMemHandle(&q, all[p], cudaIpcMemLazyEnablePeerAccess));
+            c->ar_peer[p] = q;
+            base = (uint8_t *)q;
+        }
+        a.slots[p] = (float *)base;
+        a.flags[p] = (unsigned int *)(base + flag_off);
+    }
+    c->ar_ok = true;
+    return FIBER_OK;
+}
+
 static int tp_setup(gpu_context *c, const model_t *m, int rank, int world, const uint8_t *nccl_id) {
     const model_params_t &p = c->p;
     fiber_tp_plan_t plan;
@@ -826,6 +883,8 @@ static int tp_setup(gpu_context *c, const model_t *m, int rank, int world, const
     memcpy(&id, nccl_id, sizeof(id));
     const ncclResult_t r = ncclCommInitRank(&c->comm, world, id, rank);
     if (r != ncclSuccess) return set_err(FIBER_ECUDA, "ncclCommInitRank: %s", ncclGetErrorString(r));
+    const char *coll = getenv("FIBER_TP_ALLREDUCE");
+    if (world <= AR_MAX_WORLD && !(coll && strcmp(coll, "nccl") == 0)) return ar_setup(c, dim);
     return FIBER_OK;
 }
 
@@ -1086,8 +1145,15 @@ static cudaError_t enqueue_step(gpu_context *c, const kv_cache_t *kv, bool loop,
             if (e == cudaSuccess && c->tp_world > 1 && (kind == 2 || kind == 4)) {
                 // sum of the ranks' partial products (+ residual from rank 0)
                 float *buf = kind == 2 ? c->x2 : c->x;
-                if (ncclAllReduce(buf, buf, c->p.dim, ncclFloat, ncclSum, c->comm, st) != ncclSuccess)
+                if (c->ar_ok) {
+                    ArParams a = c->ar;
+                    a.buf = buf;
+                    a.n = c->p.dim;
+                    ar_oneshot_kernel<<<1, AR_THREADS, 0, st>>>(a);
+                    e = cudaGetLastError();
+                } else if (ncclAllReduce(buf, buf, c->p.dim, ncclFloat, ncclSum, c->comm, st) != ncclSuccess) {
                     e = cudaErrorUnknown;
+                }
             }
         }
     if (e == cudaSuccess) e = enqueue_lm_head(c, loop, st);
@@ -1141,6 +1207,8 @@ static int check_kv(gpu_context *c, const kv_cache_t *kv) {
 static int device_status(gpu_context *c) {
     if (c->h_io->err == 1) return set_err(FIBER_EARG, "position out of range on the device");
     if (c->h_io->err == 2) return set_err(FIBER_EARG, "token id out of range on the device");
+    if (c->h_io->err == 7)
+        return set_err(FIBER_ETIMEOUT, "tensor-parallel all-reduce: a peer's data did not arrive in time");
     if (c->h_io->err == 5)
         return set_err(FIBER_EUNSUPPORTED,
                        "an activation exceeded the fp16 fragment range of the persistent kernel; use decode mode 1");
@@ -2148,5 +2216,10 @@ extern "C" int fiber_decode_sample(fiber_ctx_t *c, kv_cache_t *kv, int32_t first
     CK(cudaMemcpyAsync(rng_state, c->smp_rng, sizeof(unsigned long long), cudaMemcpyDeviceToHost, c->stream));
     CK(cudaStreamSynchronize(c->stream));
     return device_status(c);
+}
+
+extern "C" int fiber_tp_collective(fiber_ctx_t *c) {
+    if (!c) return set_err(FIBER_EARG, "no context");
+    return c->tp_world <= 1 ? 0 : (c->ar_ok ? 2 : 1);
 }
 

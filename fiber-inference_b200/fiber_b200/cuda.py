@@ -30,7 +30,7 @@ EXPORTED = [
     "fiber_dequant", "fiber_gemv_host", "gpu_init", "gpu_free", "gpu_embed", "gpu_forward_token",
     "gpu_get_logits", "gpu_forward_classifier", "gpu_get_device", "kv_cache_init", "kv_cache_init_paged",
     "kv_cache_free", "kv_cache_write", "kv_cache_read", "fiber_gemv_argmax_noalloc", "fiber_prefill_slot",
-    "fiber_decode_greedy_batch", "fiber_sample", "fiber_decode_sample",
+    "fiber_decode_greedy_batch", "fiber_sample", "fiber_decode_sample", "fiber_tp_collective",
 ]
 
 
@@ -86,6 +86,7 @@ def cuda_lib() -> C.CDLL:
         L.fiber_cuda_init_tp.restype = C.c_void_p
         L.fiber_cuda_init_tp.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_int]
         L.fiber_tp_info.argtypes = [C.c_void_p, C.POINTER(TPPlan)]
+        L.fiber_tp_collective.argtypes = [C.c_void_p]
         L.fiber_set_prefill_mode.argtypes = [C.c_void_p, C.c_int]
         L.fiber_gemm.argtypes = [C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_void_p,
                                  C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p]
@@ -325,6 +326,11 @@ class Context:
     def set_prefill_mode(self, mode: int):
         """0: batched tensor-core prefill when supported (default); 1: one decode step per token."""
         _check(cuda_lib().fiber_set_prefill_mode(self.h, int(mode)), "fiber_set_prefill_mode")
+
+    @property
+    def tp_collective(self) -> int:
+        """fiber_tp_collective: 0 none, 1 NCCL, 2 one-shot peer all-reduce."""
+        return int(cuda_lib().fiber_tp_collective(self.h))
 
     @property
     def mode(self) -> int:

@@ -1,6 +1,7 @@
-"""Tensor-parallel decode on two GPUs (one process per GPU, NCCL all-reduce after
-Wo and W_down): both ranks produce the oracle's greedy tokens, and teacher-forced
-logits stay within the decode tolerances. Skipped with fewer than two GPUs."""
+"""Tensor-parallel decode on two GPUs (one process per GPU, an all-reduce after Wo and
+W_down: the one-shot peer-memory all-reduce, or NCCL): both ranks produce the oracle's
+greedy tokens, teacher-forced logits stay within the decode tolerances, and with the
+peer all-reduce both ranks' logits are bit-identical. Skipped with fewer than two GPUs."""
 from __future__ import annotations
 
 import numpy as np
@@ -16,8 +17,12 @@ pytestmark = pytest.mark.gpu
 MAX_ABS, REL_RMS = 2e-2, 1e-3
 
 
-def _worker(rank, world, nid, path, prompt, n_gen, q):
+def _worker(rank, world, nid, path, prompt, n_gen, q, coll):
     try:
+        import os
+
+        if coll == "nccl":
+            os.environ["FIBER_TP_ALLREDUCE"] = "nccl"
         hm = fb.HostModel(path)
         ctx = fb.Context(hm, device=rank, max_seq=256, tp=(rank, world, nid))
         kv = ctx.kv(256)
@@ -29,14 +34,16 @@ def _worker(rank, world, nid, path, prompt, n_gen, q):
         first = ctx.prefill(kv2, np.asarray(prompt, np.int32))
         toks, _ = ctx.decode_greedy(kv2, first, len(prompt), n_gen)
         plan = ctx.plan
-        q.put((rank, first, toks.tolist(), np.stack(logits), (plan.heads, plan.kv_heads, plan.ffn_blocks), None))
+        q.put((rank, first, toks.tolist(), np.stack(logits),
+               (plan.heads, plan.kv_heads, plan.ffn_blocks, ctx.tp_collective), None))
         ctx.close()
     except Exception as e:  # report instead of hanging the parent
         q.put((rank, None, None, None, None, repr(e)))
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_tp2_matches_oracle(tiny_model):
+@pytest.mark.parametrize("coll", ["peer", "nccl"])
+def test_tp2_matches_oracle(tiny_model, coll):
     path = tiny_model("tp")
     hm = fb.HostModel(path)
     p = hm.params
@@ -46,7 +53,7 @@ def test_tp2_matches_oracle(tiny_model):
     nid = fb.tp_unique_id()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_worker, args=(r, 2, nid, path, prompt, n_gen, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, nid, path, prompt, n_gen, q, coll)) for r in range(2)]
     for pr in procs:
         pr.start()
     res = {}
@@ -61,7 +68,10 @@ def test_tp2_matches_oracle(tiny_model):
                 pr.kill()
     for r in (0, 1):
         assert res[r][5] is None, res[r][5]
-    assert res[0][4] == (4, 2, 2) and res[1][4] == (4, 2, 2)
+    want_coll = 2 if coll == "peer" else 1
+    assert res[0][4] == (4, 2, 2, want_coll) and res[1][4] == (4, 2, 2, want_coll)
+    if coll == "peer":  # every rank sums the slots in the same order
+        assert np.array_equal(res[0][3], res[1][3])
 
     om = orc.Model(path)
     st = om.state(256, kv_fp16=True)
