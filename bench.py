@@ -412,8 +412,9 @@ def run_batch(args, fb, torch, dist, rank, world, local):
     """Batched greedy decode (config 4 at batch 8 / 32, config 5 at batch 64): B sequences per
     step on KV slots 0..B-1 through the tensor-core layer pass, one captured graph per step.
     Config 4: the 1.1B Q5_K_M model, every slot's KV pre-filled with seeded N(0,1) fp16 keys /
-    values for 2048 positions, 256 steps. Config 5: the 7B Q4_K_M model, every slot prefilled
-    with its own 512-token prompt, 256 steps. One replica per rank (weak scaling)."""
+    values for 2048 positions, 256 steps; one replica per rank (weak scaling). Config 5: the 7B
+    Q4_K_M model, every slot prefilled with its own 512-token prompt, 256 steps, tensor-parallel
+    over the ranks (strong scaling: the same B sequences whatever N)."""
     B = args.batch
     if args.workload == "7b-tp":
         path, P, D = MODEL_7B, 512, 256
@@ -432,7 +433,13 @@ def run_batch(args, fb, torch, dist, rank, world, local):
         D = args.decode_len
     hm = fb.HostModel(path)
     p = hm.params
-    ctx = fb.Context(hm, device=local, max_seq=P + D, max_batch=B)
+    tp = args.workload == "7b-tp" and world > 1
+    if tp:
+        box = [fb.tp_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(box, src=0)
+        ctx = fb.Context(hm, device=local, max_seq=P + D, tp=(rank, world, box[0]), max_batch=B)
+    else:
+        ctx = fb.Context(hm, device=local, max_seq=P + D, max_batch=B)
     kv = ctx.kv(P + D, max_batch=B)
     kvd = p.n_kv_heads * p.head_dim
     t_fill = time.perf_counter()
@@ -464,8 +471,9 @@ def run_batch(args, fb, torch, dist, rank, world, local):
         t = torch.tensor([ms_total, wall * 1e3], device=f"cuda:{local}", dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms_total, wall = float(t[0].item()), float(t[1].item()) / 1e3
-    value = world * args.steps * D * B / (ms_total / 1e3)
-    e2e = world * args.steps * D * B / wall
+    reps = 1 if tp else world  # tensor parallel: the ranks share one batch
+    value = reps * args.steps * D * B / (ms_total / 1e3)
+    e2e = reps * args.steps * D * B / wall
     mid = P + D // 2
     if args.workload == "7b-tp":
         weights, kv_seq = WEIGHTS_7B, 524_288 * mid
@@ -480,15 +488,16 @@ def run_batch(args, fb, torch, dist, rank, world, local):
     step_bytes = weights + B * kv_seq
     peak, peak_kind = peaks()
     if rank == 0:
-        ach = step_bytes * (value / B) / world / 1e9
+        ach = step_bytes * (value / B / reps) / (world if tp else 1) / 1e9
         name = {"7b-tp": "7B Q4_K_M (Llama-2-7B shape), each slot prefilled with a 512-token prompt",
                 "q5km-long": "1.1B Q5_K_M (TinyLlama shape), every slot's KV pre-filled to 2048 positions"}[args.workload]
         line = {"metric": f"decode tok/s ({args.workload}, bs={B})", "value": value, "unit": "tok/s",
                 "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_total / args.steps,
-                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16 x f16 -> f32",
+                "higher_is_better": True, "scaling": "strong" if tp else "weak", "vs_baseline": None,
+                "dtype": "f16 x f16 -> f32",
                 "data": "synthetic (seeded random-init weights; seeded prompt ids or seeded N(0,1) KV)",
-                "config": {"workload": name, "context": P, "decode_tokens_per_step": D, "global_batch": B * world,
-                           "parallelism": f"replicas x{world}",
+                "config": {"workload": name, "context": P, "decode_tokens_per_step": D, "global_batch": B * reps,
+                           "parallelism": f"tp{world}" if tp else f"replicas x{world}",
                            "step_mode": "batched layer pass (tcgen05 GEMMs), one captured graph per step",
                            "fill_seconds": t_fill},
                 "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 8 * B / D, "d2h_bytes_per_step": 4 * B},

@@ -399,6 +399,7 @@ struct gpu_context {
     int prefill_mode = 0;           // 0: batched when the model allows it, 1: token by token
     int pf_cap = 0;
     float *pf_x = nullptr, *pf_qkv = nullptr, *pf_att = nullptr, *pf_hg = nullptr, *pf_hu = nullptr;
+    float *pf_x2 = nullptr;            // tensor parallel: residual stream after Wo's all-reduce
     uint8_t *pf_bp = nullptr;          // GEMM input packed as the MMA's B operand (hi / lo fp16)
     std::vector<CUtensorMap> pf_maps;  // per layer: tensor maps of wq wk wv wo w1 w2 w3
     std::vector<const uint8_t *> pf_w; // per layer: the GEMMs' weights (wq .. w3; padded Q6_K copies)
@@ -438,7 +439,7 @@ extern "C" void fiber_cuda_free(fiber_ctx_t *c) {
     if (c->ar_epoch) cudaFree(c->ar_epoch);
     if (c->comm) ncclCommDestroy(c->comm);
     for (void *q : c->pf_pad) cudaFree(q);
-    void *dev[] = {c->smp_rng, c->smp_out, c->att_ws, c->att_tickets, c->bt_pos, c->bt_arg, c->bt_rec, c->bt_step, c->bt_logits, c->pf_x, c->pf_qkv, c->pf_att, c->pf_hg, c->pf_hu, c->pf_bp, c->pf_tok, c->x2, c->d_shard, c->d_data, c->x, c->qkv, c->att, c->h, c->logits, c->rope, c->io, c->rec,
+    void *dev[] = {c->pf_x2, c->smp_rng, c->smp_out, c->att_ws, c->att_tickets, c->bt_pos, c->bt_arg, c->bt_rec, c->bt_step, c->bt_logits, c->pf_x, c->pf_qkv, c->pf_att, c->pf_hg, c->pf_hu, c->pf_bp, c->pf_tok, c->x2, c->d_shard, c->d_data, c->x, c->qkv, c->att, c->h, c->logits, c->rope, c->io, c->rec,
                    c->att_part, c->att_cnt, c->am_part, c->am_cnt, c->d_phases, c->d_bar,
                    c->pk_gf[0], c->pk_gf[1], c->pk_gf[2], c->pk_gf[3], c->pk_ss[0], c->pk_ss[1]};
     for (void *p : dev)
@@ -1261,7 +1262,7 @@ static bool g5_type_ok(int t) { return t == T_Q4_K || t == T_Q5_K || t == T_Q6_K
 // The batched layer pass (tensor-core GEMMs) covers this model: prefill chunks and
 // batched decode steps.
 static bool batched_ok(const gpu_context *c) {
-    if (c->tp_world != 1) return false;
+    if ((c->nh_l * (int)c->p.head_dim) % 256) return false;  // Wo's input columns: whole super-blocks
     if (!g5_type_ok(c->t_out) || c->G > 8 || ((uintptr_t)c->out & 15)) return false;
     for (const LayerDev &d : c->L) {
         const int ts[7] = {d.tq, d.tk, d.tv, d.to, d.t1, d.t2, d.t3};
@@ -1402,9 +1403,11 @@ static cudaError_t pf_pack(gpu_context *c, const float *x, int cols, const float
 
 // One tensor-core GEMM of the prefill on the packed input: y[t][off + r] (+)= W[r,:] . xn[t,:]
 static cudaError_t pf_gemm(gpu_context *c, const CUtensorMap &map, const uint8_t *w, int type, int rows, int cols,
-                           float *y, int ldy, int off, bool acc, int n, cudaStream_t st) {
+                           float *y, int ldy, int off, bool acc, int n, cudaStream_t st,
+                           const float *resid = nullptr) {
     G5Params g;
     memset(&g, 0, sizeof(g));
+    g.resid = resid;
     g.wmap = map;
     g.w = w;
     g.type = type;
@@ -1426,23 +1429,33 @@ static cudaError_t pf_gemm(gpu_context *c, const CUtensorMap &map, const uint8_t
 // SwiGLU, down GEMM (+residual).
 static cudaError_t enqueue_layers(gpu_context *c, const kv_cache_t *kv, int n, const TokenPlace &at, cudaStream_t st) {
     const model_params_t &p = c->p;
-    const int dim = p.dim, ffn = p.ffn_dim, hd = p.head_dim, kvd = c->kvd, ldq = dim + 2 * kvd;
+    // this rank's share (the whole model when tp_world == 1): query / KV heads, FFN rows
+    const int dim = p.dim, hd = p.head_dim, qd = c->nh_l * hd, kvd = c->nkv_l * hd, ffn = c->ffn_l;
+    const int ldq = qd + 2 * kvd;
+    const bool tp = c->tp_world > 1, lead = c->tp_rank == 0;
+    // tensor parallel: partial products summed over the ranks (rank 0 adds the residual)
+    auto reduce = [&](float *buf) -> cudaError_t {
+        if (!tp) return cudaSuccess;
+        return ncclAllReduce(buf, buf, (size_t)n * dim, ncclFloat, ncclSum, c->comm, st) == ncclSuccess
+                   ? cudaSuccess
+                   : cudaErrorUnknown;
+    };
     cudaError_t e = cudaSuccess;
     for (uint32_t l = 0; l < p.n_layers && e == cudaSuccess; l++) {
         const LayerDev &d = c->L[l];
         const CUtensorMap *mp = &c->pf_maps[7 * l];
         const uint8_t *const *pw = &c->pf_w[7 * l];
         if ((e = pf_pack(c, c->pf_x, dim, d.attn_norm, n, st))) break;
-        if ((e = pf_gemm(c, mp[0], pw[0], d.tq, dim, dim, c->pf_qkv, ldq, 0, false, n, st))) break;
-        if ((e = pf_gemm(c, mp[1], pw[1], d.tk, kvd, dim, c->pf_qkv, ldq, dim, false, n, st))) break;
-        if ((e = pf_gemm(c, mp[2], pw[2], d.tv, kvd, dim, c->pf_qkv, ldq, dim + kvd, false, n, st))) break;
+        if ((e = pf_gemm(c, mp[0], pw[0], d.tq, qd, dim, c->pf_qkv, ldq, 0, false, n, st))) break;
+        if ((e = pf_gemm(c, mp[1], pw[1], d.tk, kvd, dim, c->pf_qkv, ldq, qd, false, n, st))) break;
+        if ((e = pf_gemm(c, mp[2], pw[2], d.tv, kvd, dim, c->pf_qkv, ldq, qd + kvd, false, n, st))) break;
         RopeKvParams rk;
         rk.qkv = c->pf_qkv;
         rk.ldq = ldq;
         rk.at = at;
         rk.rope = c->rope;
-        rk.n_heads = p.n_heads;
-        rk.n_kv = p.n_kv_heads;
+        rk.n_heads = c->nh_l;
+        rk.n_kv = c->nkv_l;
         rk.hd = hd;
         rk.k_pool = kv->k_pool;
         rk.v_pool = kv->v_pool;
@@ -1455,28 +1468,40 @@ static cudaError_t enqueue_layers(gpu_context *c, const kv_cache_t *kv, int n, c
         ap.qkv = c->pf_qkv;
         ap.ldq = ldq;
         ap.out = c->pf_att;
-        ap.ldo = dim;
+        ap.ldo = qd;
         ap.at = at;
         ap.k_pool = kv->k_pool;
         ap.v_pool = kv->v_pool;
         ap.page_table = kv->page_table;
         ap.layer = l;
         ap.n_layers = p.n_layers;
-        ap.n_kv = p.n_kv_heads;
-        ap.n_heads = p.n_heads;
+        ap.n_kv = c->nkv_l;
+        ap.n_heads = c->nh_l;
         ap.scale = 1.0f / sqrtf((float)hd);
         ap.part = c->att_ws;
         ap.tickets = c->att_tickets;
         if ((e = launch_attn_prefill(c, ap, n, st))) break;
-        if ((e = pf_pack(c, c->pf_att, dim, nullptr, n, st))) break;
-        if ((e = pf_gemm(c, mp[3], pw[3], d.to, dim, dim, c->pf_x, dim, 0, true, n, st))) break;
-        if ((e = pf_pack(c, c->pf_x, dim, d.ffn_norm, n, st))) break;
+        if ((e = pf_pack(c, c->pf_att, qd, nullptr, n, st))) break;
+        // residual stream after Wo: pf_x (single GPU) or pf_x2 (sum over the ranks)
+        float *xa = tp ? c->pf_x2 : c->pf_x;
+        if (tp) {
+            if ((e = pf_gemm(c, mp[3], pw[3], d.to, dim, qd, xa, dim, 0, false, n, st, lead ? c->pf_x : nullptr))) break;
+            if ((e = reduce(xa))) break;
+        } else if ((e = pf_gemm(c, mp[3], pw[3], d.to, dim, qd, xa, dim, 0, true, n, st))) {
+            break;
+        }
+        if ((e = pf_pack(c, xa, dim, d.ffn_norm, n, st))) break;
         if ((e = pf_gemm(c, mp[4], pw[4], d.t1, ffn, dim, c->pf_hg, ffn, 0, false, n, st))) break;
         if ((e = pf_gemm(c, mp[6], pw[6], d.t3, ffn, dim, c->pf_hu, ffn, 0, false, n, st))) break;
         swiglu_rows_kernel<<<(n * ffn + 255) / 256, 256, 0, st>>>(c->pf_hg, c->pf_hu, (size_t)n * ffn);
         if ((e = cudaGetLastError()) != cudaSuccess) break;
         if ((e = pf_pack(c, c->pf_hg, ffn, nullptr, n, st))) break;
-        e = pf_gemm(c, mp[5], pw[5], d.t2, dim, ffn, c->pf_x, dim, 0, true, n, st);
+        if (tp) {
+            if ((e = pf_gemm(c, mp[5], pw[5], d.t2, dim, ffn, c->pf_x, dim, 0, false, n, st, lead ? xa : nullptr))) break;
+            e = reduce(c->pf_x);
+        } else {
+            e = pf_gemm(c, mp[5], pw[5], d.t2, dim, ffn, c->pf_x, dim, 0, true, n, st);
+        }
     }
     return e;
 }
@@ -1542,6 +1567,7 @@ static int pf_alloc(gpu_context *c) {
     const size_t kmax = p.dim > p.ffn_dim ? p.dim : p.ffn_dim;
     CK(cudaMalloc(&c->pf_bp, (T + G5_T - 1) / G5_T * G5_T * kmax * 4));
     CK(cudaMalloc(&c->pf_tok, T * 4));
+    if (c->tp_world > 1) CK(cudaMalloc(&c->pf_x2, T * p.dim * 4));
     const size_t B = c->max_batch;
     CK(cudaMalloc(&c->bt_pos, B * 4));
     CK(cudaMalloc(&c->bt_arg, B * 4));
@@ -1553,12 +1579,13 @@ static int pf_alloc(gpu_context *c) {
     CK(cudaMemset(c->att_tickets, 0, ATT_PART_ENTRIES * sizeof(unsigned int)));
     c->pf_maps.assign(7 * p.n_layers, CUtensorMap{});
     c->pf_w.assign(7 * p.n_layers, nullptr);
-    const int dim = p.dim, ffn = p.ffn_dim, kvd = c->kvd;
+    // this rank's share: rows of Wq / Wk / Wv / W1 / W3, input columns of Wo / W2
+    const int dim = p.dim, hd = p.head_dim, qd = c->nh_l * hd, kvd = c->nkv_l * hd, ffn = c->ffn_l;
     for (uint32_t l = 0; l < p.n_layers; l++) {
         const LayerDev &d = c->L[l];
         const uint8_t *ws[7] = {d.wq, d.wk, d.wv, d.wo, d.w1, d.w2, d.w3};
         const int ts[7] = {d.tq, d.tk, d.tv, d.to, d.t1, d.t2, d.t3};
-        const int rows[7] = {dim, kvd, kvd, dim, ffn, dim, ffn}, cols[7] = {dim, dim, dim, dim, dim, ffn, dim};
+        const int rows[7] = {qd, kvd, kvd, dim, ffn, dim, ffn}, cols[7] = {dim, dim, dim, qd, dim, ffn, dim};
         for (int k = 0; k < 7; k++) {
             const uint8_t **pw = &c->pf_w[7 * l + k];
             CK(g5_weights(c, ws[k], ts[k], rows[k], cols[k], pw));
@@ -2221,5 +2248,15 @@ extern "C" int fiber_decode_sample(fiber_ctx_t *c, kv_cache_t *kv, int32_t first
 extern "C" int fiber_tp_collective(fiber_ctx_t *c) {
     if (!c) return set_err(FIBER_EARG, "no context");
     return c->tp_world <= 1 ? 0 : (c->ar_ok ? 2 : 1);
+}
+
+extern "C" int fiber_set_max_batch(fiber_ctx_t *c, int max_batch) {
+    if (!c || max_batch < 1 || max_batch > FIBER_MAX_BATCH)
+        return set_err(FIBER_EARG, "fiber_set_max_batch: max_batch outside [1, %d]", FIBER_MAX_BATCH);
+    if (c->pf_cap) return set_err(FIBER_EARG, "fiber_set_max_batch: the batched buffers already exist");
+    if (max_batch > 1 && !batched_ok(c))
+        return set_err(FIBER_EUNSUPPORTED, "batched decode does not cover this model");
+    c->max_batch = max_batch;
+    return FIBER_OK;
 }
 

@@ -66,6 +66,7 @@ struct G5Params {
     float *y;              // [ntok][ldy]
     int ldy, out_off;
     int epi;               // G5_STORE: y = acc; G5_RESID: y += acc
+    const float *resid;    // non-null: y = resid + acc (same layout as y; out of place)
     int *err;              // set to 6 when a wait gave up
 };
 // Split-K: gridDim.z = ks CTAs per tile, launched as one thread-block cluster (1, 1, ks).
@@ -576,8 +577,8 @@ __global__ void __launch_bounds__(G5_THREADS, 1) gemm_tc5_kernel(const __grid_co
                         const int t = tile * G5_T + c0 / 2 + j;
                         if (t < p.ntok) {
                             const float y = __fadd_rn(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1]));
-                            float *dst = p.y + (size_t)t * p.ldy + p.out_off + row0 + rr;
-                            *dst = p.epi == G5_RESID ? __fadd_rn(*dst, y) : y;
+                            const size_t o = (size_t)t * p.ldy + p.out_off + row0 + rr;
+                            p.y[o] = p.resid ? __fadd_rn(p.resid[o], y) : (p.epi == G5_RESID ? __fadd_rn(p.y[o], y) : y);
                         }
                     }
                 }
@@ -611,8 +612,8 @@ __global__ void __launch_bounds__(G5_THREADS, 1) gemm_tc5_kernel(const __grid_co
 #pragma unroll
                 for (int j = 0; j < 4; j++) {
                     if (r0 + j >= vrows) break;
-                    float *dst = p.y + (size_t)t * p.ldy + p.out_off + row0 + r0 + j;
-                    *dst = p.epi == G5_RESID ? __fadd_rn(*dst, vals[j]) : vals[j];
+                    const size_t o = (size_t)t * p.ldy + p.out_off + row0 + r0 + j;
+                    p.y[o] = p.resid ? __fadd_rn(p.resid[o], vals[j]) : (p.epi == G5_RESID ? __fadd_rn(p.y[o], vals[j]) : vals[j]);
                 }
             }
         }

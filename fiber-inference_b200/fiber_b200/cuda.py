@@ -30,7 +30,7 @@ EXPORTED = [
     "fiber_dequant", "fiber_gemv_host", "gpu_init", "gpu_free", "gpu_embed", "gpu_forward_token",
     "gpu_get_logits", "gpu_forward_classifier", "gpu_get_device", "kv_cache_init", "kv_cache_init_paged",
     "kv_cache_free", "kv_cache_write", "kv_cache_read", "fiber_gemv_argmax_noalloc", "fiber_prefill_slot",
-    "fiber_decode_greedy_batch", "fiber_sample", "fiber_decode_sample", "fiber_tp_collective",
+    "fiber_decode_greedy_batch", "fiber_sample", "fiber_decode_sample", "fiber_tp_collective", "fiber_set_max_batch",
 ]
 
 
@@ -87,6 +87,7 @@ def cuda_lib() -> C.CDLL:
         L.fiber_cuda_init_tp.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_int]
         L.fiber_tp_info.argtypes = [C.c_void_p, C.POINTER(TPPlan)]
         L.fiber_tp_collective.argtypes = [C.c_void_p]
+        L.fiber_set_max_batch.argtypes = [C.c_void_p, C.c_int]
         L.fiber_set_prefill_mode.argtypes = [C.c_void_p, C.c_int]
         L.fiber_gemm.argtypes = [C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_void_p,
                                  C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p]
@@ -243,6 +244,8 @@ class Context:
             self.h = cuda_lib().fiber_cuda_init_tp(host_model.h, device, rank, world, idbuf, max_seq)
         if not self.h:
             raise FiberError(f"fiber_cuda_init: {cuda_lib().fiber_last_error().decode()}")
+        if tp is not None and max_batch > 1:
+            _check(cuda_lib().fiber_set_max_batch(self.h, int(max_batch)), "fiber_set_max_batch")
         self.device = device
         self.max_seq = max_seq or self.p.context_length
         self.plan = TPPlan()

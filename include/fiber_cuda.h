@@ -176,6 +176,10 @@ int fiber_tp_info(fiber_ctx_t *ctx, fiber_tp_plan_t *out);
  * fiber_cuda_init_tp selects NCCL. */
 int fiber_tp_collective(fiber_ctx_t *ctx);
 
+/* Raise the sequences one batched step can carry (as fiber_cuda_init's max_batch; the
+ * tensor-parallel constructor starts at 1). Only before the first batched call. */
+int fiber_set_max_batch(fiber_ctx_t *ctx, int max_batch);
+
 /* Timeline of one persistent decode step (mode 0): runs the step for `token` at
  * `pos` and fills out[n_phases][n_ctas][10] (uint64) with, per phase and CTA:
  * 0 globaltimer ns when the phase's grid barrier released the CTA, 1 SM cycles

@@ -1,7 +1,9 @@
 """Tensor-parallel decode on two GPUs (one process per GPU, an all-reduce after Wo and
 W_down: the one-shot peer-memory all-reduce, or NCCL): both ranks produce the oracle's
 greedy tokens, teacher-forced logits stay within the decode tolerances, and with the
-peer all-reduce both ranks' logits are bit-identical. Skipped with fewer than two GPUs."""
+peer all-reduce both ranks' logits are bit-identical. The batched layer pass (prefill,
+several sequences per step) is sharded the same way and reproduces the oracle per
+sequence. Skipped with fewer than two GPUs."""
 from __future__ import annotations
 
 import numpy as np
@@ -24,7 +26,7 @@ def _worker(rank, world, nid, path, prompt, n_gen, q, coll):
         if coll == "nccl":
             os.environ["FIBER_TP_ALLREDUCE"] = "nccl"
         hm = fb.HostModel(path)
-        ctx = fb.Context(hm, device=rank, max_seq=256, tp=(rank, world, nid))
+        ctx = fb.Context(hm, device=rank, max_seq=256, tp=(rank, world, nid), max_batch=3)
         kv = ctx.kv(256)
         logits = []
         for pos, t in enumerate(prompt[:6]):  # teacher-forced, every rank in lockstep
@@ -33,12 +35,17 @@ def _worker(rank, world, nid, path, prompt, n_gen, q, coll):
         kv2 = ctx.kv(256)
         first = ctx.prefill(kv2, np.asarray(prompt, np.int32))
         toks, _ = ctx.decode_greedy(kv2, first, len(prompt), n_gen)
+        # batched: three sequences of different lengths on KV slots 0..2
+        kv3 = ctx.kv(256, max_batch=3)
+        prompts = [prompt[: 4 + 3 * i] for i in range(3)]
+        firsts = [ctx.prefill(kv3, pr, slot=i) for i, pr in enumerate(prompts)]
+        btoks, _ = ctx.decode_greedy_batch(kv3, firsts, [len(pr) for pr in prompts], 20)
         plan = ctx.plan
         q.put((rank, first, toks.tolist(), np.stack(logits),
-               (plan.heads, plan.kv_heads, plan.ffn_blocks, ctx.tp_collective), None))
+               (plan.heads, plan.kv_heads, plan.ffn_blocks, ctx.tp_collective), None, firsts, btoks.tolist()))
         ctx.close()
     except Exception as e:  # report instead of hanging the parent
-        q.put((rank, None, None, None, None, repr(e)))
+        q.put((rank, None, None, None, None, repr(e), None, None))
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
@@ -86,3 +93,10 @@ def test_tp2_matches_oracle(tiny_model, coll):
     for r in (0, 1):
         assert res[r][1] == want[0]
         assert res[r][2] == want[1:].tolist()
+    # batched (tensor-parallel layer pass): each sequence equals the oracle run alone
+    for i in range(3):
+        pr = prompt[: 4 + 3 * i]
+        wb = om.state(256, kv_fp16=True).generate(pr, 20)
+        for r in (0, 1):
+            assert res[r][6][i] == wb[0], (r, i)
+            assert [row[i] for row in res[r][7]] == wb[1:].tolist(), (r, i)
