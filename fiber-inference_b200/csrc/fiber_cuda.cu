@@ -1297,9 +1297,23 @@ static int attn_psplit(int n, int n_kv, int max_pos) {
     return ps < 1 ? 1 : ps;
 }
 
+template <int HD, int G>
+static cudaError_t launch_attn_prefill_tb_t(const AttnPrefillParams &a, int n, cudaStream_t st) {
+    constexpr int TB = apf_tb(HD, G);
+    attn_prefill_tb_kernel<HD, G, TB><<<dim3((n + TB - 1) / TB, a.n_kv), ATTN_THREADS, 0, st>>>(a, n);
+    return cudaGetLastError();
+}
+
 static cudaError_t launch_attn_prefill(const gpu_context *c, const AttnPrefillParams &a, int n, cudaStream_t st) {
     const int hd = c->p.head_dim, G = c->G;
     const int ps = (a.part && a.tickets) ? attn_psplit(n, a.n_kv, a.at.max_pos) : 1;
+    if (ps == 1 && !a.at.pos && a.at.slot_step == 0 && G < 8) {  // prompt chunk: blocks of tokens
+#define APT_CASE(H, GG) \
+    if (hd == H && G == GG) return launch_attn_prefill_tb_t<H, GG>(a, n, st);
+        APT_CASE(64, 1) APT_CASE(64, 2) APT_CASE(64, 4)
+        APT_CASE(128, 1) APT_CASE(128, 2) APT_CASE(128, 4)
+#undef APT_CASE
+    }
 #define APF_CASE(H, GG) \
     if (hd == H && G == GG) return launch_attn_prefill_t<H, GG>(a, n, ps, st);
     APF_CASE(64, 1) APF_CASE(64, 2) APF_CASE(64, 4) APF_CASE(64, 8)

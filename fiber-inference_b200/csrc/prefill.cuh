@@ -116,6 +116,66 @@ struct AttnPrefillParams {
     unsigned int *tickets;  // [n][n_kv], zero between launches
 };
 
+// One page (nt <= 64 positions, staged in ks / vs) for one query vector q (shared
+// memory, HD floats), on one warp: scores (lanes over positions, fp32 FMAs over fp16 K),
+// page max and sum, P.V, then the online merge into the running (m, l, o) state
+// (first: the state starts here).
+template <int HD>
+FDEV void apf_page(const float *q, const uint16_t (*ks)[HD + 2], const uint16_t (*vs)[HD], int nt, float scale,
+                   int lane, bool first, float &m_run, float &l_run, float (&o_run)[HD / 32]) {
+    constexpr int DPL = HD / 32;
+    float sc2[2];
+#pragma unroll
+    for (int k = 0; k < 2; k++) {
+        const int r = lane + 32 * k;
+        float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;
+        if (r < nt) {
+#pragma unroll
+            for (int d = 0; d < HD; d += 4) {
+                d0 = fmaf(q[d + 0], __half2float(__ushort_as_half(ks[r][d + 0])), d0);
+                d1 = fmaf(q[d + 1], __half2float(__ushort_as_half(ks[r][d + 1])), d1);
+                d2 = fmaf(q[d + 2], __half2float(__ushort_as_half(ks[r][d + 2])), d2);
+                d3 = fmaf(q[d + 3], __half2float(__ushort_as_half(ks[r][d + 3])), d3);
+            }
+        }
+        sc2[k] = r < nt ? __fmul_rn((d0 + d1) + (d2 + d3), scale) : -INFINITY;
+    }
+    float m = fmaxf(sc2[0], sc2[1]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    const float e0 = lane < nt ? expf(sc2[0] - m) : 0.f;
+    const float e1 = lane + 32 < nt ? expf(sc2[1] - m) : 0.f;
+    float l = e0 + e1;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+    float o1[DPL], o2[DPL];
+#pragma unroll
+    for (int j = 0; j < DPL; j++) o1[j] = o2[j] = 0.f;
+    for (int r = 0; r < min(nt, 32); r++) {
+        const float w = __shfl_sync(0xffffffffu, e0, r);
+#pragma unroll
+        for (int j = 0; j < DPL; j++) o1[j] = fmaf(w, __half2float(__ushort_as_half(vs[r][lane + 32 * j])), o1[j]);
+    }
+    for (int r = 32; r < nt; r++) {
+        const float w = __shfl_sync(0xffffffffu, e1, r - 32);
+#pragma unroll
+        for (int j = 0; j < DPL; j++) o2[j] = fmaf(w, __half2float(__ushort_as_half(vs[r][lane + 32 * j])), o2[j]);
+    }
+    if (first) {
+        m_run = m;
+        l_run = l;
+#pragma unroll
+        for (int j = 0; j < DPL; j++) o_run[j] = o1[j] + o2[j];
+    } else {
+        const float M = fmaxf(m_run, m);
+        const float al = expf(m_run - M), be = expf(m - M);
+        l_run = fmaf(al, l_run, be * l);
+#pragma unroll
+        for (int j = 0; j < DPL; j++) o_run[j] = fmaf(al, o_run[j], be * (o1[j] + o2[j]));
+        m_run = M;
+    }
+}
+
 // CTA (token t, KV head g[, page split z]): the G query heads of g attend to positions
 // 0 .. pos(t) of the token's slot, page by page (64 positions) with the decode path's
 // score / softmax / P.V arithmetic, pages combined online.
@@ -152,59 +212,8 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_prefill_kernel(const AttnPr
             *reinterpret_cast<uint4 *>(&vs[r][8 * k8]) = vv4;
         }
         __syncthreads();
-        for (int h = warp; h < G; h += ATTN_THREADS / 32) {
-            float sc2[2];
-#pragma unroll
-            for (int k = 0; k < 2; k++) {
-                const int r = lane + 32 * k;
-                float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;
-                if (r < nt) {
-#pragma unroll
-                    for (int d = 0; d < HD; d += 4) {
-                        d0 = fmaf(qs[h][d + 0], __half2float(__ushort_as_half(ks[r][d + 0])), d0);
-                        d1 = fmaf(qs[h][d + 1], __half2float(__ushort_as_half(ks[r][d + 1])), d1);
-                        d2 = fmaf(qs[h][d + 2], __half2float(__ushort_as_half(ks[r][d + 2])), d2);
-                        d3 = fmaf(qs[h][d + 3], __half2float(__ushort_as_half(ks[r][d + 3])), d3);
-                    }
-                }
-                sc2[k] = r < nt ? __fmul_rn((d0 + d1) + (d2 + d3), a.scale) : -INFINITY;
-            }
-            float m = fmaxf(sc2[0], sc2[1]);
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-            const float e0 = lane < nt ? expf(sc2[0] - m) : 0.f;
-            const float e1 = lane + 32 < nt ? expf(sc2[1] - m) : 0.f;
-            float l = e0 + e1;
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
-            float o1[DPL], o2[DPL];
-#pragma unroll
-            for (int j = 0; j < DPL; j++) o1[j] = o2[j] = 0.f;
-            for (int r = 0; r < min(nt, 32); r++) {
-                const float w = __shfl_sync(0xffffffffu, e0, r);
-#pragma unroll
-                for (int j = 0; j < DPL; j++) o1[j] = fmaf(w, __half2float(__ushort_as_half(vs[r][lane + 32 * j])), o1[j]);
-            }
-            for (int r = 32; r < nt; r++) {
-                const float w = __shfl_sync(0xffffffffu, e1, r - 32);
-#pragma unroll
-                for (int j = 0; j < DPL; j++) o2[j] = fmaf(w, __half2float(__ushort_as_half(vs[r][lane + 32 * j])), o2[j]);
-            }
-            // G <= 8 heads: warp h keeps head h's running state across pages
-            if (c == cbeg) {
-                m_run = m;
-                l_run = l;
-#pragma unroll
-                for (int j = 0; j < DPL; j++) o_run[j] = o1[j] + o2[j];
-            } else {
-                const float M = fmaxf(m_run, m);
-                const float al = expf(m_run - M), be = expf(m - M);
-                l_run = fmaf(al, l_run, be * l);
-#pragma unroll
-                for (int j = 0; j < DPL; j++) o_run[j] = fmaf(al, o_run[j], be * (o1[j] + o2[j]));
-                m_run = M;
-            }
-        }
+        for (int h = warp; h < G; h += ATTN_THREADS / 32)  // warp h keeps head h's state
+            apf_page<HD>(qs[h], ks, vs, nt, a.scale, lane, c == cbeg, m_run, l_run, o_run);
     }
     if (ps == 1) {
         if (warp < G)
@@ -253,6 +262,80 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_prefill_kernel(const AttnPr
         for (int j = 0; j < DPL; j++) a.out[(size_t)t * a.ldo + (size_t)(g * G + warp) * HD + lane + 32 * j] = o[j] / L;
     }
     if (tid == 0) *ticket = 0u;
+}
+
+// Prompt chunks (every token of one KV slot, consecutive positions) of models with
+// fewer than 8 query heads per KV head: CTA (block of TB consecutive tokens, KV head g). Each page is staged once for the block; the G x TB
+// (query head, token) pairs are spread over the 8 warps (pair p: token p / G, head
+// p % G; warp w takes pairs w, w + 8, ...), each pair with apf_page's arithmetic in the
+// same page order as attn_prefill_kernel, so the outputs are the same bit for bit.
+// Tokens per block: 8 / G, so that each warp holds one (head, token) pair (the work per
+// warp stays that of attn_prefill_kernel and the freed warps take more tokens), as far as
+// the q vectors fit the 48 KB of static shared memory next to one K and one V page.
+HDCE int apf_tb(int hd, int g) {
+    const int page = ATTN_P * (hd + 2) * 2 + ATTN_P * hd * 2, free_b = 48 * 1024 - page;
+    int tb = 8 / g;
+    while (tb > 1 && tb * g * hd * 4 > free_b) tb >>= 1;
+    return tb;
+}
+
+template <int HD, int G, int TB>
+__global__ void __launch_bounds__(ATTN_THREADS) attn_prefill_tb_kernel(const AttnPrefillParams a, int n) {
+    constexpr int P = ATTN_P, KST = HD + 2, DPL = HD / 32, NW = ATTN_THREADS / 32;
+    constexpr int PAIRS = G * TB, PPW = (PAIRS + NW - 1) / NW;
+    __shared__ __align__(16) float qs[TB][G][HD];
+    __shared__ __align__(16) uint16_t ks[P][KST];
+    __shared__ __align__(16) uint16_t vs[P][HD];
+    const int t0 = blockIdx.x * TB, g = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int nvalid = min(TB, n - t0);
+    const int pos0 = place_pos(a.at, t0), posl = pos0 + nvalid - 1;
+    if (pos0 < 0 || posl >= a.at.max_pos) return;  // rope_kv_kernel reported it
+    const int nch = (posl + 1 + P - 1) / P;
+    const int32_t *pages = place_pages(a.at, a.page_table, t0);
+    for (int i = tid; i < nvalid * G * HD; i += ATTN_THREADS) {
+        const int tt = i / (G * HD), h = (i / HD) % G, d = i % HD;
+        qs[tt][h][d] = a.qkv[(size_t)(t0 + tt) * a.ldq + (size_t)(g * G + h) * HD + d];
+    }
+    float m_run[PPW], l_run[PPW], o_run[PPW][DPL];
+#pragma unroll
+    for (int q = 0; q < PPW; q++) {
+        m_run[q] = -INFINITY;
+        l_run[q] = 0.f;
+#pragma unroll
+        for (int j = 0; j < DPL; j++) o_run[q][j] = 0.f;
+    }
+    __syncthreads();  // qs staged
+    for (int c = 0; c < nch; c++) {
+        __syncthreads();  // previous page consumed
+        const int p0 = c * P, nt = min(P, posl + 1 - p0);
+        const size_t base = (((size_t)pages[c] * a.n_layers + a.layer) * a.n_kv + g) * (size_t)P * HD;
+        constexpr int V8 = HD / 8;
+        for (int i = tid; i < nt * V8; i += ATTN_THREADS) {
+            const int r = i / V8, k8 = i % V8;
+            const uint4 kv4 = *reinterpret_cast<const uint4 *>(a.k_pool + base + (size_t)r * HD + 8 * k8);
+            const uint4 vv4 = *reinterpret_cast<const uint4 *>(a.v_pool + base + (size_t)r * HD + 8 * k8);
+            uint32_t *kd = reinterpret_cast<uint32_t *>(&ks[r][8 * k8]);
+            kd[0] = kv4.x; kd[1] = kv4.y; kd[2] = kv4.z; kd[3] = kv4.w;
+            *reinterpret_cast<uint4 *>(&vs[r][8 * k8]) = vv4;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int q = 0; q < PPW; q++) {
+            const int pr = warp + q * NW, tt = pr / G, h = pr % G;
+            if (pr >= PAIRS || tt >= nvalid) continue;
+            const int ntt = min(P, pos0 + tt + 1 - p0);  // this token's causal limit in the page
+            if (ntt <= 0) continue;                      // page entirely after this token
+            apf_page<HD>(qs[tt][h], ks, vs, ntt, a.scale, lane, c == 0, m_run[q], l_run[q], o_run[q]);
+        }
+    }
+#pragma unroll
+    for (int q = 0; q < PPW; q++) {
+        const int pr = warp + q * NW, tt = pr / G, h = pr % G;
+        if (pr >= PAIRS || tt >= nvalid) continue;
+#pragma unroll
+        for (int j = 0; j < DPL; j++)
+            a.out[(size_t)(t0 + tt) * a.ldo + (size_t)(g * G + h) * HD + lane + 32 * j] = o_run[q][j] / l_run[q];
+    }
 }
 
 __global__ void swiglu_rows_kernel(float *hg, const float *__restrict__ hu, size_t n) {
