@@ -1286,13 +1286,12 @@ static cudaError_t launch_attn_prefill_t(const AttnPrefillParams &a, int n, int 
     return cudaGetLastError();
 }
 
-// Page split: only when the (token, KV head) CTAs alone leave most SMs idle and the
-// contexts can be long.
+// Page split: enough (token, KV head, split) CTAs for about four waves, each split
+// keeping at least 4 of the longest context's pages (short contexts stay unsplit).
 static int attn_psplit(int n, int n_kv, int max_pos) {
     const int base = n * n_kv, pages = (max_pos + ATTN_P - 1) / ATTN_P;
-    if (base * 3 >= sm_count() * 2) return 1;
-    int ps = (2 * sm_count() + base - 1) / base;
-    ps = std::min(ps, std::min(16, pages / 2));
+    int ps = (4 * sm_count() + base - 1) / base;
+    ps = std::min(ps, std::min(16, pages / 4));
     ps = std::min(ps, ATT_PART_ENTRIES / base);
     return ps < 1 ? 1 : ps;
 }
