@@ -793,13 +793,13 @@ extern "C" int fiber_tp_unique_id(uint8_t out[FIBER_TP_ID_BYTES]) {
 // addressed in place in the uploaded GGUF data; Wo and W_down are cut along their
 // input dimension (whole super-blocks of every row) into d_shard; an NCCL
 // communicator joins the ranks.
-// The one-shot all-reduce's buffers: every rank allocates its slot / flag area, the
-// areas' IPC handles are all-gathered over NCCL (which also orders every rank's zeroing
-// before any peer's first push), and each rank maps its peers' areas.
+// The one-shot all-reduce's buffers: every rank allocates its slot area (zeroed: epoch
+// 0, before any call), the areas' IPC handles are all-gathered over NCCL (which also
+// orders every rank's zeroing before any peer's first push), and each rank maps its
+// peers' areas.
 static int ar_setup(gpu_context *c, int n_max) {
     const int W = c->tp_world, R = c->tp_rank;
-    const size_t slot_bytes = (size_t)2 * W * n_max * 4, flag_off = (slot_bytes + 255) / 256 * 256;
-    const size_t total = flag_off + (size_t)2 * W * sizeof(unsigned int);
+    const size_t total = (size_t)2 * W * n_max * sizeof(unsigned long long);
     CK(cudaMalloc(&c->ar_local, total));
     CK(cudaMemset(c->ar_local, 0, total));
     CK(cudaMalloc(&c->ar_epoch, sizeof(unsigned int)));
@@ -825,15 +825,12 @@ static int ar_setup(gpu_context *c, int n_max) {
     a.epoch = c->ar_epoch;
     a.err = &c->io->err;
     for (int p = 0; p < W; p++) {
-        uint8_t *base = (uint8_t *)c->ar_local;
+        void *base = c->ar_local;
         if (p != R) {
-            void *q = nullptr;
-            CK(cudaIpcOpenMemHandle(&q, all[p], cudaIpcMemLazyEnablePeerAccess));
-            c->ar_peer[p] = q;
-            base = (uint8_t *)q;
+            CK(cudaIpcOpenMemHandle(&base, all[p], cudaIpcMemLazyEnablePeerAccess));
+            c->ar_peer[p] = base;
         }
-        a.slots[p] = (float *)base;
-        a.flags[p] = (unsigned int *)(base + flag_off);
+        a.slots[p] = (unsigned long long *)base;
     }
     c->ar_ok = true;
     return FIBER_OK;
@@ -1286,11 +1283,11 @@ static cudaError_t launch_attn_prefill_t(const AttnPrefillParams &a, int n, int 
     return cudaGetLastError();
 }
 
-// Page split: enough (token, KV head, split) CTAs for about four waves, each split
+// Page split: enough (token, KV head, split) CTAs for about eight waves, each split
 // keeping at least 4 of the longest context's pages (short contexts stay unsplit).
 static int attn_psplit(int n, int n_kv, int max_pos) {
     const int base = n * n_kv, pages = (max_pos + ATTN_P - 1) / ATTN_P;
-    int ps = (4 * sm_count() + base - 1) / base;
+    int ps = (8 * sm_count() + base - 1) / base;
     ps = std::min(ps, std::min(16, pages / 4));
     ps = std::min(ps, ATT_PART_ENTRIES / base);
     return ps < 1 ? 1 : ps;

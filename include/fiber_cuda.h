@@ -169,9 +169,10 @@ fiber_ctx_t *fiber_cuda_init_tp(const model_t *m, int device, int rank, int worl
 int fiber_tp_info(fiber_ctx_t *ctx, fiber_tp_plan_t *out);
 
 /* The all-reduce a sharded step uses after Wo and after W_down: 0 none (world 1),
- * 1 NCCL (ncclAllReduce), 2 the one-shot peer-memory all-reduce (each rank pushes its
- * partial into every rank's slot over NVLink, release / acquire flags with a bounded
- * wait, every rank sums the slots in rank order: identical results on all ranks).
+ * 1 NCCL (ncclAllReduce), 2 the one-shot peer-memory all-reduce (each rank stores its
+ * partial into every rank's slot over NVLink, each 8-byte word holding a value and the
+ * call's epoch; readers poll the words with a bounded wait, and every rank sums the
+ * partials in rank order: identical results on all ranks).
  * 2 is the default for up to 8 ranks; FIBER_TP_ALLREDUCE=nccl in the environment at
  * fiber_cuda_init_tp selects NCCL. */
 int fiber_tp_collective(fiber_ctx_t *ctx);
