@@ -1391,8 +1391,7 @@ static cudaError_t g5_weights(gpu_context *c, const uint8_t *w, int type, int ro
 
 static cudaError_t launch_g5_pack(const G5PackParams &a, cudaStream_t st) {
     const dim3 grid(((a.ntok + G5_T - 1) / G5_T) * (G5_T / 4), a.cols / G5_PACK_COLS);
-    g5_pack_kernel<<<grid, 128, 0, st>>>(a);
-    return cudaGetLastError();
+    return launch_pdl(g5_pack_kernel, grid, dim3(128), 0, st, a);
 }
 
 // Pack n rows of x (RMS-normalised with weights nw when given) into c->pf_bp.
@@ -2066,13 +2065,15 @@ static cudaError_t launch_g5_t(const G5Params &p, cudaStream_t st) {
     cfg.blockDim = dim3(G5_THREADS);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;  // the K splits of a tile: one cluster
     attr[0].val.clusterDim.x = 1;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = ks;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = pdl_enabled() ? 2 : 1;
     return cudaLaunchKernelEx(&cfg, gemm_tc5_kernel<T>, p);
 }
 

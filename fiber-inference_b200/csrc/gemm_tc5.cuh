@@ -335,6 +335,8 @@ __global__ void __launch_bounds__(128) g5_pack_kernel(const G5PackParams a) {
     __shared__ float rr[4];
     const int tile = blockIdx.x >> 4, grp = blockIdx.x & 15, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int t0 = tile * G5_T + 4 * grp, nchunk = a.cols / G5_KC, col0 = blockIdx.y * G5_PACK_COLS;
+    pdl_trigger();  // launched with programmatic stream serialization: x comes from the
+    pdl_wait();     // previous kernel
     {
         const int t = t0 + warp;
         float r = 1.0f;
@@ -442,6 +444,11 @@ __global__ void __launch_bounds__(G5_THREADS, 1) gemm_tc5_kernel(const __grid_co
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = tmem_slot;
     G5_MARK(11, 0);
+    // Programmatic dependent launch: the next kernel may set up while this one runs; this
+    // one's weights (constant) stream in before the previous kernel has finished, the
+    // packed inputs only after it (producer's pdl_wait below; every later use of the
+    // inputs or of y is ordered after that wait through the mbarriers).
+    pdl_trigger();
     G5_MARK(16, 0);
 
     if (warp == 0) {
@@ -476,6 +483,7 @@ __global__ void __launch_bounds__(G5_THREADS, 1) gemm_tc5_kernel(const __grid_co
             if (i >= NB) ok = g5_wait(&bempty[s], (uint32_t)((i / NB - 1) & 1), &fail);
             ok = __all_sync(0xffffffffu, ok);
             if (!ok) break;
+            if (i == 0) pdl_wait();  // the packed inputs were written by an earlier kernel
             if (lane == 0) {
                 g5_expect_tx(&bfull[s], (uint32_t)G5_B_BYTES);
                 g5_bulk(Bbuf + s * G5_B_BYTES, p.bp + ((size_t)(tile * nchunk + c) << 15), (uint32_t)G5_B_BYTES,
