@@ -37,7 +37,7 @@ constexpr int PK_WARPS = PK_CONSUMERS / 32;
 constexpr int PK_THREADS = PK_CONSUMERS + 32;   // + producer warp
 constexpr int PK_NDESC = 16;                    // tiles in flight per CTA
 constexpr int PK_RPRE = 8;                      // residual rows prefetched for this many tiles
-constexpr long long PK_SPIN_LIMIT = 1ll << 22;  // grid-barrier polls (with ~100 ns sleeps)
+constexpr long long PK_SPIN_LIMIT = 1ll << 24;  // grid-barrier polls (also limited to PK_WAIT_NS)
 // Optional per-phase, per-CTA timeline (PParams::trace non-null), fields:
 //  0 globaltimer (ns) when the phase's grid barrier released the CTA
 //  1 SM cycles from the phase start to that release     2 cycles staging the input vector
@@ -246,13 +246,13 @@ FDEV bool pk_grid_wait(const PParams &P, int ph) {
         if (ph > 0) {
             bool ok = false;
             const unsigned int *cnt = P.bar + (ph - 1);
-            for (long long i = 0; i < PK_SPIN_LIMIT; i++) {
+            const unsigned long long t0 = gtimer();
+            for (long long i = 0; i < PK_SPIN_LIMIT; i++) {  // each poll is an L2 round trip
                 if (ld_acquire_u32(cnt) >= gridDim.x) {
                     ok = true;
                     break;
                 }
-                if ((i & 63) == 63 && pk_abort) break;
-                __nanosleep(32);
+                if ((i & 63) == 63 && (pk_abort || gtimer() - t0 > PK_WAIT_NS)) break;
             }
             if (!ok) {
                 pk_abort = 1;
@@ -966,10 +966,8 @@ __global__ void __launch_bounds__(PK_THREADS, 1) decode_persistent_kernel(const 
             // descriptor has landed
             cp_async_wait_all();
             cbar();
-            if (tid == 0) {
-                __threadfence();
-                atomicAdd(P.bar + ph, 1u);
-            }
+            if (tid == 0)  // release: the CTA's writes (ordered before it by the barrier) first
+                asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(P.bar + ph) : "memory");
         }
         T.mark(5);
     }
