@@ -177,24 +177,23 @@ FDEV void pk_fetch_phase(PPhase *dst, const PPhase *src, int lane) {
 
 // mbarrier wait that suspends the thread (up to hint_ns) instead of spinning, so
 // a waiting thread takes no issue slots from the warps that share its scheduler.
-FDEV bool mbar_try_wait_hint(uint64_t *bar, uint32_t parity, uint32_t hint_ns) {
-    uint32_t ok;
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
-        : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
-        : "memory");
-    return ok != 0;
-}
-
 constexpr unsigned long long PK_WAIT_NS = 2000000000ull;  // a ring wait gives up after 2 s
 
 // Bounded mbarrier wait (time-limited) that also gives up when another thread
 // has aborted.
+FDEV bool pk_mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
 FDEV bool pk_mbar_wait(uint64_t *bar, uint32_t parity) {
     const unsigned long long t0 = gtimer();
     for (;;) {
-        if (mbar_try_wait_hint(bar, parity, 20000)) return true;
+        if (pk_mbar_try_wait(bar, parity)) return true;
         if (pk_abort || gtimer() - t0 > PK_WAIT_NS) return false;
     }
 }
