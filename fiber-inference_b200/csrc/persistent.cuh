@@ -148,6 +148,10 @@ FDEV void cbar() { asm volatile("bar.sync 1, %0;" ::"n"(PK_CONSUMERS) : "memory"
 FDEV void mbar_arrive(uint64_t *bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
+// n arrivals at once (a ring slot's empty barrier expects one per consumer warp)
+FDEV void mbar_arrive_n(uint64_t *bar, uint32_t n) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(n) : "memory");
+}
 
 FDEV int tile_bytes_of(const PSeg &s, int nmat) { return nmat * TC_M * s.stride; }
 
@@ -191,6 +195,7 @@ FDEV bool pk_mbar_try_wait(uint64_t *bar, uint32_t parity) {
     return ok != 0;
 }
 FDEV bool pk_mbar_wait(uint64_t *bar, uint32_t parity) {
+    if (pk_mbar_try_wait(bar, parity)) return true;  // usual case: no timer read
     const unsigned long long t0 = gtimer();
     for (;;) {
         if (pk_mbar_try_wait(bar, parity)) return true;
@@ -234,7 +239,7 @@ FDEV const uint8_t *ring_acquire(const PParams &P, int seq, long long &wfull) {
 }
 FDEV void ring_release(int seq) {
     cbar();
-    if (threadIdx.x == 0) mbar_arrive(&pk_empty[seq % PK_NDESC]);
+    if (threadIdx.x == 0) mbar_arrive_n(&pk_empty[seq % PK_NDESC], PK_WARPS);  // for all eight warps
 }
 
 // Wait until every CTA has finished phase ph - 1 (all consumer threads; thread 0
@@ -353,22 +358,31 @@ FDEV void pk_dot(const uint8_t *buf, int stride, const uint2 *xf, int nb) {
 
 // ---- attention -----------------------------------------------------------------------
 
-// One query head h of the attention phase, on one CTA: RoPE of q and of the new
-// position's k; the CTA holding query head g*G (g = h's KV head) appends the new
-// K/V row (fp16) to the cache; the KV head's pages come through the ring (the
-// producer prefetched them, in page order) and warp w takes pages w, w+8, ...,
-// combining its pages online (max, sum, o); the eight warp results are merged in
-// shared memory in warp order and the head's output is written as Wo's input
-// fragments (elements h*hd .. h*hd + hd - 1). Scores use fp32 FMAs over fp16 K
-// (lanes over positions, each lane starting at a rotated word so the reads of
-// the dense page are free of bank conflicts). Returns false when the step stopped.
+// One query head h of the attention phase, on one CTA. Threads 0..HD/2-1 rotate
+// q and the new position's k (RoPE), the next HD threads round the new v row, at
+// the same time; the CTA holding query head g*G (g = h's KV head) appends the new
+// K/V row (fp16) to the cache. The KV head's pages come through the ring (the
+// producer prefetched them, in page order) and every warp works on every page:
+// warp w takes the page's positions 8w .. 8w+7, four lanes per position, each
+// lane a quarter of the head dims (q in registers; K words read in a per-lane
+// rotated order, so the 32 lanes read 32 distinct banks), then the softmax
+// weights of those positions and their P.V (lane = head dims lane, lane + 32, ..),
+// combined online across pages (max, sum, o). A page's ring slot is free when all
+// eight warps have arrived on its empty barrier. The position being decoded is
+// taken from the fresh rows (nk, nv), not from the page copy, which may predate
+// the append. The eight warp results are merged in shared memory in warp order and
+// the head's output is written as Wo's input fragments (elements h*hd .. h*hd +
+// hd - 1). Returns false when the step stopped.
 template <int HD, int G>
 FDEV bool pk_attn_head(const PParams &P, const PPhase &F, int h, int pos, int nch, int &seq, long long &wfull,
                        unsigned long long *tr) {
     const long long c0 = clock64();
     constexpr int PG = ATTN_P;
-    constexpr int W = HD / 2;    // 32-bit words of a K/V row
-    constexpr int DPL = HD / 32;  // head dims per lane in P.V
+    constexpr int W = HD / 2;          // 32-bit words of a K/V row
+    constexpr int DPL = HD / 32;       // head dims per lane in P.V
+    constexpr int PW = PG / PK_WARPS;  // positions of a page per warp
+    constexpr int QW = W / 4;          // K words per lane (a quarter of the row)
+    static_assert(PW == 8 && (QW == 8 || QW == 16), "eight warps, head_dim 64 or 128");
     const AttnParams &a = P.attn;
     uint8_t *sm = reinterpret_cast<uint8_t *>(pk_xf(P));
     float *qs = reinterpret_cast<float *>(sm);                       // [HD] rotated q
@@ -377,18 +391,17 @@ FDEV bool pk_attn_head(const PParams &P, const PPhase &F, int h, int pos, int nc
     float *wm = reinterpret_cast<float *>(sm + HD * 4 + HD * 4);     // [PK_WARPS][HD + 2] warp results
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int g = h / G, seqlen = pos + 1, tn = pos - (nch - 1) * PG;
-    const float2 *rp = a.rope + (size_t)pos * (HD / 2);
-    const float *qh = a.qkv + (size_t)h * HD;
-    const float *kr = a.qkv + (size_t)a.n_heads * HD + (size_t)g * HD;
-    const float *vr = kr + (size_t)a.n_kv * HD;
     const bool writer = h % G == 0;  // appends the new K/V row of KV head g
     const size_t base = (((size_t)a.page_table[nch - 1] * a.n_layers + F.layer) * a.n_kv + g) * (size_t)PG * HD;
-    for (int j = tid; j < HD / 2; j += PK_CONSUMERS) {
-        const float2 cs = __ldg(rp + j);
+    if (tid < HD / 2) {
+        const int j = tid;
+        const float2 cs = __ldg(a.rope + (size_t)pos * (HD / 2) + j);
+        const float *qh = a.qkv + (size_t)h * HD;
+        const float *kr = a.qkv + (size_t)a.n_heads * HD + (size_t)g * HD;
         const float x1 = __ldcg(qh + j), x2 = __ldcg(qh + j + HD / 2);
+        const float k1 = __ldcg(kr + j), k2 = __ldcg(kr + j + HD / 2);
         qs[j] = __fsub_rn(__fmul_rn(x1, cs.x), __fmul_rn(x2, cs.y));
         qs[j + HD / 2] = __fadd_rn(__fmul_rn(x1, cs.y), __fmul_rn(x2, cs.x));
-        const float k1 = __ldcg(kr + j), k2 = __ldcg(kr + j + HD / 2);
         const uint16_t y1 = __half_as_ushort(__float2half_rn(__fsub_rn(__fmul_rn(k1, cs.x), __fmul_rn(k2, cs.y))));
         const uint16_t y2 = __half_as_ushort(__float2half_rn(__fadd_rn(__fmul_rn(k1, cs.y), __fmul_rn(k2, cs.x))));
         nk[j] = y1;
@@ -397,8 +410,9 @@ FDEV bool pk_attn_head(const PParams &P, const PPhase &F, int h, int pos, int nc
             a.k_pool[base + (size_t)tn * HD + j] = y1;
             a.k_pool[base + (size_t)tn * HD + j + HD / 2] = y2;
         }
-    }
-    for (int j = tid; j < HD; j += PK_CONSUMERS) {
+    } else if (tid < HD / 2 + HD) {
+        const int j = tid - HD / 2;
+        const float *vr = a.qkv + (size_t)a.n_heads * HD + (size_t)(a.n_kv + g) * HD;
         const uint16_t h16 = __half_as_ushort(__float2half_rn(__ldcg(vr + j)));
         nv[j] = h16;
         if (writer) a.v_pool[base + (size_t)tn * HD + j] = h16;
@@ -406,11 +420,22 @@ FDEV bool pk_attn_head(const PParams &P, const PPhase &F, int h, int pos, int nc
     cbar();  // qs, nk, nv ready
     const long long c1 = clock64();
 
+    // lane roles: position pi of the warp's eight, quarter qq of the head dims
+    const int pi = lane >> 2, qq = lane & 3;
+    const int rot = QW == 8 ? pi : 2 * pi + (qq >> 1);  // word rotation (bank = qq*QW + rotated word, mod 32)
+    float qr[2 * QW];
+#pragma unroll
+    for (int i = 0; i < QW; i++) {
+        const float2 v = *reinterpret_cast<const float2 *>(qs + qq * 2 * QW + 2 * ((i + rot) & (QW - 1)));
+        qr[2 * i] = v.x;
+        qr[2 * i + 1] = v.y;
+    }
+    const int tw = warp * PW;  // this warp's first position in a page
     float m_run = -INFINITY, l_run = 0.f, o_run[DPL];
 #pragma unroll
     for (int j = 0; j < DPL; j++) o_run[j] = 0.f;
     bool stopped = false;
-    for (int pg = warp; pg < nch; pg += PK_WARPS) {
+    for (int pg = 0; pg < nch; pg++) {
         const long long sq = seq + pg;
         const int d = (int)(sq % PK_NDESC);
         int got = 1;
@@ -428,78 +453,66 @@ FDEV bool pk_attn_head(const PParams &P, const PPhase &F, int h, int pos, int nc
             break;
         }
         const uint8_t *tile = pk_ring() + pk_tile_off[d];
-        const uint32_t *kw = reinterpret_cast<const uint32_t *>(tile);
-        uint16_t *vpg = reinterpret_cast<uint16_t *>(const_cast<uint8_t *>(tile)) + PG * HD;
-        const int t0 = pg * PG, nt = min(PG, seqlen - t0);
+        const int nt = min(PG, seqlen - pg * PG);  // valid positions of the page
         const bool last = pg == nch - 1;
-        if (last) {  // the page holding pos: the new V row replaces the copy's (stale) row
-            for (int j = lane; j < W; j += 32)
-                reinterpret_cast<uint32_t *>(vpg + (size_t)tn * HD)[j] = reinterpret_cast<const uint32_t *>(nv)[j];
-            __syncwarp();
-        }
-        // scores of positions lane and lane + 32
-        float sc2[2];
+        const int t = tw + pi;
+        // score of position t: this lane's quarter, then the four quarters
+        float d0 = 0.f, d1 = 0.f;
+        if (t < nt) {
+            const uint32_t *krow = ((last && t == tn) ? reinterpret_cast<const uint32_t *>(nk)
+                                                      : reinterpret_cast<const uint32_t *>(tile) + (size_t)t * W) +
+                                   qq * QW;
 #pragma unroll
-        for (int k = 0; k < 2; k++) {
-            const int t = lane + 32 * k;
-            const uint32_t *row = (last && t == tn) ? reinterpret_cast<const uint32_t *>(nk) : kw + (size_t)t * W;
-            float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;
-            if (t < nt) {
-#pragma unroll 8
-                for (int w2 = 0; w2 < W; w2 += 2) {
-                    const int wa = (w2 + lane) % W, wb = (w2 + 1 + lane) % W;
-                    const float2 ka = __half22float2(*reinterpret_cast<const __half2 *>(row + wa));
-                    const float2 kb = __half22float2(*reinterpret_cast<const __half2 *>(row + wb));
-                    const float2 qa = *reinterpret_cast<const float2 *>(qs + 2 * wa);
-                    const float2 qb = *reinterpret_cast<const float2 *>(qs + 2 * wb);
-                    d0 = fmaf(qa.x, ka.x, d0);
-                    d1 = fmaf(qa.y, ka.y, d1);
-                    d2 = fmaf(qb.x, kb.x, d2);
-                    d3 = fmaf(qb.y, kb.y, d3);
+            for (int i = 0; i < QW; i++) {
+                const float2 kf = __half22float2(*reinterpret_cast<const __half2 *>(krow + ((i + rot) & (QW - 1))));
+                d0 = fmaf(qr[2 * i], kf.x, d0);
+                d1 = fmaf(qr[2 * i + 1], kf.y, d1);
+            }
+        }
+        float s = d0 + d1;
+        s += __shfl_xor_sync(0xffffffffu, s, 1);
+        s += __shfl_xor_sync(0xffffffffu, s, 2);
+        s = t < nt ? __fmul_rn(s, a.scale) : -INFINITY;
+        const int nvw = min(PW, nt - tw);  // valid positions of this warp (warp-uniform)
+        if (nvw > 0) {
+            float m = fmaxf(s, __shfl_xor_sync(0xffffffffu, s, 4));
+            m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 8));
+            m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 16));
+            const float M = fmaxf(m_run, m);
+            const float p = t < nt ? expf(s - M) : 0.f;
+            const float al = m_run == -INFINITY ? 0.f : expf(m_run - M);
+            // running sum per lane (this lane's position); the lanes are summed after the pages
+            l_run = fmaf(al, l_run, p);
+            const uint16_t *vpg = reinterpret_cast<const uint16_t *>(tile) + (size_t)PG * HD;
+            // P.V over the warp's positions: every row of the page copy is in bounds, so the
+            // loads are unconditional and invalid positions are zeroed by a select
+            float vv[PW][DPL], pw[PW];
+#pragma unroll
+            for (int u = 0; u < PW; u++) {
+                pw[u] = __shfl_sync(0xffffffffu, p, 4 * u);
+                const uint16_t *vrow = (last && tw + u == tn) ? nv : vpg + (size_t)(tw + u) * HD;
+#pragma unroll
+                for (int j = 0; j < DPL; j++) {
+                    const float v = __half2float(__ushort_as_half(vrow[lane + 32 * j]));
+                    vv[u][j] = u < nvw ? v : 0.f;
                 }
             }
-            sc2[k] = t < nt ? __fmul_rn((d0 + d1) + (d2 + d3), a.scale) : -INFINITY;
-        }
-        float m = fmaxf(sc2[0], sc2[1]);
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        const float e0 = lane < nt ? expf(sc2[0] - m) : 0.f;
-        const float e1 = lane + 32 < nt ? expf(sc2[1] - m) : 0.f;
-        float l = e0 + e1;
+            for (int j = 0; j < DPL; j++) {
+                float ov = 0.f;
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
-        float o1[DPL], o2[DPL];
-#pragma unroll
-        for (int j = 0; j < DPL; j++) o1[j] = o2[j] = 0.f;
-        const int n0 = min(nt, 32);
-        for (int t = 0; t < n0; t++) {
-            const float w = __shfl_sync(0xffffffffu, e0, t);
-#pragma unroll
-            for (int j = 0; j < DPL; j++)
-                o1[j] = fmaf(w, __half2float(__ushort_as_half(vpg[(size_t)t * HD + lane + 32 * j])), o1[j]);
-        }
-        for (int t = 32; t < nt; t++) {
-            const float w = __shfl_sync(0xffffffffu, e1, t - 32);
-#pragma unroll
-            for (int j = 0; j < DPL; j++)
-                o2[j] = fmaf(w, __half2float(__ushort_as_half(vpg[(size_t)t * HD + lane + 32 * j])), o2[j]);
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&pk_empty[d]);  // page consumed
-        if (pg == warp) {
-            m_run = m;
-            l_run = l;
-#pragma unroll
-            for (int j = 0; j < DPL; j++) o_run[j] = o1[j] + o2[j];
-        } else {
-            const float M = fmaxf(m_run, m);
-            const float al = expf(m_run - M), be = expf(m - M);
-            l_run = fmaf(al, l_run, be * l);
-#pragma unroll
-            for (int j = 0; j < DPL; j++) o_run[j] = fmaf(al, o_run[j], be * (o1[j] + o2[j]));
+                for (int u = 0; u < PW; u++) ov = fmaf(pw[u], vv[u][j], ov);
+                o_run[j] = fmaf(al, o_run[j], ov);
+            }
             m_run = M;
         }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&pk_empty[d]);  // this warp is done with the page
     }
+    // the warp's sum over its eight positions (lanes of one quarter; all quarters agree)
+    l_run += __shfl_xor_sync(0xffffffffu, l_run, 4);
+    l_run += __shfl_xor_sync(0xffffffffu, l_run, 8);
+    l_run += __shfl_xor_sync(0xffffffffu, l_run, 16);
     // warp results -> shared memory, merged in warp order (trace: 8 = q/k/v ready, 9 = page loop)
     float *wr = wm + warp * (HD + 2);
 #pragma unroll
@@ -524,7 +537,7 @@ FDEV bool pk_attn_head(const PParams &P, const PPhase &F, int h, int pos, int nc
 #pragma unroll
         for (int w = 0; w < PK_WARPS; w++) {
             const float mw = wm[w * (HD + 2)];
-            if (mw == -INFINITY) continue;  // a warp without pages
+            if (mw == -INFINITY) continue;  // a warp without positions
             const float e = expf(mw - M);
             L = fmaf(e, wm[w * (HD + 2) + 1], L);
             O = fmaf(e, wm[w * (HD + 2) + 2 + dd], O);
@@ -892,7 +905,7 @@ __global__ void __launch_bounds__(PK_THREADS, 1) decode_persistent_kernel(const 
     if (tid == 0) {
         for (int d = 0; d < PK_NDESC; d++) {
             mbar_init(&pk_full[d], 1);
-            mbar_init(&pk_empty[d], 1);
+            mbar_init(&pk_empty[d], PK_WARPS);  // one arrival per consumer warp
         }
         mbar_fence_init();
         pk_abort = 0;
