@@ -93,9 +93,9 @@ class Clocks:
                 "samples": len(sm)}
 
 
-# DRAM traffic of one decode_persistent_kernel launch from an ncu capture (prefill step at
-# position 5): dram__bytes_read.sum + dram__bytes_write.sum, and that launch's algorithmic bytes.
-PK_CAPTURE = {"dram_bytes": 635_117_056 + 4_474_368, "algorithmic_bytes": 633_500_000, "position": 5}
+# DRAM traffic of one decode_persistent_kernel launch from an ncu capture (decode step at
+# position 13): dram__bytes_read.sum + dram__bytes_write.sum, and that launch's algorithmic bytes.
+PK_CAPTURE = {"dram_bytes": 635_233_536 + 6_902_784, "algorithmic_bytes": 633_700_000, "position": 13}
 
 
 def traffic_of(mode: int, roof: dict) -> dict:
