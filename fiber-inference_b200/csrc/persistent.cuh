@@ -807,9 +807,13 @@ __device__ __noinline__ void pk_producer(const PParams &P, int pos, int nch) {
     long long seq = 0, oldest = 0, pwait = 0;
     auto reserve = [&](int size, int &d) -> uint8_t * {
         int skip;
+        bool wrap;
         for (;;) {
             if (seq == oldest) head = 0;  // ring empty: restart at the front
-            skip = head + size > P.ring_bytes ? P.ring_bytes - head : 0;
+            // a tile that does not fit before the end starts at the front; the bytes up to
+            // the end (none when the last tile ended exactly there) are charged to it
+            wrap = head + size > P.ring_bytes;
+            skip = wrap ? P.ring_bytes - head : 0;
             if (seq - oldest < PK_NDESC && used + skip + size <= P.ring_bytes) break;
             const int od = (int)(oldest % PK_NDESC);
             const long long w0 = clock64();
@@ -823,7 +827,7 @@ __device__ __noinline__ void pk_producer(const PParams &P, int pos, int nch) {
             used -= need[od];
             oldest++;
         }
-        if (skip) head = 0;
+        if (wrap) head = 0;  // also when skip is 0: head == ring_bytes is past the ring
         uint8_t *dst = ring + head;
         head += size;
         d = (int)(seq % PK_NDESC);
