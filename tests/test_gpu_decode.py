@@ -202,3 +202,23 @@ def test_persistent_and_per_phase_kernels_agree(tiny_model, name):
     ga, _ = a.decode_greedy(ka, 3, len(toks), 60)
     gb, _ = b.decode_greedy(kb, 3, len(toks), 60)
     assert ga.tolist() == gb.tolist()
+
+
+@pytest.mark.parametrize("ring_kb", [64, 96])
+def test_ring_filled_exactly_by_attention_pages(tiny_model, monkeypatch, ring_kb):
+    """A weight/KV ring whose size is a multiple of the attention page pair (head_dim
+    128: 32 KB of K and V per page), so a tile can end exactly at the ring's end and
+    the next one must start again at the front. Positions up to 199 need up to four
+    pages per head, more than such a ring holds at once."""
+    monkeypatch.setenv("FIBER_PK_RING_KB", str(ring_kb))
+    path = tiny_model("q6k")
+    hm = fb.HostModel(path)
+    a = _ctx(hm, 256, 0)
+    b = _ctx(hm, 256, 1)
+    ka, kb = a.kv(256), b.kv(256)
+    toks = _prompt(hm.params.vocab_size, 200, 11)
+    for pos, t in enumerate(toks):
+        ia, la = a.forward(ka, int(t), pos)
+        ib, lb = b.forward(kb, int(t), pos)
+        assert np.abs(la - lb).max() <= 1e-4 * (np.abs(lb).max() + 1), pos
+        assert ia == ib, pos
