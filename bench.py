@@ -523,8 +523,9 @@ def main():
     ap.add_argument("--prompt-len", type=int, default=PROMPT_LEN, help="shorter runs for profiling only")
     ap.add_argument("--decode-len", type=int, default=DECODE_LEN, help="shorter runs for profiling only")
     ap.add_argument("--skip-extras", action="store_true", help="no single-GEMV, e2e or CPU legs (profiling)")
-    ap.add_argument("--step-mode", type=int, default=None, choices=[0, 1],
-                    help="0: one persistent kernel per token (default when the model fits it); 1: one kernel per phase")
+    ap.add_argument("--step-mode", type=int, default=None, choices=[0, 1, 2],
+                    help="0: grid-barrier persistent kernel per token; 1: one kernel per phase; "
+                         "2: dataflow kernel per token")
     ap.add_argument("--batch", type=int, default=1,
                     help="sequences per step for q5km-long / 7b-tp (>1: batched decode, one replica per rank)")
     ap.add_argument("--workload", default="1.1b", choices=["1.1b", "7b-tp", "stories", "q5km-long", "prefill"],
@@ -636,10 +637,11 @@ def main():
         kern["lm_head"]["bytes_per_launch"] + kern["embed"]["bytes_per_launch"]
     launches = ctx.step_launches() * D * args.steps
     mode = ctx.mode
-    if mode == 0:
+    if mode in (0, 2):
         # one cooperative kernel per token: the step kernel is the dominant (only) kernel
         us_tok = ms_total * 1e3 / (args.steps * D)
-        roof = {"kernel": "decode_persistent_kernel (one launch per token)", "achieved": step_bytes / us_tok / 1e3,
+        kname = "decode_flow_kernel" if mode == 2 else "decode_persistent_kernel"
+        roof = {"kernel": f"{kname} (one launch per token)", "achieved": step_bytes / us_tok / 1e3,
                 "algorithmic_bytes_per_launch": step_bytes, "us_per_launch": us_tok,
                 "timing": "CUDA events on the decode stream around the timed steps"}
     else:
@@ -658,7 +660,8 @@ def main():
                    "prompt": P, "decode_tokens_per_step": D, "global_batch": 1,
                    "parallelism": f"replicas x{world}", "l2": "inputs larger than L2 (633 MB weights/token)",
                    "deterministic_tokens": deterministic, "prefill_tok_s": prefill_tps,
-                   "step_mode": "persistent kernel per token" if mode == 0 else "one kernel per phase"},
+                   "step_mode": {0: "persistent kernel per token", 1: "one kernel per phase",
+                                 2: "dataflow kernel per token"}[mode]},
         "roofline": dict(roof, bound="hbm", peak=peak, unit="GB/s", frac=roof["achieved"] / peak,
                          peak_source=peak_kind, **traffic_of(mode, roof)),
         "decode_roofline": {"bytes_per_token": step_bytes, "achieved_gbs": step_bytes * value / world / 1e9,

@@ -32,6 +32,7 @@
 #include "gemv_tc.cuh"
 #include "launch.cuh"
 #include "persistent.cuh"
+#include "flow.cuh"
 #include "gemm_tc5.cuh"
 #include "prefill.cuh"
 #include "sample.cuh"
@@ -382,6 +383,17 @@ struct gpu_context {
     int pk_ring = 0, pk_xfr = 0, pk_xs = 0, pk_nw = 0, pk_grid = 0;
     size_t pk_smem = 0;
     void *pk_kernel = nullptr;
+    // dataflow one-kernel step (flow.cuh)
+    bool fl_ok = false;               // the model fits the dataflow kernel
+    FPhase *d_fphases = nullptr;
+    std::vector<FPhase> fphases;
+    uint64_t *fl_words = nullptr;     // tagged words of every phase output of one step
+    unsigned int *fl_sync = nullptr;  // [0] launch tag, [1] exit count, [2] argmax ticket, [4..) attention tickets
+    float *fl_att_part = nullptr;     // attention split states
+    unsigned long long *fl_am = nullptr;  // per-CTA argmax keys
+    int fl_ring = 0, fl_frag = 0, fl_xres = 0, fl_xin = 0, fl_nw = 0, fl_grid = 0, fl_max_split = 0;
+    size_t fl_smem = 0;
+    void *fl_kernel = nullptr;
     // tensor parallelism: this rank's share of query heads, KV heads and FFN blocks
     // (the whole model when tp_world == 1)
     int tp_rank = 0, tp_world = 1;
@@ -441,6 +453,7 @@ extern "C" void fiber_cuda_free(fiber_ctx_t *c) {
     for (void *q : c->pf_pad) cudaFree(q);
     void *dev[] = {c->pf_x2, c->smp_rng, c->smp_out, c->att_ws, c->att_tickets, c->bt_pos, c->bt_arg, c->bt_rec, c->bt_step, c->bt_logits, c->pf_x, c->pf_qkv, c->pf_att, c->pf_hg, c->pf_hu, c->pf_bp, c->pf_tok, c->x2, c->d_shard, c->d_data, c->x, c->qkv, c->att, c->h, c->logits, c->rope, c->io, c->rec,
                    c->att_part, c->att_cnt, c->am_part, c->am_cnt, c->d_phases, c->d_bar,
+                   c->d_fphases, c->fl_words, c->fl_sync, c->fl_att_part, c->fl_am,
                    c->pk_gf[0], c->pk_gf[1], c->pk_gf[2], c->pk_gf[3], c->pk_ss[0], c->pk_ss[1]};
     for (void *p : dev)
         if (p) cudaFree(p);
@@ -646,6 +659,174 @@ static int pk_build(gpu_context *c) {
     return FIBER_OK;
 }
 
+template <int HD, int G>
+static void *fl_kernel_ptr() {
+    return reinterpret_cast<void *>(decode_flow_kernel<HD, G>);
+}
+
+// Phase table, tagged-word buffers and launch geometry of the dataflow step kernel;
+// leaves fl_ok false when the model does not fit it.
+static int flow_build(gpu_context *c) {
+    const model_params_t &p = c->p;
+    const int dim = p.dim, ffn = p.ffn_dim, kvd = c->kvd, hd = p.head_dim, L = (int)p.n_layers;
+    c->fl_ok = false;
+    bool types_ok = tc_type_ok(c->t_out);
+    for (const LayerDev &d : c->L) {
+        const int ts[7] = {d.tq, d.tk, d.tv, d.to, d.t1, d.t2, d.t3};
+        for (int t : ts) types_ok = types_ok && tc_type_ok(t);
+        int distinct = 1 + (d.tk != d.tq) + (d.tv != d.tq && d.tv != d.tk);
+        types_ok = types_ok && distinct <= 2;
+    }
+    int scratch = 0;
+#define FL_CASE(H, GG)                                         \
+    if (hd == H && c->G == GG) {                               \
+        c->fl_kernel = fl_kernel_ptr<H, GG>();                 \
+        scratch = FlowAttn<H, GG>::SCRATCH_FLOATS;             \
+    }
+    FL_CASE(64, 1) FL_CASE(64, 2) FL_CASE(64, 4) FL_CASE(64, 8)
+    FL_CASE(128, 1) FL_CASE(128, 2) FL_CASE(128, 4) FL_CASE(128, 8)
+#undef FL_CASE
+    if (!types_ok || !c->fl_kernel) return FIBER_OK;
+    int sms = 0;
+    CK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, c->device));
+    const int grid = sms;
+
+    // tagged words: per layer x (input of QKV), q|k|v, attention, x after Wo, h; then the final x
+    const size_t per_layer = (size_t)dim + (dim + 2 * kvd) + dim + dim + ffn;
+    const size_t n_words = per_layer * L + dim;
+    CK(cudaMalloc(&c->fl_words, n_words * 8));
+    CK(cudaMemset(c->fl_words, 0, n_words * 8));  // tag 0: never a launch's tag
+    auto xw = [&](int l) { return c->fl_words + per_layer * l; };
+    auto qkvw = [&](int l) { return xw(l) + dim; };
+    auto attw = [&](int l) { return qkvw(l) + dim + 2 * kvd; };
+    auto x1w = [&](int l) { return attw(l) + dim; };
+    auto hw = [&](int l) { return x1w(l) + dim; };
+    auto xnext = [&](int l) { return l + 1 < L ? xw(l + 1) : c->fl_words + per_layer * L; };
+
+    std::vector<FPhase> &ph = c->fphases;
+    ph.clear();
+    auto base = [&](int kind, int cols, int layer) {
+        FPhase f;
+        memset(&f, 0, sizeof(f));
+        f.kind = kind;
+        f.cols = cols;
+        f.layer = layer;
+        f.nmat = 1;
+        f.eps = p.rms_norm_eps;
+        return f;
+    };
+    auto tiles_of = [](FPhase &f) {
+        f.n_tiles = 0;
+        for (int k = 0; k < f.nseg; k++) f.n_tiles += f.seg[k].tiles;
+    };
+    for (int l = 0; l < L; l++) {
+        const LayerDev &d = c->L[l];
+        FPhase q = base(FL_QKV, dim, l);
+        q.nseg = 3;
+        q.seg[0] = make_pseg(d.wq, nullptr, d.tq, dim, 0, dim);
+        q.seg[1] = make_pseg(d.wk, nullptr, d.tk, kvd, dim, dim);
+        q.seg[2] = make_pseg(d.wv, nullptr, d.tv, kvd, dim + kvd, dim);
+        q.embed_in = l == 0;
+        q.in = l == 0 ? nullptr : xw(l);
+        q.norm_w = d.attn_norm;
+        q.out = qkvw(l);
+        tiles_of(q);
+        FPhase a = base(FL_ATTN, dim, l);
+        a.in = qkvw(l);
+        a.out = attw(l);
+        FPhase o = base(FL_RESID, dim, l);
+        o.nseg = 1;
+        o.seg[0] = make_pseg(d.wo, nullptr, d.to, dim, 0, dim);
+        o.in = attw(l);
+        o.out = x1w(l);
+        tiles_of(o);
+        FPhase u = base(FL_SWIGLU, dim, l);
+        u.nseg = 1;
+        u.nmat = 2;
+        u.seg[0] = make_pseg(d.w1, d.w3, d.t1, ffn, 0, dim);
+        u.in = x1w(l);
+        u.norm_w = d.ffn_norm;
+        u.out = hw(l);
+        tiles_of(u);
+        FPhase dn = base(FL_RESID, ffn, l);
+        dn.nseg = 1;
+        dn.seg[0] = make_pseg(d.w2, nullptr, d.t2, dim, 0, ffn);
+        dn.in = hw(l);
+        dn.out = xnext(l);
+        tiles_of(dn);
+        // a norm phase keeps its fp32 input as the residual of the next residual phase
+        q.stage_ctas = std::min(grid, std::max(q.n_tiles, o.n_tiles));
+        o.stage_ctas = std::min(grid, o.n_tiles);
+        u.stage_ctas = std::min(grid, std::max(u.n_tiles, dn.n_tiles));
+        dn.stage_ctas = std::min(grid, dn.n_tiles);
+        ph.push_back(q);
+        ph.push_back(a);
+        ph.push_back(o);
+        ph.push_back(u);
+        ph.push_back(dn);
+    }
+    FPhase lm = base(FL_LM, dim, 0);
+    lm.nseg = 1;
+    lm.seg[0] = make_pseg(c->out, nullptr, c->t_out, p.vocab_size, 0, dim);
+    lm.in = xnext(L - 1);
+    lm.norm_w = c->out_norm;
+    lm.logits = c->logits;
+    tiles_of(lm);
+    lm.stage_ctas = std::min(grid, lm.n_tiles);
+    ph.push_back(lm);
+
+    // shared memory: fragments (one layout per weight type of a phase), the residual
+    // copy, the non-normed input (and attention scratch), the RMSNorm weights, the ring
+    size_t max_tile = (size_t)4 * ATTN_P * hd;  // attention: one K page and one V page (fp16)
+    int frag = 0;
+    for (FPhase &f : ph) {
+        if (f.kind == FL_ATTN) continue;
+        int types = 1;
+        for (int k = 0; k < f.nseg; k++) {
+            max_tile = std::max(max_tile, (size_t)f.nmat * TC_M * f.seg[k].stride);
+            if (f.seg[k].type != f.seg[0].type) types = 2;
+        }
+        frag = std::max(frag, types * f.cols * 4);
+    }
+    frag = (frag + 127) & ~127;
+    const int xres = (dim + 31) & ~31;
+    const int xin = (std::max(std::max(dim, ffn), scratch) + 31) & ~31;
+    const int nw = (dim + 31) & ~31;
+    cudaFuncAttributes fa;
+    CK(cudaFuncGetAttributes(&fa, c->fl_kernel));
+    int optin = 0;
+    CK(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, c->device));
+    const long long avail = (long long)optin - (long long)fa.sharedSizeBytes - frag - (long long)(xres + xin + nw) * 4 - 1024;
+    if (avail < (long long)max_tile) return FIBER_OK;  // tiles do not fit
+    c->fl_ring = (int)(avail & ~127ll);
+    if (const char *e = getenv("FIBER_FL_RING_KB")) {  // tuning knob: cap the ring (KB)
+        const long long cap = atoll(e) * 1024;
+        if (cap >= (long long)max_tile && cap < c->fl_ring) c->fl_ring = (int)(cap & ~127ll);
+    }
+    c->fl_frag = frag;
+    c->fl_xres = xres;
+    c->fl_xin = xin;
+    c->fl_nw = nw;
+    c->fl_smem = (size_t)c->fl_ring + frag + (size_t)(xres + xin + nw) * 4;
+    CK(cudaFuncSetAttribute(c->fl_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)c->fl_smem));
+    int per_sm = 0;
+    CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, c->fl_kernel, FL_THREADS, c->fl_smem));
+    if (per_sm < 1) return FIBER_OK;
+    c->fl_grid = grid;
+    c->fl_max_split = std::max(1, grid / (int)p.n_kv_heads);
+    CK(cudaMalloc(&c->fl_att_part, (size_t)p.n_kv_heads * c->fl_max_split * c->G * (hd + 2) * 4));
+    CK(cudaMalloc(&c->fl_am, (size_t)grid * 8));
+    const size_t n_sync = 4 + p.n_kv_heads;
+    CK(cudaMalloc(&c->fl_sync, n_sync * 4));
+    CK(cudaMemset(c->fl_sync, 0, n_sync * 4));
+    const unsigned int one = 1u;  // first launch tag
+    CK(cudaMemcpy(c->fl_sync, &one, 4, cudaMemcpyHostToDevice));
+    CK(cudaMalloc(&c->d_fphases, ph.size() * sizeof(FPhase)));
+    CK(cudaMemcpy(c->d_fphases, ph.data(), ph.size() * sizeof(FPhase), cudaMemcpyHostToDevice));
+    c->fl_ok = true;
+    return FIBER_OK;
+}
+
 static int tp_setup(gpu_context *c, const model_t *m, int rank, int world, const uint8_t *nccl_id);
 
 static int ctx_init(gpu_context *c, const model_t *m, int device, int max_seq, int rank, int world,
@@ -753,7 +934,8 @@ static int ctx_init(gpu_context *c, const model_t *m, int device, int max_seq, i
         c->mode = 1;  // sharded steps run the per-phase kernels with NCCL all-reduces
         return FIBER_OK;
     }
-    return pk_build(c);
+    if ((rc = pk_build(c)) != FIBER_OK) return rc;
+    return flow_build(c);
 }
 
 // ---- tensor parallelism ------------------------------------------------------------
@@ -1134,8 +1316,71 @@ static cudaError_t enqueue_persistent(gpu_context *c, const kv_cache_t *kv, bool
     return cudaLaunchKernelExC(&cfg, c->pk_kernel, args);
 }
 
+// Decode modes: 0 the grid-barrier persistent kernel, 1 one kernel per phase (CUDA
+// graph), 2 the dataflow kernel (tagged-word hand-off between phases).
+static bool use_flow(const gpu_context *c) { return c->mode == 2 && c->fl_ok; }
+static bool use_pk(const gpu_context *c) { return c->mode == 0 && c->pk_ok; }
+
+// Enqueue one decode step as one launch of the dataflow kernel (cooperative: all
+// CTAs co-resident, one per SM). No per-launch memset: every hand-off word carries
+// the launch tag, which the kernel advances when its last CTA exits.
+static cudaError_t enqueue_flow(gpu_context *c, const kv_cache_t *kv, bool loop, cudaStream_t st,
+                                unsigned long long *trace = nullptr) {
+    const model_params_t &p = c->p;
+    FParams P;
+    memset(&P, 0, sizeof(P));
+    P.phases = c->d_fphases;
+    P.n_phases = (int)c->fphases.size();
+    P.embd = c->embd;
+    P.embd_type = c->t_embd;
+    P.dim = p.dim;
+    P.vocab = p.vocab_size;
+    P.rope = c->rope;
+    P.k_pool = kv->k_pool;
+    P.v_pool = kv->v_pool;
+    P.page_table = kv->page_table;
+    P.n_layers = p.n_layers;
+    P.n_kv = c->nkv_l;
+    P.n_heads = c->nh_l;
+    P.max_seq = c->max_seq < kv->max_seq ? c->max_seq : kv->max_seq;
+    P.att_scale = 1.0f / sqrtf((float)p.head_dim);
+    P.att_max_split = c->fl_max_split;
+    P.att_part = c->fl_att_part;
+    P.att_tick = c->fl_sync + 4;
+    P.am_key = c->fl_am;
+    P.am_count = c->fl_sync + 2;
+    P.io_token = &c->io->token;
+    P.io_pos = &c->io->pos;
+    P.io_argmax = &c->io->argmax;
+    P.io_err = &c->io->err;
+    P.io_step = &c->io->step;
+    P.rec_tokens = c->rec;
+    P.loop = loop ? 1 : 0;
+    P.epoch = c->fl_sync;
+    P.exit_count = c->fl_sync + 1;
+    P.ring_bytes = c->fl_ring;
+    P.frag_bytes = c->fl_frag;
+    P.xres_floats = c->fl_xres;
+    P.xin_floats = c->fl_xin;
+    P.nw_floats = c->fl_nw;
+    P.trace = trace;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(c->fl_grid);
+    cfg.blockDim = dim3(FL_THREADS);
+    cfg.dynamicSmemBytes = c->fl_smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;  // all CTAs co-resident: consumers wait on other CTAs' words
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    void *args[] = {&P};
+    return cudaLaunchKernelExC(&cfg, c->fl_kernel, args);
+}
+
 static cudaError_t enqueue_step(gpu_context *c, const kv_cache_t *kv, bool loop, cudaStream_t st) {
-    if (c->mode == 0 && c->pk_ok) return enqueue_persistent(c, kv, loop, st);
+    if (use_flow(c)) return enqueue_flow(c, kv, loop, st);
+    if (use_pk(c)) return enqueue_persistent(c, kv, loop, st);
     cudaError_t e = enqueue_kind(c, kv, 6, 0, loop, st);
     for (uint32_t l = 0; l < c->p.n_layers && e == cudaSuccess; l++)
         for (int kind = 0; kind <= 4 && e == cudaSuccess; kind++) {
@@ -1182,7 +1427,12 @@ static int get_graph(gpu_context *c, const kv_cache_t *kv, bool loop, cudaGraphE
 // One decode step on the context stream: the persistent kernel is launched
 // directly (one memset + one kernel), the per-phase path replays its graph.
 static int run_step(gpu_context *c, const kv_cache_t *kv, bool loop) {
-    if (c->mode == 0 && c->pk_ok) {
+    if (use_flow(c)) {
+        cudaError_t e = enqueue_flow(c, kv, loop, c->stream);
+        if (e != cudaSuccess) return set_err(FIBER_ECUDA, "dataflow step launch: %s", cudaGetErrorString(e));
+        return FIBER_OK;
+    }
+    if (use_pk(c)) {
         cudaError_t e = enqueue_persistent(c, kv, loop, c->stream);
         if (e != cudaSuccess) return set_err(FIBER_ECUDA, "persistent step launch: %s", cudaGetErrorString(e));
         return FIBER_OK;
@@ -1208,12 +1458,14 @@ static int device_status(gpu_context *c) {
     if (c->h_io->err == 7)
         return set_err(FIBER_ETIMEOUT, "tensor-parallel all-reduce: a peer's data did not arrive in time");
     if (c->h_io->err == 5)
-        return set_err(FIBER_EUNSUPPORTED,
-                       "an activation exceeded the fp16 fragment range of the persistent kernel; use decode mode 1");
+        return set_err(FIBER_EUNSUPPORTED, use_flow(c) ? "a non-finite activation in the decode step"
+                                                       : "an activation exceeded the fp16 fragment range of the "
+                                                         "persistent kernel; use decode mode 1 or 2");
     if (c->h_io->err == 4) {
         // a bounded wait gave up mid-step: merge tickets may be left non-zero
         cudaMemset(c->att_cnt, 0, (size_t)c->p.n_kv_heads * sizeof(unsigned int));
         cudaMemset(c->am_cnt, 0, sizeof(unsigned int));
+        if (c->fl_sync) cudaMemset(c->fl_sync + 1, 0, (3 + c->p.n_kv_heads) * sizeof(unsigned int));
         cudaDeviceSynchronize();
         return set_err(FIBER_ETIMEOUT, "a device-side wait timed out during the decode step");
     }
@@ -1785,8 +2037,9 @@ extern "C" int fiber_decode_greedy_batch(fiber_ctx_t *c, kv_cache_t *kv, const i
 }
 
 extern "C" int fiber_set_decode_mode(fiber_ctx_t *c, int mode) {
-    if (!c || mode < 0 || mode > 1) return set_err(FIBER_EARG, "fiber_set_decode_mode: mode must be 0 or 1");
+    if (!c || mode < 0 || mode > 2) return set_err(FIBER_EARG, "fiber_set_decode_mode: mode must be 0, 1 or 2");
     if (mode == 0 && !c->pk_ok) return set_err(FIBER_EUNSUPPORTED, "the persistent step kernel does not fit this model");
+    if (mode == 2 && !c->fl_ok) return set_err(FIBER_EUNSUPPORTED, "the dataflow step kernel does not fit this model");
     if (c->mode != mode) {
         free_graph(c->g_step);
         free_graph(c->g_loop);
@@ -1797,12 +2050,12 @@ extern "C" int fiber_set_decode_mode(fiber_ctx_t *c, int mode) {
 
 extern "C" int fiber_get_decode_mode(fiber_ctx_t *c) {
     if (!c) return set_err(FIBER_EARG, "no context");
-    return (c->mode == 0 && c->pk_ok) ? 0 : 1;
+    return use_flow(c) ? 2 : use_pk(c) ? 0 : 1;
 }
 
 extern "C" int fiber_step_launches(fiber_ctx_t *c) {
     if (!c) return set_err(FIBER_EARG, "no context");
-    if (c->mode == 0 && c->pk_ok) return 1;
+    if (use_flow(c) || use_pk(c)) return 1;
     int n = 2;  // embed + lm_head
     for (const LayerDev &d : c->L) n += 4 + 1 + (d.tk != d.tq) + (d.tv != d.tk);
     return n;
@@ -1811,15 +2064,17 @@ extern "C" int fiber_step_launches(fiber_ctx_t *c) {
 extern "C" int fiber_trace_step(fiber_ctx_t *c, kv_cache_t *kv, int token, int pos, uint64_t *out, size_t cap,
                                 int *n_phases, int *n_ctas) {
     if (!c || !out || !n_phases || !n_ctas) return set_err(FIBER_EARG, "fiber_trace_step: null argument");
-    if (!c->pk_ok) return set_err(FIBER_EUNSUPPORTED, "the persistent step kernel does not cover this model");
+    const bool fl = use_flow(c);
+    if (!fl && !c->pk_ok) return set_err(FIBER_EUNSUPPORTED, "the persistent step kernels do not cover this model");
     int rc = check_kv(c, kv);
     if (rc) return rc;
     const int lim = c->max_seq < kv->max_seq ? c->max_seq : kv->max_seq;
     if (pos < 0 || pos >= lim) return set_err(FIBER_EARG, "position %d outside [0, %d)", pos, lim);
     if (token < 0 || token >= (int)c->p.vocab_size) return set_err(FIBER_EARG, "token %d out of range", token);
-    const size_t n = c->phases.size() * (size_t)c->pk_grid * PK_TRACE_FIELDS;
-    *n_phases = (int)c->phases.size();
-    *n_ctas = c->pk_grid;
+    const size_t n = fl ? c->fphases.size() * (size_t)c->fl_grid * FL_TRACE_FIELDS
+                        : c->phases.size() * (size_t)c->pk_grid * PK_TRACE_FIELDS;
+    *n_phases = (int)(fl ? c->fphases.size() : c->phases.size());
+    *n_ctas = fl ? c->fl_grid : c->pk_grid;
     if (cap < n) return set_err(FIBER_EARG, "trace buffer holds %zu values, %zu needed", cap, n);
     CK(cudaSetDevice(c->device));
     unsigned long long *d_tr = nullptr;
@@ -1829,7 +2084,7 @@ extern "C" int fiber_trace_step(fiber_ctx_t *c, kv_cache_t *kv, int token, int p
     c->h_io->pos = pos;
     c->h_io->err = 0;
     if (e == cudaSuccess) e = cudaMemcpyAsync(c->io, c->h_io, sizeof(StepIO), cudaMemcpyHostToDevice, c->stream);
-    if (e == cudaSuccess) e = enqueue_persistent(c, kv, false, c->stream, d_tr);
+    if (e == cudaSuccess) e = fl ? enqueue_flow(c, kv, false, c->stream, d_tr) : enqueue_persistent(c, kv, false, c->stream, d_tr);
     if (e == cudaSuccess) e = cudaMemcpyAsync(out, d_tr, n * 8, cudaMemcpyDeviceToHost, c->stream);
     if (e == cudaSuccess) e = cudaMemcpyAsync(c->h_io, c->io, sizeof(StepIO), cudaMemcpyDeviceToHost, c->stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
@@ -1913,7 +2168,7 @@ extern "C" int fiber_decode_greedy(fiber_ctx_t *c, kv_cache_t *kv, int32_t first
     c->h_io->err = 0;
     CK(cudaMemcpyAsync(c->io, c->h_io, sizeof(StepIO), cudaMemcpyHostToDevice, c->stream));
     {
-        if (!(c->mode == 0 && c->pk_ok)) {  // build the graph before the timed region
+        if (!use_flow(c) && !use_pk(c)) {  // build the graph before the timed region
             cudaGraphExec_t g;
             if ((rc = get_graph(c, kv, true, &g)) != FIBER_OK) return rc;
         }
@@ -2237,7 +2492,7 @@ extern "C" int fiber_decode_sample(fiber_ctx_t *c, kv_cache_t *kv, int32_t first
     c->h_io->err = 0;
     CK(cudaMemcpyAsync(c->io, c->h_io, sizeof(StepIO), cudaMemcpyHostToDevice, c->stream));
     CK(cudaMemcpyAsync(c->smp_rng, rng_state, sizeof(unsigned long long), cudaMemcpyHostToDevice, c->stream));
-    if (!(c->mode == 0 && c->pk_ok)) {  // build the step graph before the timed region
+    if (!use_flow(c) && !use_pk(c)) {  // build the step graph before the timed region
         cudaGraphExec_t g;
         if ((rc = get_graph(c, kv, false, &g)) != FIBER_OK) return rc;
     }

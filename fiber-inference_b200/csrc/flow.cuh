@@ -1,0 +1,906 @@
+// flow.cuh — one decode step as one cooperative kernel whose phases hand their
+// results to each other as tagged words instead of meeting at grid barriers.
+//
+// A phase's output vector (q|k|v, the attention output, the residual stream, the
+// SwiGLU activations) is written as 8-byte words (fp32 value in the low half, the
+// launch's tag in the high half) with single 64-bit stores; a consumer polls the
+// words it needs and takes each one as soon as it carries this launch's tag. So a
+// phase waits only for the data it reads (one L2 round trip after the last
+// producer's store), never for every CTA of the grid, and needs no separate
+// flag, fence or staging copy. Every output word of a step is written exactly
+// once per launch (one buffer per layer and kind), so a word can only be stale
+// from an earlier launch, whose tag differs.
+//
+// Per CTA (one per SM, all co-resident: cooperative launch):
+//   * warp 8, one lane (producer): streams this CTA's weight tiles of every phase,
+//     and the K/V pages of its attention unit, with cp.async.bulk into a byte ring
+//     in shared memory (FIFO, full/empty mbarrier pair per slot), in consumption
+//     order, so loading runs ahead across phases and waits;
+//   * warps 0..7 (consumers), per GEMV phase: poll the input words, RMSNorm them
+//     where the phase has one, scale by a power of two (keeps the fp16 hi/lo split
+//     in range for any activation size), write the MMA fragments; then per tile
+//     every warp decodes and multiplies its super-blocks (TcDot) and writes its
+//     partial sums; the last warp to finish a tile (shared-memory ticket) sums the
+//     eight partials, applies the epilogue (residual add, SwiGLU, logits + argmax
+//     candidate) and stores the output words — no CTA barrier per tile;
+//   * attention: one unit per (KV head, page split) with all query heads of the
+//     group, so K/V pages are read once per group; split states are merged in
+//     split order by the last unit to finish (ticket).
+// Every wait is bounded (%globaltimer); on timeout the kernel records error 4,
+// stops issuing work and returns once its own copies have landed.
+#pragma once
+#include "persistent.cuh"
+
+namespace fiber {
+
+constexpr int FL_WARPS = 8;
+constexpr int FL_CONSUMERS = FL_WARPS * 32;
+constexpr int FL_THREADS = FL_CONSUMERS + 32;  // + producer warp
+constexpr int FL_NDESC = 16;                   // ring slots
+constexpr unsigned long long FL_WAIT_NS = 2000000000ull;
+// Optional per-phase, per-CTA timeline (FParams::trace non-null), fields:
+//  0 globaltimer (ns) at the phase start   1 cycles polling the input words
+//  2 cycles RMSNorm + fragments            3 cycles from the tiles' start to the phase end
+//  4 cycles warp 0 waited for ring slots   5 globaltimer (ns) at the phase end
+//  6 producer: globaltimer after issuing the phase's last copy   7 producer: cycles waiting for ring space
+constexpr int FL_TRACE_FIELDS = 8;
+
+enum : int { FL_QKV = 0, FL_ATTN = 1, FL_RESID = 2, FL_SWIGLU = 3, FL_LM = 4 };
+
+struct __align__(16) FPhase {
+    int kind;
+    int nseg;
+    int nmat;        // 2 for SwiGLU (gate + up), else 1
+    int cols;        // input length
+    int layer;
+    int n_tiles;
+    int embed_in;    // layer 0 QKV: the input is the embedding row of the current token
+    int stage_ctas;  // CTAs below this stage the input (they have tiles here, or keep it for the next residual phase)
+    float eps;
+    int pad_;
+    const uint64_t *in;    // tagged input words (cols of them); null for the embedding input
+    const float *norm_w;   // RMSNorm weights of the input, or null
+    uint64_t *out;         // tagged output words (QKV: q|k|v, ATTN: attention, RESID: x, SWIGLU: h)
+    float *logits;         // LM: fp32 logits
+    PSeg seg[3];
+};
+static_assert(sizeof(FPhase) % 16 == 0 && sizeof(FPhase) / 16 <= 32, "phase descriptors are copied in 16-byte chunks");
+
+struct FParams {
+    const FPhase *phases;  // device array
+    int n_phases;
+    const uint8_t *embd;
+    int embd_type;
+    int dim, vocab;
+    // attention
+    const float2 *rope;          // [max_seq][hd/2] (cos, sin)
+    uint16_t *k_pool, *v_pool;   // fp16 bits, [page][layer][kv_head][P][hd]
+    const int32_t *page_table;
+    int n_layers, n_kv, n_heads, max_seq;
+    float att_scale;
+    int att_max_split;           // page splits per KV head at most
+    float *att_part;             // [n_kv][att_max_split][G][hd + 2] split states
+    unsigned int *att_tick;      // [n_kv] merge tickets, zero between launches
+    // greedy argmax and step state
+    unsigned long long *am_key;  // [gridDim.x] per-CTA best (value, index) keys
+    unsigned int *am_count;      // ticket, zero between launches
+    int32_t *io_token, *io_pos, *io_argmax, *io_err, *io_step;
+    int32_t *rec_tokens;
+    int loop;                    // 1: feed the argmax back as the next token, advance pos, record it
+    unsigned int *epoch;         // tag of the current launch (advanced by the last CTA to exit)
+    unsigned int *exit_count;
+    int ring_bytes, frag_bytes, xres_floats, xin_floats, nw_floats;
+    unsigned long long *trace;   // [n_phases][gridDim.x][FL_TRACE_FIELDS] or null
+};
+
+// ---- per-CTA state ----------------------------------------------------------------------
+// dynamic: [ring][fragments frag_bytes][xres xres_floats][xin xin_floats][norm weights nw_floats]
+extern __shared__ __align__(128) uint8_t fl_dyn[];
+__shared__ __align__(8) uint64_t fl_full[FL_NDESC];
+__shared__ __align__(8) uint64_t fl_empty[FL_NDESC];
+__shared__ __align__(16) FPhase fl_F[2];
+__shared__ __align__(16) float fl_red[FL_NDESC][FL_WARPS][2][TC_M];  // per ring slot: warp partial sums
+__shared__ unsigned int fl_redcnt[FL_NDESC];                          // warps done with the slot's tile
+__shared__ float fl_stat[2 * FL_WARPS];
+__shared__ unsigned long long fl_best;   // this CTA's best logit key
+__shared__ int fl_tile_off[FL_NDESC];
+__shared__ volatile int fl_abort;
+__shared__ unsigned int fl_ticket;
+__shared__ float fl_scale[2];            // staged input: fragment scale, its inverse
+
+FDEV uint8_t *fl_ring() { return fl_dyn; }
+FDEV uint2 *fl_frag(const FParams &P) { return reinterpret_cast<uint2 *>(fl_dyn + P.ring_bytes); }
+FDEV float *fl_xres(const FParams &P) { return reinterpret_cast<float *>(fl_dyn + P.ring_bytes + P.frag_bytes); }
+FDEV float *fl_xin(const FParams &P) { return fl_xres(P) + P.xres_floats; }
+FDEV float *fl_nw(const FParams &P) { return fl_xin(P) + P.xin_floats; }
+
+// ---- tagged words ----------------------------------------------------------------------
+
+FDEV uint64_t ll_word(float v, uint32_t tag) { return ((uint64_t)tag << 32) | __float_as_uint(v); }
+FDEV void ll_store(uint64_t *p, float v, uint32_t tag) {
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(ll_word(v, tag)) : "memory");
+}
+FDEV ulonglong2 ll_load2(const uint64_t *p) {
+    ulonglong2 r;
+    asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(r.x), "=l"(r.y) : "l"(p) : "memory");
+    return r;
+}
+
+FDEV void fl_fail(const FParams &P) {
+    fl_abort = 1;
+    *P.io_err = 4;
+}
+
+// Consumer barrier that also returns the OR of v over the 256 consumer threads, so
+// every thread takes the same branch after it (a stop decision never splits them).
+FDEV bool cbar_any(bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.or.pred q, 1, %2, p;\n selp.u32 %0, 1, 0, q;\n}\n"
+        : "=r"(r)
+        : "r"((uint32_t)v), "n"(FL_CONSUMERS)
+        : "memory");
+    return r != 0;
+}
+
+// Copy phase descriptor src into shared memory with 16-byte async copies (lanes of
+// one warp); complete after cp_async_wait_all + a barrier.
+FDEV void fl_fetch_phase(FPhase *dst, const FPhase *src, int lane) {
+    constexpr int CH = (int)(sizeof(FPhase) / 16);
+    if (lane < CH) cp_async16(reinterpret_cast<uint4 *>(dst) + lane, reinterpret_cast<const uint4 *>(src) + lane);
+}
+
+FDEV void fl_locate(const FPhase &F, int tile, int &s, int &lt) {
+    s = 0;
+    lt = tile;
+    while (s + 1 < F.nseg && lt >= F.seg[s].tiles) lt -= F.seg[s++].tiles;
+}
+
+// Poll n tagged words (n even, src 16-byte aligned) into dst[0..n) (shared memory).
+// All consumer threads; each issues up to eight 16-byte loads before it waits, then
+// reloads only the words without this launch's tag. Returns false on timeout.
+FDEV bool fl_poll(const FParams &P, const uint64_t *src, float *dst, int n, uint32_t tag) {
+    const int nch = n >> 1;
+    for (int base = threadIdx.x; base < nch; base += 8 * FL_CONSUMERS) {
+        ulonglong2 w[8];
+        uint32_t pend = 0;
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const int c = base + i * FL_CONSUMERS;
+            if (c < nch) {
+                w[i] = ll_load2(src + 2 * c);
+                pend |= 1u << i;
+            }
+        }
+        unsigned long long t0 = 0;
+        for (long long it = 0;; it++) {
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                if ((pend >> i) & 1u) {
+                    if ((uint32_t)(w[i].x >> 32) == tag && (uint32_t)(w[i].y >> 32) == tag) {
+                        const int c = base + i * FL_CONSUMERS;
+                        dst[2 * c] = __uint_as_float((uint32_t)w[i].x);
+                        dst[2 * c + 1] = __uint_as_float((uint32_t)w[i].y);
+                        pend &= ~(1u << i);
+                    }
+                }
+            }
+            if (!pend) break;
+            if (it == 0) {
+                t0 = gtimer();
+            } else if ((it & 15) == 0 && (fl_abort || gtimer() - t0 > FL_WAIT_NS)) {
+                fl_fail(P);
+                return false;
+            }
+#pragma unroll
+            for (int i = 0; i < 8; i++)
+                if ((pend >> i) & 1u) w[i] = ll_load2(src + 2 * (base + i * FL_CONSUMERS));
+        }
+    }
+    return true;
+}
+
+// Bounded wait on a ring slot by one lane.
+FDEV bool fl_mbar_wait(uint64_t *bar, uint32_t parity) {
+    if (pk_mbar_try_wait(bar, parity)) return true;
+    const unsigned long long t0 = gtimer();
+    for (;;) {
+        if (pk_mbar_try_wait(bar, parity)) return true;
+        if (fl_abort || gtimer() - t0 > FL_WAIT_NS) return false;
+    }
+}
+
+// Warp-level acquire of ring item `seq`: lane 0 waits, the warp agrees.
+FDEV const uint8_t *fl_acquire(const FParams &P, long long seq, long long &wcycles) {
+    const int d = (int)(seq % FL_NDESC);
+    int ok = 1;
+    if ((threadIdx.x & 31) == 0) {
+        const long long c0 = clock64();
+        ok = fl_mbar_wait(&fl_full[d], (uint32_t)((seq / FL_NDESC) & 1));
+        if (!ok) fl_fail(P);
+        wcycles += clock64() - c0;
+    }
+    ok = __shfl_sync(0xffffffffu, ok, 0);
+    return ok ? fl_ring() + fl_tile_off[d] : nullptr;
+}
+
+// Block-wide reduction over the consumer threads of two values (sum, max), fixed order.
+FDEV void fl_reduce2(float &sum, float &mx) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    }
+    if (lane == 0) {
+        fl_stat[warp] = sum;
+        fl_stat[FL_WARPS + warp] = mx;
+    }
+    cbar();
+    sum = 0.f;
+    mx = 0.f;
+#pragma unroll
+    for (int w = 0; w < FL_WARPS; w++) {
+        sum += fl_stat[w];
+        mx = fmaxf(mx, fl_stat[FL_WARPS + w]);
+    }
+    cbar();  // fl_stat reused
+}
+
+// Power-of-two scale that puts the largest staged magnitude m in [2^13, 2^14):
+// the fp16 hi part stays far below 65504 and the lo part stays normal.
+FDEV void fl_set_scale(float m, float &scale, float &inv) {
+    int eb = (int)((__float_as_uint(m) >> 23) & 0xFF);
+    eb = max(14, min(eb, 254));
+    scale = __uint_as_float((uint32_t)(267 - eb) << 23);
+    inv = __uint_as_float((uint32_t)(eb - 13) << 23);
+}
+
+template <int HD, int G>
+struct FlowAttn;
+
+// ---- GEMV phase -----------------------------------------------------------------------
+
+// Stage the phase input: poll (or decode the embedding row), RMSNorm scale, fragments
+// for each weight type of the phase. All consumer threads. Returns false when stopped.
+FDEV bool fl_stage(const FParams &P, const FPhase &F, uint32_t tag, int token, unsigned long long *tr) {
+    const int tid = threadIdx.x;
+    const int n = F.cols, nb = n >> 8;
+    const bool norm = F.norm_w != nullptr;
+    float *xs = norm ? fl_xres(P) : fl_xin(P);
+    float *nw = fl_nw(P);
+    long long c0 = clock64();
+    if (norm)
+        for (int i = tid; i < (n >> 2); i += FL_CONSUMERS) cp_async16(nw + 4 * i, F.norm_w + 4 * i);
+    if (F.embed_in) {  // every CTA decodes the embedding row itself (src/gpu_ffn.m:466-482)
+        int tok = token;
+        if (tok < 0 || tok >= P.vocab) {
+            if (tid == 0 && blockIdx.x == 0) *P.io_err = 2;
+            tok = 0;
+        }
+        for (int i = tid; i < n; i += FL_CONSUMERS) {
+            float v;
+            switch (P.embd_type) {
+            case T_F16: v = h2f(reinterpret_cast<const uint16_t *>(P.embd)[(size_t)tok * n + i]); break;
+            case T_F32: v = round_f16(reinterpret_cast<const float *>(P.embd)[(size_t)tok * n + i]); break;
+            case T_Q4_K: v = round_f16(decode_elem<T_Q4_K>(P.embd + ((size_t)tok * nb + (i >> 8)) * 144, i & 255)); break;
+            case T_Q5_K: v = round_f16(decode_elem<T_Q5_K>(P.embd + ((size_t)tok * nb + (i >> 8)) * 176, i & 255)); break;
+            default: v = round_f16(decode_elem<T_Q6_K>(P.embd + ((size_t)tok * nb + (i >> 8)) * 210, i & 255)); break;
+            }
+            xs[i] = v;
+        }
+    }
+    const bool ok = F.embed_in || fl_poll(P, F.in, xs, n, tag);
+    cp_async_wait_all();
+    if (cbar_any(!ok || fl_abort)) return false;
+    if (tr) tr[1] = (unsigned long long)(clock64() - c0);
+    c0 = clock64();
+    // sums of squares (RMSNorm) and the largest |x * w| (fragment scale)
+    float ss = 0.f, mx = 0.f;
+    for (int i = tid; i < n; i += FL_CONSUMERS) {
+        const float v = xs[i];
+        ss = fmaf(v, v, ss);
+        mx = fmaxf(mx, fabsf(norm ? v * nw[i] : v));
+    }
+    fl_reduce2(ss, mx);
+    const float rrms = norm ? 1.0f / sqrtf(ss / (float)n + F.eps) : 1.0f;
+    if (!(mx < 3.0e38f) || !(rrms < 3.0e38f)) {  // non-finite activations
+        if (tid == 0) *P.io_err = 5;
+        mx = 1.0f;
+    }
+    float scale, inv;
+    fl_set_scale(norm ? mx * rrms * 1.001f : mx, scale, inv);
+    if (tid == 0) {
+        fl_scale[0] = scale;
+        fl_scale[1] = inv;
+    }
+    int type_b = -1;
+    for (int k = 1; k < F.nseg; k++)
+        if (F.seg[k].type != F.seg[0].type && type_b < 0) type_b = F.seg[k].type;
+    uint2 *xf0 = fl_frag(P), *xf1 = xf0 + (size_t)nb * 128;
+    for (int pass = 0; pass < (type_b >= 0 ? 2 : 1); pass++) {
+        uint2 *dst = pass ? xf1 : xf0;
+        switch (pass ? type_b : F.seg[0].type) {
+        case T_Q4_K: pk_stage<T_Q4_K>(nb, xs, norm ? nw : nullptr, rrms, scale, dst); break;
+        case T_Q6_K: pk_stage<T_Q6_K>(nb, xs, norm ? nw : nullptr, rrms, scale, dst); break;
+        default: pk_stage<T_F16>(nb, xs, norm ? nw : nullptr, rrms, scale, dst); break;
+        }
+    }
+    cbar();
+    if (tr) tr[2] = (unsigned long long)(clock64() - c0);
+    return true;
+}
+
+// Order-preserving key of a logit: larger value first, then lower index; NaN below
+// everything (the reference's strict '>' never picks it), -0 as +0.
+FDEV unsigned long long fl_key(float v, int idx) {
+    uint32_t b = __float_as_uint(v + 0.0f);
+    b = (v != v) ? 0u : ((b & 0x80000000u) ? ~b : (b | 0x80000000u));
+    return ((unsigned long long)b << 32) | (0xFFFFFFFFu - (uint32_t)idx);
+}
+
+// Epilogue of one tile (the last warp to finish it): lanes 0..15 own its rows.
+FDEV void fl_epilogue(const FParams &P, const FPhase &F, const PSeg &S, int lt, int d, uint32_t tag) {
+    const int lane = threadIdx.x & 31;
+    if (lane < TC_M) {
+        const int r = lt * TC_M + lane;
+        float v0 = 0.f, v1 = 0.f;
+#pragma unroll
+        for (int w = 0; w < FL_WARPS; w++) v0 += fl_red[d][w][0][lane];
+        const float inv = fl_scale[1];
+        v0 *= inv;
+        if (F.nmat == 2) {
+#pragma unroll
+            for (int w = 0; w < FL_WARPS; w++) v1 += fl_red[d][w][1][lane];
+            v1 *= inv;
+        }
+        if (r < S.rows) {
+            switch (F.kind) {
+            case FL_QKV: ll_store(F.out + S.out_off + r, v0, tag); break;
+            case FL_RESID: ll_store(F.out + r, __fadd_rn(fl_xres(P)[r], v0), tag); break;
+            case FL_SWIGLU: {
+                const float h = __fmul_rn(__fdiv_rn(v0, __fadd_rn(1.0f, expf(-v0))), v1);
+                ll_store(F.out + r, h, tag);
+                break;
+            }
+            default:  // FL_LM
+                F.logits[r] = v0;
+                atomicMax(&fl_best, fl_key(v0, r));
+                break;
+            }
+        }
+    }
+}
+
+// One tile of the phase, warp-level: decode + multiply this warp's super-blocks,
+// publish the partial sums; the last of the eight warps runs the epilogue and only
+// then frees the ring slot (the slot's partial sums stay valid until it is refilled).
+template <int T, int NMAT>
+FDEV void fl_tile(const FParams &P, const FPhase &F, const PSeg &S, int lt, const uint8_t *buf, const uint2 *xf,
+                  int d, uint32_t tag) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    const int nb = F.cols >> 8;
+    float acc[NMAT][4];
+#pragma unroll
+    for (int m = 0; m < NMAT; m++)
+#pragma unroll
+        for (int i = 0; i < 4; i++) acc[m][i] = 0.f;
+    for (int b = warp; b < nb; b += FL_WARPS) {
+        const uint2 *xfb = xf + (size_t)b * 128;
+#pragma unroll
+        for (int m = 0; m < NMAT; m++) {
+            const uint8_t *mb = buf + (size_t)m * TC_M * S.stride + (size_t)b * TcType<T>::BB;
+            TcDot<T>::run(mb + (size_t)g * S.stride, mb + (size_t)(g + 8) * S.stride, xfb, g, t, acc[m]);
+        }
+    }
+    if (t == 0) {
+#pragma unroll
+        for (int m = 0; m < NMAT; m++) {
+            fl_red[d][warp][m][g] = acc[m][0] + acc[m][1];
+            fl_red[d][warp][m][g + 8] = acc[m][2] + acc[m][3];
+        }
+    }
+    __syncwarp();
+    unsigned int old = 0;
+    if (lane == 0) {
+        __threadfence_block();
+        old = atomicAdd(&fl_redcnt[d], 1u);
+    }
+    old = __shfl_sync(0xffffffffu, old, 0);
+    if (old == FL_WARPS - 1) {
+        __threadfence_block();
+        fl_epilogue(P, F, S, lt, d, tag);
+        if (lane == 0) fl_redcnt[d] = 0u;
+        __syncwarp();
+    }
+    if (lane == 0) mbar_arrive(&fl_empty[d]);
+}
+
+// The CTA's tiles of one GEMV phase (tile = blockIdx.x + k * gridDim.x), warp-level.
+FDEV bool fl_tiles(const FParams &P, const FPhase &F, long long &seq, uint32_t tag, long long &wcycles) {
+    const int nb = F.cols >> 8;
+    const uint2 *xf0 = fl_frag(P), *xf1 = xf0 + (size_t)nb * 128;
+    for (int tile = blockIdx.x; tile < F.n_tiles; tile += gridDim.x) {
+        int sidx, lt;
+        fl_locate(F, tile, sidx, lt);
+        const PSeg &S = F.seg[sidx];
+        const uint8_t *buf = fl_acquire(P, seq, wcycles);
+        if (!buf) return false;
+        const int d = (int)(seq % FL_NDESC);
+        const uint2 *xf = (S.type == F.seg[0].type) ? xf0 : xf1;
+        if (F.nmat == 2) {
+            switch (S.type) {
+            case T_Q4_K: fl_tile<T_Q4_K, 2>(P, F, S, lt, buf, xf, d, tag); break;
+            case T_Q6_K: fl_tile<T_Q6_K, 2>(P, F, S, lt, buf, xf, d, tag); break;
+            default: fl_tile<T_F16, 2>(P, F, S, lt, buf, xf, d, tag); break;
+            }
+        } else {
+            switch (S.type) {
+            case T_Q4_K: fl_tile<T_Q4_K, 1>(P, F, S, lt, buf, xf, d, tag); break;
+            case T_Q6_K: fl_tile<T_Q6_K, 1>(P, F, S, lt, buf, xf, d, tag); break;
+            default: fl_tile<T_F16, 1>(P, F, S, lt, buf, xf, d, tag); break;
+            }
+        }
+        seq++;
+    }
+    return true;
+}
+
+// ---- attention ------------------------------------------------------------------------
+
+// Units of the attention phase at position pos: n_kv * S, S page splits per KV head
+// (at most one per page, at most att_max_split); unit u = g * S + j runs on CTA
+// gridDim.x - 1 - u, pages [j * nch / S, (j + 1) * nch / S).
+FDEV int fl_att_splits(const FParams &P, int nch) { return max(1, min(nch, P.att_max_split)); }
+
+template <int HD, int G>
+struct FlowAttn {
+    static constexpr int PG = ATTN_P;
+    static constexpr int WPH = FL_WARPS / G;          // warps per query head
+    static constexpr int PW = PG / WPH;               // positions of a page per warp
+    static constexpr int LPP = PW >= 32 ? 1 : 32 / PW;  // lanes per position
+    static constexpr int PPL = PW >= 32 ? PW / 32 : 1;  // positions per lane
+    static constexpr int W = HD / 2;                  // 32-bit words of a K/V row
+    static constexpr int WS = W / LPP;                // words of a row per lane (its slice)
+    static constexpr int DPL = HD / 32;               // head dims per lane in P.V
+    static_assert(G == 1 || G == 2 || G == 4 || G == 8, "query heads per KV head");
+    static_assert(HD == 64 || HD == 128, "head_dim 64 or 128");
+
+    // shared scratch (in the xin region): q [G][HD] fp32, nk/nv [HD] fp16, warp states [8][HD + 2],
+    // the polled q | k | v [(G + 2) * HD]
+    static constexpr int SCRATCH_FLOATS = G * HD + HD + FL_WARPS * (HD + 2) + (G + 2) * HD;
+
+    // rotated word index of a lane's slice (the lanes of a warp hit 32 distinct banks)
+    static FDEV int rot(int lane) {
+        const int pi = lane / LPP, qq = lane % LPP;
+        if (WS >= 32) return lane;
+        return HD == 128 ? 2 * pi + (qq >> 1) : pi;
+    }
+
+    static FDEV bool unit(const FParams &P, const FPhase &F, int g, int j, int S, int pos, int nch, long long &seq,
+                          uint32_t tag, long long &wcycles) {
+        const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+        float *sm = fl_xin(P);
+        float *qs = sm;                                             // [G][HD]
+        uint16_t *nk = reinterpret_cast<uint16_t *>(sm + G * HD);   // [HD]
+        uint16_t *nv = nk + HD;                                     // [HD]
+        float *wm = sm + G * HD + HD;                               // [FL_WARPS][HD + 2]
+        float *raw = wm + FL_WARPS * (HD + 2);                      // [(G + 2) * HD] q | k | v as polled
+        const uint64_t *qkv = F.in;
+        const int q0 = g * G * HD, k0 = P.n_heads * HD + g * HD, v0 = (P.n_heads + P.n_kv) * HD + g * HD;
+        bool got = fl_poll(P, qkv + q0, raw, G * HD, tag);
+        got = got && fl_poll(P, qkv + k0, raw + G * HD, HD, tag);
+        got = got && fl_poll(P, qkv + v0, raw + G * HD + HD, HD, tag);
+        if (cbar_any(!got || fl_abort)) return false;
+        const int tn = pos - (nch - 1) * PG;  // row of the new position in the last page
+        const bool writer = j == S - 1;       // the unit holding the last page appends the new K/V row
+        const size_t base = (((size_t)P.page_table[nch - 1] * P.n_layers + F.layer) * P.n_kv + g) * (size_t)PG * HD;
+        const float2 *rp = P.rope + (size_t)pos * (HD / 2);
+        for (int i = tid; i < (G + 1) * (HD / 2); i += FL_CONSUMERS) {  // RoPE (src/fiber_proof.m:30-51)
+            const int h = i / (HD / 2), jj = i % (HD / 2);
+            const float2 cs = __ldg(rp + jj);
+            const float x1 = raw[h * HD + jj], x2 = raw[h * HD + jj + HD / 2];
+            const float y1 = __fsub_rn(__fmul_rn(x1, cs.x), __fmul_rn(x2, cs.y));
+            const float y2 = __fadd_rn(__fmul_rn(x1, cs.y), __fmul_rn(x2, cs.x));
+            if (h < G) {
+                qs[h * HD + jj] = y1;
+                qs[h * HD + jj + HD / 2] = y2;
+            } else {
+                const uint16_t b1 = __half_as_ushort(__float2half_rn(y1)), b2 = __half_as_ushort(__float2half_rn(y2));
+                nk[jj] = b1;
+                nk[jj + HD / 2] = b2;
+                if (writer) {
+                    P.k_pool[base + (size_t)tn * HD + jj] = b1;
+                    P.k_pool[base + (size_t)tn * HD + jj + HD / 2] = b2;
+                }
+            }
+        }
+        for (int i = tid; i < HD; i += FL_CONSUMERS) {
+            const uint16_t b = __half_as_ushort(__float2half_rn(raw[G * HD + HD + i]));
+            nv[i] = b;
+            if (writer) P.v_pool[base + (size_t)tn * HD + i] = b;
+        }
+        cbar();
+
+        // this warp: query head hw of the group, positions [ws * PW, ws * PW + PW) of every page
+        const int hw = warp / WPH, ws = warp % WPH;
+        const int pi = lane / LPP, qq = lane % LPP, r = rot(lane);
+        const float *qh = qs + hw * HD + qq * (2 * WS);
+        float m_run = -INFINITY, l_run = 0.f, o_run[DPL];
+#pragma unroll
+        for (int k = 0; k < DPL; k++) o_run[k] = 0.f;
+        const int p0 = (int)((long long)j * nch / S), p1 = (int)((long long)(j + 1) * nch / S);
+        bool ok = true;
+        for (int pg = p0; pg < p1; pg++) {
+            const uint8_t *tile = fl_acquire(P, seq, wcycles);
+            if (!tile) {
+                ok = false;
+                break;
+            }
+            const int d = (int)(seq % FL_NDESC);
+            seq++;
+            const bool last = pg == nch - 1;
+            const int nt = last ? tn + 1 : PG;  // valid positions of the page
+            const uint32_t *kp = reinterpret_cast<const uint32_t *>(tile);
+            const uint16_t *vp = reinterpret_cast<const uint16_t *>(tile) + (size_t)PG * HD;
+            float s[PPL];
+#pragma unroll
+            for (int e = 0; e < PPL; e++) {
+                const int t = ws * PW + pi + 32 * e;
+                const uint32_t *krow = (last && t == tn) ? reinterpret_cast<const uint32_t *>(nk) + qq * WS
+                                                         : kp + (size_t)t * W + qq * WS;
+                float d0 = 0.f, d1 = 0.f;
+#pragma unroll 8
+                for (int i = 0; i < WS; i++) {
+                    const int wi = (i + r) & (WS - 1);
+                    const float2 kf = __half22float2(*reinterpret_cast<const __half2 *>(krow + wi));
+                    const float2 qf = *reinterpret_cast<const float2 *>(qh + 2 * wi);
+                    d0 = fmaf(qf.x, kf.x, d0);
+                    d1 = fmaf(qf.y, kf.y, d1);
+                }
+                float v = d0 + d1;
+                if (LPP >= 2) v += __shfl_xor_sync(0xffffffffu, v, 1);
+                if (LPP >= 4) v += __shfl_xor_sync(0xffffffffu, v, 2);
+                s[e] = t < nt ? __fmul_rn(v, P.att_scale) : -INFINITY;
+            }
+            // page maximum over the warp's positions, running max
+            float m = s[0];
+#pragma unroll
+            for (int e = 1; e < PPL; e++) m = fmaxf(m, s[e]);
+#pragma unroll
+            for (int o = LPP; o < 32; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+            const float M = fmaxf(m_run, m);
+            if (M != -INFINITY) {
+                const float al = m_run == -INFINITY ? 0.f : expf(m_run - M);
+                float p[PPL], psum = 0.f;
+#pragma unroll
+                for (int e = 0; e < PPL; e++) {
+                    p[e] = s[e] == -INFINITY ? 0.f : expf(s[e] - M);
+                    psum += p[e];
+                }
+                l_run = fmaf(al, l_run, qq == 0 ? psum : 0.f);  // one lane per position counts it
+#pragma unroll
+                for (int k = 0; k < DPL; k++) o_run[k] *= al;
+                // P.V over the warp's positions; lane owns dims 2*lane + {0,1} (+64 for HD 128)
+                constexpr int PU = PW < 32 ? PW : 32;  // positions per lane slot
+#pragma unroll
+                for (int e = 0; e < PPL; e++) {
+#pragma unroll 8
+                    for (int u2 = 0; u2 < PU; u2++) {
+                        const float pu = __shfl_sync(0xffffffffu, p[e], u2 * LPP);
+                        const int t = ws * PW + 32 * e + u2;
+                        const uint32_t *vrow = (last && t == tn) ? reinterpret_cast<const uint32_t *>(nv)
+                                                                 : reinterpret_cast<const uint32_t *>(vp + (size_t)t * HD);
+#pragma unroll
+                        for (int k = 0; k < DPL / 2; k++) {
+                            const float2 vf = __half22float2(*reinterpret_cast<const __half2 *>(vrow + lane + 32 * k));
+                            o_run[2 * k] = fmaf(pu, vf.x, o_run[2 * k]);
+                            o_run[2 * k + 1] = fmaf(pu, vf.y, o_run[2 * k + 1]);
+                        }
+                    }
+                }
+                m_run = M;
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&fl_empty[d]);
+        }
+        // warp totals -> shared memory
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) l_run += __shfl_xor_sync(0xffffffffu, l_run, o);
+        float *wr = wm + warp * (HD + 2);
+#pragma unroll
+        for (int k = 0; k < DPL / 2; k++) {
+            wr[2 + 2 * (lane + 32 * k)] = o_run[2 * k];
+            wr[2 + 2 * (lane + 32 * k) + 1] = o_run[2 * k + 1];
+        }
+        if (lane == 0) {
+            wr[0] = m_run;
+            wr[1] = l_run;
+        }
+        if (cbar_any(!ok || fl_abort)) return false;
+        // merge the WPH warps of each head (warp order); then finish or publish the split state
+        float *part = P.att_part + ((size_t)g * P.att_max_split + j) * G * (HD + 2);
+        for (int i = tid; i < G * (HD + 2); i += FL_CONSUMERS) {
+            const int h = i / (HD + 2), e = i % (HD + 2);
+            float M = -INFINITY;
+#pragma unroll
+            for (int w = 0; w < WPH; w++) M = fmaxf(M, wm[(h * WPH + w) * (HD + 2)]);
+            float acc = 0.f;
+            if (e == 0) {
+                acc = M;
+            } else {
+#pragma unroll
+                for (int w = 0; w < WPH; w++) {
+                    const float mw = wm[(h * WPH + w) * (HD + 2)];
+                    if (mw == -INFINITY) continue;
+                    acc = fmaf(expf(mw - M), wm[(h * WPH + w) * (HD + 2) + e], acc);
+                }
+            }
+            if (S == 1) {
+                if (e >= 2) {
+                    const float L = [&] {
+                        float l = 0.f;
+#pragma unroll
+                        for (int w = 0; w < WPH; w++) {
+                            const float mw = wm[(h * WPH + w) * (HD + 2)];
+                            if (mw != -INFINITY) l = fmaf(expf(mw - M), wm[(h * WPH + w) * (HD + 2) + 1], l);
+                        }
+                        return l;
+                    }();
+                    ll_store(F.out + (size_t)(g * G + h) * HD + (e - 2), acc / L, tag);
+                }
+            } else {
+                part[i] = acc;
+            }
+        }
+        if (S == 1) return true;
+        cbar();
+        if (tid == 0) {
+            __threadfence();
+            fl_ticket = atomicAdd(P.att_tick + g, 1u);
+        }
+        cbar();
+        if (fl_ticket != (unsigned int)(S - 1)) return true;
+        // last split of this KV head: merge the S states in split order
+        __threadfence();
+        if (tid == 0) atomicExch(P.att_tick + g, 0u);
+        const float *pg0 = P.att_part + (size_t)g * P.att_max_split * G * (HD + 2);
+        for (int i = tid; i < G * HD; i += FL_CONSUMERS) {
+            const int h = i / HD, e = i % HD;
+            float M = -INFINITY;
+            for (int jj = 0; jj < S; jj++) M = fmaxf(M, __ldcg(pg0 + ((size_t)jj * G + h) * (HD + 2)));
+            float L = 0.f, O = 0.f;
+            for (int jj = 0; jj < S; jj++) {
+                const float *st = pg0 + ((size_t)jj * G + h) * (HD + 2);
+                const float mj = __ldcg(st);
+                if (mj == -INFINITY) continue;
+                const float f = expf(mj - M);
+                L = fmaf(f, __ldcg(st + 1), L);
+                O = fmaf(f, __ldcg(st + 2 + e), O);
+            }
+            ll_store(F.out + (size_t)(g * G + h) * HD + e, O / L, tag);
+        }
+        return true;
+    }
+};
+
+// ---- argmax, exit -------------------------------------------------------------------------
+
+// After the lm_head phase: publish this CTA's best key; the last CTA reduces all of
+// them, writes the token and (loop mode) advances the step state.
+FDEV void fl_argmax_finish(const FParams &P) {
+    const int tid = threadIdx.x, lane = tid & 31;
+    cbar();  // every epilogue of this CTA is done
+    if (tid == 0) {
+        P.am_key[blockIdx.x] = fl_best;
+        __threadfence();
+        fl_ticket = atomicAdd(P.am_count, 1u);
+    }
+    cbar();
+    if (fl_ticket != gridDim.x - 1) return;
+    __threadfence();
+    if (tid < 32) {
+        unsigned long long best = 0ull;
+        for (int i = lane; i < (int)gridDim.x; i += 32) best = max(best, __ldcg(P.am_key + i));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) best = max(best, __shfl_xor_sync(0xffffffffu, best, o));
+        if (lane == 0) {
+            const int bi = (int)(0xFFFFFFFFu - (uint32_t)(best & 0xFFFFFFFFu));
+            *P.io_argmax = bi;
+            if (P.loop) {
+                *P.io_token = bi;
+                *P.io_pos = *P.io_pos + 1;
+                const int st = *P.io_step;
+                P.rec_tokens[st] = bi;
+                *P.io_step = st + 1;
+            }
+            *P.am_count = 0u;
+        }
+    }
+}
+
+// ---- producer ---------------------------------------------------------------------------
+
+template <int HD>
+__device__ __noinline__ void fl_producer(const FParams &P, int pos, int nch, int S) {
+    uint8_t *ring = fl_ring();
+    int head = 0, used = 0, need[FL_NDESC];
+    long long seq = 0, oldest = 0, pwait = 0;
+    auto reserve = [&](int size, int &d) -> uint8_t * {
+        int skip;
+        bool wrap;
+        for (;;) {
+            if (seq == oldest) head = 0;  // ring empty: restart at the front
+            // a tile that does not fit before the end starts at the front; the bytes up to
+            // the end (none when the last tile ended exactly there) are charged to it
+            wrap = head + size > P.ring_bytes;
+            skip = wrap ? P.ring_bytes - head : 0;
+            if (seq - oldest < FL_NDESC && used + skip + size <= P.ring_bytes) break;
+            const int od = (int)(oldest % FL_NDESC);
+            const long long w0 = clock64();
+            const bool got = fl_mbar_wait(&fl_empty[od], (uint32_t)((oldest / FL_NDESC) & 1));
+            pwait += clock64() - w0;
+            if (!got) {
+                fl_fail(P);
+                return nullptr;
+            }
+            used -= need[od];
+            oldest++;
+        }
+        if (wrap) head = 0;
+        uint8_t *dst = ring + head;
+        head += size;
+        d = (int)(seq % FL_NDESC);
+        need[d] = skip + size;
+        used += skip + size;
+        fl_tile_off[d] = (int)(dst - ring);
+        return dst;
+    };
+    const int units = P.n_kv * S;
+    const int u = (int)gridDim.x - 1 - (int)blockIdx.x;  // this CTA's attention unit, if u < units
+    for (int ph = 0; ph < P.n_phases && !fl_abort; ph++) {
+        const FPhase &F = P.phases[ph];
+        pwait = 0;
+        if (F.kind == FL_ATTN) {
+            constexpr uint32_t PAGE = ATTN_P * HD * 2;
+            if (nch > 0 && u < units) {
+                const int g = u / S, j = u % S;
+                const int p0 = (int)((long long)j * nch / S), p1 = (int)((long long)(j + 1) * nch / S);
+                for (int pg = p0; pg < p1 && !fl_abort; pg++) {
+                    int d;
+                    uint8_t *dst = reserve(2 * PAGE, d);
+                    if (!dst) break;
+                    const size_t base =
+                        (((size_t)P.page_table[pg] * P.n_layers + F.layer) * P.n_kv + g) * (size_t)ATTN_P * HD;
+                    mbar_expect_tx(&fl_full[d], 2 * PAGE);
+                    bulk_g2s(dst, P.k_pool + base, PAGE, &fl_full[d]);
+                    bulk_g2s(dst + PAGE, P.v_pool + base, PAGE, &fl_full[d]);
+                    seq++;
+                }
+            }
+        } else {
+            for (int tile = blockIdx.x; tile < F.n_tiles && !fl_abort; tile += gridDim.x) {
+                int s, lt;
+                fl_locate(F, tile, s, lt);
+                const PSeg &Sg = F.seg[s];
+                int d;
+                uint8_t *dst = reserve(tile_bytes_of(Sg, F.nmat), d);
+                if (!dst) break;
+                // plain-copied tail first, then the arrive (release), then the bulk copies
+                const int r0 = lt * TC_M, nrows = min(TC_M, Sg.rows - r0);
+                const uint32_t mat_bytes = (uint32_t)nrows * Sg.row_bytes;
+                const uint32_t main_bytes = Sg.per_row ? mat_bytes : (mat_bytes & ~15u);
+                for (int m = 0; m < F.nmat; m++) {
+                    const uint8_t *src = (m == 0 ? Sg.w : Sg.w2) + (size_t)r0 * Sg.row_bytes;
+                    uint8_t *mdst = dst + (size_t)m * TC_M * Sg.stride;
+                    for (uint32_t k = main_bytes; k < mat_bytes; k++) mdst[k] = src[k];
+                }
+                mbar_expect_tx(&fl_full[d], main_bytes * F.nmat);
+                for (int m = 0; m < F.nmat; m++) {
+                    const uint8_t *src = (m == 0 ? Sg.w : Sg.w2) + (size_t)r0 * Sg.row_bytes;
+                    uint8_t *mdst = dst + (size_t)m * TC_M * Sg.stride;
+                    if (Sg.per_row) {
+                        for (int r = 0; r < nrows; r++)
+                            bulk_g2s(mdst + (size_t)r * Sg.stride, src + (size_t)r * Sg.row_bytes, Sg.row_bytes,
+                                     &fl_full[d]);
+                    } else if (main_bytes) {
+                        bulk_g2s(mdst, src, main_bytes, &fl_full[d]);
+                    }
+                }
+                seq++;
+            }
+        }
+        if (P.trace) {
+            unsigned long long *tr = P.trace + ((size_t)ph * gridDim.x + blockIdx.x) * FL_TRACE_FIELDS;
+            tr[6] = gtimer();
+            tr[7] = (unsigned long long)pwait;
+        }
+    }
+    // copies still in flight land before the CTA exits: the consumers wait on every
+    // item; after an abort, wait (bounded) here for the issued ones
+    if (fl_abort)
+        for (long long k = oldest; k < seq; k++) mbar_wait(&fl_full[k % FL_NDESC], (uint32_t)((k / FL_NDESC) & 1));
+}
+
+// ---- the kernel -------------------------------------------------------------------------
+
+template <int HD, int G>
+__global__ void __launch_bounds__(FL_THREADS, 1) decode_flow_kernel(const __grid_constant__ FParams P) {
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (tid == 0) {
+        for (int d = 0; d < FL_NDESC; d++) {
+            mbar_init(&fl_full[d], 1);
+            mbar_init(&fl_empty[d], FL_WARPS);  // one arrival per consumer warp
+            fl_redcnt[d] = 0u;
+        }
+        mbar_fence_init();
+        fl_abort = 0;
+        fl_best = 0ull;
+    }
+    if (warp == 0) fl_fetch_phase(&fl_F[0], P.phases, lane);
+    cp_async_wait_all();
+    const uint32_t tag = *(volatile unsigned int *)P.epoch;
+    const int pos = *P.io_pos;
+    const int token0 = *P.io_token;
+    __syncthreads();  // the only full-CTA barrier
+
+    const bool pos_ok = pos >= 0 && pos < P.max_seq;
+    const int nch = pos_ok ? pos / ATTN_P + 1 : 0;
+    const int S = fl_att_splits(P, nch);
+    if (!pos_ok && tid == 0 && blockIdx.x == 0) *P.io_err = 1;
+
+    if (!pos_ok) {
+        // nothing to decode (the host checks positions before launching; this is the
+        // device-side guard): every phase is skipped, the tag still advances
+    } else if (warp == FL_WARPS) {
+        if (lane == 0) fl_producer<HD>(P, pos, nch, S);
+    } else {
+        long long seq = 0;
+        const int units = P.n_kv * S;
+        const int u = (int)gridDim.x - 1 - (int)blockIdx.x;
+        for (int ph = 0; ph < P.n_phases; ph++) {
+            const FPhase &F = fl_F[ph & 1];
+            unsigned long long *tr = (P.trace && tid == 0)
+                                         ? P.trace + ((size_t)ph * gridDim.x + blockIdx.x) * FL_TRACE_FIELDS
+                                         : nullptr;
+            long long wcycles = 0;
+            // every warp is past the previous phase (its epilogues included): the
+            // descriptor buffer of phase ph + 1 and the staging areas are free
+            if (cbar_any(fl_abort)) break;
+            if (warp == 0 && ph + 1 < P.n_phases) fl_fetch_phase(&fl_F[(ph + 1) & 1], P.phases + ph + 1, lane);
+            if (tr) tr[0] = gtimer();
+            const long long c0 = clock64();
+            bool ok = true;
+            if (F.kind == FL_ATTN) {
+                if (nch > 0 && u < units) ok = FlowAttn<HD, G>::unit(P, F, u / S, u % S, S, pos, nch, seq, tag, wcycles);
+            } else if ((int)blockIdx.x < F.stage_ctas) {
+                ok = fl_stage(P, F, tag, token0, tr);
+                if (ok) {
+                    ok = fl_tiles(P, F, seq, tag, wcycles);
+                    ok = !cbar_any(!ok || fl_abort);  // all warps past their tiles (epilogues done)
+                }
+            }
+            if (ok && F.kind == FL_LM) fl_argmax_finish(P);
+            cp_async_wait_all();
+            if (tr) {
+                tr[3] = (unsigned long long)(clock64() - c0);
+                tr[4] = (unsigned long long)wcycles;
+                tr[5] = gtimer();
+            }
+            if (!ok) break;
+        }
+        cp_async_wait_all();
+    }
+    // the last CTA to exit advances the launch tag (also after an abort, so the next
+    // launch never mistakes this launch's words for its own)
+    __syncthreads();
+    if (tid == 0) {
+        __threadfence();
+        if (atomicAdd(P.exit_count, 1u) == gridDim.x - 1) {
+            *P.exit_count = 0u;
+            *P.epoch = tag + 1u;
+        }
+    }
+}
+
+}  // namespace fiber

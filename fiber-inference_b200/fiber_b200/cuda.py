@@ -323,7 +323,8 @@ class Context:
         return out, float(ms.value), int(st.value)
 
     def set_mode(self, mode: int):
-        """0: persistent one-kernel step (default when supported); 1: one kernel per phase."""
+        """0: grid-barrier persistent one-kernel step; 1: one kernel per phase;
+        2: dataflow one-kernel step (tagged-word hand-off between phases)."""
         _check(cuda_lib().fiber_set_decode_mode(self.h, int(mode)), "fiber_set_decode_mode")
 
     def set_prefill_mode(self, mode: int):
@@ -348,10 +349,14 @@ class Context:
     TRACE_FIELDS = ["t_release_ns", "cyc_barrier", "cyc_stage", "cyc_tiles", "cyc_wait_tiles", "cyc_arrive",
                     "t_producer_done_ns", "cyc_producer_wait", "cyc_attn_qkv", "cyc_attn_pages"]
 
+    FLOW_TRACE_FIELDS = ["t_start_ns", "cyc_poll", "cyc_stage", "cyc_phase", "cyc_wait_ring", "t_end_ns",
+                         "t_producer_done_ns", "cyc_producer_wait"]
+
     def trace_step(self, kv: KVCache, token: int, pos: int, max_phases: int = 4096, max_ctas: int = 1024):
-        """Per-phase, per-CTA timeline of one persistent step: uint64 array
-        [n_phases, n_ctas, len(TRACE_FIELDS)] with the fields of TRACE_FIELDS."""
-        nf = len(self.TRACE_FIELDS)
+        """Per-phase, per-CTA timeline of one one-kernel step: uint64 array
+        [n_phases, n_ctas, n_fields] with the fields of TRACE_FIELDS (mode 0) or
+        FLOW_TRACE_FIELDS (mode 2)."""
+        nf = len(self.FLOW_TRACE_FIELDS if self.mode == 2 else self.TRACE_FIELDS)
         buf = np.zeros(max_phases * max_ctas * nf, np.uint64)
         nph, nct = C.c_int(), C.c_int()
         _check(cuda_lib().fiber_trace_step(self.h, kv.addr, int(token), int(pos), buf.ctypes.data, buf.size,

@@ -22,10 +22,13 @@ def _rel_rms(a, b):
 
 
 def _ctx(hm, max_seq, mode):
+    """Context in decode mode `mode` (0 grid-barrier persistent kernel, 1 one kernel per
+    phase, 2 dataflow kernel); skips when that kernel does not cover the model."""
     ctx = fb.Context(hm, max_seq=max_seq)
-    if mode == 0 and ctx.mode != 0:
-        pytest.skip("the persistent step kernel does not cover this model")
-    ctx.set_mode(mode)
+    try:
+        ctx.set_mode(mode)
+    except fb.FiberError:
+        pytest.skip(f"decode mode {mode} does not cover this model")
     return ctx
 
 
@@ -34,7 +37,7 @@ def _prompt(vocab, n, seed):
     return rng.integers(1, vocab, n).astype(np.int32)
 
 
-@pytest.mark.parametrize("mode", [0, 1])
+@pytest.mark.parametrize("mode", [0, 1, 2])
 @pytest.mark.parametrize("name", ["q4km", "q5km", "f16", "q6k", "gqa8", "hd128"])
 def test_teacher_forced_logits(tiny_model, name, mode):
     path = tiny_model(name)
@@ -52,7 +55,7 @@ def test_teacher_forced_logits(tiny_model, name, mode):
         assert am == int(np.argmax(lg))
 
 
-@pytest.mark.parametrize("mode", [0, 1])
+@pytest.mark.parametrize("mode", [0, 1, 2])
 @pytest.mark.parametrize("name", ["q4km", "q5km", "f16", "gqa8"])
 def test_greedy_tokens_match_oracle(tiny_model, name, mode):
     path = tiny_model(name)
@@ -70,7 +73,7 @@ def test_greedy_tokens_match_oracle(tiny_model, name, mode):
     assert dev.tolist() == want[1:].tolist()
 
 
-@pytest.mark.parametrize("mode", [0, 1])
+@pytest.mark.parametrize("mode", [0, 1, 2])
 def test_device_loop_equals_host_loop(tiny_model, mode):
     path = tiny_model("gqa8")
     hm = fb.HostModel(path)
@@ -113,7 +116,7 @@ def test_kv_cache_contents_match_oracle(tiny_model):
             assert np.abs(v[pos] - ov).max() <= 2e-3 * (np.abs(ov).max() + 1e-3)
 
 
-@pytest.mark.parametrize("mode", [0, 1])
+@pytest.mark.parametrize("mode", [0, 1, 2])
 def test_prefilled_long_context(tiny_model, mode):
     """Long context over many KV pages: cache pre-filled with seeded N(0,1)
     keys/values (as in the long-context workload), then greedy decode."""
@@ -184,13 +187,14 @@ def test_errors_are_reported_not_faulted(tiny_model):
     assert 0 <= am < hm.params.vocab_size
 
 
+@pytest.mark.parametrize("mode", [0, 2])
 @pytest.mark.parametrize("name", ["q4km", "f16", "gqa8", "hd128", "q6k"])
-def test_persistent_and_per_phase_kernels_agree(tiny_model, name):
-    """Both ways of running a step compute the same arithmetic per row; the
-    token sequences must match and the logits agree to fp32 reordering noise."""
+def test_persistent_and_per_phase_kernels_agree(tiny_model, name, mode):
+    """The one-kernel steps and the per-phase kernels compute the same arithmetic per
+    row; the token sequences must match and the logits agree to fp32 reordering noise."""
     path = tiny_model(name)
     hm = fb.HostModel(path)
-    a = _ctx(hm, 256, 0)
+    a = _ctx(hm, 256, mode)
     b = _ctx(hm, 256, 1)
     ka, kb = a.kv(256), b.kv(256)
     toks = _prompt(hm.params.vocab_size, 70, 9)
@@ -204,16 +208,18 @@ def test_persistent_and_per_phase_kernels_agree(tiny_model, name):
     assert ga.tolist() == gb.tolist()
 
 
+@pytest.mark.parametrize("mode", [0, 2])
 @pytest.mark.parametrize("ring_kb", [64, 96])
-def test_ring_filled_exactly_by_attention_pages(tiny_model, monkeypatch, ring_kb):
+def test_ring_filled_exactly_by_attention_pages(tiny_model, monkeypatch, ring_kb, mode):
     """A weight/KV ring whose size is a multiple of the attention page pair (head_dim
     128: 32 KB of K and V per page), so a tile can end exactly at the ring's end and
     the next one must start again at the front. Positions up to 199 need up to four
     pages per head, more than such a ring holds at once."""
     monkeypatch.setenv("FIBER_PK_RING_KB", str(ring_kb))
+    monkeypatch.setenv("FIBER_FL_RING_KB", str(ring_kb))
     path = tiny_model("q6k")
     hm = fb.HostModel(path)
-    a = _ctx(hm, 256, 0)
+    a = _ctx(hm, 256, mode)
     b = _ctx(hm, 256, 1)
     ka, kb = a.kv(256), b.kv(256)
     toks = _prompt(hm.params.vocab_size, 200, 11)
