@@ -8,7 +8,10 @@
  * taken on the device and the logits never leave HBM; otherwise the logits are
  * copied back and sampled by the host sampler (top-k / top-p).
  * Additions: --gpu N (device ordinal), --synth PRESET (write a seeded synthetic
- * model to --model's path first: stories, tinyllama, tinyllama-q5, llama7b).
+ * model to --model's path first: stories, tinyllama, tinyllama-q5, llama7b),
+ * --ids (also print the prompt and generated token ids to stderr). The prompt is
+ * prefilled with one fiber_prefill call (batched on the tensor cores) instead of
+ * the reference's token-by-token loop.
  * --no-ane and --arch belong to Apple-only paths and are not accepted.
  */
 #include <getopt.h>
@@ -47,6 +50,7 @@ static void usage(const char *prog) {
     fprintf(stderr, "  --benchmark         Print per-token timing\n");
     fprintf(stderr, "  --gpu <n>           CUDA device ordinal (default: 0)\n");
     fprintf(stderr, "  --synth <preset>    Write a seeded synthetic model to --model first\n");
+    fprintf(stderr, "  --ids               Also print prompt and generated token ids to stderr\n");
     fprintf(stderr, "  --help              Show this help\n");
 }
 
@@ -67,7 +71,7 @@ static void list_tensors(const model_t *m) {
 
 int main(int argc, char **argv) {
     const char *model_path = NULL, *prompt = "Hello", *synth = NULL;
-    int max_gen = 128, top_k = 40, list_flag = 0, bench_flag = 0, device = 0;
+    int max_gen = 128, top_k = 40, list_flag = 0, bench_flag = 0, device = 0, ids_flag = 0;
     unsigned ctx_len = 0;
     float temperature = 0.7f, top_p = 0.9f;
     static struct option opts[] = {
@@ -77,7 +81,7 @@ int main(int argc, char **argv) {
         {"top-p", required_argument, 0, 'P'},       {"list-tensors", no_argument, 0, 't'},
         {"benchmark", no_argument, 0, 'b'},         {"gpu", required_argument, 0, 'g'},
         {"synth", required_argument, 0, 's'},       {"help", no_argument, 0, 'h'},
-        {0, 0, 0, 0}};
+        {"ids", no_argument, 0, 'i'},               {0, 0, 0, 0}};
     int o;
     while ((o = getopt_long(argc, argv, "m:p:n:c:T:k:P:tbh", opts, NULL)) != -1) {
         switch (o) {
@@ -92,6 +96,7 @@ int main(int argc, char **argv) {
         case 'b': bench_flag = 1; break;
         case 'g': device = atoi(optarg); break;
         case 's': synth = optarg; break;
+        case 'i': ids_flag = 1; break;
         case 'h': usage(argv[0]); return 0;
         default: usage(argv[0]); return 1;
         }
@@ -184,22 +189,36 @@ int main(int argc, char **argv) {
     for (int i = 0; i < n_prompt; i++) printf("%s", tokenizer_decode(tok, prompt_tokens[i]));
     fflush(stdout);
 
+    if (ids_flag) {
+        fprintf(stderr, "prompt ids:");
+        for (int i = 0; i < n_prompt; i++) fprintf(stderr, " %d", prompt_tokens[i]);
+        fprintf(stderr, "\n");
+    }
+
+    // prefill: the whole prompt in one call (greedy), or all but the last token and
+    // then the last one with its logits for the sampler
     int rc = 0, next = 0;
     t0 = now_ms();
-    for (int i = 0; i < n_prompt && rc == 0; i++) {
-        const int32_t tk = prompt_tokens[i], ps = i;
+    {
         int32_t am = 0;
-        rc = fiber_forward_token(gpu, kv, &tk, &ps, 1, (!greedy && i == n_prompt - 1) ? logits : NULL, &am);
+        const int n_pre = greedy ? n_prompt : n_prompt - 1;
+        if (n_pre > 0) rc = fiber_prefill(gpu, kv, prompt_tokens, n_pre, 0, &am);
+        if (rc == 0 && !greedy) {
+            const int32_t tk = prompt_tokens[n_prompt - 1], ps = n_prompt - 1;
+            rc = fiber_forward_token(gpu, kv, &tk, &ps, 1, logits, &am);
+        }
         next = am;
     }
     const double prefill_ms = now_ms() - t0;
     if (rc == 0 && !greedy) next = sampler_sample(&sampler, logits);
+    int *gen_ids = ids_flag ? (int *)malloc((size_t)(max_gen > 0 ? max_gen : 1) * sizeof(int)) : NULL;
 
     int pos = n_prompt, gen = 0;
     const double g0 = now_ms();
     for (int i = 0; rc == 0 && i < max_gen && pos < (int)ctx_len; i++) {
         printf("%s", tokenizer_decode(tok, next));
         fflush(stdout);
+        if (gen_ids) gen_ids[gen] = next;
         gen++;
         if (next == tokenizer_eos(tok)) break;
         const double s0 = now_ms();
@@ -212,6 +231,12 @@ int main(int argc, char **argv) {
     }
     const double gen_ms = now_ms() - g0;
     if (rc != 0) fprintf(stderr, "\nError: %s\n", fiber_last_error());
+    if (gen_ids) {
+        fprintf(stderr, "generated ids:");
+        for (int i = 0; i < gen; i++) fprintf(stderr, " %d", gen_ids[i]);
+        fprintf(stderr, "\n");
+        free(gen_ids);
+    }
 
     printf("\n\n--- Stats ---\n");
     printf("Prefill: %d tokens in %.1f ms (%.1f tok/s)\n", n_prompt, prefill_ms, n_prompt / (prefill_ms / 1000.0));

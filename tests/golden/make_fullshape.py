@@ -123,7 +123,9 @@ def run_prompted(name: str, out: dict, arrays: dict):
         arrays[f"logits_{s}"] = lg
     st.close()
     om.close()
-    if orc.ref_available() and name != "q5long":
+    # the reference's own cpu_forward_token runs single-threaded here: hours at 7B, so it
+    # is run on the 1.1B-and-smaller workloads only
+    if orc.ref_available() and name not in ("q5long", "llama7b"):
         rm = orc.RefModel(path)
         kv = rm.kv(P + D + 1)
         for p in range(P - 1):
