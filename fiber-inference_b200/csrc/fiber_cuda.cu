@@ -389,11 +389,14 @@ struct gpu_context {
     std::vector<FPhase> fphases;
     uint64_t *fl_words = nullptr;     // tagged words of every phase output of one step
     unsigned int *fl_sync = nullptr;  // [0] launch tag, [1] exit count, [2] argmax ticket, [4..) attention tickets
-    float *fl_att_part = nullptr;     // attention split states
+    uint64_t *fl_att_words = nullptr; // tagged attention split states
     unsigned long long *fl_am = nullptr;  // per-CTA argmax keys
     int fl_ring = 0, fl_frag = 0, fl_xres = 0, fl_xin = 0, fl_nw = 0, fl_grid = 0, fl_max_split = 0;
     size_t fl_smem = 0;
     void *fl_kernel = nullptr;
+    const void *fl_map_k = nullptr, *fl_map_v = nullptr;  // pools (and their row count) the maps describe
+    long long fl_map_rows = 0;
+    CUtensorMap fl_kmap, fl_vmap;
     // tensor parallelism: this rank's share of query heads, KV heads and FFN blocks
     // (the whole model when tp_world == 1)
     int tp_rank = 0, tp_world = 1;
@@ -453,7 +456,7 @@ extern "C" void fiber_cuda_free(fiber_ctx_t *c) {
     for (void *q : c->pf_pad) cudaFree(q);
     void *dev[] = {c->pf_x2, c->smp_rng, c->smp_out, c->att_ws, c->att_tickets, c->bt_pos, c->bt_arg, c->bt_rec, c->bt_step, c->bt_logits, c->pf_x, c->pf_qkv, c->pf_att, c->pf_hg, c->pf_hu, c->pf_bp, c->pf_tok, c->x2, c->d_shard, c->d_data, c->x, c->qkv, c->att, c->h, c->logits, c->rope, c->io, c->rec,
                    c->att_part, c->att_cnt, c->am_part, c->am_cnt, c->d_phases, c->d_bar,
-                   c->d_fphases, c->fl_words, c->fl_sync, c->fl_att_part, c->fl_am,
+                   c->d_fphases, c->fl_words, c->fl_sync, c->fl_att_words, c->fl_am,
                    c->pk_gf[0], c->pk_gf[1], c->pk_gf[2], c->pk_gf[3], c->pk_ss[0], c->pk_ss[1]};
     for (void *p : dev)
         if (p) cudaFree(p);
@@ -789,16 +792,27 @@ static int flow_build(gpu_context *c) {
         frag = std::max(frag, types * f.cols * 4);
     }
     frag = (frag + 127) & ~127;
+    // attention splits per KV head: about four pages each, at most 8 (split 0 merges the others)
+    const int max_split = std::max(1, std::min(8, grid / (int)p.n_kv_heads));
+    scratch += (max_split - 1) * c->G * (hd + 2);
     const int xres = (dim + 31) & ~31;
     const int xin = (std::max(std::max(dim, ffn), scratch) + 31) & ~31;
     const int nw = (dim + 31) & ~31;
     cudaFuncAttributes fa;
     CK(cudaFuncGetAttributes(&fa, c->fl_kernel));
+    // the producer / consumer register split (setmaxnreg) must fit the registers the
+    // block is launched with, or the consumers' increase would wait forever
+    if ((long long)fa.numRegs * FL_THREADS < 4LL * 32 * FL_REG_PRODUCER + 8LL * 32 * FL_REG_CONSUMER) {
+        fprintf(stderr, "fiber: dataflow kernel launched with %d registers per thread; register split does not fit\n",
+                fa.numRegs);
+        return FIBER_OK;
+    }
     int optin = 0;
     CK(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, c->device));
-    const long long avail = (long long)optin - (long long)fa.sharedSizeBytes - frag - (long long)(xres + xin + nw) * 4 - 1024;
-    if (avail < (long long)max_tile) return FIBER_OK;  // tiles do not fit
-    c->fl_ring = (int)(avail & ~127ll);
+    const long long avail =
+        (long long)optin - (long long)fa.sharedSizeBytes - FL_RING_PAD - frag - (long long)(xres + xin + nw) * 4 - 1024;
+    if (avail < (long long)max_tile + 1024) return FIBER_OK;  // tiles do not fit
+    c->fl_ring = (int)(avail & ~1023ll);
     if (const char *e = getenv("FIBER_FL_RING_KB")) {  // tuning knob: cap the ring (KB)
         const long long cap = atoll(e) * 1024;
         if (cap >= (long long)max_tile && cap < c->fl_ring) c->fl_ring = (int)(cap & ~127ll);
@@ -807,14 +821,16 @@ static int flow_build(gpu_context *c) {
     c->fl_xres = xres;
     c->fl_xin = xin;
     c->fl_nw = nw;
-    c->fl_smem = (size_t)c->fl_ring + frag + (size_t)(xres + xin + nw) * 4;
+    c->fl_smem = (size_t)FL_RING_PAD + c->fl_ring + frag + (size_t)(xres + xin + nw) * 4;
     CK(cudaFuncSetAttribute(c->fl_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)c->fl_smem));
     int per_sm = 0;
     CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, c->fl_kernel, FL_THREADS, c->fl_smem));
     if (per_sm < 1) return FIBER_OK;
     c->fl_grid = grid;
-    c->fl_max_split = std::max(1, grid / (int)p.n_kv_heads);
-    CK(cudaMalloc(&c->fl_att_part, (size_t)p.n_kv_heads * c->fl_max_split * c->G * (hd + 2) * 4));
+    c->fl_max_split = max_split;
+    const size_t att_words = (size_t)L * p.n_kv_heads * max_split * c->G * (hd + 2);
+    CK(cudaMalloc(&c->fl_att_words, att_words * 8));
+    CK(cudaMemset(c->fl_att_words, 0, att_words * 8));
     CK(cudaMalloc(&c->fl_am, (size_t)grid * 8));
     const size_t n_sync = 4 + p.n_kv_heads;
     CK(cudaMalloc(&c->fl_sync, n_sync * 4));
@@ -1321,14 +1337,49 @@ static cudaError_t enqueue_persistent(gpu_context *c, const kv_cache_t *kv, bool
 static bool use_flow(const gpu_context *c) { return c->mode == 2 && c->fl_ok; }
 static bool use_pk(const gpu_context *c) { return c->mode == 0 && c->pk_ok; }
 
+// 2D tensor map of a K or V pool for the dataflow attention: rows = page * layer * kv_head
+// * 64 positions, head_dim fp16 columns; box 64 columns x 64 rows, 128-byte swizzle.
+static bool fl_make_kv_map(CUtensorMap *map, const uint16_t *pool, const kv_cache_t *kv) {
+    memset(map, 0, sizeof(*map));
+    static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+    if (!encode) {
+        void *fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault, &q) !=
+                cudaSuccess ||
+            q != cudaDriverEntryPointSuccess || !fn)
+            return false;
+        encode = (PFN_cuTensorMapEncodeTiled_v12000)fn;
+    }
+    const cuuint64_t rows = (cuuint64_t)kv->n_pages * kv->n_layers * kv->n_kv_heads * kv->page_size;
+    const cuuint64_t dims[2] = {(cuuint64_t)kv->head_dim, rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)kv->head_dim * 2};
+    const cuuint32_t box[2] = {64u, (cuuint32_t)kv->page_size};
+    const cuuint32_t estr[2] = {1, 1};
+    return encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, (void *)pool, dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // Enqueue one decode step as one launch of the dataflow kernel (cooperative: all
 // CTAs co-resident, one per SM). No per-launch memset: every hand-off word carries
 // the launch tag, which the kernel advances when its last CTA exits.
 static cudaError_t enqueue_flow(gpu_context *c, const kv_cache_t *kv, bool loop, cudaStream_t st,
                                 unsigned long long *trace = nullptr) {
     const model_params_t &p = c->p;
+    const long long rows = (long long)kv->n_pages * kv->n_layers * kv->n_kv_heads * kv->page_size;
+    if (c->fl_map_k != kv->k_pool || c->fl_map_v != kv->v_pool || c->fl_map_rows != rows) {
+        c->fl_map_k = c->fl_map_v = nullptr;
+        if (!fl_make_kv_map(&c->fl_kmap, kv->k_pool, kv) || !fl_make_kv_map(&c->fl_vmap, kv->v_pool, kv))
+            return cudaErrorInvalidValue;
+        c->fl_map_k = kv->k_pool;
+        c->fl_map_v = kv->v_pool;
+        c->fl_map_rows = rows;
+    }
     FParams P;
     memset(&P, 0, sizeof(P));
+    P.kmap = c->fl_kmap;
+    P.vmap = c->fl_vmap;
     P.phases = c->d_fphases;
     P.n_phases = (int)c->fphases.size();
     P.embd = c->embd;
@@ -1345,8 +1396,9 @@ static cudaError_t enqueue_flow(gpu_context *c, const kv_cache_t *kv, bool loop,
     P.max_seq = c->max_seq < kv->max_seq ? c->max_seq : kv->max_seq;
     P.att_scale = 1.0f / sqrtf((float)p.head_dim);
     P.att_max_split = c->fl_max_split;
-    P.att_part = c->fl_att_part;
-    P.att_tick = c->fl_sync + 4;
+    P.att_words = c->fl_att_words;
+    P.hd = (int)p.head_dim;
+    P.G = c->G;
     P.am_key = c->fl_am;
     P.am_count = c->fl_sync + 2;
     P.io_token = &c->io->token;
@@ -2059,6 +2111,11 @@ extern "C" int fiber_step_launches(fiber_ctx_t *c) {
     int n = 2;  // embed + lm_head
     for (const LayerDev &d : c->L) n += 4 + 1 + (d.tk != d.tq) + (d.tv != d.tk);
     return n;
+}
+
+extern "C" int fiber_step_ring_bytes(fiber_ctx_t *c) {
+    if (!c) return set_err(FIBER_EARG, "no context");
+    return use_flow(c) ? c->fl_ring : use_pk(c) ? c->pk_ring : 0;
 }
 
 extern "C" int fiber_trace_step(fiber_ctx_t *c, kv_cache_t *kv, int token, int pos, uint64_t *out, size_t cap,

@@ -29,21 +29,33 @@
 // Every wait is bounded (%globaltimer); on timeout the kernel records error 4,
 // stops issuing work and returns once its own copies have landed.
 #pragma once
+#include <cuda.h>
+
 #include "persistent.cuh"
 
 namespace fiber {
 
 constexpr int FL_WARPS = 8;
 constexpr int FL_CONSUMERS = FL_WARPS * 32;
-constexpr int FL_THREADS = FL_CONSUMERS + 32;  // + producer warp
+// + a producer warpgroup (warps 8..11; lane 0 of warp 8 streams the ring). With 12
+// warps the launch gives every thread 168 registers (three warps share each SM
+// sub-partition's register file); the producer group then drops to FL_REG_PRODUCER
+// and the consumer warps rise to FL_REG_CONSUMER (setmaxnreg): 4 x 32 x 40 +
+// 8 x 32 x 232 = 12 x 32 x 168, exactly the launch's registers.
+constexpr int FL_THREADS = FL_CONSUMERS + 128;
+constexpr int FL_REG_PRODUCER = 40, FL_REG_CONSUMER = 232;
+static_assert(4 * 32 * FL_REG_PRODUCER + 8 * 32 * FL_REG_CONSUMER <= FL_THREADS * 168, "register split");
 constexpr int FL_NDESC = 16;                   // ring slots
 constexpr unsigned long long FL_WAIT_NS = 2000000000ull;
+constexpr int FL_RING_PAD = 1024;              // the ring starts at the first 1024-byte boundary (swizzled copies)
 // Optional per-phase, per-CTA timeline (FParams::trace non-null), fields:
 //  0 globaltimer (ns) at the phase start   1 cycles polling the input words
 //  2 cycles RMSNorm + fragments            3 cycles from the tiles' start to the phase end
 //  4 cycles warp 0 waited for ring slots   5 globaltimer (ns) at the phase end
 //  6 producer: globaltimer after issuing the phase's last copy   7 producer: cycles waiting for ring space
-constexpr int FL_TRACE_FIELDS = 8;
+//  attention units: 1 cycles polling q|k|v   2 RoPE, K/V append, q fragments
+//  8 cycles of the page loop   9 cycles merging (warps, then splits: includes polling them)
+constexpr int FL_TRACE_FIELDS = 10;
 
 enum : int { FL_QKV = 0, FL_ATTN = 1, FL_RESID = 2, FL_SWIGLU = 3, FL_LM = 4 };
 
@@ -67,6 +79,10 @@ struct __align__(16) FPhase {
 static_assert(sizeof(FPhase) % 16 == 0 && sizeof(FPhase) / 16 <= 32, "phase descriptors are copied in 16-byte chunks");
 
 struct FParams {
+    // K and V pools as 2D tensors [rows = page * layer * kv_head * 64 positions][head_dim] fp16,
+    // box 64 x 64 with 128-byte swizzle (attention pages)
+    alignas(64) CUtensorMap kmap;
+    alignas(64) CUtensorMap vmap;
     const FPhase *phases;  // device array
     int n_phases;
     const uint8_t *embd;
@@ -79,8 +95,8 @@ struct FParams {
     int n_layers, n_kv, n_heads, max_seq;
     float att_scale;
     int att_max_split;           // page splits per KV head at most
-    float *att_part;             // [n_kv][att_max_split][G][hd + 2] split states
-    unsigned int *att_tick;      // [n_kv] merge tickets, zero between launches
+    uint64_t *att_words;         // tagged split states [n_layers][n_kv][att_max_split][G][hd + 2]
+    int hd, G;                   // head_dim, query heads per KV head (the q|k|v word layout)
     // greedy argmax and step state
     unsigned long long *am_key;  // [gridDim.x] per-CTA best (value, index) keys
     unsigned int *am_count;      // ticket, zero between launches
@@ -94,7 +110,7 @@ struct FParams {
 };
 
 // ---- per-CTA state ----------------------------------------------------------------------
-// dynamic: [ring][fragments frag_bytes][xres xres_floats][xin xin_floats][norm weights nw_floats]
+// dynamic: [pad to 1024][ring][fragments frag_bytes][xres xres_floats][xin xin_floats][norm weights nw_floats]
 extern __shared__ __align__(128) uint8_t fl_dyn[];
 __shared__ __align__(8) uint64_t fl_full[FL_NDESC];
 __shared__ __align__(8) uint64_t fl_empty[FL_NDESC];
@@ -107,10 +123,13 @@ __shared__ int fl_tile_off[FL_NDESC];
 __shared__ volatile int fl_abort;
 __shared__ unsigned int fl_ticket;
 __shared__ float fl_scale[2];            // staged input: fragment scale, its inverse
+__shared__ float2 fl_rope[64];           // RoPE (cos, sin) row of this launch's position
 
-FDEV uint8_t *fl_ring() { return fl_dyn; }
-FDEV uint2 *fl_frag(const FParams &P) { return reinterpret_cast<uint2 *>(fl_dyn + P.ring_bytes); }
-FDEV float *fl_xres(const FParams &P) { return reinterpret_cast<float *>(fl_dyn + P.ring_bytes + P.frag_bytes); }
+FDEV uint8_t *fl_ring() { return fl_dyn + ((FL_RING_PAD - (smem_u32(fl_dyn) & (FL_RING_PAD - 1))) & (FL_RING_PAD - 1)); }
+FDEV uint2 *fl_frag(const FParams &P) { return reinterpret_cast<uint2 *>(fl_dyn + FL_RING_PAD + P.ring_bytes); }
+FDEV float *fl_xres(const FParams &P) {
+    return reinterpret_cast<float *>(fl_dyn + FL_RING_PAD + P.ring_bytes + P.frag_bytes);
+}
 FDEV float *fl_xin(const FParams &P) { return fl_xres(P) + P.xres_floats; }
 FDEV float *fl_nw(const FParams &P) { return fl_xin(P) + P.xin_floats; }
 
@@ -259,11 +278,45 @@ FDEV void fl_set_scale(float m, float &scale, float &inv) {
 template <int HD, int G>
 struct FlowAttn;
 
+// v - (fp16 value in the low half of h), exact in fp32 (v's fp16 rounding error)
+FDEV float fl_rem(uint32_t h, float v) {
+    float r;
+    asm("{\n .reg .f16 l, u, m;\n mov.b32 {l, u}, %1;\n mov.b16 m, 0xBC00;\n fma.rn.f32.f16 %0, l, m, %2;\n}\n"
+        : "=f"(r)
+        : "r"(h), "f"(v));
+    return r;
+}
+
+// Fragments of the staged input for weight type T (the k-slot order TcDot<T> reads,
+// TcType<T>::elem): per group f the fp16 hi parts of its four elements, then the lo
+// parts (hi + lo carries ~22 bits), v = (x * rrms) * w * scale where the phase has an
+// RMSNorm. Two packed conversions per pair of elements (hi, then the exact remainder).
+template <int T>
+FDEV void fl_frags(int nb, const float *xs, const float *nw, float rrms, float scale, uint2 *xf) {
+    for (int f = threadIdx.x; f < nb * 64; f += FL_CONSUMERS) {
+        const int b = f >> 6, s = (f >> 2) & 15, t = f & 3;
+        float v[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const int k = b * 256 + TcType<T>::elem(t, s, i);
+            float x = xs[k];
+            if (nw) x = __fmul_rn(__fmul_rn(x, rrms), nw[k]);
+            v[i] = x * scale;
+        }
+        const uint32_t h01 = pack_f16x2(v[0], v[1]), h23 = pack_f16x2(v[2], v[3]);
+        const uint32_t l01 = pack_f16x2(fl_rem(h01, v[0]), fl_rem(h01 >> 16, v[1]));
+        const uint32_t l23 = pack_f16x2(fl_rem(h23, v[2]), fl_rem(h23 >> 16, v[3]));
+        xf[2 * f + 0] = make_uint2(h01, h23);
+        xf[2 * f + 1] = make_uint2(l01, l23);
+    }
+}
+
 // ---- GEMV phase -----------------------------------------------------------------------
 
 // Stage the phase input: poll (or decode the embedding row), RMSNorm scale, fragments
 // for each weight type of the phase. All consumer threads. Returns false when stopped.
-FDEV bool fl_stage(const FParams &P, const FPhase &F, uint32_t tag, int token, unsigned long long *tr) {
+__device__ __noinline__ bool fl_stage(const FParams &P, const FPhase &F, uint32_t tag, int token,
+                                      unsigned long long *tr) {
     const int tid = threadIdx.x;
     const int n = F.cols, nb = n >> 8;
     const bool norm = F.norm_w != nullptr;
@@ -321,9 +374,9 @@ FDEV bool fl_stage(const FParams &P, const FPhase &F, uint32_t tag, int token, u
     for (int pass = 0; pass < (type_b >= 0 ? 2 : 1); pass++) {
         uint2 *dst = pass ? xf1 : xf0;
         switch (pass ? type_b : F.seg[0].type) {
-        case T_Q4_K: pk_stage<T_Q4_K>(nb, xs, norm ? nw : nullptr, rrms, scale, dst); break;
-        case T_Q6_K: pk_stage<T_Q6_K>(nb, xs, norm ? nw : nullptr, rrms, scale, dst); break;
-        default: pk_stage<T_F16>(nb, xs, norm ? nw : nullptr, rrms, scale, dst); break;
+        case T_Q4_K: fl_frags<T_Q4_K>(nb, xs, norm ? nw : nullptr, rrms, scale, dst); break;
+        case T_Q6_K: fl_frags<T_Q6_K>(nb, xs, norm ? nw : nullptr, rrms, scale, dst); break;
+        default: fl_frags<T_F16>(nb, xs, norm ? nw : nullptr, rrms, scale, dst); break;
         }
     }
     cbar();
@@ -356,7 +409,23 @@ FDEV void fl_epilogue(const FParams &P, const FPhase &F, const PSeg &S, int lt, 
         }
         if (r < S.rows) {
             switch (F.kind) {
-            case FL_QKV: ll_store(F.out + S.out_off + r, v0, tag); break;
+            case FL_QKV: {  // q|k|v grouped by KV head: [g][G query heads | k | v] x hd
+                const int o = S.out_off + r;
+                const int qd = P.n_heads * P.hd, kd = P.n_kv * P.hd;
+                int gi, slot;
+                if (o < qd) {
+                    gi = o / (P.G * P.hd);
+                    slot = o % (P.G * P.hd);
+                } else if (o < qd + kd) {
+                    gi = (o - qd) / P.hd;
+                    slot = P.G * P.hd + (o - qd) % P.hd;
+                } else {
+                    gi = (o - qd - kd) / P.hd;
+                    slot = (P.G + 1) * P.hd + (o - qd - kd) % P.hd;
+                }
+                ll_store(F.out + (size_t)gi * (P.G + 2) * P.hd + slot, v0, tag);
+                break;
+            }
             case FL_RESID: ll_store(F.out + r, __fadd_rn(fl_xres(P)[r], v0), tag); break;
             case FL_SWIGLU: {
                 const float h = __fmul_rn(__fdiv_rn(v0, __fadd_rn(1.0f, expf(-v0))), v1);
@@ -449,62 +518,106 @@ FDEV bool fl_tiles(const FParams &P, const FPhase &F, long long &seq, uint32_t t
 // ---- attention ------------------------------------------------------------------------
 
 // Units of the attention phase at position pos: n_kv * S, S page splits per KV head
-// (at most one per page, at most att_max_split); unit u = g * S + j runs on CTA
-// gridDim.x - 1 - u, pages [j * nch / S, (j + 1) * nch / S).
-FDEV int fl_att_splits(const FParams &P, int nch) { return max(1, min(nch, P.att_max_split)); }
+// (about eight pages per unit, one per warp, so a unit's pages arrive while the QKV
+// phase runs and are processed in parallel; at most att_max_split); unit u = g * S + j runs on CTA gridDim.x - 1 - u,
+// pages [j * nch / S, (j + 1) * nch / S).
+constexpr int FL_PAGES_PER_UNIT = 8;  // one page per consumer warp
+FDEV int fl_att_splits(const FParams &P, int nch) {
+    return max(1, min((nch + FL_PAGES_PER_UNIT - 1) / FL_PAGES_PER_UNIT, P.att_max_split));
+}
 
+// fragments / copies for the attention unit
+FDEV void mma16808(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k8.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%0,%1,%2,%3};\n"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(b0));
+}
+FDEV void ldsm_x4_trans(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+FDEV uint32_t lds32(uint32_t addr) {
+    uint32_t v;
+    asm volatile("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(addr));
+    return v;
+}
+// 2D tensor copy (no multicast) of one box into shared memory, completion on bar
+FDEV void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+            "r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+FDEV uint32_t pack_hi_lo(float a, float b, uint32_t &lo) {  // fp16 hi parts of (a, b); lo parts returned in lo
+    const __half2 h = __floats2half2_rn(a, b);
+    const float2 hf = __half22float2(h);
+    const __half2 l = __floats2half2_rn(a - hf.x, b - hf.y);
+    lo = *reinterpret_cast<const uint32_t *>(&l);
+    return *reinterpret_cast<const uint32_t *>(&h);
+}
+
+// Attention unit on the tensor cores. K/V pages arrive by tensor copies in the
+// 128-byte swizzled layout: a page of K (or V) is HD/64 column halves of
+// [64 rows][128 bytes], 16-byte chunk c of row r stored at chunk c ^ (r & 7), so
+// the fragment loads below hit 32 distinct banks.
 template <int HD, int G>
 struct FlowAttn {
     static constexpr int PG = ATTN_P;
-    static constexpr int WPH = FL_WARPS / G;          // warps per query head
-    static constexpr int PW = PG / WPH;               // positions of a page per warp
-    static constexpr int LPP = PW >= 32 ? 1 : 32 / PW;  // lanes per position
-    static constexpr int PPL = PW >= 32 ? PW / 32 : 1;  // positions per lane
-    static constexpr int W = HD / 2;                  // 32-bit words of a K/V row
-    static constexpr int WS = W / LPP;                // words of a row per lane (its slice)
-    static constexpr int DPL = HD / 32;               // head dims per lane in P.V
+    static constexpr int KS = HD / 16;   // k-steps of q.k
+    static constexpr int NT = HD / 8;    // 8-dim tiles of P.V
+    static constexpr int HALF = 64 * 128;  // bytes of one 64-dim column half of a page
+    static constexpr int PAGE = PG * HD * 2;
     static_assert(G == 1 || G == 2 || G == 4 || G == 8, "query heads per KV head");
     static_assert(HD == 64 || HD == 128, "head_dim 64 or 128");
+    static_assert(PG == 64 && FL_WARPS == 8, "eight warps x eight positions per page");
 
-    // shared scratch (in the xin region): q [G][HD] fp32, nk/nv [HD] fp16, warp states [8][HD + 2],
-    // the polled q | k | v [(G + 2) * HD]
-    static constexpr int SCRATCH_FLOATS = G * HD + HD + FL_WARPS * (HD + 2) + (G + 2) * HD;
+    // shared scratch (in the xin region): q [G][HD] fp32, nk/nv [HD] fp16 each,
+    // warp states [8][G][HD + 2], the polled q | k | v [(G + 2) * HD]; then the other
+    // splits' states [att_max_split - 1][G][HD + 2] (sized by the host)
+    static constexpr int SCRATCH_FLOATS = G * HD + HD + FL_WARPS * G * (HD + 2) + (G + 2) * HD;
 
-    // rotated word index of a lane's slice (the lanes of a warp hit 32 distinct banks)
-    static FDEV int rot(int lane) {
-        const int pi = lane / LPP, qq = lane % LPP;
-        if (WS >= 32) return lane;
-        return HD == 128 ? 2 * pi + (qq >> 1) : pi;
-    }
+    // byte offset of (row r, dims 8c .. 8c+7) in a swizzled page
+    static FDEV uint32_t swz(int r, int c) { return (uint32_t)((c >> 3) * HALF + r * 128 + (((c & 7) ^ (r & 7)) << 4)); }
 
-    static FDEV bool unit(const FParams &P, const FPhase &F, int g, int j, int S, int pos, int nch, long long &seq,
-                          uint32_t tag, long long &wcycles) {
-        const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    static __device__ __noinline__ bool unit(const FParams &P, const FPhase &F, int g, int j, int S, int pos, int nch,
+                                             long long &seq, uint32_t tag, long long &wcycles, unsigned long long *tr) {
+        const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, gl = lane >> 2, t = lane & 3;
+        long long ck = clock64();
+        auto mark = [&](int field) {
+            if (tr) {
+                const long long n = clock64();
+                tr[field] = (unsigned long long)(n - ck);
+                ck = n;
+            }
+        };
         float *sm = fl_xin(P);
         float *qs = sm;                                             // [G][HD]
         uint16_t *nk = reinterpret_cast<uint16_t *>(sm + G * HD);   // [HD]
         uint16_t *nv = nk + HD;                                     // [HD]
-        float *wm = sm + G * HD + HD;                               // [FL_WARPS][HD + 2]
-        float *raw = wm + FL_WARPS * (HD + 2);                      // [(G + 2) * HD] q | k | v as polled
-        const uint64_t *qkv = F.in;
-        const int q0 = g * G * HD, k0 = P.n_heads * HD + g * HD, v0 = (P.n_heads + P.n_kv) * HD + g * HD;
-        bool got = fl_poll(P, qkv + q0, raw, G * HD, tag);
-        got = got && fl_poll(P, qkv + k0, raw + G * HD, HD, tag);
-        got = got && fl_poll(P, qkv + v0, raw + G * HD + HD, HD, tag);
+        float *wm = sm + G * HD + HD;                               // [FL_WARPS][G][HD + 2]
+        float *raw = wm + FL_WARPS * G * (HD + 2);                  // [(G + 2) * HD] q | k | v as polled
+        float *others = raw + (G + 2) * HD;                         // [S - 1][G][HD + 2] other splits' states
+        const bool got = fl_poll(P, F.in + (size_t)g * (G + 2) * HD, raw, (G + 2) * HD, tag);
         if (cbar_any(!got || fl_abort)) return false;
+        mark(1);
         const int tn = pos - (nch - 1) * PG;  // row of the new position in the last page
         const bool writer = j == S - 1;       // the unit holding the last page appends the new K/V row
         const size_t base = (((size_t)P.page_table[nch - 1] * P.n_layers + F.layer) * P.n_kv + g) * (size_t)PG * HD;
-        const float2 *rp = P.rope + (size_t)pos * (HD / 2);
+        const float2 *rp = fl_rope;
+        float qmax = 0.f;
         for (int i = tid; i < (G + 1) * (HD / 2); i += FL_CONSUMERS) {  // RoPE (src/fiber_proof.m:30-51)
             const int h = i / (HD / 2), jj = i % (HD / 2);
-            const float2 cs = __ldg(rp + jj);
+            const float2 cs = rp[jj];
             const float x1 = raw[h * HD + jj], x2 = raw[h * HD + jj + HD / 2];
             const float y1 = __fsub_rn(__fmul_rn(x1, cs.x), __fmul_rn(x2, cs.y));
             const float y2 = __fadd_rn(__fmul_rn(x1, cs.y), __fmul_rn(x2, cs.x));
             if (h < G) {
                 qs[h * HD + jj] = y1;
                 qs[h * HD + jj + HD / 2] = y2;
+                qmax = fmaxf(qmax, fmaxf(fabsf(y1), fabsf(y2)));
             } else {
                 const uint16_t b1 = __half_as_ushort(__float2half_rn(y1)), b2 = __half_as_ushort(__float2half_rn(y2));
                 nk[jj] = b1;
@@ -520,18 +633,46 @@ struct FlowAttn {
             nv[i] = b;
             if (writer) P.v_pool[base + (size_t)tn * HD + i] = b;
         }
-        cbar();
+        float dummy = 0.f;
+        fl_reduce2(dummy, qmax);  // barriers: qs, nk, nv complete
+        if (!(qmax < 3.0e38f)) {
+            if (tid == 0) *P.io_err = 5;
+            qmax = 1.0f;
+        }
+        float qscale, qinv;
+        fl_set_scale(qmax, qscale, qinv);
+        const float sscale = __fmul_rn(qinv, P.att_scale);  // exact power of two times 1/sqrt(hd)
 
-        // this warp: query head hw of the group, positions [ws * PW, ws * PW + PW) of every page
-        const int hw = warp / WPH, ws = warp % WPH;
-        const int pi = lane / LPP, qq = lane % LPP, r = rot(lane);
-        const float *qh = qs + hw * HD + qq * (2 * WS);
-        float m_run = -INFINITY, l_run = 0.f, o_run[DPL];
+        // q as the A operand: row gl = head gl (hi part), row gl + 8 = its lo part; rows of
+        // missing heads are zero
+        uint32_t qa[KS][4];
 #pragma unroll
-        for (int k = 0; k < DPL; k++) o_run[k] = 0.f;
+        for (int ks = 0; ks < KS; ks++) {
+            if (gl < G) {
+                const float *qr = qs + gl * HD + 16 * ks + 2 * t;
+                uint32_t lo0, lo1;
+                qa[ks][0] = pack_hi_lo(qr[0] * qscale, qr[1] * qscale, lo0);
+                qa[ks][2] = pack_hi_lo(qr[8] * qscale, qr[9] * qscale, lo1);
+                qa[ks][1] = lo0;
+                qa[ks][3] = lo1;
+            } else {
+                qa[ks][0] = qa[ks][1] = qa[ks][2] = qa[ks][3] = 0u;
+            }
+        }
+        mark(2);
+        // this warp: whole pages p0 + warp, p0 + warp + 8, ... (all G heads; lane: head gl);
+        // every warp steps through every item of the ring, the owner frees it
+        float m_run = -INFINITY, l_run = 0.f, o[NT][4];
+#pragma unroll
+        for (int n = 0; n < NT; n++) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+        const uint32_t nk_a = smem_u32(nk), nv_a = smem_u32(nv);
         const int p0 = (int)((long long)j * nch / S), p1 = (int)((long long)(j + 1) * nch / S);
         bool ok = true;
         for (int pg = p0; pg < p1; pg++) {
+            if ((pg - p0) % FL_WARPS != warp) {
+                seq++;
+                continue;
+            }
             const uint8_t *tile = fl_acquire(P, seq, wcycles);
             if (!tile) {
                 ok = false;
@@ -540,146 +681,145 @@ struct FlowAttn {
             const int d = (int)(seq % FL_NDESC);
             seq++;
             const bool last = pg == nch - 1;
-            const int nt = last ? tn + 1 : PG;  // valid positions of the page
-            const uint32_t *kp = reinterpret_cast<const uint32_t *>(tile);
-            const uint16_t *vp = reinterpret_cast<const uint16_t *>(tile) + (size_t)PG * HD;
-            float s[PPL];
+            const int nvalid = last ? tn + 1 : PG;  // valid positions of the page
+            const uint32_t kb = smem_u32(tile), vb = kb + PAGE;
+            // scores of the page: n-tile nt = positions 8 nt .. 8 nt + 7; this lane loads K row 8 nt + gl
+            float sc[8][4];
 #pragma unroll
-            for (int e = 0; e < PPL; e++) {
-                const int t = ws * PW + pi + 32 * e;
-                const uint32_t *krow = (last && t == tn) ? reinterpret_cast<const uint32_t *>(nk) + qq * WS
-                                                         : kp + (size_t)t * W + qq * WS;
-                float d0 = 0.f, d1 = 0.f;
-#pragma unroll 8
-                for (int i = 0; i < WS; i++) {
-                    const int wi = (i + r) & (WS - 1);
-                    const float2 kf = __half22float2(*reinterpret_cast<const __half2 *>(krow + wi));
-                    const float2 qf = *reinterpret_cast<const float2 *>(qh + 2 * wi);
-                    d0 = fmaf(qf.x, kf.x, d0);
-                    d1 = fmaf(qf.y, kf.y, d1);
+            for (int nt = 0; nt < 8; nt++) {
+                sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+                const int r = 8 * nt + gl;
+                const bool fresh = last && r == tn;
+#pragma unroll
+                for (int ks = 0; ks < KS; ks++) {
+                    const uint32_t a0 = fresh ? nk_a + (16 * ks + 2 * t) * 2 : kb + swz(r, 2 * ks) + 4 * t;
+                    const uint32_t a1 = fresh ? nk_a + (16 * ks + 8 + 2 * t) * 2 : kb + swz(r, 2 * ks + 1) + 4 * t;
+                    mma16816(sc[nt], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], lds32(a0), lds32(a1));
                 }
-                float v = d0 + d1;
-                if (LPP >= 2) v += __shfl_xor_sync(0xffffffffu, v, 1);
-                if (LPP >= 4) v += __shfl_xor_sync(0xffffffffu, v, 2);
-                s[e] = t < nt ? __fmul_rn(v, P.att_scale) : -INFINITY;
             }
-            // page maximum over the warp's positions, running max
-            float m = s[0];
+            // lane (gl, t): positions 8 nt + 2t, 8 nt + 2t + 1 of head gl
+            float mx = -INFINITY;
 #pragma unroll
-            for (int e = 1; e < PPL; e++) m = fmaxf(m, s[e]);
-#pragma unroll
-            for (int o = LPP; o < 32; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-            const float M = fmaxf(m_run, m);
-            if (M != -INFINITY) {
-                const float al = m_run == -INFINITY ? 0.f : expf(m_run - M);
-                float p[PPL], psum = 0.f;
-#pragma unroll
-                for (int e = 0; e < PPL; e++) {
-                    p[e] = s[e] == -INFINITY ? 0.f : expf(s[e] - M);
-                    psum += p[e];
-                }
-                l_run = fmaf(al, l_run, qq == 0 ? psum : 0.f);  // one lane per position counts it
-#pragma unroll
-                for (int k = 0; k < DPL; k++) o_run[k] *= al;
-                // P.V over the warp's positions; lane owns dims 2*lane + {0,1} (+64 for HD 128)
-                constexpr int PU = PW < 32 ? PW : 32;  // positions per lane slot
-#pragma unroll
-                for (int e = 0; e < PPL; e++) {
-#pragma unroll 8
-                    for (int u2 = 0; u2 < PU; u2++) {
-                        const float pu = __shfl_sync(0xffffffffu, p[e], u2 * LPP);
-                        const int t = ws * PW + 32 * e + u2;
-                        const uint32_t *vrow = (last && t == tn) ? reinterpret_cast<const uint32_t *>(nv)
-                                                                 : reinterpret_cast<const uint32_t *>(vp + (size_t)t * HD);
-#pragma unroll
-                        for (int k = 0; k < DPL / 2; k++) {
-                            const float2 vf = __half22float2(*reinterpret_cast<const __half2 *>(vrow + lane + 32 * k));
-                            o_run[2 * k] = fmaf(pu, vf.x, o_run[2 * k]);
-                            o_run[2 * k + 1] = fmaf(pu, vf.y, o_run[2 * k + 1]);
-                        }
-                    }
-                }
+            for (int nt = 0; nt < 8; nt++) {
+                const int pa = 8 * nt + 2 * t;
+                sc[nt][0] = pa < nvalid ? __fmul_rn(sc[nt][0] + sc[nt][2], sscale) : -INFINITY;
+                sc[nt][1] = pa + 1 < nvalid ? __fmul_rn(sc[nt][1] + sc[nt][3], sscale) : -INFINITY;
+                mx = fmaxf(mx, fmaxf(sc[nt][0], sc[nt][1]));
+            }
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+            const float M = fmaxf(m_run, mx);
+            float al = 1.f, psum = 0.f;
+            const bool live = M != -INFINITY && gl < G;
+            if (live) {
+                al = m_run == -INFINITY ? 0.f : expf(m_run - M);
                 m_run = M;
             }
+#pragma unroll
+            for (int nt = 0; nt < 8; nt++) {
+#pragma unroll
+                for (int e = 0; e < 2; e++) {
+                    const float v = sc[nt][e];
+                    sc[nt][e] = (live && v != -INFINITY) ? expf(v - M) : 0.f;
+                    psum += sc[nt][e];
+                }
+            }
+            l_run = fmaf(al, l_run, psum);
+#pragma unroll
+            for (int n = 0; n < NT; n++) {
+                o[n][0] *= al;
+                o[n][1] *= al;
+                o[n][2] *= al;
+                o[n][3] *= al;
+            }
+            // P.V: k-tile kt = positions 8 kt .. 8 kt + 7 (P as the m16n8k8 A operand: row gl hi
+            // parts, row gl + 8 lo parts); V by ldmatrix.trans, matrix mi = dims 8 (4 q4 + mi) ..
+#pragma unroll
+            for (int kt = 0; kt < 8; kt++) {
+                uint32_t plo;
+                const uint32_t phi = pack_hi_lo(sc[kt][0], sc[kt][1], plo);
+                const int vr = 8 * kt + (lane & 7), mi = lane >> 3;
+                const bool vfresh = last && vr == tn;
+#pragma unroll
+                for (int q4 = 0; q4 < NT / 4; q4++) {
+                    const int c = 4 * q4 + mi;
+                    const uint32_t va = vfresh ? nv_a + c * 16 : vb + swz(vr, c);
+                    uint32_t b0, b1, b2, b3;
+                    ldsm_x4_trans(va, b0, b1, b2, b3);
+                    mma16808(o[4 * q4 + 0], phi, plo, b0);
+                    mma16808(o[4 * q4 + 1], phi, plo, b1);
+                    mma16808(o[4 * q4 + 2], phi, plo, b2);
+                    mma16808(o[4 * q4 + 3], phi, plo, b3);
+                }
+            }
             __syncwarp();
-            if (lane == 0) mbar_arrive(&fl_empty[d]);
+            if (lane == 0) mbar_arrive_n(&fl_empty[d], FL_WARPS);  // the page's only reader frees it
         }
-        // warp totals -> shared memory
+        // warp state of head gl -> shared memory
+        l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
+        l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
+        if (gl < G) {
+            float *wr = wm + (warp * G + gl) * (HD + 2);
 #pragma unroll
-        for (int o = 1; o < 32; o <<= 1) l_run += __shfl_xor_sync(0xffffffffu, l_run, o);
-        float *wr = wm + warp * (HD + 2);
-#pragma unroll
-        for (int k = 0; k < DPL / 2; k++) {
-            wr[2 + 2 * (lane + 32 * k)] = o_run[2 * k];
-            wr[2 + 2 * (lane + 32 * k) + 1] = o_run[2 * k + 1];
-        }
-        if (lane == 0) {
-            wr[0] = m_run;
-            wr[1] = l_run;
+            for (int n = 0; n < NT; n++) {
+                wr[2 + 8 * n + 2 * t] = o[n][0] + o[n][2];
+                wr[2 + 8 * n + 2 * t + 1] = o[n][1] + o[n][3];
+            }
+            if (t == 0) {
+                wr[0] = m_run;
+                wr[1] = l_run;
+            }
         }
         if (cbar_any(!ok || fl_abort)) return false;
-        // merge the WPH warps of each head (warp order); then finish or publish the split state
-        float *part = P.att_part + ((size_t)g * P.att_max_split + j) * G * (HD + 2);
+        mark(8);
+        // merge the eight warps of each head (warp order) into this split's state
+        uint64_t *mine = P.att_words + (((size_t)F.layer * P.n_kv + g) * P.att_max_split + j) * G * (HD + 2);
         for (int i = tid; i < G * (HD + 2); i += FL_CONSUMERS) {
             const int h = i / (HD + 2), e = i % (HD + 2);
             float M = -INFINITY;
 #pragma unroll
-            for (int w = 0; w < WPH; w++) M = fmaxf(M, wm[(h * WPH + w) * (HD + 2)]);
-            float acc = 0.f;
-            if (e == 0) {
-                acc = M;
-            } else {
+            for (int w = 0; w < FL_WARPS; w++) M = fmaxf(M, wm[(w * G + h) * (HD + 2)]);
+            float acc = 0.f, L = 0.f;
 #pragma unroll
-                for (int w = 0; w < WPH; w++) {
-                    const float mw = wm[(h * WPH + w) * (HD + 2)];
-                    if (mw == -INFINITY) continue;
-                    acc = fmaf(expf(mw - M), wm[(h * WPH + w) * (HD + 2) + e], acc);
-                }
+            for (int w = 0; w < FL_WARPS; w++) {
+                const float *st = wm + (w * G + h) * (HD + 2);
+                if (st[0] == -INFINITY) continue;  // a warp without valid positions
+                const float f = expf(st[0] - M);
+                L = fmaf(f, st[1], L);
+                if (e >= 2) acc = fmaf(f, st[e], acc);
             }
+            const float v = e == 0 ? M : (e == 1 ? L : acc);
             if (S == 1) {
-                if (e >= 2) {
-                    const float L = [&] {
-                        float l = 0.f;
-#pragma unroll
-                        for (int w = 0; w < WPH; w++) {
-                            const float mw = wm[(h * WPH + w) * (HD + 2)];
-                            if (mw != -INFINITY) l = fmaf(expf(mw - M), wm[(h * WPH + w) * (HD + 2) + 1], l);
-                        }
-                        return l;
-                    }();
-                    ll_store(F.out + (size_t)(g * G + h) * HD + (e - 2), acc / L, tag);
-                }
+                if (e >= 2) ll_store(F.out + (size_t)(g * G + h) * HD + (e - 2), acc / L, tag);
+            } else if (j > 0) {
+                ll_store(mine + i, v, tag);  // split j's state, taken by split 0
             } else {
-                part[i] = acc;
+                raw[i] = v;  // split 0 keeps its own state here (raw is no longer needed)
             }
         }
-        if (S == 1) return true;
-        cbar();
-        if (tid == 0) {
-            __threadfence();
-            fl_ticket = atomicAdd(P.att_tick + g, 1u);
+        if (S == 1 || j > 0) {
+            mark(9);
+            return true;
         }
-        cbar();
-        if (fl_ticket != (unsigned int)(S - 1)) return true;
-        // last split of this KV head: merge the S states in split order
-        __threadfence();
-        if (tid == 0) atomicExch(P.att_tick + g, 0u);
-        const float *pg0 = P.att_part + (size_t)g * P.att_max_split * G * (HD + 2);
+        // split 0: take the other splits' states as they arrive, merge all S in split order
+        const bool got2 = fl_poll(P, mine + G * (HD + 2), others, (S - 1) * G * (HD + 2), tag);
+        if (cbar_any(!got2 || fl_abort)) return false;
         for (int i = tid; i < G * HD; i += FL_CONSUMERS) {
             const int h = i / HD, e = i % HD;
+            auto st = [&](int jj) { return jj == 0 ? raw + h * (HD + 2) : others + ((jj - 1) * G + h) * (HD + 2); };
             float M = -INFINITY;
-            for (int jj = 0; jj < S; jj++) M = fmaxf(M, __ldcg(pg0 + ((size_t)jj * G + h) * (HD + 2)));
+            for (int jj = 0; jj < S; jj++) M = fmaxf(M, st(jj)[0]);
             float L = 0.f, O = 0.f;
             for (int jj = 0; jj < S; jj++) {
-                const float *st = pg0 + ((size_t)jj * G + h) * (HD + 2);
-                const float mj = __ldcg(st);
-                if (mj == -INFINITY) continue;
-                const float f = expf(mj - M);
-                L = fmaf(f, __ldcg(st + 1), L);
-                O = fmaf(f, __ldcg(st + 2 + e), O);
+                const float *q = st(jj);
+                if (q[0] == -INFINITY) continue;
+                const float f = expf(q[0] - M);
+                L = fmaf(f, q[1], L);
+                O = fmaf(f, q[2 + e], O);
             }
             ll_store(F.out + (size_t)(g * G + h) * HD + e, O / L, tag);
         }
+        mark(9);
         return true;
     }
 };
@@ -726,15 +866,17 @@ __device__ __noinline__ void fl_producer(const FParams &P, int pos, int nch, int
     uint8_t *ring = fl_ring();
     int head = 0, used = 0, need[FL_NDESC];
     long long seq = 0, oldest = 0, pwait = 0;
-    auto reserve = [&](int size, int &d) -> uint8_t * {
-        int skip;
+    auto reserve = [&](int size, int align, int &d) -> uint8_t * {
+        int skip, start;
         bool wrap;
         for (;;) {
             if (seq == oldest) head = 0;  // ring empty: restart at the front
-            // a tile that does not fit before the end starts at the front; the bytes up to
-            // the end (none when the last tile ended exactly there) are charged to it
-            wrap = head + size > P.ring_bytes;
-            skip = wrap ? P.ring_bytes - head : 0;
+            // an item that does not fit before the end starts at the front; the bytes up to
+            // its (aligned) start, or up to the end, are charged to it
+            start = (head + align - 1) & ~(align - 1);
+            wrap = start + size > P.ring_bytes;
+            if (wrap) start = 0;
+            skip = wrap ? P.ring_bytes - head : start - head;
             if (seq - oldest < FL_NDESC && used + skip + size <= P.ring_bytes) break;
             const int od = (int)(oldest % FL_NDESC);
             const long long w0 = clock64();
@@ -747,9 +889,8 @@ __device__ __noinline__ void fl_producer(const FParams &P, int pos, int nch, int
             used -= need[od];
             oldest++;
         }
-        if (wrap) head = 0;
-        uint8_t *dst = ring + head;
-        head += size;
+        uint8_t *dst = ring + start;
+        head = start + size;
         d = (int)(seq % FL_NDESC);
         need[d] = skip + size;
         used += skip + size;
@@ -768,13 +909,15 @@ __device__ __noinline__ void fl_producer(const FParams &P, int pos, int nch, int
                 const int p0 = (int)((long long)j * nch / S), p1 = (int)((long long)(j + 1) * nch / S);
                 for (int pg = p0; pg < p1 && !fl_abort; pg++) {
                     int d;
-                    uint8_t *dst = reserve(2 * PAGE, d);
+                    uint8_t *dst = reserve(2 * PAGE, 1024, d);  // swizzled boxes: 1024-byte aligned
                     if (!dst) break;
-                    const size_t base =
-                        (((size_t)P.page_table[pg] * P.n_layers + F.layer) * P.n_kv + g) * (size_t)ATTN_P * HD;
+                    const int row = ((P.page_table[pg] * P.n_layers + F.layer) * P.n_kv + g) * ATTN_P;
                     mbar_expect_tx(&fl_full[d], 2 * PAGE);
-                    bulk_g2s(dst, P.k_pool + base, PAGE, &fl_full[d]);
-                    bulk_g2s(dst + PAGE, P.v_pool + base, PAGE, &fl_full[d]);
+#pragma unroll
+                    for (int h = 0; h < HD / 64; h++) {
+                        tma_load_2d(dst + h * 64 * 128, &P.kmap, 64 * h, row, &fl_full[d]);
+                        tma_load_2d(dst + PAGE + h * 64 * 128, &P.vmap, 64 * h, row, &fl_full[d]);
+                    }
                     seq++;
                 }
             }
@@ -784,7 +927,7 @@ __device__ __noinline__ void fl_producer(const FParams &P, int pos, int nch, int
                 fl_locate(F, tile, s, lt);
                 const PSeg &Sg = F.seg[s];
                 int d;
-                uint8_t *dst = reserve(tile_bytes_of(Sg, F.nmat), d);
+                uint8_t *dst = reserve(tile_bytes_of(Sg, F.nmat), 16, d);
                 if (!dst) break;
                 // plain-copied tail first, then the arrive (release), then the bulk copies
                 const int r0 = lt * TC_M, nrows = min(TC_M, Sg.rows - r0);
@@ -846,14 +989,20 @@ __global__ void __launch_bounds__(FL_THREADS, 1) decode_flow_kernel(const __grid
 
     const bool pos_ok = pos >= 0 && pos < P.max_seq;
     const int nch = pos_ok ? pos / ATTN_P + 1 : 0;
+    if (pos_ok && tid < HD / 2) fl_rope[tid] = __ldg(P.rope + (size_t)pos * (HD / 2) + tid);
     const int S = fl_att_splits(P, nch);
     if (!pos_ok && tid == 0 && blockIdx.x == 0) *P.io_err = 1;
 
+    if (warp >= FL_WARPS) {
+        asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(FL_REG_PRODUCER));
+    } else {
+        asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(FL_REG_CONSUMER));
+    }
     if (!pos_ok) {
         // nothing to decode (the host checks positions before launching; this is the
         // device-side guard): every phase is skipped, the tag still advances
-    } else if (warp == FL_WARPS) {
-        if (lane == 0) fl_producer<HD>(P, pos, nch, S);
+    } else if (warp >= FL_WARPS) {
+        if (tid == FL_CONSUMERS) fl_producer<HD>(P, pos, nch, S);
     } else {
         long long seq = 0;
         const int units = P.n_kv * S;
@@ -872,7 +1021,7 @@ __global__ void __launch_bounds__(FL_THREADS, 1) decode_flow_kernel(const __grid
             const long long c0 = clock64();
             bool ok = true;
             if (F.kind == FL_ATTN) {
-                if (nch > 0 && u < units) ok = FlowAttn<HD, G>::unit(P, F, u / S, u % S, S, pos, nch, seq, tag, wcycles);
+                if (nch > 0 && u < units) ok = FlowAttn<HD, G>::unit(P, F, u / S, u % S, S, pos, nch, seq, tag, wcycles, tr);
             } else if ((int)blockIdx.x < F.stage_ctas) {
                 ok = fl_stage(P, F, tag, token0, tr);
                 if (ok) {

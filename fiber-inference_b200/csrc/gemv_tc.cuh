@@ -87,6 +87,29 @@ FDEV uint32_t pack_f16x2(float lo, float hi) {  // lo -> bits 0..15, hi -> bits 
     asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
     return d;
 }
+FDEV uint32_t prmt_b32(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t d;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+    return d;
+}
+FDEV uint32_t hsub2_u(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+FDEV uint32_t hmul2_u(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+// d * (fp16 low half of h) + c in fp32, one rounding
+FDEV float mixed_fma_lo(uint32_t h, uint16_t d16, float c) {
+    float r;
+    asm("{\n .reg .f16 l, h;\n mov.b32 {l, h}, %1;\n fma.rn.f32.f16 %0, %2, l, %3;\n}\n"
+        : "=f"(r)
+        : "r"(h), "h"(d16), "f"(c));
+    return r;
+}
 FDEV uint32_t h2_splat(float v) {  // exact for the small integers used here
     const __half h = __float2half_rn(v);
     const uint32_t u = __half_as_ushort(h);
@@ -206,22 +229,39 @@ struct TcDot<T_Q4_K> {
         uint32_t w[8];
     };
 
+    // Lane t's two sub-blocks 2t, 2t+1: their 6-bit scales as the byte pair scp
+    // (lo, hi) and mins as mp, then every constant by exact fp16 arithmetic on
+    // 1024 + n (byte permutes, no integer-to-float conversions):
+    // A_lo = (sc, sc), B_lo = -1024 sc, A_hi = sc'/16, B_hi = -64 sc',
+    // c = -dmin * m as one exact mixed-precision product.
     static FDEV void load_row(const uint8_t *blk, int t, Row &r) {
         const uint4 hdr = *reinterpret_cast<const uint4 *>(blk);
         const uint4 q0 = *reinterpret_cast<const uint4 *>(blk + 16 + 32 * t);
         const uint4 q1 = *reinterpret_cast<const uint4 *>(blk + 32 + 32 * t);
         r.w[0] = q0.x; r.w[1] = q0.y; r.w[2] = q0.z; r.w[3] = q0.w;
         r.w[4] = q1.x; r.w[5] = q1.y; r.w[6] = q1.z; r.w[7] = q1.w;
-        int sl, ml, sh, mh;
-        scales(hdr, t, sl, ml, sh, mh);
+        const int sh = 16 * (t & 1);
+        const uint32_t A = hdr.y >> sh, B = hdr.z >> sh, C = hdr.w >> sh;
+        uint32_t scp, mp;
+        if (t < 2) {  // sub-blocks 0..3: low 6 bits of bytes 0..3 / 4..7
+            scp = A & 0x3F3Fu;
+            mp = B & 0x3F3Fu;
+        } else {      // sub-blocks 4..7: nibbles of bytes 8..11, top bits of bytes 0..7
+            scp = (C & 0x0F0Fu) | ((A >> 2) & 0x3030u);
+            mp = ((C >> 4) & 0x0F0Fu) | ((B >> 2) & 0x3030u);
+        }
+        constexpr uint32_t M1024 = 0x64006400u;
+        const uint32_t sl2 = hsub2_u(prmt_b32(scp, 0x64646464u, 0x4040u), M1024);   // (sc, sc)
+        const uint32_t sh2 = hsub2_u(prmt_b32(scp, 0x64646464u, 0x4141u), M1024);   // (sc', sc')
+        const uint32_t mneg = hsub2_u(M1024, prmt_b32(mp, 0x64646464u, 0x4140u));  // (-m, -m')
+        r.A_lo = sl2;
+        r.B_lo = hmul2_u(sl2, 0xE400E400u);  // x -1024
+        r.A_hi = hmul2_u(sh2, 0x2C002C00u);  // x 1/16
+        r.B_hi = hmul2_u(sh2, 0xD400D400u);  // x -64
+        const uint16_t dmin16 = (uint16_t)(hdr.x >> 16);
+        r.c_lo = mixed_fma_lo(mneg, dmin16, 0.0f);
+        r.c_hi = mixed_fma_lo(mneg >> 16, dmin16, 0.0f);
         r.d16 = (uint16_t)(hdr.x & 0xFFFF);
-        const float dmin = h2f(hdr.x >> 16);
-        r.A_lo = h2_splat((float)sl);
-        r.B_lo = h2_splat(-1024.0f * (float)sl);
-        r.A_hi = h2_splat((float)sh * 0.0625f);
-        r.B_hi = h2_splat(-64.0f * (float)sh);
-        r.c_lo = -__fmul_rn(dmin, (float)ml);
-        r.c_hi = -__fmul_rn(dmin, (float)mh);
     }
 
     // fragments (a0a1 for step 2u, a4a5 for step 2u, a0a1 for step 2u+1, a4a5 for step 2u+1)
@@ -244,10 +284,12 @@ struct TcDot<T_Q4_K> {
         f3 = pack_f16x2(a, b);
     }
 
+    // two accumulator chains (even / odd k-steps), added at the end
     static FDEV void run(const uint8_t *rowg, const uint8_t *rowg8, const uint2 *xf, int g, int t, float (&acc)[4]) {
         Row ra, rb;
         load_row(rowg, t, ra);
         load_row(rowg8, t, rb);
+        float acc2[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int u = 0; u < 8; u++) {
             uint32_t a0, a4, a0n, a4n, b0, b4, b0n, b4n;
@@ -259,8 +301,10 @@ struct TcDot<T_Q4_K> {
                 x1 = xf[((2 * u + 1) * 4 + t) * 2 + g];
             }
             mma16816(acc, a0, b0, a4, b4, x0.x, x0.y);
-            mma16816(acc, a0n, b0n, a4n, b4n, x1.x, x1.y);
+            mma16816(acc2, a0n, b0n, a4n, b4n, x1.x, x1.y);
         }
+#pragma unroll
+        for (int i = 0; i < 4; i++) acc[i] += acc2[i];
     }
 };
 

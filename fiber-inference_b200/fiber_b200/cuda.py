@@ -31,6 +31,7 @@ EXPORTED = [
     "gpu_get_logits", "gpu_forward_classifier", "gpu_get_device", "kv_cache_init", "kv_cache_init_paged",
     "kv_cache_free", "kv_cache_write", "kv_cache_read", "fiber_gemv_argmax_noalloc", "fiber_prefill_slot",
     "fiber_decode_greedy_batch", "fiber_sample", "fiber_decode_sample", "fiber_tp_collective", "fiber_set_max_batch",
+    "fiber_step_ring_bytes",
 ]
 
 
@@ -79,6 +80,7 @@ def cuda_lib() -> C.CDLL:
         L.fiber_decode_greedy.argtypes = [C.c_void_p, C.c_void_p, C.c_int32, C.c_int, C.c_int, C.c_void_p,
                                           C.c_void_p]
         L.fiber_step_launches.argtypes = [C.c_void_p]
+        L.fiber_step_ring_bytes.argtypes = [C.c_void_p]
         L.fiber_set_decode_mode.argtypes = [C.c_void_p, C.c_int]
         L.fiber_get_decode_mode.argtypes = [C.c_void_p]
         L.fiber_tp_plan.argtypes = [C.c_void_p, C.c_int, C.c_int, C.POINTER(TPPlan)]
@@ -340,6 +342,11 @@ class Context:
     def mode(self) -> int:
         return int(cuda_lib().fiber_get_decode_mode(self.h))
 
+    @property
+    def ring_bytes(self) -> int:
+        """Bytes of the shared-memory ring of the current one-kernel decode mode (0 in mode 1)."""
+        return int(cuda_lib().fiber_step_ring_bytes(self.h))
+
     def step_launches(self) -> int:
         n = cuda_lib().fiber_step_launches(self.h)
         if n < 0:
@@ -350,7 +357,7 @@ class Context:
                     "t_producer_done_ns", "cyc_producer_wait", "cyc_attn_qkv", "cyc_attn_pages"]
 
     FLOW_TRACE_FIELDS = ["t_start_ns", "cyc_poll", "cyc_stage", "cyc_phase", "cyc_wait_ring", "t_end_ns",
-                         "t_producer_done_ns", "cyc_producer_wait"]
+                         "t_producer_done_ns", "cyc_producer_wait", "cyc_attn_pages", "cyc_attn_merge"]
 
     def trace_step(self, kv: KVCache, token: int, pos: int, max_phases: int = 4096, max_ctas: int = 1024):
         """Per-phase, per-CTA timeline of one one-kernel step: uint64 array

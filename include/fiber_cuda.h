@@ -133,6 +133,12 @@ int fiber_get_decode_mode(fiber_ctx_t *ctx);
 /* Number of kernels one decode step launches (all of them this library's own). */
 int fiber_step_launches(fiber_ctx_t *ctx);
 
+/* Bytes of the shared-memory weight / KV ring the current one-kernel decode mode
+ * streams through (0 in mode 1). No counterpart in the reference: the ring is how
+ * the one-kernel steps stage weights; tests use it to check a requested ring size
+ * (FIBER_PK_RING_KB / FIBER_FL_RING_KB) is the one in use. */
+int fiber_step_ring_bytes(fiber_ctx_t *ctx);
+
 /* ---- tensor parallelism (one process per GPU) ------------------------------------ */
 
 #define FIBER_TP_ID_BYTES 128
@@ -233,7 +239,7 @@ int fiber_gemv_host(int ggml_type, const void *d_w, const float *h_x, float *h_y
 
 /* ---- allocation-free greedy lm_head step ----------------------------------------
  * No counterpart in the reference. Same result as fiber_gemv followed by a greedy
- * argmax (first index of the maximum, src/sampler.c:38-46): d_y = W.x and
+ * argmax (the first index of the maximum; index 0 when every value is NaN): d_y = W.x and
  * *d_argmax, both device memory, enqueued on `stream`. It exists for callers that
  * cannot allocate device memory where they run the step: a host application
  * whose own pool owns all device memory and forbids further cudaMalloc, or a

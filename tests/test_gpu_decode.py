@@ -220,6 +220,7 @@ def test_ring_filled_exactly_by_attention_pages(tiny_model, monkeypatch, ring_kb
     path = tiny_model("q6k")
     hm = fb.HostModel(path)
     a = _ctx(hm, 256, mode)
+    assert a.ring_bytes == ring_kb * 1024, "the requested ring is not the one in use"
     b = _ctx(hm, 256, 1)
     ka, kb = a.kv(256), b.kv(256)
     toks = _prompt(hm.params.vocab_size, 200, 11)

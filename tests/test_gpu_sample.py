@@ -20,6 +20,15 @@ def _host_draws(logits_rows, temperature, top_k, top_p):
     return [int(fb.host().sampler_sample(C.byref(st), np.ascontiguousarray(r))) for r in logits_rows]
 
 
+def _ref_draws(logits_rows, temperature, top_k, top_p):
+    """The reference's own sampler_sample (src/sampler.c, compiled into oracle/_ref)."""
+    from oracle import oracle as orc
+
+    st = fb.Sampler()  # same layout as the reference's sampler_t (src/sampler.h)
+    orc.ref().sampler_init(C.addressof(st), logits_rows.shape[1], temperature, top_k, top_p)
+    return [int(orc.ref().sampler_sample(C.addressof(st), np.ascontiguousarray(r))) for r in logits_rows]
+
+
 def _device_draws(logits_rows, temperature, top_k, top_p):
     """Row i drawn with the state left by rows 0..i-1 (one row at a time, one state)."""
     import torch
@@ -44,7 +53,12 @@ def test_device_draws_equal_host_draws(V, temperature, top_k, top_p):
     rows = (rng.standard_normal((40, V)) * 2.5).astype(np.float32)
     rows[:, 7] = rows[:, 3]  # ties: equal values keep index order
     rows[::3, 11] = rows[::3].max(axis=1)  # a tie at the top in some rows
-    assert _device_draws(rows, temperature, top_k, top_p) == _host_draws(rows, temperature, top_k, top_p)
+    got = _device_draws(rows, temperature, top_k, top_p)
+    assert got == _host_draws(rows, temperature, top_k, top_p)
+    from oracle import oracle as orc
+
+    if orc.ref_available():  # and the reference's own compiled sampler.c
+        assert got == _ref_draws(rows, temperature, top_k, top_p)
 
 
 def test_batched_rows_and_limits():
@@ -62,13 +76,14 @@ def test_batched_rows_and_limits():
         fb.sample_device(d_lg.data_ptr(), 8, V, V, 0.8, 2000, 0.9, d_rng.data_ptr(), d_out.data_ptr())
 
 
-@pytest.mark.parametrize("mode", [0, 1])
+@pytest.mark.parametrize("mode", [0, 1, 2])
 def test_sampling_decode_loop_equals_host_loop(tiny_model, mode):
     hm = fb.HostModel(tiny_model("q4km"))
     ctx = fb.Context(hm, max_seq=256)
-    if mode == 0 and ctx.mode != 0:
-        pytest.skip("the persistent step kernel does not cover this model")
-    ctx.set_mode(mode)
+    try:
+        ctx.set_mode(mode)
+    except fb.FiberError:
+        pytest.skip(f"decode mode {mode} does not cover this model")
     kv = ctx.kv(256)
     prompt = np.random.default_rng(5).integers(1, hm.params.vocab_size, 12).astype(np.int32)
     first = ctx.prefill(kv, prompt)

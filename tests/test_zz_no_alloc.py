@@ -7,8 +7,8 @@ static device array. This file is named to be collected last so that a run
 stopping at the first failure has run every other test before it.
 
 The check: two calls in a row through the C-ABI give the same logits as the
-existing fiber_gemv entry point (within the GEMV tolerance used elsewhere) and the
-first index of their maximum.
+existing fiber_gemv entry point and as the CPU oracle's GEMV (within the GEMV
+tolerance used elsewhere), and the first index of their maximum.
 """
 from __future__ import annotations
 
@@ -38,6 +38,9 @@ def test_noalloc_matches_existing_gemv_twice(t, rows, cols):
     fb.gemv(t, dw.data_ptr(), dx.data_ptr(), y_ref.data_ptr(), rows, cols)
     torch.cuda.synchronize()
     ref = y_ref.cpu().numpy()
+    from oracle import oracle as orc
+
+    want = orc.gemv(t, blocks, x, rows, cols)  # the oracle: dequant.h weights, fp32 dot products
     for call in range(2):
         y = torch.full((rows,), float("nan"), dtype=torch.float32, device="cuda")
         am = torch.full((1,), -1, dtype=torch.int32, device="cuda")
@@ -48,6 +51,8 @@ def test_noalloc_matches_existing_gemv_twice(t, rows, cols):
         assert np.abs(got - ref).max() < 1e-4 * (np.abs(ref).max() + 1), call
         assert int(am.item()) == int(np.argmax(got)), call
         assert int(am.item()) == int(np.argmax(ref)), call
+        assert _rel_rms(got, want) < REL_RMS, call
+        assert int(am.item()) == int(np.argmax(want)), call
 
 
 def test_noalloc_rejects_rows_beyond_limit():
