@@ -689,6 +689,8 @@ static int flow_build(gpu_context *c) {
     FL_CASE(64, 1) FL_CASE(64, 2) FL_CASE(64, 4) FL_CASE(64, 8)
     FL_CASE(128, 1) FL_CASE(128, 2) FL_CASE(128, 4) FL_CASE(128, 8)
 #undef FL_CASE
+    // per-chunk fragment scales are kept for at most FL_MAX_CHUNKS chunks of 256 inputs
+    if (dim / 256 > FL_MAX_CHUNKS || ffn / 256 > FL_MAX_CHUNKS) types_ok = false;
     if (!types_ok || !c->fl_kernel) return FIBER_OK;
     int sms = 0;
     CK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, c->device));

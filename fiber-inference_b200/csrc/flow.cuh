@@ -122,7 +122,9 @@ __shared__ unsigned long long fl_best;   // this CTA's best logit key
 __shared__ int fl_tile_off[FL_NDESC];
 __shared__ volatile int fl_abort;
 __shared__ unsigned int fl_ticket;
-__shared__ float fl_scale[2];            // staged input: fragment scale, its inverse
+constexpr int FL_MAX_CHUNKS = 64;        // input length / 256 at most (16384 elements)
+__shared__ float fl_cinv[FL_MAX_CHUNKS]; // staged input: per-chunk inverse fragment scale
+__shared__ float fl_wss[FL_WARPS];       // staged input: per-warp sums of x^2 (RMSNorm)
 __shared__ float2 fl_rope[64];           // RoPE (cos, sin) row of this launch's position
 
 FDEV uint8_t *fl_ring() { return fl_dyn + ((FL_RING_PAD - (smem_u32(fl_dyn) & (FL_RING_PAD - 1))) & (FL_RING_PAD - 1)); }
@@ -287,20 +289,23 @@ FDEV float fl_rem(uint32_t h, float v) {
     return r;
 }
 
-// Fragments of the staged input for weight type T (the k-slot order TcDot<T> reads,
-// TcType<T>::elem): per group f the fp16 hi parts of its four elements, then the lo
-// parts (hi + lo carries ~22 bits), v = (x * rrms) * w * scale where the phase has an
-// RMSNorm. Two packed conversions per pair of elements (hi, then the exact remainder).
+// Fragments of chunk b (elements 256b .. 256b+255) of the staged input for weight
+// type T (the k-slot order TcDot<T> reads, TcType<T>::elem): per group f the fp16 hi
+// parts of its four elements, then the lo parts (hi + lo carries ~22 bits), v = x * w *
+// scale where the phase has an RMSNorm (w its weights; rrms is applied to the dot
+// products), else x * scale. Lanes of one warp, two groups each.
 template <int T>
-FDEV void fl_frags(int nb, const float *xs, const float *nw, float rrms, float scale, uint2 *xf) {
-    for (int f = threadIdx.x; f < nb * 64; f += FL_CONSUMERS) {
-        const int b = f >> 6, s = (f >> 2) & 15, t = f & 3;
+FDEV void fl_frags_chunk(int b, const float *xs, const float *nw, float scale, uint2 *xf) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int j = 0; j < 2; j++) {
+        const int f = b * 64 + lane + 32 * j, s = (f >> 2) & 15, t = f & 3;
         float v[4];
 #pragma unroll
         for (int i = 0; i < 4; i++) {
             const int k = b * 256 + TcType<T>::elem(t, s, i);
             float x = xs[k];
-            if (nw) x = __fmul_rn(__fmul_rn(x, rrms), nw[k]);
+            if (nw) x = __fmul_rn(x, nw[k]);
             v[i] = x * scale;
         }
         const uint32_t h01 = pack_f16x2(v[0], v[1]), h23 = pack_f16x2(v[2], v[3]);
@@ -313,75 +318,155 @@ FDEV void fl_frags(int nb, const float *xs, const float *nw, float rrms, float s
 
 // ---- GEMV phase -----------------------------------------------------------------------
 
-// Stage the phase input: poll (or decode the embedding row), RMSNorm scale, fragments
-// for each weight type of the phase. All consumer threads. Returns false when stopped.
-__device__ __noinline__ bool fl_stage(const FParams &P, const FPhase &F, uint32_t tag, int token,
-                                      unsigned long long *tr) {
-    const int tid = threadIdx.x;
+// Stage this warp's chunks of the phase input: chunk b (256 elements) is staged by warp
+// b % 8, the warp that multiplies super-block column b of every tile, so no other warp
+// waits for it. Per chunk: poll its tagged words (or decode the embedding row), keep
+// the fp32 values (the residual of the next residual phase), add x^2 in a fixed order
+// to this warp's RMSNorm sum (fl_wss[warp], read by the epilogues), choose the power of
+// two s_b that puts the chunk's largest |x * w| into [2^13, 2^14) (fl_cinv[b] = 1 / s_b, applied to
+// the chunk's dot products) and write its fragments for each weight type of the phase.
+// Two chunks at a time (eight 16-byte loads in flight per lane). Warp-level; returns
+// false (warp-uniform) when stopped.
+__device__ __noinline__ bool fl_stage_warp(const FParams &P, const FPhase &F, uint32_t tag, int token,
+                                           unsigned long long *tr) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n = F.cols, nb = n >> 8;
     const bool norm = F.norm_w != nullptr;
     float *xs = norm ? fl_xres(P) : fl_xin(P);
     float *nw = fl_nw(P);
-    long long c0 = clock64();
-    if (norm)
-        for (int i = tid; i < (n >> 2); i += FL_CONSUMERS) cp_async16(nw + 4 * i, F.norm_w + 4 * i);
-    if (F.embed_in) {  // every CTA decodes the embedding row itself (src/gpu_ffn.m:466-482)
-        int tok = token;
-        if (tok < 0 || tok >= P.vocab) {
-            if (tid == 0 && blockIdx.x == 0) *P.io_err = 2;
-            tok = 0;
-        }
-        for (int i = tid; i < n; i += FL_CONSUMERS) {
-            float v;
-            switch (P.embd_type) {
-            case T_F16: v = h2f(reinterpret_cast<const uint16_t *>(P.embd)[(size_t)tok * n + i]); break;
-            case T_F32: v = round_f16(reinterpret_cast<const float *>(P.embd)[(size_t)tok * n + i]); break;
-            case T_Q4_K: v = round_f16(decode_elem<T_Q4_K>(P.embd + ((size_t)tok * nb + (i >> 8)) * 144, i & 255)); break;
-            case T_Q5_K: v = round_f16(decode_elem<T_Q5_K>(P.embd + ((size_t)tok * nb + (i >> 8)) * 176, i & 255)); break;
-            default: v = round_f16(decode_elem<T_Q6_K>(P.embd + ((size_t)tok * nb + (i >> 8)) * 210, i & 255)); break;
-            }
-            xs[i] = v;
-        }
-    }
-    const bool ok = F.embed_in || fl_poll(P, F.in, xs, n, tag);
-    cp_async_wait_all();
-    if (cbar_any(!ok || fl_abort)) return false;
-    if (tr) tr[1] = (unsigned long long)(clock64() - c0);
-    c0 = clock64();
-    // sums of squares (RMSNorm) and the largest |x * w| (fragment scale)
-    float ss = 0.f, mx = 0.f;
-    for (int i = tid; i < n; i += FL_CONSUMERS) {
-        const float v = xs[i];
-        ss = fmaf(v, v, ss);
-        mx = fmaxf(mx, fabsf(norm ? v * nw[i] : v));
-    }
-    fl_reduce2(ss, mx);
-    const float rrms = norm ? 1.0f / sqrtf(ss / (float)n + F.eps) : 1.0f;
-    if (!(mx < 3.0e38f) || !(rrms < 3.0e38f)) {  // non-finite activations
-        if (tid == 0) *P.io_err = 5;
-        mx = 1.0f;
-    }
-    float scale, inv;
-    fl_set_scale(norm ? mx * rrms * 1.001f : mx, scale, inv);
-    if (tid == 0) {
-        fl_scale[0] = scale;
-        fl_scale[1] = inv;
-    }
     int type_b = -1;
     for (int k = 1; k < F.nseg; k++)
         if (F.seg[k].type != F.seg[0].type && type_b < 0) type_b = F.seg[k].type;
     uint2 *xf0 = fl_frag(P), *xf1 = xf0 + (size_t)nb * 128;
-    for (int pass = 0; pass < (type_b >= 0 ? 2 : 1); pass++) {
-        uint2 *dst = pass ? xf1 : xf0;
-        switch (pass ? type_b : F.seg[0].type) {
-        case T_Q4_K: fl_frags<T_Q4_K>(nb, xs, norm ? nw : nullptr, rrms, scale, dst); break;
-        case T_Q6_K: fl_frags<T_Q6_K>(nb, xs, norm ? nw : nullptr, rrms, scale, dst); break;
-        default: fl_frags<T_F16>(nb, xs, norm ? nw : nullptr, rrms, scale, dst); break;
-        }
+    int tok = token;
+    if (F.embed_in && (tok < 0 || tok >= P.vocab)) {
+        if (threadIdx.x == 0 && blockIdx.x == 0) *P.io_err = 2;
+        tok = 0;
     }
-    cbar();
-    if (tr) tr[2] = (unsigned long long)(clock64() - c0);
+    float ss = 0.f;
+    long long cpoll = 0, cstage = 0;
+    for (int b0 = warp; b0 < nb; b0 += 2 * FL_WARPS) {
+        const int nc = b0 + FL_WARPS < nb ? 2 : 1;  // chunks b0 and b0 + 8
+        long long c0 = clock64();
+        if (norm)
+            for (int c = 0; c < nc; c++) {
+                const int b = b0 + c * FL_WARPS;
+                cp_async16(nw + b * 256 + 4 * lane, F.norm_w + b * 256 + 4 * lane);
+                cp_async16(nw + b * 256 + 128 + 4 * lane, F.norm_w + b * 256 + 128 + 4 * lane);
+            }
+        if (F.embed_in) {  // every CTA decodes the embedding row itself (src/gpu_ffn.m:466-482)
+            for (int c = 0; c < nc; c++) {
+                const int b = b0 + c * FL_WARPS;
+                for (int e = lane; e < 256; e += 32) {
+                    const int i = b * 256 + e;
+                    float v;
+                    switch (P.embd_type) {
+                    case T_F16: v = h2f(reinterpret_cast<const uint16_t *>(P.embd)[(size_t)tok * n + i]); break;
+                    case T_F32: v = round_f16(reinterpret_cast<const float *>(P.embd)[(size_t)tok * n + i]); break;
+                    case T_Q4_K: v = round_f16(decode_elem<T_Q4_K>(P.embd + ((size_t)tok * nb + b) * 144, e)); break;
+                    case T_Q5_K: v = round_f16(decode_elem<T_Q5_K>(P.embd + ((size_t)tok * nb + b) * 176, e)); break;
+                    default: v = round_f16(decode_elem<T_Q6_K>(P.embd + ((size_t)tok * nb + b) * 210, e)); break;
+                    }
+                    xs[i] = v;
+                }
+            }
+        } else {
+            // pair k of the group: chunk b0 + 8 (k / 4), words 2 (lane + 32 (k % 4)) + {0, 1}
+            ulonglong2 w[8];
+            uint32_t pend = 0;
+#pragma unroll
+            for (int k = 0; k < 8; k++) {
+                if (k < 4 * nc) {
+                    const int b = b0 + (k >> 2) * FL_WARPS;
+                    w[k] = ll_load2(F.in + b * 256 + 2 * (lane + 32 * (k & 3)));
+                    pend |= 1u << k;
+                }
+            }
+            unsigned long long t0 = 0;
+            for (long long it = 0;; it++) {
+#pragma unroll
+                for (int k = 0; k < 8; k++) {
+                    if ((pend >> k) & 1u) {
+                        if ((uint32_t)(w[k].x >> 32) == tag && (uint32_t)(w[k].y >> 32) == tag) {
+                            const int b = b0 + (k >> 2) * FL_WARPS;
+                            const float v0 = __uint_as_float((uint32_t)w[k].x), v1 = __uint_as_float((uint32_t)w[k].y);
+                            *reinterpret_cast<float2 *>(xs + b * 256 + 2 * (lane + 32 * (k & 3))) = make_float2(v0, v1);
+                            pend &= ~(1u << k);
+                        }
+                    }
+                }
+                if (__all_sync(0xffffffffu, pend == 0)) break;
+                if (it == 0) {
+                    t0 = gtimer();
+                } else if ((it & 15) == 0) {
+                    int stop = fl_abort || gtimer() - t0 > FL_WAIT_NS;
+                    stop = __any_sync(0xffffffffu, stop);
+                    if (stop) {
+                        if (lane == 0) fl_fail(P);
+                        cp_async_wait_all();
+                        return false;
+                    }
+                }
+#pragma unroll
+                for (int k = 0; k < 8; k++)
+                    if ((pend >> k) & 1u) {
+                        const int b = b0 + (k >> 2) * FL_WARPS;
+                        w[k] = ll_load2(F.in + b * 256 + 2 * (lane + 32 * (k & 3)));
+                    }
+            }
+        }
+        cp_async_wait_all();
+        __syncwarp();
+        const long long c1 = clock64();
+        cpoll += c1 - c0;
+        for (int c = 0; c < nc; c++) {
+            const int b = b0 + c * FL_WARPS;
+            float mx = 0.f;
+#pragma unroll
+            for (int e = 0; e < 8; e++) {  // fixed order: the sums do not depend on arrival order
+                const int i = b * 256 + lane + 32 * e;
+                const float x = xs[i];
+                ss = fmaf(x, x, ss);
+                mx = fmaxf(mx, fabsf(norm ? x * nw[i] : x));
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+            if (!(mx < 3.0e38f)) {  // non-finite activations
+                if (lane == 0) *P.io_err = 5;
+                mx = 1.0f;
+            }
+            float scale, inv;
+            fl_set_scale(mx, scale, inv);
+            if (lane == 0) fl_cinv[b] = inv;
+            for (int pass = 0; pass < (type_b >= 0 ? 2 : 1); pass++) {
+                uint2 *dst = pass ? xf1 : xf0;
+                switch (pass ? type_b : F.seg[0].type) {
+                case T_Q4_K: fl_frags_chunk<T_Q4_K>(b, xs, norm ? nw : nullptr, scale, dst); break;
+                case T_Q6_K: fl_frags_chunk<T_Q6_K>(b, xs, norm ? nw : nullptr, scale, dst); break;
+                default: fl_frags_chunk<T_F16>(b, xs, norm ? nw : nullptr, scale, dst); break;
+                }
+            }
+        }
+        __syncwarp();
+        cstage += clock64() - c1;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (lane == 0) fl_wss[warp] = ss;
+    __syncwarp();
+    if (tr) {
+        tr[1] = (unsigned long long)cpoll;
+        tr[2] = (unsigned long long)cstage;
+    }
     return true;
+}
+
+// RMSNorm factor of the staged input from the eight warps' sums (fixed order).
+FDEV float fl_rrms(const FPhase &F) {
+    float ss = 0.f;
+#pragma unroll
+    for (int w = 0; w < FL_WARPS; w++) ss += fl_wss[w];
+    return 1.0f / sqrtf(ss / (float)F.cols + F.eps);
 }
 
 // Order-preserving key of a logit: larger value first, then lower index; NaN below
@@ -400,12 +485,14 @@ FDEV void fl_epilogue(const FParams &P, const FPhase &F, const PSeg &S, int lt, 
         float v0 = 0.f, v1 = 0.f;
 #pragma unroll
         for (int w = 0; w < FL_WARPS; w++) v0 += fl_red[d][w][0][lane];
-        const float inv = fl_scale[1];
-        v0 *= inv;
         if (F.nmat == 2) {
 #pragma unroll
             for (int w = 0; w < FL_WARPS; w++) v1 += fl_red[d][w][1][lane];
-            v1 *= inv;
+        }
+        if (F.norm_w) {  // y = rrms * W (x * w)
+            const float rrms = fl_rrms(F);
+            v0 *= rrms;
+            v1 *= rrms;
         }
         if (r < S.rows) {
             switch (F.kind) {
@@ -456,10 +543,14 @@ FDEV void fl_tile(const FParams &P, const FPhase &F, const PSeg &S, int lt, cons
         for (int i = 0; i < 4; i++) acc[m][i] = 0.f;
     for (int b = warp; b < nb; b += FL_WARPS) {
         const uint2 *xfb = xf + (size_t)b * 128;
+        const float inv = fl_cinv[b];  // the chunk's fragment scale, undone per chunk
 #pragma unroll
         for (int m = 0; m < NMAT; m++) {
             const uint8_t *mb = buf + (size_t)m * TC_M * S.stride + (size_t)b * TcType<T>::BB;
-            TcDot<T>::run(mb + (size_t)g * S.stride, mb + (size_t)(g + 8) * S.stride, xfb, g, t, acc[m]);
+            float part[4] = {0.f, 0.f, 0.f, 0.f};
+            TcDot<T>::run(mb + (size_t)g * S.stride, mb + (size_t)(g + 8) * S.stride, xfb, g, t, part);
+#pragma unroll
+            for (int i = 0; i < 4; i++) acc[m][i] = fmaf(part[i], inv, acc[m][i]);
         }
     }
     if (t == 0) {
@@ -1023,11 +1114,9 @@ __global__ void __launch_bounds__(FL_THREADS, 1) decode_flow_kernel(const __grid
             if (F.kind == FL_ATTN) {
                 if (nch > 0 && u < units) ok = FlowAttn<HD, G>::unit(P, F, u / S, u % S, S, pos, nch, seq, tag, wcycles, tr);
             } else if ((int)blockIdx.x < F.stage_ctas) {
-                ok = fl_stage(P, F, tag, token0, tr);
-                if (ok) {
-                    ok = fl_tiles(P, F, seq, tag, wcycles);
-                    ok = !cbar_any(!ok || fl_abort);  // all warps past their tiles (epilogues done)
-                }
+                ok = fl_stage_warp(P, F, tag, token0, tr);
+                if (ok) ok = fl_tiles(P, F, seq, tag, wcycles);
+                ok = !cbar_any(!ok || fl_abort);  // all warps past their tiles (epilogues done)
             }
             if (ok && F.kind == FL_LM) fl_argmax_finish(P);
             cp_async_wait_all();

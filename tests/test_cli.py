@@ -55,7 +55,8 @@ def test_greedy_run_matches_oracle(tiny_model, name):
     path = tiny_model(name)
     n = 32
     r = subprocess.run([_exe(), "--model", path, "--prompt", "Hello world, this is a test", "--tokens", str(n),
-                        "--temperature", "0", "--ids"], capture_output=True, text=True, timeout=600)
+                        "--temperature", "0", "--ids"], capture_output=True, text=True, errors="replace",
+                       timeout=600)
     assert r.returncode == 0, r.stderr
     assert "--- Stats ---" in r.stdout and "Prefill:" in r.stdout and "Decode:" in r.stdout
     prompt = _ids(r.stderr, "prompt ids")
