@@ -749,6 +749,7 @@ static int flow_build(gpu_context *c) {
         u.nseg = 1;
         u.nmat = 2;
         u.seg[0] = make_pseg(d.w1, d.w3, d.t1, ffn, 0, dim);
+        u.seg[0].tiles = (ffn + TC_M / 2 - 1) / (TC_M / 2);  // 8 rows of gate + the same 8 of up
         u.in = x1w(l);
         u.norm_w = d.ffn_norm;
         u.out = hw(l);
@@ -788,7 +789,7 @@ static int flow_build(gpu_context *c) {
         if (f.kind == FL_ATTN) continue;
         int types = 1;
         for (int k = 0; k < f.nseg; k++) {
-            max_tile = std::max(max_tile, (size_t)f.nmat * TC_M * f.seg[k].stride);
+            max_tile = std::max(max_tile, (size_t)TC_M * f.seg[k].stride);
             if (f.seg[k].type != f.seg[0].type) types = 2;
         }
         frag = std::max(frag, types * f.cols * 4);

@@ -55,14 +55,16 @@ constexpr int FL_RING_PAD = 1024;              // the ring starts at the first 1
 //  6 producer: globaltimer after issuing the phase's last copy   7 producer: cycles waiting for ring space
 //  attention units: 1 cycles polling q|k|v   2 RoPE, K/V append, q fragments
 //  8 cycles of the page loop   9 cycles merging (warps, then splits: includes polling them)
-constexpr int FL_TRACE_FIELDS = 10;
+//  GEMV phases: 10 globaltimer when the last warp had staged its input chunks
+//               11 globaltimer after the last tile epilogue of this CTA
+constexpr int FL_TRACE_FIELDS = 12;
 
 enum : int { FL_QKV = 0, FL_ATTN = 1, FL_RESID = 2, FL_SWIGLU = 3, FL_LM = 4 };
 
 struct __align__(16) FPhase {
     int kind;
     int nseg;
-    int nmat;        // 2 for SwiGLU (gate + up), else 1
+    int nmat;        // 2 for SwiGLU (a tile: 8 rows of gate, then the same 8 rows of up), else 1
     int cols;        // input length
     int layer;
     int n_tiles;
@@ -115,7 +117,7 @@ extern __shared__ __align__(128) uint8_t fl_dyn[];
 __shared__ __align__(8) uint64_t fl_full[FL_NDESC];
 __shared__ __align__(8) uint64_t fl_empty[FL_NDESC];
 __shared__ __align__(16) FPhase fl_F[2];
-__shared__ __align__(16) float fl_red[FL_NDESC][FL_WARPS][2][TC_M];  // per ring slot: warp partial sums
+__shared__ __align__(16) float fl_red[FL_NDESC][FL_WARPS][TC_M];  // per ring slot: warp partial sums
 __shared__ unsigned int fl_redcnt[FL_NDESC];                          // warps done with the slot's tile
 __shared__ float fl_stat[2 * FL_WARPS];
 __shared__ unsigned long long fl_best;   // this CTA's best logit key
@@ -125,6 +127,7 @@ __shared__ unsigned int fl_ticket;
 constexpr int FL_MAX_CHUNKS = 64;        // input length / 256 at most (16384 elements)
 __shared__ float fl_cinv[FL_MAX_CHUNKS]; // staged input: per-chunk inverse fragment scale
 __shared__ float fl_wss[FL_WARPS];       // staged input: per-warp sums of x^2 (RMSNorm)
+__shared__ unsigned long long fl_tmark[2];  // trace: inputs staged, last epilogue (globaltimer)
 __shared__ float2 fl_rope[64];           // RoPE (cos, sin) row of this launch's position
 
 FDEV uint8_t *fl_ring() { return fl_dyn + ((FL_RING_PAD - (smem_u32(fl_dyn) & (FL_RING_PAD - 1))) & (FL_RING_PAD - 1)); }
@@ -452,7 +455,10 @@ __device__ __noinline__ bool fl_stage_warp(const FParams &P, const FPhase &F, ui
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    if (lane == 0) fl_wss[warp] = ss;
+    if (lane == 0) {
+        fl_wss[warp] = ss;
+        if (P.trace) atomicMax(&fl_tmark[0], gtimer());
+    }
     __syncwarp();
     if (tr) {
         tr[1] = (unsigned long long)cpoll;
@@ -477,17 +483,19 @@ FDEV unsigned long long fl_key(float v, int idx) {
     return ((unsigned long long)b << 32) | (0xFFFFFFFFu - (uint32_t)idx);
 }
 
-// Epilogue of one tile (the last warp to finish it): lanes 0..15 own its rows.
+// Epilogue of one tile (the last warp to finish it): lanes 0..15 own its rows; in a
+// SwiGLU tile lane j < 8 owns output row 8 lt + j (gate in MMA row j, up in row j + 8).
 FDEV void fl_epilogue(const FParams &P, const FPhase &F, const PSeg &S, int lt, int d, uint32_t tag) {
     const int lane = threadIdx.x & 31;
-    if (lane < TC_M) {
-        const int r = lt * TC_M + lane;
+    const bool pair = F.kind == FL_SWIGLU;
+    if (lane < (pair ? TC_M / 2 : TC_M)) {
+        const int r = lt * (pair ? TC_M / 2 : TC_M) + lane;
         float v0 = 0.f, v1 = 0.f;
 #pragma unroll
-        for (int w = 0; w < FL_WARPS; w++) v0 += fl_red[d][w][0][lane];
-        if (F.nmat == 2) {
+        for (int w = 0; w < FL_WARPS; w++) v0 += fl_red[d][w][lane];
+        if (pair) {
 #pragma unroll
-            for (int w = 0; w < FL_WARPS; w++) v1 += fl_red[d][w][1][lane];
+            for (int w = 0; w < FL_WARPS; w++) v1 += fl_red[d][w][lane + TC_M / 2];
         }
         if (F.norm_w) {  // y = rrms * W (x * w)
             const float rrms = fl_rrms(F);
@@ -531,34 +539,23 @@ FDEV void fl_epilogue(const FParams &P, const FPhase &F, const PSeg &S, int lt, 
 // One tile of the phase, warp-level: decode + multiply this warp's super-blocks,
 // publish the partial sums; the last of the eight warps runs the epilogue and only
 // then frees the ring slot (the slot's partial sums stay valid until it is refilled).
-template <int T, int NMAT>
+template <int T>
 FDEV void fl_tile(const FParams &P, const FPhase &F, const PSeg &S, int lt, const uint8_t *buf, const uint2 *xf,
                   int d, uint32_t tag) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
     const int nb = F.cols >> 8;
-    float acc[NMAT][4];
-#pragma unroll
-    for (int m = 0; m < NMAT; m++)
-#pragma unroll
-        for (int i = 0; i < 4; i++) acc[m][i] = 0.f;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
     for (int b = warp; b < nb; b += FL_WARPS) {
-        const uint2 *xfb = xf + (size_t)b * 128;
         const float inv = fl_cinv[b];  // the chunk's fragment scale, undone per chunk
+        const uint8_t *mb = buf + (size_t)b * TcType<T>::BB;
+        float part[4] = {0.f, 0.f, 0.f, 0.f};
+        TcDot<T>::run(mb + (size_t)g * S.stride, mb + (size_t)(g + 8) * S.stride, xf + (size_t)b * 128, g, t, part);
 #pragma unroll
-        for (int m = 0; m < NMAT; m++) {
-            const uint8_t *mb = buf + (size_t)m * TC_M * S.stride + (size_t)b * TcType<T>::BB;
-            float part[4] = {0.f, 0.f, 0.f, 0.f};
-            TcDot<T>::run(mb + (size_t)g * S.stride, mb + (size_t)(g + 8) * S.stride, xfb, g, t, part);
-#pragma unroll
-            for (int i = 0; i < 4; i++) acc[m][i] = fmaf(part[i], inv, acc[m][i]);
-        }
+        for (int i = 0; i < 4; i++) acc[i] = fmaf(part[i], inv, acc[i]);
     }
     if (t == 0) {
-#pragma unroll
-        for (int m = 0; m < NMAT; m++) {
-            fl_red[d][warp][m][g] = acc[m][0] + acc[m][1];
-            fl_red[d][warp][m][g + 8] = acc[m][2] + acc[m][3];
-        }
+        fl_red[d][warp][g] = acc[0] + acc[1];
+        fl_red[d][warp][g + 8] = acc[2] + acc[3];
     }
     __syncwarp();
     unsigned int old = 0;
@@ -570,7 +567,11 @@ FDEV void fl_tile(const FParams &P, const FPhase &F, const PSeg &S, int lt, cons
     if (old == FL_WARPS - 1) {
         __threadfence_block();
         fl_epilogue(P, F, S, lt, d, tag);
-        if (lane == 0) fl_redcnt[d] = 0u;
+        __syncwarp();
+        if (lane == 0) {
+            fl_redcnt[d] = 0u;
+            if (P.trace) atomicMax(&fl_tmark[1], gtimer());
+        }
         __syncwarp();
     }
     if (lane == 0) mbar_arrive(&fl_empty[d]);
@@ -588,18 +589,10 @@ FDEV bool fl_tiles(const FParams &P, const FPhase &F, long long &seq, uint32_t t
         if (!buf) return false;
         const int d = (int)(seq % FL_NDESC);
         const uint2 *xf = (S.type == F.seg[0].type) ? xf0 : xf1;
-        if (F.nmat == 2) {
-            switch (S.type) {
-            case T_Q4_K: fl_tile<T_Q4_K, 2>(P, F, S, lt, buf, xf, d, tag); break;
-            case T_Q6_K: fl_tile<T_Q6_K, 2>(P, F, S, lt, buf, xf, d, tag); break;
-            default: fl_tile<T_F16, 2>(P, F, S, lt, buf, xf, d, tag); break;
-            }
-        } else {
-            switch (S.type) {
-            case T_Q4_K: fl_tile<T_Q4_K, 1>(P, F, S, lt, buf, xf, d, tag); break;
-            case T_Q6_K: fl_tile<T_Q6_K, 1>(P, F, S, lt, buf, xf, d, tag); break;
-            default: fl_tile<T_F16, 1>(P, F, S, lt, buf, xf, d, tag); break;
-            }
+        switch (S.type) {
+        case T_Q4_K: fl_tile<T_Q4_K>(P, F, S, lt, buf, xf, d, tag); break;
+        case T_Q6_K: fl_tile<T_Q6_K>(P, F, S, lt, buf, xf, d, tag); break;
+        default: fl_tile<T_F16>(P, F, S, lt, buf, xf, d, tag); break;
         }
         seq++;
     }
@@ -1018,21 +1011,24 @@ __device__ __noinline__ void fl_producer(const FParams &P, int pos, int nch, int
                 fl_locate(F, tile, s, lt);
                 const PSeg &Sg = F.seg[s];
                 int d;
-                uint8_t *dst = reserve(tile_bytes_of(Sg, F.nmat), 16, d);
+                uint8_t *dst = reserve(TC_M * Sg.stride, 16, d);
                 if (!dst) break;
-                // plain-copied tail first, then the arrive (release), then the bulk copies
-                const int r0 = lt * TC_M, nrows = min(TC_M, Sg.rows - r0);
+                // a SwiGLU tile holds rows 8 lt .. 8 lt + 7 of gate (ring rows 0..7) and of up
+                // (ring rows 8..15); other tiles rows 16 lt .. 16 lt + 15 of one matrix
+                const int nm = F.kind == FL_SWIGLU ? 2 : 1, rpt = TC_M / nm;
+                const int r0 = lt * rpt, nrows = min(rpt, Sg.rows - r0);
                 const uint32_t mat_bytes = (uint32_t)nrows * Sg.row_bytes;
                 const uint32_t main_bytes = Sg.per_row ? mat_bytes : (mat_bytes & ~15u);
-                for (int m = 0; m < F.nmat; m++) {
+                // plain-copied tail first, then the arrive (release), then the bulk copies
+                for (int m = 0; m < nm; m++) {
                     const uint8_t *src = (m == 0 ? Sg.w : Sg.w2) + (size_t)r0 * Sg.row_bytes;
-                    uint8_t *mdst = dst + (size_t)m * TC_M * Sg.stride;
+                    uint8_t *mdst = dst + (size_t)m * rpt * Sg.stride;
                     for (uint32_t k = main_bytes; k < mat_bytes; k++) mdst[k] = src[k];
                 }
-                mbar_expect_tx(&fl_full[d], main_bytes * F.nmat);
-                for (int m = 0; m < F.nmat; m++) {
+                mbar_expect_tx(&fl_full[d], main_bytes * nm);
+                for (int m = 0; m < nm; m++) {
                     const uint8_t *src = (m == 0 ? Sg.w : Sg.w2) + (size_t)r0 * Sg.row_bytes;
-                    uint8_t *mdst = dst + (size_t)m * TC_M * Sg.stride;
+                    uint8_t *mdst = dst + (size_t)m * rpt * Sg.stride;
                     if (Sg.per_row) {
                         for (int r = 0; r < nrows; r++)
                             bulk_g2s(mdst + (size_t)r * Sg.stride, src + (size_t)r * Sg.row_bytes, Sg.row_bytes,
@@ -1070,6 +1066,7 @@ __global__ void __launch_bounds__(FL_THREADS, 1) decode_flow_kernel(const __grid
         mbar_fence_init();
         fl_abort = 0;
         fl_best = 0ull;
+        fl_tmark[0] = fl_tmark[1] = 0ull;
     }
     if (warp == 0) fl_fetch_phase(&fl_F[0], P.phases, lane);
     cp_async_wait_all();
@@ -1124,6 +1121,11 @@ __global__ void __launch_bounds__(FL_THREADS, 1) decode_flow_kernel(const __grid
                 tr[3] = (unsigned long long)(clock64() - c0);
                 tr[4] = (unsigned long long)wcycles;
                 tr[5] = gtimer();
+                if (F.kind != FL_ATTN) {
+                    tr[10] = fl_tmark[0];
+                    tr[11] = fl_tmark[1];
+                }
+                fl_tmark[0] = fl_tmark[1] = 0ull;  // the next phase starts after a barrier
             }
             if (!ok) break;
         }

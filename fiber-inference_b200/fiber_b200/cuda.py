@@ -357,7 +357,8 @@ class Context:
                     "t_producer_done_ns", "cyc_producer_wait", "cyc_attn_qkv", "cyc_attn_pages"]
 
     FLOW_TRACE_FIELDS = ["t_start_ns", "cyc_poll", "cyc_stage", "cyc_phase", "cyc_wait_ring", "t_end_ns",
-                         "t_producer_done_ns", "cyc_producer_wait", "cyc_attn_pages", "cyc_attn_merge"]
+                         "t_producer_done_ns", "cyc_producer_wait", "cyc_attn_pages", "cyc_attn_merge",
+                         "t_inputs_staged_ns", "t_last_epilogue_ns"]
 
     def trace_step(self, kv: KVCache, token: int, pos: int, max_phases: int = 4096, max_ctas: int = 1024):
         """Per-phase, per-CTA timeline of one one-kernel step: uint64 array
