@@ -795,8 +795,11 @@ static int flow_build(gpu_context *c) {
         frag = std::max(frag, types * f.cols * 4);
     }
     frag = (frag + 127) & ~127;
-    // attention splits per KV head: about four pages each, at most 8 (split 0 merges the others)
-    const int max_split = std::max(1, std::min(8, grid / (int)p.n_kv_heads));
+    // attention splits per KV head: about eight pages each at max_seq, at most 8 and at most
+    // a grid's worth of units (split 0 merges the others; fewer splits, less scratch)
+    const int max_pages = (c->max_seq + ATTN_P - 1) / ATTN_P;
+    const int max_split = std::max(1, std::min(std::min(8, grid / (int)p.n_kv_heads),
+                                               (max_pages + FL_PAGES_PER_UNIT - 1) / FL_PAGES_PER_UNIT));
     scratch += (max_split - 1) * c->G * (hd + 2);
     const int xres = (dim + 31) & ~31;
     const int xin = (std::max(std::max(dim, ffn), scratch) + 31) & ~31;

@@ -57,7 +57,9 @@ constexpr int FL_RING_PAD = 1024;              // the ring starts at the first 1
 //  8 cycles of the page loop   9 cycles merging (warps, then splits: includes polling them)
 //  GEMV phases: 10 globaltimer when the last warp had staged its input chunks
 //               11 globaltimer after the last tile epilogue of this CTA
-constexpr int FL_TRACE_FIELDS = 12;
+//  attention units (warp 0): 12 cycles acquiring pages  13 cycles of q.K  14 cycles of the
+//               softmax  15 cycles of P.V
+constexpr int FL_TRACE_FIELDS = 16;
 
 enum : int { FL_QKV = 0, FL_ATTN = 1, FL_RESID = 2, FL_SWIGLU = 3, FL_LM = 4 };
 
@@ -321,6 +323,25 @@ FDEV void fl_frags_chunk(int b, const float *xs, const float *nw, float scale, u
 
 // ---- GEMV phase -----------------------------------------------------------------------
 
+// Chunk b of the embedding row of token tok, rounded to fp16 as the reference's
+// gpu_embed writes it, into xs (lanes of one warp). Only the first layer runs it, so
+// it is kept out of line (instruction-cache footprint of the per-layer path).
+__device__ __noinline__ void fl_embed_chunk(const FParams &P, int tok, int b, float *xs) {
+    const int lane = threadIdx.x & 31, n = P.dim, nb = n >> 8;
+    for (int e = lane; e < 256; e += 32) {
+        const int i = b * 256 + e;
+        float v;
+        switch (P.embd_type) {
+        case T_F16: v = h2f(reinterpret_cast<const uint16_t *>(P.embd)[(size_t)tok * n + i]); break;
+        case T_F32: v = round_f16(reinterpret_cast<const float *>(P.embd)[(size_t)tok * n + i]); break;
+        case T_Q4_K: v = round_f16(decode_elem<T_Q4_K>(P.embd + ((size_t)tok * nb + b) * 144, e)); break;
+        case T_Q5_K: v = round_f16(decode_elem<T_Q5_K>(P.embd + ((size_t)tok * nb + b) * 176, e)); break;
+        default: v = round_f16(decode_elem<T_Q6_K>(P.embd + ((size_t)tok * nb + b) * 210, e)); break;
+        }
+        xs[i] = v;
+    }
+}
+
 // Stage this warp's chunks of the phase input: chunk b (256 elements) is staged by warp
 // b % 8, the warp that multiplies super-block column b of every tile, so no other warp
 // waits for it. Per chunk: poll its tagged words (or decode the embedding row), keep
@@ -358,21 +379,7 @@ __device__ __noinline__ bool fl_stage_warp(const FParams &P, const FPhase &F, ui
                 cp_async16(nw + b * 256 + 128 + 4 * lane, F.norm_w + b * 256 + 128 + 4 * lane);
             }
         if (F.embed_in) {  // every CTA decodes the embedding row itself (src/gpu_ffn.m:466-482)
-            for (int c = 0; c < nc; c++) {
-                const int b = b0 + c * FL_WARPS;
-                for (int e = lane; e < 256; e += 32) {
-                    const int i = b * 256 + e;
-                    float v;
-                    switch (P.embd_type) {
-                    case T_F16: v = h2f(reinterpret_cast<const uint16_t *>(P.embd)[(size_t)tok * n + i]); break;
-                    case T_F32: v = round_f16(reinterpret_cast<const float *>(P.embd)[(size_t)tok * n + i]); break;
-                    case T_Q4_K: v = round_f16(decode_elem<T_Q4_K>(P.embd + ((size_t)tok * nb + b) * 144, e)); break;
-                    case T_Q5_K: v = round_f16(decode_elem<T_Q5_K>(P.embd + ((size_t)tok * nb + b) * 176, e)); break;
-                    default: v = round_f16(decode_elem<T_Q6_K>(P.embd + ((size_t)tok * nb + b) * 210, e)); break;
-                    }
-                    xs[i] = v;
-                }
-            }
+            for (int c = 0; c < nc; c++) fl_embed_chunk(P, tok, b0 + c * FL_WARPS, xs);
         } else {
             // pair k of the group: chunk b0 + 8 (k / 4), words 2 (lane + 32 (k % 4)) + {0, 1}
             ulonglong2 w[8];
@@ -757,11 +764,20 @@ struct FlowAttn {
                 seq++;
                 continue;
             }
+            long long ct = clock64();
+            auto tmark = [&](int field) {
+                if (tr) {
+                    const long long n2 = clock64();
+                    tr[field] += (unsigned long long)(n2 - ct);
+                    ct = n2;
+                }
+            };
             const uint8_t *tile = fl_acquire(P, seq, wcycles);
             if (!tile) {
                 ok = false;
                 break;
             }
+            tmark(12);
             const int d = (int)(seq % FL_NDESC);
             seq++;
             const bool last = pg == nch - 1;
@@ -781,6 +797,7 @@ struct FlowAttn {
                     mma16816(sc[nt], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], lds32(a0), lds32(a1));
                 }
             }
+            tmark(13);
             // lane (gl, t): positions 8 nt + 2t, 8 nt + 2t + 1 of head gl
             float mx = -INFINITY;
 #pragma unroll
@@ -816,6 +833,7 @@ struct FlowAttn {
                 o[n][2] *= al;
                 o[n][3] *= al;
             }
+            tmark(14);
             // P.V: k-tile kt = positions 8 kt .. 8 kt + 7 (P as the m16n8k8 A operand: row gl hi
             // parts, row gl + 8 lo parts); V by ldmatrix.trans, matrix mi = dims 8 (4 q4 + mi) ..
 #pragma unroll
@@ -836,6 +854,7 @@ struct FlowAttn {
                     mma16808(o[4 * q4 + 3], phi, plo, b3);
                 }
             }
+            tmark(15);
             __syncwarp();
             if (lane == 0) mbar_arrive_n(&fl_empty[d], FL_WARPS);  // the page's only reader frees it
         }
@@ -858,17 +877,27 @@ struct FlowAttn {
         mark(8);
         // merge the eight warps of each head (warp order) into this split's state
         uint64_t *mine = P.att_words + (((size_t)F.layer * P.n_kv + g) * P.att_max_split + j) * G * (HD + 2);
-        for (int i = tid; i < G * (HD + 2); i += FL_CONSUMERS) {
-            const int h = i / (HD + 2), e = i % (HD + 2);
+        // per head h: M = the warps' largest running max, f[h][w] = exp(m_w - M) (0 for a
+        // warp without valid positions), kept in the q scratch (q is in registers now)
+        float *fw = qs, *Mh = qs + G * FL_WARPS;
+        if (tid < G * FL_WARPS) {
+            const int h = tid / FL_WARPS, w = tid % FL_WARPS;
             float M = -INFINITY;
 #pragma unroll
-            for (int w = 0; w < FL_WARPS; w++) M = fmaxf(M, wm[(w * G + h) * (HD + 2)]);
+            for (int v = 0; v < FL_WARPS; v++) M = fmaxf(M, wm[(v * G + h) * (HD + 2)]);
+            const float m = wm[(w * G + h) * (HD + 2)];
+            fw[tid] = m == -INFINITY ? 0.f : expf(m - M);
+            if (w == 0) Mh[h] = M;
+        }
+        cbar();
+        for (int i = tid; i < G * (HD + 2); i += FL_CONSUMERS) {
+            const int h = i / (HD + 2), e = i % (HD + 2);
+            const float M = Mh[h];
             float acc = 0.f, L = 0.f;
 #pragma unroll
-            for (int w = 0; w < FL_WARPS; w++) {
+            for (int w = 0; w < FL_WARPS; w++) {  // warp order
                 const float *st = wm + (w * G + h) * (HD + 2);
-                if (st[0] == -INFINITY) continue;  // a warp without valid positions
-                const float f = expf(st[0] - M);
+                const float f = fw[h * FL_WARPS + w];
                 L = fmaf(f, st[1], L);
                 if (e >= 2) acc = fmaf(f, st[e], acc);
             }
