@@ -271,13 +271,38 @@ MODEL_7B = "/tmp/fiber_bench_llama7b_q4km.gguf"
 WEIGHTS_7B = 16 * 113_836_032 + 16 * 129_785_856 + 107_520_000 + 32 * 2 * 16_384 + 16_384 + 2_304
 
 
-def run_7b_tp(args, fb, torch, dist, rank, world, local):
-    """Config 5: 7B Q4_K_M (dim 4096, 32 layers, 32 heads, hd 128, ffn 11008) batch-1 greedy
-    decode, tensor-parallel over the N ranks (one process per GPU; NCCL all-reduce after Wo
-    and W_down inside each step's graph). Total work is fixed: scaling is strong."""
-    # config 5: 512-token prompt, 256 decode steps (shorter only when asked for)
-    P = 512 if args.prompt_len == PROMPT_LEN else args.prompt_len
-    D = 256 if args.decode_len == DECODE_LEN else args.decode_len
+def step_phase_times(ctx, kv, first: int, pos: int) -> dict:
+    """Critical-path time of each phase kind of the one-kernel step at KV position pos, from
+    the step's own per-phase timeline (fiber_trace_step): for phase k, the latest CTA end of
+    phase k minus the latest CTA end of phase k - 1, averaged over the layers (microseconds)."""
+    tr = None
+    for _ in range(3):  # the last of three (warm) traced steps
+        tr = ctx.trace_step(kv, first, pos)
+    if ctx.mode == 2:
+        end = tr[:, :, ctx.FLOW_TRACE_FIELDS.index("t_end_ns")].astype(np.int64)
+        start = tr[:, :, ctx.FLOW_TRACE_FIELDS.index("t_start_ns")].astype(np.int64)
+    else:
+        end = tr[:, :, ctx.TRACE_FIELDS.index("t_release_ns")].astype(np.int64)
+        start = end
+    n = tr.shape[0]
+    ends = np.array([end[k][end[k] > 0].max() for k in range(n)], dtype=np.float64)
+    names = ["qkv", "attention", "wo", "gate_up", "down"]
+    out = {k: [] for k in names}
+    for k in range(1, n - 1):
+        out[names[k % 5]].append((ends[k] - ends[k - 1]) / 1e3)
+    res = {k: float(np.mean(v)) for k, v in out.items() if v}
+    res["lm_head"] = float((ends[n - 1] - ends[n - 2]) / 1e3)
+    s0 = start[0][start[0] > 0].min()
+    res["step_us"] = float((ends[n - 1] - s0) / 1e3)
+    res["position"] = pos
+    return res
+
+
+def measure_7b_tp(fb, torch, dist, rank, world, local, P: int, D: int, steps: int, warmup: int) -> dict:
+    """7B Q4_K_M batch-1 greedy decode, tensor-parallel over the N ranks (one process per
+    GPU; the Wo and W_down partial sums all-reduced inside each step). Every rank returns
+    the same dict: decode tok/s from CUDA events (max over ranks), the collective used and
+    whether all ranks produced the same tokens."""
     if rank == 0 and not os.path.exists(MODEL_7B):
         fb.write_model(MODEL_7B + ".tmp", fb.synth_cfg("llama7b"))
         os.replace(MODEL_7B + ".tmp", MODEL_7B)
@@ -292,14 +317,14 @@ def run_7b_tp(args, fb, torch, dist, rank, world, local):
     t0 = time.perf_counter()
     first = ctx.prefill(kv, prompt)
     prefill_tps = P / (time.perf_counter() - t0)
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         ctx.decode_greedy(kv, first, P, D)
     if dist is not None:
         dist.barrier()
     torch.cuda.synchronize(local)
     ms_total, toks0 = 0.0, None
     with Clocks(local) as clk:
-        for _ in range(args.steps):
+        for _ in range(steps):
             toks, ms = ctx.decode_greedy(kv, first, P, D)
             ms_total += ms
             toks0 = toks if toks0 is None else toks0
@@ -313,44 +338,66 @@ def run_7b_tp(args, fb, torch, dist, rank, world, local):
         same = all(int(x.item()) == int(h.item()) for x in hs)
     else:
         same = True
-    value = args.steps * D / (ms_total / 1e3)
+    value = steps * D / (ms_total / 1e3)
     peak, peak_kind = peaks()
     kv_bytes = 524_288 * (P + D / 2)  # mean KV read per token over the decode positions
     bytes_tok = WEIGHTS_7B + kv_bytes
+    out = {"value": value, "unit": "tok/s", "n_gpus": world, "steps": steps, "warmup": warmup,
+           "ms_per_step": ms_total / steps, "prompt": P, "decode_tokens_per_step": D, "parallelism": f"tp{world}",
+           "collective": {0: "none (one GPU)", 1: "NCCL all-reduce", 2: "one-shot peer-memory all-reduce"}[
+               ctx.tp_collective],
+           "step_mode": STEP_MODES[ctx.mode] + (", all-reduce after Wo and W_down" if world > 1 else ""),
+           "tokens_identical_on_all_ranks": same, "prefill_tok_s": prefill_tps,
+           "roofline": {"bound": "hbm", "achieved": bytes_tok * value / world / 1e9, "peak": peak, "unit": "GB/s",
+                        "frac": bytes_tok * value / world / 1e9 / peak, "peak_source": peak_kind,
+                        "algorithmic_bytes_per_token": bytes_tok,
+                        "note": "per GPU: weights and KV of the whole model divided over the ranks"},
+           "gpu_launches": ctx.step_launches() * D * steps, "clocks": clk.summary()}
+    ctx.close()
+    if dist is not None:
+        dist.barrier()
+    return out
+
+
+def run_7b_tp(args, fb, torch, dist, rank, world, local):
+    """Config 5: 7B Q4_K_M (dim 4096, 32 layers, 32 heads, hd 128, ffn 11008) batch-1 greedy
+    decode, tensor-parallel over the N ranks (one process per GPU; all-reduce after Wo
+    and W_down inside each step). Total work is fixed: scaling is strong."""
+    # config 5: 512-token prompt, 256 decode steps (shorter only when asked for)
+    P = 512 if args.prompt_len == PROMPT_LEN else args.prompt_len
+    D = 256 if args.decode_len == DECODE_LEN else args.decode_len
+    r = measure_7b_tp(fb, torch, dist, rank, world, local, P, D, args.steps, args.warmup)
     if rank == 0:
-        line = {"metric": "decode tok/s (7B Q4_K_M, bs=1, tensor-parallel)", "value": value, "unit": "tok/s",
-                "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_total / args.steps,
+        line = {"metric": "decode tok/s (7B Q4_K_M, bs=1, tensor-parallel)", "value": r["value"], "unit": "tok/s",
+                "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": r["ms_per_step"],
                 "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
                 "data": "synthetic (seeded random-init weights, seeded prompt ids)",
                 "config": {"workload": "7B Q4_K_M (Llama-2-7B shape) batch-1 greedy decode, tensor-parallel",
                            "model": "dim 4096, 32 layers, 32/32 heads, hd 128, ffn 11008, vocab 32000, Q4_K_M",
                            "prompt": P, "decode_tokens_per_step": D, "global_batch": 1,
-                           "parallelism": f"tp{world}",
-                           "step_mode": "one kernel per phase + " + {0: "no", 1: "NCCL", 2: "one-shot peer-memory"}[
-                               ctx.tp_collective] + " all-reduce",
-                           "tokens_identical_on_all_ranks": same, "prefill_tok_s": prefill_tps},
-                "roofline": {"bound": "hbm", "achieved": bytes_tok * value / world / 1e9, "peak": peak, "unit": "GB/s",
-                             "frac": bytes_tok * value / world / 1e9 / peak, "peak_source": peak_kind,
-                             "traffic": None, "algorithmic_bytes_per_token": bytes_tok,
-                             "note": "per GPU: weights and KV of the whole model divided over the ranks"},
-                "gpu_launches": ctx.step_launches() * D * args.steps, "clocks": clk.summary()}
+                           "parallelism": f"tp{world}", "step_mode": r["step_mode"] + " (" + r["collective"] + ")",
+                           "tokens_identical_on_all_ranks": r["tokens_identical_on_all_ranks"],
+                           "prefill_tok_s": r["prefill_tok_s"]},
+                "roofline": dict(r["roofline"], traffic=None),
+                "gpu_launches": r["gpu_launches"], "clocks": r["clocks"]}
         print(json.dumps(line), flush=True)
-    ctx.close()
     if dist is not None:
-        dist.barrier()
         dist.destroy_process_group()
 
 
-def run_config(args, fb, torch, dist, rank, world, local):
-    """Configs 2 and 4 (batch 1, one replica per rank): the fp16 stories-shaped model with a
-    32-token prompt and 256 greedy steps; the 1.1B Q5_K_M model decoding 256 steps after its
-    KV cache was pre-filled with seeded N(0,1) fp16 keys/values for 2048 positions."""
-    if args.workload == "stories":
-        path, preset, P, D = "/tmp/fiber_bench_stories_f16.gguf", "stories", 32, 256
+CONFIG_NAMES = {"stories": "stories fp16 (dim 768, 12 layers, 12 heads, ffn 2048, vocab 32000, tied)",
+                "q5km-long": "1.1B Q5_K_M (TinyLlama shape), KV pre-filled to 2048 positions"}
+STEP_MODES = {0: "persistent kernel per token", 1: "one kernel per phase", 2: "dataflow kernel per token"}
+
+
+def measure_config(fb, torch, dist, rank, world, local, workload: str, D: int, steps: int, warmup: int) -> dict:
+    """Configs 2 and 4 at batch 1 (one replica per rank): the fp16 stories-shaped model with a
+    32-token prompt, or the 1.1B Q5_K_M model decoding after its KV cache was pre-filled with
+    seeded N(0,1) fp16 keys/values for 2048 positions. Returns the measurement as a dict."""
+    if workload == "stories":
+        path, preset, P = "/tmp/fiber_bench_stories_f16.gguf", "stories", 32
     else:
-        path, preset, P, D = "/tmp/fiber_bench_tinyllama_q5km.gguf", "tinyllama-q5", 2048, 256
-    if args.decode_len != DECODE_LEN:
-        D = args.decode_len
+        path, preset, P = "/tmp/fiber_bench_tinyllama_q5km.gguf", "tinyllama-q5", 2048
     if not os.path.exists(path):
         tmp = path + f".{os.getpid()}.tmp"
         fb.write_model(tmp, fb.synth_cfg(preset, seed=SEED))
@@ -360,52 +407,60 @@ def run_config(args, fb, torch, dist, rank, world, local):
     ctx = fb.Context(hm, device=local, max_seq=P + D)
     kv = ctx.kv(P + D)
     kvd = p.n_kv_heads * p.head_dim
-    if args.workload == "stories":
+    if workload == "stories":
         first = ctx.prefill(kv, prompt_ids(p.vocab_size)[:P])
     else:
         for layer in range(p.n_layers):
             kv.write(layer, 0, fb.randn(P * kvd, seed=100 + layer).reshape(P, kvd),
                      fb.randn(P * kvd, seed=200 + layer).reshape(P, kvd))
         first = 5
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         ctx.decode_greedy(kv, first, P, D)
     if dist is not None:
         dist.barrier()
     torch.cuda.synchronize(local)
     ms_total = 0.0
     with Clocks(local) as clk:
-        for _ in range(args.steps):
+        for _ in range(steps):
             _, ms = ctx.decode_greedy(kv, first, P, D)
             ms_total += ms
     if dist is not None:
         t = torch.tensor([ms_total], device=f"cuda:{local}", dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms_total = float(t.item())
-    value = world * args.steps * D / (ms_total / 1e3)
+    value = world * steps * D / (ms_total / 1e3)
     mid = P + D // 2
     step_bytes = 0.0
     for kind in range(7):
         _, b = ctx.time_kernel(kv, kind, mid, reps=2)
         step_bytes += b * (1 if kind >= 5 else p.n_layers)
     peak, peak_kind = peaks()
-    if rank == 0:
-        name = {"stories": "stories fp16 (dim 768, 12 layers, 12 heads, ffn 2048, vocab 32000, tied)",
-                "q5km-long": "1.1B Q5_K_M (TinyLlama shape), KV pre-filled to 2048 positions"}[args.workload]
-        line = {"metric": f"decode tok/s ({args.workload}, bs=1)", "value": value, "unit": "tok/s", "n_gpus": world,
-                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_total / args.steps,
-                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-                "dtype": "f32" if args.workload != "stories" else "f16 weights, f32 activations",
-                "data": "synthetic (seeded random-init weights; seeded prompt ids or seeded N(0,1) KV)",
-                "config": {"workload": name, "context": P, "decode_tokens_per_step": D, "global_batch": 1,
-                           "parallelism": f"replicas x{world}",
-                           "step_mode": "persistent kernel per token" if ctx.mode == 0 else "one kernel per phase"},
-                "roofline": {"bound": "hbm", "achieved": step_bytes * value / world / 1e9, "peak": peak,
-                             "unit": "GB/s", "frac": step_bytes * value / world / 1e9 / peak,
-                             "peak_source": peak_kind, "traffic": None,
-                             "algorithmic_bytes_per_token": step_bytes, "kv_position": mid},
-                "gpu_launches": ctx.step_launches() * D * args.steps, "clocks": clk.summary()}
-        print(json.dumps(line), flush=True)
+    out = {"value": value, "unit": "tok/s", "ms_per_step": ms_total / steps, "steps": steps, "warmup": warmup,
+           "workload": CONFIG_NAMES[workload], "context": P, "decode_tokens_per_step": D,
+           "dtype": "f32" if workload != "stories" else "f16 weights, f32 activations",
+           "step_mode": STEP_MODES[ctx.mode],
+           "roofline": {"bound": "hbm", "achieved": step_bytes * value / world / 1e9, "peak": peak,
+                        "unit": "GB/s", "frac": step_bytes * value / world / 1e9 / peak,
+                        "peak_source": peak_kind, "traffic": None,
+                        "algorithmic_bytes_per_token": step_bytes, "kv_position": mid},
+           "gpu_launches": ctx.step_launches() * D * steps, "clocks": clk.summary()}
     ctx.close()
+    return out
+
+
+def run_config(args, fb, torch, dist, rank, world, local):
+    """Configs 2 and 4 at batch 1 as their own bench line (256 decode steps)."""
+    D = 256 if args.decode_len == DECODE_LEN else args.decode_len
+    r = measure_config(fb, torch, dist, rank, world, local, args.workload, D, args.steps, args.warmup)
+    if rank == 0:
+        line = {"metric": f"decode tok/s ({args.workload}, bs=1)", "value": r["value"], "unit": "tok/s",
+                "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": r["ms_per_step"],
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": r["dtype"],
+                "data": "synthetic (seeded random-init weights; seeded prompt ids or seeded N(0,1) KV)",
+                "config": {"workload": r["workload"], "context": r["context"], "decode_tokens_per_step": D,
+                           "global_batch": 1, "parallelism": f"replicas x{world}", "step_mode": r["step_mode"]},
+                "roofline": r["roofline"], "gpu_launches": r["gpu_launches"], "clocks": r["clocks"]}
+        print(json.dumps(line), flush=True)
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
@@ -689,6 +744,23 @@ def main():
         barrier()
         e2e_val = world * D / (time.perf_counter() - e0)
 
+    phases = step_phase_times(ctx, kv, first, mid) if ctx.mode in (0, 2) else None
+
+    extras = {}
+    if not args.skip_extras:
+        # config 5 at every N: the 7B model decoding tensor-parallel over all ranks (strong
+        # scaling; the driver's 1..8-GPU runs record it beside the 1.1B replicas)
+        try:
+            extras["tp_7b"] = measure_7b_tp(fb, torch, dist, rank, world, local, 512, 64, 2, 1)
+        except Exception as e:  # noqa: BLE001 -- recorded in the line, the 1.1B number stands
+            extras["tp_7b"] = {"error": f"{type(e).__name__}: {e}"}
+        if world == 1:  # configs 2 and 4 at batch 1 (short runs)
+            for name, dd in (("stories", 256), ("q5km-long", 64)):
+                try:
+                    extras[name.replace("-", "_")] = measure_config(fb, torch, None, 0, 1, local, name, dd, 2, 1)
+                except Exception as e:  # noqa: BLE001
+                    extras[name.replace("-", "_")] = {"error": f"{type(e).__name__}: {e}"}
+
     if dist is not None:
         dist.barrier()
     if rank != 0:
@@ -734,14 +806,20 @@ def main():
         "roofline": dict(roof, bound="hbm", peak=peak, unit="GB/s", frac=roof["achieved"] / peak,
                          peak_source=peak_kind, **traffic_of(mode, roof)),
         "decode_roofline": {"bytes_per_token": step_bytes, "achieved_gbs": step_bytes * value / world / 1e9,
-                            "frac": step_bytes * value / world / 1e9 / peak, "per_phase_kernels": kern,
-                            "kv_position_for_kernel_timing": mid},
+                            "frac": step_bytes * value / world / 1e9 / peak,
+                            "step_phases": phases,
+                            "per_phase_kernels_mode1": kern,
+                            "kv_position_for_kernel_timing": mid,
+                            "note": "step_phases: the timed one-kernel step traced at kv_position (critical-path "
+                                    "us per phase kind, mean over layers); per_phase_kernels_mode1: each phase "
+                                    "as its own kernel (decode mode 1), for the per-kind bytes"},
         "e2e": {"value": e2e_val, "unit": "tok/s", "h2d_bytes_per_step": 32 * D, "d2h_bytes_per_step": 32 * D,
                 "api": "fiber_forward_token (host token/pos in, argmax out)"},
         "gpu_launches": launches,
         "clocks": clk.summary(),
         "wall_s": wall,
     }
+    line.update(extras)
     if not args.skip_extras:
         single = gemv_bandwidth(local)
         line["gemv_single"] = dict(single, frac=single["gbs"] / peak)

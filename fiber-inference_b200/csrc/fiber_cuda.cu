@@ -373,7 +373,8 @@ struct gpu_context {
     Graph g_step, g_loop;
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
     // persistent one-kernel step (persistent.cuh)
-    int mode = 0;                  // 0: persistent kernel when supported, 1: one kernel per phase
+    int mode = 0;                  // 0: persistent kernel, 1: one kernel per phase, 2: dataflow kernel
+                                   // (the default where the model fits it)
     bool pk_ok = false;            // the model fits the persistent kernel
     PPhase *d_phases = nullptr;
     std::vector<PPhase> phases;
@@ -957,7 +958,9 @@ static int ctx_init(gpu_context *c, const model_t *m, int device, int max_seq, i
         return FIBER_OK;
     }
     if ((rc = pk_build(c)) != FIBER_OK) return rc;
-    return flow_build(c);
+    if ((rc = flow_build(c)) != FIBER_OK) return rc;
+    if (c->fl_ok) c->mode = 2;  // the fastest step where the model fits it (dataflow kernel)
+    return FIBER_OK;
 }
 
 // ---- tensor parallelism ------------------------------------------------------------

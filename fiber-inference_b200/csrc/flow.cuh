@@ -59,6 +59,9 @@ constexpr int FL_RING_PAD = 1024;              // the ring starts at the first 1
 //               11 globaltimer after the last tile epilogue of this CTA
 //  attention units (warp 0): 12 cycles acquiring pages  13 cycles of q.K  14 cycles of the
 //               softmax  15 cycles of P.V
+//  GEMV phases (warp 0): 12 cycles in the tile dot products  13 cycles publishing partial
+//               sums (ticket)  14 cycles in the epilogues it ran and releasing the slots
+//               15 tiles + 1000 x epilogues it ran
 constexpr int FL_TRACE_FIELDS = 16;
 
 enum : int { FL_QKV = 0, FL_ATTN = 1, FL_RESID = 2, FL_SWIGLU = 3, FL_LM = 4 };
@@ -543,12 +546,34 @@ FDEV void fl_epilogue(const FParams &P, const FPhase &F, const PSeg &S, int lt, 
     }
 }
 
+// Ticket of a tile's partial sums: a CTA-scope acquire-release add on shared memory
+// (releases this warp's sums, acquires the earlier warps'), with no fence that would also
+// wait for this thread's global stores (the epilogues' outputs) to complete.
+// The counter wraps to 0 on the last warp's add (inc modulo FL_WARPS), ready for the
+// slot's next tile.
+FDEV unsigned int fl_ticket_add(unsigned int *p) {
+    unsigned int old;
+    asm volatile("atom.acq_rel.cta.shared::cta.inc.u32 %0, [%1], %2;"
+                 : "=r"(old)
+                 : "r"(smem_u32(p)), "r"((unsigned int)(FL_WARPS - 1))
+                 : "memory");
+    return old;
+}
+
+// Release of a ring slot by one warp: a relaxed arrival (the warp's reads of the slot have
+// all returned, their values are consumed, so no release ordering is needed; a release
+// would also wait for the epilogue's global stores).
+FDEV void fl_release_slot(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.relaxed.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
 // One tile of the phase, warp-level: decode + multiply this warp's super-blocks,
 // publish the partial sums; the last of the eight warps runs the epilogue and only
 // then frees the ring slot (the slot's partial sums stay valid until it is refilled).
 template <int T>
 FDEV void fl_tile(const FParams &P, const FPhase &F, const PSeg &S, int lt, const uint8_t *buf, const uint2 *xf,
-                  int d, uint32_t tag) {
+                  int d, uint32_t tag, unsigned long long *tr, long long (&tacc)[4]) {
+    const long long c0 = tr ? clock64() : 0;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
     const int nb = F.cols >> 8;
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
@@ -560,34 +585,38 @@ FDEV void fl_tile(const FParams &P, const FPhase &F, const PSeg &S, int lt, cons
 #pragma unroll
         for (int i = 0; i < 4; i++) acc[i] = fmaf(part[i], inv, acc[i]);
     }
+    const long long c1 = tr ? clock64() : 0;
     if (t == 0) {
         fl_red[d][warp][g] = acc[0] + acc[1];
         fl_red[d][warp][g + 8] = acc[2] + acc[3];
     }
-    __syncwarp();
+    __syncwarp();  // the warp's partial sums are written before lane 0 releases them
     unsigned int old = 0;
-    if (lane == 0) {
-        __threadfence_block();
-        old = atomicAdd(&fl_redcnt[d], 1u);
-    }
+    if (lane == 0) old = fl_ticket_add(&fl_redcnt[d]);
     old = __shfl_sync(0xffffffffu, old, 0);
+    const long long c2 = tr ? clock64() : 0;
     if (old == FL_WARPS - 1) {
-        __threadfence_block();
+        __syncwarp();  // lane 0 acquired the other warps' sums for the whole warp
         fl_epilogue(P, F, S, lt, d, tag);
         __syncwarp();
-        if (lane == 0) {
-            fl_redcnt[d] = 0u;
-            if (P.trace) atomicMax(&fl_tmark[1], gtimer());
-        }
+        if (lane == 0 && P.trace) atomicMax(&fl_tmark[1], gtimer());
         __syncwarp();
     }
-    if (lane == 0) mbar_arrive(&fl_empty[d]);
+    if (lane == 0) fl_release_slot(&fl_empty[d]);
+    if (tr) {  // registers here; the trace is written once per phase
+        tacc[0] += c1 - c0;
+        tacc[1] += c2 - c1;
+        tacc[2] += clock64() - c2;
+        tacc[3] += 1 + (old == FL_WARPS - 1 ? 1000 : 0);
+    }
 }
 
 // The CTA's tiles of one GEMV phase (tile = blockIdx.x + k * gridDim.x), warp-level.
-FDEV bool fl_tiles(const FParams &P, const FPhase &F, long long &seq, uint32_t tag, long long &wcycles) {
+FDEV bool fl_tiles(const FParams &P, const FPhase &F, long long &seq, uint32_t tag, long long &wcycles,
+                   unsigned long long *tr) {
     const int nb = F.cols >> 8;
     const uint2 *xf0 = fl_frag(P), *xf1 = xf0 + (size_t)nb * 128;
+    long long tacc[4] = {0, 0, 0, 0};
     for (int tile = blockIdx.x; tile < F.n_tiles; tile += gridDim.x) {
         int sidx, lt;
         fl_locate(F, tile, sidx, lt);
@@ -597,12 +626,14 @@ FDEV bool fl_tiles(const FParams &P, const FPhase &F, long long &seq, uint32_t t
         const int d = (int)(seq % FL_NDESC);
         const uint2 *xf = (S.type == F.seg[0].type) ? xf0 : xf1;
         switch (S.type) {
-        case T_Q4_K: fl_tile<T_Q4_K>(P, F, S, lt, buf, xf, d, tag); break;
-        case T_Q6_K: fl_tile<T_Q6_K>(P, F, S, lt, buf, xf, d, tag); break;
-        default: fl_tile<T_F16>(P, F, S, lt, buf, xf, d, tag); break;
+        case T_Q4_K: fl_tile<T_Q4_K>(P, F, S, lt, buf, xf, d, tag, tr, tacc); break;
+        case T_Q6_K: fl_tile<T_Q6_K>(P, F, S, lt, buf, xf, d, tag, tr, tacc); break;
+        default: fl_tile<T_F16>(P, F, S, lt, buf, xf, d, tag, tr, tacc); break;
         }
         seq++;
     }
+    if (tr)
+        for (int i = 0; i < 4; i++) tr[12 + i] = (unsigned long long)tacc[i];
     return true;
 }
 
@@ -759,6 +790,7 @@ struct FlowAttn {
         const uint32_t nk_a = smem_u32(nk), nv_a = smem_u32(nv);
         const int p0 = (int)((long long)j * nch / S), p1 = (int)((long long)(j + 1) * nch / S);
         bool ok = true;
+        long long tacc[4] = {0, 0, 0, 0};  // trace: acquire, q.K, softmax, P.V cycles
         for (int pg = p0; pg < p1; pg++) {
             if ((pg - p0) % FL_WARPS != warp) {
                 seq++;
@@ -768,7 +800,7 @@ struct FlowAttn {
             auto tmark = [&](int field) {
                 if (tr) {
                     const long long n2 = clock64();
-                    tr[field] += (unsigned long long)(n2 - ct);
+                    tacc[field - 12] += n2 - ct;
                     ct = n2;
                 }
             };
@@ -858,6 +890,8 @@ struct FlowAttn {
             __syncwarp();
             if (lane == 0) mbar_arrive_n(&fl_empty[d], FL_WARPS);  // the page's only reader frees it
         }
+        if (tr)
+            for (int i = 0; i < 4; i++) tr[12 + i] = (unsigned long long)tacc[i];
         // warp state of head gl -> shared memory
         l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
         l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
@@ -1141,7 +1175,7 @@ __global__ void __launch_bounds__(FL_THREADS, 1) decode_flow_kernel(const __grid
                 if (nch > 0 && u < units) ok = FlowAttn<HD, G>::unit(P, F, u / S, u % S, S, pos, nch, seq, tag, wcycles, tr);
             } else if ((int)blockIdx.x < F.stage_ctas) {
                 ok = fl_stage_warp(P, F, tag, token0, tr);
-                if (ok) ok = fl_tiles(P, F, seq, tag, wcycles);
+                if (ok) ok = fl_tiles(P, F, seq, tag, wcycles, tr);
                 ok = !cbar_any(!ok || fl_abort);  // all warps past their tiles (epilogues done)
             }
             if (ok && F.kind == FL_LM) fl_argmax_finish(P);

@@ -358,8 +358,8 @@ class Context:
 
     FLOW_TRACE_FIELDS = ["t_start_ns", "cyc_poll", "cyc_stage", "cyc_phase", "cyc_wait_ring", "t_end_ns",
                          "t_producer_done_ns", "cyc_producer_wait", "cyc_attn_pages", "cyc_attn_merge",
-                         "t_inputs_staged_ns", "t_last_epilogue_ns", "cyc_attn_acquire", "cyc_attn_qk",
-                         "cyc_attn_softmax", "cyc_attn_pv"]
+                         "t_inputs_staged_ns", "t_last_epilogue_ns", "cyc_attn_acquire_or_dots",
+                         "cyc_attn_qk_or_publish", "cyc_attn_softmax_or_n_epilogues", "cyc_attn_pv_or_n_tiles"]
 
     def trace_step(self, kv: KVCache, token: int, pos: int, max_phases: int = 4096, max_ctas: int = 1024):
         """Per-phase, per-CTA timeline of one one-kernel step: uint64 array

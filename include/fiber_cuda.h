@@ -111,12 +111,14 @@ int fiber_decode_sample(fiber_ctx_t *ctx, kv_cache_t *kv, int32_t first_token, i
                         int n_steps, float temperature, int top_k, float top_p,
                         unsigned long long *rng_state, int32_t *h_tokens_out, float *ms_out);
 
-/* How a decode step runs. mode 0 (default when the model fits): one cooperative
- * persistent kernel per step -- every SM streams its weight tiles of all phases
- * through a shared-memory ring and the phases are separated by grid barriers.
- * mode 1: one kernel per phase (2 + 5 * n_layers launches, PDL-chained).
- * Both give the same tokens; mode 1 also serves models the persistent kernel
- * does not cover (Q5_K weights). Returns FIBER_EUNSUPPORTED for mode 0 then. */
+/* How a decode step runs. mode 2 (default when the model fits): one cooperative
+ * dataflow kernel per step -- every SM streams its weight tiles of all phases through
+ * a shared-memory ring, and each phase waits only for the words of its input (tagged
+ * with the launch), not for a grid barrier. mode 0: the same kernel shape with a grid
+ * barrier between phases (persistent kernel). mode 1: one kernel per phase
+ * (2 + 5 * n_layers launches, PDL-chained). All give the same tokens; mode 1 also
+ * serves models the one-kernel steps do not cover (Q5_K weights). Returns
+ * FIBER_EUNSUPPORTED for mode 0 or 2 then. */
 int fiber_set_decode_mode(fiber_ctx_t *ctx, int mode);
 
 /* Tokens per pass of the batched prefill through the layer stack. */
