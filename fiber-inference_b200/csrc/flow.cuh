@@ -37,13 +37,14 @@ namespace fiber {
 
 constexpr int FL_WARPS = 8;
 constexpr int FL_CONSUMERS = FL_WARPS * 32;
-// + a producer warpgroup (warps 8..11; lane 0 of warp 8 streams the ring). With 12
-// warps the launch gives every thread 168 registers (three warps share each SM
-// sub-partition's register file); the producer group then drops to FL_REG_PRODUCER
-// and the consumer warps rise to FL_REG_CONSUMER (setmaxnreg): 4 x 32 x 40 +
-// 8 x 32 x 232 = 12 x 32 x 168, exactly the launch's registers.
+// + a producer warpgroup (warps 8..11): lane 0 of warp 8 streams the ring, warp 9 runs
+// the tile epilogues. With 12 warps the launch gives every thread 168 registers (three
+// warps share each SM sub-partition's register file); the producer group then drops to
+// FL_REG_PRODUCER and the consumer warps rise to FL_REG_CONSUMER (setmaxnreg):
+// 4 x 32 x 56 + 8 x 32 x 224 = 12 x 32 x 168, exactly the launch's registers.
 constexpr int FL_THREADS = FL_CONSUMERS + 128;
-constexpr int FL_REG_PRODUCER = 40, FL_REG_CONSUMER = 232;
+constexpr int FL_EPI_WARP = FL_WARPS + 1;
+constexpr int FL_REG_PRODUCER = 56, FL_REG_CONSUMER = 224;
 static_assert(4 * 32 * FL_REG_PRODUCER + 8 * 32 * FL_REG_CONSUMER <= FL_THREADS * 168, "register split");
 constexpr int FL_NDESC = 16;                   // ring slots
 constexpr unsigned long long FL_WAIT_NS = 2000000000ull;
@@ -59,9 +60,10 @@ constexpr int FL_RING_PAD = 1024;              // the ring starts at the first 1
 //               11 globaltimer after the last tile epilogue of this CTA
 //  attention units (warp 0): 12 cycles acquiring pages  13 cycles of q.K  14 cycles of the
 //               softmax  15 cycles of P.V
-//  GEMV phases (warp 0): 12 cycles in the tile dot products  13 cycles publishing partial
-//               sums (ticket)  14 cycles in the epilogues it ran and releasing the slots
-//               15 tiles + 1000 x epilogues it ran
+//  GEMV phases: 11 globaltimer after the last tile epilogue of this CTA (epilogue warp)
+//               12 cycles warp 0 spent in its tile dot products  13 cycles publishing them
+//               15 tiles of warp 0; epilogue warp: 8 cycles waiting for partial sums,
+//               9 cycles in epilogues, 14 globaltimer when it started the phase
 constexpr int FL_TRACE_FIELDS = 16;
 
 enum : int { FL_QKV = 0, FL_ATTN = 1, FL_RESID = 2, FL_SWIGLU = 3, FL_LM = 4 };
@@ -122,17 +124,18 @@ extern __shared__ __align__(128) uint8_t fl_dyn[];
 __shared__ __align__(8) uint64_t fl_full[FL_NDESC];
 __shared__ __align__(8) uint64_t fl_empty[FL_NDESC];
 __shared__ __align__(16) FPhase fl_F[2];
+__shared__ __align__(16) FPhase fl_E[2];  // the epilogue warp's own copies (it runs behind the consumers)
 __shared__ __align__(16) float fl_red[FL_NDESC][FL_WARPS][TC_M];  // per ring slot: warp partial sums
-__shared__ unsigned int fl_redcnt[FL_NDESC];                          // warps done with the slot's tile
+__shared__ __align__(8) uint64_t fl_done[FL_NDESC];  // per ring slot: the eight warps' partial sums written
 __shared__ float fl_stat[2 * FL_WARPS];
 __shared__ unsigned long long fl_best;   // this CTA's best logit key
 __shared__ int fl_tile_off[FL_NDESC];
 __shared__ volatile int fl_abort;
-__shared__ unsigned int fl_ticket;
 constexpr int FL_MAX_CHUNKS = 64;        // input length / 256 at most (16384 elements)
 __shared__ float fl_cinv[FL_MAX_CHUNKS]; // staged input: per-chunk inverse fragment scale
-__shared__ float fl_wss[FL_WARPS];       // staged input: per-warp sums of x^2 (RMSNorm)
-__shared__ unsigned long long fl_tmark[2];  // trace: inputs staged, last epilogue (globaltimer)
+__shared__ float fl_wss[4][FL_WARPS];    // staged input of phase ph: per-warp sums of x^2 (RMSNorm),
+                                         // at ph % 4 (the epilogue warp may run a phase or two behind)
+__shared__ unsigned long long fl_tmark[1];  // trace: globaltimer when the inputs were staged
 __shared__ float2 fl_rope[64];           // RoPE (cos, sin) row of this launch's position
 
 FDEV uint8_t *fl_ring() { return fl_dyn + ((FL_RING_PAD - (smem_u32(fl_dyn) & (FL_RING_PAD - 1))) & (FL_RING_PAD - 1)); }
@@ -354,7 +357,7 @@ __device__ __noinline__ void fl_embed_chunk(const FParams &P, int tok, int b, fl
 // the chunk's dot products) and write its fragments for each weight type of the phase.
 // Two chunks at a time (eight 16-byte loads in flight per lane). Warp-level; returns
 // false (warp-uniform) when stopped.
-__device__ __noinline__ bool fl_stage_warp(const FParams &P, const FPhase &F, uint32_t tag, int token,
+__device__ __noinline__ bool fl_stage_warp(const FParams &P, const FPhase &F, int ph, uint32_t tag, int token,
                                            unsigned long long *tr) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n = F.cols, nb = n >> 8;
@@ -466,7 +469,7 @@ __device__ __noinline__ bool fl_stage_warp(const FParams &P, const FPhase &F, ui
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
     if (lane == 0) {
-        fl_wss[warp] = ss;
+        fl_wss[ph & 3][warp] = ss;
         if (P.trace) atomicMax(&fl_tmark[0], gtimer());
     }
     __syncwarp();
@@ -477,11 +480,11 @@ __device__ __noinline__ bool fl_stage_warp(const FParams &P, const FPhase &F, ui
     return true;
 }
 
-// RMSNorm factor of the staged input from the eight warps' sums (fixed order).
-FDEV float fl_rrms(const FPhase &F) {
+// RMSNorm factor of phase ph's staged input from the eight warps' sums (fixed order).
+FDEV float fl_rrms(const FPhase &F, int ph) {
     float ss = 0.f;
 #pragma unroll
-    for (int w = 0; w < FL_WARPS; w++) ss += fl_wss[w];
+    for (int w = 0; w < FL_WARPS; w++) ss += fl_wss[ph & 3][w];
     return 1.0f / sqrtf(ss / (float)F.cols + F.eps);
 }
 
@@ -495,7 +498,7 @@ FDEV unsigned long long fl_key(float v, int idx) {
 
 // Epilogue of one tile (the last warp to finish it): lanes 0..15 own its rows; in a
 // SwiGLU tile lane j < 8 owns output row 8 lt + j (gate in MMA row j, up in row j + 8).
-FDEV void fl_epilogue(const FParams &P, const FPhase &F, const PSeg &S, int lt, int d, uint32_t tag) {
+FDEV void fl_epilogue(const FParams &P, const FPhase &F, const PSeg &S, int lt, int d, uint32_t tag, float rrms) {
     const int lane = threadIdx.x & 31;
     const bool pair = F.kind == FL_SWIGLU;
     if (lane < (pair ? TC_M / 2 : TC_M)) {
@@ -508,7 +511,6 @@ FDEV void fl_epilogue(const FParams &P, const FPhase &F, const PSeg &S, int lt, 
             for (int w = 0; w < FL_WARPS; w++) v1 += fl_red[d][w][lane + TC_M / 2];
         }
         if (F.norm_w) {  // y = rrms * W (x * w)
-            const float rrms = fl_rrms(F);
             v0 *= rrms;
             v1 *= rrms;
         }
@@ -546,20 +548,6 @@ FDEV void fl_epilogue(const FParams &P, const FPhase &F, const PSeg &S, int lt, 
     }
 }
 
-// Ticket of a tile's partial sums: a CTA-scope acquire-release add on shared memory
-// (releases this warp's sums, acquires the earlier warps'), with no fence that would also
-// wait for this thread's global stores (the epilogues' outputs) to complete.
-// The counter wraps to 0 on the last warp's add (inc modulo FL_WARPS), ready for the
-// slot's next tile.
-FDEV unsigned int fl_ticket_add(unsigned int *p) {
-    unsigned int old;
-    asm volatile("atom.acq_rel.cta.shared::cta.inc.u32 %0, [%1], %2;"
-                 : "=r"(old)
-                 : "r"(smem_u32(p)), "r"((unsigned int)(FL_WARPS - 1))
-                 : "memory");
-    return old;
-}
-
 // Release of a ring slot by one warp: a relaxed arrival (the warp's reads of the slot have
 // all returned, their values are consumed, so no release ordering is needed; a release
 // would also wait for the epilogue's global stores).
@@ -567,9 +555,10 @@ FDEV void fl_release_slot(uint64_t *bar) {
     asm volatile("mbarrier.arrive.relaxed.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
-// One tile of the phase, warp-level: decode + multiply this warp's super-blocks,
-// publish the partial sums; the last of the eight warps runs the epilogue and only
-// then frees the ring slot (the slot's partial sums stay valid until it is refilled).
+// One tile of the phase, warp-level: decode + multiply this warp's super-blocks and
+// publish the partial sums (fl_done[d]); the epilogue warp sums the eight and runs the
+// epilogue, then frees the slot with the last of its nine arrivals (the partial sums
+// live with the slot until it is refilled).
 template <int T>
 FDEV void fl_tile(const FParams &P, const FPhase &F, const PSeg &S, int lt, const uint8_t *buf, const uint2 *xf,
                   int d, uint32_t tag, unsigned long long *tr, long long (&tacc)[4]) {
@@ -591,23 +580,14 @@ FDEV void fl_tile(const FParams &P, const FPhase &F, const PSeg &S, int lt, cons
         fl_red[d][warp][g + 8] = acc[2] + acc[3];
     }
     __syncwarp();  // the warp's partial sums are written before lane 0 releases them
-    unsigned int old = 0;
-    if (lane == 0) old = fl_ticket_add(&fl_redcnt[d]);
-    old = __shfl_sync(0xffffffffu, old, 0);
-    const long long c2 = tr ? clock64() : 0;
-    if (old == FL_WARPS - 1) {
-        __syncwarp();  // lane 0 acquired the other warps' sums for the whole warp
-        fl_epilogue(P, F, S, lt, d, tag);
-        __syncwarp();
-        if (lane == 0 && P.trace) atomicMax(&fl_tmark[1], gtimer());
-        __syncwarp();
+    if (lane == 0) {
+        mbar_arrive(&fl_done[d]);        // release: the epilogue warp reads the sums
+        fl_release_slot(&fl_empty[d]);  // this warp's reads of the slot are done
     }
-    if (lane == 0) fl_release_slot(&fl_empty[d]);
     if (tr) {  // registers here; the trace is written once per phase
         tacc[0] += c1 - c0;
-        tacc[1] += c2 - c1;
-        tacc[2] += clock64() - c2;
-        tacc[3] += 1 + (old == FL_WARPS - 1 ? 1000 : 0);
+        tacc[1] += clock64() - c1;
+        tacc[3] += 1;
     }
 }
 
@@ -888,7 +868,7 @@ struct FlowAttn {
             }
             tmark(15);
             __syncwarp();
-            if (lane == 0) mbar_arrive_n(&fl_empty[d], FL_WARPS);  // the page's only reader frees it
+            if (lane == 0) mbar_arrive_n(&fl_empty[d], FL_WARPS + 1);  // the page's only reader frees it
         }
         if (tr)
             for (int i = 0; i < 4; i++) tr[12 + i] = (unsigned long long)tacc[i];
@@ -973,35 +953,106 @@ struct FlowAttn {
 
 // ---- argmax, exit -------------------------------------------------------------------------
 
-// After the lm_head phase: publish this CTA's best key; the last CTA reduces all of
-// them, writes the token and (loop mode) advances the step state.
+// After the lm_head phase, by the epilogue warp once it ran this CTA's last lm_head
+// epilogue: publish the CTA's best key; the last CTA reduces all of them, writes the token
+// and (loop mode) advances the step state.
 FDEV void fl_argmax_finish(const FParams &P) {
-    const int tid = threadIdx.x, lane = tid & 31;
-    cbar();  // every epilogue of this CTA is done
-    if (tid == 0) {
+    const int lane = threadIdx.x & 31;
+    unsigned int ticket = 0;
+    if (lane == 0) {
         P.am_key[blockIdx.x] = fl_best;
         __threadfence();
-        fl_ticket = atomicAdd(P.am_count, 1u);
+        ticket = atomicAdd(P.am_count, 1u);
     }
-    cbar();
-    if (fl_ticket != gridDim.x - 1) return;
+    ticket = __shfl_sync(0xffffffffu, ticket, 0);
+    if (ticket != gridDim.x - 1) return;
     __threadfence();
-    if (tid < 32) {
-        unsigned long long best = 0ull;
-        for (int i = lane; i < (int)gridDim.x; i += 32) best = max(best, __ldcg(P.am_key + i));
+    unsigned long long best = 0ull;
+    for (int i = lane; i < (int)gridDim.x; i += 32) best = max(best, __ldcg(P.am_key + i));
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) best = max(best, __shfl_xor_sync(0xffffffffu, best, o));
-        if (lane == 0) {
-            const int bi = (int)(0xFFFFFFFFu - (uint32_t)(best & 0xFFFFFFFFu));
-            *P.io_argmax = bi;
-            if (P.loop) {
-                *P.io_token = bi;
-                *P.io_pos = *P.io_pos + 1;
-                const int st = *P.io_step;
-                P.rec_tokens[st] = bi;
-                *P.io_step = st + 1;
+    for (int o = 16; o > 0; o >>= 1) best = max(best, __shfl_xor_sync(0xffffffffu, best, o));
+    if (lane == 0) {
+        const int bi = (int)(0xFFFFFFFFu - (uint32_t)(best & 0xFFFFFFFFu));
+        *P.io_argmax = bi;
+        if (P.loop) {
+            *P.io_token = bi;
+            *P.io_pos = *P.io_pos + 1;
+            const int st = *P.io_step;
+            P.rec_tokens[st] = bi;
+            *P.io_step = st + 1;
+        }
+        *P.am_count = 0u;
+    }
+}
+
+// The epilogue warp: walks the phases as the consumer warps do (descriptors read from
+// global memory), and for each of this CTA's GEMV tiles waits until the eight warps have
+// published their partial sums, runs the epilogue (residual add, SwiGLU, q|k|v store,
+// logits + argmax candidate) and frees the ring slot. Attention pages take ring slots
+// without an epilogue (their reader frees them). Every wait is bounded.
+__device__ __noinline__ void fl_epilogue_warp(const FParams &P, int nch, int S, uint32_t tag) {
+    const int lane = threadIdx.x & 31;
+    const int units = P.n_kv * S, u = (int)gridDim.x - 1 - (int)blockIdx.x;
+    long long seq = 0;
+    uint32_t done_phase = 0;  // parity of each slot's fl_done barrier, one bit per slot
+    fl_fetch_phase(&fl_E[0], P.phases, lane);
+    for (int ph = 0; ph < P.n_phases; ph++) {
+        cp_async_wait_all();  // descriptor ph is in fl_E[ph & 1]; fetch the next one behind it
+        __syncwarp();
+        if (ph + 1 < P.n_phases) fl_fetch_phase(&fl_E[(ph + 1) & 1], P.phases + ph + 1, lane);
+        const FPhase &F = fl_E[ph & 1];
+        const int kind = F.kind;
+        if (kind == FL_ATTN) {
+            if (nch > 0 && u < units) {
+                const int j = u % S;
+                seq += (int)((long long)(j + 1) * nch / S) - (int)((long long)j * nch / S);
             }
-            *P.am_count = 0u;
+            continue;
+        }
+        float rrms = 1.0f;
+        bool have_rrms = F.norm_w == nullptr;
+        long long cw = 0, ce = 0;  // trace: cycles waiting for partial sums, in epilogues
+        const unsigned long long t_ph = P.trace ? gtimer() : 0ull;
+        if ((int)blockIdx.x < F.stage_ctas) {
+            for (int tile = blockIdx.x; tile < F.n_tiles; tile += gridDim.x) {
+                int sidx, lt;
+                fl_locate(F, tile, sidx, lt);
+                const int d = (int)(seq % FL_NDESC);
+                int ok = 1;
+                const long long c0 = clock64();
+                if (lane == 0) {
+                    ok = fl_mbar_wait(&fl_done[d], (done_phase >> d) & 1u);
+                    if (!ok) fl_fail(P);
+                }
+                ok = __shfl_sync(0xffffffffu, ok, 0);
+                if (!ok) {
+                    cp_async_wait_all();  // the next descriptor's copy lands before the warp leaves
+                    return;
+                }
+                const long long c1 = clock64();
+                cw += c1 - c0;
+                done_phase ^= 1u << d;
+                if (!have_rrms) {  // the eight warps wrote their sums before their first tile
+                    rrms = fl_rrms(F, ph);
+                    have_rrms = true;
+                }
+                fl_epilogue(P, F, F.seg[sidx], lt, d, tag, rrms);
+                __syncwarp();
+                if (lane == 0) fl_release_slot(&fl_empty[d]);
+                ce += clock64() - c1;
+                seq++;
+            }
+        }
+        if (kind == FL_LM) {
+            __syncwarp();
+            fl_argmax_finish(P);
+        }
+        if (P.trace && lane == 0) {
+            unsigned long long *tr = P.trace + ((size_t)ph * gridDim.x + blockIdx.x) * FL_TRACE_FIELDS;
+            tr[8] = (unsigned long long)cw;
+            tr[9] = (unsigned long long)ce;
+            tr[11] = gtimer();
+            tr[14] = t_ph;
         }
     }
 }
@@ -1123,13 +1174,13 @@ __global__ void __launch_bounds__(FL_THREADS, 1) decode_flow_kernel(const __grid
     if (tid == 0) {
         for (int d = 0; d < FL_NDESC; d++) {
             mbar_init(&fl_full[d], 1);
-            mbar_init(&fl_empty[d], FL_WARPS);  // one arrival per consumer warp
-            fl_redcnt[d] = 0u;
+            mbar_init(&fl_empty[d], FL_WARPS + 1);  // each consumer warp + the epilogue warp
+            mbar_init(&fl_done[d], FL_WARPS);       // each consumer warp's partial sums
         }
         mbar_fence_init();
         fl_abort = 0;
         fl_best = 0ull;
-        fl_tmark[0] = fl_tmark[1] = 0ull;
+        fl_tmark[0] = 0ull;
     }
     if (warp == 0) fl_fetch_phase(&fl_F[0], P.phases, lane);
     cp_async_wait_all();
@@ -1154,6 +1205,7 @@ __global__ void __launch_bounds__(FL_THREADS, 1) decode_flow_kernel(const __grid
         // device-side guard): every phase is skipped, the tag still advances
     } else if (warp >= FL_WARPS) {
         if (tid == FL_CONSUMERS) fl_producer<HD>(P, pos, nch, S);
+        if (warp == FL_EPI_WARP) fl_epilogue_warp(P, nch, S, tag);
     } else {
         long long seq = 0;
         const int units = P.n_kv * S;
@@ -1174,21 +1226,17 @@ __global__ void __launch_bounds__(FL_THREADS, 1) decode_flow_kernel(const __grid
             if (F.kind == FL_ATTN) {
                 if (nch > 0 && u < units) ok = FlowAttn<HD, G>::unit(P, F, u / S, u % S, S, pos, nch, seq, tag, wcycles, tr);
             } else if ((int)blockIdx.x < F.stage_ctas) {
-                ok = fl_stage_warp(P, F, tag, token0, tr);
+                ok = fl_stage_warp(P, F, ph, tag, token0, tr);
                 if (ok) ok = fl_tiles(P, F, seq, tag, wcycles, tr);
-                ok = !cbar_any(!ok || fl_abort);  // all warps past their tiles (epilogues done)
+                ok = !cbar_any(!ok || fl_abort);  // all warps past their tiles (the epilogue warp follows)
             }
-            if (ok && F.kind == FL_LM) fl_argmax_finish(P);
             cp_async_wait_all();
             if (tr) {
                 tr[3] = (unsigned long long)(clock64() - c0);
                 tr[4] = (unsigned long long)wcycles;
                 tr[5] = gtimer();
-                if (F.kind != FL_ATTN) {
-                    tr[10] = fl_tmark[0];
-                    tr[11] = fl_tmark[1];
-                }
-                fl_tmark[0] = fl_tmark[1] = 0ull;  // the next phase starts after a barrier
+                if (F.kind != FL_ATTN) tr[10] = fl_tmark[0];
+                fl_tmark[0] = 0ull;  // the next phase starts after a barrier
             }
             if (!ok) break;
         }
