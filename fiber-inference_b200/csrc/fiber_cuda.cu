@@ -470,6 +470,8 @@ extern "C" void fiber_cuda_free(fiber_ctx_t *c) {
 }
 
 static bool tc_type_ok(int t) { return t == T_Q4_K || t == T_Q6_K || t == T_F16; }
+// the dataflow step also takes Q5_K (fp32 weights as hi + lo fp16 MMA fragments)
+static bool fl_type_ok(int t) { return tc_type_ok(t) || t == T_Q5_K; }
 
 static PSeg make_pseg(const uint8_t *w, const uint8_t *w2, int type, int rows, int out_off, int cols) {
     PSeg sg;
@@ -674,10 +676,10 @@ static int flow_build(gpu_context *c) {
     const model_params_t &p = c->p;
     const int dim = p.dim, ffn = p.ffn_dim, kvd = c->kvd, hd = p.head_dim, L = (int)p.n_layers;
     c->fl_ok = false;
-    bool types_ok = tc_type_ok(c->t_out);
+    bool types_ok = fl_type_ok(c->t_out);
     for (const LayerDev &d : c->L) {
         const int ts[7] = {d.tq, d.tk, d.tv, d.to, d.t1, d.t2, d.t3};
-        for (int t : ts) types_ok = types_ok && tc_type_ok(t);
+        for (int t : ts) types_ok = types_ok && fl_type_ok(t);
         int distinct = 1 + (d.tk != d.tq) + (d.tv != d.tq && d.tv != d.tk);
         types_ok = types_ok && distinct <= 2;
     }

@@ -242,6 +242,25 @@ FDEV bool fl_mbar_wait(uint64_t *bar, uint32_t parity) {
     }
 }
 
+// Bounded wait for a warp that has nothing else to do (the producer on ring space, the
+// epilogue warp on partial sums): each try suspends the thread until the phase completes
+// or the hint (ns) runs out, so the wait takes no issue slots from the compute warps
+// that share its SM sub-partition.
+FDEV bool fl_mbar_wait_idle(uint64_t *bar, uint32_t parity) {
+    const uint32_t a = smem_u32(bar);
+    const unsigned long long t0 = gtimer();
+    for (;;) {
+        uint32_t ok;
+        asm volatile(
+            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+            : "=r"(ok)
+            : "r"(a), "r"(parity), "r"(20000u)
+            : "memory");
+        if (ok) return true;
+        if (fl_abort || gtimer() - t0 > FL_WAIT_NS) return false;
+    }
+}
+
 // Warp-level acquire of ring item `seq`: lane 0 waits, the warp agrees.
 FDEV const uint8_t *fl_acquire(const FParams &P, long long seq, long long &wcycles) {
     const int d = (int)(seq % FL_NDESC);
@@ -459,6 +478,7 @@ __device__ __noinline__ bool fl_stage_warp(const FParams &P, const FPhase &F, in
                 switch (pass ? type_b : F.seg[0].type) {
                 case T_Q4_K: fl_frags_chunk<T_Q4_K>(b, xs, norm ? nw : nullptr, scale, dst); break;
                 case T_Q6_K: fl_frags_chunk<T_Q6_K>(b, xs, norm ? nw : nullptr, scale, dst); break;
+                case T_Q5_K: fl_frags_chunk<T_Q5_K>(b, xs, norm ? nw : nullptr, scale, dst); break;
                 default: fl_frags_chunk<T_F16>(b, xs, norm ? nw : nullptr, scale, dst); break;
                 }
             }
@@ -608,6 +628,7 @@ FDEV bool fl_tiles(const FParams &P, const FPhase &F, long long &seq, uint32_t t
         switch (S.type) {
         case T_Q4_K: fl_tile<T_Q4_K>(P, F, S, lt, buf, xf, d, tag, tr, tacc); break;
         case T_Q6_K: fl_tile<T_Q6_K>(P, F, S, lt, buf, xf, d, tag, tr, tacc); break;
+        case T_Q5_K: fl_tile<T_Q5_K>(P, F, S, lt, buf, xf, d, tag, tr, tacc); break;
         default: fl_tile<T_F16>(P, F, S, lt, buf, xf, d, tag, tr, tacc); break;
         }
         seq++;
@@ -1021,7 +1042,7 @@ __device__ __noinline__ void fl_epilogue_warp(const FParams &P, int nch, int S, 
                 int ok = 1;
                 const long long c0 = clock64();
                 if (lane == 0) {
-                    ok = fl_mbar_wait(&fl_done[d], (done_phase >> d) & 1u);
+                    ok = fl_mbar_wait_idle(&fl_done[d], (done_phase >> d) & 1u);
                     if (!ok) fl_fail(P);
                 }
                 ok = __shfl_sync(0xffffffffu, ok, 0);
@@ -1078,7 +1099,7 @@ __device__ __noinline__ void fl_producer(const FParams &P, int pos, int nch, int
             if (seq - oldest < FL_NDESC && used + skip + size <= P.ring_bytes) break;
             const int od = (int)(oldest % FL_NDESC);
             const long long w0 = clock64();
-            const bool got = fl_mbar_wait(&fl_empty[od], (uint32_t)((oldest / FL_NDESC) & 1));
+            const bool got = fl_mbar_wait_idle(&fl_empty[od], (uint32_t)((oldest / FL_NDESC) & 1));
             pwait += clock64() - w0;
             if (!got) {
                 fl_fail(P);

@@ -153,6 +153,16 @@ struct TcType<T_Q4_K> {
     }
 };
 
+// Q5_K: the low four quant bits sit in the same nibble layout as Q4_K (qs at byte 48),
+// so the k-slot map is Q4_K's; the fifth bit of element 64g + 32s + w is bit 2g + s of
+// qh[w] (metal/kernels.metal:141-169).
+template <>
+struct TcType<T_Q5_K> {
+    static constexpr int BB = 176;
+    static HDCE int elem(int t, int s, int i) { return TcType<T_Q4_K>::elem(t, s, i); }
+    static HDCE void pos(int kk, int &t, int &s, int &i) { TcType<T_Q4_K>::pos(kk, t, s, i); }
+};
+
 template <>
 struct TcType<T_Q6_K> {
     static constexpr int BB = 210;
@@ -193,7 +203,8 @@ HDCE bool tc_pos_roundtrip() {
     }
     return true;
 }
-static_assert(tc_pos_roundtrip<T_Q4_K>() && tc_pos_roundtrip<T_Q6_K>() && tc_pos_roundtrip<T_F16>(),
+static_assert(tc_pos_roundtrip<T_Q4_K>() && tc_pos_roundtrip<T_Q5_K>() && tc_pos_roundtrip<T_Q6_K>() &&
+                  tc_pos_roundtrip<T_F16>(),
               "fragment slot maps must be inverse bijections on a super-block");
 
 // ---- per-type tile dot: accumulate one super-block of rows g, g+8 --------------------
@@ -305,6 +316,104 @@ struct TcDot<T_Q4_K> {
         }
 #pragma unroll
         for (int i = 0; i < 4; i++) acc[i] += acc2[i];
+    }
+};
+
+// Q5_K keeps the reference's fp32 weights (no fp16 rounding: d*sc*q - dmin*m rounded
+// once to fp32, as metal/kernels.metal:141-169 computes it). On the tensor cores each
+// weight, scaled by a power of two s per row and super-block (largest |w * s| in
+// [2^14, 2^15)), is split into fp16 hi + lo (~22 bits; the lo part stays normal), and
+// each k-step issues two MMAs (hi, lo) into the same accumulators; the row's partial
+// sums are scaled back by 1/s (exact).
+template <>
+struct TcDot<T_Q5_K> {
+    struct Row {
+        TcDot<T_Q4_K>::Row q;  // scales, mins and d as Q4_K; q.w = the lane's 8 quant words
+        uint32_t h[8];          // the 8 qh words (every lane reads all 32 bytes)
+        float s, inv;           // the row's power-of-two weight scale and its inverse
+    };
+
+    static FDEV void load_row(const uint8_t *blk, int t, Row &r) {
+        // header (d, dmin, 12 scale bytes) has Q4_K's layout; reuse its decode, then
+        // replace the quant words (qs at 48 instead of 16)
+        TcDot<T_Q4_K>::load_row(blk, t, r.q);
+        const uint4 q0 = *reinterpret_cast<const uint4 *>(blk + 48 + 32 * t);
+        const uint4 q1 = *reinterpret_cast<const uint4 *>(blk + 64 + 32 * t);
+        r.q.w[0] = q0.x; r.q.w[1] = q0.y; r.q.w[2] = q0.z; r.q.w[3] = q0.w;
+        r.q.w[4] = q1.x; r.q.w[5] = q1.y; r.q.w[6] = q1.z; r.q.w[7] = q1.w;
+        const uint4 h0 = *reinterpret_cast<const uint4 *>(blk + 16);
+        const uint4 h1 = *reinterpret_cast<const uint4 *>(blk + 32);
+        r.h[0] = h0.x; r.h[1] = h0.y; r.h[2] = h0.z; r.h[3] = h0.w;
+        r.h[4] = h1.x; r.h[5] = h1.y; r.h[6] = h1.z; r.h[7] = h1.w;
+        // |w| <= d * 63 * 31 + dmin * 63
+        const uint32_t hx = *reinterpret_cast<const uint32_t *>(blk);
+        const float bound = fmaf(h2f((uint16_t)(hx & 0xFFFF)), 1953.0f, h2f((uint16_t)(hx >> 16)) * 63.0f);
+        int eb = (int)((__float_as_uint(bound) >> 23) & 0xFF);
+        eb = max(15, min(eb, 254));  // bound in [2^(eb-127), 2^(eb-126))
+        r.s = __uint_as_float((uint32_t)(268 - eb) << 23);    // 2^(141 - eb): bound * s < 2^15
+        r.inv = __uint_as_float((uint32_t)(eb - 14) << 23);   // 1 / s
+    }
+
+    // hi and lo fragments of a pair of fp32 weights scaled by s
+    static FDEV void split(float a, float b, float s, uint32_t &hi, uint32_t &lo) {
+        const float as = a * s, bs = b * s;
+        hi = pack_f16x2(as, bs);
+        float ra, rb;
+        asm("{\n .reg .f16 l, u, m;\n mov.b32 {l, u}, %2;\n mov.b16 m, 0xBC00;\n"
+            " fma.rn.f32.f16 %0, l, m, %3;\n fma.rn.f32.f16 %1, u, m, %4;\n}\n"
+            : "=f"(ra), "=f"(rb)
+            : "r"(hi), "f"(as), "f"(bs));
+        lo = pack_f16x2(ra, rb);
+    }
+
+    // word u of the row: hi/lo fragments for k-steps 2u (f0, f2) and 2u + 1 (f1, f3)
+    static FDEV void frags(const Row &r, int u, int t, uint32_t (&fh)[4], uint32_t (&fl)[4]) {
+        const uint32_t w = r.q.w[u], w8 = w >> 8;
+        const uint32_t bl = (r.h[u] >> (2 * t)) & 0x01010101u, bh = (r.h[u] >> (2 * t + 1)) & 0x01010101u;
+        constexpr uint32_t M = 0x64006400u;
+        // 1024 + q (low nibbles, fifth bit at bit 4) and 1024 + 16 q (high nibbles, at bit 8)
+        const uint32_t h0 = lop3_or_and(w, 0x000F000Fu, M | ((bl & 0x00010001u) << 4));
+        const uint32_t h1 = lop3_or_and(w8, 0x000F000Fu, M | (((bl >> 8) & 0x00010001u) << 4));
+        const uint32_t h2 = lop3_or_and(w, 0x00F000F0u, M | ((bh & 0x00010001u) << 8));
+        const uint32_t h3 = lop3_or_and(w8, 0x00F000F0u, M | (((bh >> 8) & 0x00010001u) << 8));
+        const uint32_t n0 = hfma2_u(h0, r.q.A_lo, r.q.B_lo), n1 = hfma2_u(h1, r.q.A_lo, r.q.B_lo);
+        const uint32_t n2 = hfma2_u(h2, r.q.A_hi, r.q.B_hi), n3 = hfma2_u(h3, r.q.A_hi, r.q.B_hi);
+        float a, b;
+        mixed_fma2(n0, r.q.d16, r.q.c_lo, a, b);
+        split(a, b, r.s, fh[0], fl[0]);
+        mixed_fma2(n1, r.q.d16, r.q.c_lo, a, b);
+        split(a, b, r.s, fh[1], fl[1]);
+        mixed_fma2(n2, r.q.d16, r.q.c_hi, a, b);
+        split(a, b, r.s, fh[2], fl[2]);
+        mixed_fma2(n3, r.q.d16, r.q.c_hi, a, b);
+        split(a, b, r.s, fh[3], fl[3]);
+    }
+
+    static FDEV void run(const uint8_t *rowg, const uint8_t *rowg8, const uint2 *xf, int g, int t, float (&acc)[4]) {
+        Row ra, rb;
+        load_row(rowg, t, ra);
+        load_row(rowg8, t, rb);
+        float pa[4] = {0.f, 0.f, 0.f, 0.f}, pb[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+            uint32_t ah[4], al[4], bh[4], bl[4];
+            frags(ra, u, t, ah, al);
+            frags(rb, u, t, bh, bl);
+            uint2 x0 = make_uint2(0u, 0u), x1 = make_uint2(0u, 0u);
+            if (g < 2) {
+                x0 = xf[((2 * u) * 4 + t) * 2 + g];
+                x1 = xf[((2 * u + 1) * 4 + t) * 2 + g];
+            }
+            // k-step 2u: a0 = f0 (row g), a1 = f0 (row g + 8), a2 = f2, a3 = f2; 2u + 1: f1, f3
+            mma16816(pa, ah[0], bh[0], ah[2], bh[2], x0.x, x0.y);
+            mma16816(pb, al[0], bl[0], al[2], bl[2], x0.x, x0.y);
+            mma16816(pa, ah[1], bh[1], ah[3], bh[3], x1.x, x1.y);
+            mma16816(pb, al[1], bl[1], al[3], bl[3], x1.x, x1.y);
+        }
+        acc[0] = fmaf(pa[0] + pb[0], ra.inv, acc[0]);
+        acc[1] = fmaf(pa[1] + pb[1], ra.inv, acc[1]);
+        acc[2] = fmaf(pa[2] + pb[2], rb.inv, acc[2]);
+        acc[3] = fmaf(pa[3] + pb[3], rb.inv, acc[3]);
     }
 };
 

@@ -35,7 +35,7 @@ class SynthCfg(C.Structure):
         ("n_kv_heads", C.c_uint32), ("ffn_dim", C.c_uint32), ("vocab", C.c_uint32),
         ("context_length", C.c_uint32), ("rope_base", C.c_float), ("eps", C.c_float),
         ("recipe", C.c_int), ("weight_std", C.c_float), ("norm_value", C.c_float),
-        ("seed", C.c_uint64), ("tied", C.c_int), ("n_threads", C.c_int),
+        ("seed", C.c_uint64), ("tied", C.c_int), ("n_threads", C.c_int), ("ffn_norm_value", C.c_float),
     ]
 
 

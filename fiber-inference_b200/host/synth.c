@@ -544,7 +544,9 @@ static int write_gguf(const char *path, const fiber_synth_cfg_t *cfg, fiber_tens
         if (fill) {
             if (fill(user, td[i].role, td[i].layer, rows, cols, vals) != 0) ok = 0;
         } else if (td[i].role < 0) {
-            for (size_t e = 0; e < cols; e++) vals[e] = cfg->norm_value;
+            const float nv = td[i].role == FIBER_ROLE_FFN_NORM && cfg->ffn_norm_value > 0.0f ? cfg->ffn_norm_value
+                                                                                               : cfg->norm_value;
+            for (size_t e = 0; e < cols; e++) vals[e] = nv;
         } else {
 #pragma omp parallel for schedule(static)
             for (long long r = 0; r < (long long)rows; r++) {

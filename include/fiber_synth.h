@@ -39,6 +39,9 @@ typedef struct {
     uint64_t seed;
     int tied;      /* 1: no output.weight (classifier = token_embd) */
     int n_threads; /* <= 0: all available */
+    float ffn_norm_value; /* > 0: value of the ffn_norm weights instead of norm_value (a
+                           * large value grows the residual stream layer by layer while the
+                           * attention inputs stay normalised: activation-range tests) */
 } fiber_synth_cfg_t;
 
 /* Fill cfg with a named preset: "stories" (768/12/12/12/2048, F16, tied),
