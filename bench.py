@@ -95,17 +95,21 @@ class Clocks:
 
 # DRAM traffic of one decode_persistent_kernel launch from an ncu capture (decode step at
 # position 13): dram__bytes_read.sum + dram__bytes_write.sum, and that launch's algorithmic bytes.
+# dram__bytes_read.sum + dram__bytes_write.sum of one step-kernel launch under ncu (profiles/),
+# with the algorithmic bytes of that launch's KV position
 PK_CAPTURE = {"dram_bytes": 635_233_536 + 6_902_784, "algorithmic_bytes": 633_700_000, "position": 13}
+FL_CAPTURE = {"dram_bytes": 639_756_800 + 5_940_480, "algorithmic_bytes": 639_348_864, "position": 132}
 
 
 def traffic_of(mode: int, roof: dict) -> dict:
     """Per-launch DRAM traffic of the dominant kernel, scaled from the ncu capture by the
     algorithmic bytes of the timed launches (traffic tracks the bytes streamed)."""
-    if mode != 0:
+    cap = {0: PK_CAPTURE, 2: FL_CAPTURE}.get(mode)
+    if cap is None:
         return {"traffic": None}
-    ratio = PK_CAPTURE["dram_bytes"] / PK_CAPTURE["algorithmic_bytes"]
+    ratio = cap["dram_bytes"] / cap["algorithmic_bytes"]
     return {"traffic": roof["algorithmic_bytes_per_launch"] * ratio,
-            "traffic_source": f"ncu capture at position {PK_CAPTURE['position']}: traffic/algorithmic = {ratio:.3f}, "
+            "traffic_source": f"ncu capture at position {cap['position']}: traffic/algorithmic = {ratio:.3f}, "
                               "scaled to the timed launches' algorithmic bytes"}
 
 
