@@ -348,9 +348,10 @@ def measure_7b_tp(fb, torch, dist, rank, world, local, P: int, D: int, steps: in
     bytes_tok = WEIGHTS_7B + kv_bytes
     out = {"value": value, "unit": "tok/s", "n_gpus": world, "steps": steps, "warmup": warmup,
            "ms_per_step": ms_total / steps, "prompt": P, "decode_tokens_per_step": D, "parallelism": f"tp{world}",
-           "collective": {0: "none (one GPU)", 1: "NCCL all-reduce", 2: "one-shot peer-memory all-reduce"}[
-               ctx.tp_collective],
-           "step_mode": STEP_MODES[ctx.mode] + (", all-reduce after Wo and W_down" if world > 1 else ""),
+           "collective": {0: "none (one GPU)", 1: "NCCL all-reduce", 2: "one-shot peer-memory all-reduce",
+                          3: "fused into the step: peer stores of the Wo / W_down partial sums, summed by "
+                             "the next phase"}[ctx.tp_collective],
+           "step_mode": STEP_MODES[ctx.mode] + (", exchange after Wo and W_down" if world > 1 else ""),
            "tokens_identical_on_all_ranks": same, "prefill_tok_s": prefill_tps,
            "roofline": {"bound": "hbm", "achieved": bytes_tok * value / world / 1e9, "peak": peak, "unit": "GB/s",
                         "frac": bytes_tok * value / world / 1e9 / peak, "peak_source": peak_kind,

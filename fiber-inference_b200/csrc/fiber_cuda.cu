@@ -386,6 +386,8 @@ struct gpu_context {
     void *pk_kernel = nullptr;
     // dataflow one-kernel step (flow.cuh)
     bool fl_ok = false;               // the model fits the dataflow kernel
+    uint64_t *fl_tp_local = nullptr;  // tensor parallel: this rank's exchange buffer of partial sums
+    void *fl_tp_peer[FL_MAX_TP] = {}; // the other ranks' exchange buffers, mapped here (CUDA IPC)
     FPhase *d_fphases = nullptr;
     std::vector<FPhase> fphases;
     uint64_t *fl_words = nullptr;     // tagged words of every phase output of one step
@@ -451,6 +453,9 @@ extern "C" void fiber_cuda_free(fiber_ctx_t *c) {
     free_graph(c->g_batch);
     for (void *q : c->ar_peer)
         if (q) cudaIpcCloseMemHandle(q);
+    for (void *q : c->fl_tp_peer)
+        if (q) cudaIpcCloseMemHandle(q);
+    if (c->fl_tp_local) cudaFree(c->fl_tp_local);
     if (c->ar_local) cudaFree(c->ar_local);
     if (c->ar_epoch) cudaFree(c->ar_epoch);
     if (c->comm) ncclCommDestroy(c->comm);
@@ -670,12 +675,45 @@ static void *fl_kernel_ptr() {
     return reinterpret_cast<void *>(decode_flow_kernel<HD, G>);
 }
 
+// Tensor parallel: this rank's exchange buffer for the dataflow step (n_words tagged words,
+// zeroed: tag 0 is never a launch's), and every other rank's, mapped here with CUDA IPC
+// (handles all-gathered over the group's NCCL communicator).
+static int fl_tp_setup(gpu_context *c, size_t n_words) {
+    const int W = c->tp_world, R = c->tp_rank;
+    CK(cudaMalloc(&c->fl_tp_local, n_words * 8));
+    CK(cudaMemset(c->fl_tp_local, 0, n_words * 8));
+    cudaIpcMemHandle_t mine;
+    CK(cudaIpcGetMemHandle(&mine, c->fl_tp_local));
+    uint8_t *d_h = nullptr;
+    CK(cudaMalloc(&d_h, (size_t)(W + 1) * sizeof(mine)));
+    std::vector<cudaIpcMemHandle_t> all(W);
+    cudaError_t e = cudaMemcpy(d_h + (size_t)W * sizeof(mine), &mine, sizeof(mine), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess &&
+        ncclAllGather(d_h + (size_t)W * sizeof(mine), d_h, sizeof(mine), ncclUint8, c->comm, c->stream) != ncclSuccess)
+        e = cudaErrorUnknown;
+    if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+    if (e == cudaSuccess) e = cudaMemcpy(all.data(), d_h, (size_t)W * sizeof(mine), cudaMemcpyDeviceToHost);
+    cudaFree(d_h);
+    if (e != cudaSuccess) return set_err(FIBER_ECUDA, "dataflow exchange setup (handle exchange): %s", cudaGetErrorString(e));
+    for (int q = 0; q < W; q++) {
+        if (q == R) continue;
+        void *base = nullptr;
+        CK(cudaIpcOpenMemHandle(&base, all[q], cudaIpcMemLazyEnablePeerAccess));
+        c->fl_tp_peer[q] = base;
+    }
+    return FIBER_OK;
+}
+
 // Phase table, tagged-word buffers and launch geometry of the dataflow step kernel;
 // leaves fl_ok false when the model does not fit it.
 static int flow_build(gpu_context *c) {
     const model_params_t &p = c->p;
-    const int dim = p.dim, ffn = p.ffn_dim, kvd = c->kvd, hd = p.head_dim, L = (int)p.n_layers;
+    // this rank's shard (the whole model on one GPU): query heads, KV heads, FFN rows
+    const int dim = p.dim, hd = p.head_dim, L = (int)p.n_layers;
+    const int qd = c->nh_l * hd, kvd = c->nkv_l * hd, ffn = c->ffn_l;
+    const int W = c->tp_world > 1 ? c->tp_world : 1;
     c->fl_ok = false;
+    if (W > FL_MAX_TP) return FIBER_OK;
     bool types_ok = fl_type_ok(c->t_out);
     for (const LayerDev &d : c->L) {
         const int ts[7] = {d.tq, d.tk, d.tv, d.to, d.t1, d.t2, d.t3};
@@ -693,23 +731,31 @@ static int flow_build(gpu_context *c) {
     FL_CASE(128, 1) FL_CASE(128, 2) FL_CASE(128, 4) FL_CASE(128, 8)
 #undef FL_CASE
     // per-chunk fragment scales are kept for at most FL_MAX_CHUNKS chunks of 256 inputs
-    if (dim / 256 > FL_MAX_CHUNKS || ffn / 256 > FL_MAX_CHUNKS) types_ok = false;
+    if (dim / 256 > FL_MAX_CHUNKS || ffn / 256 > FL_MAX_CHUNKS || qd % 256) types_ok = false;
     if (!types_ok || !c->fl_kernel) return FIBER_OK;
     int sms = 0;
     CK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, c->device));
     const int grid = sms;
 
     // tagged words: per layer x (input of QKV), q|k|v, attention, x after Wo, h; then the final x
-    const size_t per_layer = (size_t)dim + (dim + 2 * kvd) + dim + dim + ffn;
+    const size_t per_layer = (size_t)dim + (qd + 2 * kvd) + qd + dim + ffn;
     const size_t n_words = per_layer * L + dim;
     CK(cudaMalloc(&c->fl_words, n_words * 8));
     CK(cudaMemset(c->fl_words, 0, n_words * 8));  // tag 0: never a launch's tag
     auto xw = [&](int l) { return c->fl_words + per_layer * l; };
     auto qkvw = [&](int l) { return xw(l) + dim; };
-    auto attw = [&](int l) { return qkvw(l) + dim + 2 * kvd; };
-    auto x1w = [&](int l) { return attw(l) + dim; };
+    auto attw = [&](int l) { return qkvw(l) + qd + 2 * kvd; };
+    auto x1w = [&](int l) { return attw(l) + qd; };
     auto hw = [&](int l) { return x1w(l) + dim; };
     auto xnext = [&](int l) { return l + 1 < L ? xw(l + 1) : c->fl_words + per_layer * L; };
+    // tensor parallel: the exchange buffer, [layer][Wo, W_down][world][dim] words in every
+    // rank, mapped into the others; a residual phase stores its partial sums to every rank,
+    // the next norm phase adds them (rank order) to the residual it keeps
+    auto tp_block = [&](int l, int k) { return (long long)((size_t)(2 * l + k) * W * dim); };
+    if (W > 1) {
+        const int rc = fl_tp_setup(c, (size_t)2 * L * W * dim);
+        if (rc != FIBER_OK) return rc;
+    }
 
     std::vector<FPhase> &ph = c->fphases;
     ph.clear();
@@ -721,6 +767,7 @@ static int flow_build(gpu_context *c) {
         f.layer = layer;
         f.nmat = 1;
         f.eps = p.rms_norm_eps;
+        f.tp_off = -1;
         return f;
     };
     auto tiles_of = [](FPhase &f) {
@@ -731,29 +778,32 @@ static int flow_build(gpu_context *c) {
         const LayerDev &d = c->L[l];
         FPhase q = base(FL_QKV, dim, l);
         q.nseg = 3;
-        q.seg[0] = make_pseg(d.wq, nullptr, d.tq, dim, 0, dim);
-        q.seg[1] = make_pseg(d.wk, nullptr, d.tk, kvd, dim, dim);
-        q.seg[2] = make_pseg(d.wv, nullptr, d.tv, kvd, dim + kvd, dim);
+        q.seg[0] = make_pseg(d.wq, nullptr, d.tq, qd, 0, dim);
+        q.seg[1] = make_pseg(d.wk, nullptr, d.tk, kvd, qd, dim);
+        q.seg[2] = make_pseg(d.wv, nullptr, d.tv, kvd, qd + kvd, dim);
         q.embed_in = l == 0;
-        q.in = l == 0 ? nullptr : xw(l);
+        q.in = l == 0 ? nullptr : (W > 1 ? c->fl_tp_local + tp_block(l - 1, 1) : xw(l));
+        q.tp_sum = l > 0 && W > 1;
         q.norm_w = d.attn_norm;
         q.out = qkvw(l);
         tiles_of(q);
-        FPhase a = base(FL_ATTN, dim, l);
+        FPhase a = base(FL_ATTN, qd, l);
         a.in = qkvw(l);
         a.out = attw(l);
-        FPhase o = base(FL_RESID, dim, l);
+        FPhase o = base(FL_RESID, qd, l);
         o.nseg = 1;
-        o.seg[0] = make_pseg(d.wo, nullptr, d.to, dim, 0, dim);
+        o.seg[0] = make_pseg(d.wo, nullptr, d.to, dim, 0, qd);
         o.in = attw(l);
         o.out = x1w(l);
+        if (W > 1) o.tp_off = tp_block(l, 0);
         tiles_of(o);
         FPhase u = base(FL_SWIGLU, dim, l);
         u.nseg = 1;
         u.nmat = 2;
         u.seg[0] = make_pseg(d.w1, d.w3, d.t1, ffn, 0, dim);
         u.seg[0].tiles = (ffn + TC_M / 2 - 1) / (TC_M / 2);  // 8 rows of gate + the same 8 of up
-        u.in = x1w(l);
+        u.in = W > 1 ? c->fl_tp_local + tp_block(l, 0) : x1w(l);
+        u.tp_sum = W > 1;
         u.norm_w = d.ffn_norm;
         u.out = hw(l);
         tiles_of(u);
@@ -762,11 +812,13 @@ static int flow_build(gpu_context *c) {
         dn.seg[0] = make_pseg(d.w2, nullptr, d.t2, dim, 0, ffn);
         dn.in = hw(l);
         dn.out = xnext(l);
+        if (W > 1) dn.tp_off = tp_block(l, 1);
         tiles_of(dn);
-        // a norm phase keeps its fp32 input as the residual of the next residual phase
-        q.stage_ctas = std::min(grid, std::max(q.n_tiles, o.n_tiles));
+        // a norm phase keeps its fp32 input as the residual of the next residual phase (and,
+        // tensor parallel, of the next norm phase: then every CTA stages every norm phase)
+        q.stage_ctas = W > 1 ? grid : std::min(grid, std::max(q.n_tiles, o.n_tiles));
         o.stage_ctas = std::min(grid, o.n_tiles);
-        u.stage_ctas = std::min(grid, std::max(u.n_tiles, dn.n_tiles));
+        u.stage_ctas = W > 1 ? grid : std::min(grid, std::max(u.n_tiles, dn.n_tiles));
         dn.stage_ctas = std::min(grid, dn.n_tiles);
         ph.push_back(q);
         ph.push_back(a);
@@ -777,11 +829,12 @@ static int flow_build(gpu_context *c) {
     FPhase lm = base(FL_LM, dim, 0);
     lm.nseg = 1;
     lm.seg[0] = make_pseg(c->out, nullptr, c->t_out, p.vocab_size, 0, dim);
-    lm.in = xnext(L - 1);
+    lm.in = W > 1 ? c->fl_tp_local + tp_block(L - 1, 1) : xnext(L - 1);
+    lm.tp_sum = W > 1;
     lm.norm_w = c->out_norm;
     lm.logits = c->logits;
     tiles_of(lm);
-    lm.stage_ctas = std::min(grid, lm.n_tiles);
+    lm.stage_ctas = W > 1 ? grid : std::min(grid, lm.n_tiles);
     ph.push_back(lm);
 
     // shared memory: fragments (one layout per weight type of a phase), the residual
@@ -801,7 +854,7 @@ static int flow_build(gpu_context *c) {
     // attention splits per KV head: about eight pages each at max_seq, at most 8 and at most
     // a grid's worth of units (split 0 merges the others; fewer splits, less scratch)
     const int max_pages = (c->max_seq + ATTN_P - 1) / ATTN_P;
-    const int max_split = std::max(1, std::min(std::min(8, grid / (int)p.n_kv_heads),
+    const int max_split = std::max(1, std::min(std::min(8, grid / c->nkv_l),
                                                (max_pages + FL_PAGES_PER_UNIT - 1) / FL_PAGES_PER_UNIT));
     scratch += (max_split - 1) * c->G * (hd + 2);
     const int xres = (dim + 31) & ~31;
@@ -956,7 +1009,11 @@ static int ctx_init(gpu_context *c, const model_t *m, int device, int max_seq, i
     int rc = tp_setup(c, m, rank, world, nccl_id);
     if (rc) return rc;
     if (world > 1) {
-        c->mode = 1;  // sharded steps run the per-phase kernels with NCCL all-reduces
+        // sharded steps: the dataflow kernel with the exchange fused into it where the model
+        // fits it, else the per-phase kernels with an all-reduce after Wo and W_down
+        c->mode = 1;
+        if ((rc = flow_build(c)) != FIBER_OK) return rc;
+        if (c->fl_ok) c->mode = 2;
         return FIBER_OK;
     }
     if ((rc = pk_build(c)) != FIBER_OK) return rc;
@@ -1407,6 +1464,10 @@ static cudaError_t enqueue_flow(gpu_context *c, const kv_cache_t *kv, bool loop,
     P.max_seq = c->max_seq < kv->max_seq ? c->max_seq : kv->max_seq;
     P.att_scale = 1.0f / sqrtf((float)p.head_dim);
     P.att_max_split = c->fl_max_split;
+    P.tp_world = c->tp_world > 1 ? c->tp_world : 1;
+    P.tp_rank = c->tp_world > 1 ? c->tp_rank : 0;
+    for (int q = 0; q < FL_MAX_TP; q++)
+        P.tp_bufs[q] = q < P.tp_world ? (q == P.tp_rank ? c->fl_tp_local : (uint64_t *)c->fl_tp_peer[q]) : nullptr;
     P.att_words = c->fl_att_words;
     P.hd = (int)p.head_dim;
     P.G = c->G;
@@ -2581,7 +2642,9 @@ extern "C" int fiber_decode_sample(fiber_ctx_t *c, kv_cache_t *kv, int32_t first
 
 extern "C" int fiber_tp_collective(fiber_ctx_t *c) {
     if (!c) return set_err(FIBER_EARG, "no context");
-    return c->tp_world <= 1 ? 0 : (c->ar_ok ? 2 : 1);
+    if (c->tp_world <= 1) return 0;
+    if (c->mode == 2 && c->fl_ok) return 3;  // fused: peer stores in the dataflow step's residual phases
+    return c->ar_ok ? 2 : 1;
 }
 
 extern "C" int fiber_set_max_batch(fiber_ctx_t *c, int max_batch) {

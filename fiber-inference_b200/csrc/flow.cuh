@@ -47,6 +47,7 @@ constexpr int FL_EPI_WARP = FL_WARPS + 1;
 constexpr int FL_REG_PRODUCER = 56, FL_REG_CONSUMER = 224;
 static_assert(4 * 32 * FL_REG_PRODUCER + 8 * 32 * FL_REG_CONSUMER <= FL_THREADS * 168, "register split");
 constexpr int FL_NDESC = 16;                   // ring slots
+constexpr int FL_MAX_TP = 8;                   // tensor-parallel ranks at most
 constexpr unsigned long long FL_WAIT_NS = 2000000000ull;
 constexpr int FL_RING_PAD = 1024;              // the ring starts at the first 1024-byte boundary (swizzled copies)
 // Optional per-phase, per-CTA timeline (FParams::trace non-null), fields:
@@ -78,11 +79,14 @@ struct __align__(16) FPhase {
     int embed_in;    // layer 0 QKV: the input is the embedding row of the current token
     int stage_ctas;  // CTAs below this stage the input (they have tiles here, or keep it for the next residual phase)
     float eps;
-    int pad_;
+    int tp_sum;      // tensor parallel, norm phase: the input is x (the residual kept by the last norm
+                     // phase) plus every rank's partial sums, `in` = [world][cols] words in rank order
     const uint64_t *in;    // tagged input words (cols of them); null for the embedding input
     const float *norm_w;   // RMSNorm weights of the input, or null
     uint64_t *out;         // tagged output words (QKV: q|k|v, ATTN: attention, RESID: x, SWIGLU: h)
     float *logits;         // LM: fp32 logits
+    long long tp_off;      // tensor parallel, residual phase: word offset of its [world][rows] partial
+                           // sums in every rank's exchange buffer (the epilogue stores to each rank), or -1
     PSeg seg[3];
 };
 static_assert(sizeof(FPhase) % 16 == 0 && sizeof(FPhase) / 16 <= 32, "phase descriptors are copied in 16-byte chunks");
@@ -116,6 +120,10 @@ struct FParams {
     unsigned int *exit_count;
     int ring_bytes, frag_bytes, xres_floats, xin_floats, nw_floats;
     unsigned long long *trace;   // [n_phases][gridDim.x][FL_TRACE_FIELDS] or null
+    // tensor parallelism (tp_world > 1): each rank's exchange buffer, mapped into this
+    // rank (peer memory over NVLink; this rank's own is local)
+    int tp_world, tp_rank;
+    uint64_t *tp_bufs[FL_MAX_TP];
 };
 
 // ---- per-CTA state ----------------------------------------------------------------------
@@ -155,6 +163,17 @@ FDEV void ll_store(uint64_t *p, float v, uint32_t tag) {
 FDEV ulonglong2 ll_load2(const uint64_t *p) {
     ulonglong2 r;
     asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(r.x), "=l"(r.y) : "l"(p) : "memory");
+    return r;
+}
+
+// Tagged words exchanged between GPUs: system-scope stores into a peer's buffer and
+// system-scope loads of this GPU's buffer (no multicast, no bulk copies on peer memory).
+FDEV void ll_store_sys(uint64_t *p, float v, uint32_t tag) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(ll_word(v, tag)) : "memory");
+}
+FDEV ulonglong2 ll_load2_sys(const uint64_t *p) {
+    ulonglong2 r;
+    asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(r.x), "=l"(r.y) : "l"(p) : "memory");
     return r;
 }
 
@@ -367,6 +386,68 @@ __device__ __noinline__ void fl_embed_chunk(const FParams &P, int tok, int b, fl
     }
 }
 
+// Tensor parallel: chunk b of x = (residual kept in xs) + the ranks' partial sums, added
+// in rank order, so every rank computes the same x bit for bit. `in` holds [world][cols]
+// tagged words; two ranks' words are polled at a time (eight 16-byte loads per lane).
+// Lanes of one warp; returns false (warp-uniform) when stopped.
+FDEV bool fl_stage_tp_chunk(const FParams &P, const FPhase &F, int b, uint32_t tag, float *xs) {
+    const int lane = threadIdx.x & 31, n = F.cols;
+    float x[8];
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        const float2 v = *reinterpret_cast<const float2 *>(xs + b * 256 + 2 * (lane + 32 * k));
+        x[2 * k] = v.x;
+        x[2 * k + 1] = v.y;
+    }
+    for (int r0 = 0; r0 < P.tp_world; r0 += 2) {
+        const int nr = min(2, P.tp_world - r0);
+        ulonglong2 w[8];
+        uint32_t pend = 0;
+#pragma unroll
+        for (int k = 0; k < 8; k++)
+            if ((k >> 2) < nr) {
+                w[k] = ll_load2_sys(F.in + (size_t)(r0 + (k >> 2)) * n + b * 256 + 2 * (lane + 32 * (k & 3)));
+                pend |= 1u << k;
+            }
+        unsigned long long t0 = 0;
+        for (long long it = 0;; it++) {
+#pragma unroll
+            for (int k = 0; k < 8; k++)
+                if (((pend >> k) & 1u) && (uint32_t)(w[k].x >> 32) == tag && (uint32_t)(w[k].y >> 32) == tag)
+                    pend &= ~(1u << k);
+            if (__all_sync(0xffffffffu, pend == 0)) break;
+            if (it == 0) {
+                t0 = gtimer();
+            } else if ((it & 15) == 0) {
+                int stop = fl_abort || gtimer() - t0 > FL_WAIT_NS;
+                if (__any_sync(0xffffffffu, stop)) {
+                    if (lane == 0) fl_fail(P);
+                    return false;
+                }
+            }
+#pragma unroll
+            for (int k = 0; k < 8; k++)
+                if ((pend >> k) & 1u)
+                    w[k] = ll_load2_sys(F.in + (size_t)(r0 + (k >> 2)) * n + b * 256 + 2 * (lane + 32 * (k & 3)));
+        }
+#pragma unroll
+        for (int q = 0; q < 2; q++) {  // rank r0, then r0 + 1
+            if (q < nr) {
+#pragma unroll
+                for (int k = 0; k < 4; k++) {
+                    const ulonglong2 v = w[4 * q + k];
+                    x[2 * k] = __fadd_rn(x[2 * k], __uint_as_float((uint32_t)v.x));
+                    x[2 * k + 1] = __fadd_rn(x[2 * k + 1], __uint_as_float((uint32_t)v.y));
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < 4; k++)
+        *reinterpret_cast<float2 *>(xs + b * 256 + 2 * (lane + 32 * k)) = make_float2(x[2 * k], x[2 * k + 1]);
+    return true;
+}
+
 // Stage this warp's chunks of the phase input: chunk b (256 elements) is staged by warp
 // b % 8, the warp that multiplies super-block column b of every tile, so no other warp
 // waits for it. Per chunk: poll its tagged words (or decode the embedding row), keep
@@ -405,6 +486,12 @@ __device__ __noinline__ bool fl_stage_warp(const FParams &P, const FPhase &F, in
             }
         if (F.embed_in) {  // every CTA decodes the embedding row itself (src/gpu_ffn.m:466-482)
             for (int c = 0; c < nc; c++) fl_embed_chunk(P, tok, b0 + c * FL_WARPS, xs);
+        } else if (F.tp_sum) {
+            for (int c = 0; c < nc; c++)
+                if (!fl_stage_tp_chunk(P, F, b0 + c * FL_WARPS, tag, xs)) {
+                    cp_async_wait_all();
+                    return false;
+                }
         } else {
             // pair k of the group: chunk b0 + 8 (k / 4), words 2 (lane + 32 (k % 4)) + {0, 1}
             ulonglong2 w[8];
@@ -553,7 +640,14 @@ FDEV void fl_epilogue(const FParams &P, const FPhase &F, const PSeg &S, int lt, 
                 ll_store(F.out + (size_t)gi * (P.G + 2) * P.hd + slot, v0, tag);
                 break;
             }
-            case FL_RESID: ll_store(F.out + r, __fadd_rn(fl_xres(P)[r], v0), tag); break;
+            case FL_RESID:
+                if (F.tp_off >= 0) {  // this rank's partial sum, to every rank (the next phase adds them)
+                    for (int q = 0; q < P.tp_world; q++)
+                        ll_store_sys(P.tp_bufs[q] + F.tp_off + (long long)P.tp_rank * S.rows + r, v0, tag);
+                } else {
+                    ll_store(F.out + r, __fadd_rn(fl_xres(P)[r], v0), tag);
+                }
+                break;
             case FL_SWIGLU: {
                 const float h = __fmul_rn(__fdiv_rn(v0, __fadd_rn(1.0f, expf(-v0))), v1);
                 ll_store(F.out + r, h, tag);

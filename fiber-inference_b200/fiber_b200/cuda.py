@@ -335,7 +335,8 @@ class Context:
 
     @property
     def tp_collective(self) -> int:
-        """fiber_tp_collective: 0 none, 1 NCCL, 2 one-shot peer all-reduce."""
+        """fiber_tp_collective: 0 none, 1 NCCL, 2 one-shot peer all-reduce, 3 fused into the
+        dataflow step (peer stores in the residual phases)."""
         return int(cuda_lib().fiber_tp_collective(self.h))
 
     @property

@@ -171,7 +171,8 @@ int fiber_tp_unique_id(uint8_t out[FIBER_TP_ID_BYTES]);
  * (NCCL, sum) the dim-vector after Wo and after W_down inside the step graph, so
  * every rank holds the same residual stream and the same greedy token. Must be
  * called by all ranks together. The KV cache holds this rank's KV heads
- * (fiber_tp_info). Steps run the per-phase kernels (decode mode 1). */
+ * (fiber_tp_info). Steps run the dataflow kernel with the exchange fused into it
+ * (decode mode 2) where the model fits it, else the per-phase kernels (mode 1). */
 fiber_ctx_t *fiber_cuda_init_tp(const model_t *m, int device, int rank, int world,
                                 const uint8_t nccl_id[FIBER_TP_ID_BYTES], int max_seq);
 int fiber_tp_info(fiber_ctx_t *ctx, fiber_tp_plan_t *out);
@@ -182,7 +183,12 @@ int fiber_tp_info(fiber_ctx_t *ctx, fiber_tp_plan_t *out);
  * call's epoch; readers poll the words with a bounded wait, and every rank sums the
  * partials in rank order: identical results on all ranks).
  * 2 is the default for up to 8 ranks; FIBER_TP_ALLREDUCE=nccl in the environment at
- * fiber_cuda_init_tp selects NCCL. */
+ * fiber_cuda_init_tp selects NCCL. 3: the exchange is fused into the dataflow step
+ * (decode mode 2, the default where the model fits it): the Wo and W_down epilogues
+ * store each rank's partial sums into every rank's exchange buffer over NVLink (tagged
+ * words, CUDA IPC mappings), and the next phase's staging adds the ranks' partials to the
+ * residual in rank order, so no separate collective runs in the step; modes 1 and 0 use
+ * the collective above. */
 int fiber_tp_collective(fiber_ctx_t *ctx);
 
 /* Raise the sequences one batched step can carry (as fiber_cuda_init's max_batch; the

@@ -1,7 +1,9 @@
-"""Tensor-parallel decode on two GPUs (one process per GPU, an all-reduce after Wo and
-W_down: the one-shot peer-memory all-reduce, or NCCL): both ranks produce the oracle's
-greedy tokens, teacher-forced logits stay within the decode tolerances, and with the
-peer all-reduce both ranks' logits are bit-identical. The batched layer pass (prefill,
+"""Tensor-parallel decode on two GPUs (one process per GPU; the exchange after Wo and
+W_down fused into the dataflow step — each rank's epilogue stores its partial sums into
+every rank over peer memory and the next phase adds them in rank order — or, with the
+per-phase kernels, the one-shot peer-memory all-reduce or NCCL): both ranks produce the
+oracle's greedy tokens, teacher-forced logits stay within the decode tolerances, and
+where every rank adds the partials in the same order both ranks' logits are bit-identical. The batched layer pass (prefill,
 several sequences per step) is sharded the same way and reproduces the oracle per
 sequence. Skipped with fewer than two GPUs."""
 from __future__ import annotations
@@ -27,6 +29,8 @@ def _worker(rank, world, nid, path, prompt, n_gen, q, coll):
             os.environ["FIBER_TP_ALLREDUCE"] = "nccl"
         hm = fb.HostModel(path)
         ctx = fb.Context(hm, device=rank, max_seq=256, tp=(rank, world, nid), max_batch=3)
+        if coll != "fused":
+            ctx.set_mode(1)  # per-phase kernels with a separate all-reduce
         kv = ctx.kv(256)
         logits = []
         for pos, t in enumerate(prompt[:6]):  # teacher-forced, every rank in lockstep
@@ -49,7 +53,7 @@ def _worker(rank, world, nid, path, prompt, n_gen, q, coll):
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("coll", ["peer", "nccl"])
+@pytest.mark.parametrize("coll", ["fused", "peer", "nccl"])
 def test_tp2_matches_oracle(tiny_model, coll):
     path = tiny_model("tp")
     hm = fb.HostModel(path)
@@ -75,9 +79,9 @@ def test_tp2_matches_oracle(tiny_model, coll):
                 pr.kill()
     for r in (0, 1):
         assert res[r][5] is None, res[r][5]
-    want_coll = 2 if coll == "peer" else 1
+    want_coll = {"fused": 3, "peer": 2, "nccl": 1}[coll]
     assert res[0][4] == (4, 2, 2, want_coll) and res[1][4] == (4, 2, 2, want_coll)
-    if coll == "peer":  # every rank sums the slots in the same order
+    if coll != "nccl":  # every rank adds the partial sums in the same order
         assert np.array_equal(res[0][3], res[1][3])
 
     om = orc.Model(path)
