@@ -388,6 +388,8 @@ struct gpu_context {
     bool fl_ok = false;               // the model fits the dataflow kernel
     uint64_t *fl_tp_local = nullptr;  // tensor parallel: this rank's exchange buffer of partial sums
     void *fl_tp_peer[FL_MAX_TP] = {}; // the other ranks' exchange buffers, mapped here (CUDA IPC)
+    long long fl_tp_key_off = 0;      // word offset of the [world][2] argmax keys in the exchange buffers
+    bool fl_lm_shard = false;         // this call wants no logits: ranks split the lm_head (greedy)
     FPhase *d_fphases = nullptr;
     std::vector<FPhase> fphases;
     uint64_t *fl_words = nullptr;     // tagged words of every phase output of one step
@@ -753,7 +755,9 @@ static int flow_build(gpu_context *c) {
     // the next norm phase adds them (rank order) to the residual it keeps
     auto tp_block = [&](int l, int k) { return (long long)((size_t)(2 * l + k) * W * dim); };
     if (W > 1) {
-        const int rc = fl_tp_setup(c, (size_t)2 * L * W * dim);
+        // + [world][2] words: each rank's best (logit, row) key of a sharded lm_head
+        c->fl_tp_key_off = (long long)2 * L * W * dim;
+        const int rc = fl_tp_setup(c, (size_t)2 * L * W * dim + 2 * W);
         if (rc != FIBER_OK) return rc;
     }
 
@@ -1468,6 +1472,8 @@ static cudaError_t enqueue_flow(gpu_context *c, const kv_cache_t *kv, bool loop,
     P.tp_rank = c->tp_world > 1 ? c->tp_rank : 0;
     for (int q = 0; q < FL_MAX_TP; q++)
         P.tp_bufs[q] = q < P.tp_world ? (q == P.tp_rank ? c->fl_tp_local : (uint64_t *)c->fl_tp_peer[q]) : nullptr;
+    P.lm_shard = P.tp_world > 1 && c->fl_lm_shard ? 1 : 0;
+    P.tp_key_off = c->fl_tp_key_off;
     P.att_words = c->fl_att_words;
     P.hd = (int)p.head_dim;
     P.G = c->G;
@@ -1613,7 +1619,10 @@ extern "C" int fiber_forward_token(fiber_ctx_t *c, kv_cache_t *kv, const int32_t
     c->h_io->pos = pos[0];
     c->h_io->err = 0;
     CK(cudaMemcpyAsync(c->io, c->h_io, sizeof(StepIO), cudaMemcpyHostToDevice, c->stream));
-    if ((rc = run_step(c, kv, false)) != FIBER_OK) return rc;
+    c->fl_lm_shard = !logits_or_null;  // token only: tensor-parallel ranks split the lm_head
+    rc = run_step(c, kv, false);
+    c->fl_lm_shard = false;
+    if (rc != FIBER_OK) return rc;
     if (logits_or_null)
         CK(cudaMemcpyAsync(c->h_logits, c->logits, (size_t)c->p.vocab_size * 4, cudaMemcpyDeviceToHost, c->stream));
     CK(cudaMemcpyAsync(c->h_io, c->io, sizeof(StepIO), cudaMemcpyDeviceToHost, c->stream));
@@ -2302,8 +2311,10 @@ extern "C" int fiber_decode_greedy(fiber_ctx_t *c, kv_cache_t *kv, int32_t first
             if ((rc = get_graph(c, kv, true, &g)) != FIBER_OK) return rc;
         }
         CK(cudaEventRecord(c->ev0, c->stream));
-        for (int i = 0; i < n_steps; i++)
-            if ((rc = run_step(c, kv, true)) != FIBER_OK) return rc;
+        c->fl_lm_shard = true;  // tokens only: tensor-parallel ranks split the lm_head
+        for (int i = 0; i < n_steps && rc == FIBER_OK; i++) rc = run_step(c, kv, true);
+        c->fl_lm_shard = false;
+        if (rc != FIBER_OK) return rc;
         CK(cudaEventRecord(c->ev1, c->stream));
         CK(cudaEventSynchronize(c->ev1));
         if (ms_out) CK(cudaEventElapsedTime(ms_out, c->ev0, c->ev1));

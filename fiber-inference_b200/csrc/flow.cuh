@@ -124,6 +124,9 @@ struct FParams {
     // rank (peer memory over NVLink; this rank's own is local)
     int tp_world, tp_rank;
     uint64_t *tp_bufs[FL_MAX_TP];
+    int lm_shard;                // tensor parallel, no logits wanted: each rank runs its share of the
+                                 // lm_head tiles and the ranks exchange their best keys
+    long long tp_key_off;        // word offset of the [world][2] key area in the exchange buffers
 };
 
 // ---- per-CTA state ----------------------------------------------------------------------
@@ -170,6 +173,9 @@ FDEV ulonglong2 ll_load2(const uint64_t *p) {
 // system-scope loads of this GPU's buffer (no multicast, no bulk copies on peer memory).
 FDEV void ll_store_sys(uint64_t *p, float v, uint32_t tag) {
     asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(ll_word(v, tag)) : "memory");
+}
+FDEV void ll_store_bits_sys(uint64_t *p, uint32_t bits, uint32_t tag) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(((uint64_t)tag << 32) | bits) : "memory");
 }
 FDEV ulonglong2 ll_load2_sys(const uint64_t *p) {
     ulonglong2 r;
@@ -705,13 +711,27 @@ FDEV void fl_tile(const FParams &P, const FPhase &F, const PSeg &S, int lt, cons
     }
 }
 
+// Tiles [t0, t1) of phase F on this GPU: all of them, except the lm_head of a sharded
+// greedy step, where each rank takes an equal share (the ranks exchange their best keys).
+FDEV void fl_tile_range(const FParams &P, const FPhase &F, int &t0, int &t1) {
+    t0 = 0;
+    t1 = F.n_tiles;
+    if (F.kind == FL_LM && P.lm_shard) {
+        const int per = (F.n_tiles + P.tp_world - 1) / P.tp_world;
+        t0 = min(F.n_tiles, P.tp_rank * per);
+        t1 = min(F.n_tiles, t0 + per);
+    }
+}
+
 // The CTA's tiles of one GEMV phase (tile = blockIdx.x + k * gridDim.x), warp-level.
 FDEV bool fl_tiles(const FParams &P, const FPhase &F, long long &seq, uint32_t tag, long long &wcycles,
                    unsigned long long *tr) {
     const int nb = F.cols >> 8;
     const uint2 *xf0 = fl_frag(P), *xf1 = xf0 + (size_t)nb * 128;
     long long tacc[4] = {0, 0, 0, 0};
-    for (int tile = blockIdx.x; tile < F.n_tiles; tile += gridDim.x) {
+    int t0, t1;
+    fl_tile_range(P, F, t0, t1);
+    for (int tile = t0 + blockIdx.x; tile < t1; tile += gridDim.x) {
         int sidx, lt;
         fl_locate(F, tile, sidx, lt);
         const PSeg &S = F.seg[sidx];
@@ -1071,7 +1091,7 @@ struct FlowAttn {
 // After the lm_head phase, by the epilogue warp once it ran this CTA's last lm_head
 // epilogue: publish the CTA's best key; the last CTA reduces all of them, writes the token
 // and (loop mode) advances the step state.
-FDEV void fl_argmax_finish(const FParams &P) {
+FDEV void fl_argmax_finish(const FParams &P, uint32_t tag) {
     const int lane = threadIdx.x & 31;
     unsigned int ticket = 0;
     if (lane == 0) {
@@ -1086,6 +1106,42 @@ FDEV void fl_argmax_finish(const FParams &P) {
     for (int i = lane; i < (int)gridDim.x; i += 32) best = max(best, __ldcg(P.am_key + i));
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) best = max(best, __shfl_xor_sync(0xffffffffu, best, o));
+    if (P.lm_shard) {
+        // this rank's best key to every rank (two tagged words), then the largest of all
+        // ranks' keys: every rank picks the same token
+        if (lane < P.tp_world) {
+            uint64_t *dst = P.tp_bufs[lane] + P.tp_key_off + 2 * P.tp_rank;
+            ll_store_bits_sys(dst, (uint32_t)(best >> 32), tag);
+            ll_store_bits_sys(dst + 1, (uint32_t)best, tag);
+        }
+        unsigned long long k = 0ull;
+        int ok = 1;
+        if (lane < P.tp_world) {
+            const uint64_t *src = P.tp_bufs[P.tp_rank] + P.tp_key_off + 2 * lane;
+            const unsigned long long t0 = gtimer();
+            for (;;) {
+                const ulonglong2 w = ll_load2_sys(src);
+                if ((uint32_t)(w.x >> 32) == tag && (uint32_t)(w.y >> 32) == tag) {
+                    k = ((unsigned long long)(uint32_t)w.x << 32) | (uint32_t)w.y;
+                    break;
+                }
+                if (fl_abort || gtimer() - t0 > FL_WAIT_NS) {
+                    ok = 0;
+                    break;
+                }
+            }
+        }
+        if (!__all_sync(0xffffffffu, ok)) {
+            if (lane == 0) {
+                fl_fail(P);
+                *P.am_count = 0u;
+            }
+            return;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) k = max(k, __shfl_xor_sync(0xffffffffu, k, o));
+        best = k;
+    }
     if (lane == 0) {
         const int bi = (int)(0xFFFFFFFFu - (uint32_t)(best & 0xFFFFFFFFu));
         *P.io_argmax = bi;
@@ -1129,7 +1185,9 @@ __device__ __noinline__ void fl_epilogue_warp(const FParams &P, int nch, int S, 
         long long cw = 0, ce = 0;  // trace: cycles waiting for partial sums, in epilogues
         const unsigned long long t_ph = P.trace ? gtimer() : 0ull;
         if ((int)blockIdx.x < F.stage_ctas) {
-            for (int tile = blockIdx.x; tile < F.n_tiles; tile += gridDim.x) {
+            int t0, t1;
+            fl_tile_range(P, F, t0, t1);
+            for (int tile = t0 + blockIdx.x; tile < t1; tile += gridDim.x) {
                 int sidx, lt;
                 fl_locate(F, tile, sidx, lt);
                 const int d = (int)(seq % FL_NDESC);
@@ -1160,7 +1218,7 @@ __device__ __noinline__ void fl_epilogue_warp(const FParams &P, int nch, int S, 
         }
         if (kind == FL_LM) {
             __syncwarp();
-            fl_argmax_finish(P);
+            fl_argmax_finish(P, tag);
         }
         if (P.trace && lane == 0) {
             unsigned long long *tr = P.trace + ((size_t)ph * gridDim.x + blockIdx.x) * FL_TRACE_FIELDS;
@@ -1235,7 +1293,9 @@ __device__ __noinline__ void fl_producer(const FParams &P, int pos, int nch, int
                 }
             }
         } else {
-            for (int tile = blockIdx.x; tile < F.n_tiles && !fl_abort; tile += gridDim.x) {
+            int t0, t1;
+            fl_tile_range(P, F, t0, t1);
+            for (int tile = t0 + blockIdx.x; tile < t1 && !fl_abort; tile += gridDim.x) {
                 int s, lt;
                 fl_locate(F, tile, s, lt);
                 const PSeg &Sg = F.seg[s];

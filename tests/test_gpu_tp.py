@@ -3,7 +3,8 @@ W_down fused into the dataflow step — each rank's epilogue stores its partial 
 every rank over peer memory and the next phase adds them in rank order — or, with the
 per-phase kernels, the one-shot peer-memory all-reduce or NCCL): both ranks produce the
 oracle's greedy tokens, teacher-forced logits stay within the decode tolerances, and
-where every rank adds the partials in the same order both ranks' logits are bit-identical. The batched layer pass (prefill,
+where every rank adds the partials in the same order both ranks' logits are bit-identical;
+steps that want only the token split the lm_head across the ranks. The batched layer pass (prefill,
 several sequences per step) is sharded the same way and reproduces the oracle per
 sequence. Skipped with fewer than two GPUs."""
 from __future__ import annotations
@@ -36,6 +37,10 @@ def _worker(rank, world, nid, path, prompt, n_gen, q, coll):
         for pos, t in enumerate(prompt[:6]):  # teacher-forced, every rank in lockstep
             _, lg = ctx.forward(kv, int(t), pos)
             logits.append(lg)
+        # token only (no logits wanted): in the dataflow step each rank runs its share of
+        # the lm_head and the ranks exchange their best keys
+        kv_am = ctx.kv(256)
+        am_only = [ctx.forward(kv_am, int(t), pos, want_logits=False)[0] for pos, t in enumerate(prompt[:6])]
         kv2 = ctx.kv(256)
         first = ctx.prefill(kv2, np.asarray(prompt, np.int32))
         toks, _ = ctx.decode_greedy(kv2, first, len(prompt), n_gen)
@@ -46,10 +51,11 @@ def _worker(rank, world, nid, path, prompt, n_gen, q, coll):
         btoks, _ = ctx.decode_greedy_batch(kv3, firsts, [len(pr) for pr in prompts], 20)
         plan = ctx.plan
         q.put((rank, first, toks.tolist(), np.stack(logits),
-               (plan.heads, plan.kv_heads, plan.ffn_blocks, ctx.tp_collective), None, firsts, btoks.tolist()))
+               (plan.heads, plan.kv_heads, plan.ffn_blocks, ctx.tp_collective), None, firsts, btoks.tolist(),
+               am_only))
         ctx.close()
     except Exception as e:  # report instead of hanging the parent
-        q.put((rank, None, None, None, None, repr(e), None, None))
+        q.put((rank, None, None, None, None, repr(e), None, None, None))
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
@@ -92,6 +98,7 @@ def test_tp2_matches_oracle(tiny_model, coll):
         assert np.abs(lg - want_lg).max() < MAX_ABS
         err = np.sqrt(np.mean((lg.astype(np.float64) - want_lg) ** 2) / np.mean(want_lg.astype(np.float64) ** 2))
         assert err < REL_RMS
+        assert res[r][8] == [int(np.argmax(x)) for x in want_lg]
     st2 = om.state(256, kv_fp16=True)
     want = st2.generate(prompt, n_gen)
     for r in (0, 1):
