@@ -55,6 +55,10 @@ TINY_MODELS = {
     # Q6_K on attn_v / ffn_down of layer 0, so both shard paths (144- and 210-byte blocks) run
     "tp": dict(dim=512, n_layers=3, n_heads=8, n_kv_heads=4, ffn_dim=1024, vocab=1100, recipe="Q4_K_M", seed=17,
                context_length=512),
+    # splits over 4 ranks: 4 query / 1 KV head each, 11 FFN super-blocks as 2/3/3/3 (uneven,
+    # like the 7B FFN's 43 blocks over 4 ranks)
+    "tp4": dict(dim=1024, n_layers=2, n_heads=16, n_kv_heads=4, ffn_dim=2816, vocab=1100, recipe="Q4_K_M",
+                seed=18, context_length=512),
 }
 
 

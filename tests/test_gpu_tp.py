@@ -1,4 +1,4 @@
-"""Tensor-parallel decode on two GPUs (one process per GPU; the exchange after Wo and
+"""Tensor-parallel decode (one process per GPU; the exchange after Wo and
 W_down fused into the dataflow step — each rank's epilogue stores its partial sums into
 every rank over peer memory and the next phase adds them in rank order — or, with the
 per-phase kernels, the one-shot peer-memory all-reduce or NCCL): both ranks produce the
@@ -6,7 +6,8 @@ oracle's greedy tokens, teacher-forced logits stay within the decode tolerances,
 where every rank adds the partials in the same order both ranks' logits are bit-identical;
 steps that want only the token split the lm_head across the ranks. The batched layer pass (prefill,
 several sequences per step) is sharded the same way and reproduces the oracle per
-sequence. Skipped with fewer than two GPUs."""
+sequence. Two ranks, and four with a model whose FFN super-blocks split unevenly; each case is
+skipped with fewer GPUs than ranks."""
 from __future__ import annotations
 
 import numpy as np
@@ -58,10 +59,15 @@ def _worker(rank, world, nid, path, prompt, n_gen, q, coll):
         q.put((rank, None, None, None, None, repr(e), None, None, None))
 
 
-@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("coll", ["fused", "peer", "nccl"])
-def test_tp2_matches_oracle(tiny_model, coll):
-    path = tiny_model("tp")
+def _gpus() -> int:
+    return torch.cuda.device_count() if torch.cuda.is_available() else 0
+
+
+@pytest.mark.parametrize("world,coll", [(2, "fused"), (2, "peer"), (2, "nccl"), (4, "fused")])
+def test_tp_matches_oracle(tiny_model, world, coll):
+    if _gpus() < world:
+        pytest.skip(f"needs {world} GPUs")
+    path = tiny_model("tp" if world == 2 else "tp4")
     hm = fb.HostModel(path)
     p = hm.params
     rng = np.random.default_rng(5)
@@ -70,12 +76,12 @@ def test_tp2_matches_oracle(tiny_model, coll):
     nid = fb.tp_unique_id()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_worker, args=(r, 2, nid, path, prompt, n_gen, q, coll)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, nid, path, prompt, n_gen, q, coll)) for r in range(world)]
     for pr in procs:
         pr.start()
     res = {}
     try:
-        for _ in range(2):
+        for _ in range(world):
             r = q.get(timeout=300)
             res[r[0]] = r
     finally:
@@ -83,17 +89,22 @@ def test_tp2_matches_oracle(tiny_model, coll):
             pr.join(timeout=60)
             if pr.is_alive():
                 pr.kill()
-    for r in (0, 1):
+    ranks = range(world)
+    for r in ranks:
         assert res[r][5] is None, res[r][5]
     want_coll = {"fused": 3, "peer": 2, "nccl": 1}[coll]
-    assert res[0][4] == (4, 2, 2, want_coll) and res[1][4] == (4, 2, 2, want_coll)
+    nblk = p.ffn_dim // 256
+    for r in ranks:  # heads and KV heads split evenly, FFN super-blocks as evenly as they go
+        want_plan = (p.n_heads // world, p.n_kv_heads // world, (r + 1) * nblk // world - r * nblk // world)
+        assert res[r][4] == want_plan + (want_coll,), (r, res[r][4])
     if coll != "nccl":  # every rank adds the partial sums in the same order
-        assert np.array_equal(res[0][3], res[1][3])
+        for r in ranks:
+            assert np.array_equal(res[0][3], res[r][3])
 
     om = orc.Model(path)
     st = om.state(256, kv_fp16=True)
     want_lg = np.stack([st.forward(int(t), pos) for pos, t in enumerate(prompt[:6])])
-    for r in (0, 1):
+    for r in ranks:
         lg = res[r][3]
         assert np.abs(lg - want_lg).max() < MAX_ABS
         err = np.sqrt(np.mean((lg.astype(np.float64) - want_lg) ** 2) / np.mean(want_lg.astype(np.float64) ** 2))
@@ -101,13 +112,13 @@ def test_tp2_matches_oracle(tiny_model, coll):
         assert res[r][8] == [int(np.argmax(x)) for x in want_lg]
     st2 = om.state(256, kv_fp16=True)
     want = st2.generate(prompt, n_gen)
-    for r in (0, 1):
+    for r in ranks:
         assert res[r][1] == want[0]
         assert res[r][2] == want[1:].tolist()
     # batched (tensor-parallel layer pass): each sequence equals the oracle run alone
     for i in range(3):
         pr = prompt[: 4 + 3 * i]
         wb = om.state(256, kv_fp16=True).generate(pr, 20)
-        for r in (0, 1):
+        for r in ranks:
             assert res[r][6][i] == wb[0], (r, i)
             assert [row[i] for row in res[r][7]] == wb[1:].tolist(), (r, i)
