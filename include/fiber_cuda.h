@@ -188,7 +188,10 @@ int fiber_tp_info(fiber_ctx_t *ctx, fiber_tp_plan_t *out);
  * store each rank's partial sums into every rank's exchange buffer over NVLink (tagged
  * words, CUDA IPC mappings), and the next phase's staging adds the ranks' partials to the
  * residual in rank order, so no separate collective runs in the step; modes 1 and 0 use
- * the collective above. */
+ * the collective above. In mode 2, calls that want only the token (fiber_decode_greedy,
+ * fiber_forward_token without a logits buffer) also split the lm_head tiles across the
+ * ranks, which exchange their best (logit, row) keys: every rank must make the same call
+ * with the same logits choice (a rank left waiting reports error 4 after 2 s). */
 int fiber_tp_collective(fiber_ctx_t *ctx);
 
 /* Raise the sequences one batched step can carry (as fiber_cuda_init's max_batch; the
