@@ -673,8 +673,9 @@ static int pk_build(gpu_context *c) {
 }
 
 template <int HD, int G>
-static void *fl_kernel_ptr() {
-    return reinterpret_cast<void *>(decode_flow_kernel<HD, G>);
+static void *fl_kernel_ptr(bool tp) {
+    return tp ? reinterpret_cast<void *>(decode_flow_kernel<HD, G, true>)
+              : reinterpret_cast<void *>(decode_flow_kernel<HD, G, false>);
 }
 
 // Tensor parallel: this rank's exchange buffer for the dataflow step (n_words tagged words,
@@ -726,7 +727,7 @@ static int flow_build(gpu_context *c) {
     int scratch = 0;
 #define FL_CASE(H, GG)                                         \
     if (hd == H && c->G == GG) {                               \
-        c->fl_kernel = fl_kernel_ptr<H, GG>();                 \
+        c->fl_kernel = fl_kernel_ptr<H, GG>(W > 1);            \
         scratch = FlowAttn<H, GG>::SCRATCH_FLOATS;             \
     }
     FL_CASE(64, 1) FL_CASE(64, 2) FL_CASE(64, 4) FL_CASE(64, 8)

@@ -183,6 +183,12 @@ FDEV ulonglong2 ll_load2_sys(const uint64_t *p) {
     return r;
 }
 
+// Tensor parallel: one partial sum to word `off` of every rank's exchange buffer (out of
+// line: the single-GPU epilogue carries only the call).
+__device__ __noinline__ void fl_tp_store_partial(const FParams &P, long long off, float v, uint32_t tag) {
+    for (int q = 0; q < P.tp_world; q++) ll_store_sys(P.tp_bufs[q] + off, v, tag);
+}
+
 FDEV void fl_fail(const FParams &P) {
     fl_abort = 1;
     *P.io_err = 4;
@@ -463,6 +469,8 @@ FDEV bool fl_stage_tp_chunk(const FParams &P, const FPhase &F, int b, uint32_t t
 // the chunk's dot products) and write its fragments for each weight type of the phase.
 // Two chunks at a time (eight 16-byte loads in flight per lane). Warp-level; returns
 // false (warp-uniform) when stopped.
+// TP: the tensor-parallel instance (norm phases add the ranks' partial sums).
+template <bool TP>
 __device__ __noinline__ bool fl_stage_warp(const FParams &P, const FPhase &F, int ph, uint32_t tag, int token,
                                            unsigned long long *tr) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -492,7 +500,7 @@ __device__ __noinline__ bool fl_stage_warp(const FParams &P, const FPhase &F, in
             }
         if (F.embed_in) {  // every CTA decodes the embedding row itself (src/gpu_ffn.m:466-482)
             for (int c = 0; c < nc; c++) fl_embed_chunk(P, tok, b0 + c * FL_WARPS, xs);
-        } else if (F.tp_sum) {
+        } else if (TP && F.tp_sum) {
             for (int c = 0; c < nc; c++)
                 if (!fl_stage_tp_chunk(P, F, b0 + c * FL_WARPS, tag, xs)) {
                     cp_async_wait_all();
@@ -648,8 +656,7 @@ FDEV void fl_epilogue(const FParams &P, const FPhase &F, const PSeg &S, int lt, 
             }
             case FL_RESID:
                 if (F.tp_off >= 0) {  // this rank's partial sum, to every rank (the next phase adds them)
-                    for (int q = 0; q < P.tp_world; q++)
-                        ll_store_sys(P.tp_bufs[q] + F.tp_off + (long long)P.tp_rank * S.rows + r, v0, tag);
+                    fl_tp_store_partial(P, F.tp_off + (long long)P.tp_rank * S.rows + r, v0, tag);
                 } else {
                     ll_store(F.out + r, __fadd_rn(fl_xres(P)[r], v0), tag);
                 }
@@ -1343,7 +1350,11 @@ __device__ __noinline__ void fl_producer(const FParams &P, int pos, int nch, int
 
 // ---- the kernel -------------------------------------------------------------------------
 
-template <int HD, int G>
+// TP: the tensor-parallel instance (its norm phases add the ranks' partial sums while
+// staging). The single-GPU instance references none of that staging code: with it in the
+// same kernel, ptxas spilled registers in the tile loops and the attention unit (1,227 ->
+// 1,060 tok/s on one GPU).
+template <int HD, int G, bool TP>
 __global__ void __launch_bounds__(FL_THREADS, 1) decode_flow_kernel(const __grid_constant__ FParams P) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (tid == 0) {
@@ -1401,7 +1412,7 @@ __global__ void __launch_bounds__(FL_THREADS, 1) decode_flow_kernel(const __grid
             if (F.kind == FL_ATTN) {
                 if (nch > 0 && u < units) ok = FlowAttn<HD, G>::unit(P, F, u / S, u % S, S, pos, nch, seq, tag, wcycles, tr);
             } else if ((int)blockIdx.x < F.stage_ctas) {
-                ok = fl_stage_warp(P, F, ph, tag, token0, tr);
+                ok = fl_stage_warp<TP>(P, F, ph, tag, token0, tr);
                 if (ok) ok = fl_tiles(P, F, seq, tag, wcycles, tr);
                 ok = !cbar_any(!ok || fl_abort);  // all warps past their tiles (the epilogue warp follows)
             }
