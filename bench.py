@@ -98,7 +98,7 @@ class Clocks:
 # dram__bytes_read.sum + dram__bytes_write.sum of one step-kernel launch under ncu (profiles/),
 # with the algorithmic bytes of that launch's KV position
 PK_CAPTURE = {"dram_bytes": 635_233_536 + 6_902_784, "algorithmic_bytes": 633_700_000, "position": 13}
-FL_CAPTURE = {"dram_bytes": 639_756_800 + 5_940_480, "algorithmic_bytes": 639_348_864, "position": 132}
+FL_CAPTURE = {"dram_bytes": 639_928_832 + 7_345_152, "algorithmic_bytes": 639_348_864, "position": 132}
 
 
 def traffic_of(mode: int, roof: dict) -> dict:
