@@ -400,7 +400,8 @@ __device__ __noinline__ void fl_embed_chunk(const FParams &P, int tok, int b, fl
 
 // Tensor parallel: chunk b of x = (residual kept in xs) + the ranks' partial sums, added
 // in rank order, so every rank computes the same x bit for bit. `in` holds [world][cols]
-// tagged words; two ranks' words are polled at a time (eight 16-byte loads per lane).
+// tagged words, polled one rank at a time (four 16-byte loads per lane: polling two ranks
+// at once held enough registers to make ptxas spill in the tile loops and the attention unit).
 // Lanes of one warp; returns false (warp-uniform) when stopped.
 FDEV bool fl_stage_tp_chunk(const FParams &P, const FPhase &F, int b, uint32_t tag, float *xs) {
     const int lane = threadIdx.x & 31, n = F.cols;
@@ -411,20 +412,16 @@ FDEV bool fl_stage_tp_chunk(const FParams &P, const FPhase &F, int b, uint32_t t
         x[2 * k] = v.x;
         x[2 * k + 1] = v.y;
     }
-    for (int r0 = 0; r0 < P.tp_world; r0 += 2) {
-        const int nr = min(2, P.tp_world - r0);
-        ulonglong2 w[8];
-        uint32_t pend = 0;
+    for (int r = 0; r < P.tp_world; r++) {
+        const uint64_t *src = F.in + (size_t)r * n + b * 256;
+        ulonglong2 w[4];
+        uint32_t pend = 15u;
 #pragma unroll
-        for (int k = 0; k < 8; k++)
-            if ((k >> 2) < nr) {
-                w[k] = ll_load2_sys(F.in + (size_t)(r0 + (k >> 2)) * n + b * 256 + 2 * (lane + 32 * (k & 3)));
-                pend |= 1u << k;
-            }
+        for (int k = 0; k < 4; k++) w[k] = ll_load2_sys(src + 2 * (lane + 32 * k));
         unsigned long long t0 = 0;
         for (long long it = 0;; it++) {
 #pragma unroll
-            for (int k = 0; k < 8; k++)
+            for (int k = 0; k < 4; k++)
                 if (((pend >> k) & 1u) && (uint32_t)(w[k].x >> 32) == tag && (uint32_t)(w[k].y >> 32) == tag)
                     pend &= ~(1u << k);
             if (__all_sync(0xffffffffu, pend == 0)) break;
@@ -438,20 +435,13 @@ FDEV bool fl_stage_tp_chunk(const FParams &P, const FPhase &F, int b, uint32_t t
                 }
             }
 #pragma unroll
-            for (int k = 0; k < 8; k++)
-                if ((pend >> k) & 1u)
-                    w[k] = ll_load2_sys(F.in + (size_t)(r0 + (k >> 2)) * n + b * 256 + 2 * (lane + 32 * (k & 3)));
+            for (int k = 0; k < 4; k++)
+                if ((pend >> k) & 1u) w[k] = ll_load2_sys(src + 2 * (lane + 32 * k));
         }
 #pragma unroll
-        for (int q = 0; q < 2; q++) {  // rank r0, then r0 + 1
-            if (q < nr) {
-#pragma unroll
-                for (int k = 0; k < 4; k++) {
-                    const ulonglong2 v = w[4 * q + k];
-                    x[2 * k] = __fadd_rn(x[2 * k], __uint_as_float((uint32_t)v.x));
-                    x[2 * k + 1] = __fadd_rn(x[2 * k + 1], __uint_as_float((uint32_t)v.y));
-                }
-            }
+        for (int k = 0; k < 4; k++) {
+            x[2 * k] = __fadd_rn(x[2 * k], __uint_as_float((uint32_t)w[k].x));
+            x[2 * k + 1] = __fadd_rn(x[2 * k + 1], __uint_as_float((uint32_t)w[k].y));
         }
     }
 #pragma unroll
@@ -619,6 +609,7 @@ FDEV unsigned long long fl_key(float v, int idx) {
 
 // Epilogue of one tile (the last warp to finish it): lanes 0..15 own its rows; in a
 // SwiGLU tile lane j < 8 owns output row 8 lt + j (gate in MMA row j, up in row j + 8).
+template <bool TP>
 FDEV void fl_epilogue(const FParams &P, const FPhase &F, const PSeg &S, int lt, int d, uint32_t tag, float rrms) {
     const int lane = threadIdx.x & 31;
     const bool pair = F.kind == FL_SWIGLU;
@@ -655,7 +646,7 @@ FDEV void fl_epilogue(const FParams &P, const FPhase &F, const PSeg &S, int lt, 
                 break;
             }
             case FL_RESID:
-                if (F.tp_off >= 0) {  // this rank's partial sum, to every rank (the next phase adds them)
+                if (TP && F.tp_off >= 0) {  // this rank's partial sum, to every rank (the next phase adds them)
                     fl_tp_store_partial(P, F.tp_off + (long long)P.tp_rank * S.rows + r, v0, tag);
                 } else {
                     ll_store(F.out + r, __fadd_rn(fl_xres(P)[r], v0), tag);
@@ -720,10 +711,11 @@ FDEV void fl_tile(const FParams &P, const FPhase &F, const PSeg &S, int lt, cons
 
 // Tiles [t0, t1) of phase F on this GPU: all of them, except the lm_head of a sharded
 // greedy step, where each rank takes an equal share (the ranks exchange their best keys).
+template <bool TP>
 FDEV void fl_tile_range(const FParams &P, const FPhase &F, int &t0, int &t1) {
     t0 = 0;
     t1 = F.n_tiles;
-    if (F.kind == FL_LM && P.lm_shard) {
+    if (TP && F.kind == FL_LM && P.lm_shard) {
         const int per = (F.n_tiles + P.tp_world - 1) / P.tp_world;
         t0 = min(F.n_tiles, P.tp_rank * per);
         t1 = min(F.n_tiles, t0 + per);
@@ -731,13 +723,14 @@ FDEV void fl_tile_range(const FParams &P, const FPhase &F, int &t0, int &t1) {
 }
 
 // The CTA's tiles of one GEMV phase (tile = blockIdx.x + k * gridDim.x), warp-level.
+template <bool TP>
 FDEV bool fl_tiles(const FParams &P, const FPhase &F, long long &seq, uint32_t tag, long long &wcycles,
                    unsigned long long *tr) {
     const int nb = F.cols >> 8;
     const uint2 *xf0 = fl_frag(P), *xf1 = xf0 + (size_t)nb * 128;
     long long tacc[4] = {0, 0, 0, 0};
     int t0, t1;
-    fl_tile_range(P, F, t0, t1);
+    fl_tile_range<TP>(P, F, t0, t1);
     for (int tile = t0 + blockIdx.x; tile < t1; tile += gridDim.x) {
         int sidx, lt;
         fl_locate(F, tile, sidx, lt);
@@ -1098,6 +1091,7 @@ struct FlowAttn {
 // After the lm_head phase, by the epilogue warp once it ran this CTA's last lm_head
 // epilogue: publish the CTA's best key; the last CTA reduces all of them, writes the token
 // and (loop mode) advances the step state.
+template <bool TP>
 FDEV void fl_argmax_finish(const FParams &P, uint32_t tag) {
     const int lane = threadIdx.x & 31;
     unsigned int ticket = 0;
@@ -1113,7 +1107,7 @@ FDEV void fl_argmax_finish(const FParams &P, uint32_t tag) {
     for (int i = lane; i < (int)gridDim.x; i += 32) best = max(best, __ldcg(P.am_key + i));
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) best = max(best, __shfl_xor_sync(0xffffffffu, best, o));
-    if (P.lm_shard) {
+    if (TP && P.lm_shard) {
         // this rank's best key to every rank (two tagged words), then the largest of all
         // ranks' keys: every rank picks the same token
         if (lane < P.tp_world) {
@@ -1168,6 +1162,7 @@ FDEV void fl_argmax_finish(const FParams &P, uint32_t tag) {
 // published their partial sums, runs the epilogue (residual add, SwiGLU, q|k|v store,
 // logits + argmax candidate) and frees the ring slot. Attention pages take ring slots
 // without an epilogue (their reader frees them). Every wait is bounded.
+template <bool TP>
 __device__ __noinline__ void fl_epilogue_warp(const FParams &P, int nch, int S, uint32_t tag) {
     const int lane = threadIdx.x & 31;
     const int units = P.n_kv * S, u = (int)gridDim.x - 1 - (int)blockIdx.x;
@@ -1193,7 +1188,7 @@ __device__ __noinline__ void fl_epilogue_warp(const FParams &P, int nch, int S, 
         const unsigned long long t_ph = P.trace ? gtimer() : 0ull;
         if ((int)blockIdx.x < F.stage_ctas) {
             int t0, t1;
-            fl_tile_range(P, F, t0, t1);
+            fl_tile_range<TP>(P, F, t0, t1);
             for (int tile = t0 + blockIdx.x; tile < t1; tile += gridDim.x) {
                 int sidx, lt;
                 fl_locate(F, tile, sidx, lt);
@@ -1216,7 +1211,7 @@ __device__ __noinline__ void fl_epilogue_warp(const FParams &P, int nch, int S, 
                     rrms = fl_rrms(F, ph);
                     have_rrms = true;
                 }
-                fl_epilogue(P, F, F.seg[sidx], lt, d, tag, rrms);
+                fl_epilogue<TP>(P, F, F.seg[sidx], lt, d, tag, rrms);
                 __syncwarp();
                 if (lane == 0) fl_release_slot(&fl_empty[d]);
                 ce += clock64() - c1;
@@ -1225,7 +1220,7 @@ __device__ __noinline__ void fl_epilogue_warp(const FParams &P, int nch, int S, 
         }
         if (kind == FL_LM) {
             __syncwarp();
-            fl_argmax_finish(P, tag);
+            fl_argmax_finish<TP>(P, tag);
         }
         if (P.trace && lane == 0) {
             unsigned long long *tr = P.trace + ((size_t)ph * gridDim.x + blockIdx.x) * FL_TRACE_FIELDS;
@@ -1239,7 +1234,7 @@ __device__ __noinline__ void fl_epilogue_warp(const FParams &P, int nch, int S, 
 
 // ---- producer ---------------------------------------------------------------------------
 
-template <int HD>
+template <int HD, bool TP>
 __device__ __noinline__ void fl_producer(const FParams &P, int pos, int nch, int S) {
     uint8_t *ring = fl_ring();
     int head = 0, used = 0, need[FL_NDESC];
@@ -1301,7 +1296,7 @@ __device__ __noinline__ void fl_producer(const FParams &P, int pos, int nch, int
             }
         } else {
             int t0, t1;
-            fl_tile_range(P, F, t0, t1);
+            fl_tile_range<TP>(P, F, t0, t1);
             for (int tile = t0 + blockIdx.x; tile < t1 && !fl_abort; tile += gridDim.x) {
                 int s, lt;
                 fl_locate(F, tile, s, lt);
@@ -1390,8 +1385,8 @@ __global__ void __launch_bounds__(FL_THREADS, 1) decode_flow_kernel(const __grid
         // nothing to decode (the host checks positions before launching; this is the
         // device-side guard): every phase is skipped, the tag still advances
     } else if (warp >= FL_WARPS) {
-        if (tid == FL_CONSUMERS) fl_producer<HD>(P, pos, nch, S);
-        if (warp == FL_EPI_WARP) fl_epilogue_warp(P, nch, S, tag);
+        if (tid == FL_CONSUMERS) fl_producer<HD, TP>(P, pos, nch, S);
+        if (warp == FL_EPI_WARP) fl_epilogue_warp<TP>(P, nch, S, tag);
     } else {
         long long seq = 0;
         const int units = P.n_kv * S;
@@ -1413,7 +1408,7 @@ __global__ void __launch_bounds__(FL_THREADS, 1) decode_flow_kernel(const __grid
                 if (nch > 0 && u < units) ok = FlowAttn<HD, G>::unit(P, F, u / S, u % S, S, pos, nch, seq, tag, wcycles, tr);
             } else if ((int)blockIdx.x < F.stage_ctas) {
                 ok = fl_stage_warp<TP>(P, F, ph, tag, token0, tr);
-                if (ok) ok = fl_tiles(P, F, seq, tag, wcycles, tr);
+                if (ok) ok = fl_tiles<TP>(P, F, seq, tag, wcycles, tr);
                 ok = !cbar_any(!ok || fl_abort);  // all warps past their tiles (the epilogue warp follows)
             }
             cp_async_wait_all();
